@@ -1,0 +1,84 @@
+"""Loads the native library (`_lib/libsdcguard_b200.so`, built by `sdcguard_b200._build`) with ctypes and
+declares the C signature of every entry point.
+
+The kernels take raw device pointers and a CUDA stream handle; the Python wrappers in `sdcguard_b200.ops`
+pass `tensor.data_ptr()` and `torch.cuda.current_stream().cuda_stream`. On a machine with a GPU a missing
+or stale library is an error, never a silent fallback: `lib()` builds it when nvcc is available and raises
+otherwise.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from ctypes import c_float, c_int, c_longlong, c_uint, c_void_p
+from pathlib import Path
+
+_PKG = Path(__file__).resolve().parent
+LIB_PATH = _PKG / "_lib" / "libsdcguard_b200.so"
+
+_lock = threading.Lock()
+_lib = None
+
+P = c_void_p
+I = c_int
+L = c_longlong
+U = c_uint
+F = c_float
+
+# name -> (restype, argtypes)
+SIGNATURES: dict[str, tuple] = {
+    "sdc_gemm_ws_bytes": (L, [I, I]),
+    "sdc_gemm_bf16": (I, [P, L, P, P, I, I, I, P, L, P, P, F, P, P, P, P, I, U, U, U, U, F, F, F, F, F, P, I, I, I, I,
+                          U, P]),
+    "sdc_row_sqnorm_bf16": (I, [P, L, I, I, P, P]),
+}
+
+
+def _stale() -> bool:
+    if not LIB_PATH.exists():
+        return True
+    if os.environ.get("SDCGUARD_NO_REBUILD") == "1":
+        return False
+    src = _PKG / "csrc"
+    newest = max((p.stat().st_mtime for p in src.iterdir()), default=0.0)
+    return LIB_PATH.stat().st_mtime < newest
+
+
+def lib():
+    """The loaded library, building it first if it is missing or older than its sources."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if _stale():
+            from . import _build
+            try:
+                _build.build()
+            except Exception as e:  # noqa: BLE001
+                if not LIB_PATH.exists():
+                    raise RuntimeError(f"sdcguard_b200 native library missing and could not be built: {e}") from e
+        h = ctypes.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(h, name, None)
+            if fn is None:
+                raise RuntimeError(f"{LIB_PATH.name} lacks {name}: rebuild with python -m sdcguard_b200._build")
+            fn.restype = res
+            fn.argtypes = args
+        _lib = h
+        return _lib
+
+
+def available() -> bool:
+    try:
+        lib()
+        return True
+    except Exception:  # noqa: BLE001
+        return False
+
+
+def check(rc: int, what: str) -> None:
+    if rc != 0:
+        raise RuntimeError(f"{what} failed with code {rc}")

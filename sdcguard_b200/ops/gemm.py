@@ -1,0 +1,164 @@
+"""Python entry points of the checked sm_100a GEMM (`csrc/gemm_abft.cu`).
+
+    cw = CheckedWeight(weight, bias)                 # once, at load: checksum rows + block statistics
+    y = checked_linear(x, cw, state, slot)           # every call: one kernel, output + check
+    StateTable.read()                                # worst score per layer, when the caller wants it
+
+`checked_linear` needs ||x_i||_2^2 per row. Producers in this library (RMSNorm, attention, activation kernels)
+emit it for free; pass it as `row_sq`. Without it a small row-norm kernel runs first.
+
+Reference: the serving check `ServeGuard.check` (src/sdcguard/serve.py:846) and its per-layer constants
+`LayerChecksums` (serve.py:140); the training-side fused GEMM `fused_mm` (src/sdcguard/fused.py:119).
+"""
+from __future__ import annotations
+
+import math
+import threading
+from typing import Optional
+
+import torch
+
+from .. import _native
+from ..numerics import abft
+
+_ws_lock = threading.Lock()
+_WS: dict = {}          # device index -> zero-initialised workspace tensor (uint8)
+_ERR: dict = {}         # device index -> int32 error word
+
+
+def _stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """Per-device workspace of at least nbytes, zero-filled when (re)allocated. Reallocation must not happen
+    while a CUDA graph is being captured: engines call `reserve_workspace` with their largest shape first."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    with _ws_lock:
+        ws = _WS.get(idx)
+        if ws is None or ws.numel() < nbytes:
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("checked GEMM workspace too small inside CUDA graph capture: "
+                                   "call reserve_workspace() with the largest shape before capturing")
+            ws = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+            _WS[idx] = ws
+        return ws
+
+
+def reserve_workspace(device: torch.device, m: int, n: int) -> None:
+    workspace(device, int(_native.lib().sdc_gemm_ws_bytes(m, n)))
+
+
+def error_word(device: torch.device) -> torch.Tensor:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    e = _ERR.get(idx)
+    if e is None:
+        e = torch.zeros(1, dtype=torch.int32, device=device)
+        _ERR[idx] = e
+    return e
+
+
+class StateTable:
+    """Per-device int64 state rows [slots, 4], one per checked layer (layout in numerics.abft)."""
+
+    def __init__(self, device, slots: int = 256):
+        self.device = torch.device(device)
+        self.state = torch.zeros(slots, abft.STATE_COLS, dtype=torch.int64, device=self.device)
+        self.names: list[str] = []
+        self.nbs: list[int] = []
+
+    def add(self, name: str, nb: int) -> int:
+        if len(self.names) >= self.state.shape[0]:
+            grown = torch.zeros(self.state.shape[0] * 2, abft.STATE_COLS, dtype=torch.int64, device=self.device)
+            grown[: self.state.shape[0]] = self.state
+            self.state = grown
+        self.names.append(name)
+        self.nbs.append(nb)
+        return len(self.names) - 1
+
+    def read(self, reset: bool = False) -> list[dict]:
+        rows = self.state[: len(self.names)].cpu().tolist()
+        if reset:
+            self.state.zero_()
+        out = []
+        for i, r in enumerate(rows):
+            d = abft.decode_state_row(r)
+            d["name"] = self.names[i]
+            d["slot"] = i
+            if d["z"] > 0:
+                d["row"], d["block"], d["signed"] = abft.locate(d["flat"], self.nbs[i])
+            out.append(d)
+        return out
+
+
+class CheckedWeight:
+    """A bf16 weight W (n, k) with its checksum rows and block statistics, ready for `checked_linear`."""
+
+    def __init__(self, weight: torch.Tensor, bias: Optional[torch.Tensor] = None, mask: Optional[tuple] = None,
+                 c1: float = abft.C1, c2: float = abft.C2, c3: float = abft.C3):
+        if weight.dtype != torch.bfloat16 or weight.dim() != 2:
+            raise ValueError("CheckedWeight needs a 2-D bf16 weight")
+        n, k = weight.shape
+        if k % 8 or n % 8:
+            raise ValueError(f"checked GEMM needs n and k multiples of 8 (got n={n}, k={k})")
+        self.weight = weight.contiguous()
+        self.bias = None if bias is None else bias.detach().float().contiguous()
+        self.cs = abft.weight_checksums(self.weight, bias, mask)
+        self.mask = self.cs.mask
+        self.prod_coef, self.out_coef = abft.coefficients(k, c1, c2, c3)
+        self.n, self.k, self.nb = n, k, self.cs.nb
+
+    def refresh(self) -> None:
+        """Recompute the checksums after the weight was changed on purpose (e.g. a reload)."""
+        self.cs = abft.weight_checksums(self.weight, self.bias, self.mask)
+
+
+def row_sqnorm(x: torch.Tensor) -> torch.Tensor:
+    m, k = x.shape
+    out = torch.empty(m, dtype=torch.float32, device=x.device)
+    _native.check(_native.lib().sdc_row_sqnorm_bf16(x.data_ptr(), x.stride(0), m, k, out.data_ptr(),
+                                                     _stream_ptr(x.device)), "row_sqnorm")
+    return out
+
+
+def pick_bn(m: int, n: int, num_sms: int = 148) -> int:
+    """256-wide tiles when there are enough of them to fill the GPU, else 128."""
+    tiles256 = -(-m // 128) * -(-n // 256)
+    return 256 if tiles256 >= num_sms * 0.75 else 128
+
+
+def checked_linear(x: torch.Tensor, cw: CheckedWeight, state: torch.Tensor, slot: int,
+                   row_sq: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+                   z_alarm: float = abft.Z_ALARM, bn: Optional[int] = None, max_ctas: int = 0,
+                   inject: Optional[tuple] = None) -> torch.Tensor:
+    """y = x @ W^T (+ b) on tcgen05 with the ABFT check folded into `state[slot]`.
+    x: (m, k) bf16 with unit column stride. inject=(row, col, xor_bits) flips bits of one fp32 accumulator
+    element before the check and the rounding (fault-injection experiments)."""
+    if x.dtype != torch.bfloat16 or x.dim() != 2 or x.stride(1) != 1:
+        raise ValueError("checked_linear needs a 2-D bf16 x with unit column stride")
+    m, k = x.shape
+    if k != cw.k:
+        raise ValueError(f"x has {k} columns, the weight {cw.k}")
+    dev = x.device
+    if out is None:
+        out = torch.empty(m, cw.n, dtype=torch.bfloat16, device=dev)
+    if m == 0:
+        return out
+    if row_sq is None:
+        row_sq = row_sqnorm(x)
+    lib = _native.lib()
+    ws = workspace(dev, int(lib.sdc_gemm_ws_bytes(m, cw.n)))
+    err = error_word(dev)
+    if bn is None:
+        bn = pick_bn(m, cw.n)
+    s = cw.mask
+    inj_row, inj_col, inj_xor = (-1, -1, 0) if inject is None else (int(inject[0]), int(inject[1]), int(inject[2]))
+    rc = lib.sdc_gemm_bf16(
+        x.data_ptr(), x.stride(0), cw.weight.data_ptr(), cw.cs.wc.data_ptr(), m, cw.n, k, out.data_ptr(),
+        out.stride(0), None if cw.bias is None else cw.bias.data_ptr(),
+        None if cw.cs.bsum is None else cw.cs.bsum.data_ptr(), float(cw.cs.bias_max), row_sq.data_ptr(),
+        cw.cs.wstat.data_ptr(), ws.data_ptr(), state.data_ptr(), int(slot), s[0], s[1], s[2], s[3],
+        float(z_alarm), float(cw.prod_coef), float(cw.out_coef), float(abft.ABS_FLOOR), float(math.sqrt(k)),
+        err.data_ptr(), int(bn), int(max_ctas), inj_row, inj_col, inj_xor, _stream_ptr(dev))
+    _native.check(rc, "checked GEMM launch")
+    return out

@@ -1,0 +1,88 @@
+"""The checked tcgen05 GEMM against a plain PyTorch fp32 reference of the same op: output values, clean
+scores (no false alarm), detection and location of injected accumulator faults, and the state counters."""
+import math
+
+import pytest
+import torch
+
+from sdcguard_b200.numerics import abft
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [
+    (128, 128, 64),
+    (200, 384, 192),
+    (256, 1024, 1024),
+    (1000, 3072, 1024),
+    (64, 4096, 1024),
+    (1024, 1024, 3072),
+    (333, 136, 520),
+]
+
+
+def _run(m, n, k, bn, bias=False, inject=None, seed=0):
+    from sdcguard_b200.ops import gemm
+    torch.manual_seed(seed)
+    dev = torch.device("cuda")
+    x = torch.randn(m, k, device=dev).to(torch.bfloat16)
+    w = (torch.randn(n, k, device=dev) * 0.02).to(torch.bfloat16)
+    b = torch.randn(n, device=dev) * 0.1 if bias else None
+    cw = gemm.CheckedWeight(w, b)
+    st = gemm.StateTable(dev, 4)
+    slot = st.add("lin", cw.nb)
+    y = gemm.checked_linear(x, cw, st.state, slot, bn=bn, inject=inject)
+    torch.cuda.synchronize()
+    return x, w, b, cw, st, y
+
+
+@pytest.mark.parametrize("bn", [128, 256])
+@pytest.mark.parametrize("m,n,k", SHAPES)
+def test_output_matches_fp32_reference(m, n, k, bn):
+    x, w, b, cw, st, y = _run(m, n, k, bn)
+    ref = x.float() @ w.float().t()
+    err = (y.float() - ref).abs().max().item()
+    scale = ref.abs().max().item()
+    assert err <= 2 ** -7 * scale + 1e-3, (err, scale)
+    d = st.read()[0]
+    assert d["checks"] == 1
+    assert d["unjudged"] == 0
+    assert 0.0 < d["z"] < 2.0, d
+
+
+@pytest.mark.parametrize("bn", [128, 256])
+def test_bias_and_clean_score_matches_torch_model(bn):
+    x, w, b, cw, st, y = _run(300, 640, 256, bn, bias=True)
+    ref = x.float() @ w.float().t() + b
+    assert (y.float() - ref).abs().max().item() < 2 ** -7 * ref.abs().max().item() + 1e-3
+    d = st.read()[0]
+    r = abft.reference_check(x, w, b, cw.cs)
+    assert d["z"] < 2.0 and r["z"] < 2.0, (d, r["z"])
+
+
+@pytest.mark.parametrize("bit", [30, 28, 25, 23, 22, 20, 31])
+def test_injected_accumulator_flip_is_caught_and_located(bit):
+    m, n, k = 512, 1024, 1024
+    row = 301
+    _, _, _, _, _, y0 = _run(m, n, k, 256)
+    col = int(y0[row].float().abs().argmax())          # a large output: every listed bit moves it far
+    x, w, b, cw, st, y = _run(m, n, k, 256, inject=(row, col, 1 << bit))
+    d = st.read()[0]
+    assert d["z"] > abft.Z_ALARM, d
+    assert d["row"] == row and d["block"] == col // 128, d
+
+
+def test_state_accumulates_over_calls():
+    from sdcguard_b200.ops import gemm
+    dev = torch.device("cuda")
+    x = torch.randn(256, 512, device=dev).to(torch.bfloat16)
+    w = (torch.randn(512, 512, device=dev) * 0.05).to(torch.bfloat16)
+    cw = gemm.CheckedWeight(w)
+    st = gemm.StateTable(dev, 2)
+    s = st.add("a", cw.nb)
+    for _ in range(5):
+        gemm.checked_linear(x, cw, st.state, s)
+    torch.cuda.synchronize()
+    d = st.read()[0]
+    assert d["checks"] == 5 and d["z"] < 2.0
+    err = gemm.error_word(dev).item()
+    assert err == 0
