@@ -30,7 +30,7 @@ F = c_float
 SIGNATURES: dict[str, tuple] = {
     "sdc_gemm_ws_bytes": (L, [I, I]),
     "sdc_gemm_bf16": (I, [P, L, P, P, I, I, I, P, L, P, P, F, P, P, P, P, I, U, U, U, U, F, F, F, F, F, P, I, I, I, I,
-                          U, P]),
+                          U, P, P]),
     "sdc_row_sqnorm_bf16": (I, [P, L, I, I, P, P]),
 }
 

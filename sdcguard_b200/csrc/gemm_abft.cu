@@ -15,13 +15,17 @@
 //     rows: the plain block sum of W split into three bf16 parts (hi, mid, lo; about 24 significant bits)
 //     and the +-1-signed block sum split the same way. Those rows are extra output tiles of the same
 //     launch ("checksum tiles"), 6/128 = 4.7% extra MMA work: E = A @ Wc^T lands in TMEM like any tile.
+//   * Within each 128-row band the checksum tiles come first in the persistent tile order. Their
+//     epilogue stores E (plain, signed) per row and block to a small workspace and then bumps the band's
+//     "expected ready" counter (release).
 //   * The epilogue of an output tile computes, per row and block, sum(c), sum(s_j c), sum(c^2), sum|c|
-//     of the fp32 accumulator, writes the bf16 output, and stores the four sums to a workspace. The
-//     epilogue of a checksum tile stores E (plain, signed) per row and block.
-//   * The last CTA to finish a 128-row band (arrival counter in the workspace) judges every (row, block)
-//     of the band with the fp32-accumulator noise model and folds the worst score into the layer's
-//     state row with 64-bit atomic maxima: (z bits << 32 | flat index), (z bits << 32 | noise bits),
-//     checks executed, checksums left unjudged. The state row layout follows src/sdcguard/serve.py:55-65.
+//     of the fp32 accumulator in registers while it writes the bf16 output through TMA stores, waits
+//     (bounded) until its band's expected sums are ready, and judges its own (row, block) pairs: one
+//     per thread, with the fp32-accumulator noise model. The worst score of the tile goes into the
+//     layer's state row with 64-bit atomic maxima: (z bits << 32 | flat index), (z bits << 32 | noise
+//     bits), checks executed, checksums left unjudged (layout of src/sdcguard/serve.py:55-65).
+//     The wait cannot deadlock: a tile only waits for tiles earlier in the order, and every CTA of the
+//     persistent grid is resident.
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -36,10 +40,10 @@ constexpr int BK = 64;             // 64 bf16 = 128 bytes: one swizzle atom row
 constexpr int CSW = 128;           // checksum block width in output columns
 constexpr int CS_ROWS = 6;         // rows of Wc per block
 constexpr int A_BYTES = BM * BK * 2;
-// The workspace starts with the arrival counters at a fixed place (other launches' statistics, at
+// The workspace starts with two counters per band at a fixed place (other launches' expected sums, at
 // shape-dependent offsets, must never overlap them): room for 4096 bands = 524,288 rows.
 constexpr int MAX_BANDS = 4096;
-constexpr long long COUNTER_BYTES = MAX_BANDS * 4;
+constexpr long long COUNTER_BYTES = 2LL * MAX_BANDS * 4;
 
 struct Params {
   int M, N, K;
@@ -56,9 +60,9 @@ struct Params {
   const float2* bsum;     // [nb] plain/signed block sums of the bias, or null
   const float* row_sq;    // [M] sum of squares of each row of A
   const float4* wstat;    // [nb] {||W_b||_F, ||plain sum||_2, ||signed sum||_2, max|W_b|}
-  float4* stats;          // workspace [M][nb]
   float2* expd;           // workspace [M][nb]
-  int* counters;          // workspace [m_tiles], zero between launches
+  int* cs_done;           // workspace [m_tiles]: checksum tiles finished in the band (zero between launches)
+  int* main_done;         // workspace [m_tiles]: output tiles judged in the band (zero between launches)
   unsigned long long* state;  // [slots][4]
   int slot;
   uint32_t sgn[4];        // sign pattern of the signed checksum: bit j set -> column j counts negative
@@ -71,6 +75,7 @@ struct Params {
   int* err;
   int inj_row, inj_col;
   uint32_t inj_xor;
+  unsigned long long* dbg;   // optional per-CTA timers (null: off): [cta][8]
 };
 
 template <int BN>
@@ -82,7 +87,8 @@ struct Cfg {
   static constexpr int TMEM_COLS = 2 * BN;            // two accumulators
   static constexpr int THREADS = 128 + NWG * 128;
   static constexpr int CSB = 20 * NWG;                 // checksum blocks per checksum tile (120 columns per WG)
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int STAGING_BYTES = NWG * 4 * 4096;  // per epilogue warp: 32 rows x 128 B of bf16 output
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + STAGING_BYTES + 1024 /*align*/ + 512 /*control*/;
 };
 
 struct SmemCtl {
@@ -91,30 +97,52 @@ struct SmemCtl {
   uint64_t tfull[2];
   uint64_t tempty[2];
   uint64_t drain;
+  uint64_t ready[2];       // coordinator -> epilogue: the band's expected sums are published (per accumulator)
+  uint64_t resfull[2];     // epilogue -> coordinator: the tile's result is in res[acc]
+  uint64_t resempty[2];    // coordinator -> epilogue: res[acc] may be overwritten
   uint32_t tmem_base;
   int abort_flag;
-  int last;
-  int unj;
-  unsigned long long key0;
-  unsigned long long key1;
+  int ready_ok[2];         // 0 when the coordinator gave up waiting for the band
+  unsigned long long wkey0[8];   // per epilogue warp: worst (z, flat) key of the tile
+  unsigned long long wkey1[8];   // per epilogue warp: worst (z, noise) key
+  int wunj[8];                   // per epilogue warp: pairs left unjudged
+  unsigned long long res0[2], res1[2];
+  int resunj[2];
 };
 
-__device__ __forceinline__ void tile_coords(const Params& p, int tile, int& mt, int& nt) {
+// Tile order inside a band: checksum tiles first, then output tiles.
+__device__ __forceinline__ void tile_coords(const Params& p, int tile, int& mt, bool& cs, int& idx) {
   mt = tile / p.n_per_m;
-  nt = tile - mt * p.n_per_m;
+  const int nt = tile - mt * p.n_per_m;
+  cs = nt < p.n_cs;
+  idx = cs ? nt : nt - p.n_cs;
+}
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_gpu_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
 }
 
 template <int BN, bool INJ>
 __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
     gemm_abft_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
-                     const __grid_constant__ CUtensorMap tmWc, const Params p) {
+                     const __grid_constant__ CUtensorMap tmWc, const __grid_constant__ CUtensorMap tmC,
+                     const Params p) {
   using C = Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  SmemCtl* ctl = reinterpret_cast<SmemCtl*>(smem + C::STAGES * C::STAGE_BYTES);
+  uint8_t* staging = smem + C::STAGES * C::STAGE_BYTES;
+  SmemCtl* ctl = reinterpret_cast<SmemCtl*>(staging + C::STAGING_BYTES);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  if (p.dbg && threadIdx.x == 0) p.dbg[blockIdx.x * 8 + 5] = globaltimer();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -126,6 +154,11 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
       mbar_init(&ctl->tempty[a], C::NWG * 128);
     }
     mbar_init(&ctl->drain, 1);
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&ctl->ready[a], 1);
+      mbar_init(&ctl->resfull[a], 1);
+      mbar_init(&ctl->resempty[a], 1);
+    }
     ctl->abort_flag = 0;
     fence_mbar_init();
   }
@@ -137,6 +170,7 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmW);
     tma_prefetch_desc(&tmWc);
+    tma_prefetch_desc(&tmC);
   }
   tc_fence_before();
   __syncthreads();
@@ -154,9 +188,9 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
       uint32_t issued = 0;        // bit s: stage s has a load in flight that we have not seen land
       uint32_t issued_phase = 0;  // bit s: the full-barrier parity of that load
       for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
-        int mt, nt;
-        tile_coords(p, tile, mt, nt);
-        const bool cs = nt >= p.n_main;
+        int mt, idx;
+        bool cs;
+        tile_coords(p, tile, mt, cs, idx);
         const uint32_t bytes = A_BYTES + (cs ? (C::CSB * CS_ROWS) * BK * 2 : C::B_BYTES);
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!mbar_wait(&ctl->empty[stage], phase ^ 1u, abort_flag)) {
@@ -168,9 +202,9 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
           mbar_arrive_expect_tx(&ctl->full[stage], bytes);
           tma_load_2d(sa, &tmA, &ctl->full[stage], kb * BK, mt * BM);
           if (cs)
-            tma_load_2d(sb, &tmWc, &ctl->full[stage], kb * BK, (nt - p.n_main) * C::CSB * CS_ROWS);
+            tma_load_2d(sb, &tmWc, &ctl->full[stage], kb * BK, idx * C::CSB * CS_ROWS);
           else
-            tma_load_2d(sb, &tmW, &ctl->full[stage], kb * BK, nt * BN);
+            tma_load_2d(sb, &tmW, &ctl->full[stage], kb * BK, idx * BN);
           issued |= 1u << stage;
           issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
           if (++stage == C::STAGES) {
@@ -197,12 +231,12 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
       bool ok = true;
       const uint32_t idesc_main = idesc_bf16_f32(BM, BN);
       for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
-        int mt, nt;
-        tile_coords(p, tile, mt, nt);
+        int mt, idx;
+        bool cs;
+        tile_coords(p, tile, mt, cs, idx);
         uint32_t idesc = idesc_main;
-        if (nt >= p.n_main) {
-          const int c = nt - p.n_main;
-          const int nblk = min(C::CSB, p.nb - c * C::CSB);
+        if (cs) {
+          const int nblk = min(C::CSB, p.nb - idx * C::CSB);
           const int ncols = ((nblk * CS_ROWS + 15) / 16) * 16;
           idesc = idesc_bf16_f32(BM, ncols);
         }
@@ -248,6 +282,63 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
         mbar_wait(&ctl->drain, 0, nullptr);
       }
     }
+  } else if (warp == 3) {
+    // ------------------------------------------------------------ check coordinator
+    // Keeps global-memory round trips off the epilogue's path: waits for each band's expected sums
+    // before the epilogue needs them, and publishes the results (state atomics, band counters) after.
+    if (lane == 0) {
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      unsigned long long* st = p.state + static_cast<long long>(p.slot) * 4;
+      for (int tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x) {
+        int mt, idx;
+        bool cs;
+        tile_coords(p, tile, mt, cs, idx);
+        int ok = 1;
+        if (!cs) {
+          ok = 0;
+          const unsigned long long t0 = globaltimer();
+          for (uint32_t i = 0;; ++i) {
+            if (ld_acquire_gpu(p.cs_done + mt) >= p.n_cs) {
+              ok = 1;
+              break;
+            }
+            if ((i & 63u) == 63u && (globaltimer() - t0 > kWaitNs || *abort_flag)) break;
+          }
+          if (!ok) record_error(p.err, ERR_TIMEOUT_PEER);
+        }
+        // res[acc] is free again once the previous result in it was published (first use passes)
+        ctl->ready_ok[acc] = ok;
+        mbar_arrive(&ctl->ready[acc]);
+        if (!mbar_wait(&ctl->resfull[acc], acc_phase, abort_flag)) {
+          record_error(p.err, ERR_TIMEOUT_EPILOGUE);
+          *abort_flag = 1;
+          break;
+        }
+        if (cs) {
+          fence_acq_rel_gpu();      // release the CTA's expected sums of this tile
+          atomicAdd(p.cs_done + mt, 1);
+        } else {
+          const unsigned long long a0 = ctl->res0[acc], a1 = ctl->res1[acc];
+          const int u = ctl->resunj[acc];
+          // most tiles of a clean run are below the running maximum: skip their atomics
+          if (a0 > ld_relaxed_gpu_u64(st + 0)) atomicMax(st + 0, a0);
+          if (a1 > ld_relaxed_gpu_u64(st + 1)) atomicMax(st + 1, a1);
+          if (u) atomicAdd(st + 3, static_cast<unsigned long long>(u));
+          if (mt == 0 && idx == 0) atomicAdd(st + 2, 1ull);   // one count per launch
+          // the last output tile of the band returns the band's counters to zero for the next launch
+          if (atomicAdd(p.main_done + mt, 1) == p.n_main - 1) {
+            p.cs_done[mt] = 0;
+            p.main_done[mt] = 0;
+          }
+        }
+        mbar_arrive(&ctl->resempty[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+    }
   } else if (warp >= 4) {
     // ------------------------------------------------------------ epilogue warpgroups
     const int ew = warp - 4;          // 0 .. 4*NWG-1
@@ -259,10 +350,13 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x) {
-      int mt, nt;
-      tile_coords(p, tile, mt, nt);
+      int mt, idx;
+      bool cs;
+      tile_coords(p, tile, mt, cs, idx);
       const int row = mt * BM + row_in_tile;
+      const unsigned long long t_w0 = p.dbg ? globaltimer() : 0ull;
       const bool got = mbar_wait(&ctl->tfull[acc], acc_phase, abort_flag);
+      const unsigned long long t_w1 = p.dbg ? globaltimer() : 0ull;
       // every epilogue warp leaves together if any of them gave up (no named barrier is left waiting)
       if (named_bar_or(1, C::NWG * 128, !got)) {
         if (!got) record_error(p.err, ERR_TIMEOUT_EPILOGUE);
@@ -271,56 +365,14 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
       }
       tc_fence_after();
       const uint32_t tacc = tmem_base + static_cast<uint32_t>(acc * BN) + lane_off;
-      if (nt < p.n_main) {
-        const int col0 = nt * BN + g * CSW;
-        if (col0 < p.N) {   // warp-uniform
-          const int b = col0 / CSW;
-          float P = 0.f, S = 0.f, Q = 0.f, Aab = 0.f;
-#pragma unroll 1
-          for (int c = 0; c < CSW / 32; ++c) {
-            uint32_t r[32];
-            tmem_ld32(tacc + static_cast<uint32_t>(g * CSW + c * 32), r);
-            tmem_wait_ld();
-            const uint32_t sg = p.sgn[c];
-            const int cbase = col0 + c * 32;
-            float v[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              float x = u32_as_f32(r[j]);
-              if (p.bias != nullptr && cbase + j < p.N) x += __ldg(p.bias + cbase + j);
-              if (INJ) {
-                if (row == p.inj_row && cbase + j == p.inj_col) x = __uint_as_float(__float_as_uint(x) ^ p.inj_xor);
-              }
-              v[j] = x;
-              P += x;
-              S += ((sg >> j) & 1u) ? -x : x;
-              Q = fmaf(x, x, Q);
-              Aab += fabsf(x);
-            }
-            if (row < p.M) {
-              __nv_bfloat16* dst = p.C + static_cast<long long>(row) * p.ldc + cbase;
-#pragma unroll
-              for (int j = 0; j < 32; j += 8) {
-                if (cbase + j < p.N) {
-                  uint4 o;
-                  o.x = pack_bf16x2(v[j + 0], v[j + 1]);
-                  o.y = pack_bf16x2(v[j + 2], v[j + 3]);
-                  o.z = pack_bf16x2(v[j + 4], v[j + 5]);
-                  o.w = pack_bf16x2(v[j + 6], v[j + 7]);
-                  *reinterpret_cast<uint4*>(dst + j) = o;
-                }
-              }
-            }
-          }
-          if (row < p.M) p.stats[static_cast<long long>(row) * p.nb + b] = make_float4(P, S, Q, Aab);
-        }
-      } else {
-        const int ct = nt - p.n_main;
-        const int blk0 = ct * C::CSB + g * 20;   // first block of this warpgroup
+
+      if (cs) {
+        // ---- checksum tile: E = A @ Wc^T, three bf16 parts per sum added in fp32
+        const int blk0 = idx * C::CSB + g * 20;   // first block of this warpgroup
 #pragma unroll 1
         for (int i4 = 0; i4 < 5; ++i4) {
           const int bb = blk0 + i4 * 4;
-          if (bb < p.nb && bb < (ct + 1) * C::CSB) {  // warp-uniform
+          if (bb < p.nb) {  // warp-uniform
             uint32_t r[24];
             const uint32_t ta = tacc + static_cast<uint32_t>(g * 120 + i4 * 24);
             uint32_t (&r0)[8] = *reinterpret_cast<uint32_t(*)[8]>(&r[0]);
@@ -343,112 +395,171 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
             }
           }
         }
-      }
-      // release the accumulator to the MMA warp
-      tc_fence_before();
-      mbar_arrive(&ctl->tempty[acc]);
-      if (++acc == 2) {
-        acc = 0;
-        acc_phase ^= 1u;
-      }
+        tc_fence_before();
+        mbar_arrive(&ctl->tempty[acc]);
+        named_bar_sync(1, C::NWG * 128);
+        if (et == 0) {
+          // hand the tile to the coordinator, which releases the expected sums to other CTAs
+          mbar_wait(&ctl->resempty[acc], acc_phase ^ 1u, abort_flag);
+          mbar_arrive(&ctl->resfull[acc]);
+        }
+      } else {
+        // ---- output tile: block sums in registers, bf16 output through TMA, then judge own pairs
+        const int col0 = idx * BN + g * CSW;
+        const bool have = col0 < p.N;           // warp-uniform
+        float P = 0.f, S = 0.f, Q = 0.f, Aab = 0.f;
+        if (have) {
+          uint8_t* stg = staging + ew * 4096;     // this warp's 32 x 128 B staging tile
+#pragma unroll 1
+          for (int h = 0; h < CSW / 64; ++h) {
+            uint32_t r[64];
+            uint32_t (&ra)[32] = *reinterpret_cast<uint32_t(*)[32]>(&r[0]);
+            uint32_t (&rb)[32] = *reinterpret_cast<uint32_t(*)[32]>(&r[32]);
+            tmem_ld32(tacc + static_cast<uint32_t>(g * CSW + h * 64), ra);
+            tmem_ld32(tacc + static_cast<uint32_t>(g * CSW + h * 64 + 32), rb);
+            tmem_wait_ld();
+            const int cbase = col0 + h * 64;
+            const uint32_t sg0 = p.sgn[2 * h], sg1 = p.sgn[2 * h + 1];
+            if (p.bias != nullptr) {
+#pragma unroll
+              for (int j = 0; j < 64; ++j)
+                if (cbase + j < p.N) r[j] = __float_as_uint(u32_as_f32(r[j]) + __ldg(p.bias + cbase + j));
+            }
+#pragma unroll
+            for (int j = 0; j < 64; ++j) {
+              float x = u32_as_f32(r[j]);
+              if (INJ) {
+                if (row == p.inj_row && cbase + j == p.inj_col) x = __uint_as_float(__float_as_uint(x) ^ p.inj_xor);
+              }
+              P += x;
+              S += (((j < 32 ? sg0 : sg1) >> (j & 31)) & 1u) ? -x : x;
+              Q = fmaf(x, x, Q);
+              Aab += fabsf(x);
+              r[j] = __float_as_uint(x);
+            }
+            uint32_t packed[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) packed[j] = pack_bf16x2(u32_as_f32(r[2 * j]), u32_as_f32(r[2 * j + 1]));
+            // the previous store from this staging tile must have read it before we overwrite it
+            if (lane == 0) bulk_wait_read0();
+            __syncwarp();
+            uint8_t* myrow = stg + lane * 128;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              uint4 v = make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2], packed[4 * c + 3]);
+              *reinterpret_cast<uint4*>(myrow + ((c ^ (lane & 7)) << 4)) = v;   // 128-byte swizzle
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&tmC, stg, cbase, mt * BM + q * 32);
+              bulk_commit();
+            }
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&ctl->tempty[acc]);   // the MMA warp may refill this accumulator now
 
-      // band arrival: the last CTA to finish a tile of band mt judges the whole band
-      __threadfence();
-      named_bar_sync(1, C::NWG * 128);
-      if (et == 0) {
-        const int old = atomicAdd(p.counters + mt, 1);
-        ctl->last = (old == p.n_per_m - 1) ? 1 : 0;
-        ctl->key0 = 0ull;
-        ctl->key1 = 0ull;
-        ctl->unj = 0;
-      }
-      named_bar_sync(1, C::NWG * 128);
-      if (ctl->last) {
-        __threadfence();
-        const int r0 = mt * BM;
-        const int rows = min(BM, p.M - r0);
-        const int pairs = rows * p.nb;
+        // the coordinator has waited (bounded) for the band's expected sums; skip judging if it gave up
+        bool ready = mbar_wait(&ctl->ready[acc], acc_phase, abort_flag) && ctl->ready_ok[acc] != 0;
+        const bool skip = named_bar_or(1, C::NWG * 128, !ready);
         unsigned long long k0 = 0ull, k1 = 0ull;
         int unj = 0;
-        for (int idx = et; idx < pairs; idx += C::NWG * 128) {
-          const int rr = idx / p.nb;
-          const int b = idx - rr * p.nb;
-          const long long o = static_cast<long long>(r0 + rr) * p.nb + b;
-          const float4 st = __ldcg(p.stats + o);
-          const float2 ex = __ldcg(p.expd + o);
-          const float4 ws = __ldg(p.wstat + b);
-          float ep = ex.x, es = ex.y;
-          if (p.bsum != nullptr) {
-            const float2 bs = __ldg(p.bsum + b);
-            ep += bs.x;
-            es += bs.y;
-          }
-          const float xn = sqrtf(__ldg(p.row_sq + r0 + rr));
-          const float prod = p.prod_coef * xn * fmaxf(ws.x, fmaxf(ws.y, ws.z));
-          const float den = sqrtf(st.z) * p.out_coef + prod + p.abs_floor;
-          const float dp = fabsf(ep - st.x), ds = fabsf(es - st.y);
-          float zp = dp / den;
-          const float zs = ds / den;
-          const float worst = st.w * p.out_coef + prod + p.abs_floor;
-          zp = fminf(zp, dp / worst * p.zthr);
-          float z;
-          int which = zs > zp ? 1 : 0;
-          const bool fin_exp = isfinite(ep) && isfinite(es);
-          const bool fin_act = isfinite(st.x) && isfinite(st.y) && isfinite(st.z) && isfinite(st.w);
-          bool judged = true;
-          if (!fin_exp || !isfinite(prod)) {
-            judged = false;
-          } else if (!fin_act) {
-            const float bound = p.bound_coef * xn * ws.w + p.bias_max;
-            if (bound < 1e18f) {
-              z = __int_as_float(0x7f800000);
-              which = 0;
-            } else {
-              judged = false;
-            }
+        if (have && row < p.M) {
+          const int b = col0 / CSW;
+          if (skip) {
+            unj = 1;
           } else {
-            z = fmaxf(zp, zs);
-            if (!(z == z)) z = __int_as_float(0x7f800000);   // NaN from 0/0 cannot occur; be safe
+            const long long o = static_cast<long long>(row) * p.nb + b;
+            const float2 ex = __ldcg(p.expd + o);
+            const float4 ws = __ldg(p.wstat + b);
+            float ep = ex.x, es = ex.y;
+            if (p.bsum != nullptr) {
+              const float2 bs = __ldg(p.bsum + b);
+              ep += bs.x;
+              es += bs.y;
+            }
+            const float xn = sqrtf(__ldg(p.row_sq + row));
+            const float prod = p.prod_coef * xn * fmaxf(ws.x, fmaxf(ws.y, ws.z));
+            const float den = sqrtf(Q) * p.out_coef + prod + p.abs_floor;
+            const float dp = fabsf(ep - P), ds = fabsf(es - S);
+            const float worst = Aab * p.out_coef + prod + p.abs_floor;
+            const float zp = fminf(__fdividef(dp, den), __fdividef(dp, worst) * p.zthr);
+            const float zs = __fdividef(ds, den);
+            float z = fmaxf(zp, zs);
+            int which = zs > zp ? 1 : 0;
+            const bool fin_exp = isfinite(ep) && isfinite(es) && isfinite(prod);
+            const bool fin_act = isfinite(P) && isfinite(S) && isfinite(Q) && isfinite(Aab);
+            bool judged = true;
+            if (!fin_exp) {
+              judged = false;
+            } else if (!fin_act) {
+              const float bound = p.bound_coef * xn * ws.w + p.bias_max;
+              if (bound < 1e18f) {
+                z = __int_as_float(0x7f800000);
+                which = 0;
+              } else {
+                judged = false;
+              }
+            } else if (!(z <= 3.0e38f)) {
+              z = __int_as_float(0x7f800000);   // overflow of the ratio: far beyond any noise
+            }
+            if (judged) {
+              const unsigned long long zb = static_cast<unsigned long long>(__float_as_uint(z)) << 32;
+              k0 = zb | ((static_cast<unsigned long long>(o) * 2ull + which) & 0xffffffffull);
+              k1 = zb | __float_as_uint(den);
+            } else {
+              unj = 1;
+            }
           }
-          if (!judged) {
-            ++unj;
-            continue;
-          }
-          const unsigned long long zb = static_cast<unsigned long long>(__float_as_uint(z)) << 32;
-          const unsigned long long flat = static_cast<unsigned long long>(o) * 2ull + which;
-          const unsigned long long a0 = zb | (flat & 0xffffffffull);
-          const unsigned long long a1 = zb | __float_as_uint(den);
-          k0 = a0 > k0 ? a0 : k0;
-          k1 = a1 > k1 ? a1 : k1;
         }
         k0 = warp_max_u64(k0);
         k1 = warp_max_u64(k1);
 #pragma unroll
         for (int m = 16; m > 0; m >>= 1) unj += __shfl_xor_sync(0xffffffffu, unj, m);
         if (lane == 0) {
-          atomicMax(&ctl->key0, k0);
-          atomicMax(&ctl->key1, k1);
-          atomicAdd(&ctl->unj, unj);
+          ctl->wkey0[ew] = k0;
+          ctl->wkey1[ew] = k1;
+          ctl->wunj[ew] = unj;
         }
         named_bar_sync(1, C::NWG * 128);
         if (et == 0) {
-          unsigned long long* st = p.state + static_cast<long long>(p.slot) * 4;
-          atomicMax(st + 0, ctl->key0);
-          atomicMax(st + 1, ctl->key1);
-          if (mt == 0) atomicAdd(st + 2, 1ull);
-          if (ctl->unj) atomicAdd(st + 3, static_cast<unsigned long long>(ctl->unj));
-          p.counters[mt] = 0;   // ready for the next launch
+          unsigned long long a0 = 0ull, a1 = 0ull;
+          int u = 0;
+#pragma unroll
+          for (int w = 0; w < 4 * C::NWG; ++w) {
+            a0 = ctl->wkey0[w] > a0 ? ctl->wkey0[w] : a0;
+            a1 = ctl->wkey1[w] > a1 ? ctl->wkey1[w] : a1;
+            u += ctl->wunj[w];
+          }
+          mbar_wait(&ctl->resempty[acc], acc_phase ^ 1u, abort_flag);
+          ctl->res0[acc] = a0;
+          ctl->res1[acc] = a1;
+          ctl->resunj[acc] = u;
+          mbar_arrive(&ctl->resfull[acc]);   // the coordinator publishes it
         }
+      }
+      if (p.dbg && et == 0) {
+        unsigned long long* d = p.dbg + blockIdx.x * 8;
+        d[0] += t_w1 - t_w0;          // waiting for the accumulator
+        d[1] += globaltimer() - t_w1; // epilogue body (including the wait for expected sums)
+        d[2] += 1;                    // tiles
+      }
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
       }
     }
   }
 
+  if (warp >= 4 && lane == 0) bulk_wait0();   // staging tiles stay valid until their stores are done
   tc_fence_before();
   __syncthreads();
   if (warp == 2) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
+  if (p.dbg && threadIdx.x == 0) p.dbg[blockIdx.x * 8 + 6] = globaltimer();
 }
 
 // ------------------------------------------------------------------------------------------- host side
@@ -470,7 +581,8 @@ static EncodeTiledFn get_encode() {
 }
 
 // 2-D bf16 tensor [rows, cols] with row stride ld (elements), box {64, box_rows}, 128-byte swizzle.
-static bool make_map(CUtensorMap* m, const void* base, long long rows, long long cols, long long ld, int box_rows) {
+static bool make_map(CUtensorMap* m, const void* base, long long rows, long long cols, long long ld, int box_rows,
+                     bool promote = true) {
   EncodeTiledFn enc = get_encode();
   if (!enc) return false;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
@@ -478,7 +590,8 @@ static bool make_map(CUtensorMap* m, const void* base, long long rows, long long
   cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), static_cast<cuuint32_t>(box_rows)};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   promote ? CU_TENSOR_MAP_L2_PROMOTION_L2_256B : CU_TENSOR_MAP_L2_PROMOTION_NONE,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
@@ -495,8 +608,8 @@ static int num_sms_cached() {
 }
 
 template <int BN, bool INJ>
-static int launch(const CUtensorMap& a, const CUtensorMap& w, const CUtensorMap& wc, const Params& p, int grid,
-                  cudaStream_t stream) {
+static int launch(const CUtensorMap& a, const CUtensorMap& w, const CUtensorMap& wc, const CUtensorMap& c,
+                  const Params& p, int grid, cudaStream_t stream) {
   using Cf = Cfg<BN>;
   static bool attr_done = false;
   if (!attr_done) {
@@ -505,7 +618,7 @@ static int launch(const CUtensorMap& a, const CUtensorMap& w, const CUtensorMap&
     if (e != cudaSuccess) return static_cast<int>(e);
     attr_done = true;
   }
-  gemm_abft_kernel<BN, INJ><<<grid, Cf::THREADS, Cf::SMEM_BYTES, stream>>>(a, w, wc, p);
+  gemm_abft_kernel<BN, INJ><<<grid, Cf::THREADS, Cf::SMEM_BYTES, stream>>>(a, w, wc, c, p);
   return static_cast<int>(cudaGetLastError());
 }
 
@@ -516,12 +629,12 @@ using namespace sdc::gemm;
 
 extern "C" {
 
-// Bytes of workspace the checked GEMM needs for an M x N output: a fixed block of arrival counters (one per
-// 128-row band), then per (row, block) four fp32 sums and two fp32 expected values. The counters must be
-// zero before the first launch (every launch leaves them zero).
+// Bytes of workspace the checked GEMM needs for an M x N output: a fixed block of per-band counters, then
+// per (row, block) the two fp32 expected sums. The counters must be zero before the first launch (every
+// launch leaves them zero).
 long long sdc_gemm_ws_bytes(int M, int N) {
   const long long nb = (N + CSW - 1) / CSW;
-  return COUNTER_BYTES + static_cast<long long>(M) * nb * 24 + 256;
+  return COUNTER_BYTES + static_cast<long long>(M) * nb * 8 + 256;
 }
 
 // C[M,N] = A[M,K] @ W[N,K]^T (+ bias): bf16 in/out, fp32 accumulation on tcgen05, with the ABFT check
@@ -532,7 +645,7 @@ int sdc_gemm_bf16(const void* A, long long lda, const void* W, const void* Wc, i
                   const float* wstat, void* ws, unsigned long long* state, int slot, unsigned s0, unsigned s1,
                   unsigned s2, unsigned s3, float zthr, float prod_coef, float out_coef, float abs_floor,
                   float bound_coef, int* err, int bn, int max_ctas, int inj_row, int inj_col, unsigned inj_xor,
-                  void* stream) {
+                  void* dbg, void* stream) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   if ((K % 8) || (N % 8) || (lda % 8) || (ldc % 8) || (bn != 128 && bn != 256)) return -1;
   if ((M + BM - 1) / BM > MAX_BANDS) return -1;
@@ -557,9 +670,9 @@ int sdc_gemm_bf16(const void* A, long long lda, const void* W, const void* Wc, i
   p.row_sq = row_sq;
   p.wstat = reinterpret_cast<const float4*>(wstat);
   uint8_t* wsb = static_cast<uint8_t*>(ws);
-  p.counters = reinterpret_cast<int*>(wsb);
-  p.stats = reinterpret_cast<float4*>(wsb + COUNTER_BYTES);
-  p.expd = reinterpret_cast<float2*>(wsb + COUNTER_BYTES + static_cast<long long>(M) * nb * 16);
+  p.cs_done = reinterpret_cast<int*>(wsb);
+  p.main_done = reinterpret_cast<int*>(wsb + MAX_BANDS * 4);
+  p.expd = reinterpret_cast<float2*>(wsb + COUNTER_BYTES);
   p.state = state;
   p.slot = slot;
   p.sgn[0] = s0;
@@ -575,17 +688,20 @@ int sdc_gemm_bf16(const void* A, long long lda, const void* W, const void* Wc, i
   p.inj_row = inj_row;
   p.inj_col = inj_col;
   p.inj_xor = inj_xor;
-  CUtensorMap ma, mw, mc;
+  p.dbg = static_cast<unsigned long long*>(dbg);
+  CUtensorMap ma, mw, mc, mo;
   if (!make_map(&ma, A, M, K, lda, BM)) return -2;
   if (!make_map(&mw, W, N, K, K, bn)) return -3;
   if (!make_map(&mc, Wc, static_cast<long long>(nb) * CS_ROWS, K, K, p.csb * CS_ROWS)) return -4;
+  if (!make_map(&mo, Cout, M, N, ldc, 32, false)) return -5;
   int grid = p.total_tiles;
   const int cap = max_ctas > 0 ? max_ctas : num_sms_cached();
   if (grid > cap) grid = cap;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool inj = inj_row >= 0;
-  if (bn == 256) return inj ? launch<256, true>(ma, mw, mc, p, grid, st) : launch<256, false>(ma, mw, mc, p, grid, st);
-  return inj ? launch<128, true>(ma, mw, mc, p, grid, st) : launch<128, false>(ma, mw, mc, p, grid, st);
+  if (bn == 256)
+    return inj ? launch<256, true>(ma, mw, mc, mo, p, grid, st) : launch<256, false>(ma, mw, mc, mo, p, grid, st);
+  return inj ? launch<128, true>(ma, mw, mc, mo, p, grid, st) : launch<128, false>(ma, mw, mc, mo, p, grid, st);
 }
 
 }  // extern "C"

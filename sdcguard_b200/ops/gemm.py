@@ -130,7 +130,7 @@ def pick_bn(m: int, n: int, num_sms: int = 148) -> int:
 def checked_linear(x: torch.Tensor, cw: CheckedWeight, state: torch.Tensor, slot: int,
                    row_sq: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
                    z_alarm: float = abft.Z_ALARM, bn: Optional[int] = None, max_ctas: int = 0,
-                   inject: Optional[tuple] = None) -> torch.Tensor:
+                   inject: Optional[tuple] = None, dbg: Optional[torch.Tensor] = None) -> torch.Tensor:
     """y = x @ W^T (+ b) on tcgen05 with the ABFT check folded into `state[slot]`.
     x: (m, k) bf16 with unit column stride. inject=(row, col, xor_bits) flips bits of one fp32 accumulator
     element before the check and the rounding (fault-injection experiments)."""
@@ -159,6 +159,7 @@ def checked_linear(x: torch.Tensor, cw: CheckedWeight, state: torch.Tensor, slot
         None if cw.cs.bsum is None else cw.cs.bsum.data_ptr(), float(cw.cs.bias_max), row_sq.data_ptr(),
         cw.cs.wstat.data_ptr(), ws.data_ptr(), state.data_ptr(), int(slot), s[0], s[1], s[2], s[3],
         float(z_alarm), float(cw.prod_coef), float(cw.out_coef), float(abft.ABS_FLOOR), float(math.sqrt(k)),
-        err.data_ptr(), int(bn), int(max_ctas), inj_row, inj_col, inj_xor, _stream_ptr(dev))
+        err.data_ptr(), int(bn), int(max_ctas), inj_row, inj_col, inj_xor,
+        None if dbg is None else dbg.data_ptr(), _stream_ptr(dev))
     _native.check(rc, "checked GEMM launch")
     return out
