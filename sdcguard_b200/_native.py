@@ -19,6 +19,35 @@ LIB_PATH = _PKG / "_lib" / "libsdcguard_b200.so"
 
 _lock = threading.Lock()
 _lib = None
+_launches = [0]            # kernel launches issued through this module since the last reset
+
+
+class _Counted:
+    """Wraps a ctypes function and counts its calls (each entry point below launches one kernel, except the
+    size queries)."""
+
+    def __init__(self, fn):
+        self._fn = fn
+
+    def __call__(self, *a):
+        _launches[0] += 1
+        return self._fn(*a)
+
+
+class _Lib:
+    def __init__(self, handle):
+        self._h = handle
+
+    def __getattr__(self, name):
+        return getattr(self._h, name)
+
+
+def launch_count() -> int:
+    return _launches[0]
+
+
+def reset_launch_count() -> None:
+    _launches[0] = 0
 
 P = c_void_p
 I = c_int
@@ -32,6 +61,12 @@ SIGNATURES: dict[str, tuple] = {
     "sdc_gemm_bf16": (I, [P, L, P, P, I, I, I, P, L, P, P, F, P, P, P, P, I, U, U, U, U, F, F, F, F, F, P, I, I, I, I,
                           U, P, P]),
     "sdc_row_sqnorm_bf16": (I, [P, L, I, I, P, P]),
+    "sdc_add_rmsnorm_bf16": (I, [P, P, P, F, I, I, P, P, P, P, P]),
+    "sdc_qk_norm_rope_kv": (I, [P, L, I, I, I, I, P, P, P, P, F, P, P, P, P, P, P]),
+    "sdc_silu_mul_bf16": (I, [P, I, I, P, P, P, P]),
+    "sdc_compare_rows_bf16": (I, [P, L, P, P, L, I, I, P, P]),
+    "sdc_attn_prefill": (I, [P, P, P, P, I, P, P, I, P, I, I, I, F, P, P]),
+    "sdc_attn_decode": (I, [P, P, P, P, I, P, P, P, I, I, I, I, I, F, P, P]),
 }
 
 
@@ -61,13 +96,16 @@ def lib():
                 if not LIB_PATH.exists():
                     raise RuntimeError(f"sdcguard_b200 native library missing and could not be built: {e}") from e
         h = ctypes.CDLL(str(LIB_PATH))
+        wrapped = _Lib(h)
         for name, (res, args) in SIGNATURES.items():
             fn = getattr(h, name, None)
             if fn is None:
                 raise RuntimeError(f"{LIB_PATH.name} lacks {name}: rebuild with python -m sdcguard_b200._build")
             fn.restype = res
             fn.argtypes = args
-        _lib = h
+            if not name.endswith("_bytes"):
+                setattr(wrapped, name, _Counted(fn))
+        _lib = wrapped
         return _lib
 
 

@@ -1,0 +1,262 @@
+"""Decoder-only transformer (Llama / Qwen3 family) running on this library's sm_100a kernels, with every
+GEMM checked by the fused ABFT epilogue and the other ops checked by exact replay of a rotating sample of rows.
+
+Per layer (rows = tokens of the batch):
+    h, y  = add_rmsnorm(prev, h)                    replay-checked on sampled rows
+    qkv   = checked GEMM  y @ Wqkv^T                ABFT, every row
+    q,k,v = qk_norm + RoPE, k/v -> paged cache      replay in compare mode (q bits, cache bits, slot mapping)
+    o     = paged attention (prefill or decode)      replay-checked on sampled rows
+    a     = checked GEMM  o @ Wo^T                  ABFT
+    h, y2 = add_rmsnorm(a, h)                       replay-checked
+    gu    = checked GEMM  y2 @ Wgu^T                ABFT
+    act   = silu(g) * u                             replay-checked
+    out   = checked GEMM  act @ Wdown^T             ABFT
+then the final norm and the checked LM-head GEMM on the rows whose next token is needed.
+
+`checked=False` runs the same model with cuBLAS GEMMs (torch.matmul) and no checks: the unchecked baseline.
+
+Weights are random (N(0, 0.02) for matrices, ones for norms): the benchmarks use synthetic data of the named
+shapes. Reference: the guarded serving path of src/sdcguard/serve.py (ServeGuard.attach / check_static) and the
+vLLM integration points of src/sdcguard/vllm_plugin.py:2315-2501; here the model itself is the engine.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+from typing import Optional
+
+import torch
+
+from ..numerics import abft
+from ..ops import attention, gemm, layers
+
+
+@dataclass(frozen=True)
+class DecoderConfig:
+    name: str
+    layers: int
+    hidden: int
+    heads: int
+    kv_heads: int
+    head_dim: int
+    intermediate: int
+    vocab: int
+    rope_theta: float
+    rms_eps: float
+    qk_norm: bool
+    tie_embeddings: bool = False
+    rope_scaling: Optional[dict] = None
+    max_position: int = 8192
+
+
+QWEN3_0_6B = DecoderConfig("Qwen3-0.6B", 28, 1024, 16, 8, 128, 3072, 151936, 1_000_000.0, 1e-6, True,
+                           tie_embeddings=True, max_position=40960)
+LLAMA3_8B = DecoderConfig("Llama-3-8B", 32, 4096, 32, 8, 128, 14336, 128256, 500_000.0, 1e-5, False,
+                          rope_scaling=None, max_position=8192)
+TINY = DecoderConfig("tiny", 2, 256, 4, 2, 128, 512, 1024, 10_000.0, 1e-6, True, max_position=4096)
+
+CONFIGS = {c.name: c for c in (QWEN3_0_6B, LLAMA3_8B, TINY)}
+
+
+@dataclass
+class StepMeta:
+    """Device-side description of one forward step (prefill batch or decode step)."""
+    mode: str                         # "prefill" or "decode"
+    tokens: torch.Tensor              # (T,) int64 input ids
+    pos: torch.Tensor                 # (T,) int32 positions
+    slots: torch.Tensor               # (T,) int64 KV slots (block * 16 + offset)
+    block_table: torch.Tensor         # (R, max_pages) int32
+    logits_rows: torch.Tensor         # (L,) int64 rows whose next token is computed
+    tiles: Optional[torch.Tensor] = None        # prefill tiles (n, 4) int32
+    seq_req: Optional[torch.Tensor] = None      # decode: (B,) int32 block-table row
+    ctx: Optional[torch.Tensor] = None          # decode: (B,) int32 keys per sequence
+    max_ctx: int = 0
+    # replay sample (checked mode): rows and their attention replay description
+    sample_rows: Optional[torch.Tensor] = None  # (S,) int32
+    sample_tiles: Optional[torch.Tensor] = None  # prefill replay tiles
+    sample_idx: Optional[torch.Tensor] = None   # prefill replay token list (same rows, tile order)
+
+
+def _init_linear(n: int, k: int, gen: torch.Generator, device) -> torch.Tensor:
+    w = torch.empty(n, k, dtype=torch.float32, device="cpu").normal_(0.0, 0.02, generator=gen)
+    return w.to(device=device, dtype=torch.bfloat16)
+
+
+@dataclass
+class LayerWeights:
+    ln1: torch.Tensor
+    ln2: torch.Tensor
+    qkv: torch.Tensor
+    o: torch.Tensor
+    gate_up: torch.Tensor
+    down: torch.Tensor
+    q_norm: Optional[torch.Tensor] = None
+    k_norm: Optional[torch.Tensor] = None
+    cw: dict = field(default_factory=dict)   # name -> gemm.CheckedWeight
+
+
+class CheckedDecoder:
+    """The model plus its check state. Slots of the state table name each checked op (`state.names`)."""
+
+    def __init__(self, cfg: DecoderConfig, device="cuda", checked: bool = True, seed: int = 0,
+                 weights: Optional[dict] = None, tp_rank: int = 0, tp_size: int = 1):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.checked = checked
+        self.nq = cfg.heads // tp_size
+        self.nkv = max(1, cfg.kv_heads // tp_size)
+        self.inter = cfg.intermediate // tp_size
+        d = cfg.head_dim
+        gen = torch.Generator().manual_seed(seed)
+        dev = self.device
+        self.embed = _init_linear(cfg.vocab, cfg.hidden, gen, dev)
+        self.final_ln = torch.ones(cfg.hidden, dtype=torch.bfloat16, device=dev)
+        self.lm_head = self.embed if cfg.tie_embeddings else _init_linear(cfg.vocab, cfg.hidden, gen, dev)
+        self.layers: list[LayerWeights] = []
+        for _ in range(cfg.layers):
+            lw = LayerWeights(
+                ln1=torch.ones(cfg.hidden, dtype=torch.bfloat16, device=dev),
+                ln2=torch.ones(cfg.hidden, dtype=torch.bfloat16, device=dev),
+                qkv=_init_linear((self.nq + 2 * self.nkv) * d, cfg.hidden, gen, dev),
+                o=_init_linear(cfg.hidden, self.nq * d, gen, dev),
+                gate_up=_init_linear(2 * self.inter, cfg.hidden, gen, dev),
+                down=_init_linear(cfg.hidden, self.inter, gen, dev),
+                q_norm=torch.ones(d, dtype=torch.bfloat16, device=dev) if cfg.qk_norm else None,
+                k_norm=torch.ones(d, dtype=torch.bfloat16, device=dev) if cfg.qk_norm else None,
+            )
+            self.layers.append(lw)
+        self.rope = layers.rope_table(min(cfg.max_position, 16384), d, cfg.rope_theta, cfg.rope_scaling, device=dev)
+        self.state = gemm.StateTable(dev, 16 * cfg.layers + 8)
+        self.slot: dict[str, int] = {}
+        if checked:
+            for i, lw in enumerate(self.layers):
+                for name in ("qkv", "o", "gate_up", "down"):
+                    cw = gemm.CheckedWeight(getattr(lw, name))
+                    lw.cw[name] = cw
+                    self.slot[f"L{i}.{name}"] = self.state.add(f"layers.{i}.{name} (ABFT GEMM)", cw.nb)
+                for name in ("norm1", "rope_kv", "attn", "norm2", "act"):
+                    self.slot[f"L{i}.{name}"] = self.state.add(f"layers.{i}.{name} (replay)", 1)
+            self.lm_cw = gemm.CheckedWeight(self.lm_head)
+            self.slot["lm_head"] = self.state.add("lm_head (ABFT GEMM)", self.lm_cw.nb)
+            self.slot["final_norm"] = self.state.add("final_norm (replay)", 1)
+        self._bufs: dict = {}
+
+    # ---------------------------------------------------------------- buffers
+    def buffers(self, T: int) -> dict:
+        """Scratch activations for up to T rows, reused across steps (views keep their data pointers)."""
+        b = self._bufs.get("cap", 0)
+        if T <= b:
+            return self._bufs
+        cfg, dev, bf = self.cfg, self.device, torch.bfloat16
+        H, D = cfg.hidden, cfg.head_dim
+        nq, nkv = self.nq, self.nkv
+        self._bufs = dict(
+            cap=T,
+            x=torch.empty(T, H, dtype=bf, device=dev),
+            resid=torch.empty(T, H, dtype=bf, device=dev),
+            y=torch.empty(T, H, dtype=bf, device=dev),
+            rs=torch.empty(T, dtype=torch.float32, device=dev),
+            qkv=torch.empty(T, (nq + 2 * nkv) * D, dtype=bf, device=dev),
+            q=torch.empty(T, nq, D, dtype=bf, device=dev),
+            attn=torch.empty(T, nq, D, dtype=bf, device=dev),
+            attn_rep=torch.empty(T, nq, D, dtype=bf, device=dev),
+            ors=torch.empty(T, dtype=torch.float32, device=dev),
+            a=torch.empty(T, H, dtype=bf, device=dev),
+            gu=torch.empty(T, 2 * self.inter, dtype=bf, device=dev),
+            act=torch.empty(T, self.inter, dtype=bf, device=dev),
+            y_rep=torch.empty(max(1, T // 32 + 64), H, dtype=bf, device=dev),
+            act_rep=torch.empty(max(1, T // 32 + 64), self.inter, dtype=bf, device=dev),
+            rs_rep=torch.empty(max(1, T // 32 + 64), dtype=torch.float32, device=dev),
+        )
+        if self.checked:
+            gemm.reserve_workspace(dev, T, max(2 * self.inter, (nq + 2 * nkv) * D, H))
+            gemm.reserve_workspace(dev, min(T, 1024), cfg.vocab)
+        return self._bufs
+
+    # ---------------------------------------------------------------- ops
+    def _linear(self, x, w, cw, name, out, row_sq):
+        if not self.checked:
+            return torch.matmul(x, w.t(), out=out)
+        return gemm.checked_linear(x, cw, self.state.state, self.slot[name], row_sq=row_sq, out=out)
+
+    def _st(self, name) -> torch.Tensor:
+        return self.state.state[self.slot[name]]
+
+    def forward(self, meta: StepMeta, cache: torch.Tensor) -> torch.Tensor:
+        """Runs one step; returns logits (L, vocab) bf16 for meta.logits_rows. cache: (layers, blocks, 2, nkv,
+        16, 128) bf16."""
+        cfg = self.cfg
+        T = meta.tokens.shape[0]
+        B = self.buffers(T)
+        x, resid, y, rs = B["x"][:T], B["resid"][:T], B["y"][:T], B["rs"][:T]
+        qkv, q, att, ors = B["qkv"][:T], B["q"][:T], B["attn"][:T], B["ors"][:T]
+        a, gu, act = B["a"][:T], B["gu"][:T], B["act"][:T]
+        torch.index_select(self.embed, 0, meta.tokens, out=x)
+        S = meta.sample_rows
+        chk = self.checked and S is not None and S.numel() > 0
+        s_n = S.shape[0] if chk else 0
+        nq, nkv, D = self.nq, self.nkv, cfg.head_dim
+        for i, lw in enumerate(self.layers):
+            lc = cache[i]
+            if i == 0:
+                layers.add_rmsnorm(x, lw.ln1, cfg.rms_eps, residual=None, resid_out=resid, out=y, row_sq=rs)
+            else:
+                layers.add_rmsnorm(x, lw.ln1, cfg.rms_eps, residual=resid, resid_out=resid, out=y, row_sq=rs)
+            if chk:
+                yr, _ = layers.add_rmsnorm(resid, lw.ln1, cfg.rms_eps, out=B["y_rep"][:s_n], row_sq=B["rs_rep"][:s_n],
+                                           rows=S)
+                layers.compare_rows(y, S, yr, self._st(f"L{i}.norm1"))
+            self._linear(y, lw.qkv, lw.cw.get("qkv"), f"L{i}.qkv", qkv, rs)
+            layers.qk_norm_rope_kv(qkv, nq, nkv, meta.pos, meta.slots, lw.q_norm, lw.k_norm, cfg.rms_eps, self.rope,
+                                   q, lc)
+            if chk:
+                layers.qk_norm_rope_kv(qkv, nq, nkv, meta.pos, meta.slots, lw.q_norm, lw.k_norm, cfg.rms_eps,
+                                       self.rope, q, lc, rows=S, check=self._st(f"L{i}.rope_kv"))
+            ors.zero_()
+            if meta.mode == "prefill":
+                attention.prefill(q, lc, meta.block_table, meta.pos, meta.tiles, nq, nkv, out=att, row_sq=ors)
+                if chk:
+                    rep = B["attn_rep"][:T]
+                    attention.prefill(q, lc, meta.block_table, meta.pos, meta.sample_tiles, nq, nkv, out=rep,
+                                      row_idx=meta.sample_idx)
+                    layers.compare_rows(att.view(T, -1), meta.sample_idx, rep.view(T, -1).index_select(
+                        0, meta.sample_idx), self._st(f"L{i}.attn"))
+            else:
+                attention.decode(q, lc, meta.block_table, meta.seq_req, meta.ctx, nq, nkv, meta.max_ctx, out=att,
+                                 row_sq=ors)
+                if chk:
+                    rep = B["attn_rep"][:T]
+                    attention.decode(q, lc, meta.block_table, meta.seq_req, meta.ctx, nq, nkv, meta.max_ctx,
+                                     out=rep, seq_idx=S)
+                    layers.compare_rows(att.view(T, -1), S, rep.view(T, -1).index_select(0, S),
+                                        self._st(f"L{i}.attn"))
+            self._linear(att.view(T, nq * D), lw.o, lw.cw.get("o"), f"L{i}.o", a, ors)
+            layers.add_rmsnorm(a, lw.ln2, cfg.rms_eps, residual=resid, resid_out=resid, out=y, row_sq=rs)
+            if chk:
+                yr, _ = layers.add_rmsnorm(resid, lw.ln2, cfg.rms_eps, out=B["y_rep"][:s_n], row_sq=B["rs_rep"][:s_n],
+                                           rows=S)
+                layers.compare_rows(y, S, yr, self._st(f"L{i}.norm2"))
+            self._linear(y, lw.gate_up, lw.cw.get("gate_up"), f"L{i}.gate_up", gu, rs)
+            layers.silu_mul(gu, out=act, row_sq=rs)
+            if chk:
+                ar, _ = layers.silu_mul(gu, out=B["act_rep"][:s_n], row_sq=B["rs_rep"][:s_n], rows=S)
+                layers.compare_rows(act, S, ar, self._st(f"L{i}.act"))
+            self._linear(act, lw.down, lw.cw.get("down"), f"L{i}.down", x, rs)
+        # final norm on the rows that produce tokens, then the LM head
+        L = meta.logits_rows.shape[0]
+        xs = x.index_select(0, meta.logits_rows)
+        rsd = resid.index_select(0, meta.logits_rows)
+        yl, rsl = layers.add_rmsnorm(xs, self.final_ln, cfg.rms_eps, residual=rsd, resid_out=rsd)
+        if self.checked:
+            one = torch.zeros(1, dtype=torch.int32, device=self.device)
+            yr, _ = layers.add_rmsnorm(rsd, self.final_ln, cfg.rms_eps, rows=one)
+            layers.compare_rows(yl, one, yr, self._st("final_norm"))
+        logits = torch.empty(L, cfg.vocab, dtype=torch.bfloat16, device=self.device)
+        if self.checked:
+            gemm.checked_linear(yl, self.lm_cw, self.state.state, self.slot["lm_head"], row_sq=rsl, out=logits)
+        else:
+            torch.matmul(yl, self.lm_head.t(), out=logits)
+        return logits
+
+    def read_checks(self, reset: bool = False) -> list[dict]:
+        return self.state.read(reset=reset)

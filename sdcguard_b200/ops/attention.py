@@ -1,0 +1,93 @@
+"""Paged attention entry points (`csrc/attention.cu`): causal prefill over a batch of requests and single-token
+decode, both over a paged KV cache with 16-token pages, plus the host-side tiling of prefill work.
+
+Rows of both kernels are deterministic (see the kernel file), so `replay_*` recompute a sample of rows on
+separate CTAs and `ops.layers.compare_rows` checks them bit for bit. The reference samples (token, head) pairs
+and recomputes them in fp32 against an error bound (src/sdcguard/serve_attn.py:5-48, `attn_check_triton`
+:574); the replay needs no bound, so every flipped bit in a sampled row is seen.
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional, Sequence
+
+import torch
+
+from .. import _native
+
+ROWS = 128
+
+
+def _s(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def prefill_tiles(q_starts: Sequence[int], q_lens: Sequence[int], group: int) -> torch.Tensor:
+    """(n, 4) int32 tiles (request, first token, tokens, -1) covering every request's new tokens, ordered
+    longest-running first (later tiles of a causal prompt attend to more keys)."""
+    tpc = ROWS // group
+    tiles = []
+    for r, (s, n) in enumerate(zip(q_starts, q_lens)):
+        for off in range(0, n, tpc):
+            tiles.append((r, s + off, min(tpc, n - off), -1))
+    tiles.sort(key=lambda t: -(t[1]))
+    return torch.tensor(tiles, dtype=torch.int32).view(-1, 4)
+
+
+def replay_tiles(sampled: Sequence[Sequence[int]], group: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """Tiles for a replay of sampled tokens: sampled[r] lists request r's sampled token indices."""
+    tpc = ROWS // group
+    tiles, idx = [], []
+    for r, toks in enumerate(sampled):
+        for off in range(0, len(toks), tpc):
+            chunk = list(toks[off:off + tpc])
+            tiles.append((r, 0, len(chunk), len(idx)))
+            idx.extend(chunk)
+    t = torch.tensor(tiles, dtype=torch.int32).view(-1, 4)
+    return t, torch.tensor(idx, dtype=torch.int32)
+
+
+def prefill(q: torch.Tensor, cache: torch.Tensor, block_table: torch.Tensor, pos: torch.Tensor,
+            tiles: torch.Tensor, nq: int, nkv: int, out: Optional[torch.Tensor] = None,
+            row_idx: Optional[torch.Tensor] = None, row_sq: Optional[torch.Tensor] = None,
+            scale: Optional[float] = None) -> torch.Tensor:
+    """q: (T, nq, 128) bf16; tiles/row_idx/pos/block_table int32 on the device. out: (T, nq, 128) or, for a
+    replay, any tensor indexed by the same token ids."""
+    if out is None:
+        out = torch.empty_like(q)
+    scale = 1.0 / math.sqrt(128) if scale is None else scale
+    _native.check(_native.lib().sdc_attn_prefill(
+        q.data_ptr(), out.data_ptr(), cache.data_ptr(), block_table.data_ptr(), block_table.shape[1],
+        pos.data_ptr(), tiles.data_ptr(), tiles.shape[0], None if row_idx is None else row_idx.data_ptr(), nq, nkv,
+        128, float(scale), None if row_sq is None else row_sq.data_ptr(), _s(q)), "attention prefill")
+    return out
+
+
+def decode(q: torch.Tensor, cache: torch.Tensor, block_table: torch.Tensor, seq_req: torch.Tensor,
+           ctx: torch.Tensor, nq: int, nkv: int, max_ctx: int, out: Optional[torch.Tensor] = None,
+           seq_idx: Optional[torch.Tensor] = None, nseq: Optional[int] = None,
+           row_sq: Optional[torch.Tensor] = None, scale: Optional[float] = None) -> torch.Tensor:
+    """q: (B, nq, 128); one CTA per (sequence, kv head). seq_idx selects sequences to run (replay)."""
+    if out is None:
+        out = torch.empty_like(q)
+    scale = 1.0 / math.sqrt(128) if scale is None else scale
+    n = nseq if nseq is not None else (seq_idx.shape[0] if seq_idx is not None else q.shape[0])
+    _native.check(_native.lib().sdc_attn_decode(
+        q.data_ptr(), out.data_ptr(), cache.data_ptr(), block_table.data_ptr(), block_table.shape[1],
+        seq_req.data_ptr(), ctx.data_ptr(), None if seq_idx is None else seq_idx.data_ptr(), n, nq, nkv, 128,
+        int(max_ctx), float(scale), None if row_sq is None else row_sq.data_ptr(), _s(q)), "attention decode")
+    return out
+
+
+def reference_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_pos: torch.Tensor) -> torch.Tensor:
+    """fp32 reference for one request: q (t, nq, d), k/v (n, nkv, d), causal by absolute positions."""
+    nq, nkv = q.shape[1], k.shape[1]
+    g = nq // nkv
+    kf = k.float().repeat_interleave(g, dim=1)
+    vf = v.float().repeat_interleave(g, dim=1)
+    s = torch.einsum("thd,nhd->htn", q.float(), kf) / math.sqrt(q.shape[-1])
+    keys = torch.arange(k.shape[0], device=q.device)
+    mask = keys[None, :] > q_pos[:, None]
+    s = s.masked_fill(mask[None], float("-inf"))
+    p = torch.softmax(s, dim=-1)
+    return torch.einsum("htn,nhd->thd", p, vf)

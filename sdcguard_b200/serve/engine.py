@@ -1,0 +1,262 @@
+"""Single-GPU serving engine for the checked decoder: paged KV cache with 16-token pages, prefill batches
+bounded by a token budget, then batched decode replayed from a CUDA graph, with the generated tokens kept on
+the device until the end of the call (no host synchronisation per step).
+
+    eng = LLMEngine(QWEN3_0_6B, checked=True)
+    out = eng.generate(prompts, prompt_lens, max_new_tokens=128)   # pinned int64 host tensors in, host out
+    report = eng.guard.poll()                                       # check results (see serve/guard.py)
+
+Checks in every step (checked=True): ABFT on every GEMM row; exact replay of a rotating 1/`sample_every`
+sample of rows for the norms, the q/k norm + RoPE + KV-cache write, attention and the activation.
+
+Reference: the serving stack is vLLM in the reference (src/sdcguard/vllm_plugin.py, `GPUModelRunner.execute_model`
+patch :2430-2501 with mark_step/poll); here the engine is this package's own, with the same hook points
+(`serve.plugin`).
+"""
+from __future__ import annotations
+
+import math
+import time
+from dataclasses import dataclass
+from typing import Optional, Sequence
+
+import torch
+
+from ..models.decoder import CheckedDecoder, DecoderConfig, StepMeta
+from ..ops import attention
+from .guard import ServeGuard
+
+PAGE = 16
+
+
+class BlockAllocator:
+    """Free list of KV pages (page 0 is reserved as a never-read zero page)."""
+
+    def __init__(self, num_blocks: int):
+        self.num_blocks = num_blocks
+        self.free = list(range(num_blocks - 1, 0, -1))
+
+    def alloc(self, n: int) -> list[int]:
+        if n > len(self.free):
+            raise RuntimeError(f"KV cache full: need {n} pages, {len(self.free)} free")
+        out = [self.free.pop() for _ in range(n)]
+        return out
+
+    def release(self, pages: Sequence[int]) -> None:
+        self.free.extend(reversed(list(pages)))
+
+
+def kv_bytes_per_page(cfg: DecoderConfig, nkv: int) -> int:
+    return cfg.layers * 2 * nkv * PAGE * cfg.head_dim * 2
+
+
+class LLMEngine:
+    def __init__(self, cfg: DecoderConfig, device="cuda", checked: bool = True, num_blocks: Optional[int] = None,
+                 max_prefill_tokens: int = 16384, max_num_seqs: int = 256, sample_every: int = 64,
+                 cuda_graph: bool = True, seed: int = 0, kv_fraction: float = 0.6, model: Optional[CheckedDecoder] = None):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.model = model or CheckedDecoder(cfg, self.device, checked=checked, seed=seed)
+        self.checked = self.model.checked
+        self.max_prefill_tokens = max_prefill_tokens
+        self.max_num_seqs = max_num_seqs
+        self.sample_every = sample_every
+        self.cuda_graph = cuda_graph
+        if num_blocks is None:
+            free, _ = torch.cuda.mem_get_info(self.device)
+            num_blocks = int(free * kv_fraction) // kv_bytes_per_page(cfg, self.model.nkv)
+        self.cache = torch.zeros(cfg.layers, num_blocks, 2, self.model.nkv, PAGE, cfg.head_dim,
+                                 dtype=torch.bfloat16, device=self.device)
+        self.alloc = BlockAllocator(num_blocks)
+        self.guard = ServeGuard(self.model)
+        # every activation buffer and the GEMM workspace are sized once, before any CUDA graph is captured
+        self.model.buffers(max(max_prefill_tokens, max_num_seqs))
+        self._graphs: dict = {}
+        self._graph_kernels: dict = {}     # graph key -> this library's kernels captured in it
+        self._graph_replayed = 0           # kernels of this library executed by graph replays
+        self.step_counter = 0
+        self.stats = {"prefill_tokens": 0, "decode_tokens": 0, "steps": 0}
+
+    # ---------------------------------------------------------------- sampling of replay rows
+    def _sample(self, n: int) -> list[int]:
+        salt = self.step_counter % self.sample_every
+        return [r for r in range(n) if (r + salt) % self.sample_every == 0]
+
+    # ---------------------------------------------------------------- prefill
+    def _prefill_batch(self, reqs: list[int], prompts_dev: torch.Tensor, plens: list[int], bt_dev: torch.Tensor,
+                       bt_host: list[list[int]], out_tokens: torch.Tensor) -> None:
+        dev = self.device
+        toks, pos, slots, starts, lens, last = [], [], [], [], [], []
+        t0 = 0
+        for r in reqs:
+            n = plens[r]
+            starts.append(t0)
+            lens.append(n)
+            pos.extend(range(n))
+            pages = bt_host[r]
+            slots.extend(pages[p // PAGE] * PAGE + p % PAGE for p in range(n))
+            t0 += n
+            last.append(t0 - 1)
+        T = t0
+        rows_req = torch.tensor(reqs, dtype=torch.long)
+        tok_dev = torch.cat([prompts_dev[r, :plens[r]] for r in reqs])
+        group = self.model.nq // self.model.nkv
+        tiles = attention.prefill_tiles(starts, lens, group)
+        # the tiles index block-table rows of this batch: gather those rows
+        bt_b = bt_dev.index_select(0, rows_req.to(dev))
+        meta = StepMeta(
+            mode="prefill", tokens=tok_dev,
+            pos=torch.tensor(pos, dtype=torch.int32).to(dev, non_blocking=True),
+            slots=torch.tensor(slots, dtype=torch.int64).to(dev, non_blocking=True),
+            block_table=bt_b, logits_rows=torch.tensor(last, dtype=torch.int64).to(dev, non_blocking=True),
+            tiles=tiles.to(dev, non_blocking=True))
+        if self.checked:
+            samp = self._sample(T)
+            per_req: list[list[int]] = [[] for _ in reqs]
+            ri = 0
+            for tkn in samp:
+                while tkn >= starts[ri] + lens[ri]:
+                    ri += 1
+                per_req[ri].append(tkn)
+            rt, ridx = attention.replay_tiles(per_req, group)
+            meta.sample_rows = torch.tensor(samp, dtype=torch.int32).to(dev, non_blocking=True)
+            meta.sample_tiles = rt.to(dev, non_blocking=True)
+            meta.sample_idx = ridx.to(dev, non_blocking=True)
+        logits = self.model.forward(meta, self.cache)
+        nxt = torch.argmax(logits, dim=-1)
+        out_tokens.index_put_((rows_req.to(dev), torch.zeros(len(reqs), dtype=torch.long, device=dev)), nxt)
+        self.step_counter += 1
+        self.stats["prefill_tokens"] += T
+        self.stats["steps"] += 1
+
+    # ---------------------------------------------------------------- decode
+    def _decode_graph(self, B: int, max_pages: int, max_ctx: int, S: int):
+        key = (B, max_pages, max_ctx, S)
+        g = self._graphs.get(key)
+        if g is not None:
+            return g
+        dev = self.device
+        st = dict(
+            tokens=torch.zeros(B, dtype=torch.long, device=dev),
+            pos=torch.zeros(B, dtype=torch.int32, device=dev),
+            slots=torch.zeros(B, dtype=torch.int64, device=dev),
+            ctx=torch.ones(B, dtype=torch.int32, device=dev),
+            seq_req=torch.arange(B, dtype=torch.int32, device=dev),
+            bt=torch.zeros(B, max_pages, dtype=torch.int32, device=dev),
+            rows=torch.arange(B, dtype=torch.long, device=dev),
+            sample=torch.zeros(max(S, 1), dtype=torch.int32, device=dev),
+        )
+        meta = StepMeta(mode="decode", tokens=st["tokens"], pos=st["pos"], slots=st["slots"], block_table=st["bt"],
+                        logits_rows=st["rows"], seq_req=st["seq_req"], ctx=st["ctx"], max_ctx=max_ctx,
+                        sample_rows=st["sample"] if (self.checked and S > 0) else None)
+        self.model.buffers(B)
+
+        def run():
+            logits = self.model.forward(meta, self.cache)
+            return torch.argmax(logits, dim=-1)
+
+        if not self.cuda_graph:
+            g = (None, st, run)
+            self._graphs[key] = g
+            return g
+        # warm up outside the graph (lazy module loading, workspace sizing), on a side stream as capture requires
+        s = torch.cuda.Stream(device=dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            run()
+        torch.cuda.current_stream(dev).wait_stream(s)
+        graph = torch.cuda.CUDAGraph()
+        from .. import _native
+        n0 = _native.launch_count()
+        with torch.cuda.graph(graph):
+            out = run()
+        # captured calls are not launches; they run at every replay
+        self._graph_kernels[key] = _native.launch_count() - n0
+        _native._launches[0] = n0
+        g = (graph, st, out)
+        self._graphs[key] = g
+        return g
+
+    def _decode(self, plens: list[int], bt_dev: torch.Tensor, out_tokens: torch.Tensor, max_new: int) -> None:
+        dev = self.device
+        N = len(plens)
+        for b0 in range(0, N, self.max_num_seqs):
+            idx = list(range(b0, min(N, b0 + self.max_num_seqs)))
+            B = len(idx)
+            max_pages = bt_dev.shape[1]
+            max_ctx = max(plens[r] for r in idx) + max_new
+            max_ctx = -(-max_ctx // 256) * 256
+            S = -(-B // self.sample_every) if self.checked else 0
+            graph, st, out = self._decode_graph(B, max_pages, max_ctx, S)
+            rows = torch.tensor(idx, dtype=torch.long, device=dev)
+            st["bt"].copy_(bt_dev.index_select(0, rows))
+            pl = torch.tensor([plens[r] for r in idx], dtype=torch.int64, device=dev)
+            steps = torch.arange(max_new - 1, dtype=torch.int64, device=dev)
+            pos_all = pl[None, :] + steps[:, None]                       # (steps, B)
+            pages = st["bt"].long().gather(1, (pos_all // PAGE).t()).t()  # (steps, B)
+            slots_all = pages * PAGE + pos_all % PAGE
+            samples = []
+            for s in range(max_new - 1):
+                salt = (self.step_counter + s) % self.sample_every
+                sm = [b for b in range(B) if (b + salt) % self.sample_every == 0]
+                sm = (sm + sm[:1] * S)[:S] if sm else [0] * S
+                samples.append(sm)
+            samp_all = torch.tensor(samples, dtype=torch.int32).to(dev) if S else None
+            for s in range(max_new - 1):
+                st["tokens"].copy_(out_tokens.index_select(0, rows)[:, s])
+                st["pos"].copy_(pos_all[s])
+                st["slots"].copy_(slots_all[s])
+                st["ctx"].copy_(pos_all[s] + 1)
+                if S:
+                    st["sample"].copy_(samp_all[s])
+                if graph is not None:
+                    graph.replay()
+                    self._graph_replayed += self._graph_kernels[(B, max_pages, max_ctx, S)]
+                    nxt = out
+                else:
+                    nxt = out()
+                out_tokens[rows, s + 1] = nxt
+            self.step_counter += max_new - 1
+            self.stats["decode_tokens"] += B * (max_new - 1)
+            self.stats["steps"] += max_new - 1
+
+    def graph_launches(self) -> int:
+        """This library's kernels executed by CUDA-graph replays so far (eager launches are counted by
+        sdcguard_b200._native.launch_count)."""
+        return self._graph_replayed
+
+    # ---------------------------------------------------------------- public API
+    def generate(self, prompts: torch.Tensor, prompt_lens: Sequence[int], max_new_tokens: int) -> torch.Tensor:
+        """prompts: (N, max_len) int64 token ids (ideally pinned host memory); returns (N, max_new_tokens) int64
+        generated ids on the host. Greedy decoding, no early stop (synthetic workloads)."""
+        dev = self.device
+        N = prompts.shape[0]
+        plens = [int(x) for x in prompt_lens]
+        prompts_dev = prompts.to(dev, non_blocking=True)
+        need = [-(-(n + max_new_tokens) // PAGE) for n in plens]
+        bt_host = [self.alloc.alloc(k) for k in need]
+        max_pages = max(need)
+        bt = torch.zeros(N, max_pages, dtype=torch.int32)
+        for r, pg in enumerate(bt_host):
+            bt[r, :len(pg)] = torch.tensor(pg, dtype=torch.int32)
+        bt_dev = bt.to(dev, non_blocking=True)
+        out_tokens = torch.zeros(N, max_new_tokens, dtype=torch.long, device=dev)
+        try:
+            batch, ntok = [], 0
+            for r in range(N):
+                if batch and ntok + plens[r] > self.max_prefill_tokens:
+                    self._prefill_batch(batch, prompts_dev, plens, bt_dev, bt_host, out_tokens)
+                    batch, ntok = [], 0
+                batch.append(r)
+                ntok += plens[r]
+            if batch:
+                self._prefill_batch(batch, prompts_dev, plens, bt_dev, bt_host, out_tokens)
+            if max_new_tokens > 1:
+                self._decode(plens, bt_dev, out_tokens, max_new_tokens)
+            host = torch.empty(N, max_new_tokens, dtype=torch.long, pin_memory=True)
+            host.copy_(out_tokens, non_blocking=True)
+            torch.cuda.current_stream(dev).synchronize()
+            return host
+        finally:
+            for pg in bt_host:
+                self.alloc.release(pg)

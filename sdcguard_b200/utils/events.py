@@ -1,0 +1,96 @@
+"""Alert events and their log: the record every detector emits (schema of src/sdcguard/events.py:44-87 kept so
+tooling that reads the reference's JSONL alert logs reads these too), device identity for pulling the bad GPU,
+and the rollback-checkpoint rule (src/sdcguard/events.py:90-103)."""
+from __future__ import annotations
+
+import json
+import logging
+import os
+import socket
+import time
+from dataclasses import asdict, dataclass, field
+from typing import Optional
+
+log = logging.getLogger("sdcguard")
+
+
+def device_identity(device=None) -> dict:
+    """Host, rank, and (for a CUDA device) name, UUID, PCI bus id and physical index of the GPU."""
+    import torch
+    info: dict = {"host": socket.gethostname(), "rank": None, "device": None, "gpu_uuid": None}
+    try:
+        import torch.distributed as dist
+        if dist.is_available() and dist.is_initialized():
+            info["rank"] = dist.get_rank()
+    except Exception:  # noqa: BLE001
+        pass
+    if device is None:
+        return info
+    dev = torch.device(device)
+    info["device"] = str(dev)
+    if dev.type != "cuda":
+        return info
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    try:
+        props = torch.cuda.get_device_properties(idx)
+        info["gpu_name"] = props.name
+        uuid = str(getattr(props, "uuid", "") or "")
+        if uuid:
+            info["gpu_uuid"] = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+        bus = getattr(props, "pci_bus_id", None)
+        if bus is not None:
+            info["pci_bus_id"] = "%08X:%02X:%02X.0" % (getattr(props, "pci_domain_id", 0) or 0, bus,
+                                                        getattr(props, "pci_device_id", 0) or 0)
+    except Exception:  # noqa: BLE001  identity is best effort
+        pass
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    ids = [v.strip() for v in vis.split(",")] if vis else None
+    info["gpu_index"] = ids[idx] if ids and idx < len(ids) else str(idx)
+    return info
+
+
+@dataclass
+class SDCEvent:
+    detector: str                 # "checksum", "replay", "kv_transfer", "alltoall", "canary", "replica", ...
+    step: Optional[int]
+    detail: dict = field(default_factory=dict)
+    identity: dict = field(default_factory=dict)
+    time: float = field(default_factory=time.time)
+
+    def to_json(self) -> str:
+        return json.dumps(asdict(self), default=str)
+
+
+class EventLog:
+    """Events in memory, optionally appended to a JSONL file. A failed write is counted, never raised."""
+
+    def __init__(self, path: Optional[str] = None):
+        self.path = path
+        self.events: list[SDCEvent] = []
+        self.write_errors = 0
+
+    def add(self, ev: SDCEvent) -> None:
+        self.events.append(ev)
+        if not self.path:
+            return
+        try:
+            os.makedirs(os.path.dirname(os.path.abspath(self.path)) or ".", exist_ok=True)
+            with open(self.path, "a") as f:
+                f.write(ev.to_json() + "\n")
+        except OSError as e:
+            self.write_errors += 1
+            if self.write_errors == 1:
+                log.warning("sdcguard: cannot append alerts to %s (%s); they stay in memory", self.path, e)
+
+    def first_step(self) -> Optional[int]:
+        steps = [e.step for e in self.events if e.step is not None]
+        return min(steps) if steps else None
+
+
+def rollback_checkpoint(first_alert_step: int, checkpoint_steps: list[int], check_every: int = 1,
+                        windows: int = 1) -> Optional[int]:
+    """Newest checkpoint no later than the last check known to have passed (first_alert_step - check_every *
+    windows); None when there is none."""
+    cutoff = first_alert_step - check_every * max(1, windows)
+    ok = [s for s in checkpoint_steps if s <= cutoff]
+    return max(ok) if ok else None
