@@ -705,3 +705,59 @@ int sdc_gemm_bf16(const void* A, long long lda, const void* W, const void* Wc, i
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------------------------------------------------
+// Allocation-free variant (declared and documented in gemm_noalloc.h): the workspace is a file-scope device
+// array instead of caller memory. This section only adds an entry point; sdc_gemm_bf16 is unchanged.
+#include "gemm_noalloc.h"
+
+namespace {
+
+// Zero-initialised when the module loads; in host code this name is only a stand-in for the symbol, never a
+// device address: the address comes from cudaGetSymbolAddress below.
+static __device__ __align__(256) unsigned char g_gemm_noalloc_scratch[SDC_GEMM_NOALLOC_SCRATCH_BYTES];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[kMaxDevices] = {};
+
+}  // namespace
+
+extern "C" int sdc_gemm_bf16_noalloc(const void* A, long long lda, const void* W, const void* Wc, int M, int N, int K,
+                                     void* Cout, long long ldc, const float* bias, const float* bsum, float bias_max,
+                                     const float* row_sq, const float* wstat, unsigned long long* state, int slot,
+                                     unsigned s0, unsigned s1, unsigned s2, unsigned s3, float zthr, float prod_coef,
+                                     float out_coef, float abs_floor, float bound_coef, int* err, int bn, int max_ctas,
+                                     void* stream) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  const long long pairs = static_cast<long long>(M) * ((N + CSW - 1) / CSW);
+  if (pairs > SDC_GEMM_NOALLOC_MAX_PAIRS || sdc_gemm_ws_bytes(M, N) > SDC_GEMM_NOALLOC_SCRATCH_BYTES) {
+    std::fprintf(stderr,
+                 "sdc_gemm_bf16_noalloc: M=%d x ceil(N/128)=%lld (row, block) pairs exceed the fixed workspace "
+                 "(%lld pairs); use sdc_gemm_bf16 with a caller workspace\n",
+                 M, static_cast<long long>((N + CSW - 1) / CSW), static_cast<long long>(SDC_GEMM_NOALLOC_MAX_PAIRS));
+    return SDC_GEMM_NOALLOC_TOO_LARGE;
+  }
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  if (dev < 0 || dev >= kMaxDevices) return -1;
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (g_noalloc_addr[dev] == nullptr) {
+      void* p = nullptr;
+      e = cudaGetSymbolAddress(&p, g_gemm_noalloc_scratch);   // device `dev` is current here
+      if (e != cudaSuccess || p == nullptr) return e != cudaSuccess ? static_cast<int>(e) : -1;
+      g_noalloc_addr[dev] = p;
+    }
+    scratch = g_noalloc_addr[dev];
+  }
+  // the band counters must start at zero (a launch that gave up can leave them set); the expected sums are
+  // always written before they are read
+  e = cudaMemsetAsync(scratch, 0, COUNTER_BYTES, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return static_cast<int>(e);
+  return sdc_gemm_bf16(A, lda, W, Wc, M, N, K, Cout, ldc, bias, bsum, bias_max, row_sq, wstat, scratch, state, slot,
+                       s0, s1, s2, s3, zthr, prod_coef, out_coef, abs_floor, bound_coef, err, bn, max_ctas, -1, -1, 0u,
+                       nullptr, stream);
+}
