@@ -66,7 +66,8 @@ SIGNATURES: dict[str, tuple] = {
     "sdc_silu_mul_bf16": (I, [P, I, I, P, P, P, P]),
     "sdc_compare_rows_bf16": (I, [P, L, P, P, L, I, I, P, P]),
     "sdc_attn_prefill": (I, [P, P, P, P, I, P, P, I, P, I, I, I, F, P, P]),
-    "sdc_attn_decode": (I, [P, P, P, P, I, P, P, P, I, I, I, I, I, F, P, P]),
+    "sdc_attn_decode": (I, [P, P, P, P, I, P, P, P, I, I, I, I, I, F, P, P, P]),
+    "sdc_attn_decode_splits": (I, [I]),
 }
 
 
@@ -103,7 +104,7 @@ def lib():
                 raise RuntimeError(f"{LIB_PATH.name} lacks {name}: rebuild with python -m sdcguard_b200._build")
             fn.restype = res
             fn.argtypes = args
-            if not name.endswith("_bytes"):
+            if not (name.endswith("_bytes") or name.endswith("_splits")):
                 setattr(wrapped, name, _Counted(fn))
         _lib = wrapped
         return _lib

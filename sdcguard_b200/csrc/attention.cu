@@ -277,6 +277,13 @@ __global__ void __launch_bounds__(WARPS * 32, 1) prefill_kernel(const PrefillPar
 }
 
 // ---------------------------------------------------------------------------------------------- decode
+// Split-KV decode ("flash decoding"): the keys of each (sequence, kv head) are cut into chunks of SPLIT keys at
+// absolute multiples of SPLIT; one CTA per chunk writes the chunk's softmax statistics and unnormalised output,
+// and a combine kernel merges the chunks of a row in a fixed order. Chunk boundaries and reduction orders
+// depend only on the row, so a replay of any subset of sequences reproduces their outputs bit for bit.
+constexpr int SPLIT = 256;                 // keys per chunk (16 pages)
+constexpr int REC = D + 4;                 // floats per partial record: o[D], m, l, pad
+
 struct DecodeParams {
   const __nv_bfloat16* q;     // [B, nq, D] (one new token per sequence)
   __nv_bfloat16* o;           // [B, nq, D]
@@ -287,66 +294,82 @@ struct DecodeParams {
   const int* ctx;             // [B] keys to attend (including the new token)
   const int* seq_idx;         // optional list of sequences to run (replay); null = all
   int nq, nkv;
-  int max_ctx;                // shared-memory logits capacity per head
+  int max_splits;             // chunks per sequence the partial buffer holds
   float scale_log2;
+  float* part;                // [B][nkv][max_splits][G][REC] scratch
   float* row_sq;
 };
 
-// One CTA (4 warps) per (sequence, kv head). Pass 1: logits of every key for the G query heads into shared
-// memory; then the softmax; pass 2: P V with lane l owning dims 4l..4l+3; warps combine in a fixed order.
 template <int G>
-__global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
-  extern __shared__ __align__(16) uint8_t sm[];
-  float* sq = reinterpret_cast<float*>(sm);           // [G][D]
-  float* lg = sq + G * D;                              // [G][max_ctx]
-  float* part = lg + G * p.max_ctx;                    // [4 warps][G][D]
+__global__ void __launch_bounds__(128) decode_split_kernel(const DecodeParams p) {
+  __shared__ __align__(16) float sq[G][D];
+  __shared__ float lg[G][SPLIT];
+  __shared__ __align__(16) float wpart[4][G][D];
   __shared__ float red[4][G];
   __shared__ float stat[2][G];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int b = p.seq_idx ? p.seq_idx[blockIdx.x] : blockIdx.x;
-  const int kvh = blockIdx.y;
+  const int kvh = blockIdx.y, sp = blockIdx.z;
   const int n = p.ctx[b];
-  const int* bt = p.block_table + static_cast<long long>(p.seq_req[b]) * p.max_pages;
+  const int k0 = sp * SPLIT;
+  if (k0 >= n) return;
+  const int nk = min(SPLIT, n - k0);
+  const int* bt = p.block_table + static_cast<long long>(p.seq_req[b]) * p.max_pages + k0 / PAGE;
   for (int i = tid; i < G * D; i += 128) {
     const int hg = i / D, d = i % D;
-    sq[i] = __bfloat162float(p.q[(static_cast<long long>(b) * p.nq + kvh * G + hg) * D + d]);
+    sq[hg][d] = __bfloat162float(p.q[(static_cast<long long>(b) * p.nq + kvh * G + hg) * D + d]);
   }
   __syncthreads();
-  const int npages = (n + PAGE - 1) / PAGE;
-  // pass 1: logits
-  const int kk = lane >> 1, half = lane & 1;
-  for (int pg = warp; pg < npages; pg += 4) {
-    const long long blk = bt[pg];
-    const __nv_bfloat16* kp = p.cache + (((blk * 2) * p.nkv + kvh) * PAGE + kk) * D + half * 64;
-    float acc[G];
+  const int npages = (nk + PAGE - 1) / PAGE;
+  // pass 1: logits. lane -> key (lane / 2) of the page, half (lane & 1) of the head dims
+  {
+    const int kk = lane >> 1, half = lane & 1;
+    for (int pg = warp; pg < npages; pg += 4) {
+      const long long blk = bt[pg];
+      const __nv_bfloat16* kp = p.cache + (((blk * 2) * p.nkv + kvh) * PAGE + kk) * D + half * 64;
+      uint4 v[8];
 #pragma unroll
-    for (int h = 0; h < G; ++h) acc[h] = 0.f;
+      for (int c = 0; c < 8; ++c) v[c] = *reinterpret_cast<const uint4*>(kp + c * 8);
+      float acc[G];
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      uint4 v = *reinterpret_cast<const uint4*>(kp + c * 8);
-      const __nv_bfloat162* hv = reinterpret_cast<const __nv_bfloat162*>(&v);
+      for (int h = 0; h < G; ++h) acc[h] = 0.f;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 f = __bfloat1622float2(hv[i]);
-        const int d = half * 64 + c * 8 + 2 * i;
+      for (int c = 0; c < 8; ++c) {
+        const __nv_bfloat162* hv = reinterpret_cast<const __nv_bfloat162*>(&v[c]);
+        const int d0 = half * 64 + c * 8;
 #pragma unroll
-        for (int h = 0; h < G; ++h) acc[h] = fmaf(f.x, sq[h * D + d], fmaf(f.y, sq[h * D + d + 1], acc[h]));
+        for (int h = 0; h < G; ++h) {
+          const float4 qa = *reinterpret_cast<const float4*>(&sq[h][d0]);
+          const float4 qb = *reinterpret_cast<const float4*>(&sq[h][d0 + 4]);
+          const float2 f0 = __bfloat1622float2(hv[0]), f1 = __bfloat1622float2(hv[1]);
+          const float2 f2 = __bfloat1622float2(hv[2]), f3 = __bfloat1622float2(hv[3]);
+          float a = acc[h];
+          a = fmaf(f0.x, qa.x, a);
+          a = fmaf(f0.y, qa.y, a);
+          a = fmaf(f1.x, qa.z, a);
+          a = fmaf(f1.y, qa.w, a);
+          a = fmaf(f2.x, qb.x, a);
+          a = fmaf(f2.y, qb.y, a);
+          a = fmaf(f3.x, qb.z, a);
+          a = fmaf(f3.y, qb.w, a);
+          acc[h] = a;
+        }
+      }
+#pragma unroll
+      for (int h = 0; h < G; ++h) acc[h] += __shfl_xor_sync(0xffffffffu, acc[h], 1);
+      const int key = pg * PAGE + kk;
+      if (half == 0 && key < nk) {
+#pragma unroll
+        for (int h = 0; h < G; ++h) lg[h][key] = acc[h] * p.scale_log2;
       }
     }
-#pragma unroll
-    for (int h = 0; h < G; ++h) acc[h] += __shfl_xor_sync(0xffffffffu, acc[h], 1);
-    const int key = pg * PAGE + kk;
-    if (half == 0 && key < n) {
-#pragma unroll
-      for (int h = 0; h < G; ++h) lg[h * p.max_ctx + key] = acc[h] * p.scale_log2;
-    }
   }
   __syncthreads();
-  // softmax statistics per head (fixed-order reductions)
+  // chunk softmax statistics (fixed-order reductions)
 #pragma unroll
   for (int h = 0; h < G; ++h) {
     float mx = -INFINITY;
-    for (int k = tid; k < n; k += 128) mx = fmaxf(mx, lg[h * p.max_ctx + k]);
+    for (int k = tid; k < nk; k += 128) mx = fmaxf(mx, lg[h][k]);
 #pragma unroll
     for (int m = 16; m > 0; m >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, m));
     if (lane == 0) red[warp][h] = mx;
@@ -358,9 +381,9 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
   for (int h = 0; h < G; ++h) {
     const float mx = stat[0][h];
     float sum = 0.f;
-    for (int k = tid; k < n; k += 128) {
-      const float e = ex2(lg[h * p.max_ctx + k] - mx);
-      lg[h * p.max_ctx + k] = e;
+    for (int k = tid; k < SPLIT; k += 128) {
+      const float e = k < nk ? ex2(lg[h][k] - mx) : 0.f;
+      lg[h][k] = e;
       sum += e;
     }
 #pragma unroll
@@ -369,41 +392,87 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
   }
   __syncthreads();
   if (tid < G) stat[1][tid] = (red[0][tid] + red[1][tid]) + (red[2][tid] + red[3][tid]);
-  __syncthreads();
-  // pass 2: P V
-  float acc[G][4];
+  // pass 2: P V. Per page the warp loads 16 keys x 128 dims as 256 chunks of 8 dims; lane l takes chunks
+  // l + 32 i: dims (l % 16) * 8 .. +8 of keys l / 16 + 2 i. Lanes l and l ^ 16 are combined at the end.
+  float acc[G][8];
 #pragma unroll
-  for (int h = 0; h < G; ++h) acc[h][0] = acc[h][1] = acc[h][2] = acc[h][3] = 0.f;
+  for (int h = 0; h < G; ++h)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[h][j] = 0.f;
+  const int dcol = (lane & 15) * 8, kofs = lane >> 4;
   for (int pg = warp; pg < npages; pg += 4) {
     const long long blk = bt[pg];
-    const __nv_bfloat16* vp = p.cache + (((blk * 2 + 1) * p.nkv + kvh) * PAGE) * D + lane * 4;
-    const int kend = min(PAGE, n - pg * PAGE);
-    for (int k = 0; k < kend; ++k) {
-      uint2 v = *reinterpret_cast<const uint2*>(vp + k * D);
-      const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.x));
-      const float2 f1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.y));
+    const __nv_bfloat16* vp = p.cache + (((blk * 2 + 1) * p.nkv + kvh) * PAGE) * D + dcol;
 #pragma unroll
-      for (int h = 0; h < G; ++h) {
-        const float w = lg[h * p.max_ctx + pg * PAGE + k];
-        acc[h][0] = fmaf(w, f0.x, acc[h][0]);
-        acc[h][1] = fmaf(w, f0.y, acc[h][1]);
-        acc[h][2] = fmaf(w, f1.x, acc[h][2]);
-        acc[h][3] = fmaf(w, f1.y, acc[h][3]);
+    for (int half = 0; half < 2; ++half) {      // 4 loads in flight at a time keeps G = 4, 8 out of spills
+      uint4 v[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) v[i] = *reinterpret_cast<const uint4*>(vp + (kofs + 2 * (4 * half + i)) * D);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int key = pg * PAGE + kofs + 2 * (4 * half + i);   // weights beyond nk are zero
+        const __nv_bfloat162* hv = reinterpret_cast<const __nv_bfloat162*>(&v[i]);
+        const float2 f0 = __bfloat1622float2(hv[0]), f1 = __bfloat1622float2(hv[1]);
+        const float2 f2 = __bfloat1622float2(hv[2]), f3 = __bfloat1622float2(hv[3]);
+#pragma unroll
+        for (int h = 0; h < G; ++h) {
+          const float w = lg[h][key];
+          acc[h][0] = fmaf(w, f0.x, acc[h][0]);
+          acc[h][1] = fmaf(w, f0.y, acc[h][1]);
+          acc[h][2] = fmaf(w, f1.x, acc[h][2]);
+          acc[h][3] = fmaf(w, f1.y, acc[h][3]);
+          acc[h][4] = fmaf(w, f2.x, acc[h][4]);
+          acc[h][5] = fmaf(w, f2.y, acc[h][5]);
+          acc[h][6] = fmaf(w, f3.x, acc[h][6]);
+          acc[h][7] = fmaf(w, f3.y, acc[h][7]);
+        }
       }
     }
   }
 #pragma unroll
   for (int h = 0; h < G; ++h)
 #pragma unroll
-    for (int i = 0; i < 4; ++i) part[(warp * G + h) * D + lane * 4 + i] = acc[h][i];
+    for (int j = 0; j < 8; ++j) acc[h][j] += __shfl_xor_sync(0xffffffffu, acc[h][j], 16);
+  if (lane < 16) {
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      *reinterpret_cast<float4*>(&wpart[warp][h][dcol]) = make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
+      *reinterpret_cast<float4*>(&wpart[warp][h][dcol + 4]) = make_float4(acc[h][4], acc[h][5], acc[h][6], acc[h][7]);
+    }
+  }
   __syncthreads();
-  float sqsum = 0.f;
+  float* rec = p.part + ((static_cast<long long>(b) * p.nkv + kvh) * p.max_splits + sp) * G * REC;
   for (int i = tid; i < G * D; i += 128) {
     const int h = i / D, d = i % D;
-    const float v = ((part[(0 * G + h) * D + d] + part[(1 * G + h) * D + d]) +
-                     (part[(2 * G + h) * D + d] + part[(3 * G + h) * D + d])) /
-                    stat[1][h];
-    const __nv_bfloat16 ob = __float2bfloat16(v);
+    rec[h * REC + d] = (wpart[0][h][d] + wpart[1][h][d]) + (wpart[2][h][d] + wpart[3][h][d]);
+  }
+  if (tid < G) {
+    rec[tid * REC + D] = stat[0][tid];
+    rec[tid * REC + D + 1] = stat[1][tid];
+  }
+}
+
+// Merges the chunks of each (sequence, kv head) in chunk order; one CTA of 128 threads, thread = head dim.
+template <int G>
+__global__ void __launch_bounds__(128) decode_combine_kernel(const DecodeParams p) {
+  const int b = p.seq_idx ? p.seq_idx[blockIdx.x] : blockIdx.x;
+  const int kvh = blockIdx.y, d = threadIdx.x, lane = d & 31;
+  const int n = p.ctx[b];
+  const int ns = (n + SPLIT - 1) / SPLIT;
+  const float* base = p.part + (static_cast<long long>(b) * p.nkv + kvh) * p.max_splits * G * REC;
+  float sqsum = 0.f;
+#pragma unroll
+  for (int h = 0; h < G; ++h) {
+    float M = -INFINITY;
+    for (int s = 0; s < ns; ++s) M = fmaxf(M, base[(s * G + h) * REC + D]);
+    float L = 0.f, acc = 0.f;
+    for (int s = 0; s < ns; ++s) {
+      const float* r = base + (s * G + h) * REC;
+      const float sc = ex2(r[D] - M);
+      L = fmaf(r[D + 1], sc, L);
+      acc = fmaf(r[d], sc, acc);
+    }
+    const __nv_bfloat16 ob = __float2bfloat16(acc / L);
     p.o[(static_cast<long long>(b) * p.nq + kvh * G + h) * D + d] = ob;
     const float f = __bfloat162float(ob);
     sqsum = fmaf(f, f, sqsum);
@@ -451,11 +520,15 @@ int sdc_attn_prefill(const void* q, void* o, const void* cache, const int* block
   return static_cast<int>(cudaGetLastError());
 }
 
+int sdc_attn_decode_splits(int max_ctx) { return (max_ctx + SPLIT - 1) / SPLIT; }
+
+// Scratch: `part` holds nseq_rows x nkv x max_splits x (nq / nkv) x (D + 4) floats, where nseq_rows covers
+// every sequence index used (seq_idx entries included) and max_splits = sdc_attn_decode_splits(max_ctx).
 int sdc_attn_decode(const void* q, void* o, const void* cache, const int* block_table, int max_pages,
                     const int* seq_req, const int* ctx, const int* seq_idx, int nseq, int nq, int nkv, int head_dim,
-                    int max_ctx, float scale, void* row_sq, void* stream) {
+                    int max_ctx, float scale, void* part, void* row_sq, void* stream) {
   if (nseq <= 0) return 0;
-  if (head_dim != D || nq % nkv) return -1;
+  if (head_dim != D || nq % nkv || part == nullptr) return -1;
   DecodeParams p;
   p.q = static_cast<const __nv_bfloat16*>(q);
   p.o = static_cast<__nv_bfloat16*>(o);
@@ -467,34 +540,21 @@ int sdc_attn_decode(const void* q, void* o, const void* cache, const int* block_
   p.seq_idx = seq_idx;
   p.nq = nq;
   p.nkv = nkv;
-  p.max_ctx = max_ctx;
+  p.max_splits = sdc_attn_decode_splits(max_ctx);
   p.scale_log2 = scale * 1.4426950408889634f;
+  p.part = static_cast<float*>(part);
   p.row_sq = static_cast<float*>(row_sq);
   const int G = nq / nkv;
-  const size_t smem = static_cast<size_t>(G) * D * 4 + static_cast<size_t>(G) * max_ctx * 4 + 4ull * G * D * 4;
-  dim3 grid(nseq, nkv);
+  dim3 grid(nseq, nkv, p.max_splits), grid2(nseq, nkv);
   auto st = static_cast<cudaStream_t>(stream);
-  cudaError_t e = cudaSuccess;
-#define SDC_DECODE_CASE(GG)                                                                             \
-  case GG: {                                                                                            \
-    static size_t attr_##GG = 0;                                                                        \
-    if (smem > attr_##GG) {                                                                             \
-      e = cudaFuncSetAttribute(decode_kernel<GG>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
-      if (e != cudaSuccess) return static_cast<int>(e);                                                 \
-      attr_##GG = smem;                                                                                 \
-    }                                                                                                   \
-    decode_kernel<GG><<<grid, 128, smem, st>>>(p);                                                      \
-    break;                                                                                              \
-  }
   switch (G) {
-    SDC_DECODE_CASE(1)
-    SDC_DECODE_CASE(2)
-    SDC_DECODE_CASE(4)
-    SDC_DECODE_CASE(8)
+    case 1: decode_split_kernel<1><<<grid, 128, 0, st>>>(p); decode_combine_kernel<1><<<grid2, 128, 0, st>>>(p); break;
+    case 2: decode_split_kernel<2><<<grid, 128, 0, st>>>(p); decode_combine_kernel<2><<<grid2, 128, 0, st>>>(p); break;
+    case 4: decode_split_kernel<4><<<grid, 128, 0, st>>>(p); decode_combine_kernel<4><<<grid2, 128, 0, st>>>(p); break;
+    case 8: decode_split_kernel<8><<<grid, 128, 0, st>>>(p); decode_combine_kernel<8><<<grid2, 128, 0, st>>>(p); break;
     default:
       return -1;
   }
-#undef SDC_DECODE_CASE
   return static_cast<int>(cudaGetLastError());
 }
 

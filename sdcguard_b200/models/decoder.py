@@ -173,6 +173,18 @@ class CheckedDecoder:
             gemm.reserve_workspace(dev, min(T, 1024), cfg.vocab)
         return self._bufs
 
+    def decode_scratch(self, nseq: int, max_ctx: int) -> torch.Tensor:
+        """Split-KV partials for decode; sized once for the largest batch and context seen (graph-safe: a decode
+        graph is captured after the engine reserved it)."""
+        key = (nseq, max_ctx)
+        cur = self._bufs.get("dscratch")
+        need = attention.decode_scratch(nseq, self.nq, self.nkv, max_ctx, "meta").numel()
+        if cur is None or cur.numel() < need:
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("decode scratch too small inside graph capture")
+            self._bufs["dscratch"] = torch.empty(need, dtype=torch.float32, device=self.device)
+        return self._bufs["dscratch"]
+
     # ---------------------------------------------------------------- ops
     def _linear(self, x, w, cw, name, out, row_sq):
         if not self.checked:
@@ -222,12 +234,13 @@ class CheckedDecoder:
                     layers.compare_rows(att.view(T, -1), meta.sample_idx, rep.view(T, -1).index_select(
                         0, meta.sample_idx), self._st(f"L{i}.attn"))
             else:
+                scratch = self.decode_scratch(T, meta.max_ctx)
                 attention.decode(q, lc, meta.block_table, meta.seq_req, meta.ctx, nq, nkv, meta.max_ctx, out=att,
-                                 row_sq=ors)
+                                 row_sq=ors, scratch=scratch)
                 if chk:
                     rep = B["attn_rep"][:T]
                     attention.decode(q, lc, meta.block_table, meta.seq_req, meta.ctx, nq, nkv, meta.max_ctx,
-                                     out=rep, seq_idx=S)
+                                     out=rep, seq_idx=S, scratch=scratch)
                     layers.compare_rows(att.view(T, -1), S, rep.view(T, -1).index_select(0, S),
                                         self._st(f"L{i}.attn"))
             self._linear(att.view(T, nq * D), lw.o, lw.cw.get("o"), f"L{i}.o", a, ors)

@@ -63,19 +63,30 @@ def prefill(q: torch.Tensor, cache: torch.Tensor, block_table: torch.Tensor, pos
     return out
 
 
+def decode_scratch(nseq_rows: int, nq: int, nkv: int, max_ctx: int, device) -> torch.Tensor:
+    """Partial-result scratch for `decode` (per sequence, kv head and 256-key chunk)."""
+    splits = int(_native.lib().sdc_attn_decode_splits(int(max_ctx)))
+    return torch.empty(nseq_rows * nkv * splits * (nq // nkv) * 132, dtype=torch.float32, device=device)
+
+
 def decode(q: torch.Tensor, cache: torch.Tensor, block_table: torch.Tensor, seq_req: torch.Tensor,
            ctx: torch.Tensor, nq: int, nkv: int, max_ctx: int, out: Optional[torch.Tensor] = None,
            seq_idx: Optional[torch.Tensor] = None, nseq: Optional[int] = None,
-           row_sq: Optional[torch.Tensor] = None, scale: Optional[float] = None) -> torch.Tensor:
-    """q: (B, nq, 128); one CTA per (sequence, kv head). seq_idx selects sequences to run (replay)."""
+           row_sq: Optional[torch.Tensor] = None, scale: Optional[float] = None,
+           scratch: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """q: (B, nq, 128); split-KV: one CTA per (sequence, kv head, 256-key chunk), then a fixed-order combine.
+    seq_idx selects sequences to run (replay). scratch: from `decode_scratch` (allocated here if absent)."""
     if out is None:
         out = torch.empty_like(q)
     scale = 1.0 / math.sqrt(128) if scale is None else scale
     n = nseq if nseq is not None else (seq_idx.shape[0] if seq_idx is not None else q.shape[0])
+    if scratch is None:
+        scratch = decode_scratch(q.shape[0], nq, nkv, max_ctx, q.device)
     _native.check(_native.lib().sdc_attn_decode(
         q.data_ptr(), out.data_ptr(), cache.data_ptr(), block_table.data_ptr(), block_table.shape[1],
         seq_req.data_ptr(), ctx.data_ptr(), None if seq_idx is None else seq_idx.data_ptr(), n, nq, nkv, 128,
-        int(max_ctx), float(scale), None if row_sq is None else row_sq.data_ptr(), _s(q)), "attention decode")
+        int(max_ctx), float(scale), scratch.data_ptr(), None if row_sq is None else row_sq.data_ptr(), _s(q)),
+        "attention decode")
     return out
 
 

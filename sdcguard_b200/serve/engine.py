@@ -53,7 +53,8 @@ def kv_bytes_per_page(cfg: DecoderConfig, nkv: int) -> int:
 class LLMEngine:
     def __init__(self, cfg: DecoderConfig, device="cuda", checked: bool = True, num_blocks: Optional[int] = None,
                  max_prefill_tokens: int = 16384, max_num_seqs: int = 256, sample_every: int = 64,
-                 cuda_graph: bool = True, seed: int = 0, kv_fraction: float = 0.6, model: Optional[CheckedDecoder] = None):
+                 cuda_graph: bool = True, seed: int = 0, kv_fraction: float = 0.6, model: Optional[CheckedDecoder] = None,
+                 max_model_len: int = 4096):
         self.cfg = cfg
         self.device = torch.device(device)
         self.model = model or CheckedDecoder(cfg, self.device, checked=checked, seed=seed)
@@ -71,6 +72,8 @@ class LLMEngine:
         self.guard = ServeGuard(self.model)
         # every activation buffer and the GEMM workspace are sized once, before any CUDA graph is captured
         self.model.buffers(max(max_prefill_tokens, max_num_seqs))
+        self.max_model_len = -(-max_model_len // 256) * 256
+        self.model.decode_scratch(max_num_seqs, self.max_model_len)
         self._graphs: dict = {}
         self._graph_kernels: dict = {}     # graph key -> this library's kernels captured in it
         self._graph_replayed = 0           # kernels of this library executed by graph replays
@@ -185,7 +188,9 @@ class LLMEngine:
             B = len(idx)
             max_pages = bt_dev.shape[1]
             max_ctx = max(plens[r] for r in idx) + max_new
-            max_ctx = -(-max_ctx // 256) * 256
+            if max_ctx > self.max_model_len:
+                raise ValueError(f"sequence of {max_ctx} tokens exceeds max_model_len={self.max_model_len}")
+            max_ctx = self.max_model_len
             S = -(-B // self.sample_every) if self.checked else 0
             graph, st, out = self._decode_graph(B, max_pages, max_ctx, S)
             rows = torch.tensor(idx, dtype=torch.long, device=dev)
