@@ -1,0 +1,58 @@
+"""`sdcguard` command line.
+
+    sdcguard gate DIR --require checksum [--arm A] [--json]   per-request KV-checksum coverage gate (exit 0 PASS, 2 HOLD)
+    sdcguard transfer-check DIR [--json]                     transfer-only coverage (exit 0 PASS, 2 HOLD)
+    sdcguard transfer-compare BASE CAND [--json]             coverage preservation between two builds (always 2)
+    sdcguard pd-record OUT [--gpus ...]                      record a checked prefill/decode run of this engine
+    sdcguard selftest                                        GPU self-test of every checked kernel
+    sdcguard campaign                                        fault-injection campaign on the GPU paths
+    sdcguard check                                           GPU check card (GEMM, bandwidth, injected faults)
+    sdcguard version
+
+The first three keep the reference's commands, exit codes and output (src/sdcguard/cli.py:343-463 dispatch).
+"""
+from __future__ import annotations
+
+import sys
+
+
+def _version(argv) -> int:
+    from . import __version__
+    print("sdcguard_b200", __version__)
+    return 0
+
+
+def _lazy(module: str, fn: str):
+    def run(argv):
+        import importlib
+        return getattr(importlib.import_module(module, __package__), fn)(argv)
+    return run
+
+
+COMMANDS = {
+    "gate": _lazy(".coverage.gate", "main"),
+    "transfer-check": _lazy(".coverage.transfer", "main"),
+    "transfer-compare": _lazy(".coverage.transfer", "main_compare"),
+    "pd-record": _lazy(".serve.pd", "main"),
+    "selftest": _lazy(".tools.selftest", "main"),
+    "campaign": _lazy(".tools.campaign", "main"),
+    "check": _lazy(".tools.check", "main"),
+    "version": _version,
+}
+
+
+def main(argv=None) -> int:
+    argv = list(sys.argv[1:] if argv is None else argv)
+    if not argv or argv[0] in ("-h", "--help"):
+        print(__doc__)
+        return 0 if argv else 2
+    cmd, rest = argv[0], argv[1:]
+    fn = COMMANDS.get(cmd)
+    if fn is None:
+        print(f"sdcguard: unknown command {cmd!r}\n{__doc__}", file=sys.stderr)
+        return 2
+    return int(fn(rest) or 0)
+
+
+if __name__ == "__main__":
+    sys.exit(main())
