@@ -68,6 +68,8 @@ SIGNATURES: dict[str, tuple] = {
     "sdc_attn_prefill": (I, [P, P, P, P, I, P, P, I, P, I, I, I, F, P, P]),
     "sdc_attn_decode": (I, [P, P, P, P, I, P, P, P, I, I, I, I, I, F, P, P, P]),
     "sdc_attn_decode_splits": (I, [I]),
+    "sdc_kv_page_checksums": (I, [P, L, L, I, P, I, ctypes.c_ulonglong, P, P]),
+    "sdc_kv_pull_pages": (I, [P, L, P, L, L, I, P, P, I, ctypes.c_ulonglong, P, P, P, P, P]),
 }
 
 

@@ -458,6 +458,9 @@ def checksum_gate(result_raw: bytes, archive_raw: bytes, preflight_raw, required
 
 def inspect(path, required, arm=None) -> dict:
     path = Path(path)
+    from . import own
+    if path.is_dir() and own.is_own_recording(path):
+        return own.inspect(path)
     if path.is_file():
         ev.parse_json(ev.read_file(path.parent, path.name))
         return decide([], required, ["legacy_summary_has_no_complete_per_request_check_evidence"], arm=arm)

@@ -231,37 +231,65 @@ class LLMEngine:
         return self._graph_replayed
 
     # ---------------------------------------------------------------- public API
+    def check_tokens(self, prompts: torch.Tensor, plens: Sequence[int]) -> None:
+        """Host-side range check of prompt token ids (an out-of-range id must be an error here, not a device
+        assert in the embedding gather)."""
+        if prompts.device.type != "cpu":
+            return
+        for r, n in enumerate(plens):
+            row = prompts[r, :n]
+            if n and (int(row.min()) < 0 or int(row.max()) >= self.cfg.vocab):
+                raise ValueError(f"request {r}: token ids must lie in [0, {self.cfg.vocab})")
+
+    def block_tables(self, pages: Sequence[Sequence[int]]) -> torch.Tensor:
+        """(N, max_pages) int32 device block table from per-request page lists."""
+        max_pages = max(len(p) for p in pages)
+        bt = torch.zeros(len(pages), max_pages, dtype=torch.int32)
+        for r, pg in enumerate(pages):
+            bt[r, :len(pg)] = torch.tensor(list(pg), dtype=torch.int32)
+        return bt.to(self.device, non_blocking=True)
+
+    def prefill(self, prompts_dev: torch.Tensor, plens: Sequence[int], pages: Sequence[Sequence[int]],
+                out_tokens: torch.Tensor) -> None:
+        """Prefill every request into its pages (token budget per batch) and write each request's first generated
+        token to out_tokens[:, 0]. The pages stay allocated (the caller owns them)."""
+        plens = [int(x) for x in plens]
+        bt_dev = self.block_tables(pages)
+        batch, ntok = [], 0
+        for r in range(len(plens)):
+            if batch and ntok + plens[r] > self.max_prefill_tokens:
+                self._prefill_batch(batch, prompts_dev, plens, bt_dev, pages, out_tokens)
+                batch, ntok = [], 0
+            batch.append(r)
+            ntok += plens[r]
+        if batch:
+            self._prefill_batch(batch, prompts_dev, plens, bt_dev, pages, out_tokens)
+
+    def decode_from(self, plens: Sequence[int], pages: Sequence[Sequence[int]], out_tokens: torch.Tensor,
+                    max_new_tokens: int) -> None:
+        """Decode max_new_tokens - 1 further tokens for requests whose prompts are already in `pages` and whose
+        first token is out_tokens[:, 0] (e.g. KV pages received from a prefill engine)."""
+        if max_new_tokens > 1:
+            self._decode([int(x) for x in plens], self.block_tables(pages), out_tokens, max_new_tokens)
+
     def generate(self, prompts: torch.Tensor, prompt_lens: Sequence[int], max_new_tokens: int) -> torch.Tensor:
         """prompts: (N, max_len) int64 token ids (ideally pinned host memory); returns (N, max_new_tokens) int64
         generated ids on the host. Greedy decoding, no early stop (synthetic workloads)."""
         dev = self.device
         N = prompts.shape[0]
         plens = [int(x) for x in prompt_lens]
+        self.check_tokens(prompts, plens)
         prompts_dev = prompts.to(dev, non_blocking=True)
         need = [-(-(n + max_new_tokens) // PAGE) for n in plens]
-        bt_host = [self.alloc.alloc(k) for k in need]
-        max_pages = max(need)
-        bt = torch.zeros(N, max_pages, dtype=torch.int32)
-        for r, pg in enumerate(bt_host):
-            bt[r, :len(pg)] = torch.tensor(pg, dtype=torch.int32)
-        bt_dev = bt.to(dev, non_blocking=True)
+        pages = [self.alloc.alloc(k) for k in need]
         out_tokens = torch.zeros(N, max_new_tokens, dtype=torch.long, device=dev)
         try:
-            batch, ntok = [], 0
-            for r in range(N):
-                if batch and ntok + plens[r] > self.max_prefill_tokens:
-                    self._prefill_batch(batch, prompts_dev, plens, bt_dev, bt_host, out_tokens)
-                    batch, ntok = [], 0
-                batch.append(r)
-                ntok += plens[r]
-            if batch:
-                self._prefill_batch(batch, prompts_dev, plens, bt_dev, bt_host, out_tokens)
-            if max_new_tokens > 1:
-                self._decode(plens, bt_dev, out_tokens, max_new_tokens)
+            self.prefill(prompts_dev, plens, pages, out_tokens)
+            self.decode_from(plens, pages, out_tokens, max_new_tokens)
             host = torch.empty(N, max_new_tokens, dtype=torch.long, pin_memory=True)
             host.copy_(out_tokens, non_blocking=True)
             torch.cuda.current_stream(dev).synchronize()
             return host
         finally:
-            for pg in bt_host:
+            for pg in pages:
                 self.alloc.release(pg)
