@@ -59,7 +59,7 @@ F = c_float
 SIGNATURES: dict[str, tuple] = {
     "sdc_gemm_ws_bytes": (L, [I, I]),
     "sdc_gemm_bf16": (I, [P, L, P, P, I, I, I, P, L, P, P, F, P, P, P, P, I, U, U, U, U, F, F, F, F, F, P, I, I, I, I,
-                          U, P, P]),
+                          U, P, P, P]),
     "sdc_row_sqnorm_bf16": (I, [P, L, I, I, P, P]),
     "sdc_add_rmsnorm_bf16": (I, [P, P, P, F, I, I, P, P, P, P, P]),
     "sdc_qk_norm_rope_kv": (I, [P, L, I, I, I, I, P, P, P, P, F, P, P, P, P, P, P]),
@@ -68,6 +68,17 @@ SIGNATURES: dict[str, tuple] = {
     "sdc_attn_prefill": (I, [P, P, P, P, I, P, P, I, P, I, I, I, F, P, P]),
     "sdc_attn_decode": (I, [P, P, P, P, I, P, P, P, I, I, I, I, I, F, P, P, P]),
     "sdc_attn_decode_splits": (I, [I]),
+    "sdc_tp_signal": (I, [P, P, I, I, P]),
+    "sdc_tp_reduce_scatter": (I, [P, P, P, P, I, I, I, I, P, F, P, P, P]),
+    "sdc_tp_all_gather": (I, [P, P, P, P, I, I, I, P, P, P, P]),
+    "sdc_seal_rows": (I, [P, L, I, I, P, P]),
+    "sdc_symm_alloc": (I, [ctypes.c_ulonglong, ctypes.POINTER(ctypes.c_void_p)]),
+    "sdc_symm_free": (I, [P]),
+    "sdc_ipc_handle": (I, [P, P]),
+    "sdc_ipc_handle_bytes": (I, []),
+    "sdc_ipc_open": (I, [P, ctypes.POINTER(ctypes.c_void_p)]),
+    "sdc_ipc_close": (I, [P]),
+    "sdc_enable_peer_access": (I, [I]),
     "sdc_kv_page_checksums": (I, [P, L, L, I, P, I, ctypes.c_ulonglong, P, P]),
     "sdc_kv_pull_pages": (I, [P, L, P, L, L, I, P, P, I, ctypes.c_ulonglong, P, P, P, P, P]),
 }
@@ -106,7 +117,8 @@ def lib():
                 raise RuntimeError(f"{LIB_PATH.name} lacks {name}: rebuild with python -m sdcguard_b200._build")
             fn.restype = res
             fn.argtypes = args
-            if not (name.endswith("_bytes") or name.endswith("_splits")):
+            if not (name.endswith("_bytes") or name.endswith("_splits") or "_symm_" in name or "_ipc_" in name
+                    or name.endswith("_peer_access")):
                 setattr(wrapped, name, _Counted(fn))
         _lib = wrapped
         return _lib

@@ -78,7 +78,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
-// ---------------------------------------------------------------- TMA (no multicast anywhere)
+// ---------------------------------------------------------------- TMA (plain per-CTA tile copies)
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::
@@ -179,6 +179,17 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_addr) {
 __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
   return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
          (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+// ---------------------------------------------------------------- seals
+// Exact integrity hash of stored data, one 32-bit value per (row, 128-column block) = 64 words of two bf16:
+//     seal = sum_w ((word_w XOR key_w) * SEAL_MUL) mod 2^32,  key_w = (w + 1) * 0x9E3779B9
+// SEAL_MUL is odd, so flipping any single bit of any word changes its term by an odd multiple of a power of two
+// below 2^32 and the seal always changes. Producers compute it from the bits they store; consumers recompute it
+// from the bits they receive.
+constexpr uint32_t SEAL_MUL = 0x85EBCA6Bu;
+__device__ __forceinline__ uint32_t seal_term(uint32_t word, uint32_t w) {
+  return (word ^ ((w + 1u) * 0x9E3779B9u)) * SEAL_MUL;
 }
 
 // ---------------------------------------------------------------- numeric helpers

@@ -76,6 +76,7 @@ struct Params {
   int inj_row, inj_col;
   uint32_t inj_xor;
   unsigned long long* dbg;   // optional per-CTA timers (null: off): [cta][8]
+  uint32_t* seal;            // optional [M][nb] hash of the stored bf16 bits of each (row, block) (null: off)
 };
 
 template <int BN>
@@ -408,6 +409,7 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
         const int col0 = idx * BN + g * CSW;
         const bool have = col0 < p.N;           // warp-uniform
         float P = 0.f, S = 0.f, Q = 0.f, Aab = 0.f;
+        uint32_t seal = 0u;
         if (have) {
           uint8_t* stg = staging + ew * 4096;     // this warp's 32 x 128 B staging tile
 #pragma unroll 1
@@ -440,6 +442,10 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
             uint32_t packed[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) packed[j] = pack_bf16x2(u32_as_f32(r[2 * j]), u32_as_f32(r[2 * j + 1]));
+            if (p.seal != nullptr) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) seal += seal_term(packed[j], static_cast<uint32_t>(h * 32 + j));
+            }
             // the previous store from this staging tile must have read it before we overwrite it
             if (lane == 0) bulk_wait_read0();
             __syncwarp();
@@ -456,6 +462,7 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
               bulk_commit();
             }
           }
+          if (p.seal != nullptr && row < p.M) p.seal[static_cast<long long>(row) * p.nb + col0 / CSW] = seal;
         }
         tc_fence_before();
         mbar_arrive(&ctl->tempty[acc]);   // the MMA warp may refill this accumulator now
@@ -645,7 +652,7 @@ int sdc_gemm_bf16(const void* A, long long lda, const void* W, const void* Wc, i
                   const float* wstat, void* ws, unsigned long long* state, int slot, unsigned s0, unsigned s1,
                   unsigned s2, unsigned s3, float zthr, float prod_coef, float out_coef, float abs_floor,
                   float bound_coef, int* err, int bn, int max_ctas, int inj_row, int inj_col, unsigned inj_xor,
-                  void* dbg, void* stream) {
+                  void* dbg, void* seal, void* stream) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   if ((K % 8) || (N % 8) || (lda % 8) || (ldc % 8) || (bn != 128 && bn != 256)) return -1;
   if ((M + BM - 1) / BM > MAX_BANDS) return -1;
@@ -689,6 +696,7 @@ int sdc_gemm_bf16(const void* A, long long lda, const void* W, const void* Wc, i
   p.inj_col = inj_col;
   p.inj_xor = inj_xor;
   p.dbg = static_cast<unsigned long long*>(dbg);
+  p.seal = static_cast<uint32_t*>(seal);
   CUtensorMap ma, mw, mc, mo;
   if (!make_map(&ma, A, M, K, lda, BM)) return -2;
   if (!make_map(&mw, W, N, K, K, bn)) return -3;
@@ -759,5 +767,5 @@ extern "C" int sdc_gemm_bf16_noalloc(const void* A, long long lda, const void* W
   if (e != cudaSuccess) return static_cast<int>(e);
   return sdc_gemm_bf16(A, lda, W, Wc, M, N, K, Cout, ldc, bias, bsum, bias_max, row_sq, wstat, scratch, state, slot,
                        s0, s1, s2, s3, zthr, prod_coef, out_coef, abs_floor, bound_coef, err, bn, max_ctas, -1, -1, 0u,
-                       nullptr, stream);
+                       nullptr, nullptr, stream);
 }

@@ -13,7 +13,7 @@
 //
 //   * page_checksums: H of local pages (the producer's "sent" checksum array, or a consumer re-verifying pages
 //     it already holds, e.g. a reused prefix-cache block).
-//   * pull_pages: copy pages from a peer GPU's cache (plain 16-byte loads over NVLink, no TMA, no multicast) into
+//   * pull_pages: copy pages from a peer GPU's cache (plain 16-byte loads over NVLink) into
 //     the local cache, hashing the words as they arrive, then a compare pass checks every page against the
 //     producer's array and records a per-page result and mismatches into a state row.
 //

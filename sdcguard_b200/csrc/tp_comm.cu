@@ -1,0 +1,250 @@
+// Tensor-parallel collectives over NVLink peer memory with carried checksums (sm_100a). No NCCL on these paths.
+//
+// Every rank owns symmetric buffers (same shapes on every rank, peers' copies mapped into this process through
+// CUDA IPC) and an int64 flag array flags[world] that peers write. One collective step:
+//
+//   signal   : gen += 1 on this rank; store gen into flags[my_rank] of every peer (release, system scope).
+//   wait     : spin (bounded) until every flags[r] of this rank >= gen (acquire, system scope).
+//
+// Every rank calls signal/wait the same number of times in the same order, so the generations agree; counters
+// live on the device, which keeps the sequence valid inside CUDA graphs.
+//
+//   reduce-scatter (pull): rank d sums rows [d R, (d+1) R) of every peer's partial output (a row-parallel GEMM's
+//     K-shard result), peer by peer in rank order, in fp32, and rounds once. Checks, per (row, 128-column block):
+//       * transit: the seal of the bits read from peer r equals the seal peer r's GEMM epilogue computed from
+//         the bits it stored (exact 32-bit hash, any single flipped bit changes it);
+//       * arithmetic: sum of the reduced block equals the sum over peers of their block sums, within the
+//         rounding of the bf16 output and the fp32 adds (linearity of block checksums).
+//   all-gather (pull): every rank copies every peer's row shard into its full-size buffer and checks each
+//     (row, block) against the owner's seal.
+// Results go to a state row (worst score with location, launches, blocks checked). Waits never trap: after the
+// deadline the kernel records a timeout in the error word and skips the work.
+#include "common.cuh"
+
+namespace sdc {
+namespace tp {
+
+constexpr int MAXW = 8;
+
+struct Peers {
+  const void* ptr[MAXW];    // per rank: base of that rank's copy of a symmetric buffer
+};
+
+__device__ __forceinline__ long long ld_acquire_sys(const long long* p) {
+  long long v;
+  asm volatile("ld.acquire.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(long long* p, long long v) {
+  asm volatile("st.release.sys.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// one thread: bump the generation and publish it to every peer's flag slot for this rank
+__global__ void signal_kernel(long long* gen, Peers flags, int world, int rank) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  const long long g = *gen + 1;
+  *gen = g;
+  __threadfence_system();
+  for (int r = 0; r < world; ++r) st_release_sys(static_cast<long long*>(const_cast<void*>(flags.ptr[r])) + rank, g);
+}
+
+// every CTA's thread 0 waits for all peers to reach this rank's generation; returns false on timeout
+__device__ bool wait_all(const long long* gen, const long long* my_flags, int world, int* err) {
+  __shared__ int ok;
+  if (threadIdx.x == 0) {
+    const long long g = *gen;
+    ok = 1;
+    const unsigned long long t0 = globaltimer();
+    for (int r = 0; r < world && ok; ++r) {
+      while (ld_acquire_sys(my_flags + r) < g) {
+        if (globaltimer() - t0 > kWaitNs) {
+          ok = 0;
+          record_error(err, ERR_TIMEOUT_PEER);
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  return ok != 0;
+}
+
+__device__ __forceinline__ float2 bf2(uint32_t w) {
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w));
+}
+
+__device__ __forceinline__ void report(unsigned long long* state, float z, unsigned long long flat) {
+  if (state == nullptr) return;
+  atomicMax(state + 0, (static_cast<unsigned long long>(__float_as_uint(z)) << 32) | (flat & 0xffffffffull));
+  atomicMax(state + 1, static_cast<unsigned long long>(__float_as_uint(z)) << 32);
+}
+
+// One warp per (row, 128-column block) of this rank's rows; lane l owns columns 4l..4l+3 of the block.
+// parts: peers' partial outputs [M][N] bf16; seals: peers' seals [M][nb] u32; out: this rank's [R][N].
+__global__ void __launch_bounds__(256) rs_pull_kernel(Peers parts, Peers seals, const long long* gen,
+                                                      const long long* my_flags, int world, int rank, int R, int N,
+                                                      __nv_bfloat16* __restrict__ out, float tol,
+                                                      unsigned long long* state, int* err) {
+  if (!wait_all(gen, my_flags, world, err)) return;
+  const int nb = (N + 127) / 128;
+  const int lane = threadIdx.x & 31;
+  const long long wid = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  if (blockIdx.x == 0 && threadIdx.x == 0 && state != nullptr) atomicAdd(state + 2, 1ull);
+  if (wid >= static_cast<long long>(R) * nb) return;
+  const int lr = static_cast<int>(wid / nb), b = static_cast<int>(wid % nb);
+  const long long row = static_cast<long long>(rank) * R + lr;
+  const int col = b * 128 + lane * 4;
+  const bool in = col < N;   // N % 8 == 0: a lane's 4 columns are all in or all out
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  float sum_in = 0.f, abs_in = 0.f;
+  int bad_peer = -1;
+  for (int r = 0; r < world; ++r) {
+    uint2 v = make_uint2(0u, 0u);
+    if (in) v = __ldcg(reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(parts.ptr[r]) + row * N + col));
+    uint32_t h = seal_term(v.x, static_cast<uint32_t>(lane * 2)) + seal_term(v.y, static_cast<uint32_t>(lane * 2 + 1));
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) h += __shfl_xor_sync(0xffffffffu, h, m);
+    const float2 a = bf2(v.x), c = bf2(v.y);
+    acc[0] += a.x;
+    acc[1] += a.y;
+    acc[2] += c.x;
+    acc[3] += c.y;
+    sum_in += (a.x + a.y) + (c.x + c.y);
+    abs_in += (fabsf(a.x) + fabsf(a.y)) + (fabsf(c.x) + fabsf(c.y));
+    if (lane == 0) {
+      const uint32_t want = __ldcg(static_cast<const uint32_t*>(seals.ptr[r]) + row * nb + b);
+      if (want != h && bad_peer < 0) bad_peer = r;
+    }
+  }
+  uint2 o;
+  {
+    __nv_bfloat162 p0 = __floats2bfloat162_rn(acc[0], acc[1]);
+    __nv_bfloat162 p1 = __floats2bfloat162_rn(acc[2], acc[3]);
+    o.x = *reinterpret_cast<uint32_t*>(&p0);
+    o.y = *reinterpret_cast<uint32_t*>(&p1);
+  }
+  if (in) *reinterpret_cast<uint2*>(out + static_cast<long long>(lr) * N + col) = o;
+  const float2 q0 = bf2(o.x), q1 = bf2(o.y);
+  float sum_out = (q0.x + q0.y) + (q1.x + q1.y);
+  float abs_out = (fabsf(q0.x) + fabsf(q0.y)) + (fabsf(q1.x) + fabsf(q1.y));
+#pragma unroll
+  for (int m = 16; m > 0; m >>= 1) {
+    sum_in += __shfl_xor_sync(0xffffffffu, sum_in, m);
+    abs_in += __shfl_xor_sync(0xffffffffu, abs_in, m);
+    sum_out += __shfl_xor_sync(0xffffffffu, sum_out, m);
+    abs_out += __shfl_xor_sync(0xffffffffu, abs_out, m);
+  }
+  if (lane == 0) {
+    const unsigned long long flat = static_cast<unsigned long long>(lr) * nb + b;
+    if (bad_peer >= 0) {
+      report(state, __int_as_float(0x7f800000), flat * MAXW + bad_peer);
+    } else {
+      // bf16 rounding of every output (2^-9 relative) and the fp32 adds (world terms per output)
+      const float bound = tol * (abs_out * 0.001953125f + abs_in * world * 5.96e-8f) + 1e-30f;
+      const float z = fabsf(sum_out - sum_in) / bound;
+      if (!(z <= 1.0f)) report(state, z > 3.0e38f || z != z ? __int_as_float(0x7f800000) : z * 6.0f, flat * MAXW);
+    }
+  }
+}
+
+// One warp per (row, 128-column block) of the full gathered tensor [world * R][N].
+// shards: peers' row shards [R][N]; seals: peers' shard seals [R][nb]; out: full buffer.
+__global__ void __launch_bounds__(256) ag_pull_kernel(Peers shards, Peers seals, const long long* gen,
+                                                      const long long* my_flags, int world, int R, int N,
+                                                      __nv_bfloat16* __restrict__ out, unsigned long long* state,
+                                                      int* err) {
+  if (!wait_all(gen, my_flags, world, err)) return;
+  const int nb = (N + 127) / 128;
+  const int lane = threadIdx.x & 31;
+  const long long wid = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  if (blockIdx.x == 0 && threadIdx.x == 0 && state != nullptr) atomicAdd(state + 2, 1ull);
+  if (wid >= static_cast<long long>(world) * R * nb) return;
+  const long long grow = wid / nb;
+  const int b = static_cast<int>(wid % nb);
+  const int owner = static_cast<int>(grow / R);
+  const long long lr = grow - static_cast<long long>(owner) * R;
+  const int col = b * 128 + lane * 4;
+  uint2 v = make_uint2(0u, 0u);
+  if (col < N) v = __ldcg(reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(shards.ptr[owner]) + lr * N + col));
+  uint32_t h = seal_term(v.x, static_cast<uint32_t>(lane * 2)) + seal_term(v.y, static_cast<uint32_t>(lane * 2 + 1));
+#pragma unroll
+  for (int m = 16; m > 0; m >>= 1) h += __shfl_xor_sync(0xffffffffu, h, m);
+  if (col < N) *reinterpret_cast<uint2*>(out + grow * N + col) = v;
+  if (lane == 0) {
+    const uint32_t want = __ldcg(static_cast<const uint32_t*>(seals.ptr[owner]) + lr * nb + b);
+    if (want != h) report(state, __int_as_float(0x7f800000), static_cast<unsigned long long>(grow) * nb + b);
+  }
+}
+
+// Seals of a bf16 [M][N] tensor: one warp per (row, block); the producer side of a checked transfer.
+__global__ void __launch_bounds__(256) seal_rows_kernel(const __nv_bfloat16* __restrict__ x, long long ld, int M,
+                                                        int N, uint32_t* __restrict__ seals) {
+  const int nb = (N + 127) / 128;
+  const int lane = threadIdx.x & 31;
+  const long long wid = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  if (wid >= static_cast<long long>(M) * nb) return;
+  const long long row = wid / nb;
+  const int b = static_cast<int>(wid % nb);
+  const int col = b * 128 + lane * 4;
+  uint2 v = make_uint2(0u, 0u);
+  if (col < N) v = *reinterpret_cast<const uint2*>(x + row * ld + col);
+  uint32_t h = seal_term(v.x, static_cast<uint32_t>(lane * 2)) + seal_term(v.y, static_cast<uint32_t>(lane * 2 + 1));
+#pragma unroll
+  for (int m = 16; m > 0; m >>= 1) h += __shfl_xor_sync(0xffffffffu, h, m);
+  if (lane == 0) seals[row * nb + b] = h;
+}
+
+}  // namespace tp
+}  // namespace sdc
+
+using namespace sdc::tp;
+
+extern "C" {
+
+static Peers make_peers(const unsigned long long* ptrs, int world) {
+  Peers p;
+  for (int i = 0; i < MAXW; ++i) p.ptr[i] = i < world ? reinterpret_cast<const void*>(ptrs[i]) : nullptr;
+  return p;
+}
+
+int sdc_tp_signal(void* gen, const unsigned long long* flag_ptrs, int world, int rank, void* stream) {
+  if (world < 1 || world > MAXW) return -1;
+  signal_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<long long*>(gen),
+                                                                   make_peers(flag_ptrs, world), world, rank);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int sdc_tp_reduce_scatter(const unsigned long long* part_ptrs, const unsigned long long* seal_ptrs, const void* gen,
+                          const void* my_flags, int world, int rank, int R, int N, void* out, float tol, void* state,
+                          int* err, void* stream) {
+  if (world < 1 || world > MAXW || N % 8) return -1;
+  const long long warps = static_cast<long long>(R) * ((N + 127) / 128);
+  const unsigned blocks = static_cast<unsigned>((warps * 32 + 255) / 256);
+  rs_pull_kernel<<<blocks > 0 ? blocks : 1, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      make_peers(part_ptrs, world), make_peers(seal_ptrs, world), static_cast<const long long*>(gen),
+      static_cast<const long long*>(my_flags), world, rank, R, N, static_cast<__nv_bfloat16*>(out), tol,
+      static_cast<unsigned long long*>(state), err);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int sdc_tp_all_gather(const unsigned long long* shard_ptrs, const unsigned long long* seal_ptrs, const void* gen,
+                      const void* my_flags, int world, int R, int N, void* out, void* state, int* err, void* stream) {
+  if (world < 1 || world > MAXW || N % 8) return -1;
+  const long long warps = static_cast<long long>(world) * R * ((N + 127) / 128);
+  const unsigned blocks = static_cast<unsigned>((warps * 32 + 255) / 256);
+  ag_pull_kernel<<<blocks > 0 ? blocks : 1, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      make_peers(shard_ptrs, world), make_peers(seal_ptrs, world), static_cast<const long long*>(gen),
+      static_cast<const long long*>(my_flags), world, R, N, static_cast<__nv_bfloat16*>(out),
+      static_cast<unsigned long long*>(state), err);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int sdc_seal_rows(const void* x, long long ld, int M, int N, void* seals, void* stream) {
+  if (M <= 0) return 0;
+  const long long warps = static_cast<long long>(M) * ((N + 127) / 128);
+  seal_rows_kernel<<<static_cast<unsigned>((warps * 32 + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), ld, M, N, static_cast<uint32_t*>(seals));
+  return static_cast<int>(cudaGetLastError());
+}
+
+}  // extern "C"

@@ -130,10 +130,12 @@ def pick_bn(m: int, n: int, num_sms: int = 148) -> int:
 def checked_linear(x: torch.Tensor, cw: CheckedWeight, state: torch.Tensor, slot: int,
                    row_sq: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
                    z_alarm: float = abft.Z_ALARM, bn: Optional[int] = None, max_ctas: int = 0,
-                   inject: Optional[tuple] = None, dbg: Optional[torch.Tensor] = None) -> torch.Tensor:
+                   inject: Optional[tuple] = None, dbg: Optional[torch.Tensor] = None,
+                   seal: Optional[torch.Tensor] = None) -> torch.Tensor:
     """y = x @ W^T (+ b) on tcgen05 with the ABFT check folded into `state[slot]`.
     x: (m, k) bf16 with unit column stride. inject=(row, col, xor_bits) flips bits of one fp32 accumulator
-    element before the check and the rounding (fault-injection experiments)."""
+    element before the check and the rounding (fault-injection experiments). seal: optional (m, nb) int32 output,
+    an exact hash of the stored bf16 bits of every (row, 128-column block) (see `seal_reference`)."""
     if x.dtype != torch.bfloat16 or x.dim() != 2 or x.stride(1) != 1:
         raise ValueError("checked_linear needs a 2-D bf16 x with unit column stride")
     m, k = x.shape
@@ -160,6 +162,24 @@ def checked_linear(x: torch.Tensor, cw: CheckedWeight, state: torch.Tensor, slot
         cw.cs.wstat.data_ptr(), ws.data_ptr(), state.data_ptr(), int(slot), s[0], s[1], s[2], s[3],
         float(z_alarm), float(cw.prod_coef), float(cw.out_coef), float(abft.ABS_FLOOR), float(math.sqrt(k)),
         err.data_ptr(), int(bn), int(max_ctas), inj_row, inj_col, inj_xor,
-        None if dbg is None else dbg.data_ptr(), _stream_ptr(dev))
+        None if dbg is None else dbg.data_ptr(), None if seal is None else seal.data_ptr(), _stream_ptr(dev))
     _native.check(rc, "checked GEMM launch")
     return out
+
+
+SEAL_MUL = 0x85EBCA6B
+
+
+def seal_reference(y: torch.Tensor) -> torch.Tensor:
+    """(m, nb) int32 seals of a bf16 (m, n) tensor: per (row, 128-column block, zero-padded past column n), sum over
+    its 64 words of two bf16 of ((word ^ (w + 1) * 0x9E3779B9) * 0x85EBCA6B) mod 2^32 (what the kernels compute)."""
+    m, n = y.shape
+    nb = -(-n // 128)
+    pad = torch.zeros(m, nb * 128, dtype=torch.bfloat16, device=y.device)
+    pad[:, :n] = y
+    words = pad.view(torch.int32).view(m, nb, 64).to(torch.int64) & 0xFFFFFFFF
+    w = torch.arange(64, dtype=torch.int64, device=y.device)
+    keys = ((w + 1) * 0x9E3779B9) & 0xFFFFFFFF
+    terms = ((words ^ keys) * SEAL_MUL) & 0xFFFFFFFF
+    s = terms.sum(-1) & 0xFFFFFFFF
+    return torch.where(s >= 2 ** 31, s - 2 ** 32, s).to(torch.int32)

@@ -1,0 +1,114 @@
+"""Tensor-parallel collectives with carried checksums over NVLink peer memory (`csrc/tp_comm.cu`).
+
+    comm = TPComm(heap, max_rows, hidden)
+    # row-parallel GEMM: write the partial output and its seals straight into the symmetric buffers
+    gemm.checked_linear(x, w_shard, ..., out=comm.partial(M), seal=comm.partial_seal(M))
+    comm.reduce_scatter(M, out=rows_of_this_rank)      # pull peers' partials, verify seals and linearity
+    # column-parallel GEMM input: write this rank's rows into the shard buffer, seal them, gather all rows
+    comm.shard(R).copy_(...); comm.all_gather(R, out=full)
+
+Sequence parallelism: rows (tokens) are split evenly over ranks; rank d owns rows [d R, (d+1) R).
+
+The NCCL baseline of the same steps is `reduce_scatter_nccl` / `all_gather_nccl` (no checks).
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from .. import _native
+from ..numerics import abft
+from .symm import SymmetricHeap
+
+TOL = 4.0     # multiplier on the rounding bound of the linearity check
+
+
+class TPComm:
+    def __init__(self, heap, max_rows: int, hidden: int):
+        self.heap = heap
+        self.rank, self.world = heap.rank, heap.world
+        if max_rows % self.world:
+            raise ValueError("max_rows must be a multiple of the world size")
+        self.hidden = hidden
+        nb = -(-hidden // 128)
+        self.nb = nb
+        self.part = heap.alloc([max_rows, hidden], torch.bfloat16)
+        self.part_seal = heap.alloc([max_rows, nb], torch.int32)
+        self.shard_buf = heap.alloc([max_rows // self.world, hidden], torch.bfloat16)
+        self.shard_seal = heap.alloc([max_rows // self.world, nb], torch.int32)
+        self.flags = heap.alloc([self.world], torch.int64)
+        self.gen = torch.zeros(1, dtype=torch.int64, device=heap.device)
+        self.err = torch.zeros(1, dtype=torch.int32, device=heap.device)
+        self.state = torch.zeros(2, abft.STATE_COLS, dtype=torch.int64, device=heap.device)   # 0: RS, 1: AG
+
+    def _s(self):
+        return torch.cuda.current_stream(self.heap.device).cuda_stream
+
+    def partial(self, M: int) -> torch.Tensor:
+        return self.part.local[:M]
+
+    def partial_seal(self, M: int) -> torch.Tensor:
+        return self.part_seal.local[:M]
+
+    def shard(self, R: int) -> torch.Tensor:
+        return self.shard_buf.local[:R]
+
+    def signal(self) -> None:
+        _native.check(_native.lib().sdc_tp_signal(self.gen.data_ptr(), self.flags.ptrs, self.world, self.rank,
+                                                   self._s()), "tp signal")
+
+    def reduce_scatter(self, M: int, out: torch.Tensor) -> torch.Tensor:
+        """Signals that this rank's partial(M) and partial_seal(M) are written, waits for every peer, then sums
+        rows [rank R, (rank+1) R) of all partials into out (R, hidden) with seal and linearity checks."""
+        R = M // self.world
+        self.signal()
+        _native.check(_native.lib().sdc_tp_reduce_scatter(
+            self.part.ptrs, self.part_seal.ptrs, self.gen.data_ptr(), self.flags.local.data_ptr(), self.world,
+            self.rank, R, self.hidden, out.data_ptr(), TOL, self.state[0].data_ptr(), self.err.data_ptr(), self._s()),
+            "tp reduce-scatter")
+        return out
+
+    def all_gather(self, R: int, out: torch.Tensor) -> torch.Tensor:
+        """Seals this rank's shard(R), signals, waits, and gathers every rank's shard into out (world R, hidden),
+        checking each row block against its owner's seal."""
+        _native.check(_native.lib().sdc_seal_rows(self.shard_buf.local.data_ptr(), self.hidden, R, self.hidden,
+                                                  self.shard_seal.local.data_ptr(), self._s()), "seal rows")
+        self.signal()
+        _native.check(_native.lib().sdc_tp_all_gather(
+            self.shard_buf.ptrs, self.shard_seal.ptrs, self.gen.data_ptr(), self.flags.local.data_ptr(), self.world,
+            R, self.hidden, out.data_ptr(), self.state[1].data_ptr(), self.err.data_ptr(), self._s()), "tp all-gather")
+        return out
+
+    def close(self) -> None:
+        """Collective: wait until every rank is done with every buffer, then unmap and free them."""
+        torch.cuda.synchronize(self.heap.device)
+        if self.world > 1:
+            dist.barrier()
+        self.heap.close()
+
+    def read_state(self, reset: bool = True) -> dict:
+        rows = self.state.cpu().tolist()
+        if reset:
+            self.state.zero_()
+        names = ("reduce_scatter", "all_gather")
+        return {n: abft.decode_state_row(r) for n, r in zip(names, rows)} | {"error": int(self.err.item())}
+
+
+def seal_rows(x: torch.Tensor, seals: torch.Tensor) -> torch.Tensor:
+    m, n = x.shape
+    _native.check(_native.lib().sdc_seal_rows(x.data_ptr(), x.stride(0), m, n, seals.data_ptr(),
+                                              torch.cuda.current_stream(x.device).cuda_stream), "seal rows")
+    return seals
+
+
+# ------------------------------------------------------------------------------------------ NCCL baseline
+def reduce_scatter_nccl(partial: torch.Tensor, out: torch.Tensor, group=None) -> torch.Tensor:
+    dist.reduce_scatter_tensor(out, partial, group=group)
+    return out
+
+
+def all_gather_nccl(shard: torch.Tensor, out: torch.Tensor, group=None) -> torch.Tensor:
+    dist.all_gather_into_tensor(out, shard, group=group)
+    return out
