@@ -273,3 +273,7 @@ class CheckedDecoder:
 
     def read_checks(self, reset: bool = False) -> list[dict]:
         return self.state.read(reset=reset)
+
+    def sample(self, logits: torch.Tensor) -> torch.Tensor:
+        """Greedy next token (the engine's sampler)."""
+        return torch.argmax(logits, dim=-1)

@@ -66,14 +66,18 @@ class StateTable:
         self.state = torch.zeros(slots, abft.STATE_COLS, dtype=torch.int64, device=self.device)
         self.names: list[str] = []
         self.nbs: list[int] = []
+        self.kinds: list[str] = []
 
-    def add(self, name: str, nb: int) -> int:
+    def add(self, name: str, nb: int, kind: str = "gemm") -> int:
+        """kind "gemm": location = checksum index (row, block, signed); "collective": location = (row, block,
+        peer) as the TP collective kernels encode it ((row * nb + block) * 8 + peer)."""
         if len(self.names) >= self.state.shape[0]:
             grown = torch.zeros(self.state.shape[0] * 2, abft.STATE_COLS, dtype=torch.int64, device=self.device)
             grown[: self.state.shape[0]] = self.state
             self.state = grown
         self.names.append(name)
         self.nbs.append(nb)
+        self.kinds.append(kind)
         return len(self.names) - 1
 
     def read(self, reset: bool = False) -> list[dict]:
@@ -85,7 +89,10 @@ class StateTable:
             d = abft.decode_state_row(r)
             d["name"] = self.names[i]
             d["slot"] = i
-            if d["z"] > 0:
+            if d["z"] > 0 and self.kinds[i] == "collective":
+                rb, d["peer"] = divmod(d["flat"], 8)
+                d["row"], d["block"] = divmod(rb, self.nbs[i])
+            elif d["z"] > 0:
                 d["row"], d["block"], d["signed"] = abft.locate(d["flat"], self.nbs[i])
             out.append(d)
         return out
@@ -113,9 +120,10 @@ class CheckedWeight:
         self.cs = abft.weight_checksums(self.weight, self.bias, self.mask)
 
 
-def row_sqnorm(x: torch.Tensor) -> torch.Tensor:
+def row_sqnorm(x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     m, k = x.shape
-    out = torch.empty(m, dtype=torch.float32, device=x.device)
+    if out is None:
+        out = torch.empty(m, dtype=torch.float32, device=x.device)
     _native.check(_native.lib().sdc_row_sqnorm_bf16(x.data_ptr(), x.stride(0), m, k, out.data_ptr(),
                                                      _stream_ptr(x.device)), "row_sqnorm")
     return out

@@ -42,6 +42,12 @@ class TPComm:
         self.gen = torch.zeros(1, dtype=torch.int64, device=heap.device)
         self.err = torch.zeros(1, dtype=torch.int32, device=heap.device)
         self.state = torch.zeros(2, abft.STATE_COLS, dtype=torch.int64, device=heap.device)   # 0: RS, 1: AG
+        self._inject: Optional[tuple] = None
+
+    def inject_next(self, row: int, col: int, bit: int = 0) -> None:
+        """Fault injection: the next reduce_scatter flips one bit of this rank's sealed partial (row, col) before
+        the peers read it, as a corrupted transfer would."""
+        self._inject = (row, col, bit)
 
     def _s(self):
         return torch.cuda.current_stream(self.heap.device).cuda_stream
@@ -63,6 +69,11 @@ class TPComm:
         """Signals that this rank's partial(M) and partial_seal(M) are written, waits for every peer, then sums
         rows [rank R, (rank+1) R) of all partials into out (R, hidden) with seal and linearity checks."""
         R = M // self.world
+        if self._inject is not None:
+            r, c, bit = self._inject
+            self._inject = None
+            v = self.part.local.view(torch.int16)[r, c]
+            v.bitwise_xor_(1 << bit if bit < 15 else -(1 << 15))
         self.signal()
         _native.check(_native.lib().sdc_tp_reduce_scatter(
             self.part.ptrs, self.part_seal.ptrs, self.gen.data_ptr(), self.flags.local.data_ptr(), self.world,

@@ -126,7 +126,7 @@ class LLMEngine:
             meta.sample_tiles = rt.to(dev, non_blocking=True)
             meta.sample_idx = ridx.to(dev, non_blocking=True)
         logits = self.model.forward(meta, self.cache)
-        nxt = torch.argmax(logits, dim=-1)
+        nxt = self.model.sample(logits)
         out_tokens.index_put_((rows_req.to(dev), torch.zeros(len(reqs), dtype=torch.long, device=dev)), nxt)
         self.step_counter += 1
         self.stats["prefill_tokens"] += T
@@ -156,7 +156,7 @@ class LLMEngine:
 
         def run():
             logits = self.model.forward(meta, self.cache)
-            return torch.argmax(logits, dim=-1)
+            return self.model.sample(logits)
 
         if not self.cuda_graph:
             g = (None, st, run)

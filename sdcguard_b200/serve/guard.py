@@ -47,10 +47,10 @@ class ServeGuard:
                 t["alarms"] += 1
                 if self._identity is None:
                     self._identity = device_identity(self.model.device)
-                det = "checksum" if "GEMM" in r["name"] else "replay"
+                det = "checksum" if "GEMM" in r["name"] else "collective" if "collective" in r["name"] else "replay"
                 detail = {"layer": r["name"], "z": z, "noise": r["noise"], "flat": r["flat"]}
                 if "row" in r:
-                    detail.update(row=r["row"], block=r["block"], signed=r["signed"])
+                    detail.update({k: r[k] for k in ("row", "block", "signed", "peer") if k in r})
                 ev = SDCEvent(detector=det, step=self.step, detail=detail, identity=self._identity)
                 self.log.add(ev)
                 events.append(ev)

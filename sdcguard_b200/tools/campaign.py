@@ -121,3 +121,30 @@ def quick(seed: int = 0, trials: int = 96, device="cuda") -> dict:
         "replay_rows": {"flips": rep_n, "caught": rep_caught, "rate": round(rep_caught / max(1, rep_n), 4),
                         "false_alarms": int(clean_rep[0, 0].item() != 0)},
     }
+
+
+def main(argv=None) -> int:
+    """`sdcguard campaign [--seed S] [--trials N] [--device cuda:0] [--json]`: exit 0 when every flip above the
+    noise was caught and the clean runs raised nothing, 1 otherwise."""
+    import argparse
+    import json
+    ap = argparse.ArgumentParser(prog="sdcguard campaign")
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--trials", type=int, default=96)
+    ap.add_argument("--device", default="cuda:0")
+    ap.add_argument("--json", action="store_true")
+    a = ap.parse_args(argv)
+    res = quick(a.seed, a.trials, a.device)
+    g, r = res["gemm_accumulator"], res["replay_rows"]
+    if a.json:
+        print(json.dumps(res, sort_keys=True))
+    else:
+        print(f"gemm accumulator flips: {g['caught']}/{g['flips']} caught; above noise {g['caught_above_noise']}/"
+              f"{g['above_noise']}; below noise {g['below_noise']['caught']}/{g['below_noise']['flips']}; "
+              f"clean worst z {g['clean_worst_z']}, false alarms {g['false_alarms']}")
+        for cls, c in sorted(g["by_bit_class"].items()):
+            print(f"  {cls:14s} {c['caught']}/{c['flips']} (above noise {c['caught_above_noise']}/{c['above_noise']})")
+        print(f"replayed-row flips: {r['caught']}/{r['flips']} caught; false alarms {r['false_alarms']}")
+    ok = g["caught_above_noise"] == g["above_noise"] and not g["false_alarms"] and r["caught"] == r["flips"] \
+        and not r["false_alarms"]
+    return 0 if ok else 1
