@@ -36,6 +36,7 @@ struct PrefillParams {
   int nq, nkv;
   float scale_log2;           // softmax scale * log2(e)
   float* row_sq;              // [T] += ||o_token||^2 over heads (zeroed by the caller), or null
+  unsigned long long* check;  // check mode: compare with o instead of writing (state row), or null
 };
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
@@ -257,14 +258,24 @@ __global__ void __launch_bounds__(WARPS * 32, 1) prefill_kernel(const PrefillPar
     const int d = dt * 8 + 2 * t4;
     const uint32_t v0 = pack_bf16x2(o[dt][0] * inv0, o[dt][1] * inv0);
     const uint32_t v1 = pack_bf16x2(o[dt][2] * inv1, o[dt][3] * inv1);
-    if (tok0 >= 0) *reinterpret_cast<uint32_t*>(p.o + (static_cast<long long>(tok0) * p.nq + h0) * D + d) = v0;
-    if (tok1 >= 0) *reinterpret_cast<uint32_t*>(p.o + (static_cast<long long>(tok1) * p.nq + h1) * D + d) = v1;
+    uint32_t* o0 = reinterpret_cast<uint32_t*>(p.o + (static_cast<long long>(tok0) * p.nq + h0) * D + d);
+    uint32_t* o1 = reinterpret_cast<uint32_t*>(p.o + (static_cast<long long>(tok1) * p.nq + h1) * D + d);
+    if (p.check == nullptr) {
+      if (tok0 >= 0) *o0 = v0;
+      if (tok1 >= 0) *o1 = v1;
+    } else {
+      if (tok0 >= 0 && bf16x2_differ(v0, *o0))
+        report_replay_mismatch(p.check, static_cast<unsigned long long>(tok0) * p.nq * D + h0 * D + d);
+      if (tok1 >= 0 && bf16x2_differ(v1, *o1))
+        report_replay_mismatch(p.check, static_cast<unsigned long long>(tok1) * p.nq * D + h1 * D + d);
+    }
     const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v0));
     const float2 f1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v1));
     sq0 = fmaf(f0.x, f0.x, fmaf(f0.y, f0.y, sq0));
     sq1 = fmaf(f1.x, f1.x, fmaf(f1.y, f1.y, sq1));
   }
-  if (p.row_sq != nullptr) {
+  if (p.check != nullptr && blockIdx.x == 0 && threadIdx.x == 0) atomicAdd(p.check + 2, 1ull);
+  if (p.row_sq != nullptr && p.check == nullptr) {
     sq0 += __shfl_xor_sync(0xffffffffu, sq0, 1);
     sq0 += __shfl_xor_sync(0xffffffffu, sq0, 2);
     sq1 += __shfl_xor_sync(0xffffffffu, sq1, 1);
@@ -281,8 +292,17 @@ __global__ void __launch_bounds__(WARPS * 32, 1) prefill_kernel(const PrefillPar
 // absolute multiples of SPLIT; one CTA per chunk writes the chunk's softmax statistics and unnormalised output,
 // and a combine kernel merges the chunks of a row in a fixed order. Chunk boundaries and reduction orders
 // depend only on the row, so a replay of any subset of sequences reproduces their outputs bit for bit.
-constexpr int SPLIT = 256;                 // keys per chunk (16 pages)
+//
+// Memory path: decode reads every K and V byte of the context once, so the kernel is bound by HBM. Each CTA
+// stages its chunk with bulk copies (one 4 KB `cp.async.bulk` per page for K and for V, completing on two
+// mbarriers) so that the whole chunk (32 KB of K, 32 KB of V) is in flight at once without holding registers,
+// and computes from shared memory: QK^T starts when K has landed while V is still arriving.
+//  - QK^T: thread = key; the 16 chunks of 8 dims of a key row are visited in a rotated order (chunk (i + lane)
+//    mod 16), so the 8 lanes of each shared-memory phase read 8 different 16-byte bank groups of K and of q.
+//  - PV: warp = 32 keys, lane = 4 output dims; V rows are read as contiguous 256-byte rows.
+constexpr int SPLIT = 128;                 // keys per chunk (8 pages)
 constexpr int REC = D + 4;                 // floats per partial record: o[D], m, l, pad
+constexpr int PAGE_BYTES = PAGE * D * 2;   // 4 KB: one page of K (or V) of one kv head
 
 struct DecodeParams {
   const __nv_bfloat16* q;     // [B, nq, D] (one new token per sequence)
@@ -298,15 +318,42 @@ struct DecodeParams {
   float scale_log2;
   float* part;                // [B][nkv][max_splits][G][REC] scratch
   float* row_sq;
+  int* err;                   // error word (bounded waits), or null
+  unsigned long long* check;  // check mode (replay): compare with o instead of writing (state row), or null
 };
 
 template <int G>
+struct DecodeSmem {
+  __nv_bfloat16 k[SPLIT * D];           // 32 KB; reused for the per-warp PV partials after QK^T
+  __nv_bfloat16 v[SPLIT * D];           // 32 KB
+  __nv_bfloat16 q[G * D];
+  float p[G][SPLIT];                    // logits, then exp2(logit - max)
+  float red[4][G];
+  float stat[2][G];
+  uint64_t bar[2];
+};
+
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(smem_dst)),
+               "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void bf8_to_f32(const uint4& u, float (&f)[8]) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 t = __bfloat1622float2(h[j]);
+    f[2 * j] = t.x;
+    f[2 * j + 1] = t.y;
+  }
+}
+
+template <int G>
 __global__ void __launch_bounds__(128) decode_split_kernel(const DecodeParams p) {
-  __shared__ __align__(16) float sq[G][D];
-  __shared__ float lg[G][SPLIT];
-  __shared__ __align__(16) float wpart[4][G][D];
-  __shared__ float red[4][G];
-  __shared__ float stat[2][G];
+  extern __shared__ __align__(128) unsigned char dsm_raw[];
+  DecodeSmem<G>& sm = *reinterpret_cast<DecodeSmem<G>*>(dsm_raw);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int b = p.seq_idx ? p.seq_idx[blockIdx.x] : blockIdx.x;
   const int kvh = blockIdx.y, sp = blockIdx.z;
@@ -314,141 +361,124 @@ __global__ void __launch_bounds__(128) decode_split_kernel(const DecodeParams p)
   const int k0 = sp * SPLIT;
   if (k0 >= n) return;
   const int nk = min(SPLIT, n - k0);
-  const int* bt = p.block_table + static_cast<long long>(p.seq_req[b]) * p.max_pages + k0 / PAGE;
-  for (int i = tid; i < G * D; i += 128) {
-    const int hg = i / D, d = i % D;
-    sq[hg][d] = __bfloat162float(p.q[(static_cast<long long>(b) * p.nq + kvh * G + hg) * D + d]);
+  const int npages = (nk + PAGE - 1) / PAGE;
+  if (tid == 0) {
+    mbar_init(&sm.bar[0], 1);
+    mbar_init(&sm.bar[1], 1);
+    fence_mbar_init();
   }
   __syncthreads();
-  const int npages = (nk + PAGE - 1) / PAGE;
-  // pass 1: logits. lane -> key (lane / 2) of the page, half (lane & 1) of the head dims
-  {
-    const int kk = lane >> 1, half = lane & 1;
-    for (int pg = warp; pg < npages; pg += 4) {
-      const long long blk = bt[pg];
-      const __nv_bfloat16* kp = p.cache + (((blk * 2) * p.nkv + kvh) * PAGE + kk) * D + half * 64;
-      uint4 v[8];
-#pragma unroll
-      for (int c = 0; c < 8; ++c) v[c] = *reinterpret_cast<const uint4*>(kp + c * 8);
-      float acc[G];
-#pragma unroll
-      for (int h = 0; h < G; ++h) acc[h] = 0.f;
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const __nv_bfloat162* hv = reinterpret_cast<const __nv_bfloat162*>(&v[c]);
-        const int d0 = half * 64 + c * 8;
-#pragma unroll
-        for (int h = 0; h < G; ++h) {
-          const float4 qa = *reinterpret_cast<const float4*>(&sq[h][d0]);
-          const float4 qb = *reinterpret_cast<const float4*>(&sq[h][d0 + 4]);
-          const float2 f0 = __bfloat1622float2(hv[0]), f1 = __bfloat1622float2(hv[1]);
-          const float2 f2 = __bfloat1622float2(hv[2]), f3 = __bfloat1622float2(hv[3]);
-          float a = acc[h];
-          a = fmaf(f0.x, qa.x, a);
-          a = fmaf(f0.y, qa.y, a);
-          a = fmaf(f1.x, qa.z, a);
-          a = fmaf(f1.y, qa.w, a);
-          a = fmaf(f2.x, qb.x, a);
-          a = fmaf(f2.y, qb.y, a);
-          a = fmaf(f3.x, qb.z, a);
-          a = fmaf(f3.y, qb.w, a);
-          acc[h] = a;
-        }
-      }
-#pragma unroll
-      for (int h = 0; h < G; ++h) acc[h] += __shfl_xor_sync(0xffffffffu, acc[h], 1);
-      const int key = pg * PAGE + kk;
-      if (half == 0 && key < nk) {
-#pragma unroll
-        for (int h = 0; h < G; ++h) lg[h][key] = acc[h] * p.scale_log2;
-      }
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&sm.bar[0], npages * PAGE_BYTES);
+      mbar_arrive_expect_tx(&sm.bar[1], npages * PAGE_BYTES);
+    }
+    __syncwarp();
+    if (lane < 2 * npages) {          // lanes 0..npages-1 copy K pages, the next npages lanes V pages
+      const int pg = lane % npages, kv = lane / npages;
+      const long long blk = p.block_table[static_cast<long long>(p.seq_req[b]) * p.max_pages + k0 / PAGE + pg];
+      const __nv_bfloat16* src = p.cache + (((blk * 2 + kv) * p.nkv + kvh) * PAGE) * D;
+      bulk_load((kv ? sm.v : sm.k) + pg * PAGE * D, src, PAGE_BYTES, &sm.bar[kv]);
     }
   }
+  for (int i = tid; i < G * D / 8; i += 128)
+    reinterpret_cast<uint4*>(sm.q)[i] =
+        reinterpret_cast<const uint4*>(p.q + (static_cast<long long>(b) * p.nq + kvh * G) * D)[i];
   __syncthreads();
+  bool ok = mbar_wait(&sm.bar[0], 0, nullptr);
+  // QK^T: thread tid = key tid of the chunk
+  float lg[G];
+  {
+    float acc[G];
+#pragma unroll
+    for (int h = 0; h < G; ++h) acc[h] = 0.f;
+    const __nv_bfloat16* krow = sm.k + tid * D;
+#pragma unroll 4
+    for (int i = 0; i < 16; ++i) {
+      const int c = (i + lane) & 15;
+      float kf[8];
+      bf8_to_f32(*reinterpret_cast<const uint4*>(krow + c * 8), kf);
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        float qf[8];
+        bf8_to_f32(*reinterpret_cast<const uint4*>(sm.q + h * D + c * 8), qf);
+        float a = acc[h];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) a = fmaf(kf[j], qf[j], a);
+        acc[h] = a;
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < G; ++h) lg[h] = tid < nk ? acc[h] * p.scale_log2 : -INFINITY;
+  }
   // chunk softmax statistics (fixed-order reductions)
 #pragma unroll
   for (int h = 0; h < G; ++h) {
-    float mx = -INFINITY;
-    for (int k = tid; k < nk; k += 128) mx = fmaxf(mx, lg[h][k]);
+    float mx = lg[h];
 #pragma unroll
     for (int m = 16; m > 0; m >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, m));
-    if (lane == 0) red[warp][h] = mx;
+    if (lane == 0) sm.red[warp][h] = mx;
   }
   __syncthreads();
-  if (tid < G) stat[0][tid] = fmaxf(fmaxf(red[0][tid], red[1][tid]), fmaxf(red[2][tid], red[3][tid]));
-  __syncthreads();
+  float e[G];
 #pragma unroll
   for (int h = 0; h < G; ++h) {
-    const float mx = stat[0][h];
-    float sum = 0.f;
-    for (int k = tid; k < SPLIT; k += 128) {
-      const float e = k < nk ? ex2(lg[h][k] - mx) : 0.f;
-      lg[h][k] = e;
-      sum += e;
-    }
+    const float mx = fmaxf(fmaxf(sm.red[0][h], sm.red[1][h]), fmaxf(sm.red[2][h], sm.red[3][h]));
+    e[h] = tid < nk ? ex2(lg[h] - mx) : 0.f;
+    sm.p[h][tid] = e[h];
+    if (tid == 0) sm.stat[0][h] = mx;
+  }
+  __syncthreads();        // every thread has read red[] (max) and written p[]
+#pragma unroll
+  for (int h = 0; h < G; ++h) {
+    float sum = e[h];
 #pragma unroll
     for (int m = 16; m > 0; m >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, m);
-    if (lane == 0) red[warp][h] = sum;
+    if (lane == 0) sm.red[warp][h] = sum;
   }
-  __syncthreads();
-  if (tid < G) stat[1][tid] = (red[0][tid] + red[1][tid]) + (red[2][tid] + red[3][tid]);
-  // pass 2: P V. Per page the warp loads 16 keys x 128 dims as 256 chunks of 8 dims; lane l takes chunks
-  // l + 32 i: dims (l % 16) * 8 .. +8 of keys l / 16 + 2 i. Lanes l and l ^ 16 are combined at the end.
-  float acc[G][8];
+  ok = mbar_wait(&sm.bar[1], 0, nullptr) && ok;
+  // PV: warp -> keys [32 warp, 32 warp + 32), lane -> dims 4 lane .. 4 lane + 3
+  float acc[G][4];
 #pragma unroll
   for (int h = 0; h < G; ++h)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) acc[h][j] = 0.f;
-  const int dcol = (lane & 15) * 8, kofs = lane >> 4;
-  for (int pg = warp; pg < npages; pg += 4) {
-    const long long blk = bt[pg];
-    const __nv_bfloat16* vp = p.cache + (((blk * 2 + 1) * p.nkv + kvh) * PAGE) * D + dcol;
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {      // 4 loads in flight at a time keeps G = 4, 8 out of spills
-      uint4 v[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) v[i] = *reinterpret_cast<const uint4*>(vp + (kofs + 2 * (4 * half + i)) * D);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int key = pg * PAGE + kofs + 2 * (4 * half + i);   // weights beyond nk are zero
-        const __nv_bfloat162* hv = reinterpret_cast<const __nv_bfloat162*>(&v[i]);
-        const float2 f0 = __bfloat1622float2(hv[0]), f1 = __bfloat1622float2(hv[1]);
-        const float2 f2 = __bfloat1622float2(hv[2]), f3 = __bfloat1622float2(hv[3]);
-#pragma unroll
-        for (int h = 0; h < G; ++h) {
-          const float w = lg[h][key];
-          acc[h][0] = fmaf(w, f0.x, acc[h][0]);
-          acc[h][1] = fmaf(w, f0.y, acc[h][1]);
-          acc[h][2] = fmaf(w, f1.x, acc[h][2]);
-          acc[h][3] = fmaf(w, f1.y, acc[h][3]);
-          acc[h][4] = fmaf(w, f2.x, acc[h][4]);
-          acc[h][5] = fmaf(w, f2.y, acc[h][5]);
-          acc[h][6] = fmaf(w, f3.x, acc[h][6]);
-          acc[h][7] = fmaf(w, f3.y, acc[h][7]);
-        }
-      }
-    }
-  }
-#pragma unroll
-  for (int h = 0; h < G; ++h)
-#pragma unroll
-    for (int j = 0; j < 8; ++j) acc[h][j] += __shfl_xor_sync(0xffffffffu, acc[h][j], 16);
-  if (lane < 16) {
+    for (int j = 0; j < 4; ++j) acc[h][j] = 0.f;
+  const int kbeg = warp * 32, kend = min(kbeg + 32, nk);
+  for (int k = kbeg; k < kend; ++k) {
+    const uint2 u = *reinterpret_cast<const uint2*>(sm.v + k * D + lane * 4);
+    const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+    const float2 f1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
 #pragma unroll
     for (int h = 0; h < G; ++h) {
-      *reinterpret_cast<float4*>(&wpart[warp][h][dcol]) = make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
-      *reinterpret_cast<float4*>(&wpart[warp][h][dcol + 4]) = make_float4(acc[h][4], acc[h][5], acc[h][6], acc[h][7]);
+      const float w = sm.p[h][k];
+      acc[h][0] = fmaf(w, f0.x, acc[h][0]);
+      acc[h][1] = fmaf(w, f0.y, acc[h][1]);
+      acc[h][2] = fmaf(w, f1.x, acc[h][2]);
+      acc[h][3] = fmaf(w, f1.y, acc[h][3]);
     }
   }
+  // per-warp partials go where K was (every thread finished QK^T before the first barrier above)
+  float* wpart = reinterpret_cast<float*>(sm.k);     // [4][G][D]
+#pragma unroll
+  for (int h = 0; h < G; ++h)
+    *reinterpret_cast<float4*>(wpart + (warp * G + h) * D + lane * 4) =
+        make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
   __syncthreads();
   float* rec = p.part + ((static_cast<long long>(b) * p.nkv + kvh) * p.max_splits + sp) * G * REC;
   for (int i = tid; i < G * D; i += 128) {
     const int h = i / D, d = i % D;
-    rec[h * REC + d] = (wpart[0][h][d] + wpart[1][h][d]) + (wpart[2][h][d] + wpart[3][h][d]);
+    rec[h * REC + d] = (wpart[(0 * G + h) * D + d] + wpart[(1 * G + h) * D + d]) +
+                       (wpart[(2 * G + h) * D + d] + wpart[(3 * G + h) * D + d]);
   }
   if (tid < G) {
-    rec[tid * REC + D] = stat[0][tid];
-    rec[tid * REC + D + 1] = stat[1][tid];
+    rec[tid * REC + D] = sm.stat[0][tid];
+    rec[tid * REC + D + 1] = (sm.red[0][tid] + sm.red[1][tid]) + (sm.red[2][tid] + sm.red[3][tid]);
+  }
+  if (!ok && tid == 0) {
+    record_error(p.err, ERR_TIMEOUT_PEER);
+    // the copies were issued by this CTA: give them one more bounded wait before its shared memory is released
+    mbar_wait(&sm.bar[0], 0, nullptr);
+    mbar_wait(&sm.bar[1], 0, nullptr);
   }
 }
 
@@ -473,9 +503,20 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(const DecodeParams 
       acc = fmaf(r[d], sc, acc);
     }
     const __nv_bfloat16 ob = __float2bfloat16(acc / L);
-    p.o[(static_cast<long long>(b) * p.nq + kvh * G + h) * D + d] = ob;
+    __nv_bfloat16* dst = p.o + (static_cast<long long>(b) * p.nq + kvh * G + h) * D + d;
+    if (p.check == nullptr) {
+      *dst = ob;
+    } else {
+      const float x = __bfloat162float(ob), y = __bfloat162float(*dst);
+      if (!(x == y) && !(x != x && y != y))
+        report_replay_mismatch(p.check, static_cast<unsigned long long>(b) * p.nq * D + (kvh * G + h) * D + d);
+    }
     const float f = __bfloat162float(ob);
     sqsum = fmaf(f, f, sqsum);
+  }
+  if (p.check != nullptr) {
+    if (blockIdx.x == 0 && blockIdx.y == 0 && d == 0) atomicAdd(p.check + 2, 1ull);
+    return;
   }
   if (p.row_sq != nullptr) {
 #pragma unroll
@@ -489,11 +530,25 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(const DecodeParams 
 
 using namespace sdc::attn;
 
+template <int G>
+static int launch_decode(const DecodeParams& p, dim3 grid, dim3 grid2, cudaStream_t st) {
+  static bool attr_set = false;      // per process; the attribute applies to every device
+  const int smem = static_cast<int>(sizeof(DecodeSmem<G>));
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(decode_split_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    attr_set = true;
+  }
+  decode_split_kernel<G><<<grid, 128, smem, st>>>(p);
+  decode_combine_kernel<G><<<grid2, 128, 0, st>>>(p);
+  return static_cast<int>(cudaGetLastError());
+}
+
 extern "C" {
 
 int sdc_attn_prefill(const void* q, void* o, const void* cache, const int* block_table, int max_pages,
                      const int* pos, const void* tiles, int ntiles, const int* row_idx, int nq, int nkv,
-                     int head_dim, float scale, void* row_sq, void* stream) {
+                     int head_dim, float scale, void* row_sq, void* check, void* stream) {
   if (ntiles <= 0) return 0;
   if (head_dim != D || nq % nkv || (ROWS % (nq / nkv))) return -1;
   PrefillParams p;
@@ -509,6 +564,8 @@ int sdc_attn_prefill(const void* q, void* o, const void* cache, const int* block
   p.nkv = nkv;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.row_sq = static_cast<float*>(row_sq);
+  p.check = static_cast<unsigned long long*>(check);
+  if (p.check != nullptr && row_idx == nullptr) return -1;
   const int smem = ROWS * 256 + 4 * BN * 256;
   static bool attr = false;
   if (!attr) {
@@ -526,7 +583,7 @@ int sdc_attn_decode_splits(int max_ctx) { return (max_ctx + SPLIT - 1) / SPLIT; 
 // every sequence index used (seq_idx entries included) and max_splits = sdc_attn_decode_splits(max_ctx).
 int sdc_attn_decode(const void* q, void* o, const void* cache, const int* block_table, int max_pages,
                     const int* seq_req, const int* ctx, const int* seq_idx, int nseq, int nq, int nkv, int head_dim,
-                    int max_ctx, float scale, void* part, void* row_sq, void* stream) {
+                    int max_ctx, float scale, void* part, void* row_sq, void* check, void* stream) {
   if (nseq <= 0) return 0;
   if (head_dim != D || nq % nkv || part == nullptr) return -1;
   DecodeParams p;
@@ -544,18 +601,20 @@ int sdc_attn_decode(const void* q, void* o, const void* cache, const int* block_
   p.scale_log2 = scale * 1.4426950408889634f;
   p.part = static_cast<float*>(part);
   p.row_sq = static_cast<float*>(row_sq);
+  p.err = nullptr;
+  p.check = static_cast<unsigned long long*>(check);
+  if (p.check != nullptr && seq_idx == nullptr) return -1;
   const int G = nq / nkv;
   dim3 grid(nseq, nkv, p.max_splits), grid2(nseq, nkv);
   auto st = static_cast<cudaStream_t>(stream);
   switch (G) {
-    case 1: decode_split_kernel<1><<<grid, 128, 0, st>>>(p); decode_combine_kernel<1><<<grid2, 128, 0, st>>>(p); break;
-    case 2: decode_split_kernel<2><<<grid, 128, 0, st>>>(p); decode_combine_kernel<2><<<grid2, 128, 0, st>>>(p); break;
-    case 4: decode_split_kernel<4><<<grid, 128, 0, st>>>(p); decode_combine_kernel<4><<<grid2, 128, 0, st>>>(p); break;
-    case 8: decode_split_kernel<8><<<grid, 128, 0, st>>>(p); decode_combine_kernel<8><<<grid2, 128, 0, st>>>(p); break;
+    case 1: return launch_decode<1>(p, grid, grid2, st);
+    case 2: return launch_decode<2>(p, grid, grid2, st);
+    case 4: return launch_decode<4>(p, grid, grid2, st);
+    case 8: return launch_decode<8>(p, grid, grid2, st);
     default:
       return -1;
   }
-  return static_cast<int>(cudaGetLastError());
 }
 
 }  // extern "C"

@@ -195,6 +195,22 @@ __device__ __forceinline__ uint32_t seal_term(uint32_t word, uint32_t w) {
 // ---------------------------------------------------------------- numeric helpers
 __device__ __forceinline__ float u32_as_f32(uint32_t u) { return __uint_as_float(u); }
 
+// ---------------------------------------------------------------- exact replay comparison
+// A replayed value must equal the first run's value as a number (a sign-of-zero difference is not an error;
+// two NaNs compare equal). Returns true when the two packed bf16 pairs differ.
+__device__ __forceinline__ bool bf16x2_differ(uint32_t a, uint32_t b) {
+  const float2 x = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&a));
+  const float2 y = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&b));
+  const bool d0 = !(x.x == y.x) && !(x.x != x.x && y.x != y.x);
+  const bool d1 = !(x.y == y.y) && !(x.y != x.y && y.y != y.y);
+  return d0 || d1;
+}
+// Reports a replay mismatch into a state row as an infinite score at `flat` (row * width + column).
+__device__ __forceinline__ void report_replay_mismatch(unsigned long long* state, unsigned long long flat) {
+  atomicMax(state + 0, (0x7f800000ull << 32) | (flat & 0xffffffffull));
+  atomicMax(state + 1, 0x7f800000ull << 32);
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);

@@ -8,6 +8,10 @@
 //     k, v into the paged KV cache at each token's slot.
 //   * silu_mul: out = silu(gate) * up, with ||out_row||^2.
 //
+// Check mode (add_rmsnorm, silu_mul): with `check` (a state row) and `rows`, the kernel recomputes the sampled
+// rows and compares every value with what the first launch stored at those rows, instead of writing; a
+// mismatch is an infinite score at (row * width + column). One check is counted per launch.
+//
 // Paged KV cache layout for one layer: [num_blocks][2 (K, V)][kv_heads][16 tokens][head_dim] bf16.
 #include "common.cuh"
 
@@ -19,6 +23,19 @@ __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int m = 16; m > 0; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
   return v;
+}
+
+// Check mode: the CTA's first mismatching column (min over threads), reported once; launch counted by CTA 0.
+__device__ __forceinline__ void replay_report_block(unsigned long long* state, int bad, long long row, int width,
+                                                    int* sbad) {
+  if (threadIdx.x == 0) *sbad = 0x7fffffff;
+  __syncthreads();
+  if (bad != 0x7fffffff) atomicMin(sbad, bad);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (blockIdx.x == 0) atomicAdd(state + 2, 1ull);
+    if (*sbad != 0x7fffffff) report_replay_mismatch(state, static_cast<unsigned long long>(row) * width + *sbad);
+  }
 }
 
 template <int NT>
@@ -41,8 +58,11 @@ __global__ void __launch_bounds__(128) add_rmsnorm_kernel(const __nv_bfloat16* _
                                                           const __nv_bfloat16* residual,
                                                           const __nv_bfloat16* __restrict__ w, float eps, int H,
                                                           __nv_bfloat16* __restrict__ y, __nv_bfloat16* resid_out,
-                                                          float* __restrict__ row_sq, const int* rows) {
+                                                          float* __restrict__ row_sq, const int* rows,
+                                                          unsigned long long* check) {
   __shared__ float red[4];
+  __shared__ int sbad;
+  int bad = 0x7fffffff;
   const long long row = blockIdx.x;
   const long long in_row = rows ? rows[blockIdx.x] : row;
   const __nv_bfloat16* xr = x + in_row * H;
@@ -102,8 +122,20 @@ __global__ void __launch_bounds__(128) add_rmsnorm_kernel(const __nv_bfloat16* _
         float2 r = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&op[i]));
         ys = fmaf(r.x, r.x, fmaf(r.y, r.y, ys));
       }
-      *reinterpret_cast<uint4*>(y + row * H + col) = o;
+      if (check == nullptr) {
+        *reinterpret_cast<uint4*>(y + row * H + col) = o;
+      } else {
+        const uint4 f = *reinterpret_cast<const uint4*>(y + in_row * H + col);
+        const uint32_t* fp = reinterpret_cast<const uint32_t*>(&f);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          if (bad == 0x7fffffff && bf16x2_differ(op[i], fp[i])) bad = col + 2 * i;
+      }
     }
+  }
+  if (check != nullptr) {
+    replay_report_block(check, bad, in_row, H, &sbad);
+    return;
   }
   const float yt = block_sum<128>(ys, red);
   if (threadIdx.x == 0 && row_sq != nullptr) row_sq[row] = yt;
@@ -187,8 +219,10 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(
 // out[row, :] = silu(gu[row, :I]) * gu[row, I:]; one CTA of 128 threads per row, I % 8 == 0.
 __global__ void __launch_bounds__(128) silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, int I,
                                                        __nv_bfloat16* __restrict__ out, float* __restrict__ row_sq,
-                                                       const int* rows) {
+                                                       const int* rows, unsigned long long* check) {
   __shared__ float red[4];
+  __shared__ int sbad;
+  int bad = 0x7fffffff;
   const long long row = blockIdx.x;
   const long long in_row = rows ? rows[blockIdx.x] : row;
   const __nv_bfloat16* g = gu + in_row * 2 * I;
@@ -211,7 +245,19 @@ __global__ void __launch_bounds__(128) silu_mul_kernel(const __nv_bfloat16* __re
       float2 r = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&op[i]));
       ss = fmaf(r.x, r.x, fmaf(r.y, r.y, ss));
     }
-    *reinterpret_cast<uint4*>(out + row * I + col) = o;
+    if (check == nullptr) {
+      *reinterpret_cast<uint4*>(out + row * I + col) = o;
+    } else {
+      const uint4 f = *reinterpret_cast<const uint4*>(out + in_row * I + col);
+      const uint32_t* fp = reinterpret_cast<const uint32_t*>(&f);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if (bad == 0x7fffffff && bf16x2_differ(op[i], fp[i])) bad = col + 2 * i;
+    }
+  }
+  if (check != nullptr) {
+    replay_report_block(check, bad, in_row, I, &sbad);
+    return;
   }
   const float t = block_sum<128>(ss, red);
   if (threadIdx.x == 0 && row_sq != nullptr) row_sq[row] = t;
@@ -222,7 +268,7 @@ __global__ void __launch_bounds__(128) silu_mul_kernel(const __nv_bfloat16* __re
 extern "C" {
 
 int sdc_add_rmsnorm_bf16(const void* x, const void* residual, const void* w, float eps, int M, int H, void* y,
-                         void* resid_out, void* row_sq, const int* rows, void* stream) {
+                         void* resid_out, void* row_sq, const int* rows, void* check, void* stream) {
   if (M <= 0) return 0;
   if (H % 8 || H > 8192) return -1;
   auto st = static_cast<cudaStream_t>(stream);
@@ -233,10 +279,12 @@ int sdc_add_rmsnorm_bf16(const void* x, const void* residual, const void* w, flo
   auto Y = static_cast<__nv_bfloat16*>(y);
   auto RO = static_cast<__nv_bfloat16*>(resid_out);
   auto S = static_cast<float*>(row_sq);
-  if (vpt <= 1) sdc::add_rmsnorm_kernel<1><<<M, 128, 0, st>>>(X, R, W, eps, H, Y, RO, S, rows);
-  else if (vpt <= 2) sdc::add_rmsnorm_kernel<2><<<M, 128, 0, st>>>(X, R, W, eps, H, Y, RO, S, rows);
-  else if (vpt <= 4) sdc::add_rmsnorm_kernel<4><<<M, 128, 0, st>>>(X, R, W, eps, H, Y, RO, S, rows);
-  else sdc::add_rmsnorm_kernel<8><<<M, 128, 0, st>>>(X, R, W, eps, H, Y, RO, S, rows);
+  auto C = static_cast<unsigned long long*>(check);
+  if (C != nullptr && (rows == nullptr || RO != nullptr)) return -1;   // check mode: sampled rows, no writes
+  if (vpt <= 1) sdc::add_rmsnorm_kernel<1><<<M, 128, 0, st>>>(X, R, W, eps, H, Y, RO, S, rows, C);
+  else if (vpt <= 2) sdc::add_rmsnorm_kernel<2><<<M, 128, 0, st>>>(X, R, W, eps, H, Y, RO, S, rows, C);
+  else if (vpt <= 4) sdc::add_rmsnorm_kernel<4><<<M, 128, 0, st>>>(X, R, W, eps, H, Y, RO, S, rows, C);
+  else sdc::add_rmsnorm_kernel<8><<<M, 128, 0, st>>>(X, R, W, eps, H, Y, RO, S, rows, C);
   return static_cast<int>(cudaGetLastError());
 }
 
@@ -255,11 +303,13 @@ int sdc_qk_norm_rope_kv(const void* qkv, long long ld, int T, int nq, int nkv, i
   return static_cast<int>(cudaGetLastError());
 }
 
-int sdc_silu_mul_bf16(const void* gu, int M, int I, void* out, void* row_sq, const int* rows, void* stream) {
+int sdc_silu_mul_bf16(const void* gu, int M, int I, void* out, void* row_sq, const int* rows, void* check,
+                      void* stream) {
   if (M <= 0) return 0;
-  if (I % 8) return -1;
+  if (I % 8 || (check != nullptr && rows == nullptr)) return -1;
   sdc::silu_mul_kernel<<<M, 128, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(gu), I, static_cast<__nv_bfloat16*>(out), static_cast<float*>(row_sq), rows);
+      static_cast<const __nv_bfloat16*>(gu), I, static_cast<__nv_bfloat16*>(out), static_cast<float*>(row_sq), rows,
+      static_cast<unsigned long long*>(check));
   return static_cast<int>(cudaGetLastError());
 }
 

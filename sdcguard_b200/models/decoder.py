@@ -159,14 +159,10 @@ class CheckedDecoder:
             qkv=torch.empty(T, (nq + 2 * nkv) * D, dtype=bf, device=dev),
             q=torch.empty(T, nq, D, dtype=bf, device=dev),
             attn=torch.empty(T, nq, D, dtype=bf, device=dev),
-            attn_rep=torch.empty(T, nq, D, dtype=bf, device=dev),
             ors=torch.empty(T, dtype=torch.float32, device=dev),
             a=torch.empty(T, H, dtype=bf, device=dev),
             gu=torch.empty(T, 2 * self.inter, dtype=bf, device=dev),
             act=torch.empty(T, self.inter, dtype=bf, device=dev),
-            y_rep=torch.empty(max(1, T // 32 + 64), H, dtype=bf, device=dev),
-            act_rep=torch.empty(max(1, T // 32 + 64), self.inter, dtype=bf, device=dev),
-            rs_rep=torch.empty(max(1, T // 32 + 64), dtype=torch.float32, device=dev),
         )
         if self.checked:
             gemm.reserve_workspace(dev, T, max(2 * self.inter, (nq + 2 * nkv) * D, H))
@@ -206,7 +202,6 @@ class CheckedDecoder:
         torch.index_select(self.embed, 0, meta.tokens, out=x)
         S = meta.sample_rows
         chk = self.checked and S is not None and S.numel() > 0
-        s_n = S.shape[0] if chk else 0
         nq, nkv, D = self.nq, self.nkv, cfg.head_dim
         for i, lw in enumerate(self.layers):
             lc = cache[i]
@@ -215,9 +210,7 @@ class CheckedDecoder:
             else:
                 layers.add_rmsnorm(x, lw.ln1, cfg.rms_eps, residual=resid, resid_out=resid, out=y, row_sq=rs)
             if chk:
-                yr, _ = layers.add_rmsnorm(resid, lw.ln1, cfg.rms_eps, out=B["y_rep"][:s_n], row_sq=B["rs_rep"][:s_n],
-                                           rows=S)
-                layers.compare_rows(y, S, yr, self._st(f"L{i}.norm1"))
+                layers.add_rmsnorm(resid, lw.ln1, cfg.rms_eps, out=y, rows=S, check=self._st(f"L{i}.norm1"))
             self._linear(y, lw.qkv, lw.cw.get("qkv"), f"L{i}.qkv", qkv, rs)
             layers.qk_norm_rope_kv(qkv, nq, nkv, meta.pos, meta.slots, lw.q_norm, lw.k_norm, cfg.rms_eps, self.rope,
                                    q, lc)
@@ -228,32 +221,23 @@ class CheckedDecoder:
             if meta.mode == "prefill":
                 attention.prefill(q, lc, meta.block_table, meta.pos, meta.tiles, nq, nkv, out=att, row_sq=ors)
                 if chk:
-                    rep = B["attn_rep"][:T]
-                    attention.prefill(q, lc, meta.block_table, meta.pos, meta.sample_tiles, nq, nkv, out=rep,
-                                      row_idx=meta.sample_idx)
-                    layers.compare_rows(att.view(T, -1), meta.sample_idx, rep.view(T, -1).index_select(
-                        0, meta.sample_idx), self._st(f"L{i}.attn"))
+                    attention.prefill(q, lc, meta.block_table, meta.pos, meta.sample_tiles, nq, nkv, out=att,
+                                      row_idx=meta.sample_idx, check=self._st(f"L{i}.attn"))
             else:
                 scratch = self.decode_scratch(T, meta.max_ctx)
                 attention.decode(q, lc, meta.block_table, meta.seq_req, meta.ctx, nq, nkv, meta.max_ctx, out=att,
                                  row_sq=ors, scratch=scratch)
                 if chk:
-                    rep = B["attn_rep"][:T]
                     attention.decode(q, lc, meta.block_table, meta.seq_req, meta.ctx, nq, nkv, meta.max_ctx,
-                                     out=rep, seq_idx=S, scratch=scratch)
-                    layers.compare_rows(att.view(T, -1), S, rep.view(T, -1).index_select(0, S),
-                                        self._st(f"L{i}.attn"))
+                                     out=att, seq_idx=S, scratch=scratch, check=self._st(f"L{i}.attn"))
             self._linear(att.view(T, nq * D), lw.o, lw.cw.get("o"), f"L{i}.o", a, ors)
             layers.add_rmsnorm(a, lw.ln2, cfg.rms_eps, residual=resid, resid_out=resid, out=y, row_sq=rs)
             if chk:
-                yr, _ = layers.add_rmsnorm(resid, lw.ln2, cfg.rms_eps, out=B["y_rep"][:s_n], row_sq=B["rs_rep"][:s_n],
-                                           rows=S)
-                layers.compare_rows(y, S, yr, self._st(f"L{i}.norm2"))
+                layers.add_rmsnorm(resid, lw.ln2, cfg.rms_eps, out=y, rows=S, check=self._st(f"L{i}.norm2"))
             self._linear(y, lw.gate_up, lw.cw.get("gate_up"), f"L{i}.gate_up", gu, rs)
             layers.silu_mul(gu, out=act, row_sq=rs)
             if chk:
-                ar, _ = layers.silu_mul(gu, out=B["act_rep"][:s_n], row_sq=B["rs_rep"][:s_n], rows=S)
-                layers.compare_rows(act, S, ar, self._st(f"L{i}.act"))
+                layers.silu_mul(gu, out=act, rows=S, check=self._st(f"L{i}.act"))
             self._linear(act, lw.down, lw.cw.get("down"), f"L{i}.down", x, rs)
         # final norm on the rows that produce tokens, then the LM head
         L = meta.logits_rows.shape[0]
@@ -262,8 +246,7 @@ class CheckedDecoder:
         yl, rsl = layers.add_rmsnorm(xs, self.final_ln, cfg.rms_eps, residual=rsd, resid_out=rsd)
         if self.checked:
             one = torch.zeros(1, dtype=torch.int32, device=self.device)
-            yr, _ = layers.add_rmsnorm(rsd, self.final_ln, cfg.rms_eps, rows=one)
-            layers.compare_rows(yl, one, yr, self._st("final_norm"))
+            layers.add_rmsnorm(rsd, self.final_ln, cfg.rms_eps, out=yl, rows=one, check=self._st("final_norm"))
         logits = torch.empty(L, cfg.vocab, dtype=torch.bfloat16, device=self.device)
         if self.checked:
             gemm.checked_linear(yl, self.lm_cw, self.state.state, self.slot["lm_head"], row_sq=rsl, out=logits)

@@ -120,11 +120,7 @@ class TPDecoder:
                           act=torch.empty(T, self.inter, dtype=bf, device=dev),
                           xs=torch.empty(R, H, dtype=bf, device=dev), resid=torch.empty(R, H, dtype=bf, device=dev),
                           ys=torch.empty(R, H, dtype=bf, device=dev), rss=torch.empty(R, dtype=torch.float32, device=dev),
-                          part=torch.empty(T, H, dtype=bf, device=dev),
-                          attn_rep=torch.empty(T, self.nq, D, dtype=bf, device=dev),
-                          y_rep=torch.empty(max(1, T // 32 + 64), H, dtype=bf, device=dev),
-                          act_rep=torch.empty(max(1, T // 32 + 64), self.inter, dtype=bf, device=dev),
-                          rs_rep=torch.empty(max(1, T // 32 + 64), dtype=torch.float32, device=dev))
+                          part=torch.empty(T, H, dtype=bf, device=dev))
         if self.checked:
             gemm.reserve_workspace(dev, T, max(2 * self.inter, H, (self.nq + 2 * self.nkv) * D))
             gemm.reserve_workspace(dev, min(T, 1024), self.vocab_l)
@@ -176,11 +172,7 @@ class TPDecoder:
         return self.state.state[self.slot[name]]
 
     def _norm_replay(self, ys, w, R, S_loc, name):
-        B = self._bufs
-        n = S_loc.shape[0]
-        yr, _ = layers.add_rmsnorm(B["resid"][:R], w, self.cfg.rms_eps, out=B["y_rep"][:n], row_sq=B["rs_rep"][:n],
-                                   rows=S_loc)
-        layers.compare_rows(ys, S_loc, yr, self._st(name))
+        layers.add_rmsnorm(self._bufs["resid"][:R], w, self.cfg.rms_eps, out=ys, rows=S_loc, check=self._st(name))
 
     def forward(self, meta: StepMeta, cache: torch.Tensor) -> torch.Tensor:
         cfg = self.cfg
@@ -204,7 +196,6 @@ class TPDecoder:
         S = meta.sample_rows
         chk = self.checked and S is not None and S.numel() > 0
         S_loc = torch.remainder(S, R).to(torch.int32) if chk else None
-        s_n = S.shape[0] if chk else 0
         torch.index_select(self.embed, 0, meta.tokens[self.rank * R:(self.rank + 1) * R], out=xs)
         for i, lw in enumerate(self.layers):
             lc = cache[i]
@@ -225,21 +216,15 @@ class TPDecoder:
                 attention.prefill(q, lc, meta.block_table, meta.pos, meta.tiles, nq, nkv, out=att,
                                   row_sq=ors if self.checked else None)
                 if chk:
-                    rep = B["attn_rep"][:T]
-                    attention.prefill(q, lc, meta.block_table, meta.pos, meta.sample_tiles, nq, nkv, out=rep,
-                                      row_idx=meta.sample_idx)
-                    layers.compare_rows(att.view(T, -1), meta.sample_idx, rep.view(T, -1).index_select(
-                        0, meta.sample_idx), self._st(f"L{i}.attn"))
+                    attention.prefill(q, lc, meta.block_table, meta.pos, meta.sample_tiles, nq, nkv, out=att,
+                                      row_idx=meta.sample_idx, check=self._st(f"L{i}.attn"))
             else:
                 scratch = self.decode_scratch(T0, meta.max_ctx)
                 attention.decode(q[:T0], lc, meta.block_table, meta.seq_req, meta.ctx, nq, nkv, meta.max_ctx,
                                  out=att[:T0], row_sq=ors if self.checked else None, scratch=scratch)
                 if chk:
-                    rep = B["attn_rep"][:T0]
                     attention.decode(q[:T0], lc, meta.block_table, meta.seq_req, meta.ctx, nq, nkv, meta.max_ctx,
-                                     out=rep, seq_idx=S, scratch=scratch)
-                    layers.compare_rows(att.view(T, -1), S, rep.view(T0, -1).index_select(0, S),
-                                        self._st(f"L{i}.attn"))
+                                     out=att[:T0], seq_idx=S, scratch=scratch, check=self._st(f"L{i}.attn"))
             self._rowpar(att.view(T, nq * D), lw.o, lw.cw.get("o"), f"L{i}.o", T, R, ors, xs)
             ys = self._norm_into_shard(xs, lw.ln2, B["resid"][:R], R)
             if chk:
@@ -249,8 +234,7 @@ class TPDecoder:
             self._linear(yfull, lw.gate_up, lw.cw.get("gate_up"), f"L{i}.gate_up", gu, yrs)
             layers.silu_mul(gu, out=act, row_sq=rs)
             if chk:
-                ar, _ = layers.silu_mul(gu, out=B["act_rep"][:s_n], row_sq=B["rs_rep"][:s_n], rows=S)
-                layers.compare_rows(act, S, ar, self._st(f"L{i}.act"))
+                layers.silu_mul(gu, out=act, rows=S, check=self._st(f"L{i}.act"))
             self._rowpar(act, lw.down, lw.cw.get("down"), f"L{i}.down", T, R, rs, xs)
         ys = self._norm_into_shard(xs, self.final_ln, B["resid"][:R], R)
         if chk:
@@ -266,6 +250,8 @@ class TPDecoder:
 
     def sample(self, logits: torch.Tensor) -> torch.Tensor:
         """Greedy token over the vocabulary shards of all ranks."""
+        if self.world == 1:
+            return torch.argmax(logits, dim=-1)
         mx, idx = logits.float().max(dim=-1)
         pair = torch.stack([mx, (idx + self.rank * self.vocab_l).float()], dim=-1)     # (L, 2)
         allp = torch.empty(self.world, *pair.shape, dtype=pair.dtype, device=pair.device)

@@ -50,21 +50,23 @@ def replay_tiles(sampled: Sequence[Sequence[int]], group: int) -> tuple[torch.Te
 def prefill(q: torch.Tensor, cache: torch.Tensor, block_table: torch.Tensor, pos: torch.Tensor,
             tiles: torch.Tensor, nq: int, nkv: int, out: Optional[torch.Tensor] = None,
             row_idx: Optional[torch.Tensor] = None, row_sq: Optional[torch.Tensor] = None,
-            scale: Optional[float] = None) -> torch.Tensor:
+            scale: Optional[float] = None, check: Optional[torch.Tensor] = None) -> torch.Tensor:
     """q: (T, nq, 128) bf16; tiles/row_idx/pos/block_table int32 on the device. out: (T, nq, 128) or, for a
-    replay, any tensor indexed by the same token ids."""
+    replay, any tensor indexed by the same token ids. With `check` (a state row; replay tiles and row_idx
+    given), the sampled rows are recomputed and compared with `out` instead of written."""
     if out is None:
         out = torch.empty_like(q)
     scale = 1.0 / math.sqrt(128) if scale is None else scale
     _native.check(_native.lib().sdc_attn_prefill(
         q.data_ptr(), out.data_ptr(), cache.data_ptr(), block_table.data_ptr(), block_table.shape[1],
         pos.data_ptr(), tiles.data_ptr(), tiles.shape[0], None if row_idx is None else row_idx.data_ptr(), nq, nkv,
-        128, float(scale), None if row_sq is None else row_sq.data_ptr(), _s(q)), "attention prefill")
+        128, float(scale), None if row_sq is None else row_sq.data_ptr(), None if check is None else check.data_ptr(),
+        _s(q)), "attention prefill")
     return out
 
 
 def decode_scratch(nseq_rows: int, nq: int, nkv: int, max_ctx: int, device) -> torch.Tensor:
-    """Partial-result scratch for `decode` (per sequence, kv head and 256-key chunk)."""
+    """Partial-result scratch for `decode` (per sequence, kv head and 128-key chunk)."""
     splits = int(_native.lib().sdc_attn_decode_splits(int(max_ctx)))
     return torch.empty(nseq_rows * nkv * splits * (nq // nkv) * 132, dtype=torch.float32, device=device)
 
@@ -73,9 +75,10 @@ def decode(q: torch.Tensor, cache: torch.Tensor, block_table: torch.Tensor, seq_
            ctx: torch.Tensor, nq: int, nkv: int, max_ctx: int, out: Optional[torch.Tensor] = None,
            seq_idx: Optional[torch.Tensor] = None, nseq: Optional[int] = None,
            row_sq: Optional[torch.Tensor] = None, scale: Optional[float] = None,
-           scratch: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """q: (B, nq, 128); split-KV: one CTA per (sequence, kv head, 256-key chunk), then a fixed-order combine.
-    seq_idx selects sequences to run (replay). scratch: from `decode_scratch` (allocated here if absent)."""
+           scratch: Optional[torch.Tensor] = None, check: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """q: (B, nq, 128); split-KV: one CTA per (sequence, kv head, 128-key chunk), then a fixed-order combine.
+    seq_idx selects sequences to run (replay). scratch: from `decode_scratch` (allocated here if absent).
+    With `check` (a state row; seq_idx given), the selected rows are recomputed and compared with `out`."""
     if out is None:
         out = torch.empty_like(q)
     scale = 1.0 / math.sqrt(128) if scale is None else scale
@@ -85,8 +88,8 @@ def decode(q: torch.Tensor, cache: torch.Tensor, block_table: torch.Tensor, seq_
     _native.check(_native.lib().sdc_attn_decode(
         q.data_ptr(), out.data_ptr(), cache.data_ptr(), block_table.data_ptr(), block_table.shape[1],
         seq_req.data_ptr(), ctx.data_ptr(), None if seq_idx is None else seq_idx.data_ptr(), n, nq, nkv, 128,
-        int(max_ctx), float(scale), scratch.data_ptr(), None if row_sq is None else row_sq.data_ptr(), _s(q)),
-        "attention decode")
+        int(max_ctx), float(scale), scratch.data_ptr(), None if row_sq is None else row_sq.data_ptr(),
+        None if check is None else check.data_ptr(), _s(q)), "attention decode")
     return out
 
 

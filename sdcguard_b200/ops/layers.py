@@ -20,18 +20,21 @@ def _p(t: Optional[torch.Tensor]):
 
 def add_rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: Optional[torch.Tensor] = None,
                 resid_out: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
-                row_sq: Optional[torch.Tensor] = None, rows: Optional[torch.Tensor] = None):
+                row_sq: Optional[torch.Tensor] = None, rows: Optional[torch.Tensor] = None,
+                check: Optional[torch.Tensor] = None):
     """y = RMSNorm(x (+ residual)) * weight; h = x + residual written to resid_out (may alias residual);
-    ||y_row||^2 to row_sq. Returns (y, row_sq). With `rows`, output row i is computed from input row rows[i]."""
+    ||y_row||^2 to row_sq. Returns (y, row_sq). With `rows`, output row i is computed from input row rows[i].
+    With `check` (a state row) and `rows`: replay check, rows rows[i] of `out` (the first run's output) are
+    recomputed and compared, nothing is written."""
     m = x.shape[0] if rows is None else rows.shape[0]
     h = x.shape[-1]
     if out is None:
         out = torch.empty(m, h, dtype=torch.bfloat16, device=x.device)
-    if row_sq is None:
+    if row_sq is None and check is None:
         row_sq = torch.empty(m, dtype=torch.float32, device=x.device)
     _native.check(_native.lib().sdc_add_rmsnorm_bf16(
         x.data_ptr(), _p(residual), weight.data_ptr(), float(eps), m, h, out.data_ptr(), _p(resid_out),
-        row_sq.data_ptr(), _p(rows), _s(x)), "add_rmsnorm")
+        _p(row_sq), _p(rows), _p(check), _s(x)), "add_rmsnorm")
     return out, row_sq
 
 
@@ -50,15 +53,16 @@ def qk_norm_rope_kv(qkv: torch.Tensor, nq: int, nkv: int, pos: torch.Tensor, slo
 
 
 def silu_mul(gu: torch.Tensor, out: Optional[torch.Tensor] = None, row_sq: Optional[torch.Tensor] = None,
-             rows: Optional[torch.Tensor] = None):
+             rows: Optional[torch.Tensor] = None, check: Optional[torch.Tensor] = None):
+    """out = silu(gate) * up with ||out_row||^2; `rows` / `check` as in add_rmsnorm (replay check in place)."""
     m = gu.shape[0] if rows is None else rows.shape[0]
     i = gu.shape[-1] // 2
     if out is None:
         out = torch.empty(m, i, dtype=torch.bfloat16, device=gu.device)
-    if row_sq is None:
+    if row_sq is None and check is None:
         row_sq = torch.empty(m, dtype=torch.float32, device=gu.device)
-    _native.check(_native.lib().sdc_silu_mul_bf16(gu.data_ptr(), m, i, out.data_ptr(), row_sq.data_ptr(), _p(rows),
-                                                   _s(gu)), "silu_mul")
+    _native.check(_native.lib().sdc_silu_mul_bf16(gu.data_ptr(), m, i, out.data_ptr(), _p(row_sq), _p(rows),
+                                                   _p(check), _s(gu)), "silu_mul")
     return out, row_sq
 
 

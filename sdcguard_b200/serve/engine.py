@@ -79,6 +79,8 @@ class LLMEngine:
         self._graph_replayed = 0           # kernels of this library executed by graph replays
         self.step_counter = 0
         self.stats = {"prefill_tokens": 0, "decode_tokens": 0, "steps": 0}
+        self.phase_timing = False          # record device time of the prefill and decode phases of generate()
+        self.last_phase_ms: dict = {}
 
     # ---------------------------------------------------------------- sampling of replay rows
     def _sample(self, n: int) -> list[int]:
@@ -284,11 +286,20 @@ class LLMEngine:
         pages = [self.alloc.alloc(k) for k in need]
         out_tokens = torch.zeros(N, max_new_tokens, dtype=torch.long, device=dev)
         try:
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)] if self.phase_timing else None
+            if ev:
+                ev[0].record()
             self.prefill(prompts_dev, plens, pages, out_tokens)
+            if ev:
+                ev[1].record()
             self.decode_from(plens, pages, out_tokens, max_new_tokens)
+            if ev:
+                ev[2].record()
             host = torch.empty(N, max_new_tokens, dtype=torch.long, pin_memory=True)
             host.copy_(out_tokens, non_blocking=True)
             torch.cuda.current_stream(dev).synchronize()
+            if ev:
+                self.last_phase_ms = {"prefill": ev[0].elapsed_time(ev[1]), "decode": ev[1].elapsed_time(ev[2])}
             return host
         finally:
             for pg in pages:

@@ -94,11 +94,16 @@ def run(args) -> dict:
         g0 = eng.graph_launches()
         dev_ms, wall_ms = _timed(step, args.steps, world)
         launches = (_native.launch_count() + eng.graph_launches() - g0) // max(1, args.steps)
+        eng.phase_timing = True
+        step()
+        eng.phase_timing = False
+        phases = {k: round(_max(v, world), 2) for k, v in eng.last_phase_ms.items()}
         ev = eng.guard.poll()
         cov = eng.guard.coverage_report()
         outs[arm] = box["out"]
         r = {"dev_ms": dev_ms, "wall_ms": wall_ms, "tokens_per_s": tokens_per_step / (dev_ms / 1e3),
-             "e2e_tokens_per_s": tokens_per_step / (wall_ms / 1e3), "gpu_launches": launches}
+             "e2e_tokens_per_s": tokens_per_step / (wall_ms / 1e3), "gpu_launches": launches,
+             "phase_ms": phases}
         if checked:
             r.update(checks=cov["checks"], unjudged=cov["unjudged"], worst_clean_z=cov["worst_clean_z"],
                      false_alarms=int(_max(len(ev), world)))

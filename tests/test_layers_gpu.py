@@ -147,7 +147,7 @@ def test_prefill_matches_reference_and_replays_exactly(nq, nkv):
     assert (st[0, 0].item() >> 32) == 0x7F800000
 
 
-@pytest.mark.parametrize("nq,nkv", [(16, 8), (32, 8), (4, 1)])
+@pytest.mark.parametrize("nq,nkv", [(16, 8), (32, 8), (4, 1), (64, 8), (8, 8)])
 def test_decode_matches_reference_and_replays_exactly(nq, nkv):
     from sdcguard_b200.ops import attention
     ctxs = [1, 17, 300, 1029]
@@ -167,3 +167,59 @@ def test_decode_matches_reference_and_replays_exactly(nq, nkv):
     attention.decode(q, cache, bt, req, ctx, nq, nkv, max_ctx=2048, out=out2, seq_idx=idx)
     torch.cuda.synchronize()
     assert torch.equal(out2[idx.long()], out[idx.long()])
+
+
+def _z_flat(st_row):
+    from sdcguard_b200.numerics import abft
+    d = abft.decode_state_row(st_row.cpu().tolist())
+    return d["z"], d["flat"], d["checks"]
+
+
+def test_in_kernel_replay_checks_clean_and_flipped():
+    """Check mode of the norm, activation and attention kernels: recompute sampled rows and compare in place."""
+    from sdcguard_b200.ops import attention, layers
+    st = torch.zeros(8, 4, dtype=torch.int64, device=DEV)
+    rows = torch.tensor([3, 17, 40], dtype=torch.int32, device=DEV)
+    x = torch.randn(64, 1024, device=DEV).bfloat16()
+    w = torch.ones(1024, device=DEV).bfloat16()
+    y, _ = layers.add_rmsnorm(x, w, 1e-6)
+    layers.add_rmsnorm(x, w, 1e-6, out=y, rows=rows, check=st[0])
+    y.view(torch.int16)[17, 100] ^= 4
+    layers.add_rmsnorm(x, w, 1e-6, out=y, rows=rows, check=st[1])
+    gu = torch.randn(64, 2 * 512, device=DEV).bfloat16()
+    a, _ = layers.silu_mul(gu)
+    layers.silu_mul(gu, out=a, rows=rows, check=st[2])
+    a.view(torch.int16)[40, 511] ^= 1
+    layers.silu_mul(gu, out=a, rows=rows, check=st[3])
+    # decode
+    ctxs = [33, 300, 1029]
+    nq, nkv = 16, 8
+    cache, bt = _paged_setup(ctxs, [0] * 3, nkv, seed=4)
+    q = (torch.randn(3, nq, 128, device=DEV) * 0.5).bfloat16()
+    ctx = torch.tensor(ctxs, dtype=torch.int32, device=DEV)
+    req = torch.arange(3, dtype=torch.int32, device=DEV)
+    out = attention.decode(q, cache, bt, req, ctx, nq, nkv, max_ctx=2048)
+    sel = torch.tensor([0, 2], dtype=torch.int32, device=DEV)
+    attention.decode(q, cache, bt, req, ctx, nq, nkv, max_ctx=2048, out=out, seq_idx=sel, check=st[4])
+    out.view(torch.int16)[2, 5, 7] ^= 1
+    attention.decode(q, cache, bt, req, ctx, nq, nkv, max_ctx=2048, out=out, seq_idx=sel, check=st[5])
+    # prefill
+    lens = [100, 60]
+    cache2, bt2 = _paged_setup(lens, [0, 0], nkv, seed=5)
+    T = sum(lens)
+    qp = (torch.randn(T, nq, 128, device=DEV) * 0.5).bfloat16()
+    pos = torch.tensor(list(range(100)) + list(range(60)), dtype=torch.int32, device=DEV)
+    tiles = attention.prefill_tiles([0, 100], lens, nq // nkv).to(DEV)
+    op = attention.prefill(qp, cache2, bt2, pos, tiles, nq, nkv)
+    rt, ridx = attention.replay_tiles([[5, 99], [130]], nq // nkv)
+    attention.prefill(qp, cache2, bt2, pos, rt.to(DEV), nq, nkv, out=op, row_idx=ridx.to(DEV), check=st[6])
+    op.view(torch.int16)[130, 3, 64] ^= 2
+    attention.prefill(qp, cache2, bt2, pos, rt.to(DEV), nq, nkv, out=op, row_idx=ridx.to(DEV), check=st[7])
+    torch.cuda.synchronize()
+    for clean in (0, 2, 4, 6):
+        z, _, n = _z_flat(st[clean])
+        assert z == 0 and n == 1, (clean, z, n)
+    assert _z_flat(st[1])[:2] == (math.inf, 17 * 1024 + 100)
+    assert _z_flat(st[3])[:2] == (math.inf, 40 * 512 + 511)
+    assert _z_flat(st[5])[:2] == (math.inf, 2 * nq * 128 + 5 * 128 + 7)
+    assert _z_flat(st[7])[:2] == (math.inf, 130 * nq * 128 + 3 * 128 + 64)
