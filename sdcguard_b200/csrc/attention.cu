@@ -14,6 +14,7 @@
 // attention by a sampled fp32 recompute against an error bound (src/sdcguard/serve_attn.py:5-48, kernels
 // `_attn_part` :335 and `_attn_judge` :414); an exact replay needs no bound and sees every flipped bit.
 #include "common.cuh"
+#include "tma_host.h"
 
 namespace sdc {
 namespace attn {
@@ -264,17 +265,17 @@ __global__ void __launch_bounds__(WARPS * 32, 1) prefill_kernel(const PrefillPar
       if (tok0 >= 0) *o0 = v0;
       if (tok1 >= 0) *o1 = v1;
     } else {
-      if (tok0 >= 0 && bf16x2_differ(v0, *o0))
-        report_replay_mismatch(p.check, static_cast<unsigned long long>(tok0) * p.nq * D + h0 * D + d);
-      if (tok1 >= 0 && bf16x2_differ(v1, *o1))
-        report_replay_mismatch(p.check, static_cast<unsigned long long>(tok1) * p.nq * D + h1 * D + d);
+      const int e0 = tok0 >= 0 ? bf16x2_diff(v0, *o0) : -1;
+      const int e1 = tok1 >= 0 ? bf16x2_diff(v1, *o1) : -1;
+      if (e0 >= 0) report_replay_mismatch(p.check, static_cast<unsigned long long>(tok0) * p.nq * D + h0 * D + d + e0);
+      if (e1 >= 0) report_replay_mismatch(p.check, static_cast<unsigned long long>(tok1) * p.nq * D + h1 * D + d + e1);
     }
     const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v0));
     const float2 f1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v1));
     sq0 = fmaf(f0.x, f0.x, fmaf(f0.y, f0.y, sq0));
     sq1 = fmaf(f1.x, f1.x, fmaf(f1.y, f1.y, sq1));
   }
-  if (p.check != nullptr && blockIdx.x == 0 && threadIdx.x == 0) atomicAdd(p.check + 2, 1ull);
+  if (p.check != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) atomicAdd(p.check + 2, 1ull);
   if (p.row_sq != nullptr && p.check == nullptr) {
     sq0 += __shfl_xor_sync(0xffffffffu, sq0, 1);
     sq0 += __shfl_xor_sync(0xffffffffu, sq0, 2);
@@ -293,14 +294,17 @@ __global__ void __launch_bounds__(WARPS * 32, 1) prefill_kernel(const PrefillPar
 // and a combine kernel merges the chunks of a row in a fixed order. Chunk boundaries and reduction orders
 // depend only on the row, so a replay of any subset of sequences reproduces their outputs bit for bit.
 //
-// Memory path: decode reads every K and V byte of the context once, so the kernel is bound by HBM. Each CTA
-// stages its chunk with bulk copies (one 4 KB `cp.async.bulk` per page for K and for V, completing on two
-// mbarriers) so that the whole chunk (32 KB of K, 32 KB of V) is in flight at once without holding registers,
-// and computes from shared memory: QK^T starts when K has landed while V is still arriving.
-//  - QK^T: thread = key; the 16 chunks of 8 dims of a key row are visited in a rotated order (chunk (i + lane)
-//    mod 16), so the 8 lanes of each shared-memory phase read 8 different 16-byte bank groups of K and of q.
-//  - PV: warp = 32 keys, lane = 4 output dims; V rows are read as contiguous 256-byte rows.
-constexpr int SPLIT = 128;                 // keys per chunk (8 pages)
+// Memory path: decode reads every K and V byte of the context once, so the kernel is bound by HBM. A CTA owns
+// one (sequence, kv head) and every gridDim.z-th chunk of it; TMA copies each chunk's pages (one 16-row x
+// 128-byte box per page, half head dim and K or V, with the 128-byte swizzle) into one of two buffers, so the
+// copies of the next chunk are in flight while the current chunk is computed. The sequence's block-table row
+// is read once into shared memory.
+// Arithmetic on tensor cores (mma.m16n8k16, bf16 in, fp32 accumulate): the G query heads of the kv head are
+// the rows of the A operand (rows G..15 are zero); each warp takes 16 keys of the chunk: S = Q K^T from
+// swizzle-conflict-free ldmatrix loads of K, the chunk's softmax statistics across the four warps through
+// shared memory, then O_w = P V with P kept in registers as the A operand. The chunk record is the sum of the
+// four warps' O in a fixed order, so it depends only on the chunk, not on which CTA computed it.
+constexpr int SPLIT = 64;                  // keys per chunk (4 pages)
 constexpr int REC = D + 4;                 // floats per partial record: o[D], m, l, pad
 constexpr int PAGE_BYTES = PAGE * D * 2;   // 4 KB: one page of K (or V) of one kv head
 
@@ -322,16 +326,23 @@ struct DecodeParams {
   unsigned long long* check;  // check mode (replay): compare with o instead of writing (state row), or null
 };
 
+constexpr int MAX_BT = 512;                // block-table entries staged per sequence (8192 tokens)
+constexpr int HALF_BYTES = SPLIT * 128;    // one half (64 dims) of the chunk's K or V rows: 8 KB
+
 template <int G>
 struct DecodeSmem {
-  __nv_bfloat16 k[SPLIT * D];           // 32 KB; reused for the per-warp PV partials after QK^T
-  __nv_bfloat16 v[SPLIT * D];           // 32 KB
-  __nv_bfloat16 q[G * D];
-  float p[G][SPLIT];                    // logits, then exp2(logit - max)
-  float red[4][G];
-  float stat[2][G];
-  uint64_t bar[2];
+  uint8_t k[2][2 * HALF_BYTES];         // [buffer][half][key][128 B, swizzled]; reused for per-warp O partials
+  uint8_t v[2][2 * HALF_BYTES];
+  float red[4][8];                      // per-warp row maxima
+  float red2[4][8];                     // per-warp row sums
+  int bt[MAX_BT];
+  uint64_t bar[2][2];                   // [buffer][K, V]
 };
+
+// byte offset of 16-byte chunk j (0..15 over the head dim) of row `key` in a [half][key][128 B] swizzled buffer
+__device__ __forceinline__ uint32_t kv_off(int key, int j) {
+  return static_cast<uint32_t>((j >> 3) * HALF_BYTES + key * 128 + (((j & 7) ^ (key & 7)) << 4));
+}
 
 __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
@@ -351,158 +362,216 @@ __device__ __forceinline__ void bf8_to_f32(const uint4& u, float (&f)[8]) {
 }
 
 template <int G>
-__global__ void __launch_bounds__(128) decode_split_kernel(const DecodeParams p) {
-  extern __shared__ __align__(128) unsigned char dsm_raw[];
-  DecodeSmem<G>& sm = *reinterpret_cast<DecodeSmem<G>*>(dsm_raw);
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int b = p.seq_idx ? p.seq_idx[blockIdx.x] : blockIdx.x;
-  const int kvh = blockIdx.y, sp = blockIdx.z;
-  const int n = p.ctx[b];
+__device__ __forceinline__ void decode_issue(DecodeSmem<G>& sm, const CUtensorMap* tm, const DecodeParams& p, int buf,
+                                             int sp, int n, int kvh, int lane) {
   const int k0 = sp * SPLIT;
-  if (k0 >= n) return;
-  const int nk = min(SPLIT, n - k0);
-  const int npages = (nk + PAGE - 1) / PAGE;
-  if (tid == 0) {
-    mbar_init(&sm.bar[0], 1);
-    mbar_init(&sm.bar[1], 1);
-    fence_mbar_init();
+  const int npages = (min(SPLIT, n - k0) + PAGE - 1) / PAGE;
+  if (lane == 0) {
+    mbar_arrive_expect_tx(&sm.bar[buf][0], npages * PAGE_BYTES);
+    mbar_arrive_expect_tx(&sm.bar[buf][1], npages * PAGE_BYTES);
   }
-  __syncthreads();
-  if (warp == 0) {
-    if (lane == 0) {
-      mbar_arrive_expect_tx(&sm.bar[0], npages * PAGE_BYTES);
-      mbar_arrive_expect_tx(&sm.bar[1], npages * PAGE_BYTES);
-    }
-    __syncwarp();
-    if (lane < 2 * npages) {          // lanes 0..npages-1 copy K pages, the next npages lanes V pages
-      const int pg = lane % npages, kv = lane / npages;
-      const long long blk = p.block_table[static_cast<long long>(p.seq_req[b]) * p.max_pages + k0 / PAGE + pg];
-      const __nv_bfloat16* src = p.cache + (((blk * 2 + kv) * p.nkv + kvh) * PAGE) * D;
-      bulk_load((kv ? sm.v : sm.k) + pg * PAGE * D, src, PAGE_BYTES, &sm.bar[kv]);
-    }
-  }
-  for (int i = tid; i < G * D / 8; i += 128)
-    reinterpret_cast<uint4*>(sm.q)[i] =
-        reinterpret_cast<const uint4*>(p.q + (static_cast<long long>(b) * p.nq + kvh * G) * D)[i];
-  __syncthreads();
-  bool ok = mbar_wait(&sm.bar[0], 0, nullptr);
-  // QK^T: thread tid = key tid of the chunk
-  float lg[G];
-  {
-    float acc[G];
-#pragma unroll
-    for (int h = 0; h < G; ++h) acc[h] = 0.f;
-    const __nv_bfloat16* krow = sm.k + tid * D;
-#pragma unroll 4
-    for (int i = 0; i < 16; ++i) {
-      const int c = (i + lane) & 15;
-      float kf[8];
-      bf8_to_f32(*reinterpret_cast<const uint4*>(krow + c * 8), kf);
-#pragma unroll
-      for (int h = 0; h < G; ++h) {
-        float qf[8];
-        bf8_to_f32(*reinterpret_cast<const uint4*>(sm.q + h * D + c * 8), qf);
-        float a = acc[h];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) a = fmaf(kf[j], qf[j], a);
-        acc[h] = a;
-      }
-    }
-#pragma unroll
-    for (int h = 0; h < G; ++h) lg[h] = tid < nk ? acc[h] * p.scale_log2 : -INFINITY;
-  }
-  // chunk softmax statistics (fixed-order reductions)
-#pragma unroll
-  for (int h = 0; h < G; ++h) {
-    float mx = lg[h];
-#pragma unroll
-    for (int m = 16; m > 0; m >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, m));
-    if (lane == 0) sm.red[warp][h] = mx;
-  }
-  __syncthreads();
-  float e[G];
-#pragma unroll
-  for (int h = 0; h < G; ++h) {
-    const float mx = fmaxf(fmaxf(sm.red[0][h], sm.red[1][h]), fmaxf(sm.red[2][h], sm.red[3][h]));
-    e[h] = tid < nk ? ex2(lg[h] - mx) : 0.f;
-    sm.p[h][tid] = e[h];
-    if (tid == 0) sm.stat[0][h] = mx;
-  }
-  __syncthreads();        // every thread has read red[] (max) and written p[]
-#pragma unroll
-  for (int h = 0; h < G; ++h) {
-    float sum = e[h];
-#pragma unroll
-    for (int m = 16; m > 0; m >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, m);
-    if (lane == 0) sm.red[warp][h] = sum;
-  }
-  ok = mbar_wait(&sm.bar[1], 0, nullptr) && ok;
-  // PV: warp -> keys [32 warp, 32 warp + 32), lane -> dims 4 lane .. 4 lane + 3
-  float acc[G][4];
-#pragma unroll
-  for (int h = 0; h < G; ++h)
-#pragma unroll
-    for (int j = 0; j < 4; ++j) acc[h][j] = 0.f;
-  const int kbeg = warp * 32, kend = min(kbeg + 32, nk);
-  for (int k = kbeg; k < kend; ++k) {
-    const uint2 u = *reinterpret_cast<const uint2*>(sm.v + k * D + lane * 4);
-    const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
-    const float2 f1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
-#pragma unroll
-    for (int h = 0; h < G; ++h) {
-      const float w = sm.p[h][k];
-      acc[h][0] = fmaf(w, f0.x, acc[h][0]);
-      acc[h][1] = fmaf(w, f0.y, acc[h][1]);
-      acc[h][2] = fmaf(w, f1.x, acc[h][2]);
-      acc[h][3] = fmaf(w, f1.y, acc[h][3]);
-    }
-  }
-  // per-warp partials go where K was (every thread finished QK^T before the first barrier above)
-  float* wpart = reinterpret_cast<float*>(sm.k);     // [4][G][D]
-#pragma unroll
-  for (int h = 0; h < G; ++h)
-    *reinterpret_cast<float4*>(wpart + (warp * G + h) * D + lane * 4) =
-        make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
-  __syncthreads();
-  float* rec = p.part + ((static_cast<long long>(b) * p.nkv + kvh) * p.max_splits + sp) * G * REC;
-  for (int i = tid; i < G * D; i += 128) {
-    const int h = i / D, d = i % D;
-    rec[h * REC + d] = (wpart[(0 * G + h) * D + d] + wpart[(1 * G + h) * D + d]) +
-                       (wpart[(2 * G + h) * D + d] + wpart[(3 * G + h) * D + d]);
-  }
-  if (tid < G) {
-    rec[tid * REC + D] = sm.stat[0][tid];
-    rec[tid * REC + D + 1] = (sm.red[0][tid] + sm.red[1][tid]) + (sm.red[2][tid] + sm.red[3][tid]);
-  }
-  if (!ok && tid == 0) {
-    record_error(p.err, ERR_TIMEOUT_PEER);
-    // the copies were issued by this CTA: give them one more bounded wait before its shared memory is released
-    mbar_wait(&sm.bar[0], 0, nullptr);
-    mbar_wait(&sm.bar[1], 0, nullptr);
+  __syncwarp();
+  if (lane < 4 * npages) {            // lane -> (page, K/V, half)
+    const int pg = lane % npages, w = lane / npages, kv = w >> 1, half = w & 1;
+    const long long blk = sm.bt[k0 / PAGE + pg];
+    const int row = static_cast<int>(((blk * 2 + kv) * p.nkv + kvh) * PAGE);
+    uint8_t* dst = (kv ? sm.v[buf] : sm.k[buf]) + half * HALF_BYTES + pg * PAGE * 128;
+    tma_load_2d(dst, tm, &sm.bar[buf][kv], half * 64, row);
   }
 }
 
-// Merges the chunks of each (sequence, kv head) in chunk order; one CTA of 128 threads, thread = head dim.
+template <int G>
+__global__ void __launch_bounds__(128) decode_split_kernel(const __grid_constant__ CUtensorMap tm, const DecodeParams p) {
+  extern __shared__ __align__(128) unsigned char dsm_raw[];
+  // the swizzled buffers need 1024-byte alignment
+  unsigned char* base = dsm_raw + ((1024 - (smem_u32(dsm_raw) & 1023)) & 1023);
+  DecodeSmem<G>& sm = *reinterpret_cast<DecodeSmem<G>*>(base);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t = lane & 3;          // mma fragment row (head) and column pair
+  const int b = p.seq_idx ? p.seq_idx[blockIdx.x] : blockIdx.x;
+  const int kvh = blockIdx.y;
+  const int n = p.ctx[b];
+  if (static_cast<int>(blockIdx.z) * SPLIT >= n) return;
+  if (tid == 0) {
+    tma_prefetch_desc(&tm);
+    mbar_init(&sm.bar[0][0], 1);
+    mbar_init(&sm.bar[0][1], 1);
+    mbar_init(&sm.bar[1][0], 1);
+    mbar_init(&sm.bar[1][1], 1);
+    fence_mbar_init();
+  }
+  const int npg_all = min((n + PAGE - 1) / PAGE, MAX_BT);
+  const int* btrow = p.block_table + static_cast<long long>(p.seq_req[b]) * p.max_pages;
+  for (int i = tid; i < npg_all; i += 128) sm.bt[i] = btrow[i];
+  // Q as mma A fragments (rows = heads of this kv head, zero beyond G): a0 = (g, 16 ks + 2t), a2 = (g, +8)
+  uint32_t qa[8][2];
+  {
+    const __nv_bfloat16* qrow = p.q + (static_cast<long long>(b) * p.nq + kvh * G + g) * D;
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      qa[ks][0] = g < G ? *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + 2 * t) : 0u;
+      qa[ks][1] = g < G ? *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + 8 + 2 * t) : 0u;
+    }
+  }
+  __syncthreads();
+  if (warp == 0) decode_issue(sm, &tm, p, 0, blockIdx.z, n, kvh, lane);
+  bool ok = true;
+  const int mi = lane >> 3, rr = lane & 7;        // ldmatrix: matrix index and row of this lane's address
+  int it = 0;
+  for (int sp = blockIdx.z; sp * SPLIT < n; sp += gridDim.z, ++it) {
+    const int buf = it & 1;
+    const uint32_t par = (it >> 1) & 1;
+    const int nsp = sp + gridDim.z;
+    if (warp == 0 && nsp * SPLIT < n) decode_issue(sm, &tm, p, buf ^ 1, nsp, n, kvh, lane);   // next chunk
+    const int nk = min(SPLIT, n - sp * SPLIT);
+    ok = mbar_wait(&sm.bar[buf][0], par, nullptr) && ok;
+    // S = Q K^T for keys [16 warp, 16 warp + 16): two n-tiles of 8 keys
+    float sc[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sc[nt][e] = 0.f;
+    {
+      const uint32_t kb = smem_u32(sm.k[buf]);
+      const int key = warp * 16 + (mi >> 1) * 8 + rr;
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(kb + kv_off(key, 2 * ks + (mi & 1)), b0, b1, b2, b3);
+        mma_bf16(sc[0], qa[ks][0], 0u, qa[ks][1], 0u, b0, b1);
+        mma_bf16(sc[1], qa[ks][0], 0u, qa[ks][1], 0u, b2, b3);
+      }
+    }
+    // scores of row g: keys 16 warp + 8 nt + 2 t + e (e = 0, 1); rows g + 8 are padding
+    float x[2][2];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int kk = warp * 16 + nt * 8 + 2 * t + e;
+        x[nt][e] = (kk < nk && g < G) ? sc[nt][e] * p.scale_log2 : -INFINITY;
+        mx = fmaxf(mx, x[nt][e]);
+      }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    if (t == 0) sm.red[warp][g] = mx;
+    __syncthreads();      // (A) red[] complete; every warp is done reading k[buf]
+    const float M = fmaxf(fmaxf(sm.red[0][g], sm.red[1][g]), fmaxf(sm.red[2][g], sm.red[3][g]));
+    uint32_t pa[2];
+    float lsum = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      const float p0 = x[nt][0] == -INFINITY ? 0.f : ex2(x[nt][0] - M);
+      const float p1 = x[nt][1] == -INFINITY ? 0.f : ex2(x[nt][1] - M);
+      pa[nt] = pack_bf16x2(p0, p1);
+      const float2 r = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&pa[nt]));
+      lsum += r.x + r.y;                    // the row sum of the weights the MMA uses
+    }
+    lsum += __shfl_xor_sync(0xffffffffu, lsum, 1);
+    lsum += __shfl_xor_sync(0xffffffffu, lsum, 2);
+    if (t == 0) sm.red2[warp][g] = lsum;
+    ok = mbar_wait(&sm.bar[buf][1], par, nullptr) && ok;
+    if (nk < SPLIT) {
+      // the last chunk of the sequence: V rows past its last page were not loaded (their weights are zero, but
+      // stale shared memory could hold NaN bit patterns); clear them
+      const int r0 = ((nk + PAGE - 1) / PAGE) * PAGE;
+      for (int i = tid; i < (SPLIT - r0) * 16; i += 128) {
+        const int r = r0 + (i >> 4), c = i & 15;
+        *reinterpret_cast<uint4*>(sm.v[buf] + (c >> 3) * HALF_BYTES + r * 128 + (c & 7) * 16) = make_uint4(0, 0, 0, 0);
+      }
+      __syncthreads();
+    }
+    // O_w = P V: 16 n-tiles of 8 dims
+    float o[16][4];
+#pragma unroll
+    for (int dt = 0; dt < 16; ++dt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) o[dt][e] = 0.f;
+    {
+      const uint32_t vb = smem_u32(sm.v[buf]);
+      const int key = warp * 16 + (mi & 1) * 8 + rr;
+#pragma unroll
+      for (int pr = 0; pr < 8; ++pr) {
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(vb + kv_off(key, 2 * pr + (mi >> 1)), b0, b1, b2, b3);
+        mma_bf16(o[2 * pr], pa[0], 0u, pa[1], 0u, b0, b1);
+        mma_bf16(o[2 * pr + 1], pa[0], 0u, pa[1], 0u, b2, b3);
+      }
+    }
+    // per-warp partials (rows < G) go where this chunk's K was (no warp reads k[buf] after barrier A)
+    float* wpart = reinterpret_cast<float*>(sm.k[buf]);     // [4][G][D]
+    if (g < G) {
+#pragma unroll
+      for (int dt = 0; dt < 16; ++dt)
+        *reinterpret_cast<float2*>(wpart + (warp * G + g) * D + dt * 8 + 2 * t) = make_float2(o[dt][0], o[dt][1]);
+    }
+    __syncthreads();      // (C) wpart and red2[] complete
+    float* rec = p.part + ((static_cast<long long>(b) * p.nkv + kvh) * p.max_splits + sp) * G * REC;
+    for (int i = tid; i < G * D; i += 128) {
+      const int h = i / D, d = i % D;
+      rec[h * REC + d] = (wpart[(0 * G + h) * D + d] + wpart[(1 * G + h) * D + d]) +
+                         (wpart[(2 * G + h) * D + d] + wpart[(3 * G + h) * D + d]);
+    }
+    if (tid < G) {
+      rec[tid * REC + D] = fmaxf(fmaxf(sm.red[0][tid], sm.red[1][tid]), fmaxf(sm.red[2][tid], sm.red[3][tid]));
+      rec[tid * REC + D + 1] = (sm.red2[0][tid] + sm.red2[1][tid]) + (sm.red2[2][tid] + sm.red2[3][tid]);
+    }
+    fence_proxy_async_smem();   // this buffer's generic writes (partials, cleared rows) before its next TMA fill
+    __syncthreads();      // (D) buffer buf and red[], red2[] free for later chunks
+  }
+  if (!ok && tid == 0) record_error(p.err, ERR_TIMEOUT_PEER);
+}
+
+// Merges the chunks of each (sequence, kv head) in chunk order; one CTA of 128 threads. The chunk maxima and
+// weights are computed in parallel over chunks, then thread d sums dimension d over the chunks in order.
+constexpr int MAX_SPLITS = MAX_BT * PAGE / SPLIT;
+
 template <int G>
 __global__ void __launch_bounds__(128) decode_combine_kernel(const DecodeParams p) {
+  __shared__ float wsh[G][MAX_SPLITS];
+  __shared__ float Lsh[G];
+  __shared__ float msh[4][G];
   const int b = p.seq_idx ? p.seq_idx[blockIdx.x] : blockIdx.x;
-  const int kvh = blockIdx.y, d = threadIdx.x, lane = d & 31;
+  const int kvh = blockIdx.y, d = threadIdx.x, lane = d & 31, warp = d >> 5;
   const int n = p.ctx[b];
   const int ns = (n + SPLIT - 1) / SPLIT;
   const float* base = p.part + (static_cast<long long>(b) * p.nkv + kvh) * p.max_splits * G * REC;
+  float m[G];
+#pragma unroll
+  for (int h = 0; h < G; ++h) {
+    float v = -INFINITY;
+    for (int s = d; s < ns; s += 128) v = fmaxf(v, base[(s * G + h) * REC + D]);
+#pragma unroll
+    for (int k = 16; k > 0; k >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, k));
+    if (lane == 0) msh[warp][h] = v;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int h = 0; h < G; ++h) {
+    m[h] = fmaxf(fmaxf(msh[0][h], msh[1][h]), fmaxf(msh[2][h], msh[3][h]));
+    for (int s = d; s < ns; s += 128) wsh[h][s] = ex2(base[(s * G + h) * REC + D] - m[h]);
+  }
+  __syncthreads();
+  if (warp == 0) {
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      float l = 0.f;
+      for (int s = lane; s < ns; s += 32) l = fmaf(base[(s * G + h) * REC + D + 1], wsh[h][s], l);
+#pragma unroll
+      for (int k = 16; k > 0; k >>= 1) l += __shfl_xor_sync(0xffffffffu, l, k);
+      if (lane == 0) Lsh[h] = l;
+    }
+  }
+  __syncthreads();
   float sqsum = 0.f;
 #pragma unroll
   for (int h = 0; h < G; ++h) {
-    float M = -INFINITY;
-    for (int s = 0; s < ns; ++s) M = fmaxf(M, base[(s * G + h) * REC + D]);
-    float L = 0.f, acc = 0.f;
-    for (int s = 0; s < ns; ++s) {
-      const float* r = base + (s * G + h) * REC;
-      const float sc = ex2(r[D] - M);
-      L = fmaf(r[D + 1], sc, L);
-      acc = fmaf(r[d], sc, acc);
-    }
-    const __nv_bfloat16 ob = __float2bfloat16(acc / L);
+    float acc = 0.f;
+    const float* r = base + h * REC + d;
+#pragma unroll 8
+    for (int s = 0; s < ns; ++s) acc = fmaf(r[s * G * REC], wsh[h][s], acc);
+    const __nv_bfloat16 ob = __float2bfloat16(acc / Lsh[h]);
     __nv_bfloat16* dst = p.o + (static_cast<long long>(b) * p.nq + kvh * G + h) * D + d;
     if (p.check == nullptr) {
       *dst = ob;
@@ -531,15 +600,15 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(const DecodeParams 
 using namespace sdc::attn;
 
 template <int G>
-static int launch_decode(const DecodeParams& p, dim3 grid, dim3 grid2, cudaStream_t st) {
+static int launch_decode(const DecodeParams& p, const CUtensorMap& tm, dim3 grid, dim3 grid2, cudaStream_t st) {
   static bool attr_set = false;      // per process; the attribute applies to every device
-  const int smem = static_cast<int>(sizeof(DecodeSmem<G>));
+  const int smem = static_cast<int>(sizeof(DecodeSmem<G>)) + 1024;   // + room to align the buffers to 1 KB
   if (!attr_set) {
     cudaError_t e = cudaFuncSetAttribute(decode_split_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return static_cast<int>(e);
     attr_set = true;
   }
-  decode_split_kernel<G><<<grid, 128, smem, st>>>(p);
+  decode_split_kernel<G><<<grid, 128, smem, st>>>(tm, p);
   decode_combine_kernel<G><<<grid2, 128, 0, st>>>(p);
   return static_cast<int>(cudaGetLastError());
 }
@@ -581,11 +650,14 @@ int sdc_attn_decode_splits(int max_ctx) { return (max_ctx + SPLIT - 1) / SPLIT; 
 
 // Scratch: `part` holds nseq_rows x nkv x max_splits x (nq / nkv) x (D + 4) floats, where nseq_rows covers
 // every sequence index used (seq_idx entries included) and max_splits = sdc_attn_decode_splits(max_ctx).
-int sdc_attn_decode(const void* q, void* o, const void* cache, const int* block_table, int max_pages,
-                    const int* seq_req, const int* ctx, const int* seq_idx, int nseq, int nq, int nkv, int head_dim,
-                    int max_ctx, float scale, void* part, void* row_sq, void* check, void* stream) {
+int sdc_attn_decode(const void* q, void* o, const void* cache, long long num_blocks, const int* block_table,
+                    int max_pages, const int* seq_req, const int* ctx, const int* seq_idx, int nseq, int nq, int nkv,
+                    int head_dim, int max_ctx, float scale, void* part, void* row_sq, void* check, void* stream) {
   if (nseq <= 0) return 0;
-  if (head_dim != D || nq % nkv || part == nullptr) return -1;
+  if (head_dim != D || nq % nkv || part == nullptr || nq / nkv > 8) return -1;
+  // the layer's cache as [num_blocks * 2 * nkv * 16 rows, 128] bf16; one box = one page of K or V, half the dims
+  CUtensorMap tm;
+  if (!make_map_bf16_sw128(&tm, cache, num_blocks * 2 * nkv * PAGE, D, D, 64, PAGE)) return -2;
   DecodeParams p;
   p.q = static_cast<const __nv_bfloat16*>(q);
   p.o = static_cast<__nv_bfloat16*>(o);
@@ -605,13 +677,17 @@ int sdc_attn_decode(const void* q, void* o, const void* cache, const int* block_
   p.check = static_cast<unsigned long long*>(check);
   if (p.check != nullptr && seq_idx == nullptr) return -1;
   const int G = nq / nkv;
-  dim3 grid(nseq, nkv, p.max_splits), grid2(nseq, nkv);
+  // CTAs per (sequence, kv head): enough for about four waves of three CTAs per SM over the whole batch
+  int z = (148 * 3 * 4 + nseq * nkv - 1) / (nseq * nkv);
+  z = z < 1 ? 1 : (z > p.max_splits ? p.max_splits : z);
+  if (max_ctx > MAX_BT * PAGE) return -1;
+  dim3 grid(nseq, nkv, z), grid2(nseq, nkv);
   auto st = static_cast<cudaStream_t>(stream);
   switch (G) {
-    case 1: return launch_decode<1>(p, grid, grid2, st);
-    case 2: return launch_decode<2>(p, grid, grid2, st);
-    case 4: return launch_decode<4>(p, grid, grid2, st);
-    case 8: return launch_decode<8>(p, grid, grid2, st);
+    case 1: return launch_decode<1>(p, tm, grid, grid2, st);
+    case 2: return launch_decode<2>(p, tm, grid, grid2, st);
+    case 4: return launch_decode<4>(p, tm, grid, grid2, st);
+    case 8: return launch_decode<8>(p, tm, grid, grid2, st);
     default:
       return -1;
   }

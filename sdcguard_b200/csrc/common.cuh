@@ -197,13 +197,14 @@ __device__ __forceinline__ float u32_as_f32(uint32_t u) { return __uint_as_float
 
 // ---------------------------------------------------------------- exact replay comparison
 // A replayed value must equal the first run's value as a number (a sign-of-zero difference is not an error;
-// two NaNs compare equal). Returns true when the two packed bf16 pairs differ.
-__device__ __forceinline__ bool bf16x2_differ(uint32_t a, uint32_t b) {
+// two NaNs compare equal). Returns the index (0 low, 1 high) of the first differing value of two packed bf16
+// pairs, or -1 when they are equal.
+__device__ __forceinline__ int bf16x2_diff(uint32_t a, uint32_t b) {
   const float2 x = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&a));
   const float2 y = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&b));
-  const bool d0 = !(x.x == y.x) && !(x.x != x.x && y.x != y.x);
-  const bool d1 = !(x.y == y.y) && !(x.y != x.y && y.y != y.y);
-  return d0 || d1;
+  if (!(x.x == y.x) && !(x.x != x.x && y.x != y.x)) return 0;
+  if (!(x.y == y.y) && !(x.y != x.y && y.y != y.y)) return 1;
+  return -1;
 }
 // Reports a replay mismatch into a state row as an infinite score at `flat` (row * width + column).
 __device__ __forceinline__ void report_replay_mismatch(unsigned long long* state, unsigned long long flat) {

@@ -31,6 +31,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "tma_host.h"
 
 namespace sdc {
 namespace gemm {
@@ -53,6 +54,7 @@ struct Params {
   int n_per_m;     // n_main + n_cs
   int m_tiles;
   int total_tiles;
+  int group;       // bands per tile group (L2 rasterisation)
   int csb;         // checksum blocks per checksum tile
   __nv_bfloat16* C;
   long long ldc;
@@ -111,12 +113,22 @@ struct SmemCtl {
   int resunj[2];
 };
 
-// Tile order inside a band: checksum tiles first, then output tiles.
+// Persistent tile order. Bands (128 output rows) are taken in groups of `group` bands; inside a group come
+// first the checksum tiles of all its bands, then its output tiles column-major (the `group` bands of one
+// W slab are consecutive). The tiles in flight at any time then share a few W slabs and the group's A rows,
+// which stay in L2, instead of streaming all of W once per band. Every output tile still comes after the
+// checksum tiles of its band, which is what the band wait relies on.
 __device__ __forceinline__ void tile_coords(const Params& p, int tile, int& mt, bool& cs, int& idx) {
-  mt = tile / p.n_per_m;
-  const int nt = tile - mt * p.n_per_m;
-  cs = nt < p.n_cs;
-  idx = cs ? nt : nt - p.n_cs;
+  const int per_group = p.group * p.n_per_m;
+  const int g = tile / per_group;
+  const int l = tile - g * per_group;
+  const int b0 = g * p.group;
+  const int gm = min(p.group, p.m_tiles - b0);
+  const int ncs = gm * p.n_cs;
+  cs = l < ncs;
+  const int l2 = cs ? l : l - ncs;
+  mt = b0 + l2 % gm;
+  idx = l2 / gm;
 }
 
 __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
@@ -570,37 +582,10 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
 }
 
 // ------------------------------------------------------------------------------------------- host side
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn get_encode() {
-  static EncodeTiledFn fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(ptr);
-  });
-  return fn;
-}
-
-// 2-D bf16 tensor [rows, cols] with row stride ld (elements), box {64, box_rows}, 128-byte swizzle.
+// 2-D bf16 tensor map with a {64, box_rows} box and 128-byte swizzle (tma_host.h)
 static bool make_map(CUtensorMap* m, const void* base, long long rows, long long cols, long long ld, int box_rows,
                      bool promote = true) {
-  EncodeTiledFn enc = get_encode();
-  if (!enc) return false;
-  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 2)};
-  cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), static_cast<cuuint32_t>(box_rows)};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                   promote ? CU_TENSOR_MAP_L2_PROMOTION_L2_256B : CU_TENSOR_MAP_L2_PROMOTION_NONE,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
+  return make_map_bf16_sw128(m, base, rows, cols, ld, BK, box_rows, promote);
 }
 
 static int num_sms_cached() {
@@ -669,6 +654,12 @@ int sdc_gemm_bf16(const void* A, long long lda, const void* W, const void* Wc, i
   p.n_per_m = p.n_main + p.n_cs;
   p.m_tiles = (M + BM - 1) / BM;
   p.total_tiles = p.m_tiles * p.n_per_m;
+  {
+    // bands per group: the group's A rows stay within about 24 MB of L2
+    const long long band_bytes = static_cast<long long>(BM) * K * 2;
+    int g = static_cast<int>((24ll << 20) / (band_bytes > 0 ? band_bytes : 1));
+    p.group = g < 1 ? 1 : (g > 16 ? 16 : (g > p.m_tiles ? p.m_tiles : g));
+  }
   p.C = static_cast<__nv_bfloat16*>(Cout);
   p.ldc = ldc;
   p.bias = bias;

@@ -128,8 +128,10 @@ __global__ void __launch_bounds__(128) add_rmsnorm_kernel(const __nv_bfloat16* _
         const uint4 f = *reinterpret_cast<const uint4*>(y + in_row * H + col);
         const uint32_t* fp = reinterpret_cast<const uint32_t*>(&f);
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-          if (bad == 0x7fffffff && bf16x2_differ(op[i], fp[i])) bad = col + 2 * i;
+        for (int i = 0; i < 4; ++i) {
+          const int e = bf16x2_diff(op[i], fp[i]);
+          if (bad == 0x7fffffff && e >= 0) bad = col + 2 * i + e;
+        }
       }
     }
   }
@@ -251,8 +253,10 @@ __global__ void __launch_bounds__(128) silu_mul_kernel(const __nv_bfloat16* __re
       const uint4 f = *reinterpret_cast<const uint4*>(out + in_row * I + col);
       const uint32_t* fp = reinterpret_cast<const uint32_t*>(&f);
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
-        if (bad == 0x7fffffff && bf16x2_differ(op[i], fp[i])) bad = col + 2 * i;
+      for (int i = 0; i < 4; ++i) {
+        const int e = bf16x2_diff(op[i], fp[i]);
+        if (bad == 0x7fffffff && e >= 0) bad = col + 2 * i + e;
+      }
     }
   }
   if (check != nullptr) {

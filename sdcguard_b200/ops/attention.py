@@ -86,7 +86,7 @@ def decode(q: torch.Tensor, cache: torch.Tensor, block_table: torch.Tensor, seq_
     if scratch is None:
         scratch = decode_scratch(q.shape[0], nq, nkv, max_ctx, q.device)
     _native.check(_native.lib().sdc_attn_decode(
-        q.data_ptr(), out.data_ptr(), cache.data_ptr(), block_table.data_ptr(), block_table.shape[1],
+        q.data_ptr(), out.data_ptr(), cache.data_ptr(), cache.shape[0], block_table.data_ptr(), block_table.shape[1],
         seq_req.data_ptr(), ctx.data_ptr(), None if seq_idx is None else seq_idx.data_ptr(), n, nq, nkv, 128,
         int(max_ctx), float(scale), scratch.data_ptr(), None if row_sq is None else row_sq.data_ptr(),
         None if check is None else check.data_ptr(), _s(q)), "attention decode")
