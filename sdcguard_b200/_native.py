@@ -53,6 +53,7 @@ P = c_void_p
 I = c_int
 L = c_longlong
 U = c_uint
+U64 = ctypes.c_ulonglong
 F = c_float
 
 # name -> (restype, argtypes)
@@ -68,6 +69,7 @@ SIGNATURES: dict[str, tuple] = {
     "sdc_attn_prefill": (I, [P, P, P, P, I, P, P, I, P, I, I, I, F, P, P, P]),
     "sdc_attn_decode": (I, [P, P, P, L, P, I, P, P, P, I, I, I, I, I, F, P, P, P, P]),
     "sdc_attn_decode_splits": (I, [I]),
+    "sdc_fingerprint_many": (I, [P, I, L, U64, P, P]),
     "sdc_tp_signal": (I, [P, P, I, I, P]),
     "sdc_tp_reduce_scatter": (I, [P, P, P, P, I, I, I, I, P, F, P, P, P]),
     "sdc_tp_all_gather": (I, [P, P, P, P, I, I, I, P, P, P, P]),

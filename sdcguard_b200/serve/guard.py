@@ -28,9 +28,16 @@ class ServeGuard:
         self.totals: dict[str, dict] = {}
         self.step: Optional[int] = None
         self._identity = None
+        self.weight_scan = None
+        self.scan_budget_mb = 0.0
 
     def mark_step(self, step: int) -> None:
         self.step = step
+
+    def attach_weight_scan(self, scan, budget_mb: float = 256.0) -> None:
+        """Scan `budget_mb` of weights (serve.weights.WeightScan) at every poll."""
+        self.weight_scan = scan
+        self.scan_budget_mb = budget_mb
 
     def poll(self, reset: bool = True) -> list[SDCEvent]:
         """Read every state row (one device->host copy), record events for alarms, reset the rows."""
@@ -52,6 +59,12 @@ class ServeGuard:
                 if "row" in r:
                     detail.update({k: r[k] for k in ("row", "block", "signed", "peer") if k in r})
                 ev = SDCEvent(detector=det, step=self.step, detail=detail, identity=self._identity)
+                self.log.add(ev)
+                events.append(ev)
+                if self.on_alert:
+                    self.on_alert(ev)
+        if self.weight_scan is not None:
+            for ev in self.weight_scan.poll(self.scan_budget_mb, step=self.step):
                 self.log.add(ev)
                 events.append(ev)
                 if self.on_alert:
