@@ -1,0 +1,198 @@
+"""Training guard: every protected nn.Linear runs its forward GEMM and both backward GEMMs (dX = dY W and
+dW = dY^T X) through the checked sm_100a GEMM, so all three carry the ABFT check of their fp32 accumulators.
+Results fold into a device state table; the host reads it once per checked step.
+
+    guard = SDCGuard(check_every=10)
+    guard.protect(model)                        # swaps nn.Linear modules (bf16, CUDA) for CheckedLinear
+    for step, batch in enumerate(loader):
+        with guard.at_step(step):               # checked on steps where step % check_every == 0
+            loss = model(batch).loss
+            loss.backward()
+        opt.step(); opt.zero_grad()
+    guard.events                                # SDCEvents (detector "checksum", detail: layer, phase, row, block)
+
+The backward operands are laid out for the kernel's C = A B^T form: dX = dY (W^T)^T with W^T materialised, and
+dW = (dY^T) (X^T)^T with dY^T and X^T materialised; the checksum rows of W^T and of X^T are built for the step.
+Shapes the kernel does not take (dimensions not multiples of 8) run unchecked and are counted in `coverage()`.
+
+Reference: `SDCGuard` (src/sdcguard/guard.py:788): `protect` :1096 swaps nn.Linear for a checked-linear autograd
+function covering fwd, dX and dW (`_CheckedLinear` :448, `_checked_forward` :471, `_checked_backward` :497), checks
+queued and read back once per step (`_queue` :1739, `_flush` :1882), `at_step` :1420 with an every-N schedule.
+"""
+from __future__ import annotations
+
+import contextlib
+from typing import Optional
+
+import torch
+import torch.nn.functional as F
+
+from ..numerics import abft
+from ..ops import gemm
+from ..utils.events import EventLog, SDCEvent, device_identity
+
+PHASES = ("fwd", "dx", "dw")
+
+
+class _Cache:
+    """Checksum data of one weight, rebuilt when the weight's version changes (after an optimizer step)."""
+
+    def __init__(self):
+        self.key = None
+        self.cw: Optional[gemm.CheckedWeight] = None
+        self.cwT: Optional[gemm.CheckedWeight] = None
+
+    def get(self, w: torch.Tensor, b: Optional[torch.Tensor]):
+        key = (w.data_ptr(), w._version, None if b is None else b._version)
+        if key != self.key:
+            self.cw = gemm.CheckedWeight(w.detach(), b)
+            self.cwT = None
+            self.key = key
+        return self.cw
+
+    def get_t(self, w: torch.Tensor):
+        if self.cwT is None:
+            self.cwT = gemm.CheckedWeight(w.detach().t().contiguous())
+        return self.cwT
+
+
+class _CheckedLinearFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, b, mod):
+        g = mod.guard
+        k = x.shape[-1]
+        x2 = x.reshape(-1, k).contiguous()
+        cw = mod.cache.get(w, b)
+        y = gemm.checked_linear(x2, cw, g.table.state, mod.slots["fwd"], z_alarm=g.z_alarm,
+                                inject=g._take_inject(mod.name, "fwd"))
+        ctx.save_for_backward(x2, w)
+        ctx.mod = mod
+        ctx.has_bias = b is not None
+        ctx.xshape = x.shape
+        return y.view(*x.shape[:-1], w.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, w = ctx.saved_tensors
+        mod, g = ctx.mod, ctx.mod.guard
+        n = w.shape[0]
+        dy2 = dy.reshape(-1, n).contiguous()
+        m = dy2.shape[0]
+        dx = dw = db = None
+        if ctx.needs_input_grad[0]:
+            dx = gemm.checked_linear(dy2, mod.cache.get_t(w), g.table.state, mod.slots["dx"], z_alarm=g.z_alarm,
+                                     inject=g._take_inject(mod.name, "dx")).view(ctx.xshape)
+        if ctx.needs_input_grad[1]:
+            if m % 8 == 0:
+                xt = gemm.CheckedWeight(x2.t().contiguous())        # (k, m): rows = output columns of dW
+                dw = gemm.checked_linear(dy2.t().contiguous(), xt, g.table.state, mod.slots["dw"],
+                                         z_alarm=g.z_alarm, inject=g._take_inject(mod.name, "dw"))
+            else:
+                dw = dy2.t() @ x2
+                g.unchecked += 1
+        if ctx.has_bias and ctx.needs_input_grad[2]:
+            db = dy2.float().sum(0).to(dy2.dtype)
+        return dx, dw, db, None
+
+
+class CheckedLinear(torch.nn.Module):
+    def __init__(self, lin: torch.nn.Linear, guard: "SDCGuard", name: str):
+        super().__init__()
+        self.weight = lin.weight
+        self.bias = lin.bias
+        self.in_features, self.out_features = lin.in_features, lin.out_features
+        self.guard = guard
+        self.name = name
+        self.cache = _Cache()
+        self.slots = {}
+        n, k = lin.out_features, lin.in_features
+        nbs = {"fwd": -(-n // abft.BLOCK), "dx": -(-k // abft.BLOCK), "dw": -(-k // abft.BLOCK)}
+        for ph in PHASES:
+            self.slots[ph] = guard.table.add(f"{name}.{ph} (ABFT GEMM)", nbs[ph])
+
+    def forward(self, x):
+        g = self.guard
+        ok = (g.active and x.is_cuda and x.dtype == torch.bfloat16 and self.weight.dtype == torch.bfloat16
+              and self.in_features % 8 == 0 and self.out_features % 8 == 0)
+        if not ok:
+            if g.active:
+                g.unchecked += 1
+            return F.linear(x, self.weight, self.bias)
+        g.checked_calls += 1
+        return _CheckedLinearFn.apply(x, self.weight, self.bias, self)
+
+
+class SDCGuard:
+    def __init__(self, check_every: int = 1, z_alarm: float = abft.Z_ALARM, device=None,
+                 log: Optional[EventLog] = None, on_alert=None):
+        self.check_every = max(1, int(check_every))
+        self.z_alarm = z_alarm
+        self.device = torch.device(device or "cuda")
+        self.table = gemm.StateTable(self.device, 512)
+        self.log = log or EventLog()
+        self.on_alert = on_alert
+        self.events: list[SDCEvent] = []
+        self.active = False
+        self.step: Optional[int] = None
+        self.checked_calls = 0
+        self.unchecked = 0
+        self.checks = 0
+        self.steps_checked = 0
+        self.worst_clean = 0.0
+        self._inject: dict = {}
+        self.modules: list[CheckedLinear] = []
+
+    def protect(self, model: torch.nn.Module) -> torch.nn.Module:
+        for pname, parent in list(model.named_modules()):
+            for cname, child in list(parent.named_children()):
+                if isinstance(child, torch.nn.Linear):
+                    full = f"{pname}.{cname}" if pname else cname
+                    mod = CheckedLinear(child, self, full)
+                    setattr(parent, cname, mod)
+                    self.modules.append(mod)
+        return model
+
+    @contextlib.contextmanager
+    def at_step(self, step: int):
+        self.step = step
+        self.active = step % self.check_every == 0
+        try:
+            yield self
+        finally:
+            if self.active:
+                self.flush(step)
+            self.active = False
+
+    def inject_next(self, layer: str, phase: str, row: int, col: int, bit: int) -> None:
+        """Fault injection: flip `bit` of fp32 accumulator (row, col) of the next `phase` GEMM of `layer`."""
+        self._inject[(layer, phase)] = (row, col, 1 << bit)
+
+    def _take_inject(self, layer: str, phase: str):
+        return self._inject.pop((layer, phase), None)
+
+    def flush(self, step: Optional[int] = None) -> list[SDCEvent]:
+        rows = self.table.read(reset=True)
+        self.steps_checked += 1
+        new = []
+        ident = None
+        for r in rows:
+            self.checks += r["checks"]
+            if r["z"] > self.z_alarm:
+                ident = ident or device_identity(self.device)
+                layer, ph = r["name"].split(" ")[0].rsplit(".", 1)
+                ev = SDCEvent(detector="checksum", step=step,
+                              detail={"layer": layer, "phase": ph, "z": r["z"], "row": r.get("row"),
+                                      "block": r.get("block"), "noise": r["noise"]}, identity=ident)
+                self.log.add(ev)
+                new.append(ev)
+                if self.on_alert:
+                    self.on_alert(ev)
+            else:
+                self.worst_clean = max(self.worst_clean, r["z"])
+        self.events += new
+        return new
+
+    def coverage(self) -> dict:
+        return {"layers": len(self.modules), "checked_calls": self.checked_calls, "unchecked_calls": self.unchecked,
+                "checks": self.checks, "steps_checked": self.steps_checked, "alarms": len(self.events),
+                "worst_clean_z": self.worst_clean}
