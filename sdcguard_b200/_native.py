@@ -70,6 +70,11 @@ SIGNATURES: dict[str, tuple] = {
     "sdc_attn_decode": (I, [P, P, P, L, P, I, P, P, P, I, I, I, I, I, F, P, P, P, P]),
     "sdc_attn_decode_splits": (I, [I]),
     "sdc_fingerprint_many": (I, [P, I, L, U64, P, P]),
+    "sdc_ep_dispatch": (I, [P, P, I, I, I, I, I, I, I, P, P, P, P, P, P, P, P, I, I, I, P]),
+    "sdc_ep_receive": (I, [P, P, P, P, P, I, I, I, I, I, P, P, P, P, P, P]),
+    "sdc_ep_combine_push": (I, [P, P, P, I, I, I, I, I, I, P, P, P, P, I, I, I, P]),
+    "sdc_ep_combine": (I, [P, P, P, P, P, P, I, I, I, I, I, I, I, P, P, P, P]),
+    "sdc_router_topk": (I, [P, I, I, I, I, P, P, P, I, P, P]),
     "sdc_tp_signal": (I, [P, P, I, I, P]),
     "sdc_tp_reduce_scatter": (I, [P, P, P, P, I, I, I, I, P, F, P, P, P]),
     "sdc_tp_all_gather": (I, [P, P, P, P, I, I, I, P, P, P, P]),

@@ -20,54 +20,17 @@
 // Results go to a state row (worst score with location, launches, blocks checked). Waits never trap: after the
 // deadline the kernel records a timeout in the error word and skips the work.
 #include "common.cuh"
+#include "peer.cuh"
 
 namespace sdc {
 namespace tp {
 
-constexpr int MAXW = 8;
-
-struct Peers {
-  const void* ptr[MAXW];    // per rank: base of that rank's copy of a symmetric buffer
-};
-
-__device__ __forceinline__ long long ld_acquire_sys(const long long* p) {
-  long long v;
-  asm volatile("ld.acquire.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void st_release_sys(long long* p, long long v) {
-  asm volatile("st.release.sys.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-
-// one thread: bump the generation and publish it to every peer's flag slot for this rank
-__global__ void signal_kernel(long long* gen, Peers flags, int world, int rank) {
-  if (threadIdx.x != 0 || blockIdx.x != 0) return;
-  const long long g = *gen + 1;
-  *gen = g;
-  __threadfence_system();
-  for (int r = 0; r < world; ++r) st_release_sys(static_cast<long long*>(const_cast<void*>(flags.ptr[r])) + rank, g);
-}
-
-// every CTA's thread 0 waits for all peers to reach this rank's generation; returns false on timeout
-__device__ bool wait_all(const long long* gen, const long long* my_flags, int world, int* err) {
-  __shared__ int ok;
-  if (threadIdx.x == 0) {
-    const long long g = *gen;
-    ok = 1;
-    const unsigned long long t0 = globaltimer();
-    for (int r = 0; r < world && ok; ++r) {
-      while (ld_acquire_sys(my_flags + r) < g) {
-        if (globaltimer() - t0 > kWaitNs) {
-          ok = 0;
-          record_error(err, ERR_TIMEOUT_PEER);
-          break;
-        }
-      }
-    }
-  }
-  __syncthreads();
-  return ok != 0;
-}
+using peer::MAXW;
+using peer::Peers;
+using peer::ld_acquire_sys;
+using peer::st_release_sys;
+using peer::signal_kernel;
+using peer::wait_all;
 
 __device__ __forceinline__ float2 bf2(uint32_t w) {
   return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w));
@@ -201,11 +164,7 @@ using namespace sdc::tp;
 
 extern "C" {
 
-static Peers make_peers(const unsigned long long* ptrs, int world) {
-  Peers p;
-  for (int i = 0; i < MAXW; ++i) p.ptr[i] = i < world ? reinterpret_cast<const void*>(ptrs[i]) : nullptr;
-  return p;
-}
+using sdc::peer::make_peers;
 
 int sdc_tp_signal(void* gen, const unsigned long long* flag_ptrs, int world, int rank, void* stream) {
   if (world < 1 || world > MAXW) return -1;
