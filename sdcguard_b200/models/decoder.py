@@ -99,8 +99,10 @@ class CheckedDecoder:
     """The model plus its check state. Slots of the state table name each checked op (`state.names`)."""
 
     def __init__(self, cfg: DecoderConfig, device="cuda", checked: bool = True, seed: int = 0,
-                 weights: Optional[dict] = None, tp_rank: int = 0, tp_size: int = 1):
+                 weights: Optional[dict] = None, tp_rank: int = 0, tp_size: int = 1, moe_layers: Optional[list] = None):
+        """moe_layers: one `models.moe.MoELayer` per layer in place of the dense MLP (expert-parallel models)."""
         self.cfg = cfg
+        self.moe = moe_layers
         self.device = torch.device(device)
         self.checked = checked
         self.nq = cfg.heads // tp_size
@@ -119,8 +121,8 @@ class CheckedDecoder:
                 ln2=torch.ones(cfg.hidden, dtype=torch.bfloat16, device=dev),
                 qkv=_init_linear((self.nq + 2 * self.nkv) * d, cfg.hidden, gen, dev),
                 o=_init_linear(cfg.hidden, self.nq * d, gen, dev),
-                gate_up=_init_linear(2 * self.inter, cfg.hidden, gen, dev),
-                down=_init_linear(cfg.hidden, self.inter, gen, dev),
+                gate_up=None if moe_layers else _init_linear(2 * self.inter, cfg.hidden, gen, dev),
+                down=None if moe_layers else _init_linear(cfg.hidden, self.inter, gen, dev),
                 q_norm=torch.ones(d, dtype=torch.bfloat16, device=dev) if cfg.qk_norm else None,
                 k_norm=torch.ones(d, dtype=torch.bfloat16, device=dev) if cfg.qk_norm else None,
             )
@@ -131,6 +133,8 @@ class CheckedDecoder:
         if checked:
             for i, lw in enumerate(self.layers):
                 for name in ("qkv", "o", "gate_up", "down"):
+                    if getattr(lw, name) is None:
+                        continue
                     cw = gemm.CheckedWeight(getattr(lw, name))
                     lw.cw[name] = cw
                     self.slot[f"L{i}.{name}"] = self.state.add(f"layers.{i}.{name} (ABFT GEMM)", cw.nb)
@@ -139,6 +143,15 @@ class CheckedDecoder:
             self.lm_cw = gemm.CheckedWeight(self.lm_head)
             self.slot["lm_head"] = self.state.add("lm_head (ABFT GEMM)", self.lm_cw.nb)
             self.slot["final_norm"] = self.state.add("final_norm (replay)", 1)
+        if moe_layers:
+            for i, m in enumerate(moe_layers):
+                m.attach(self.state, f"layers.{i}.moe")
+            comm = moe_layers[0].comm
+            if checked:
+                d = self.state.add("ep dispatch (transfer seals)", comm.nb, "rowblock")
+                c = self.state.add("ep combine (transfer seals)", comm.nb, "rowblock")
+                assert c == d + 1
+                comm.state = self.state.state[d:d + 2]
         self._bufs: dict = {}
 
     # ---------------------------------------------------------------- buffers
@@ -161,11 +174,11 @@ class CheckedDecoder:
             attn=torch.empty(T, nq, D, dtype=bf, device=dev),
             ors=torch.empty(T, dtype=torch.float32, device=dev),
             a=torch.empty(T, H, dtype=bf, device=dev),
-            gu=torch.empty(T, 2 * self.inter, dtype=bf, device=dev),
-            act=torch.empty(T, self.inter, dtype=bf, device=dev),
+            gu=torch.empty(T if not self.moe else 1, 2 * self.inter, dtype=bf, device=dev),
+            act=torch.empty(T if not self.moe else 1, self.inter, dtype=bf, device=dev),
         )
         if self.checked:
-            gemm.reserve_workspace(dev, T, max(2 * self.inter, (nq + 2 * nkv) * D, H))
+            gemm.reserve_workspace(dev, T, max(2 * self.inter if not self.moe else 0, (nq + 2 * nkv) * D, H))
             gemm.reserve_workspace(dev, min(T, 1024), cfg.vocab)
         return self._bufs
 
@@ -234,6 +247,9 @@ class CheckedDecoder:
             layers.add_rmsnorm(a, lw.ln2, cfg.rms_eps, residual=resid, resid_out=resid, out=y, row_sq=rs)
             if chk:
                 layers.add_rmsnorm(resid, lw.ln2, cfg.rms_eps, out=y, rows=S, check=self._st(f"L{i}.norm2"))
+            if self.moe:
+                x = self.moe[i].forward(y, S if chk else None)
+                continue
             self._linear(y, lw.gate_up, lw.cw.get("gate_up"), f"L{i}.gate_up", gu, rs)
             layers.silu_mul(gu, out=act, row_sq=rs)
             if chk:

@@ -70,7 +70,8 @@ class StateTable:
 
     def add(self, name: str, nb: int, kind: str = "gemm") -> int:
         """kind "gemm": location = checksum index (row, block, signed); "collective": location = (row, block,
-        peer) as the TP collective kernels encode it ((row * nb + block) * 8 + peer)."""
+        peer) as the TP collective kernels encode it ((row * nb + block) * 8 + peer); "rowblock": (row, block)
+        (row * nb + block), the expert-parallel transfers."""
         if len(self.names) >= self.state.shape[0]:
             grown = torch.zeros(self.state.shape[0] * 2, abft.STATE_COLS, dtype=torch.int64, device=self.device)
             grown[: self.state.shape[0]] = self.state
@@ -92,6 +93,8 @@ class StateTable:
             if d["z"] > 0 and self.kinds[i] == "collective":
                 rb, d["peer"] = divmod(d["flat"], 8)
                 d["row"], d["block"] = divmod(rb, self.nbs[i])
+            elif d["z"] > 0 and self.kinds[i] == "rowblock":
+                d["row"], d["block"] = divmod(d["flat"], self.nbs[i])
             elif d["z"] > 0:
                 d["row"], d["block"], d["signed"] = abft.locate(d["flat"], self.nbs[i])
             out.append(d)
