@@ -79,6 +79,9 @@ struct Params {
   uint32_t inj_xor;
   unsigned long long* dbg;   // optional per-CTA timers (null: off): [cta][8]
   uint32_t* seal;            // optional [M][nb] hash of the stored bf16 bits of each (row, block) (null: off)
+  int ksplit;                // K splits (1: the fused epilogue; > 1: partial accumulators + reduce kernel)
+  int kb_per;                // k-blocks per split
+  float* part;               // ksplit > 1: [ksplit][M][N + 6 nb] fp32 partial accumulators
 };
 
 template <int BN>
@@ -131,6 +134,16 @@ __device__ __forceinline__ void tile_coords(const Params& p, int tile, int& mt, 
   idx = l2 / gm;
 }
 
+// Split-K: tile t of the persistent order is (base tile t / ksplit, split t % ksplit); consecutive splits of a
+// tile go to different CTAs.
+__device__ __forceinline__ void tile_coords_k(const Params& p, int tile, int& mt, bool& cs, int& idx, int& kb0,
+                                              int& kb1, int kblocks) {
+  const int ks = tile % p.ksplit;
+  tile_coords(p, tile / p.ksplit, mt, cs, idx);
+  kb0 = ks * p.kb_per;
+  kb1 = min(kblocks, kb0 + p.kb_per);
+}
+
 __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
   int v;
   asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -140,6 +153,147 @@ __device__ __forceinline__ unsigned long long ld_relaxed_gpu_u64(const unsigned 
   unsigned long long v;
   asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
+}
+
+// Judges one (row, 128-column block) pair: P, S, Q, Aab are the plain, signed, squared and absolute sums of the
+// fp32 accumulator block (bias included), ex the expected plain / signed sums from the checksum rows. Noise
+// model of the fp32 accumulation (c1, c2, c3 folded into prod_coef and out_coef). Sets the state keys
+// (z bits << 32 | flat, z bits << 32 | noise bits) or marks the pair unjudged.
+__device__ __forceinline__ void judge_pair(const Params& p, int row, int b, float P, float S, float Q, float Aab,
+                                           float2 ex, unsigned long long& k0, unsigned long long& k1, int& unj) {
+  const long long o = static_cast<long long>(row) * p.nb + b;
+  const float4 ws = __ldg(p.wstat + b);
+  float ep = ex.x, es = ex.y;
+  if (p.bsum != nullptr) {
+    const float2 bs = __ldg(p.bsum + b);
+    ep += bs.x;
+    es += bs.y;
+  }
+  const float xn = sqrtf(__ldg(p.row_sq + row));
+  const float prod = p.prod_coef * xn * fmaxf(ws.x, fmaxf(ws.y, ws.z));
+  const float den = sqrtf(Q) * p.out_coef + prod + p.abs_floor;
+  const float dp = fabsf(ep - P), ds = fabsf(es - S);
+  const float worst = Aab * p.out_coef + prod + p.abs_floor;
+  const float zp = fminf(__fdividef(dp, den), __fdividef(dp, worst) * p.zthr);
+  const float zs = __fdividef(ds, den);
+  float z = fmaxf(zp, zs);
+  int which = zs > zp ? 1 : 0;
+  const bool fin_exp = isfinite(ep) && isfinite(es) && isfinite(prod);
+  const bool fin_act = isfinite(P) && isfinite(S) && isfinite(Q) && isfinite(Aab);
+  bool judged = true;
+  if (!fin_exp) {
+    judged = false;
+  } else if (!fin_act) {
+    const float bound = p.bound_coef * xn * ws.w + p.bias_max;
+    if (bound < 1e18f) {
+      z = __int_as_float(0x7f800000);
+      which = 0;
+    } else {
+      judged = false;
+    }
+  } else if (!(z <= 3.0e38f)) {
+    z = __int_as_float(0x7f800000);   // overflow of the ratio: far beyond any noise
+  }
+  if (judged) {
+    const unsigned long long zb = static_cast<unsigned long long>(__float_as_uint(z)) << 32;
+    k0 = zb | ((static_cast<unsigned long long>(o) * 2ull + which) & 0xffffffffull);
+    k1 = zb | __float_as_uint(den);
+  } else {
+    unj = 1;
+  }
+}
+
+// Split-K reduce and check: one warp per (row, 128-column block); lane l owns columns 4l .. 4l+3. Sums the
+// splits' fp32 partials in split order, applies bias and the injected fault, forms the block sums, writes the
+// bf16 output (and its seal), and judges the block against the checksum columns (summed the same way) with the
+// fused epilogue's judge. One state update per CTA.
+template <bool INJ>
+__global__ void __launch_bounds__(256) split_reduce_kernel(const Params p) {
+  __shared__ unsigned long long sk0[8], sk1[8];
+  __shared__ int su[8];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long wid = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const long long pw = static_cast<long long>(p.N) + 6ll * p.nb;
+  const long long plane = static_cast<long long>(p.M) * pw;
+  unsigned long long k0 = 0ull, k1 = 0ull;
+  int unj = 0;
+  if (wid < static_cast<long long>(p.M) * p.nb) {
+    const int row = static_cast<int>(wid / p.nb), b = static_cast<int>(wid % p.nb);
+    const int c = b * CSW + lane * 4;
+    const bool in = c < p.N;
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    const float* base = p.part + static_cast<long long>(row) * pw;
+    if (in) {
+      for (int ks = 0; ks < p.ksplit; ++ks) {
+        const float4 t = __ldcg(reinterpret_cast<const float4*>(base + ks * plane + c));
+        v[0] += t.x;
+        v[1] += t.y;
+        v[2] += t.z;
+        v[3] += t.w;
+      }
+      if (p.bias != nullptr) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[j] += __ldg(p.bias + c + j);
+      }
+      if (INJ) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (row == p.inj_row && c + j == p.inj_col) v[j] = __uint_as_float(__float_as_uint(v[j]) ^ p.inj_xor);
+      }
+    }
+    // checksum columns: lanes 0..5 sum part i of the expected sums over the splits
+    float e = 0.f;
+    if (lane < 6)
+      for (int ks = 0; ks < p.ksplit; ++ks) e += __ldcg(base + ks * plane + p.N + b * 6 + lane);
+    const float e0 = __shfl_sync(0xffffffffu, e, 0), e1 = __shfl_sync(0xffffffffu, e, 1);
+    const float e2 = __shfl_sync(0xffffffffu, e, 2), e3 = __shfl_sync(0xffffffffu, e, 3);
+    const float e4 = __shfl_sync(0xffffffffu, e, 4), e5 = __shfl_sync(0xffffffffu, e, 5);
+    const uint32_t sg = p.sgn[lane >> 3];
+    float P = 0.f, S = 0.f, Q = 0.f, A = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int col = lane * 4 + j;
+      P += v[j];
+      S += ((sg >> (col & 31)) & 1u) ? -v[j] : v[j];
+      Q = fmaf(v[j], v[j], Q);
+      A += fabsf(v[j]);
+    }
+    const uint32_t w0 = pack_bf16x2(v[0], v[1]), w1 = pack_bf16x2(v[2], v[3]);
+    uint32_t h = seal_term(w0, static_cast<uint32_t>(lane * 2)) + seal_term(w1, static_cast<uint32_t>(lane * 2 + 1));
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) {
+      P += __shfl_xor_sync(0xffffffffu, P, m);
+      S += __shfl_xor_sync(0xffffffffu, S, m);
+      Q += __shfl_xor_sync(0xffffffffu, Q, m);
+      A += __shfl_xor_sync(0xffffffffu, A, m);
+      h += __shfl_xor_sync(0xffffffffu, h, m);
+    }
+    if (in) *reinterpret_cast<uint2*>(p.C + static_cast<long long>(row) * p.ldc + c) = make_uint2(w0, w1);
+    if (lane == 0) {
+      if (p.seal != nullptr) p.seal[static_cast<long long>(row) * p.nb + b] = h;
+      judge_pair(p, row, b, P, S, Q, A, make_float2(e0 + e1 + e2, e3 + e4 + e5), k0, k1, unj);
+    }
+  }
+  if (lane == 0) {
+    sk0[warp] = k0;
+    sk1[warp] = k1;
+    su[warp] = unj;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned long long a0 = 0ull, a1 = 0ull;
+    int u = 0;
+    for (int w = 0; w < 8; ++w) {
+      a0 = sk0[w] > a0 ? sk0[w] : a0;
+      a1 = sk1[w] > a1 ? sk1[w] : a1;
+      u += su[w];
+    }
+    unsigned long long* st = p.state + static_cast<long long>(p.slot) * 4;
+    if (a0) atomicMax(st + 0, a0);
+    if (a1) atomicMax(st + 1, a1);
+    if (u) atomicAdd(st + 3, static_cast<unsigned long long>(u));
+    if (blockIdx.x == 0) atomicAdd(st + 2, 1ull);
+  }
 }
 
 template <int BN, bool INJ>
@@ -201,11 +355,11 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
       uint32_t issued = 0;        // bit s: stage s has a load in flight that we have not seen land
       uint32_t issued_phase = 0;  // bit s: the full-barrier parity of that load
       for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
-        int mt, idx;
+        int mt, idx, kb0, kb1;
         bool cs;
-        tile_coords(p, tile, mt, cs, idx);
+        tile_coords_k(p, tile, mt, cs, idx, kb0, kb1, kblocks);
         const uint32_t bytes = A_BYTES + (cs ? (C::CSB * CS_ROWS) * BK * 2 : C::B_BYTES);
-        for (int kb = 0; kb < kblocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&ctl->empty[stage], phase ^ 1u, abort_flag)) {
             ok = false;
             break;
@@ -244,9 +398,9 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
       bool ok = true;
       const uint32_t idesc_main = idesc_bf16_f32(BM, BN);
       for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
-        int mt, idx;
+        int mt, idx, kb0, kb1;
         bool cs;
-        tile_coords(p, tile, mt, cs, idx);
+        tile_coords_k(p, tile, mt, cs, idx, kb0, kb1, kblocks);
         uint32_t idesc = idesc_main;
         if (cs) {
           const int nblk = min(C::CSB, p.nb - idx * C::CSB);
@@ -259,7 +413,7 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-        for (int kb = 0; kb < kblocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&ctl->full[stage], phase, abort_flag)) {
             ok = false;
             break;
@@ -272,7 +426,7 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
 #pragma unroll
           for (int ks = 0; ks < BK / 16; ++ks) {
             // advance 16 bf16 = 32 bytes along K inside the swizzle atom: +2 in the >>4 address field
-            umma_f16(d_tmem, adesc + 2ull * ks, bdesc + 2ull * ks, idesc, (kb | ks) != 0 ? 1u : 0u);
+            umma_f16(d_tmem, adesc + 2ull * ks, bdesc + 2ull * ks, idesc, (kb != kb0 || ks != 0) ? 1u : 0u);
           }
           umma_commit(&ctl->empty[stage]);
           if (++stage == C::STAGES) {
@@ -299,7 +453,8 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
     // ------------------------------------------------------------ check coordinator
     // Keeps global-memory round trips off the epilogue's path: waits for each band's expected sums
     // before the epilogue needs them, and publishes the results (state atomics, band counters) after.
-    if (lane == 0) {
+    // In split-K mode the check runs in the reduce kernel: nothing to coordinate.
+    if (lane == 0 && p.ksplit == 1) {
       int acc = 0;
       uint32_t acc_phase = 0;
       unsigned long long* st = p.state + static_cast<long long>(p.slot) * 4;
@@ -365,7 +520,7 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
     for (int tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x) {
       int mt, idx;
       bool cs;
-      tile_coords(p, tile, mt, cs, idx);
+      tile_coords(p, tile / p.ksplit, mt, cs, idx);
       const int row = mt * BM + row_in_tile;
       const unsigned long long t_w0 = p.dbg ? globaltimer() : 0ull;
       const bool got = mbar_wait(&ctl->tfull[acc], acc_phase, abort_flag);
@@ -379,7 +534,53 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
       tc_fence_after();
       const uint32_t tacc = tmem_base + static_cast<uint32_t>(acc * BN) + lane_off;
 
-      if (cs) {
+      if (p.ksplit > 1) {
+        // ---- split-K: store this split's fp32 accumulator rows; the reduce kernel sums and checks them
+        const int ks = tile % p.ksplit;
+        const long long pw = static_cast<long long>(p.N) + 6ll * p.nb;
+        float* prow = p.part + (static_cast<long long>(ks) * p.M + row) * pw;
+        if (cs) {
+          const int blk0 = idx * C::CSB + g * 20;
+#pragma unroll 1
+          for (int i4 = 0; i4 < 5; ++i4) {
+            const int bb = blk0 + i4 * 4;
+            if (bb < p.nb) {
+              uint32_t r[24];
+              const uint32_t ta = tacc + static_cast<uint32_t>(g * 120 + i4 * 24);
+              tmem_ld8(ta, *reinterpret_cast<uint32_t(*)[8]>(&r[0]));
+              tmem_ld8(ta + 8, *reinterpret_cast<uint32_t(*)[8]>(&r[8]));
+              tmem_ld8(ta + 16, *reinterpret_cast<uint32_t(*)[8]>(&r[16]));
+              tmem_wait_ld();
+              if (row < p.M) {
+                const int nbk = min(4, p.nb - bb);
+                float* dst = prow + p.N + static_cast<long long>(bb) * 6;
+                for (int j = 0; j < 6 * nbk; ++j) dst[j] = u32_as_f32(r[j]);
+              }
+            }
+          }
+        } else {
+          const int col0 = idx * BN + g * CSW;
+          if (col0 < p.N) {
+#pragma unroll 1
+            for (int h = 0; h < CSW / 64; ++h) {
+              uint32_t r[64];
+              tmem_ld32(tacc + static_cast<uint32_t>(g * CSW + h * 64), *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+              tmem_ld32(tacc + static_cast<uint32_t>(g * CSW + h * 64 + 32), *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+              tmem_wait_ld();
+              const int cbase = col0 + h * 64;
+              if (row < p.M) {
+#pragma unroll
+                for (int j = 0; j < 64; j += 4)
+                  if (cbase + j < p.N)    // N % 8 == 0: a group of 4 is all in or all out
+                    *reinterpret_cast<float4*>(prow + cbase + j) = make_float4(
+                        u32_as_f32(r[j]), u32_as_f32(r[j + 1]), u32_as_f32(r[j + 2]), u32_as_f32(r[j + 3]));
+              }
+            }
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&ctl->tempty[acc]);
+      } else if (cs) {
         // ---- checksum tile: E = A @ Wc^T, three bf16 parts per sum added in fp32
         const int blk0 = idx * C::CSB + g * 20;   // first block of this warpgroup
 #pragma unroll 1
@@ -485,51 +686,11 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
         unsigned long long k0 = 0ull, k1 = 0ull;
         int unj = 0;
         if (have && row < p.M) {
-          const int b = col0 / CSW;
           if (skip) {
             unj = 1;
           } else {
-            const long long o = static_cast<long long>(row) * p.nb + b;
-            const float2 ex = __ldcg(p.expd + o);
-            const float4 ws = __ldg(p.wstat + b);
-            float ep = ex.x, es = ex.y;
-            if (p.bsum != nullptr) {
-              const float2 bs = __ldg(p.bsum + b);
-              ep += bs.x;
-              es += bs.y;
-            }
-            const float xn = sqrtf(__ldg(p.row_sq + row));
-            const float prod = p.prod_coef * xn * fmaxf(ws.x, fmaxf(ws.y, ws.z));
-            const float den = sqrtf(Q) * p.out_coef + prod + p.abs_floor;
-            const float dp = fabsf(ep - P), ds = fabsf(es - S);
-            const float worst = Aab * p.out_coef + prod + p.abs_floor;
-            const float zp = fminf(__fdividef(dp, den), __fdividef(dp, worst) * p.zthr);
-            const float zs = __fdividef(ds, den);
-            float z = fmaxf(zp, zs);
-            int which = zs > zp ? 1 : 0;
-            const bool fin_exp = isfinite(ep) && isfinite(es) && isfinite(prod);
-            const bool fin_act = isfinite(P) && isfinite(S) && isfinite(Q) && isfinite(Aab);
-            bool judged = true;
-            if (!fin_exp) {
-              judged = false;
-            } else if (!fin_act) {
-              const float bound = p.bound_coef * xn * ws.w + p.bias_max;
-              if (bound < 1e18f) {
-                z = __int_as_float(0x7f800000);
-                which = 0;
-              } else {
-                judged = false;
-              }
-            } else if (!(z <= 3.0e38f)) {
-              z = __int_as_float(0x7f800000);   // overflow of the ratio: far beyond any noise
-            }
-            if (judged) {
-              const unsigned long long zb = static_cast<unsigned long long>(__float_as_uint(z)) << 32;
-              k0 = zb | ((static_cast<unsigned long long>(o) * 2ull + which) & 0xffffffffull);
-              k1 = zb | __float_as_uint(den);
-            } else {
-              unj = 1;
-            }
+            const int b = col0 / CSW;
+            judge_pair(p, row, b, P, S, Q, Aab, __ldcg(p.expd + static_cast<long long>(row) * p.nb + b), k0, k1, unj);
           }
         }
         k0 = warp_max_u64(k0);
@@ -624,20 +785,36 @@ extern "C" {
 // Bytes of workspace the checked GEMM needs for an M x N output: a fixed block of per-band counters, then
 // per (row, block) the two fp32 expected sums. The counters must be zero before the first launch (every
 // launch leaves them zero).
-long long sdc_gemm_ws_bytes(int M, int N) {
+// Split-K applies to outputs of at most two bands (decode-sized M) that would leave most SMs idle; the partial
+// accumulators of up to kMaxSplit splits follow the expected sums in the workspace.
+constexpr int kMaxSplit = 8;
+constexpr int kSplitMaxN = 32768;
+
+static long long ws_bytes_base(int M, int N) {
   const long long nb = (N + CSW - 1) / CSW;
   return COUNTER_BYTES + static_cast<long long>(M) * nb * 8 + 256;
+}
+
+static long long part_bytes(int M, int N) {
+  const long long nb = (N + CSW - 1) / CSW;
+  return static_cast<long long>(kMaxSplit) * M * (N + 6 * nb) * 4;
+}
+
+static bool split_eligible(int M, int N) { return (M + BM - 1) / BM <= 2 && N <= kSplitMaxN; }
+
+long long sdc_gemm_ws_bytes(int M, int N) {
+  return ws_bytes_base(M, N) + (split_eligible(M, N) ? part_bytes(M, N) + 256 : 0);
 }
 
 // C[M,N] = A[M,K] @ W[N,K]^T (+ bias): bf16 in/out, fp32 accumulation on tcgen05, with the ABFT check
 // described at the top of this file. Wc[6*nb, K] holds the checksum rows of W (see sdcguard_b200/ops/gemm.py).
 // Returns 0 or a CUDA error code; -1 for bad arguments.
-int sdc_gemm_bf16(const void* A, long long lda, const void* W, const void* Wc, int M, int N, int K, void* Cout,
-                  long long ldc, const float* bias, const float* bsum, float bias_max, const float* row_sq,
-                  const float* wstat, void* ws, unsigned long long* state, int slot, unsigned s0, unsigned s1,
-                  unsigned s2, unsigned s3, float zthr, float prod_coef, float out_coef, float abs_floor,
-                  float bound_coef, int* err, int bn, int max_ctas, int inj_row, int inj_col, unsigned inj_xor,
-                  void* dbg, void* seal, void* stream) {
+static int gemm_run(const void* A, long long lda, const void* W, const void* Wc, int M, int N, int K, void* Cout,
+                    long long ldc, const float* bias, const float* bsum, float bias_max, const float* row_sq,
+                    const float* wstat, void* ws, unsigned long long* state, int slot, unsigned s0, unsigned s1,
+                    unsigned s2, unsigned s3, float zthr, float prod_coef, float out_coef, float abs_floor,
+                    float bound_coef, int* err, int bn, int max_ctas, int inj_row, int inj_col, unsigned inj_xor,
+                    void* dbg, void* seal, void* stream, bool allow_split) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   if ((K % 8) || (N % 8) || (lda % 8) || (ldc % 8) || (bn != 128 && bn != 256)) return -1;
   if ((M + BM - 1) / BM > MAX_BANDS) return -1;
@@ -688,6 +865,22 @@ int sdc_gemm_bf16(const void* A, long long lda, const void* W, const void* Wc, i
   p.inj_xor = inj_xor;
   p.dbg = static_cast<unsigned long long*>(dbg);
   p.seal = static_cast<uint32_t*>(seal);
+  p.ksplit = 1;
+  p.kb_per = (K + BK - 1) / BK;
+  p.part = nullptr;
+  // splitting pays when each CTA would stream a long K (measured: K = 1024 is faster unsplit)
+  if (allow_split && split_eligible(M, N) && K >= 2048 && max_ctas == 0 && dbg == nullptr) {
+    const int kblocks = (K + BK - 1) / BK;
+    int sp = num_sms_cached() / p.total_tiles;
+    sp = sp > kMaxSplit ? kMaxSplit : sp;
+    sp = sp > kblocks / 4 ? kblocks / 4 : sp;
+    if (sp >= 2) {
+      p.kb_per = (kblocks + sp - 1) / sp;
+      p.ksplit = (kblocks + p.kb_per - 1) / p.kb_per;     // no empty split
+      p.total_tiles *= p.ksplit;
+      p.part = reinterpret_cast<float*>(wsb + ((ws_bytes_base(M, N) + 255) / 256) * 256);
+    }
+  }
   CUtensorMap ma, mw, mc, mo;
   if (!make_map(&ma, A, M, K, lda, BM)) return -2;
   if (!make_map(&mw, W, N, K, K, bn)) return -3;
@@ -698,9 +891,30 @@ int sdc_gemm_bf16(const void* A, long long lda, const void* W, const void* Wc, i
   if (grid > cap) grid = cap;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool inj = inj_row >= 0;
+  int rc;
   if (bn == 256)
-    return inj ? launch<256, true>(ma, mw, mc, mo, p, grid, st) : launch<256, false>(ma, mw, mc, mo, p, grid, st);
-  return inj ? launch<128, true>(ma, mw, mc, mo, p, grid, st) : launch<128, false>(ma, mw, mc, mo, p, grid, st);
+    rc = inj ? launch<256, true>(ma, mw, mc, mo, p, grid, st) : launch<256, false>(ma, mw, mc, mo, p, grid, st);
+  else
+    rc = inj ? launch<128, true>(ma, mw, mc, mo, p, grid, st) : launch<128, false>(ma, mw, mc, mo, p, grid, st);
+  if (rc != 0 || p.ksplit == 1) return rc;
+  const long long warps = static_cast<long long>(M) * nb;
+  const unsigned blocks = static_cast<unsigned>((warps * 32 + 255) / 256);
+  if (inj)
+    split_reduce_kernel<true><<<blocks, 256, 0, st>>>(p);
+  else
+    split_reduce_kernel<false><<<blocks, 256, 0, st>>>(p);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int sdc_gemm_bf16(const void* A, long long lda, const void* W, const void* Wc, int M, int N, int K, void* Cout,
+                  long long ldc, const float* bias, const float* bsum, float bias_max, const float* row_sq,
+                  const float* wstat, void* ws, unsigned long long* state, int slot, unsigned s0, unsigned s1,
+                  unsigned s2, unsigned s3, float zthr, float prod_coef, float out_coef, float abs_floor,
+                  float bound_coef, int* err, int bn, int max_ctas, int inj_row, int inj_col, unsigned inj_xor,
+                  void* dbg, void* seal, void* stream) {
+  return gemm_run(A, lda, W, Wc, M, N, K, Cout, ldc, bias, bsum, bias_max, row_sq, wstat, ws, state, slot, s0, s1, s2,
+                  s3, zthr, prod_coef, out_coef, abs_floor, bound_coef, err, bn, max_ctas, inj_row, inj_col, inj_xor,
+                  dbg, seal, stream, true);
 }
 
 }  // extern "C"
@@ -730,7 +944,7 @@ extern "C" int sdc_gemm_bf16_noalloc(const void* A, long long lda, const void* W
                                      void* stream) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   const long long pairs = static_cast<long long>(M) * ((N + CSW - 1) / CSW);
-  if (pairs > SDC_GEMM_NOALLOC_MAX_PAIRS || sdc_gemm_ws_bytes(M, N) > SDC_GEMM_NOALLOC_SCRATCH_BYTES) {
+  if (pairs > SDC_GEMM_NOALLOC_MAX_PAIRS || ws_bytes_base(M, N) > SDC_GEMM_NOALLOC_SCRATCH_BYTES) {
     std::fprintf(stderr,
                  "sdc_gemm_bf16_noalloc: M=%d x ceil(N/128)=%lld (row, block) pairs exceed the fixed workspace "
                  "(%lld pairs); use sdc_gemm_bf16 with a caller workspace\n",
@@ -756,7 +970,8 @@ extern "C" int sdc_gemm_bf16_noalloc(const void* A, long long lda, const void* W
   // always written before they are read
   e = cudaMemsetAsync(scratch, 0, COUNTER_BYTES, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return static_cast<int>(e);
-  return sdc_gemm_bf16(A, lda, W, Wc, M, N, K, Cout, ldc, bias, bsum, bias_max, row_sq, wstat, scratch, state, slot,
-                       s0, s1, s2, s3, zthr, prod_coef, out_coef, abs_floor, bound_coef, err, bn, max_ctas, -1, -1, 0u,
-                       nullptr, nullptr, stream);
+  // the fixed scratch is sized for the expected sums only: no split-K partials here
+  return gemm_run(A, lda, W, Wc, M, N, K, Cout, ldc, bias, bsum, bias_max, row_sq, wstat, scratch, state, slot, s0, s1,
+                  s2, s3, zthr, prod_coef, out_coef, abs_floor, bound_coef, err, bn, max_ctas, -1, -1, 0u, nullptr,
+                  nullptr, stream, false);
 }

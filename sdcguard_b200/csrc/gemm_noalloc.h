@@ -24,6 +24,10 @@
 //     wrong check results: serialise them on one stream.
 //   * The first call on a device looks up the array's device address (cudaGetSymbolAddress, with that device
 //     current) and keeps it; make that first call before any stream capture.
+//   * It always runs the one-pass kernel. For decode-sized M the regular entry point splits K over more CTAs
+//     (partial accumulators in its workspace, then a reduce-and-check kernel), so for those shapes the two
+//     results agree to fp32 rounding rather than bit for bit; with a CTA cap (max_ctas > 0) the regular entry
+//     point runs the same one-pass kernel and the results are identical.
 //   * It calls no cudaMalloc, cudaFree or allocating library routine.
 #pragma once
 

@@ -86,3 +86,27 @@ def test_state_accumulates_over_calls():
     assert d["checks"] == 5 and d["z"] < 2.0
     err = gemm.error_word(dev).item()
     assert err == 0
+
+
+@pytest.mark.parametrize("bn", [128, 256])
+def test_split_k_small_m_output_check_seal_and_injection(bn):
+    """Decode-sized M runs split over K (partial accumulators, then the reduce-and-judge kernel)."""
+    from sdcguard_b200.ops import gemm
+    torch.manual_seed(3)
+    dev = torch.device("cuda")
+    m, n, k = 64, 1024, 4096
+    x = torch.randn(m, k, device=dev).to(torch.bfloat16)
+    w = (torch.randn(n, k, device=dev) * 0.02).to(torch.bfloat16)
+    b = torch.randn(n, device=dev) * 0.1
+    cw = gemm.CheckedWeight(w, b)
+    st = gemm.StateTable(dev, 4)
+    s0, s1 = st.add("clean", cw.nb), st.add("inj", cw.nb)
+    seal = torch.empty(m, cw.nb, dtype=torch.int32, device=dev)
+    y = gemm.checked_linear(x, cw, st.state, s0, bn=bn, seal=seal)
+    ref = x.float() @ w.float().t() + b
+    assert (y.float() - ref).abs().max().item() <= 2 ** -7 * ref.abs().max().item() + 1e-3
+    assert torch.equal(seal, gemm.seal_reference(y))
+    gemm.checked_linear(x, cw, st.state, s1, bn=bn, inject=(10, 700, 1 << 28))
+    rows = st.read()
+    assert rows[0]["checks"] == 1 and rows[0]["unjudged"] == 0 and rows[0]["z"] < 2.0, rows[0]
+    assert rows[1]["z"] > abft.Z_ALARM and rows[1]["row"] == 10 and rows[1]["block"] == 5, rows[1]

@@ -48,7 +48,10 @@ def test_noalloc_entry_matches_regular_entry_twice():
         rs = gemm.row_sqnorm(x)
         st = gemm.StateTable(dev, 4)
         a, b = st.add("regular", cw.nb), st.add("noalloc", cw.nb)
-        y_ref = gemm.checked_linear(x, cw, st.state, a, row_sq=rs, bn=256)
+        # the regular entry splits K for decode-sized M; the allocation-free one never does: compare with the
+        # regular entry's one-pass kernel (a CTA cap turns the split off)
+        nsm = torch.cuda.get_device_properties(dev).multi_processor_count
+        y_ref = gemm.checked_linear(x, cw, st.state, a, row_sq=rs, bn=256, max_ctas=nsm)
         err = torch.zeros(1, dtype=torch.int32, device=dev)
         y = torch.empty_like(y_ref)
         assert _call(fn, x, cw, y, st.state, b, rs, err) == 0
