@@ -79,6 +79,7 @@ class LLMEngine:
         self._graph_replayed = 0           # kernels of this library executed by graph replays
         self.step_counter = 0
         self.stats = {"prefill_tokens": 0, "decode_tokens": 0, "steps": 0}
+        self.hooks = None                  # serve.plugin.PluginHooks (register() sets it)
         self.phase_timing = False          # record device time of the prefill and decode phases of generate()
         self.last_phase_ms: dict = {}
 
@@ -133,6 +134,8 @@ class LLMEngine:
         self.step_counter += 1
         self.stats["prefill_tokens"] += T
         self.stats["steps"] += 1
+        if self.hooks is not None:
+            self.hooks.after_step("prefill", [reqs[i] for i, n in enumerate(lens) for _ in range(n)])
 
     # ---------------------------------------------------------------- decode
     def _decode_graph(self, B: int, max_pages: int, max_ctx: int, S: int):
@@ -223,6 +226,8 @@ class LLMEngine:
                 else:
                     nxt = out()
                 out_tokens[rows, s + 1] = nxt
+                if self.hooks is not None:
+                    self.hooks.after_step("decode", idx)
             self.step_counter += max_new - 1
             self.stats["decode_tokens"] += B * (max_new - 1)
             self.stats["steps"] += max_new - 1
