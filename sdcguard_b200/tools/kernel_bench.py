@@ -1,0 +1,132 @@
+"""Microbenchmarks of single kernels (CUDA-event timing after warm-up, L2 flushed between timed launches), for
+profiling and for the numbers in the profile summaries.
+
+    python -m sdcguard_b200.tools.kernel_bench gemm --m 4096 --n 28672 --k 4096 [--iters 10]
+    python -m sdcguard_b200.tools.kernel_bench decode --batch 256 --nq 16 --nkv 8 --ctx 1600
+    python -m sdcguard_b200.tools.kernel_bench prefill --seqs 8 --len 2048 --nq 16 --nkv 8
+
+Each prints one JSON line: duration (median of the timed launches), achieved TFLOP/s or GB/s, and the cuBLAS
+time of the same GEMM shape for reference.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+
+import torch
+
+L2_FLUSH_BYTES = 256 << 20     # larger than the 126 MB L2
+
+
+def _timed(fn, iters: int, flush: bool = True) -> float:
+    buf = torch.empty(L2_FLUSH_BYTES, dtype=torch.int8, device="cuda") if flush else None
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(iters):
+        if buf is not None:
+            buf.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        b.synchronize()
+        ts.append(a.elapsed_time(b))
+    ts.sort()
+    return ts[len(ts) // 2]
+
+
+def bench_gemm(m, n, k, iters, bn=None):
+    from ..ops import gemm
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(0)
+    x = torch.randn(m, k, device=dev, generator=g).bfloat16()
+    w = (torch.randn(n, k, device=dev, generator=g) * 0.02).bfloat16()
+    cw = gemm.CheckedWeight(w)
+    st = gemm.StateTable(dev, 2)
+    s = st.add("gemm", cw.nb)
+    rs = gemm.row_sqnorm(x)
+    out = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+    ms = _timed(lambda: gemm.checked_linear(x, cw, st.state, s, row_sq=rs, out=out, bn=bn), iters)
+    mc = _timed(lambda: torch.matmul(x, w.t(), out=out), iters)
+    r = st.read()[0]
+    fl = 2.0 * m * n * k
+    return {"kernel": "checked_gemm", "m": m, "n": n, "k": k, "bn": bn or gemm.pick_bn(m, n), "us": round(ms * 1e3, 1),
+            "tflops": round(fl / ms / 1e9, 1), "cublas_us": round(mc * 1e3, 1),
+            "cublas_tflops": round(fl / mc / 1e9, 1), "worst_clean_z": round(r["z"], 4), "checks": r["checks"]}
+
+
+def bench_decode(batch, nq, nkv, ctx, iters):
+    from ..ops import attention
+    dev = torch.device("cuda")
+    pages_per = -(-ctx // 16) + 1
+    nblk = batch * pages_per + 1
+    g = torch.Generator(device=dev).manual_seed(0)
+    cache = torch.randn(nblk, 2, nkv, 16, 128, device=dev, generator=g).bfloat16()
+    perm = torch.randperm(nblk - 1, device=dev, generator=g)[: batch * pages_per].int() + 1
+    bt = perm.view(batch, pages_per).contiguous()
+    q = torch.randn(batch, nq, 128, device=dev, generator=g).bfloat16()
+    c = torch.full((batch,), ctx, dtype=torch.int32, device=dev)
+    req = torch.arange(batch, dtype=torch.int32, device=dev)
+    scratch = attention.decode_scratch(batch, nq, nkv, 4096, dev)
+    out = torch.empty_like(q)
+    ms = _timed(lambda: attention.decode(q, cache, bt, req, c, nq, nkv, 4096, out=out, scratch=scratch), iters)
+    byts = batch * ctx * nkv * 2 * 256
+    return {"kernel": "decode_attention", "batch": batch, "nq": nq, "nkv": nkv, "ctx": ctx, "us": round(ms * 1e3, 1),
+            "gbs": round(byts / ms / 1e6, 1), "kv_bytes": byts}
+
+
+def bench_prefill(seqs, length, nq, nkv, iters):
+    from ..ops import attention
+    dev = torch.device("cuda")
+    pages_per = -(-length // 16)
+    nblk = seqs * pages_per + 1
+    g = torch.Generator(device=dev).manual_seed(0)
+    cache = torch.randn(nblk, 2, nkv, 16, 128, device=dev, generator=g).bfloat16()
+    bt = (torch.arange(seqs * pages_per, device=dev, dtype=torch.int32) + 1).view(seqs, pages_per)
+    T = seqs * length
+    q = torch.randn(T, nq, 128, device=dev, generator=g).bfloat16()
+    pos = torch.arange(length, dtype=torch.int32, device=dev).repeat(seqs)
+    tiles = attention.prefill_tiles([i * length for i in range(seqs)], [length] * seqs, nq // nkv).to(dev)
+    out = torch.empty_like(q)
+    ms = _timed(lambda: attention.prefill(q, cache, bt, pos, tiles, nq, nkv, out=out), iters)
+    fl = 4.0 * seqs * nq * 128 * length * (length + 1) / 2       # causal QK^T and PV
+    return {"kernel": "prefill_attention", "seqs": seqs, "len": length, "nq": nq, "nkv": nkv,
+            "us": round(ms * 1e3, 1), "tflops": round(fl / ms / 1e9, 1)}
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(prog="python -m sdcguard_b200.tools.kernel_bench")
+    sub = ap.add_subparsers(dest="what", required=True)
+    a = sub.add_parser("gemm")
+    a.add_argument("--m", type=int, default=4096)
+    a.add_argument("--n", type=int, default=28672)
+    a.add_argument("--k", type=int, default=4096)
+    a.add_argument("--bn", type=int, default=None)
+    b = sub.add_parser("decode")
+    b.add_argument("--batch", type=int, default=256)
+    b.add_argument("--nq", type=int, default=16)
+    b.add_argument("--nkv", type=int, default=8)
+    b.add_argument("--ctx", type=int, default=1600)
+    c = sub.add_parser("prefill")
+    c.add_argument("--seqs", type=int, default=8)
+    c.add_argument("--len", type=int, default=2048)
+    c.add_argument("--nq", type=int, default=16)
+    c.add_argument("--nkv", type=int, default=8)
+    for p in (a, b, c):
+        p.add_argument("--iters", type=int, default=10)
+    args = ap.parse_args(argv)
+    if args.what == "gemm":
+        r = bench_gemm(args.m, args.n, args.k, args.iters, args.bn)
+    elif args.what == "decode":
+        r = bench_decode(args.batch, args.nq, args.nkv, args.ctx, args.iters)
+    else:
+        r = bench_prefill(args.seqs, args.len, args.nq, args.nkv, args.iters)
+    print(json.dumps(r), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())
