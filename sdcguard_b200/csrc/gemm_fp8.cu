@@ -1,0 +1,544 @@
+// Block-scaled fp8 checked GEMM for sm_100a: C = (A_q * s_a) @ (W_q * s_w)^T in bf16, with A_q, W_q fp8 E4M3,
+// s_a one power-of-two scale per row and 128-wide K block (1 x 128), s_w one per 128 x 128 block of W, fp32
+// accumulation on tcgen05 (kind::f8f6f4), and the ABFT check of every 128-column block of every output row.
+//
+// Scaling on Blackwell without a block-scale MMA: every 128-wide K block is one accumulation into a fresh TMEM
+// accumulator (four MMAs of K = 32); the epilogue warps read it with tcgen05.ld and add it to fp32 registers
+// multiplied by s_a[row, kb] * s_w[block, kb] ("promotion"). Two TMEM accumulators alternate, so the tensor cores
+// fill one K block while the epilogue promotes the previous one.
+//
+// The check needs no second pass and no other CTA. The B operand of every tile is 144 rows: the tile's 128 rows
+// of W_q and 16 checksum rows of its 128-column block (12 used): the plain and the +-1-signed sums of the block's
+// quantized rows, each split into six fp8 parts with their own power-of-two scales (about 24 significant bits in
+// total). The MMA computes the tile and its expected sums in one instruction stream (12.5% more MMA columns); the
+// epilogue promotes the checksum columns with the part scales, forms the block's plain / signed / squared /
+// absolute sums of the promoted accumulator, and judges them with the fp32-accumulation noise model of the bf16
+// kernel. Because the checksum rows are sums of the same quantized weights that the MMA uses, the identity holds
+// exactly up to rounding; a fault in the MMA, in TMEM or in the promotion breaks it.
+//
+// Also here: the activation quantizer (bf16 -> E4M3 with 1 x 128 power-of-two scales, and ||dequantized row||^2
+// for the noise model), with an exact replay mode that re-quantizes sampled rows and compares codes and scales
+// (the fp8 quantisation check).
+//
+// Reference: the reference does not check fp8 GEMMs at all (src/sdcguard/guard.py:81-87; docs/STATUS.md "FP8 matmul
+// arithmetic: Planned"); its fp8 check re-quantizes two sampled rows against a one-step tolerance
+// (src/sdcguard/serve_fp8.py:1-24).
+#include <cuda_fp8.h>
+
+#include <cstring>
+
+#include "common.cuh"
+#include "tma_host.h"
+
+namespace sdc {
+namespace gemm8 {
+
+constexpr int BM = 128;
+constexpr int BN = 128;               // output columns per tile = one check block
+constexpr int CSR = 16;               // checksum rows per block in the B operand (12 used)
+constexpr int BNC = BN + CSR;         // MMA N
+constexpr int BK = 128;               // fp8 elements (= bytes) per K block = one scale block
+constexpr int A_BYTES = BM * BK;
+constexpr int B_BYTES = BNC * BK;
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;   // 34 KB, a multiple of 1 KB
+constexpr int STAGES = 6;
+constexpr int THREADS = 256;
+constexpr int STAGING_BYTES = 4 * 4096;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + STAGING_BYTES + 1024 + 512;
+constexpr int TMEM_COLS = 512;
+constexpr int SLOT_COLS = 256;
+constexpr float FP8_MAX = 448.f;
+
+struct Params8 {
+  int M, N, K, nb, kbs, m_tiles, total_tiles, group;
+  const float* sa;        // [M][kbs]
+  const float* sw;        // [nb][kbs]
+  const float* csc;       // [nb][kbs][12]: power-of-two scale of each checksum part
+  const float* row_sq;    // [M] ||dequantized row of A||^2
+  const float4* wstat;    // [nb] {||W_b||_F, ||plain||, ||signed||, max|W_b|} of the dequantized weights
+  __nv_bfloat16* C;
+  long long ldc;
+  unsigned long long* state;
+  int slot;
+  uint32_t sgn[4];
+  float zthr, prod_coef, out_coef, abs_floor, bound_coef;
+  int* err;
+  int inj_row, inj_col;
+  uint32_t inj_xor;
+};
+
+struct Ctl {
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+__device__ __forceinline__ void umma_f8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// kind::f8f6f4 instruction descriptor: A and B E4M3 (format 0), D fp32, both K-major
+__host__ __device__ constexpr uint32_t idesc_e4m3_f32(int M, int N) {
+  return (1u << 4) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void tile_coords8(const Params8& p, int tile, int& mt, int& nt) {
+  const int per_group = p.group * p.nb;
+  const int g = tile / per_group;
+  const int l = tile - g * per_group;
+  const int b0 = g * p.group;
+  const int gm = min(p.group, p.m_tiles - b0);
+  mt = b0 + l % gm;
+  nt = l / gm;
+}
+
+__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long* a) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(a) : "memory");
+  return v;
+}
+
+// the judge of the bf16 kernel (no bias in this GEMM)
+__device__ __forceinline__ void judge8(const Params8& p, int row, int b, float P, float S, float Q, float Aab, float ep,
+                                       float es, unsigned long long& k0, unsigned long long& k1, int& unj) {
+  const long long o = static_cast<long long>(row) * p.nb + b;
+  const float4 ws = __ldg(p.wstat + b);
+  const float xn = sqrtf(__ldg(p.row_sq + row));
+  const float prod = p.prod_coef * xn * fmaxf(ws.x, fmaxf(ws.y, ws.z));
+  const float den = sqrtf(Q) * p.out_coef + prod + p.abs_floor;
+  const float dp = fabsf(ep - P), ds = fabsf(es - S);
+  const float worst = Aab * p.out_coef + prod + p.abs_floor;
+  const float zp = fminf(__fdividef(dp, den), __fdividef(dp, worst) * p.zthr);
+  const float zs = __fdividef(ds, den);
+  float z = fmaxf(zp, zs);
+  int which = zs > zp ? 1 : 0;
+  const bool fin_exp = isfinite(ep) && isfinite(es) && isfinite(prod);
+  const bool fin_act = isfinite(P) && isfinite(S) && isfinite(Q) && isfinite(Aab);
+  bool judged = true;
+  if (!fin_exp) {
+    judged = false;
+  } else if (!fin_act) {
+    const float bound = p.bound_coef * xn * ws.w;
+    if (bound < 1e18f) {
+      z = __int_as_float(0x7f800000);
+      which = 0;
+    } else {
+      judged = false;
+    }
+  } else if (!(z <= 3.0e38f)) {
+    z = __int_as_float(0x7f800000);
+  }
+  if (judged) {
+    const unsigned long long zb = static_cast<unsigned long long>(__float_as_uint(z)) << 32;
+    k0 = zb | ((static_cast<unsigned long long>(o) * 2ull + which) & 0xffffffffull);
+    k1 = zb | __float_as_uint(den);
+  } else {
+    unj = 1;
+  }
+}
+
+template <bool INJ>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
+                    const __grid_constant__ CUtensorMap tmWc, const __grid_constant__ CUtensorMap tmC,
+                    const Params8 p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* staging = smem + STAGES * STAGE_BYTES;
+  Ctl* ctl = reinterpret_cast<Ctl*>(staging + STAGING_BYTES);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&ctl->full[s], 1);
+      mbar_init(&ctl->empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&ctl->tfull[a], 1);
+      mbar_init(&ctl->tempty[a], 128);
+    }
+    mbar_init(&ctl->drain, 1);
+    ctl->abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 2) {
+    tmem_alloc(&ctl->tmem_base, TMEM_COLS);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmW);
+    tma_prefetch_desc(&tmWc);
+    tma_prefetch_desc(&tmC);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = ctl->tmem_base;
+  volatile int* abort_flag = &ctl->abort_flag;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      uint32_t issued = 0, issued_phase = 0;
+      for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
+        int mt, nt;
+        tile_coords8(p, tile, mt, nt);
+        for (int kb = 0; kb < p.kbs; ++kb) {
+          if (!mbar_wait(&ctl->empty[stage], phase ^ 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + stage * STAGE_BYTES;
+          uint8_t* sb = sa + A_BYTES;
+          mbar_arrive_expect_tx(&ctl->full[stage], STAGE_BYTES);
+          tma_load_2d(sa, &tmA, &ctl->full[stage], kb * BK, mt * BM);
+          tma_load_2d(sb, &tmW, &ctl->full[stage], kb * BK, nt * BN);
+          tma_load_2d(sb + BN * BK, &tmWc, &ctl->full[stage], kb * BK, nt * CSR);
+          issued |= 1u << stage;
+          issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        record_error(p.err, ERR_TIMEOUT_PRODUCER);
+        *abort_flag = 1;
+        for (int s = 0; s < STAGES; ++s)
+          if (issued & (1u << s)) mbar_wait(&ctl->full[s], (issued_phase >> s) & 1u, nullptr);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer: one accumulator per K block
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      unsigned g = 0;
+      const uint32_t idesc = idesc_e4m3_f32(BM, BNC);
+      for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
+        for (int kb = 0; kb < p.kbs && ok; ++kb, ++g) {
+          const int slot = g & 1;
+          if (!mbar_wait(&ctl->tempty[slot], ((g >> 1) & 1u) ^ 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (!mbar_wait(&ctl->full[stage], phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
+          const uint64_t adesc = umma_desc_sw128(sa);
+          const uint64_t bdesc = umma_desc_sw128(sa + A_BYTES);
+          const uint32_t d = tmem_base + static_cast<uint32_t>(slot * SLOT_COLS);
+#pragma unroll
+          for (int ks = 0; ks < BK / 32; ++ks)     // 32 fp8 = 32 bytes per MMA: +2 in the >>4 address field
+            umma_f8(d, adesc + 2ull * ks, bdesc + 2ull * ks, idesc, ks != 0 ? 1u : 0u);
+          umma_commit(&ctl->empty[stage]);
+          umma_commit(&ctl->tfull[slot]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        record_error(p.err, ERR_TIMEOUT_MMA);
+        *abort_flag = 1;
+        umma_commit(&ctl->drain);
+        mbar_wait(&ctl->drain, 0, nullptr);
+      }
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ epilogue: promote, judge, store
+    const int q = warp & 3;
+    const int ew = warp - 4;
+    const int row_in_tile = q * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+    unsigned long long* st = p.state + static_cast<long long>(p.slot) * 4;
+    uint8_t* stg = staging + ew * 4096;
+    unsigned g = 0;
+    bool stop = false;
+    for (int tile = blockIdx.x; tile < p.total_tiles && !stop; tile += gridDim.x) {
+      int mt, nt;
+      tile_coords8(p, tile, mt, nt);
+      const int row = mt * BM + row_in_tile;
+      const bool valid = row < p.M;
+      float acc[BN];
+      float cs[12];
+#pragma unroll
+      for (int j = 0; j < BN; ++j) acc[j] = 0.f;
+#pragma unroll
+      for (int j = 0; j < 12; ++j) cs[j] = 0.f;
+      for (int kb = 0; kb < p.kbs; ++kb, ++g) {
+        const int slot = g & 1;
+        const bool got = mbar_wait(&ctl->tfull[slot], (g >> 1) & 1u, abort_flag);
+        if (named_bar_or(1, 128, !got)) {
+          if (!got) record_error(p.err, ERR_TIMEOUT_EPILOGUE);
+          *abort_flag = 1;
+          stop = true;
+          break;
+        }
+        tc_fence_after();
+        const float s = (valid ? __ldg(p.sa + static_cast<long long>(row) * p.kbs + kb) : 0.f) *
+                        __ldg(p.sw + static_cast<long long>(nt) * p.kbs + kb);
+        const uint32_t ta = tmem_base + static_cast<uint32_t>(slot * SLOT_COLS) + lane_off;
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          uint32_t r[32];
+          tmem_ld32(ta + h * 32, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc[h * 32 + j] = fmaf(u32_as_f32(r[j]), s, acc[h * 32 + j]);
+        }
+        {
+          uint32_t r[16];
+          tmem_ld8(ta + BN, *reinterpret_cast<uint32_t(*)[8]>(&r[0]));
+          tmem_ld8(ta + BN + 8, *reinterpret_cast<uint32_t(*)[8]>(&r[8]));
+          tmem_wait_ld();
+          const float* cp = p.csc + (static_cast<long long>(nt) * p.kbs + kb) * 12;
+#pragma unroll
+          for (int j = 0; j < 12; ++j) cs[j] = fmaf(u32_as_f32(r[j]), s * __ldg(cp + j), cs[j]);
+        }
+        tc_fence_before();
+        mbar_arrive(&ctl->tempty[slot]);
+      }
+      if (stop) break;
+      // ---- the tile's 128 columns of this row are final: injected fault, block sums, judge, store
+      const int col0 = nt * BN;
+      if (INJ && row == p.inj_row) {
+#pragma unroll
+        for (int j = 0; j < BN; ++j)
+          if (col0 + j == p.inj_col) acc[j] = __uint_as_float(__float_as_uint(acc[j]) ^ p.inj_xor);
+      }
+      float P = 0.f, S = 0.f, Q = 0.f, Aab = 0.f;
+#pragma unroll
+      for (int j = 0; j < BN; ++j) {
+        const float x = acc[j];
+        P += x;
+        S += ((p.sgn[j >> 5] >> (j & 31)) & 1u) ? -x : x;
+        Q = fmaf(x, x, Q);
+        Aab += fabsf(x);
+      }
+      unsigned long long k0 = 0ull, k1 = 0ull;
+      int unj = 0;
+      if (valid) {
+        const float ep = ((cs[0] + cs[1]) + (cs[2] + cs[3])) + (cs[4] + cs[5]);
+        const float es = ((cs[6] + cs[7]) + (cs[8] + cs[9])) + (cs[10] + cs[11]);
+        judge8(p, row, nt, P, S, Q, Aab, ep, es, k0, k1, unj);
+      }
+#pragma unroll
+      for (int h = 0; h < BN / 64; ++h) {
+        uint32_t packed[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) packed[j] = pack_bf16x2(acc[h * 64 + 2 * j], acc[h * 64 + 2 * j + 1]);
+        if (lane == 0) bulk_wait_read0();
+        __syncwarp();
+        uint8_t* myrow = stg + lane * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const uint4 v = make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2], packed[4 * c + 3]);
+          *reinterpret_cast<uint4*>(myrow + ((c ^ (lane & 7)) << 4)) = v;   // 128-byte swizzle
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmC, stg, col0 + h * 64, mt * BM + q * 32);
+          bulk_commit();
+        }
+      }
+      k0 = warp_max_u64(k0);
+      k1 = warp_max_u64(k1);
+#pragma unroll
+      for (int m = 16; m > 0; m >>= 1) unj += __shfl_xor_sync(0xffffffffu, unj, m);
+      if (lane == 0) {
+        if (k0 > ld_relaxed_u64(st + 0)) atomicMax(st + 0, k0);
+        if (k1 > ld_relaxed_u64(st + 1)) atomicMax(st + 1, k1);
+        if (unj) atomicAdd(st + 3, static_cast<unsigned long long>(unj));
+        if (tile == 0 && q == 0) atomicAdd(st + 2, 1ull);      // one count per launch
+      }
+    }
+  }
+
+  if (warp >= 4 && lane == 0) bulk_wait0();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------------------------------- quantizer
+// One warp per row: for every 128-column block, amax -> s = the smallest power of two with amax / s <= 448,
+// q = E4M3(x / s) (saturating), and ||dequantized row||^2. In check mode (check != null, rows = sampled rows)
+// the codes and scales are recomputed and compared with the stored ones instead of written.
+__global__ void __launch_bounds__(256) act_quant_kernel(const __nv_bfloat16* __restrict__ x, long long ldx, int M, int K,
+                                                        uint8_t* __restrict__ xq, float* __restrict__ sa,
+                                                        float* __restrict__ row_sq, const int* rows, int nrows,
+                                                        unsigned long long* check) {
+  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (check != nullptr && blockIdx.x == 0 && threadIdx.x == 0) atomicAdd(check + 2, 1ull);
+  const int n = rows ? nrows : M;
+  if (w >= n) return;
+  const int row = rows ? rows[w] : w;
+  const int kbs = K / 128;
+  float sq = 0.f;
+  int bad = -1;
+  for (int kb = 0; kb < kbs; ++kb) {
+    const int c = kb * 128 + lane * 4;
+    const uint2 raw = *reinterpret_cast<const uint2*>(x + static_cast<long long>(row) * ldx + c);
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
+    const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
+    float amax = fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(b.x), fabsf(b.y)));
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, m));
+    float s = 1.f;
+    if (amax > 0.f && isfinite(amax)) {
+      int ex;
+      const float fr = frexpf(amax / FP8_MAX, &ex);     // amax / 448 = fr * 2^ex, fr in [0.5, 1)
+      s = ldexpf(1.f, fr == 0.5f ? ex - 1 : ex);
+    }
+    const float inv = 1.f / s;                          // exact: s is a power of two
+    const float v[4] = {a.x * inv, a.y * inv, b.x * inv, b.y * inv};
+    uint32_t codes = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const __nv_fp8_storage_t cq = __nv_cvt_float_to_fp8(v[j], __NV_SATFINITE, __NV_E4M3);
+      codes |= static_cast<uint32_t>(cq) << (8 * j);
+      __nv_fp8_e4m3 e;
+      e.__x = cq;
+      const float d = static_cast<float>(e) * s;
+      sq = fmaf(d, d, sq);
+    }
+    uint32_t* qp = reinterpret_cast<uint32_t*>(xq + static_cast<long long>(row) * K + c);
+    float* sp = sa + static_cast<long long>(row) * kbs + kb;
+    if (check == nullptr) {
+      *qp = codes;
+      if (lane == 0) *sp = s;
+    } else {
+      const bool diff = *qp != codes || (lane == 0 && !(*sp == s));
+      if (diff && bad < 0) bad = c;
+    }
+  }
+#pragma unroll
+  for (int m = 16; m > 0; m >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, m);
+  if (check == nullptr) {
+    if (lane == 0 && row_sq != nullptr) row_sq[row] = sq;
+  } else {
+    int b = bad < 0 ? 0x7fffffff : bad;
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) b = min(b, __shfl_xor_sync(0xffffffffu, b, m));
+    if (lane == 0 && b != 0x7fffffff) report_replay_mismatch(check, static_cast<unsigned long long>(row) * K + b);
+  }
+}
+
+}  // namespace gemm8
+}  // namespace sdc
+
+using namespace sdc::gemm8;
+
+template <bool INJ>
+static int launch8(const CUtensorMap& a, const CUtensorMap& w, const CUtensorMap& wc, const CUtensorMap& c,
+                   const Params8& p, int grid, cudaStream_t st) {
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_fp8_kernel<INJ>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    attr = true;
+  }
+  gemm_fp8_kernel<INJ><<<grid, THREADS, SMEM_BYTES, st>>>(a, w, wc, c, p);
+  return static_cast<int>(cudaGetLastError());
+}
+
+extern "C" {
+
+// A_q [M][K] E4M3 codes with scales sa [M][K/128]; W_q [N][K] with scales sw [N/128][K/128]; Wc_q [16 N/128][K]
+// checksum rows with part scales csc [N/128][K/128][12]. N and K must be multiples of 128.
+int sdc_gemm_fp8(const void* Aq, const float* sa, const void* Wq, const void* Wcq, const float* sw, const float* csc,
+                 int M, int N, int K, void* Cout, long long ldc, const float* row_sq, const float* wstat,
+                 unsigned long long* state, int slot, unsigned s0, unsigned s1, unsigned s2, unsigned s3, float zthr,
+                 float prod_coef, float out_coef, float abs_floor, float bound_coef, int* err, int inj_row,
+                 int inj_col, unsigned inj_xor, void* stream) {
+  if (M <= 0) return 0;
+  if (N <= 0 || K <= 0 || N % BN || K % BK || ldc % 8) return -1;
+  Params8 p;
+  std::memset(&p, 0, sizeof(p));
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.nb = N / BN;
+  p.kbs = K / BK;
+  p.m_tiles = (M + BM - 1) / BM;
+  p.total_tiles = p.m_tiles * p.nb;
+  {
+    const long long band = static_cast<long long>(BM) * K;
+    int g = static_cast<int>((24ll << 20) / band);
+    p.group = g < 1 ? 1 : (g > 16 ? 16 : (g > p.m_tiles ? p.m_tiles : g));
+  }
+  p.sa = sa;
+  p.sw = sw;
+  p.csc = csc;
+  p.row_sq = row_sq;
+  p.wstat = reinterpret_cast<const float4*>(wstat);
+  p.C = static_cast<__nv_bfloat16*>(Cout);
+  p.ldc = ldc;
+  p.state = state;
+  p.slot = slot;
+  p.sgn[0] = s0;
+  p.sgn[1] = s1;
+  p.sgn[2] = s2;
+  p.sgn[3] = s3;
+  p.zthr = zthr;
+  p.prod_coef = prod_coef;
+  p.out_coef = out_coef;
+  p.abs_floor = abs_floor;
+  p.bound_coef = bound_coef;
+  p.err = err;
+  p.inj_row = inj_row;
+  p.inj_col = inj_col;
+  p.inj_xor = inj_xor;
+  CUtensorMap ma, mw, mc, mo;
+  if (!make_map_u8_sw128(&ma, Aq, M, K, K, BK, BM)) return -2;
+  if (!make_map_u8_sw128(&mw, Wq, N, K, K, BK, BN)) return -3;
+  if (!make_map_u8_sw128(&mc, Wcq, static_cast<long long>(p.nb) * CSR, K, K, BK, CSR)) return -4;
+  if (!make_map_bf16_sw128(&mo, Cout, M, N, ldc, 64, 32, false)) return -5;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int grid = p.total_tiles < sms ? p.total_tiles : sms;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return inj_row >= 0 ? launch8<true>(ma, mw, mc, mo, p, grid, st) : launch8<false>(ma, mw, mc, mo, p, grid, st);
+}
+
+// x [M][K] bf16 (row stride ldx) -> xq [M][K] E4M3 codes, sa [M][K/128], row_sq [M]. rows / check: replay mode.
+int sdc_fp8_quant_act(const void* x, long long ldx, int M, int K, void* xq, float* sa, float* row_sq, const int* rows,
+                      int nrows, void* check, void* stream) {
+  if (K % 128 || ldx % 4) return -1;
+  const int n = rows ? nrows : M;
+  if (n <= 0) return 0;
+  act_quant_kernel<<<(n * 32 + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), ldx, M, K, static_cast<uint8_t*>(xq), sa, row_sq, rows, nrows,
+      static_cast<unsigned long long*>(check));
+  return static_cast<int>(cudaGetLastError());
+}
+
+}  // extern "C"

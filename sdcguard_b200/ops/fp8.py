@@ -1,0 +1,128 @@
+"""Block-scaled fp8 checked GEMM (`csrc/gemm_fp8.cu`): E4M3 operands, 1 x 128 activation scales and 128 x 128 weight
+scales (powers of two, as UE8M0 scale factors are), fp32 accumulation, bf16 output, ABFT check of every 128-column
+block of every row in the same kernel.
+
+    fw = Fp8Weight(w_bf16)                          # once: quantize W, checksum rows of the quantized blocks
+    xq = quantize_act(x)                            # E4M3 codes, scales, ||dequantized row||^2
+    y = checked_linear_fp8(xq, fw, state, slot)     # output + check
+    quantize_act(x, out=xq, rows=sample, check=state[s])   # exact replay of sampled rows (quantisation check)
+
+Checksum rows: for each 128-column block b of W and each 128-wide K block kb, the plain and the +-1-signed sums of
+the block's quantized rows (sums of E4M3 values, exact in fp32) are split into six E4M3 parts, each with its own
+power-of-two scale (`csc`), so 12 rows of fp8 carry about 24 significant bits; they are rows 16 b .. 16 b + 11 of
+`wcq` (rows 12 to 15 zero) and ride in the same MMA as the tile's 128 weight rows.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+from .. import _native
+from ..numerics import abft
+from .gemm import _stream_ptr, error_word
+
+FP8_MAX = 448.0
+PARTS = 6
+
+
+def pow2_scale(amax: torch.Tensor) -> torch.Tensor:
+    """Smallest power of two s with amax / s <= 448 (1 where amax is 0)."""
+    r = amax.double() / FP8_MAX
+    m, e = torch.frexp(r)
+    e = torch.where(m == 0.5, e - 1, e)
+    s = torch.ldexp(torch.ones_like(r), e)
+    return torch.where(amax > 0, s, torch.ones_like(r)).float()
+
+
+def to_e4m3(x: torch.Tensor) -> torch.Tensor:
+    return x.clamp(-FP8_MAX, FP8_MAX).to(torch.float8_e4m3fn)
+
+
+class Fp8Weight:
+    def __init__(self, weight: torch.Tensor, mask: Optional[tuple] = None, c1: float = abft.C1, c2: float = abft.C2,
+                 c3: float = abft.C3):
+        n, k = weight.shape
+        if n % 128 or k % 128:
+            raise ValueError(f"fp8 checked GEMM needs n and k multiples of 128 (got n={n}, k={k})")
+        dev = weight.device
+        self.n, self.k, self.nb, self.kbs = n, k, n // 128, k // 128
+        self.mask = mask or abft.sign_mask()
+        w = weight.detach().float().view(self.nb, 128, self.kbs, 128)
+        self.sw = pow2_scale(w.abs().amax(dim=(1, 3))).contiguous()                  # (nb, kbs)
+        q = to_e4m3(w / self.sw[:, None, :, None])
+        self.wq = q.view(n, k).contiguous()
+        qf = q.float()                                                                # quantized values
+        deq = qf * self.sw[:, None, :, None]
+        s = abft.sign_vector(self.mask, dtype=torch.float32, device=dev).view(1, 128, 1, 1)
+        plain = qf.double().sum(1)                                                    # (nb, kbs, 128) exact
+        signed = (qf.double() * s.double()).sum(1)
+        rows = torch.zeros(self.nb, 16, self.kbs, 128, dtype=torch.float32, device=dev)
+        csc = torch.zeros(self.nb, self.kbs, 12, dtype=torch.float32, device=dev)
+        for j, total in enumerate((plain, signed)):
+            r = total.clone()
+            for i in range(PARTS):
+                amax = r.abs().amax(dim=2)                                            # (nb, kbs)
+                sc = pow2_scale(amax).double()
+                part = to_e4m3((r / sc[..., None]).float()).float().double()
+                rows[:, 6 * j + i] = part.float()
+                csc[:, :, 6 * j + i] = torch.where(amax > 0, sc, torch.zeros_like(sc)).float()
+                r = r - part * sc[..., None]
+        self.wcq = to_e4m3(rows).view(self.nb * 16, self.kbs * 128).contiguous()
+        self.csc = csc.contiguous()
+        dq = deq.view(self.nb, 128, k).double()
+        pl, sg = dq.sum(1), (dq * s.view(1, 128, 1).double()).sum(1)
+        self.wstat = torch.stack([torch.linalg.vector_norm(dq, dim=(1, 2)), torch.linalg.vector_norm(pl, dim=1),
+                                  torch.linalg.vector_norm(sg, dim=1), dq.abs().amax(dim=(1, 2))], dim=1).float()
+        self.prod_coef, self.out_coef = abft.coefficients(k, c1, c2, c3)
+
+    def dequantized(self) -> torch.Tensor:
+        return (self.wq.float().view(self.nb, 128, self.kbs, 128) * self.sw[:, None, :, None]).view(self.n, self.k)
+
+
+@dataclass
+class Fp8Act:
+    q: torch.Tensor         # (m, k) float8_e4m3fn
+    sa: torch.Tensor        # (m, k / 128) fp32 powers of two
+    row_sq: torch.Tensor    # (m,) ||dequantized row||^2
+
+    def dequantized(self) -> torch.Tensor:
+        m, k = self.q.shape
+        return (self.q.float().view(m, k // 128, 128) * self.sa[:, :, None]).view(m, k)
+
+
+def quantize_act(x: torch.Tensor, out: Optional[Fp8Act] = None, rows: Optional[torch.Tensor] = None,
+                 check: Optional[torch.Tensor] = None) -> Fp8Act:
+    """x (m, k) bf16 -> E4M3 codes with 1 x 128 power-of-two scales. With rows and check: exact replay of the
+    sampled rows against `out` (the stored codes and scales), nothing written."""
+    m, k = x.shape
+    if out is None:
+        out = Fp8Act(torch.empty(m, k, dtype=torch.float8_e4m3fn, device=x.device),
+                     torch.empty(m, k // 128, dtype=torch.float32, device=x.device),
+                     torch.empty(m, dtype=torch.float32, device=x.device))
+    _native.check(_native.lib().sdc_fp8_quant_act(
+        x.data_ptr(), x.stride(0), m, k, out.q.data_ptr(), out.sa.data_ptr(), out.row_sq.data_ptr(),
+        None if rows is None else rows.data_ptr(), 0 if rows is None else rows.numel(),
+        None if check is None else check.data_ptr(), _stream_ptr(x.device)), "fp8 quantize")
+    return out
+
+
+def checked_linear_fp8(xa: Fp8Act, fw: Fp8Weight, state: torch.Tensor, slot: int, out: Optional[torch.Tensor] = None,
+                       z_alarm: float = abft.Z_ALARM, inject: Optional[tuple] = None) -> torch.Tensor:
+    m, k = xa.q.shape
+    if k != fw.k:
+        raise ValueError(f"activations have {k} columns, the weight {fw.k}")
+    dev = xa.q.device
+    if out is None:
+        out = torch.empty(m, fw.n, dtype=torch.bfloat16, device=dev)
+    s = fw.mask
+    ir, ic, ix = (-1, -1, 0) if inject is None else (int(inject[0]), int(inject[1]), int(inject[2]))
+    _native.check(_native.lib().sdc_gemm_fp8(
+        xa.q.data_ptr(), xa.sa.data_ptr(), fw.wq.data_ptr(), fw.wcq.data_ptr(), fw.sw.data_ptr(), fw.csc.data_ptr(),
+        m, fw.n, k, out.data_ptr(), out.stride(0), xa.row_sq.data_ptr(), fw.wstat.data_ptr(), state.data_ptr(),
+        int(slot), s[0], s[1], s[2], s[3], float(z_alarm), float(fw.prod_coef), float(fw.out_coef),
+        float(abft.ABS_FLOOR), float(math.sqrt(k)), error_word(dev).data_ptr(), ir, ic, ix, _stream_ptr(dev)),
+        "fp8 checked GEMM")
+    return out

@@ -58,6 +58,35 @@ def bench_gemm(m, n, k, iters, bn=None):
             "cublas_tflops": round(fl / mc / 1e9, 1), "worst_clean_z": round(r["z"], 4), "checks": r["checks"]}
 
 
+def bench_fp8(m, n, k, iters):
+    from ..ops import gemm
+    from ..ops.fp8 import Fp8Weight, checked_linear_fp8, quantize_act
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(0)
+    x = torch.randn(m, k, device=dev, generator=g).bfloat16()
+    w = (torch.randn(n, k, device=dev, generator=g) * 0.02).bfloat16()
+    fw = Fp8Weight(w)
+    xa = quantize_act(x)
+    st = gemm.StateTable(dev, 2)
+    s = st.add("fp8", fw.nb)
+    out = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+    ms = _timed(lambda: checked_linear_fp8(xa, fw, st.state, s, out=out), iters)
+    mq = _timed(lambda: quantize_act(x, out=xa), iters)
+    r = st.read()[0]
+    fl = 2.0 * m * n * k
+    res = {"kernel": "checked_gemm_fp8", "m": m, "n": n, "k": k, "us": round(ms * 1e3, 1),
+           "tflops": round(fl / ms / 1e9, 1), "quant_us": round(mq * 1e3, 1), "worst_clean_z": round(r["z"], 4)}
+    try:        # unchecked reference: torch's scaled fp8 matmul (per-tensor scales), when available
+        a8 = x.float().clamp(-448, 448).to(torch.float8_e4m3fn)
+        b8 = w.float().mul(64).clamp(-448, 448).to(torch.float8_e4m3fn)
+        one = torch.ones((), device=dev)
+        mt = _timed(lambda: torch._scaled_mm(a8, b8.t(), scale_a=one, scale_b=one, out_dtype=torch.bfloat16), iters)
+        res.update(torch_scaled_mm_us=round(mt * 1e3, 1), torch_scaled_mm_tflops=round(fl / mt / 1e9, 1))
+    except Exception as e:  # noqa: BLE001
+        res["torch_scaled_mm"] = f"unavailable: {type(e).__name__}"
+    return res
+
+
 def bench_decode(batch, nq, nkv, ctx, iters):
     from ..ops import attention
     dev = torch.device("cuda")
@@ -110,16 +139,22 @@ def main(argv=None) -> int:
     b.add_argument("--nq", type=int, default=16)
     b.add_argument("--nkv", type=int, default=8)
     b.add_argument("--ctx", type=int, default=1600)
+    f = sub.add_parser("fp8")
+    f.add_argument("--m", type=int, default=4096)
+    f.add_argument("--n", type=int, default=28672)
+    f.add_argument("--k", type=int, default=4096)
     c = sub.add_parser("prefill")
     c.add_argument("--seqs", type=int, default=8)
     c.add_argument("--len", type=int, default=2048)
     c.add_argument("--nq", type=int, default=16)
     c.add_argument("--nkv", type=int, default=8)
-    for p in (a, b, c):
+    for p in (a, b, c, f):
         p.add_argument("--iters", type=int, default=10)
     args = ap.parse_args(argv)
     if args.what == "gemm":
         r = bench_gemm(args.m, args.n, args.k, args.iters, args.bn)
+    elif args.what == "fp8":
+        r = bench_fp8(args.m, args.n, args.k, args.iters)
     elif args.what == "decode":
         r = bench_decode(args.batch, args.nq, args.nkv, args.ctx, args.iters)
     else:
