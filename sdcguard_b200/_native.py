@@ -66,7 +66,7 @@ SIGNATURES: dict[str, tuple] = {
     "sdc_qk_norm_rope_kv": (I, [P, L, I, I, I, I, P, P, P, P, F, P, P, P, P, P, P]),
     "sdc_silu_mul_bf16": (I, [P, I, I, P, P, P, P, P]),
     "sdc_compare_rows_bf16": (I, [P, L, P, P, L, I, I, P, P]),
-    "sdc_attn_prefill": (I, [P, P, P, P, I, P, P, I, P, I, I, I, F, P, P, P]),
+    "sdc_attn_prefill": (I, [P, P, P, L, P, I, P, P, I, P, I, I, I, F, P, P, P]),
     "sdc_attn_decode": (I, [P, P, P, L, P, I, P, P, P, I, I, I, I, I, F, P, P, P, P]),
     "sdc_attn_decode_splits": (I, [I]),
     "sdc_fingerprint_many": (I, [P, I, L, U64, P, P]),

@@ -1,12 +1,12 @@
-// Paged-KV attention for serving (sm_100a): causal prefill (tensor cores, mma.m16n8k16 bf16 -> fp32,
-// flash-attention style online softmax) and single-token decode (CUDA cores, memory-bound), for grouped-query
-// attention with head_dim 128 and 16-token KV pages.
+// Paged-KV attention for serving (sm_100a): causal prefill (tcgen05 MMAs with S and O in TMEM, online softmax
+// with a conditional rescale) and single-token decode (split-KV, TMA-staged chunks, mma.m16n8k16), for
+// grouped-query attention with head_dim 128 and 16-token KV pages.
 //
 // KV cache layout for one layer: [num_blocks][2 (K, V)][kv_heads][16][128] bf16; a request's pages are listed
 // in its row of the block table.
 //
 // Row determinism. The arithmetic that produces one output row depends only on that row's query, its
-// position and the keys: key tiles start at absolute multiples of 64, tiles that are fully masked for a row
+// position and the keys: key tiles start at absolute multiples of the tile size, tiles that are fully masked for a row
 // leave its running max, sum and accumulator bit-identical (scale exp2(0) = 1, p = 0), and reductions run in
 // a fixed order. So running the same kernel again on any subset of rows (the `row_idx` list) reproduces their
 // outputs exactly. The serving check uses this: a rotating 1/64 sample of rows is recomputed on different
@@ -21,9 +21,7 @@ namespace attn {
 
 constexpr int D = 128;
 constexpr int PAGE = 16;
-constexpr int BN = 64;     // keys per tile
 constexpr int ROWS = 128;  // (token, head) rows per prefill CTA
-constexpr int WARPS = 8;
 
 struct PrefillParams {
   const __nv_bfloat16* q;     // [T, nq, D]
@@ -40,16 +38,6 @@ struct PrefillParams {
   unsigned long long* check;  // check mode: compare with o instead of writing (state row), or null
 };
 
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem)), "l"(gmem),
-               "r"(valid ? 16 : 0)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
                : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
@@ -73,218 +61,348 @@ __device__ __forceinline__ float ex2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
-// byte offset of (row, 16-byte chunk) in a [rows][128] bf16 tile with the chunk index XOR-swizzled by row
-__device__ __forceinline__ uint32_t swz(int row, int chunk) {
-  return static_cast<uint32_t>(row * 256 + ((chunk ^ (row & 7)) << 4));
-}
 
-__global__ void __launch_bounds__(WARPS * 32, 1) prefill_kernel(const PrefillParams p) {
-  extern __shared__ __align__(128) uint8_t sm[];
-  uint8_t* sQ = sm;                         // ROWS x 256 B
-  uint8_t* sK = sQ + ROWS * 256;            // 2 stages x BN x 256 B
-  uint8_t* sV = sK + 2 * BN * 256;          // 2 stages x BN x 256 B
-  __shared__ int s_tok[ROWS];
-  __shared__ int s_pos[ROWS];
-  __shared__ int s_maxpos;
+// ---------------------------------------------------------------------------------------------- prefill, tcgen05
+// The same tiles and row determinism as `prefill_kernel`, on the 5th-generation tensor cores:
+//   warp 0   TMA: the request's K and V pages of a 128-key tile (one 16-row x 128-byte box per page, half the head
+//            dim, K or V, 128-byte swizzle) into one of two stages; the unloaded V rows of a partial last tile are
+//            cleared (their weights are zero, stale shared memory could hold NaN patterns);
+//   warp 1   MMA: S = Q K^T into one of two TMEM accumulators (M = 128 rows, N = 128 keys, K = 128), and
+//            O += P V into a third (V as an MN-major operand, dims contiguous); S of tile j+1 is computed while
+//            the softmax works on tile j;
+//   warps 4-7 one thread per row: read S from TMEM, causal mask, running max with a conditional rescale (the
+//            reference maximum only moves when a row's maximum grows by more than 2^8, so O in TMEM is rescaled
+//            rarely), P = exp2(S - max) as bf16 into shared memory (the A operand of PV), the row sum of the bf16
+//            weights, and at the end O / l to the output (or compared with it in check mode).
+// Every decision is per row, key tiles start at absolute multiples of 128, and fully masked tiles change nothing,
+// so a replay of any subset of rows reproduces their outputs bit for bit.
+namespace pf {
+constexpr int KT = 128;                   // keys per tile
+constexpr int HALF_B = 128 * 128;         // one dims-half (64 bf16 = 128 B) of a 128-row tile
+constexpr int TILE_B = 2 * HALF_B;        // 32 KB: 128 rows x 128 dims bf16
+constexpr int OFF_Q = 0, OFF_K = TILE_B, OFF_V = 3 * TILE_B, OFF_P = 5 * TILE_B, OFF_CTL = 6 * TILE_B;
+constexpr float RESCALE_LOG2 = 8.f;
+constexpr int PG_BYTES = PAGE * D * 2;    // one page of K (or V) of one kv head
+struct Ctl {
+  uint64_t k_full[2], v_full[2], kv_empty[2], s_full[2], s_empty[2];
+  uint64_t p_full, pv_done, q_ready, drain;
+  uint32_t tmem_base;
+  int abort_flag;
+  int maxpos;
+  int tok[ROWS];
+  int pos[ROWS];
+};
+constexpr int SMEM = OFF_CTL + static_cast<int>(sizeof(Ctl)) + 1024;
+}  // namespace pf
 
+__global__ void __launch_bounds__(256, 1) prefill_tc_kernel(const __grid_constant__ CUtensorMap tm,
+                                                            const PrefillParams p) {
+  using namespace pf;
+  extern __shared__ uint8_t pf_raw[];
+  uint8_t* sm = pf_raw + ((1024 - (smem_u32(pf_raw) & 1023)) & 1023);
+  Ctl* ctl = reinterpret_cast<Ctl*>(sm + OFF_CTL);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = p.nq / p.nkv;
-  const int tpc = ROWS / G;                 // tokens per CTA
+  const int tpc = ROWS / G;
   const int4 tile = p.tiles[blockIdx.x];
   const int req = tile.x, kvh = blockIdx.y;
-  if (tid == 0) s_maxpos = -1;
+  if (tid == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&ctl->k_full[i], 1);
+      mbar_init(&ctl->v_full[i], 1);
+      mbar_init(&ctl->kv_empty[i], 1);
+      mbar_init(&ctl->s_full[i], 1);
+      mbar_init(&ctl->s_empty[i], ROWS);
+    }
+    mbar_init(&ctl->p_full, ROWS);
+    mbar_init(&ctl->pv_done, 1);
+    mbar_init(&ctl->q_ready, ROWS);
+    mbar_init(&ctl->drain, 1);
+    ctl->abort_flag = 0;
+    ctl->maxpos = -1;
+    fence_mbar_init();
+  }
+  if (warp == 2) {
+    tmem_alloc(&ctl->tmem_base, 512);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) tma_prefetch_desc(&tm);
+  tc_fence_before();
   __syncthreads();
-  for (int r = tid; r < ROWS; r += blockDim.x) {
+  tc_fence_after();
+  if (tid >= 128) {
+    const int r = tid - 128;
     const int ti = r / G;
     int tok = -1;
     if (ti < tile.z && ti < tpc) tok = tile.w >= 0 ? p.row_idx[tile.w + ti] : tile.y + ti;
-    s_tok[r] = tok;
+    ctl->tok[r] = tok;
     const int ps = tok >= 0 ? p.pos[tok] : -1;
-    s_pos[r] = ps;
-    if (ps >= 0) atomicMax(&s_maxpos, ps);
+    ctl->pos[r] = ps;
+    if (ps >= 0) atomicMax(&ctl->maxpos, ps);
   }
   __syncthreads();
-  const int maxpos = s_maxpos;
+  const int maxpos = ctl->maxpos;
+  const int ntiles = maxpos >= 0 ? maxpos / KT + 1 : 0;
+  const uint32_t tmem = ctl->tmem_base;
+  volatile int* abort_flag = &ctl->abort_flag;
   const int* bt = p.block_table + static_cast<long long>(req) * p.max_pages;
 
-  // Q rows -> shared memory
-  for (int c = tid; c < ROWS * 16; c += blockDim.x) {
-    const int r = c >> 4, ch = c & 15;
-    const int tok = s_tok[r];
-    const int head = kvh * G + (r % G);
-    const __nv_bfloat16* src = p.q + (static_cast<long long>(tok < 0 ? 0 : tok) * p.nq + head) * D + ch * 8;
-    cp_async16(sQ + swz(r, ch), src, tok >= 0);
-  }
-  cp_async_commit();
-
-  const int ntiles = maxpos >= 0 ? maxpos / BN + 1 : 0;
-  auto load_kv = [&](int kt, int stage) {
-    uint8_t* dk = sK + stage * BN * 256;
-    uint8_t* dv = sV + stage * BN * 256;
-    for (int c = tid; c < BN * 16 * 2; c += blockDim.x) {
-      const int isv = c >= BN * 16;
-      const int cc = isv ? c - BN * 16 : c;
-      const int key = cc >> 4, ch = cc & 15;
-      const int gkey = kt * BN + key;
-      const int page = gkey / PAGE;
-      const bool valid = gkey <= maxpos;
-      const long long blk = valid ? bt[page] : 0;
-      const __nv_bfloat16* src =
-          p.cache + (((blk * 2 + isv) * p.nkv + kvh) * PAGE + (gkey % PAGE)) * D + ch * 8;
-      cp_async16((isv ? dv : dk) + swz(key, ch), src, valid);
-    }
-    cp_async_commit();
-  };
-  if (ntiles > 0) load_kv(0, 0);
-
-  // per-thread rows: g and g+8 of the warp's 16
-  const int g = lane >> 2, t4 = lane & 3;
-  const int r0 = warp * 16 + g, r1 = r0 + 8;
-  const int pos0 = s_pos[r0], pos1 = s_pos[r1];
-  int wmin = min(pos0 < 0 ? 0x7fffffff : pos0, pos1 < 0 ? 0x7fffffff : pos1);
-#pragma unroll
-  for (int m = 1; m < 32; m <<= 1) wmin = min(wmin, __shfl_xor_sync(0xffffffffu, wmin, m));
-
-  float o[16][4];
-#pragma unroll
-  for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-  const uint32_t qbase = smem_u32(sQ);
-
-  for (int kt = 0; kt < ntiles; ++kt) {
-    const int stage = kt & 1;
-    if (kt + 1 < ntiles) {
-      load_kv(kt + 1, stage ^ 1);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
-    __syncthreads();
-    const uint32_t kbase = smem_u32(sK + stage * BN * 256);
-    const uint32_t vbase = smem_u32(sV + stage * BN * 256);
-
-    float s[8][4];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
-#pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
-      uint32_t a0, a1, a2, a3;
-      const int qr = warp * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
-      ldsm_x4(qbase + swz(qr, kk * 2 + (lane >> 4)), a0, a1, a2, a3);
-#pragma unroll
-      for (int n2 = 0; n2 < 4; ++n2) {
-        uint32_t b0, b1, b2, b3;
-        const int kr = n2 * 16 + (lane & 7) + 8 * (lane >> 4);
-        ldsm_x4(kbase + swz(kr, kk * 2 + ((lane >> 3) & 1)), b0, b1, b2, b3);
-        mma_bf16(s[2 * n2], a0, a1, a2, a3, b0, b1);
-        mma_bf16(s[2 * n2 + 1], a0, a1, a2, a3, b2, b3);
+  if (warp == 0 && ntiles > 0) {
+    // ------------------------------------------------------------ TMA producer (all 32 lanes issue)
+    bool ok = true;
+    int last = -1;                        // last tile whose loads were issued
+    for (int j = 0; j < ntiles && ok; ++j) {
+      const int st = j & 1;
+      bool got = true;
+      if (lane == 0) got = mbar_wait(&ctl->kv_empty[st], ((j >> 1) & 1u) ^ 1u, abort_flag);
+      if (!__shfl_sync(0xffffffffu, got ? 1 : 0, 0)) {
+        ok = false;
+        break;
       }
-    }
-    // scale, causal mask (only tiles that reach past the warp's smallest position need it)
-    const bool need_mask = kt * BN + BN - 1 > wmin;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float v = s[j][e] * p.scale_log2;
-        if (need_mask) {
-          const int key = kt * BN + 8 * j + 2 * t4 + (e & 1);
-          const int ps = e < 2 ? pos0 : pos1;
-          if (key > ps) v = -INFINITY;
+      const int npg = min(KT / PAGE, maxpos / PAGE - j * (KT / PAGE) + 1);
+      uint8_t* kbuf = sm + OFF_K + st * TILE_B;
+      uint8_t* vbuf = sm + OFF_V + st * TILE_B;
+      if (npg < KT / PAGE) {
+        for (int i = lane; i < (KT - npg * PAGE) * 16; i += 32) {
+          const int rr = npg * PAGE + (i >> 4), c = i & 15;
+          *reinterpret_cast<uint4*>(vbuf + (c >> 3) * HALF_B + rr * 128 + (c & 7) * 16) = make_uint4(0, 0, 0, 0);
         }
-        s[j][e] = v;
+        fence_proxy_async_smem();
+      }
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&ctl->k_full[st], npg * PG_BYTES);
+        mbar_arrive_expect_tx(&ctl->v_full[st], npg * PG_BYTES);
+      }
+      __syncwarp();
+      if (lane < 4 * npg) {
+        const int pg = lane >> 2, kv = (lane >> 1) & 1, half = lane & 1;
+        const long long blk = bt[j * (KT / PAGE) + pg];
+        const int row = static_cast<int>(((blk * 2 + kv) * p.nkv + kvh) * PAGE);
+        uint8_t* dst = (kv ? vbuf : kbuf) + half * HALF_B + pg * PAGE * 128;
+        tma_load_2d(dst, &tm, kv ? &ctl->v_full[st] : &ctl->k_full[st], half * 64, row);
+      }
+      last = j;
+    }
+    if (!ok && lane == 0) {
+      record_error(nullptr, ERR_TIMEOUT_PRODUCER);
+      *abort_flag = 1;
+      // the copies already issued must land before the CTA's shared memory is released (bounded waits)
+      for (int j = last > 0 ? last - 1 : 0; j <= last; ++j) {
+        mbar_wait(&ctl->k_full[j & 1], (j >> 1) & 1u, nullptr);
+        mbar_wait(&ctl->v_full[j & 1], (j >> 1) & 1u, nullptr);
       }
     }
-    float mx0 = -INFINITY, mx1 = -INFINITY;
+  } else if (warp == 1 && ntiles > 0) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      bool ok = mbar_wait(&ctl->q_ready, 0, abort_flag);
+      const uint32_t idesc_s = idesc_bf16_f32(128, KT);
+      const uint32_t idesc_o = idesc_bf16_f32(128, D) | (1u << 16);     // B (V) MN-major
+      const uint32_t qa = smem_u32(sm + OFF_Q), pa = smem_u32(sm + OFF_P);
+      for (int j = 0; j <= ntiles && ok; ++j) {
+        if (j < ntiles) {
+          const int st = j & 1;
+          const uint32_t par = (j >> 1) & 1u;
+          ok = mbar_wait(&ctl->k_full[st], par, abort_flag) && mbar_wait(&ctl->s_empty[st], par ^ 1u, abort_flag);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t ka = smem_u32(sm + OFF_K + st * TILE_B);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      mx0 = fmaxf(mx0, fmaxf(s[j][0], s[j][1]));
-      mx1 = fmaxf(mx1, fmaxf(s[j][2], s[j][3]));
-    }
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-    const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
-    const float u0 = n0 == -INFINITY ? 0.f : n0, u1 = n1 == -INFINITY ? 0.f : n1;
-    const float al0 = ex2(m0 - u0), al1 = ex2(m1 - u1);
-    m0 = n0;
-    m1 = n1;
-    float ps0 = 0.f, ps1 = 0.f;
-    uint32_t pa[8][2];
+          for (int ks = 0; ks < D / 16; ++ks) {
+            const uint32_t off = (ks >> 2) * HALF_B + (ks & 3) * 32;
+            umma_f16(tmem + st * KT, umma_desc_sw128(qa + off), umma_desc_sw128(ka + off), idesc_s, ks ? 1u : 0u);
+          }
+          umma_commit(&ctl->s_full[st]);
+        }
+        if (j >= 1) {
+          const int jj = j - 1, st = jj & 1;
+          ok = mbar_wait(&ctl->p_full, jj & 1u, abort_flag) && mbar_wait(&ctl->v_full[st], (jj >> 1) & 1u, abort_flag);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t va = smem_u32(sm + OFF_V + st * TILE_B);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float p0 = ex2(s[j][0] - u0), p1 = ex2(s[j][1] - u0);
-      const float p2 = ex2(s[j][2] - u1), p3 = ex2(s[j][3] - u1);
-      ps0 += p0 + p1;
-      ps1 += p2 + p3;
-      pa[j][0] = pack_bf16x2(p0, p1);
-      pa[j][1] = pack_bf16x2(p2, p3);
-    }
-    l0 = l0 * al0 + ps0;
-    l1 = l1 * al1 + ps1;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      o[i][0] *= al0;
-      o[i][1] *= al0;
-      o[i][2] *= al1;
-      o[i][3] *= al1;
-    }
-#pragma unroll
-    for (int kk2 = 0; kk2 < 4; ++kk2) {
-      const uint32_t a0 = pa[2 * kk2][0], a1 = pa[2 * kk2][1], a2 = pa[2 * kk2 + 1][0], a3 = pa[2 * kk2 + 1][1];
-#pragma unroll
-      for (int dt = 0; dt < 8; ++dt) {
-        uint32_t b0, b1, b2, b3;
-        const int vr = kk2 * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
-        ldsm_x4_t(vbase + swz(vr, dt * 2 + (lane >> 4)), b0, b1, b2, b3);
-        mma_bf16(o[2 * dt], a0, a1, a2, a3, b0, b1);
-        mma_bf16(o[2 * dt + 1], a0, a1, a2, a3, b2, b3);
+          for (int ks = 0; ks < KT / 16; ++ks) {
+            const uint64_t ad = umma_desc_sw128(pa + (ks >> 2) * HALF_B + (ks & 3) * 32);
+            const uint64_t bd = umma_desc_sw128_mn(va + ks * 2048, HALF_B, 1024);
+            umma_f16(tmem + 2 * KT, ad, bd, idesc_o, (jj > 0 || ks > 0) ? 1u : 0u);
+          }
+          umma_commit(&ctl->pv_done);
+          umma_commit(&ctl->kv_empty[st]);
+        }
+      }
+      if (!ok) {
+        record_error(nullptr, ERR_TIMEOUT_MMA);
+        *abort_flag = 1;
+        umma_commit(&ctl->drain);           // let the issued MMAs land before TMEM is released
+        mbar_wait(&ctl->drain, 0, nullptr);
       }
     }
-    __syncthreads();   // this stage is refilled by the next iteration's prefetch
-  }
-
-  // finalise: full row sums across the quad, normalise, store
-  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
-  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
-  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
-  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-  const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f, inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
-  const int tok0 = s_tok[r0], tok1 = s_tok[r1];
-  const int h0 = kvh * G + (r0 % G), h1 = kvh * G + (r1 % G);
-  float sq0 = 0.f, sq1 = 0.f;
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ softmax / output: thread = row
+    const int r = tid - 128;
+    const int q4 = warp & 3;
+    const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
+    const int tok = ctl->tok[r];
+    const int pos = ctl->pos[r];
+    const int head = kvh * G + (r % G);
+    // Q row -> shared memory (128-byte swizzle, two dims-halves)
+    {
+      uint8_t* qd = sm + OFF_Q;
+      const uint4* src = reinterpret_cast<const uint4*>(p.q + (static_cast<long long>(tok < 0 ? 0 : tok) * p.nq + head) * D);
 #pragma unroll
-  for (int dt = 0; dt < 16; ++dt) {
-    const int d = dt * 8 + 2 * t4;
-    const uint32_t v0 = pack_bf16x2(o[dt][0] * inv0, o[dt][1] * inv0);
-    const uint32_t v1 = pack_bf16x2(o[dt][2] * inv1, o[dt][3] * inv1);
-    uint32_t* o0 = reinterpret_cast<uint32_t*>(p.o + (static_cast<long long>(tok0) * p.nq + h0) * D + d);
-    uint32_t* o1 = reinterpret_cast<uint32_t*>(p.o + (static_cast<long long>(tok1) * p.nq + h1) * D + d);
-    if (p.check == nullptr) {
-      if (tok0 >= 0) *o0 = v0;
-      if (tok1 >= 0) *o1 = v1;
-    } else {
-      const int e0 = tok0 >= 0 ? bf16x2_diff(v0, *o0) : -1;
-      const int e1 = tok1 >= 0 ? bf16x2_diff(v1, *o1) : -1;
-      if (e0 >= 0) report_replay_mismatch(p.check, static_cast<unsigned long long>(tok0) * p.nq * D + h0 * D + d + e0);
-      if (e1 >= 0) report_replay_mismatch(p.check, static_cast<unsigned long long>(tok1) * p.nq * D + h1 * D + d + e1);
+      for (int c = 0; c < 16; ++c) {
+        const uint4 v = tok >= 0 ? src[c] : make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(qd + (c >> 3) * HALF_B + r * 128 + (((c & 7) ^ (r & 7)) << 4)) = v;
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&ctl->q_ready);
     }
-    const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v0));
-    const float2 f1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v1));
-    sq0 = fmaf(f0.x, f0.x, fmaf(f0.y, f0.y, sq0));
-    sq1 = fmaf(f1.x, f1.x, fmaf(f1.y, f1.y, sq1));
+    float m_use = -INFINITY, l = 0.f;
+    bool stop = ntiles == 0;
+    for (int j = 0; j < ntiles; ++j) {
+      const int st = j & 1;
+      const bool got = mbar_wait(&ctl->s_full[st], (j >> 1) & 1u, abort_flag);
+      if (named_bar_or(1, ROWS, !got)) {
+        *abort_flag = 1;
+        stop = true;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t sa = tmem + st * KT + lane_off;
+      // pass 1: masked maximum of the tile
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < KT / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld32(sa + c * 32, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int key = j * KT + c * 32 + i;
+          if (key <= pos) mx = fmaxf(mx, u32_as_f32(v[i]) * p.scale_log2);
+        }
+      }
+      float alpha = 1.f;
+      if (mx > -INFINITY && (m_use == -INFINITY || mx > m_use + RESCALE_LOG2)) {
+        alpha = m_use == -INFINITY ? 1.f : ex2(m_use - mx);
+        l *= alpha;
+        m_use = mx;
+      }
+      // pass 2: weights as bf16, their row sum
+      uint32_t pk[KT / 2];
+      float ls = 0.f;
+#pragma unroll
+      for (int c = 0; c < KT / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld32(sa + c * 32, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          const int key = j * KT + c * 32 + i;
+          const float p0 = (key <= pos && m_use > -INFINITY) ? ex2(u32_as_f32(v[i]) * p.scale_log2 - m_use) : 0.f;
+          const float p1 = (key + 1 <= pos && m_use > -INFINITY) ? ex2(u32_as_f32(v[i + 1]) * p.scale_log2 - m_use) : 0.f;
+          const uint32_t w = pack_bf16x2(p0, p1);
+          pk[(c * 32 + i) >> 1] = w;
+          const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w));
+          ls += f.x + f.y;
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&ctl->s_empty[st]);
+      l += ls;
+      if (j >= 1) {
+        const bool okp = mbar_wait(&ctl->pv_done, (j - 1) & 1u, abort_flag);
+        if (named_bar_or(1, ROWS, !okp)) {
+          *abort_flag = 1;
+          stop = true;
+          break;
+        }
+        tc_fence_after();
+        // rescale O (warp-collective TMEM access; rows that keep their maximum multiply by 1)
+        if (__any_sync(0xffffffffu, alpha != 1.f)) {
+          const uint32_t oa = tmem + 2 * KT + lane_off;
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t v[32];
+            tmem_ld32(oa + c * 32, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(u32_as_f32(v[i]) * alpha);
+            tmem_st32(oa + c * 32, v);
+          }
+          tmem_wait_st();
+        }
+      }
+      // P row -> shared memory (A operand of PV: keys are K, 128-byte swizzle, two key-halves)
+      uint8_t* pd = sm + OFF_P;
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        const uint4 v = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+        *reinterpret_cast<uint4*>(pd + (c >> 3) * HALF_B + r * 128 + (((c & 7) ^ (r & 7)) << 4)) = v;
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&ctl->p_full);
+    }
+    if (!stop && ntiles > 0) {
+      const bool okp = mbar_wait(&ctl->pv_done, (ntiles - 1) & 1u, abort_flag);
+      if (named_bar_or(1, ROWS, !okp)) {
+        *abort_flag = 1;
+        stop = true;
+      }
+    }
+    if (!stop && ntiles > 0) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const uint32_t oa = tmem + 2 * KT + lane_off;
+      __nv_bfloat16* orow = p.o + (static_cast<long long>(tok < 0 ? 0 : tok) * p.nq + head) * D;
+      float sq = 0.f;
+      int bad = -1;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld32(oa + c * 32, v);
+        tmem_wait_ld();
+        uint32_t w[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          w[i] = pack_bf16x2(u32_as_f32(v[2 * i]) * inv, u32_as_f32(v[2 * i + 1]) * inv);
+          const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+          sq = fmaf(f.x, f.x, fmaf(f.y, f.y, sq));
+        }
+        if (tok >= 0) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const uint4 nv = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+            if (p.check == nullptr) {
+              dst[i] = nv;
+            } else if (bad < 0) {
+              const uint4 ov = dst[i];
+              const uint32_t a[4] = {nv.x, nv.y, nv.z, nv.w}, b[4] = {ov.x, ov.y, ov.z, ov.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int dd = bf16x2_diff(a[e], b[e]);
+                if (bad < 0 && dd >= 0) bad = c * 32 + i * 8 + e * 2 + dd;
+              }
+            }
+          }
+        }
+      }
+      if (tok >= 0) {
+        if (p.check != nullptr && bad >= 0)
+          report_replay_mismatch(p.check, static_cast<unsigned long long>(tok) * p.nq * D + head * D + bad);
+        if (p.check == nullptr && p.row_sq != nullptr) atomicAdd(p.row_sq + tok, sq);
+      }
+    }
+    if (p.check != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && r == 0) atomicAdd(p.check + 2, 1ull);
   }
-  if (p.check != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) atomicAdd(p.check + 2, 1ull);
-  if (p.row_sq != nullptr && p.check == nullptr) {
-    sq0 += __shfl_xor_sync(0xffffffffu, sq0, 1);
-    sq0 += __shfl_xor_sync(0xffffffffu, sq0, 2);
-    sq1 += __shfl_xor_sync(0xffffffffu, sq1, 1);
-    sq1 += __shfl_xor_sync(0xffffffffu, sq1, 2);
-    if (t4 == 0) {
-      if (tok0 >= 0) atomicAdd(p.row_sq + tok0, sq0);
-      if (tok1 >= 0) atomicAdd(p.row_sq + tok1, sq1);
-    }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
   }
 }
 
@@ -615,8 +733,8 @@ static int launch_decode(const DecodeParams& p, const CUtensorMap& tm, dim3 grid
 
 extern "C" {
 
-int sdc_attn_prefill(const void* q, void* o, const void* cache, const int* block_table, int max_pages,
-                     const int* pos, const void* tiles, int ntiles, const int* row_idx, int nq, int nkv,
+int sdc_attn_prefill(const void* q, void* o, const void* cache, long long num_blocks, const int* block_table,
+                     int max_pages, const int* pos, const void* tiles, int ntiles, const int* row_idx, int nq, int nkv,
                      int head_dim, float scale, void* row_sq, void* check, void* stream) {
   if (ntiles <= 0) return 0;
   if (head_dim != D || nq % nkv || (ROWS % (nq / nkv))) return -1;
@@ -635,14 +753,16 @@ int sdc_attn_prefill(const void* q, void* o, const void* cache, const int* block
   p.row_sq = static_cast<float*>(row_sq);
   p.check = static_cast<unsigned long long*>(check);
   if (p.check != nullptr && row_idx == nullptr) return -1;
-  const int smem = ROWS * 256 + 4 * BN * 256;
+  CUtensorMap tm;
+  if (!make_map_bf16_sw128(&tm, cache, num_blocks * 2 * nkv * PAGE, D, D, 64, PAGE)) return -2;
   static bool attr = false;
   if (!attr) {
-    cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e = cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, pf::SMEM);
+    if (e != cudaSuccess) return static_cast<int>(e);
     attr = true;
   }
   dim3 grid(ntiles, nkv);
-  prefill_kernel<<<grid, WARPS * 32, smem, static_cast<cudaStream_t>(stream)>>>(p);
+  prefill_tc_kernel<<<grid, 256, pf::SMEM, static_cast<cudaStream_t>(stream)>>>(tm, p);
   return static_cast<int>(cudaGetLastError());
 }
 

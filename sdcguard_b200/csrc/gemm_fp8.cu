@@ -41,12 +41,18 @@ constexpr int BK = 128;               // fp8 elements (= bytes) per K block = on
 constexpr int A_BYTES = BM * BK;
 constexpr int B_BYTES = BNC * BK;
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;   // 34 KB, a multiple of 1 KB
-constexpr int STAGES = 6;
-constexpr int THREADS = 256;
-constexpr int STAGING_BYTES = 4 * 4096;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + STAGING_BYTES + 1024 + 512;
+constexpr int STAGES = 5;
+constexpr int EWG = 2;                // epilogue warpgroups: warpgroup g promotes columns [64 g, 64 g + 64)
+constexpr int HALF = BN / EWG;
+constexpr int THREADS = 128 + 128 * EWG;
+constexpr int STAGING_BYTES = 4 * EWG * 4096;  // per epilogue warp: 32 rows x 64 bf16
+constexpr int XCH_BYTES = 2 * 128 * 16;        // per tile parity: warpgroup 1's (P, S, Q, |.|) of each row
+constexpr int MAX_KBS = 128;                   // K <= 16384
+constexpr int SCL_BYTES = MAX_KBS * 13 * 4;    // the tile's weight scales and checksum part scales
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + STAGING_BYTES + XCH_BYTES + SCL_BYTES + 1024 + 512;
 constexpr int TMEM_COLS = 512;
-constexpr int SLOT_COLS = 256;
+constexpr int SLOT_COLS = BNC;                 // three accumulators of 144 columns
+constexpr int NSLOT = 3;
 constexpr float FP8_MAX = 448.f;
 
 struct Params8 {
@@ -70,8 +76,8 @@ struct Params8 {
 struct Ctl {
   uint64_t full[STAGES];
   uint64_t empty[STAGES];
-  uint64_t tfull[2];
-  uint64_t tempty[2];
+  uint64_t tfull[NSLOT];
+  uint64_t tempty[NSLOT];
   uint64_t drain;
   uint32_t tmem_base;
   int abort_flag;
@@ -155,7 +161,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* staging = smem + STAGES * STAGE_BYTES;
-  Ctl* ctl = reinterpret_cast<Ctl*>(staging + STAGING_BYTES);
+  float4* xch = reinterpret_cast<float4*>(staging + STAGING_BYTES);   // [2][128]
+  float* scl = reinterpret_cast<float*>(staging + STAGING_BYTES + XCH_BYTES);   // [kbs] sw, then [kbs][12] csc
+  Ctl* ctl = reinterpret_cast<Ctl*>(staging + STAGING_BYTES + XCH_BYTES + SCL_BYTES);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
@@ -163,9 +171,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&ctl->full[s], 1);
       mbar_init(&ctl->empty[s], 1);
     }
-    for (int a = 0; a < 2; ++a) {
+    for (int a = 0; a < NSLOT; ++a) {
       mbar_init(&ctl->tfull[a], 1);
-      mbar_init(&ctl->tempty[a], 128);
+      mbar_init(&ctl->tempty[a], 128 * EWG);
     }
     mbar_init(&ctl->drain, 1);
     ctl->abort_flag = 0;
@@ -233,8 +241,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t idesc = idesc_e4m3_f32(BM, BNC);
       for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
         for (int kb = 0; kb < p.kbs && ok; ++kb, ++g) {
-          const int slot = g & 1;
-          if (!mbar_wait(&ctl->tempty[slot], ((g >> 1) & 1u) ^ 1u, abort_flag)) {
+          const int slot = static_cast<int>(g % NSLOT);
+          if (!mbar_wait(&ctl->tempty[slot], ((g / NSLOT) & 1u) ^ 1u, abort_flag)) {
             ok = false;
             break;
           }
@@ -268,87 +276,91 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------ epilogue: promote, judge, store
-    const int q = warp & 3;
+    const int q = warp & 3;                // TMEM lane quarter
     const int ew = warp - 4;
+    const int gi = ew >> 2;                // warpgroup: columns [64 gi, 64 gi + 64); warpgroup 0 also checksums
+    const int et = threadIdx.x - 128;
     const int row_in_tile = q * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
     unsigned long long* st = p.state + static_cast<long long>(p.slot) * 4;
     uint8_t* stg = staging + ew * 4096;
     unsigned g = 0;
+    int it = 0;
     bool stop = false;
-    for (int tile = blockIdx.x; tile < p.total_tiles && !stop; tile += gridDim.x) {
+    for (int tile = blockIdx.x; tile < p.total_tiles && !stop; tile += gridDim.x, ++it) {
       int mt, nt;
       tile_coords8(p, tile, mt, nt);
       const int row = mt * BM + row_in_tile;
       const bool valid = row < p.M;
-      float acc[BN];
+      float acc[HALF];
       float cs[12];
 #pragma unroll
-      for (int j = 0; j < BN; ++j) acc[j] = 0.f;
+      for (int j = 0; j < HALF; ++j) acc[j] = 0.f;
 #pragma unroll
       for (int j = 0; j < 12; ++j) cs[j] = 0.f;
+      // the tile's weight scales and checksum part scales -> shared memory (every epilogue thread finished the
+      // previous tile: it passed the previous tile's exchange barrier)
+      for (int i = et; i < p.kbs * 13; i += 128 * EWG)
+        scl[i] = i < p.kbs ? __ldg(p.sw + static_cast<long long>(nt) * p.kbs + i)
+                           : __ldg(p.csc + static_cast<long long>(nt) * p.kbs * 12 + (i - p.kbs));
+      named_bar_sync(3, 128 * EWG);
+      const float* sap = p.sa + static_cast<long long>(valid ? row : 0) * p.kbs;
+      float sa_n = __ldg(sap);              // the next K block's row scale is loaded before the wait
       for (int kb = 0; kb < p.kbs; ++kb, ++g) {
-        const int slot = g & 1;
-        const bool got = mbar_wait(&ctl->tfull[slot], (g >> 1) & 1u, abort_flag);
-        if (named_bar_or(1, 128, !got)) {
+        const float s = (valid ? sa_n : 0.f) * scl[kb];
+        if (kb + 1 < p.kbs) sa_n = __ldg(sap + kb + 1);
+        const int slot = static_cast<int>(g % NSLOT);
+        const bool got = mbar_wait(&ctl->tfull[slot], (g / NSLOT) & 1u, abort_flag);
+        if (named_bar_or(1, 128 * EWG, !got)) {
           if (!got) record_error(p.err, ERR_TIMEOUT_EPILOGUE);
           *abort_flag = 1;
           stop = true;
           break;
         }
         tc_fence_after();
-        const float s = (valid ? __ldg(p.sa + static_cast<long long>(row) * p.kbs + kb) : 0.f) *
-                        __ldg(p.sw + static_cast<long long>(nt) * p.kbs + kb);
         const uint32_t ta = tmem_base + static_cast<uint32_t>(slot * SLOT_COLS) + lane_off;
+        if (gi == 0) {
+          uint32_t c16[16];
+          tmem_ld8(ta + BN, *reinterpret_cast<uint32_t(*)[8]>(&c16[0]));
+          tmem_ld8(ta + BN + 8, *reinterpret_cast<uint32_t(*)[8]>(&c16[8]));
+          tmem_wait_ld();
+          const float* cp = scl + p.kbs + kb * 12;
 #pragma unroll
-        for (int h = 0; h < 4; ++h) {
+          for (int j = 0; j < 12; ++j) cs[j] = fmaf(u32_as_f32(c16[j]), s * cp[j], cs[j]);
+        }
+#pragma unroll
+        for (int h = 0; h < HALF / 32; ++h) {
           uint32_t r[32];
-          tmem_ld32(ta + h * 32, r);
+          tmem_ld32(ta + gi * HALF + h * 32, r);
           tmem_wait_ld();
 #pragma unroll
           for (int j = 0; j < 32; ++j) acc[h * 32 + j] = fmaf(u32_as_f32(r[j]), s, acc[h * 32 + j]);
-        }
-        {
-          uint32_t r[16];
-          tmem_ld8(ta + BN, *reinterpret_cast<uint32_t(*)[8]>(&r[0]));
-          tmem_ld8(ta + BN + 8, *reinterpret_cast<uint32_t(*)[8]>(&r[8]));
-          tmem_wait_ld();
-          const float* cp = p.csc + (static_cast<long long>(nt) * p.kbs + kb) * 12;
-#pragma unroll
-          for (int j = 0; j < 12; ++j) cs[j] = fmaf(u32_as_f32(r[j]), s * __ldg(cp + j), cs[j]);
         }
         tc_fence_before();
         mbar_arrive(&ctl->tempty[slot]);
       }
       if (stop) break;
-      // ---- the tile's 128 columns of this row are final: injected fault, block sums, judge, store
-      const int col0 = nt * BN;
+      // ---- this row's 64 columns are final: injected fault, partial block sums, store
+      const int c0 = nt * BN + gi * HALF;
       if (INJ && row == p.inj_row) {
 #pragma unroll
-        for (int j = 0; j < BN; ++j)
-          if (col0 + j == p.inj_col) acc[j] = __uint_as_float(__float_as_uint(acc[j]) ^ p.inj_xor);
+        for (int j = 0; j < HALF; ++j)
+          if (c0 + j == p.inj_col) acc[j] = __uint_as_float(__float_as_uint(acc[j]) ^ p.inj_xor);
       }
       float P = 0.f, S = 0.f, Q = 0.f, Aab = 0.f;
 #pragma unroll
-      for (int j = 0; j < BN; ++j) {
+      for (int j = 0; j < HALF; ++j) {
+        const int col = gi * HALF + j;         // column within the block
         const float x = acc[j];
         P += x;
-        S += ((p.sgn[j >> 5] >> (j & 31)) & 1u) ? -x : x;
+        S += ((p.sgn[col >> 5] >> (col & 31)) & 1u) ? -x : x;
         Q = fmaf(x, x, Q);
         Aab += fabsf(x);
       }
-      unsigned long long k0 = 0ull, k1 = 0ull;
-      int unj = 0;
-      if (valid) {
-        const float ep = ((cs[0] + cs[1]) + (cs[2] + cs[3])) + (cs[4] + cs[5]);
-        const float es = ((cs[6] + cs[7]) + (cs[8] + cs[9])) + (cs[10] + cs[11]);
-        judge8(p, row, nt, P, S, Q, Aab, ep, es, k0, k1, unj);
-      }
-#pragma unroll
-      for (int h = 0; h < BN / 64; ++h) {
+      {
         uint32_t packed[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) packed[j] = pack_bf16x2(acc[h * 64 + 2 * j], acc[h * 64 + 2 * j + 1]);
+        for (int j = 0; j < 32; ++j) packed[j] = pack_bf16x2(acc[2 * j], acc[2 * j + 1]);
         if (lane == 0) bulk_wait_read0();
         __syncwarp();
         uint8_t* myrow = stg + lane * 128;
@@ -360,20 +372,39 @@ __global__ void __launch_bounds__(THREADS, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          tma_store_2d(&tmC, stg, col0 + h * 64, mt * BM + q * 32);
+          tma_store_2d(&tmC, stg, c0, mt * BM + q * 32);
           bulk_commit();
         }
       }
-      k0 = warp_max_u64(k0);
-      k1 = warp_max_u64(k1);
+      // ---- warpgroup 1 hands its half-block sums to warpgroup 0, which judges the block
+      float4* xb = xch + (it & 1) * 128;
+      if (gi == 1) xb[row_in_tile] = make_float4(P, S, Q, Aab);
+      named_bar_sync(2, 128 * EWG);
+      if (gi == 0) {
+        const float4 o = xb[row_in_tile];
+        P += o.x;
+        S += o.y;
+        Q += o.z;
+        Aab += o.w;
+        unsigned long long k0 = 0ull, k1 = 0ull;
+        int unj = 0;
+        if (valid) {
+          const float ep = ((cs[0] + cs[1]) + (cs[2] + cs[3])) + (cs[4] + cs[5]);
+          const float es = ((cs[6] + cs[7]) + (cs[8] + cs[9])) + (cs[10] + cs[11]);
+          judge8(p, row, nt, P, S, Q, Aab, ep, es, k0, k1, unj);
+        }
+        k0 = warp_max_u64(k0);
+        k1 = warp_max_u64(k1);
 #pragma unroll
-      for (int m = 16; m > 0; m >>= 1) unj += __shfl_xor_sync(0xffffffffu, unj, m);
-      if (lane == 0) {
-        if (k0 > ld_relaxed_u64(st + 0)) atomicMax(st + 0, k0);
-        if (k1 > ld_relaxed_u64(st + 1)) atomicMax(st + 1, k1);
-        if (unj) atomicAdd(st + 3, static_cast<unsigned long long>(unj));
-        if (tile == 0 && q == 0) atomicAdd(st + 2, 1ull);      // one count per launch
+        for (int m = 16; m > 0; m >>= 1) unj += __shfl_xor_sync(0xffffffffu, unj, m);
+        if (lane == 0) {
+          if (k0 > ld_relaxed_u64(st + 0)) atomicMax(st + 0, k0);
+          if (k1 > ld_relaxed_u64(st + 1)) atomicMax(st + 1, k1);
+          if (unj) atomicAdd(st + 3, static_cast<unsigned long long>(unj));
+          if (tile == 0 && q == 0) atomicAdd(st + 2, 1ull);      // one count per launch
+        }
       }
+      (void)et;
     }
   }
 
@@ -387,23 +418,24 @@ __global__ void __launch_bounds__(THREADS, 1)
 }
 
 // ------------------------------------------------------------------------------------------- quantizer
-// One warp per row: for every 128-column block, amax -> s = the smallest power of two with amax / s <= 448,
-// q = E4M3(x / s) (saturating), and ||dequantized row||^2. In check mode (check != null, rows = sampled rows)
-// the codes and scales are recomputed and compared with the stored ones instead of written.
+// One CTA of 8 warps per row; warp w takes the 128-column blocks w, w + 8, ...: amax -> s = the smallest power of
+// two with amax / s <= 448, q = E4M3(x / s) (saturating); ||dequantized row||^2 is reduced in shared memory. In check
+// mode (check != null, rows = sampled rows) the codes and scales are recomputed and compared with the stored ones
+// instead of written.
 __global__ void __launch_bounds__(256) act_quant_kernel(const __nv_bfloat16* __restrict__ x, long long ldx, int M, int K,
                                                         uint8_t* __restrict__ xq, float* __restrict__ sa,
                                                         float* __restrict__ row_sq, const int* rows, int nrows,
                                                         unsigned long long* check) {
-  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
+  __shared__ float red[8];
+  __shared__ int sbad;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (check != nullptr && blockIdx.x == 0 && threadIdx.x == 0) atomicAdd(check + 2, 1ull);
-  const int n = rows ? nrows : M;
-  if (w >= n) return;
-  const int row = rows ? rows[w] : w;
+  const int row = rows ? rows[blockIdx.x] : blockIdx.x;
   const int kbs = K / 128;
+  if (threadIdx.x == 0) sbad = 0x7fffffff;
+  __syncthreads();
   float sq = 0.f;
-  int bad = -1;
-  for (int kb = 0; kb < kbs; ++kb) {
+  for (int kb = warp; kb < kbs; kb += 8) {
     const int c = kb * 128 + lane * 4;
     const uint2 raw = *reinterpret_cast<const uint2*>(x + static_cast<long long>(row) * ldx + c);
     const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
@@ -436,18 +468,22 @@ __global__ void __launch_bounds__(256) act_quant_kernel(const __nv_bfloat16* __r
       if (lane == 0) *sp = s;
     } else {
       const bool diff = *qp != codes || (lane == 0 && !(*sp == s));
-      if (diff && bad < 0) bad = c;
+      const unsigned m = __ballot_sync(0xffffffffu, diff);
+      if (lane == 0 && m) atomicMin(&sbad, kb * 128 + (__ffs(m) - 1) * 4);
     }
   }
 #pragma unroll
   for (int m = 16; m > 0; m >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, m);
-  if (check == nullptr) {
-    if (lane == 0 && row_sq != nullptr) row_sq[row] = sq;
-  } else {
-    int b = bad < 0 ? 0x7fffffff : bad;
-#pragma unroll
-    for (int m = 16; m > 0; m >>= 1) b = min(b, __shfl_xor_sync(0xffffffffu, b, m));
-    if (lane == 0 && b != 0x7fffffff) report_replay_mismatch(check, static_cast<unsigned long long>(row) * K + b);
+  if (lane == 0) red[warp] = sq;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (check == nullptr) {
+      float t = 0.f;
+      for (int w = 0; w < 8; ++w) t += red[w];
+      if (row_sq != nullptr) row_sq[row] = t;
+    } else if (sbad != 0x7fffffff) {
+      report_replay_mismatch(check, static_cast<unsigned long long>(row) * K + sbad);
+    }
   }
 }
 
@@ -479,7 +515,7 @@ int sdc_gemm_fp8(const void* Aq, const float* sa, const void* Wq, const void* Wc
                  float prod_coef, float out_coef, float abs_floor, float bound_coef, int* err, int inj_row,
                  int inj_col, unsigned inj_xor, void* stream) {
   if (M <= 0) return 0;
-  if (N <= 0 || K <= 0 || N % BN || K % BK || ldc % 8) return -1;
+  if (N <= 0 || K <= 0 || N % BN || K % BK || K / BK > MAX_KBS || ldc % 8) return -1;
   Params8 p;
   std::memset(&p, 0, sizeof(p));
   p.M = M;
@@ -535,7 +571,8 @@ int sdc_fp8_quant_act(const void* x, long long ldx, int M, int K, void* xq, floa
   if (K % 128 || ldx % 4) return -1;
   const int n = rows ? nrows : M;
   if (n <= 0) return 0;
-  act_quant_kernel<<<(n * 32 + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+  auto st = static_cast<cudaStream_t>(stream);
+  act_quant_kernel<<<static_cast<unsigned>(n), 256, 0, st>>>(
       static_cast<const __nv_bfloat16*>(x), ldx, M, K, static_cast<uint8_t*>(xq), sa, row_sq, rows, nrows,
       static_cast<unsigned long long*>(check));
   return static_cast<int>(cudaGetLastError());

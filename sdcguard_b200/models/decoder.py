@@ -99,8 +99,16 @@ class CheckedDecoder:
     """The model plus its check state. Slots of the state table name each checked op (`state.names`)."""
 
     def __init__(self, cfg: DecoderConfig, device="cuda", checked: bool = True, seed: int = 0,
-                 weights: Optional[dict] = None, tp_rank: int = 0, tp_size: int = 1, moe_layers: Optional[list] = None):
-        """moe_layers: one `models.moe.MoELayer` per layer in place of the dense MLP (expert-parallel models)."""
+                 weights: Optional[dict] = None, tp_rank: int = 0, tp_size: int = 1, moe_layers: Optional[list] = None,
+                 precision: str = "bf16"):
+        """moe_layers: one `models.moe.MoELayer` per layer in place of the dense MLP (expert-parallel models).
+        precision "fp8": the four projections of every layer run on the block-scaled fp8 checked GEMM (activations
+        quantized per call with 1 x 128 scales, replay-checked on the sampled rows); the LM head stays bf16."""
+        if precision not in ("bf16", "fp8"):
+            raise ValueError("precision must be bf16 or fp8")
+        if precision == "fp8" and not checked:
+            raise ValueError("the fp8 path is the checked fp8 GEMM")
+        self.precision = precision
         self.cfg = cfg
         self.moe = moe_layers
         self.device = torch.device(device)
@@ -130,10 +138,18 @@ class CheckedDecoder:
         self.rope = layers.rope_table(min(cfg.max_position, 16384), d, cfg.rope_theta, cfg.rope_scaling, device=dev)
         self.state = gemm.StateTable(dev, 16 * cfg.layers + 8)
         self.slot: dict[str, int] = {}
+        if precision == "fp8":
+            from ..ops.fp8 import Fp8Linears
+            self.fp8 = Fp8Linears(dev)
         if checked:
             for i, lw in enumerate(self.layers):
                 for name in ("qkv", "o", "gate_up", "down"):
                     if getattr(lw, name) is None:
+                        continue
+                    if precision == "fp8":
+                        fw = self.fp8.add(f"L{i}.{name}", getattr(lw, name))
+                        self.slot[f"L{i}.{name}"] = self.state.add(f"layers.{i}.{name} (ABFT fp8 GEMM)", fw.nb)
+                        self.slot[f"L{i}.{name}.q"] = self.state.add(f"layers.{i}.{name}.quant (replay)", 1)
                         continue
                     cw = gemm.CheckedWeight(getattr(lw, name))
                     lw.cw[name] = cw
@@ -177,6 +193,8 @@ class CheckedDecoder:
             gu=torch.empty(T if not self.moe else 1, 2 * self.inter, dtype=bf, device=dev),
             act=torch.empty(T if not self.moe else 1, self.inter, dtype=bf, device=dev),
         )
+        if self.precision == "fp8":
+            self.fp8.reserve(T, max(H, nq * D, self.inter))
         if self.checked:
             gemm.reserve_workspace(dev, T, max(2 * self.inter if not self.moe else 0, (nq + 2 * nkv) * D, H))
             gemm.reserve_workspace(dev, min(T, 1024), cfg.vocab)
@@ -195,7 +213,10 @@ class CheckedDecoder:
         return self._bufs["dscratch"]
 
     # ---------------------------------------------------------------- ops
-    def _linear(self, x, w, cw, name, out, row_sq):
+    def _linear(self, x, w, cw, name, out, row_sq, sample=None):
+        if self.precision == "fp8":
+            return self.fp8.linear(name, x, self.state.state, self.slot[name], out,
+                                   qcheck=self.state.state[self.slot[name + ".q"]], sample=sample)
         if not self.checked:
             return torch.matmul(x, w.t(), out=out)
         return gemm.checked_linear(x, cw, self.state.state, self.slot[name], row_sq=row_sq, out=out)
@@ -224,7 +245,7 @@ class CheckedDecoder:
                 layers.add_rmsnorm(x, lw.ln1, cfg.rms_eps, residual=resid, resid_out=resid, out=y, row_sq=rs)
             if chk:
                 layers.add_rmsnorm(resid, lw.ln1, cfg.rms_eps, out=y, rows=S, check=self._st(f"L{i}.norm1"))
-            self._linear(y, lw.qkv, lw.cw.get("qkv"), f"L{i}.qkv", qkv, rs)
+            self._linear(y, lw.qkv, lw.cw.get("qkv"), f"L{i}.qkv", qkv, rs, S)
             layers.qk_norm_rope_kv(qkv, nq, nkv, meta.pos, meta.slots, lw.q_norm, lw.k_norm, cfg.rms_eps, self.rope,
                                    q, lc)
             if chk:
@@ -243,18 +264,18 @@ class CheckedDecoder:
                 if chk:
                     attention.decode(q, lc, meta.block_table, meta.seq_req, meta.ctx, nq, nkv, meta.max_ctx,
                                      out=att, seq_idx=S, scratch=scratch, check=self._st(f"L{i}.attn"))
-            self._linear(att.view(T, nq * D), lw.o, lw.cw.get("o"), f"L{i}.o", a, ors)
+            self._linear(att.view(T, nq * D), lw.o, lw.cw.get("o"), f"L{i}.o", a, ors, S)
             layers.add_rmsnorm(a, lw.ln2, cfg.rms_eps, residual=resid, resid_out=resid, out=y, row_sq=rs)
             if chk:
                 layers.add_rmsnorm(resid, lw.ln2, cfg.rms_eps, out=y, rows=S, check=self._st(f"L{i}.norm2"))
             if self.moe:
                 x = self.moe[i].forward(y, S if chk else None)
                 continue
-            self._linear(y, lw.gate_up, lw.cw.get("gate_up"), f"L{i}.gate_up", gu, rs)
+            self._linear(y, lw.gate_up, lw.cw.get("gate_up"), f"L{i}.gate_up", gu, rs, S)
             layers.silu_mul(gu, out=act, row_sq=rs)
             if chk:
                 layers.silu_mul(gu, out=act, rows=S, check=self._st(f"L{i}.act"))
-            self._linear(act, lw.down, lw.cw.get("down"), f"L{i}.down", x, rs)
+            self._linear(act, lw.down, lw.cw.get("down"), f"L{i}.down", x, rs, S)
         # final norm on the rows that produce tokens, then the LM head
         L = meta.logits_rows.shape[0]
         xs = x.index_select(0, meta.logits_rows)

@@ -35,7 +35,11 @@ from .decoder import DecoderConfig, LayerWeights, StepMeta
 
 class TPDecoder:
     def __init__(self, cfg: DecoderConfig, comm: Optional[TPComm], rank: int, world: int, device, checked: bool = True,
-                 collective: str = "own", max_rows: int = 8192, seed: int = 0):
+                 collective: str = "own", max_rows: int = 8192, seed: int = 0, precision: str = "bf16"):
+        """precision "fp8": the four projections run on the block-scaled fp8 checked GEMM (see models.decoder)."""
+        if precision not in ("bf16", "fp8") or (precision == "fp8" and not checked):
+            raise ValueError("precision must be bf16, or fp8 with checked=True")
+        self.precision = precision
         if cfg.heads % world or cfg.intermediate % world or cfg.vocab % world:
             raise ValueError("heads, intermediate size and vocabulary must divide by the TP size")
         self.cfg, self.rank, self.world = cfg, rank, world
@@ -76,9 +80,17 @@ class TPDecoder:
         self.rope = layers.rope_table(min(cfg.max_position, 16384), d, cfg.rope_theta, cfg.rope_scaling, device=dev)
         self.state = gemm.StateTable(dev, 16 * cfg.layers + 16)
         self.slot: dict[str, int] = {}
+        if precision == "fp8":
+            from ..ops.fp8 import Fp8Linears
+            self.fp8 = Fp8Linears(dev)
         if checked:
             for i, lw in enumerate(self.layers):
                 for name in ("qkv", "o", "gate_up", "down"):
+                    if precision == "fp8":
+                        fw = self.fp8.add(f"L{i}.{name}", getattr(lw, name))
+                        self.slot[f"L{i}.{name}"] = self.state.add(f"layers.{i}.{name} (ABFT fp8 GEMM, tp{rank})", fw.nb)
+                        self.slot[f"L{i}.{name}.q"] = self.state.add(f"layers.{i}.{name}.quant (replay, tp{rank})", 1)
+                        continue
                     cw = gemm.CheckedWeight(getattr(lw, name))
                     lw.cw[name] = cw
                     self.slot[f"L{i}.{name}"] = self.state.add(f"layers.{i}.{name} (ABFT GEMM, tp{rank})", cw.nb)
@@ -121,6 +133,8 @@ class TPDecoder:
                           xs=torch.empty(R, H, dtype=bf, device=dev), resid=torch.empty(R, H, dtype=bf, device=dev),
                           ys=torch.empty(R, H, dtype=bf, device=dev), rss=torch.empty(R, dtype=torch.float32, device=dev),
                           part=torch.empty(T, H, dtype=bf, device=dev))
+        if self.precision == "fp8":
+            self.fp8.reserve(T, max(H, self.nq * D, self.inter))
         if self.checked:
             gemm.reserve_workspace(dev, T, max(2 * self.inter, H, (self.nq + 2 * self.nkv) * D))
             gemm.reserve_workspace(dev, min(T, 1024), self.vocab_l)
@@ -137,7 +151,14 @@ class TPDecoder:
         return self.state.read(reset=reset)
 
     # ------------------------------------------------------------------ pieces
-    def _linear(self, x, w, cw, name, out, row_sq, seal=None):
+    def _linear(self, x, w, cw, name, out, row_sq, seal=None, sample=None):
+        if self.precision == "fp8":
+            y = self.fp8.linear(name, x, self.state.state, self.slot[name], out,
+                                qcheck=self.state.state[self.slot[name + ".q"]], sample=sample)
+            if seal is not None:
+                from ..parallel.tp import seal_rows
+                seal_rows(y, seal)
+            return y
         if not self.checked:
             return torch.matmul(x, w.t(), out=out)
         return gemm.checked_linear(x, cw, self.state.state, self.slot[name], row_sq=row_sq, out=out, seal=seal)
@@ -155,11 +176,11 @@ class TPDecoder:
                            row_sq=B["rss"][:R])
         return dst
 
-    def _rowpar(self, x, w, cw, name, T, R, row_sq, out_shard):
+    def _rowpar(self, x, w, cw, name, T, R, row_sq, out_shard, sample=None):
         """Row-parallel GEMM + reduce-scatter into out_shard (R, H)."""
         if self.collective == "own":
             self._linear(x, w, cw, name, self.comm.partial(T), row_sq,
-                         seal=self.comm.partial_seal(T) if self.checked else None)
+                         seal=self.comm.partial_seal(T) if self.checked else None, sample=sample)
             if not self.checked:
                 from ..parallel.tp import seal_rows
                 seal_rows(self.comm.partial(T), self.comm.partial_seal(T))
@@ -203,8 +224,8 @@ class TPDecoder:
             if chk:
                 self._norm_replay(ys, lw.ln1, R, S_loc, f"L{i}.norm1")
             self._ag(ys, R, yfull)
-            yrs = gemm.row_sqnorm(yfull, out=rs) if self.checked else None
-            self._linear(yfull, lw.qkv, lw.cw.get("qkv"), f"L{i}.qkv", qkv, yrs)
+            yrs = gemm.row_sqnorm(yfull, out=rs) if self.checked and self.precision == "bf16" else None
+            self._linear(yfull, lw.qkv, lw.cw.get("qkv"), f"L{i}.qkv", qkv, yrs, sample=S)
             layers.qk_norm_rope_kv(qkv, nq, nkv, meta.pos, meta.slots, lw.q_norm, lw.k_norm, cfg.rms_eps, self.rope,
                                    q, lc)
             if chk:
@@ -225,17 +246,17 @@ class TPDecoder:
                 if chk:
                     attention.decode(q[:T0], lc, meta.block_table, meta.seq_req, meta.ctx, nq, nkv, meta.max_ctx,
                                      out=att[:T0], seq_idx=S, scratch=scratch, check=self._st(f"L{i}.attn"))
-            self._rowpar(att.view(T, nq * D), lw.o, lw.cw.get("o"), f"L{i}.o", T, R, ors, xs)
+            self._rowpar(att.view(T, nq * D), lw.o, lw.cw.get("o"), f"L{i}.o", T, R, ors, xs, sample=S)
             ys = self._norm_into_shard(xs, lw.ln2, B["resid"][:R], R)
             if chk:
                 self._norm_replay(ys, lw.ln2, R, S_loc, f"L{i}.norm2")
             self._ag(ys, R, yfull)
-            yrs = gemm.row_sqnorm(yfull, out=rs) if self.checked else None
-            self._linear(yfull, lw.gate_up, lw.cw.get("gate_up"), f"L{i}.gate_up", gu, yrs)
+            yrs = gemm.row_sqnorm(yfull, out=rs) if self.checked and self.precision == "bf16" else None
+            self._linear(yfull, lw.gate_up, lw.cw.get("gate_up"), f"L{i}.gate_up", gu, yrs, sample=S)
             layers.silu_mul(gu, out=act, row_sq=rs)
             if chk:
                 layers.silu_mul(gu, out=act, rows=S, check=self._st(f"L{i}.act"))
-            self._rowpar(act, lw.down, lw.cw.get("down"), f"L{i}.down", T, R, rs, xs)
+            self._rowpar(act, lw.down, lw.cw.get("down"), f"L{i}.down", T, R, rs, xs, sample=S)
         ys = self._norm_into_shard(xs, self.final_ln, B["resid"][:R], R)
         if chk:
             self._norm_replay(ys, self.final_ln, R, S_loc, "final_norm")

@@ -58,7 +58,7 @@ def prefill(q: torch.Tensor, cache: torch.Tensor, block_table: torch.Tensor, pos
         out = torch.empty_like(q)
     scale = 1.0 / math.sqrt(128) if scale is None else scale
     _native.check(_native.lib().sdc_attn_prefill(
-        q.data_ptr(), out.data_ptr(), cache.data_ptr(), block_table.data_ptr(), block_table.shape[1],
+        q.data_ptr(), out.data_ptr(), cache.data_ptr(), cache.shape[0], block_table.data_ptr(), block_table.shape[1],
         pos.data_ptr(), tiles.data_ptr(), tiles.shape[0], None if row_idx is None else row_idx.data_ptr(), nq, nkv,
         128, float(scale), None if row_sq is None else row_sq.data_ptr(), None if check is None else check.data_ptr(),
         _s(q)), "attention prefill")

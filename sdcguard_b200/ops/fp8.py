@@ -126,3 +126,42 @@ def checked_linear_fp8(xa: Fp8Act, fw: Fp8Weight, state: torch.Tensor, slot: int
         float(abft.ABS_FLOOR), float(math.sqrt(k)), error_word(dev).data_ptr(), ir, ic, ix, _stream_ptr(dev)),
         "fp8 checked GEMM")
     return out
+
+
+class Fp8Linears:
+    """The fp8 projections of a model: quantized weights by name, one activation scratch sized for the largest
+    call (views keep their data pointers, so CUDA graphs can capture the calls), and the quantizer replay check."""
+
+    def __init__(self, device):
+        self.device = torch.device(device)
+        self.weights: dict[str, Fp8Weight] = {}
+        self.cap = (0, 0)
+        self._q = self._sa = self._rs = None
+
+    def add(self, name: str, weight: torch.Tensor) -> Fp8Weight:
+        fw = Fp8Weight(weight)
+        self.weights[name] = fw
+        return fw
+
+    def reserve(self, rows: int, k: int) -> None:
+        if rows * k <= self.cap[0] * self.cap[1] and rows <= self.cap[0]:
+            return
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("fp8 activation scratch too small inside CUDA graph capture")
+        rows, k = max(rows, self.cap[0]), max(k, self.cap[1])
+        self._q = torch.empty(rows * k, dtype=torch.float8_e4m3fn, device=self.device)
+        self._sa = torch.empty(rows * (k // 128), dtype=torch.float32, device=self.device)
+        self._rs = torch.empty(rows, dtype=torch.float32, device=self.device)
+        self.cap = (rows, k)
+
+    def act(self, m: int, k: int) -> Fp8Act:
+        self.reserve(m, k)
+        return Fp8Act(self._q[: m * k].view(m, k), self._sa[: m * (k // 128)].view(m, k // 128), self._rs[:m])
+
+    def linear(self, name: str, x: torch.Tensor, state: torch.Tensor, slot: int, out: torch.Tensor,
+               qcheck: Optional[torch.Tensor] = None, sample: Optional[torch.Tensor] = None) -> torch.Tensor:
+        m, k = x.shape
+        xa = quantize_act(x, out=self.act(m, k))
+        if qcheck is not None and sample is not None and sample.numel():
+            quantize_act(x, out=xa, rows=sample, check=qcheck)
+        return checked_linear_fp8(xa, self.weights[name], state, slot, out=out)

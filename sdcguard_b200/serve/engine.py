@@ -54,10 +54,10 @@ class LLMEngine:
     def __init__(self, cfg: DecoderConfig, device="cuda", checked: bool = True, num_blocks: Optional[int] = None,
                  max_prefill_tokens: int = 16384, max_num_seqs: int = 256, sample_every: int = 64,
                  cuda_graph: bool = True, seed: int = 0, kv_fraction: float = 0.6, model: Optional[CheckedDecoder] = None,
-                 max_model_len: int = 4096):
+                 max_model_len: int = 4096, precision: str = "bf16"):
         self.cfg = cfg
         self.device = torch.device(device)
-        self.model = model or CheckedDecoder(cfg, self.device, checked=checked, seed=seed)
+        self.model = model or CheckedDecoder(cfg, self.device, checked=checked, seed=seed, precision=precision)
         self.checked = self.model.checked
         self.max_prefill_tokens = max_prefill_tokens
         self.max_num_seqs = max_num_seqs

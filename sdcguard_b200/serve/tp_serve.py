@@ -79,7 +79,8 @@ def run(args) -> dict:
     for arm in args.arms.split(","):
         checked = arm == "checked"
         model = TPDecoder(cfg, comm if checked else None, rank, world, dev, checked=checked,
-                          collective="own" if checked else "nccl", max_rows=max_rows, seed=args.seed)
+                          collective="own" if checked else "nccl", max_rows=max_rows, seed=args.seed,
+                          precision=args.precision if checked else "bf16")
         eng = LLMEngine(cfg, dev, model=model, num_blocks=pages, max_prefill_tokens=args.max_prefill_tokens,
                         max_num_seqs=args.batch, max_model_len=args.prompt + args.new_tokens)
         box = {}
@@ -133,7 +134,8 @@ def run(args) -> dict:
     if "checked" in res and "unchecked" in res:
         res["overhead_pct"] = round(100 * (res["checked"]["dev_ms"] / res["unchecked"]["dev_ms"] - 1), 2)
     comm.close()
-    res["config"] = {"model": cfg.name, "tp": world, "batch": args.batch, "prompt": args.prompt,
+    res["config"] = {"model": cfg.name, "tp": world, "precision": args.precision, "batch": args.batch,
+                     "prompt": args.prompt,
                      "new_tokens": args.new_tokens, "steps": args.steps, "warmup": args.warmup}
     return res
 
@@ -149,6 +151,8 @@ def main(argv=None) -> int:
     ap.add_argument("--max-prefill-tokens", type=int, default=16384)
     ap.add_argument("--arms", default="checked,unchecked")
     ap.add_argument("--inject", action="store_true")
+    ap.add_argument("--precision", default="bf16", choices=["bf16", "fp8"],
+                    help="checked arm's projections: bf16, or block-scaled fp8 (the unchecked arm stays bf16)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--pg-timeout", type=int, default=300)
     a = ap.parse_args(argv)

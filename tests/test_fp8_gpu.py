@@ -78,3 +78,21 @@ def test_fp8_gemm_injected_flip_is_located(bit):
     checked_linear_fp8(xa, fw, st.state, slot, inject=(row, col, 1 << bit))
     d = st.read()[0]
     assert d["z"] > abft.Z_ALARM and d["row"] == row and d["block"] == col // 128, d
+
+
+def test_fp8_decoder_serves_clean_and_close_to_bf16():
+    """The decoder with fp8 projections: same greedy tokens as bf16 on most steps, checks run, no alarm."""
+    from sdcguard_b200.models.decoder import TINY
+    from sdcguard_b200.serve.engine import LLMEngine
+    prompts = torch.randint(0, TINY.vocab, (4, 96), generator=torch.Generator().manual_seed(0)).pin_memory()
+    outs = {}
+    for prec in ("bf16", "fp8"):
+        eng = LLMEngine(TINY, device="cuda:0", checked=True, num_blocks=64, max_prefill_tokens=512, max_num_seqs=8,
+                        sample_every=2, max_model_len=512, precision=prec)
+        outs[prec] = eng.generate(prompts, [96, 80, 64, 33], 4)
+        ev = eng.guard.poll()
+        cov = eng.guard.coverage_report()
+        assert not ev and cov["checks"] > 0 and cov["unjudged"] == 0, (prec, ev, cov)
+        if prec == "fp8":
+            assert any("fp8" in n for n in eng.model.state.names) and any("quant" in n for n in eng.model.state.names)
+    assert (outs["bf16"] == outs["fp8"]).float().mean().item() >= 0.5
