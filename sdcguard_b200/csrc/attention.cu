@@ -91,11 +91,14 @@ struct Ctl {
   int maxpos;
   int tok[ROWS];
   int pos[ROWS];
+  float xm[2][2][ROWS];                   // [tile parity][warpgroup][row] partial maxima of a tile
+  float xl[2][ROWS];                      // [warpgroup][row] partial row sums at the end
 };
 constexpr int SMEM = OFF_CTL + static_cast<int>(sizeof(Ctl)) + 1024;
+constexpr int SOFT = 2 * ROWS;            // softmax threads: warpgroup g takes keys / dims [64 g, 64 g + 64)
 }  // namespace pf
 
-__global__ void __launch_bounds__(256, 1) prefill_tc_kernel(const __grid_constant__ CUtensorMap tm,
+__global__ void __launch_bounds__(128 + 2 * ROWS, 1) prefill_tc_kernel(const __grid_constant__ CUtensorMap tm,
                                                             const PrefillParams p) {
   using namespace pf;
   extern __shared__ uint8_t pf_raw[];
@@ -112,11 +115,11 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(const __grid_constan
       mbar_init(&ctl->v_full[i], 1);
       mbar_init(&ctl->kv_empty[i], 1);
       mbar_init(&ctl->s_full[i], 1);
-      mbar_init(&ctl->s_empty[i], ROWS);
+      mbar_init(&ctl->s_empty[i], SOFT);
     }
-    mbar_init(&ctl->p_full, ROWS);
+    mbar_init(&ctl->p_full, SOFT);
     mbar_init(&ctl->pv_done, 1);
-    mbar_init(&ctl->q_ready, ROWS);
+    mbar_init(&ctl->q_ready, SOFT);
     mbar_init(&ctl->drain, 1);
     ctl->abort_flag = 0;
     ctl->maxpos = -1;
@@ -130,7 +133,7 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(const __grid_constan
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (tid >= 128) {
+  if (tid >= 128 && tid < 128 + ROWS) {
     const int r = tid - 128;
     const int ti = r / G;
     int tok = -1;
@@ -239,21 +242,24 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(const __grid_constan
       }
     }
   } else if (warp >= 4) {
-    // ------------------------------------------------------------ softmax / output: thread = row
-    const int r = tid - 128;
-    const int q4 = warp & 3;
-    const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
+    // ------------------------------------------------------------ softmax / output: thread = (row, half)
+    // warpgroup gi takes keys [64 gi, 64 gi + 64) of every tile and dims [64 gi, 64 gi + 64) of O; the two
+    // halves of a row agree on the maximum through shared memory, so both take the same rescale decisions
+    const int gi = (warp - 4) >> 2;
+    const int r = (warp & 3) * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const int tok = ctl->tok[r];
     const int pos = ctl->pos[r];
     const int head = kvh * G + (r % G);
-    // Q row -> shared memory (128-byte swizzle, two dims-halves)
+    // Q row, this warpgroup's dims half -> shared memory (128-byte swizzle)
     {
-      uint8_t* qd = sm + OFF_Q;
-      const uint4* src = reinterpret_cast<const uint4*>(p.q + (static_cast<long long>(tok < 0 ? 0 : tok) * p.nq + head) * D);
+      uint8_t* qd = sm + OFF_Q + gi * HALF_B;
+      const uint4* src = reinterpret_cast<const uint4*>(p.q + (static_cast<long long>(tok < 0 ? 0 : tok) * p.nq + head) * D +
+                                                        gi * 64);
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
+      for (int c = 0; c < 8; ++c) {
         const uint4 v = tok >= 0 ? src[c] : make_uint4(0, 0, 0, 0);
-        *reinterpret_cast<uint4*>(qd + (c >> 3) * HALF_B + r * 128 + (((c & 7) ^ (r & 7)) << 4)) = v;
+        *reinterpret_cast<uint4*>(qd + r * 128 + ((c ^ (r & 7)) << 4)) = v;
       }
       fence_proxy_async_smem();
       mbar_arrive(&ctl->q_ready);
@@ -263,43 +269,45 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(const __grid_constan
     for (int j = 0; j < ntiles; ++j) {
       const int st = j & 1;
       const bool got = mbar_wait(&ctl->s_full[st], (j >> 1) & 1u, abort_flag);
-      if (named_bar_or(1, ROWS, !got)) {
+      if (named_bar_or(1, SOFT, !got)) {
         *abort_flag = 1;
         stop = true;
         break;
       }
       tc_fence_after();
-      const uint32_t sa = tmem + st * KT + lane_off;
-      // pass 1: masked maximum of the tile
+      const uint32_t sa = tmem + st * KT + gi * 64 + lane_off;
+      const int kbase = j * KT + gi * 64;
+      // pass 1: masked maximum of this half, then of the row
       float mx = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < KT / 32; ++c) {
+      for (int c = 0; c < 2; ++c) {
         uint32_t v[32];
         tmem_ld32(sa + c * 32, v);
         tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int key = j * KT + c * 32 + i;
-          if (key <= pos) mx = fmaxf(mx, u32_as_f32(v[i]) * p.scale_log2);
-        }
+        for (int i = 0; i < 32; ++i)
+          if (kbase + c * 32 + i <= pos) mx = fmaxf(mx, u32_as_f32(v[i]) * p.scale_log2);
       }
+      ctl->xm[j & 1][gi][r] = mx;
+      named_bar_sync(2, SOFT);
+      mx = fmaxf(ctl->xm[j & 1][0][r], ctl->xm[j & 1][1][r]);
       float alpha = 1.f;
       if (mx > -INFINITY && (m_use == -INFINITY || mx > m_use + RESCALE_LOG2)) {
         alpha = m_use == -INFINITY ? 1.f : ex2(m_use - mx);
         l *= alpha;
         m_use = mx;
       }
-      // pass 2: weights as bf16, their row sum
-      uint32_t pk[KT / 2];
+      // pass 2: weights as bf16, their partial row sum
+      uint32_t pk[32];
       float ls = 0.f;
 #pragma unroll
-      for (int c = 0; c < KT / 32; ++c) {
+      for (int c = 0; c < 2; ++c) {
         uint32_t v[32];
         tmem_ld32(sa + c * 32, v);
         tmem_wait_ld();
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
-          const int key = j * KT + c * 32 + i;
+          const int key = kbase + c * 32 + i;
           const float p0 = (key <= pos && m_use > -INFINITY) ? ex2(u32_as_f32(v[i]) * p.scale_log2 - m_use) : 0.f;
           const float p1 = (key + 1 <= pos && m_use > -INFINITY) ? ex2(u32_as_f32(v[i + 1]) * p.scale_log2 - m_use) : 0.f;
           const uint32_t w = pack_bf16x2(p0, p1);
@@ -313,17 +321,17 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(const __grid_constan
       l += ls;
       if (j >= 1) {
         const bool okp = mbar_wait(&ctl->pv_done, (j - 1) & 1u, abort_flag);
-        if (named_bar_or(1, ROWS, !okp)) {
+        if (named_bar_or(1, SOFT, !okp)) {
           *abort_flag = 1;
           stop = true;
           break;
         }
         tc_fence_after();
-        // rescale O (warp-collective TMEM access; rows that keep their maximum multiply by 1)
+        // rescale this half of O (warp-collective TMEM access; rows that keep their maximum multiply by 1)
         if (__any_sync(0xffffffffu, alpha != 1.f)) {
-          const uint32_t oa = tmem + 2 * KT + lane_off;
+          const uint32_t oa = tmem + 2 * KT + gi * 64 + lane_off;
 #pragma unroll
-          for (int c = 0; c < D / 32; ++c) {
+          for (int c = 0; c < 2; ++c) {
             uint32_t v[32];
             tmem_ld32(oa + c * 32, v);
             tmem_wait_ld();
@@ -334,12 +342,12 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(const __grid_constan
           tmem_wait_st();
         }
       }
-      // P row -> shared memory (A operand of PV: keys are K, 128-byte swizzle, two key-halves)
-      uint8_t* pd = sm + OFF_P;
+      // P, this key half -> shared memory (A operand of PV, 128-byte swizzle)
+      uint8_t* pd = sm + OFF_P + gi * HALF_B;
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
+      for (int c = 0; c < 8; ++c) {
         const uint4 v = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-        *reinterpret_cast<uint4*>(pd + (c >> 3) * HALF_B + r * 128 + (((c & 7) ^ (r & 7)) << 4)) = v;
+        *reinterpret_cast<uint4*>(pd + r * 128 + ((c ^ (r & 7)) << 4)) = v;
       }
       fence_proxy_async_smem();
       tc_fence_before();
@@ -347,20 +355,23 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(const __grid_constan
     }
     if (!stop && ntiles > 0) {
       const bool okp = mbar_wait(&ctl->pv_done, (ntiles - 1) & 1u, abort_flag);
-      if (named_bar_or(1, ROWS, !okp)) {
+      if (named_bar_or(1, SOFT, !okp)) {
         *abort_flag = 1;
         stop = true;
       }
     }
     if (!stop && ntiles > 0) {
       tc_fence_after();
-      const float inv = l > 0.f ? 1.f / l : 0.f;
-      const uint32_t oa = tmem + 2 * KT + lane_off;
-      __nv_bfloat16* orow = p.o + (static_cast<long long>(tok < 0 ? 0 : tok) * p.nq + head) * D;
+      ctl->xl[gi][r] = l;
+      named_bar_sync(2, SOFT);
+      const float lt = ctl->xl[0][r] + ctl->xl[1][r];
+      const float inv = lt > 0.f ? 1.f / lt : 0.f;
+      const uint32_t oa = tmem + 2 * KT + gi * 64 + lane_off;
+      __nv_bfloat16* orow = p.o + (static_cast<long long>(tok < 0 ? 0 : tok) * p.nq + head) * D + gi * 64;
       float sq = 0.f;
       int bad = -1;
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
+      for (int c = 0; c < 2; ++c) {
         uint32_t v[32];
         tmem_ld32(oa + c * 32, v);
         tmem_wait_ld();
@@ -384,7 +395,7 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(const __grid_constan
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
                 const int dd = bf16x2_diff(a[e], b[e]);
-                if (bad < 0 && dd >= 0) bad = c * 32 + i * 8 + e * 2 + dd;
+                if (bad < 0 && dd >= 0) bad = gi * 64 + c * 32 + i * 8 + e * 2 + dd;
               }
             }
           }
@@ -396,7 +407,7 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(const __grid_constan
         if (p.check == nullptr && p.row_sq != nullptr) atomicAdd(p.row_sq + tok, sq);
       }
     }
-    if (p.check != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && r == 0) atomicAdd(p.check + 2, 1ull);
+    if (p.check != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && r == 0 && gi == 0) atomicAdd(p.check + 2, 1ull);
   }
   tc_fence_before();
   __syncthreads();
@@ -762,7 +773,7 @@ int sdc_attn_prefill(const void* q, void* o, const void* cache, long long num_bl
     attr = true;
   }
   dim3 grid(ntiles, nkv);
-  prefill_tc_kernel<<<grid, 256, pf::SMEM, static_cast<cudaStream_t>(stream)>>>(tm, p);
+  prefill_tc_kernel<<<grid, 128 + pf::SOFT, pf::SMEM, static_cast<cudaStream_t>(stream)>>>(tm, p);
   return static_cast<int>(cudaGetLastError());
 }
 
