@@ -46,6 +46,26 @@ constexpr int A_BYTES = BM * BK * 2;
 constexpr int MAX_BANDS = 4096;
 constexpr long long COUNTER_BYTES = 2LL * MAX_BANDS * 4;
 
+// Push mode (row-parallel GEMM fused with the reduce-scatter transfer): output rows [o R, (o + 1) R) belong to
+// rank o; every tile is stored straight into its owner's receive buffer at rows [off + rank R, ...) through the
+// owner's tensor map, with its seals, and the last CTA to finish publishes the generation flag to every rank.
+// off = (new generation & 1) cap: consecutive pushes use alternate regions of the receive buffer, so a rank that
+// pushes generation g + 1 never overwrites rows an owner may still be summing for generation g (the owner must
+// have finished g before any rank can finish g + 1 and push g + 2).
+struct Push {
+  int on;
+  int world, rank, R;
+  long long cap;              // rows per region of the receive buffer
+  uint32_t* seal_peer[8];     // every rank's receive seals [world R][nb]
+  long long* flag_peer[8];    // every rank's flag array [world]
+  long long* gen;             // this rank's generation counter
+  unsigned int* done;         // CTAs finished (zero between launches)
+};
+
+struct PeerMaps {
+  CUtensorMap m[8];           // every rank's receive buffer [world R][N] (push mode)
+};
+
 struct Params {
   int M, N, K;
   int nb;          // checksum blocks = ceil(N / 128)
@@ -79,6 +99,7 @@ struct Params {
   uint32_t inj_xor;
   unsigned long long* dbg;   // optional per-CTA timers (null: off): [cta][8]
   uint32_t* seal;            // optional [M][nb] hash of the stored bf16 bits of each (row, block) (null: off)
+  Push push;
   int ksplit;                // K splits (1: the fused epilogue; > 1: partial accumulators + reduce kernel)
   int kb_per;                // k-blocks per split
   float* part;               // ksplit > 1: [ksplit][M][N + 6 nb] fp32 partial accumulators
@@ -300,7 +321,7 @@ template <int BN, bool INJ>
 __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
     gemm_abft_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                      const __grid_constant__ CUtensorMap tmWc, const __grid_constant__ CUtensorMap tmC,
-                     const Params p) {
+                     const __grid_constant__ PeerMaps pm, const Params p) {
   using C = Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -515,6 +536,9 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
     const int et = threadIdx.x - 128; // epilogue thread id
     const int row_in_tile = q * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+    // push mode: the region of the receive buffer for the generation this launch publishes (the counter only
+    // changes after every CTA has finished, so all CTAs read the same value)
+    const long long push_off = p.push.on ? ((__ldcg(p.push.gen) + 1) & 1) * p.push.cap : 0;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x) {
@@ -655,7 +679,7 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
             uint32_t packed[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) packed[j] = pack_bf16x2(u32_as_f32(r[2 * j]), u32_as_f32(r[2 * j + 1]));
-            if (p.seal != nullptr) {
+            if (p.seal != nullptr || p.push.on) {
 #pragma unroll
               for (int j = 0; j < 32; ++j) seal += seal_term(packed[j], static_cast<uint32_t>(h * 32 + j));
             }
@@ -671,11 +695,23 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
-              tma_store_2d(&tmC, stg, cbase, mt * BM + q * 32);
+              if (p.push.on) {
+                const int owner = (mt * BM) / p.push.R;
+                tma_store_2d(&pm.m[owner], stg, cbase,
+                             static_cast<int>(push_off) + p.push.rank * p.push.R + (mt * BM - owner * p.push.R) + q * 32);
+              } else {
+                tma_store_2d(&tmC, stg, cbase, mt * BM + q * 32);
+              }
               bulk_commit();
             }
           }
-          if (p.seal != nullptr && row < p.M) p.seal[static_cast<long long>(row) * p.nb + col0 / CSW] = seal;
+          if (p.push.on && row < p.M) {
+            const int owner = row / p.push.R;
+            const long long r2 = push_off + static_cast<long long>(p.push.rank) * p.push.R + (row - owner * p.push.R);
+            p.push.seal_peer[owner][r2 * p.nb + col0 / CSW] = seal;
+          } else if (p.seal != nullptr && row < p.M) {
+            p.seal[static_cast<long long>(row) * p.nb + col0 / CSW] = seal;
+          }
         }
         tc_fence_before();
         mbar_arrive(&ctl->tempty[acc]);   // the MMA warp may refill this accumulator now
@@ -732,12 +768,28 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
     }
   }
 
-  if (warp >= 4 && lane == 0) bulk_wait0();   // staging tiles stay valid until their stores are done
+  if (warp >= 4 && lane == 0) {
+    bulk_wait0();   // staging tiles stay valid until their stores are done
+    if (p.push.on) asm volatile("fence.proxy.async;" ::: "memory");   // tensor stores before the flag release
+  }
   tc_fence_before();
   __syncthreads();
   if (warp == 2) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+  if (p.push.on && threadIdx.x == 0) {
+    // every store of this CTA (tensor stores and seals) is complete; the last CTA publishes the generation
+    asm volatile("fence.proxy.async;" ::: "memory");
+    __threadfence_system();
+    if (atomicAdd(p.push.done, 1u) == gridDim.x - 1) {
+      *p.push.done = 0;
+      const long long g = *p.push.gen + 1;
+      *p.push.gen = g;
+      __threadfence_system();
+      for (int r = 0; r < p.push.world; ++r)
+        asm volatile("st.release.sys.global.b64 [%0], %1;" ::"l"(p.push.flag_peer[r] + p.push.rank), "l"(g) : "memory");
+    }
   }
   if (p.dbg && threadIdx.x == 0) p.dbg[blockIdx.x * 8 + 6] = globaltimer();
 }
@@ -762,7 +814,7 @@ static int num_sms_cached() {
 
 template <int BN, bool INJ>
 static int launch(const CUtensorMap& a, const CUtensorMap& w, const CUtensorMap& wc, const CUtensorMap& c,
-                  const Params& p, int grid, cudaStream_t stream) {
+                  const PeerMaps& pm, const Params& p, int grid, cudaStream_t stream) {
   using Cf = Cfg<BN>;
   static bool attr_done = false;
   if (!attr_done) {
@@ -771,7 +823,7 @@ static int launch(const CUtensorMap& a, const CUtensorMap& w, const CUtensorMap&
     if (e != cudaSuccess) return static_cast<int>(e);
     attr_done = true;
   }
-  gemm_abft_kernel<BN, INJ><<<grid, Cf::THREADS, Cf::SMEM_BYTES, stream>>>(a, w, wc, c, p);
+  gemm_abft_kernel<BN, INJ><<<grid, Cf::THREADS, Cf::SMEM_BYTES, stream>>>(a, w, wc, c, pm, p);
   return static_cast<int>(cudaGetLastError());
 }
 
@@ -809,12 +861,22 @@ long long sdc_gemm_ws_bytes(int M, int N) {
 // C[M,N] = A[M,K] @ W[N,K]^T (+ bias): bf16 in/out, fp32 accumulation on tcgen05, with the ABFT check
 // described at the top of this file. Wc[6*nb, K] holds the checksum rows of W (see sdcguard_b200/ops/gemm.py).
 // Returns 0 or a CUDA error code; -1 for bad arguments.
+struct PushArgs {
+  int world, rank;
+  long long cap;                         // rows per region (>= M); the buffers hold two regions
+  const unsigned long long* recv_ptrs;   // every rank's receive buffer [2 cap][N]
+  const unsigned long long* seal_ptrs;   // every rank's receive seals [2 cap][nb]
+  const unsigned long long* flag_ptrs;   // every rank's flag array [world]
+  void* gen;                             // this rank's generation counter
+  void* done;                            // this rank's CTA completion counter (zero)
+};
+
 static int gemm_run(const void* A, long long lda, const void* W, const void* Wc, int M, int N, int K, void* Cout,
                     long long ldc, const float* bias, const float* bsum, float bias_max, const float* row_sq,
                     const float* wstat, void* ws, unsigned long long* state, int slot, unsigned s0, unsigned s1,
                     unsigned s2, unsigned s3, float zthr, float prod_coef, float out_coef, float abs_floor,
                     float bound_coef, int* err, int bn, int max_ctas, int inj_row, int inj_col, unsigned inj_xor,
-                    void* dbg, void* seal, void* stream, bool allow_split) {
+                    void* dbg, void* seal, void* stream, bool allow_split, const PushArgs* push = nullptr) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   if ((K % 8) || (N % 8) || (lda % 8) || (ldc % 8) || (bn != 128 && bn != 256)) return -1;
   if ((M + BM - 1) / BM > MAX_BANDS) return -1;
@@ -868,8 +930,28 @@ static int gemm_run(const void* A, long long lda, const void* W, const void* Wc,
   p.ksplit = 1;
   p.kb_per = (K + BK - 1) / BK;
   p.part = nullptr;
+  PeerMaps pm;
+  std::memset(&pm, 0, sizeof(pm));
+  if (push != nullptr) {
+    if (push->world < 1 || push->world > 8 || M % push->world || (M / push->world) % BM || ldc != N ||
+        push->cap < M || push->cap % BM)
+      return -1;
+    p.push.on = 1;
+    p.push.world = push->world;
+    p.push.rank = push->rank;
+    p.push.R = M / push->world;
+    p.push.cap = push->cap;
+    for (int r = 0; r < push->world; ++r) {
+      p.push.seal_peer[r] = reinterpret_cast<uint32_t*>(push->seal_ptrs[r]);
+      p.push.flag_peer[r] = reinterpret_cast<long long*>(push->flag_ptrs[r]);
+      if (!make_map(&pm.m[r], reinterpret_cast<const void*>(push->recv_ptrs[r]), 2 * push->cap, N, N, 32, false))
+        return -6;
+    }
+    p.push.gen = static_cast<long long*>(push->gen);
+    p.push.done = static_cast<unsigned int*>(push->done);
+  }
   // splitting pays when each CTA would stream a long K (measured: K = 1024 is faster unsplit)
-  if (allow_split && split_eligible(M, N) && K >= 2048 && max_ctas == 0 && dbg == nullptr) {
+  if (allow_split && push == nullptr && split_eligible(M, N) && K >= 2048 && max_ctas == 0 && dbg == nullptr) {
     const int kblocks = (K + BK - 1) / BK;
     int sp = num_sms_cached() / p.total_tiles;
     sp = sp > kMaxSplit ? kMaxSplit : sp;
@@ -893,9 +975,9 @@ static int gemm_run(const void* A, long long lda, const void* W, const void* Wc,
   const bool inj = inj_row >= 0;
   int rc;
   if (bn == 256)
-    rc = inj ? launch<256, true>(ma, mw, mc, mo, p, grid, st) : launch<256, false>(ma, mw, mc, mo, p, grid, st);
+    rc = inj ? launch<256, true>(ma, mw, mc, mo, pm, p, grid, st) : launch<256, false>(ma, mw, mc, mo, pm, p, grid, st);
   else
-    rc = inj ? launch<128, true>(ma, mw, mc, mo, p, grid, st) : launch<128, false>(ma, mw, mc, mo, p, grid, st);
+    rc = inj ? launch<128, true>(ma, mw, mc, mo, pm, p, grid, st) : launch<128, false>(ma, mw, mc, mo, pm, p, grid, st);
   if (rc != 0 || p.ksplit == 1) return rc;
   const long long warps = static_cast<long long>(M) * nb;
   const unsigned blocks = static_cast<unsigned>((warps * 32 + 255) / 256);
@@ -915,6 +997,24 @@ int sdc_gemm_bf16(const void* A, long long lda, const void* W, const void* Wc, i
   return gemm_run(A, lda, W, Wc, M, N, K, Cout, ldc, bias, bsum, bias_max, row_sq, wstat, ws, state, slot, s0, s1, s2,
                   s3, zthr, prod_coef, out_coef, abs_floor, bound_coef, err, bn, max_ctas, inj_row, inj_col, inj_xor,
                   dbg, seal, stream, true);
+}
+
+// Row-parallel checked GEMM fused with the reduce-scatter transfer (push mode, see `Push`): C = A @ W^T is not
+// stored locally; each output tile goes straight to the rank that owns its rows, into that rank's receive buffer
+// at rows [off + rank R, off + (rank + 1) R) with its seals (off alternates between 0 and cap, see `Push`), and the
+// launch's last CTA raises this rank's flag on every rank. M = world R with R a multiple of 128, M <= cap. The owner then sums the world slots of its receive buffer
+// (sdc_tp_reduce_local). No split-K in this mode.
+int sdc_gemm_bf16_push(const void* A, long long lda, const void* W, const void* Wc, int M, int N, int K,
+                       const float* bias, const float* bsum, float bias_max, const float* row_sq, const float* wstat,
+                       void* ws, unsigned long long* state, int slot, unsigned s0, unsigned s1, unsigned s2,
+                       unsigned s3, float zthr, float prod_coef, float out_coef, float abs_floor, float bound_coef,
+                       int* err, int bn, int inj_row, int inj_col, unsigned inj_xor, int world, int rank,
+                       long long cap, const unsigned long long* recv_ptrs, const unsigned long long* seal_ptrs,
+                       const unsigned long long* flag_ptrs, void* gen, void* done, void* stream) {
+  PushArgs pa{world, rank, cap, recv_ptrs, seal_ptrs, flag_ptrs, gen, done};
+  return gemm_run(A, lda, W, Wc, M, N, K, reinterpret_cast<void*>(recv_ptrs[rank]), N, bias, bsum, bias_max, row_sq,
+                  wstat, ws, state, slot, s0, s1, s2, s3, zthr, prod_coef, out_coef, abs_floor, bound_coef, err, bn, 0,
+                  inj_row, inj_col, inj_xor, nullptr, nullptr, stream, false, &pa);
 }
 
 }  // extern "C"

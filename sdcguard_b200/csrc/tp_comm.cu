@@ -44,11 +44,16 @@ __device__ __forceinline__ void report(unsigned long long* state, float z, unsig
 
 // One warp per (row, 128-column block) of this rank's rows; lane l owns columns 4l..4l+3 of the block.
 // parts: peers' partial outputs [M][N] bf16; seals: peers' seals [M][nb] u32; out: this rank's [R][N].
+// local = true (after a push-mode GEMM): peer r's partial rows are slot r of this rank's own receive buffer
+// (rows [off + r R, off + (r + 1) R) with off = (gen & 1) cap: consecutive pushes alternate between two regions),
+// so every read is local; the sums and checks are the same.
 __global__ void __launch_bounds__(256) rs_pull_kernel(Peers parts, Peers seals, const long long* gen,
                                                       const long long* my_flags, int world, int rank, int R, int N,
                                                       __nv_bfloat16* __restrict__ out, float tol,
-                                                      unsigned long long* state, int* err) {
+                                                      unsigned long long* state, int* err, bool local,
+                                                      long long cap) {
   if (!wait_all(gen, my_flags, world, err)) return;
+  const long long off = local ? (__ldcg(gen) & 1) * cap : 0;
   const int nb = (N + 127) / 128;
   const int lane = threadIdx.x & 31;
   const long long wid = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
@@ -63,7 +68,9 @@ __global__ void __launch_bounds__(256) rs_pull_kernel(Peers parts, Peers seals, 
   int bad_peer = -1;
   for (int r = 0; r < world; ++r) {
     uint2 v = make_uint2(0u, 0u);
-    if (in) v = __ldcg(reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(parts.ptr[r]) + row * N + col));
+    const long long prow = local ? off + static_cast<long long>(r) * R + lr : row;
+    const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(local ? parts.ptr[rank] : parts.ptr[r]);
+    if (in) v = __ldcg(reinterpret_cast<const uint2*>(src + prow * N + col));
     uint32_t h = seal_term(v.x, static_cast<uint32_t>(lane * 2)) + seal_term(v.y, static_cast<uint32_t>(lane * 2 + 1));
 #pragma unroll
     for (int m = 16; m > 0; m >>= 1) h += __shfl_xor_sync(0xffffffffu, h, m);
@@ -75,7 +82,7 @@ __global__ void __launch_bounds__(256) rs_pull_kernel(Peers parts, Peers seals, 
     sum_in += (a.x + a.y) + (c.x + c.y);
     abs_in += (fabsf(a.x) + fabsf(a.y)) + (fabsf(c.x) + fabsf(c.y));
     if (lane == 0) {
-      const uint32_t want = __ldcg(static_cast<const uint32_t*>(seals.ptr[r]) + row * nb + b);
+      const uint32_t want = __ldcg(static_cast<const uint32_t*>(local ? seals.ptr[rank] : seals.ptr[r]) + prow * nb + b);
       if (want != h && bad_peer < 0) bad_peer = r;
     }
   }
@@ -182,7 +189,22 @@ int sdc_tp_reduce_scatter(const unsigned long long* part_ptrs, const unsigned lo
   rs_pull_kernel<<<blocks > 0 ? blocks : 1, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       make_peers(part_ptrs, world), make_peers(seal_ptrs, world), static_cast<const long long*>(gen),
       static_cast<const long long*>(my_flags), world, rank, R, N, static_cast<__nv_bfloat16*>(out), tol,
-      static_cast<unsigned long long*>(state), err);
+      static_cast<unsigned long long*>(state), err, false, 0);
+  return static_cast<int>(cudaGetLastError());
+}
+
+// The owner side of a push-mode GEMM: wait for every rank's flag, then reduce the world slots of this rank's own
+// receive buffer with the same seal and linearity checks as the pull.
+int sdc_tp_reduce_local(const unsigned long long* part_ptrs, const unsigned long long* seal_ptrs, const void* gen,
+                        const void* my_flags, int world, int rank, int R, int N, long long cap, void* out, float tol,
+                        void* state, int* err, void* stream) {
+  if (world < 1 || world > MAXW || N % 8) return -1;
+  const long long warps = static_cast<long long>(R) * ((N + 127) / 128);
+  const unsigned blocks = static_cast<unsigned>((warps * 32 + 255) / 256);
+  rs_pull_kernel<<<blocks > 0 ? blocks : 1, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      make_peers(part_ptrs, world), make_peers(seal_ptrs, world), static_cast<const long long*>(gen),
+      static_cast<const long long*>(my_flags), world, rank, R, N, static_cast<__nv_bfloat16*>(out), tol,
+      static_cast<unsigned long long*>(state), err, true, cap);
   return static_cast<int>(cudaGetLastError());
 }
 

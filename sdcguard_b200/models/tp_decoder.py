@@ -178,6 +178,10 @@ class TPDecoder:
 
     def _rowpar(self, x, w, cw, name, T, R, row_sq, out_shard, sample=None):
         """Row-parallel GEMM + reduce-scatter into out_shard (R, H)."""
+        if (self.collective == "own" and self.checked and self.precision == "bf16" and self.comm.can_push(T)
+                and T > 256):
+            # one kernel does the GEMM and the transfer (tiles pushed to their owners), then a local reduce
+            return self.comm.gemm_reduce_scatter(x, cw, self.state.state, self.slot[name], out_shard, row_sq=row_sq)
         if self.collective == "own":
             self._linear(x, w, cw, name, self.comm.partial(T), row_sq,
                          seal=self.comm.partial_seal(T) if self.checked else None, sample=sample)

@@ -34,14 +34,18 @@ class TPComm:
         self.hidden = hidden
         nb = -(-hidden // 128)
         self.nb = nb
-        self.part = heap.alloc([max_rows, hidden], torch.bfloat16)
-        self.part_seal = heap.alloc([max_rows, nb], torch.int32)
+        self.max_rows = max_rows
+        # rows [0, max_rows): the local partial of the two-step path, or push region 0; [max_rows, 2 max_rows):
+        # push region 1 (consecutive fused GEMM + reduce-scatter launches alternate regions)
+        self.part = heap.alloc([2 * max_rows, hidden], torch.bfloat16)
+        self.part_seal = heap.alloc([2 * max_rows, nb], torch.int32)
         self.shard_buf = heap.alloc([max_rows // self.world, hidden], torch.bfloat16)
         self.shard_seal = heap.alloc([max_rows // self.world, nb], torch.int32)
         self.flags = heap.alloc([self.world], torch.int64)
         self.gen = torch.zeros(1, dtype=torch.int64, device=heap.device)
         self.err = torch.zeros(1, dtype=torch.int32, device=heap.device)
         self.state = torch.zeros(2, abft.STATE_COLS, dtype=torch.int64, device=heap.device)   # 0: RS, 1: AG
+        self.done = torch.zeros(1, dtype=torch.int32, device=heap.device)     # push-mode GEMM: CTAs finished
         self._inject: Optional[tuple] = None
 
     def inject_next(self, row: int, col: int, bit: int = 0) -> None:
@@ -79,6 +83,63 @@ class TPComm:
             self.part.ptrs, self.part_seal.ptrs, self.gen.data_ptr(), self.flags.local.data_ptr(), self.world,
             self.rank, R, self.hidden, out.data_ptr(), TOL, self.state[0].data_ptr(), self.err.data_ptr(), self._s()),
             "tp reduce-scatter")
+        return out
+
+    def can_push(self, M: int) -> bool:
+        """The fused GEMM + transfer needs every rank's rows to be whole 128-row tiles."""
+        return M % (128 * self.world) == 0 and M <= self.max_rows
+
+    def gemm_reduce_scatter(self, x: torch.Tensor, cw, state: torch.Tensor, slot: int, out: torch.Tensor,
+                            row_sq: Optional[torch.Tensor] = None, bn: Optional[int] = None,
+                            inject: Optional[tuple] = None) -> torch.Tensor:
+        """Row-parallel checked GEMM fused with the reduce-scatter transfer: every output tile of x @ W^T goes from
+        the GEMM epilogue straight into the receive buffer of the rank that owns its rows (TMA stores over NVLink,
+        with seals), the launch's last CTA raises this rank's flag on every rank, then this rank sums its world
+        slots locally with the seal and linearity checks. x: (M, K) with M a multiple of 128 world; out:
+        (M / world, N). inject=(row, col, xor) flips an accumulator bit inside the GEMM (caught by its ABFT
+        check); `inject_next` flips a bit of this rank's receive buffer after the transfer (caught by the seal)."""
+        self.gemm_push(x, cw, state, slot, row_sq=row_sq, bn=bn, inject=inject)
+        return self.reduce_local(x.shape[0], out)
+
+    def gemm_push(self, x: torch.Tensor, cw, state: torch.Tensor, slot: int, row_sq: Optional[torch.Tensor] = None,
+                  bn: Optional[int] = None, inject: Optional[tuple] = None) -> None:
+        import math
+        from ..ops import gemm
+        M, K = x.shape
+        if not self.can_push(M) or K != cw.k or cw.n != self.hidden or x.stride(1) != 1:
+            raise ValueError(f"push GEMM needs M % (128 world) == 0 and a ({self.hidden}, {K}) weight")
+        lib = _native.lib()
+        if row_sq is None:
+            row_sq = gemm.row_sqnorm(x)
+        dev = x.device
+        ws = gemm.workspace(dev, int(lib.sdc_gemm_ws_bytes(M, cw.n)))
+        bn = bn or gemm.pick_bn(M, cw.n)
+        ir, ic, ix = (-1, -1, 0) if inject is None else (int(inject[0]), int(inject[1]), int(inject[2]))
+        s = cw.mask
+        _native.check(lib.sdc_gemm_bf16_push(
+            x.data_ptr(), x.stride(0), cw.weight.data_ptr(), cw.cs.wc.data_ptr(), M, cw.n, K,
+            None if cw.bias is None else cw.bias.data_ptr(), None if cw.cs.bsum is None else cw.cs.bsum.data_ptr(),
+            float(cw.cs.bias_max), row_sq.data_ptr(), cw.cs.wstat.data_ptr(), ws.data_ptr(), state.data_ptr(),
+            int(slot), s[0], s[1], s[2], s[3], float(abft.Z_ALARM), float(cw.prod_coef), float(cw.out_coef),
+            float(abft.ABS_FLOOR), float(math.sqrt(K)), gemm.error_word(dev).data_ptr(), int(bn), ir, ic, ix,
+            self.world, self.rank, self.max_rows, self.part.ptrs, self.part_seal.ptrs, self.flags.ptrs, self.gen.data_ptr(),
+            self.done.data_ptr(), self._s()), "checked GEMM + reduce-scatter push")
+
+    def reduce_local(self, M: int, out: torch.Tensor) -> torch.Tensor:
+        """Waits for every rank's push of the current generation, then sums the world slots of this rank's receive
+        buffer (slot r = rows [r R, (r+1) R), written by rank r) into out with the seal and linearity checks."""
+        R = M // self.world
+        if self._inject is not None:
+            r, c, bit = self._inject
+            self._inject = None
+            torch.cuda.current_stream(self.heap.device).synchronize()    # the push has landed
+            off = (int(self.gen.item()) & 1) * self.max_rows
+            v = self.part.local.view(torch.int16)[off + r, c]
+            v.bitwise_xor_(1 << bit if bit < 15 else -(1 << 15))
+        _native.check(_native.lib().sdc_tp_reduce_local(
+            self.part.ptrs, self.part_seal.ptrs, self.gen.data_ptr(), self.flags.local.data_ptr(), self.world,
+            self.rank, R, self.hidden, self.max_rows, out.data_ptr(), TOL, self.state[0].data_ptr(),
+            self.err.data_ptr(), self._s()), "tp reduce (local)")
         return out
 
     def all_gather(self, R: int, out: torch.Tensor) -> torch.Tensor:

@@ -49,7 +49,7 @@ def _prefill_logits(world, rank, lens, tokens, inject=False):
     comm = TPComm(heap, 512, TINY.hidden)
     m = TPDecoder(TINY, comm, rank, world, dev, checked=True, collective="own", max_rows=512, seed=3)
     m.buffers(512)
-    pps = 8
+    pps = -(-max(lens) // 16)
     cache = torch.zeros(TINY.layers, 1 + len(lens) * pps, 2, m.nkv, 16, 128, dtype=torch.bfloat16, device=dev)
     meta = _meta(lens, tokens, dev, pps, m.nq // m.nkv)
     logits = m.forward(meta, cache)
@@ -134,6 +134,18 @@ def test_tp1_prefill_matches_fp32_reference():
     tokens = _tokens()
     logits, alarms, checks, _, m = _prefill_logits(1, 0, LENS, tokens)
     ref = _reference(m, LENS, tokens)
+    err = (logits - ref).abs().max().item()
+    assert err < 0.03 * ref.abs().max().item(), (err, ref.abs().max().item())
+    assert checks > 0 and not alarms, alarms
+
+
+def test_tp1_prefill_fused_push_path_matches_fp32_reference():
+    """512 tokens: the row-parallel GEMMs take the fused GEMM + reduce-scatter push path."""
+    lens = [200, 312]
+    g = torch.Generator().manual_seed(6)
+    tokens = torch.randint(0, 1024, (sum(lens),), generator=g)
+    logits, alarms, checks, _, m = _prefill_logits(1, 0, lens, tokens)
+    ref = _reference(m, lens, tokens)
     err = (logits - ref).abs().max().item()
     assert err < 0.03 * ref.abs().max().item(), (err, ref.abs().max().item())
     assert checks > 0 and not alarms, alarms
