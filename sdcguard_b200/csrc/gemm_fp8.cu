@@ -1,24 +1,29 @@
 // Block-scaled fp8 checked GEMM for sm_100a: C = (A_q * s_a) @ (W_q * s_w)^T in bf16, with A_q, W_q fp8 E4M3,
 // s_a one power-of-two scale per row and 128-wide K block (1 x 128), s_w one per 128 x 128 block of W, fp32
-// accumulation on tcgen05 (kind::f8f6f4), and the ABFT check of every 128-column block of every output row.
+// accumulation on tcgen05, and the ABFT check of every 128-column block of every output row.
 //
-// Scaling on Blackwell without a block-scale MMA: every 128-wide K block is one accumulation into a fresh TMEM
-// accumulator (four MMAs of K = 32); the epilogue warps read it with tcgen05.ld and add it to fp32 registers
-// multiplied by s_a[row, kb] * s_w[block, kb] ("promotion"). Two TMEM accumulators alternate, so the tensor cores
-// fill one K block while the epilogue promotes the previous one.
+// Scaling is done by the tensor cores: `tcgen05.mma.kind::mxf8f6f4.block_scale` multiplies every 32-wide K slice of
+// a row of A and of a row of B by a UE8M0 scale factor read from tensor memory, and accumulates the whole K extent
+// in one fp32 TMEM accumulator. The power-of-two scales are exactly UE8M0 values, so this is the same arithmetic as
+// dequantize-then-multiply. Per 128-wide K block the MMA warp copies the block's scale factors from shared memory
+// into TMEM with `tcgen05.cp .32x128b.warpx4` (issued in order with the MMAs that read them) and issues four
+// MMAs of K = 32 and N = 144 (B rows 128-143, the checksum rows, take their scale factors from the fifth column). Scale-factor layout in TMEM (and in the 512-byte shared-memory chunk it is copied from): row r of
+// a 128-row operand sits in lane r % 32 of every lane quarter, column r / 32, one byte per 32-wide K slice; the
+// four bytes of a word are the four slices of the 128-wide block, all equal here.
 //
 // The check needs no second pass and no other CTA. The B operand of every tile is 144 rows: the tile's 128 rows
 // of W_q and 16 checksum rows of its 128-column block (12 used): the plain and the +-1-signed sums of the block's
-// quantized rows, each split into six fp8 parts with their own power-of-two scales (about 24 significant bits in
-// total). The MMA computes the tile and its expected sums in one instruction stream (12.5% more MMA columns); the
-// epilogue promotes the checksum columns with the part scales, forms the block's plain / signed / squared /
-// absolute sums of the promoted accumulator, and judges them with the fp32-accumulation noise model of the bf16
-// kernel. Because the checksum rows are sums of the same quantized weights that the MMA uses, the identity holds
-// exactly up to rounding; a fault in the MMA, in TMEM or in the promotion breaks it.
+// quantized rows, each split into six fp8 parts with their own power-of-two scale factors (about 24 significant
+// bits in total). The MMA computes the tile and its expected sums in one instruction stream (12.5% more MMA
+// columns); the epilogue reads the finished accumulator once, forms the block's plain / signed / squared / absolute
+// sums, and judges them with the fp32-accumulation noise model of the bf16 kernel. Because the checksum rows are
+// sums of the same quantized weights, and carry their own scale factors, the identity holds up to rounding; a
+// fault in the MMA, in TMEM or in a weight scale factor breaks it. (A wrong activation scale factor scales the
+// row's outputs and expected sums alike; the quantizer's replay check covers the activation scale factors.)
 //
-// Also here: the activation quantizer (bf16 -> E4M3 with 1 x 128 power-of-two scales, and ||dequantized row||^2
-// for the noise model), with an exact replay mode that re-quantizes sampled rows and compares codes and scales
-// (the fp8 quantisation check).
+// Also here: the activation quantizer (bf16 -> E4M3 with 1 x 128 power-of-two scales, their UE8M0 scale-factor
+// chunks, and ||dequantized row||^2 for the noise model), with an exact replay mode that re-quantizes sampled rows
+// and compares codes, scales and scale-factor bytes (the fp8 quantisation check).
 //
 // Reference: the reference does not check fp8 GEMMs at all (src/sdcguard/guard.py:81-87; docs/STATUS.md "FP8 matmul
 // arithmetic: Planned"); its fp8 check re-quantizes two sampled rows against a one-step tolerance
@@ -40,26 +45,31 @@ constexpr int BNC = BN + CSR;         // MMA N
 constexpr int BK = 128;               // fp8 elements (= bytes) per K block = one scale block
 constexpr int A_BYTES = BM * BK;
 constexpr int B_BYTES = BNC * BK;
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;   // 34 KB, a multiple of 1 KB
+constexpr int SFA_BYTES = 512;        // 128 rows x 4 K slices
+constexpr int SFB_BYTES = 1024;       // two chunks: the 128 weight rows, the 16 checksum rows (12 used)
+constexpr int SF_OFF = A_BYTES + B_BYTES;
+constexpr int STAGE_TX = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
+constexpr int STAGE_BYTES = 36 * 1024;           // each stage starts on a 1 KB boundary (128-byte swizzle)
+static_assert(STAGE_TX <= STAGE_BYTES, "stage layout");
 constexpr int STAGES = 5;
-constexpr int EWG = 2;                // epilogue warpgroups: warpgroup g promotes columns [64 g, 64 g + 64)
+constexpr int EWG = 2;                // epilogue warpgroups: warpgroup g owns columns [64 g, 64 g + 64)
 constexpr int HALF = BN / EWG;
 constexpr int THREADS = 128 + 128 * EWG;
 constexpr int STAGING_BYTES = 4 * EWG * 4096;  // per epilogue warp: 32 rows x 64 bf16
 constexpr int XCH_BYTES = 2 * 128 * 16;        // per tile parity: warpgroup 1's (P, S, Q, |.|) of each row
 constexpr int MAX_KBS = 128;                   // K <= 16384
-constexpr int SCL_BYTES = MAX_KBS * 13 * 4;    // the tile's weight scales and checksum part scales
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + STAGING_BYTES + XCH_BYTES + SCL_BYTES + 1024 + 512;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + STAGING_BYTES + XCH_BYTES + 1024 + 512;
 constexpr int TMEM_COLS = 512;
-constexpr int SLOT_COLS = BNC;                 // three accumulators of 144 columns
-constexpr int NSLOT = 3;
+constexpr int NACC = 2;                        // accumulators (tile t in accumulator t % 2)
+constexpr int ACC_STRIDE = 160;                // columns per accumulator (144 used)
+constexpr int SFA_COL = 320;                   // 4 columns: A's 128 rows
+constexpr int SFB_COL = 352;                   // 8 columns: B's 128 weight rows, then its checksum rows
 constexpr float FP8_MAX = 448.f;
 
 struct Params8 {
   int M, N, K, nb, kbs, m_tiles, total_tiles, group;
-  const float* sa;        // [M][kbs]
-  const float* sw;        // [nb][kbs]
-  const float* csc;       // [nb][kbs][12]: power-of-two scale of each checksum part
+  const uint8_t* sfa;     // [m_tiles][kbs][512] UE8M0 scale-factor chunks of A
+  const uint8_t* sfb;     // [nb][kbs][1024] UE8M0 scale-factor chunks of the 144-row B operand of each block
   const float* row_sq;    // [M] ||dequantized row of A||^2
   const float4* wstat;    // [nb] {||W_b||_F, ||plain||, ||signed||, max|W_b|} of the dequantized weights
   __nv_bfloat16* C;
@@ -76,26 +86,53 @@ struct Params8 {
 struct Ctl {
   uint64_t full[STAGES];
   uint64_t empty[STAGES];
-  uint64_t tfull[NSLOT];
-  uint64_t tempty[NSLOT];
+  uint64_t tfull[NACC];
+  uint64_t tempty[NACC];
   uint64_t drain;
   uint32_t tmem_base;
   int abort_flag;
 };
 
-__device__ __forceinline__ void umma_f8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                        uint32_t accumulate) {
+// D (+)= (A * sfa) (B * sfb)^T for one K = 32 slice; sfa / sfb: TMEM addresses of the scale factors, idesc carries
+// the byte (K slice) of each scale-factor word to use
+__device__ __forceinline__ void umma_mx8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      "setp.ne.b32 p, %6, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%4], [%5], p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(sfa_tmem), "r"(sfb_tmem), "r"(accumulate)
       : "memory");
 }
 
-// kind::f8f6f4 instruction descriptor: A and B E4M3 (format 0), D fp32, both K-major
-__host__ __device__ constexpr uint32_t idesc_e4m3_f32(int M, int N) {
-  return (1u << 4) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+// 32 lanes x 16 bytes of shared memory -> 4 TMEM columns of lanes [0, 32), replicated into all four lane quarters
+__device__ __forceinline__ void tmem_cp_32x128b_x4(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
+// shared-memory descriptor of a 32 x 16-byte scale-factor chunk: no swizzle, K-major, 8-row core matrices of 128
+// contiguous bytes (SBO = 128 B between them; a single core matrix along K, so LBO is unused)
+__device__ __forceinline__ uint64_t sf_desc(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>(1u) << 16;                  // LBO = 16 B (unused)
+  d |= static_cast<uint64_t>(128u >> 4) << 32;           // SBO = 128 B
+  d |= static_cast<uint64_t>(1u) << 46;                  // version
+  return d;                                              // layout type 0: no swizzle
+}
+
+// kind::mxf8f6f4 block-scaled instruction descriptor: A and B E4M3 (format 0), K-major, UE8M0 scale factors,
+// D fp32; `slice` selects the byte of the scale-factor words for A (bits 29-30) and B (bits 4-5)
+__host__ __device__ constexpr uint32_t idesc_mx8(int M, int N, uint32_t slice) {
+  return (slice << 4) | (static_cast<uint32_t>(N >> 3) << 17) | (1u << 23) | (static_cast<uint32_t>(M >> 4) << 24) |
+         (slice << 29);
+}
+
+__device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(smem_dst)),
+               "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
 }
 
 __device__ __forceinline__ void tile_coords8(const Params8& p, int tile, int& mt, int& nt) {
@@ -162,8 +199,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* staging = smem + STAGES * STAGE_BYTES;
   float4* xch = reinterpret_cast<float4*>(staging + STAGING_BYTES);   // [2][128]
-  float* scl = reinterpret_cast<float*>(staging + STAGING_BYTES + XCH_BYTES);   // [kbs] sw, then [kbs][12] csc
-  Ctl* ctl = reinterpret_cast<Ctl*>(staging + STAGING_BYTES + XCH_BYTES + SCL_BYTES);
+  Ctl* ctl = reinterpret_cast<Ctl*>(staging + STAGING_BYTES + XCH_BYTES);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
@@ -171,7 +207,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&ctl->full[s], 1);
       mbar_init(&ctl->empty[s], 1);
     }
-    for (int a = 0; a < NSLOT; ++a) {
+    for (int a = 0; a < NACC; ++a) {
       mbar_init(&ctl->tfull[a], 1);
       mbar_init(&ctl->tempty[a], 128 * EWG);
     }
@@ -196,7 +232,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   volatile int* abort_flag = &ctl->abort_flag;
 
   if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer
+    // ------------------------------------------------------------ TMA producer: operands + scale-factor chunks
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
@@ -205,6 +241,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
         int mt, nt;
         tile_coords8(p, tile, mt, nt);
+        const uint8_t* sfa = p.sfa + static_cast<long long>(mt) * p.kbs * SFA_BYTES;
+        const uint8_t* sfb = p.sfb + static_cast<long long>(nt) * p.kbs * SFB_BYTES;
         for (int kb = 0; kb < p.kbs; ++kb) {
           if (!mbar_wait(&ctl->empty[stage], phase ^ 1u, abort_flag)) {
             ok = false;
@@ -212,10 +250,12 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           uint8_t* sa = smem + stage * STAGE_BYTES;
           uint8_t* sb = sa + A_BYTES;
-          mbar_arrive_expect_tx(&ctl->full[stage], STAGE_BYTES);
+          mbar_arrive_expect_tx(&ctl->full[stage], STAGE_TX);
           tma_load_2d(sa, &tmA, &ctl->full[stage], kb * BK, mt * BM);
           tma_load_2d(sb, &tmW, &ctl->full[stage], kb * BK, nt * BN);
           tma_load_2d(sb + BN * BK, &tmWc, &ctl->full[stage], kb * BK, nt * CSR);
+          bulk_g2s(sa + SF_OFF, sfa + kb * SFA_BYTES, SFA_BYTES, &ctl->full[stage]);
+          bulk_g2s(sa + SF_OFF + SFA_BYTES, sfb + kb * SFB_BYTES, SFB_BYTES, &ctl->full[stage]);
           issued |= 1u << stage;
           issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
           if (++stage == STAGES) {
@@ -232,40 +272,44 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer: one accumulator per K block
+    // ------------------------------------------------------------ MMA issuer: one accumulator per tile
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      unsigned g = 0;
-      const uint32_t idesc = idesc_e4m3_f32(BM, BNC);
-      for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
-        for (int kb = 0; kb < p.kbs && ok; ++kb, ++g) {
-          const int slot = static_cast<int>(g % NSLOT);
-          if (!mbar_wait(&ctl->tempty[slot], ((g / NSLOT) & 1u) ^ 1u, abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
+      int t = 0;
+      const uint32_t sfa_t = tmem_base + SFA_COL, sfb_t = tmem_base + SFB_COL;
+      for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x, ++t) {
+        const int acc = t & 1;
+        if (!mbar_wait(&ctl->tempty[acc], ((t >> 1) & 1u) ^ 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem_base + static_cast<uint32_t>(acc * ACC_STRIDE);
+        for (int kb = 0; kb < p.kbs; ++kb) {
           if (!mbar_wait(&ctl->full[stage], phase, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
+          tmem_cp_32x128b_x4(sfa_t, sf_desc(sa + SF_OFF));
+          tmem_cp_32x128b_x4(sfb_t, sf_desc(sa + SF_OFF + SFA_BYTES));
+          tmem_cp_32x128b_x4(sfb_t + 4, sf_desc(sa + SF_OFF + SFA_BYTES + 512));
           const uint64_t adesc = umma_desc_sw128(sa);
           const uint64_t bdesc = umma_desc_sw128(sa + A_BYTES);
-          const uint32_t d = tmem_base + static_cast<uint32_t>(slot * SLOT_COLS);
 #pragma unroll
           for (int ks = 0; ks < BK / 32; ++ks)     // 32 fp8 = 32 bytes per MMA: +2 in the >>4 address field
-            umma_f8(d, adesc + 2ull * ks, bdesc + 2ull * ks, idesc, ks != 0 ? 1u : 0u);
+            umma_mx8(d, adesc + 2ull * ks, bdesc + 2ull * ks, idesc_mx8(BM, BNC, static_cast<uint32_t>(ks)), sfa_t,
+                     sfb_t, (kb | ks) != 0 ? 1u : 0u);
           umma_commit(&ctl->empty[stage]);
-          umma_commit(&ctl->tfull[slot]);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
+        if (ok) umma_commit(&ctl->tfull[acc]);
       }
       if (!ok) {
         record_error(p.err, ERR_TIMEOUT_MMA);
@@ -275,72 +319,49 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
     }
   } else if (warp >= 4) {
-    // ------------------------------------------------------------ epilogue: promote, judge, store
+    // ------------------------------------------------------------ epilogue: read, judge, store
     const int q = warp & 3;                // TMEM lane quarter
     const int ew = warp - 4;
     const int gi = ew >> 2;                // warpgroup: columns [64 gi, 64 gi + 64); warpgroup 0 also checksums
-    const int et = threadIdx.x - 128;
     const int row_in_tile = q * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
     unsigned long long* st = p.state + static_cast<long long>(p.slot) * 4;
     uint8_t* stg = staging + ew * 4096;
-    unsigned g = 0;
-    int it = 0;
-    bool stop = false;
-    for (int tile = blockIdx.x; tile < p.total_tiles && !stop; tile += gridDim.x, ++it) {
+    int t = 0;
+    for (int tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x, ++t) {
       int mt, nt;
       tile_coords8(p, tile, mt, nt);
       const int row = mt * BM + row_in_tile;
       const bool valid = row < p.M;
+      const int acc_i = t & 1;
+      const bool got = mbar_wait(&ctl->tfull[acc_i], (t >> 1) & 1u, abort_flag);
+      if (named_bar_or(1, 128 * EWG, !got)) {
+        if (!got) record_error(p.err, ERR_TIMEOUT_EPILOGUE);
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t ta = tmem_base + static_cast<uint32_t>(acc_i * ACC_STRIDE) + lane_off;
       float acc[HALF];
       float cs[12];
-#pragma unroll
-      for (int j = 0; j < HALF; ++j) acc[j] = 0.f;
-#pragma unroll
-      for (int j = 0; j < 12; ++j) cs[j] = 0.f;
-      // the tile's weight scales and checksum part scales -> shared memory (every epilogue thread finished the
-      // previous tile: it passed the previous tile's exchange barrier)
-      for (int i = et; i < p.kbs * 13; i += 128 * EWG)
-        scl[i] = i < p.kbs ? __ldg(p.sw + static_cast<long long>(nt) * p.kbs + i)
-                           : __ldg(p.csc + static_cast<long long>(nt) * p.kbs * 12 + (i - p.kbs));
-      named_bar_sync(3, 128 * EWG);
-      const float* sap = p.sa + static_cast<long long>(valid ? row : 0) * p.kbs;
-      float sa_n = __ldg(sap);              // the next K block's row scale is loaded before the wait
-      for (int kb = 0; kb < p.kbs; ++kb, ++g) {
-        const float s = (valid ? sa_n : 0.f) * scl[kb];
-        if (kb + 1 < p.kbs) sa_n = __ldg(sap + kb + 1);
-        const int slot = static_cast<int>(g % NSLOT);
-        const bool got = mbar_wait(&ctl->tfull[slot], (g / NSLOT) & 1u, abort_flag);
-        if (named_bar_or(1, 128 * EWG, !got)) {
-          if (!got) record_error(p.err, ERR_TIMEOUT_EPILOGUE);
-          *abort_flag = 1;
-          stop = true;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t ta = tmem_base + static_cast<uint32_t>(slot * SLOT_COLS) + lane_off;
+      {
+        uint32_t r[64];
+        uint32_t c16[16];
+        tmem_ld32(ta + gi * HALF, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+        tmem_ld32(ta + gi * HALF + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
         if (gi == 0) {
-          uint32_t c16[16];
           tmem_ld8(ta + BN, *reinterpret_cast<uint32_t(*)[8]>(&c16[0]));
           tmem_ld8(ta + BN + 8, *reinterpret_cast<uint32_t(*)[8]>(&c16[8]));
-          tmem_wait_ld();
-          const float* cp = scl + p.kbs + kb * 12;
-#pragma unroll
-          for (int j = 0; j < 12; ++j) cs[j] = fmaf(u32_as_f32(c16[j]), s * cp[j], cs[j]);
         }
-#pragma unroll
-        for (int h = 0; h < HALF / 32; ++h) {
-          uint32_t r[32];
-          tmem_ld32(ta + gi * HALF + h * 32, r);
-          tmem_wait_ld();
-#pragma unroll
-          for (int j = 0; j < 32; ++j) acc[h * 32 + j] = fmaf(u32_as_f32(r[j]), s, acc[h * 32 + j]);
-        }
+        tmem_wait_ld();
         tc_fence_before();
-        mbar_arrive(&ctl->tempty[slot]);
+        mbar_arrive(&ctl->tempty[acc_i]);   // the MMA warp may start the tile after next in this accumulator
+#pragma unroll
+        for (int j = 0; j < HALF; ++j) acc[j] = u32_as_f32(r[j]);
+#pragma unroll
+        for (int j = 0; j < 12; ++j) cs[j] = gi == 0 ? u32_as_f32(c16[j]) : 0.f;
       }
-      if (stop) break;
-      // ---- this row's 64 columns are final: injected fault, partial block sums, store
+      // ---- this row's 64 columns: injected fault, partial block sums, store
       const int c0 = nt * BN + gi * HALF;
       if (INJ && row == p.inj_row) {
 #pragma unroll
@@ -377,7 +398,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
       // ---- warpgroup 1 hands its half-block sums to warpgroup 0, which judges the block
-      float4* xb = xch + (it & 1) * 128;
+      float4* xb = xch + (t & 1) * 128;
       if (gi == 1) xb[row_in_tile] = make_float4(P, S, Q, Aab);
       named_bar_sync(2, 128 * EWG);
       if (gi == 0) {
@@ -404,7 +425,6 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (tile == 0 && q == 0) atomicAdd(st + 2, 1ull);      // one count per launch
         }
       }
-      (void)et;
     }
   }
 
@@ -419,12 +439,15 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 // ------------------------------------------------------------------------------------------- quantizer
 // One CTA of 8 warps per row; warp w takes the 128-column blocks w, w + 8, ...: amax -> s = the smallest power of
-// two with amax / s <= 448, q = E4M3(x / s) (saturating); ||dequantized row||^2 is reduced in shared memory. In check
-// mode (check != null, rows = sampled rows) the codes and scales are recomputed and compared with the stored ones
-// instead of written.
+// two with amax / s <= 448, q = E4M3(x / s) (saturating); ||dequantized row||^2 is reduced in shared memory. The
+// scale also goes, as a UE8M0 byte repeated for the block's four K slices, into the GEMM's scale-factor chunk of
+// the row's 128-row tile: sfa[(tile kbs + kb) 512 + (row % 32) 16 + 4 ((row % 128) / 32)]. In check mode
+// (check != null, rows = sampled rows) codes, scales and scale-factor words are recomputed and compared with the
+// stored ones instead of written.
 __global__ void __launch_bounds__(256) act_quant_kernel(const __nv_bfloat16* __restrict__ x, long long ldx, int M, int K,
                                                         uint8_t* __restrict__ xq, float* __restrict__ sa,
-                                                        float* __restrict__ row_sq, const int* rows, int nrows,
+                                                        uint8_t* __restrict__ sfa, float* __restrict__ row_sq,
+                                                        const int* rows, int nrows,
                                                         unsigned long long* check) {
   __shared__ float red[8];
   __shared__ int sbad;
@@ -463,11 +486,17 @@ __global__ void __launch_bounds__(256) act_quant_kernel(const __nv_bfloat16* __r
     }
     uint32_t* qp = reinterpret_cast<uint32_t*>(xq + static_cast<long long>(row) * K + c);
     float* sp = sa + static_cast<long long>(row) * kbs + kb;
+    uint32_t* fp = reinterpret_cast<uint32_t*>(sfa + (static_cast<long long>(row >> 7) * kbs + kb) * 512 +
+                                               (row & 31) * 16 + ((row & 127) >> 5) * 4);
+    const uint32_t sfw = ((__float_as_uint(s) >> 23) & 0xffu) * 0x01010101u;   // s = 2^e: UE8M0 byte e + 127
     if (check == nullptr) {
       *qp = codes;
-      if (lane == 0) *sp = s;
+      if (lane == 0) {
+        *sp = s;
+        *fp = sfw;
+      }
     } else {
-      const bool diff = *qp != codes || (lane == 0 && !(*sp == s));
+      const bool diff = *qp != codes || (lane == 0 && (!(*sp == s) || *fp != sfw));
       const unsigned m = __ballot_sync(0xffffffffu, diff);
       if (lane == 0 && m) atomicMin(&sbad, kb * 128 + (__ffs(m) - 1) * 4);
     }
@@ -507,15 +536,16 @@ static int launch8(const CUtensorMap& a, const CUtensorMap& w, const CUtensorMap
 
 extern "C" {
 
-// A_q [M][K] E4M3 codes with scales sa [M][K/128]; W_q [N][K] with scales sw [N/128][K/128]; Wc_q [16 N/128][K]
-// checksum rows with part scales csc [N/128][K/128][12]. N and K must be multiples of 128.
-int sdc_gemm_fp8(const void* Aq, const float* sa, const void* Wq, const void* Wcq, const float* sw, const float* csc,
-                 int M, int N, int K, void* Cout, long long ldc, const float* row_sq, const float* wstat,
+// A_q [M][K] E4M3 codes with scale-factor chunks sfa [ceil(M/128)][K/128][512] (sdc_fp8_quant_act); W_q [N][K],
+// Wc_q [16 N/128][K] checksum rows, sfb [N/128][K/128][1024] the scale-factor chunks of each block's 144-row B
+// operand (ops/fp8.py). N and K must be multiples of 128; sfa and sfb 16-byte aligned.
+int sdc_gemm_fp8(const void* Aq, const void* sfa, const void* Wq, const void* Wcq, const void* sfb, int M, int N, int K, void* Cout, long long ldc, const float* row_sq, const float* wstat,
                  unsigned long long* state, int slot, unsigned s0, unsigned s1, unsigned s2, unsigned s3, float zthr,
                  float prod_coef, float out_coef, float abs_floor, float bound_coef, int* err, int inj_row,
                  int inj_col, unsigned inj_xor, void* stream) {
   if (M <= 0) return 0;
   if (N <= 0 || K <= 0 || N % BN || K % BK || K / BK > MAX_KBS || ldc % 8) return -1;
+  if ((reinterpret_cast<uintptr_t>(sfa) | reinterpret_cast<uintptr_t>(sfb)) & 15) return -7;
   Params8 p;
   std::memset(&p, 0, sizeof(p));
   p.M = M;
@@ -530,9 +560,8 @@ int sdc_gemm_fp8(const void* Aq, const float* sa, const void* Wq, const void* Wc
     int g = static_cast<int>((24ll << 20) / band);
     p.group = g < 1 ? 1 : (g > 16 ? 16 : (g > p.m_tiles ? p.m_tiles : g));
   }
-  p.sa = sa;
-  p.sw = sw;
-  p.csc = csc;
+  p.sfa = static_cast<const uint8_t*>(sfa);
+  p.sfb = static_cast<const uint8_t*>(sfb);
   p.row_sq = row_sq;
   p.wstat = reinterpret_cast<const float4*>(wstat);
   p.C = static_cast<__nv_bfloat16*>(Cout);
@@ -565,15 +594,17 @@ int sdc_gemm_fp8(const void* Aq, const float* sa, const void* Wq, const void* Wc
   return inj_row >= 0 ? launch8<true>(ma, mw, mc, mo, p, grid, st) : launch8<false>(ma, mw, mc, mo, p, grid, st);
 }
 
-// x [M][K] bf16 (row stride ldx) -> xq [M][K] E4M3 codes, sa [M][K/128], row_sq [M]. rows / check: replay mode.
-int sdc_fp8_quant_act(const void* x, long long ldx, int M, int K, void* xq, float* sa, float* row_sq, const int* rows,
-                      int nrows, void* check, void* stream) {
-  if (K % 128 || ldx % 4) return -1;
+// x [M][K] bf16 (row stride ldx) -> xq [M][K] E4M3 codes, sa [M][K/128], sfa [ceil(M/128)][K/128][512] UE8M0
+// scale-factor chunks (bytes of rows >= M are left as they are), row_sq [M]. rows / check: replay mode.
+int sdc_fp8_quant_act(const void* x, long long ldx, int M, int K, void* xq, float* sa, void* sfa, float* row_sq,
+                      const int* rows, int nrows, void* check, void* stream) {
+  if (K % 128 || ldx % 4 || (reinterpret_cast<uintptr_t>(sfa) & 3)) return -1;
   const int n = rows ? nrows : M;
   if (n <= 0) return 0;
   auto st = static_cast<cudaStream_t>(stream);
   act_quant_kernel<<<static_cast<unsigned>(n), 256, 0, st>>>(
-      static_cast<const __nv_bfloat16*>(x), ldx, M, K, static_cast<uint8_t*>(xq), sa, row_sq, rows, nrows,
+      static_cast<const __nv_bfloat16*>(x), ldx, M, K, static_cast<uint8_t*>(xq), sa, static_cast<uint8_t*>(sfa),
+      row_sq, rows, nrows,
       static_cast<unsigned long long*>(check));
   return static_cast<int>(cudaGetLastError());
 }

@@ -11,6 +11,11 @@ Checksum rows: for each 128-column block b of W and each 128-wide K block kb, th
 the block's quantized rows (sums of E4M3 values, exact in fp32) are split into six E4M3 parts, each with its own
 power-of-two scale (`csc`), so 12 rows of fp8 carry about 24 significant bits; they are rows 16 b .. 16 b + 11 of
 `wcq` (rows 12 to 15 zero) and ride in the same MMA as the tile's 128 weight rows.
+
+Scale factors go to the tensor cores as UE8M0 bytes (the power-of-two scale 2^e is the byte e + 127) in 512-byte
+chunks, one per 128 operand rows and 128-wide K block: row r at byte (r % 32) 16 + 4 (r // 32) + j for its four
+32-wide K slices j (`sf_chunks`). The B operand of block b has two chunks per K block: its 128 weight rows (all the
+block's scale) and its 16 checksum rows (part scale x block scale).
 """
 from __future__ import annotations
 
@@ -39,6 +44,26 @@ def pow2_scale(amax: torch.Tensor) -> torch.Tensor:
 
 def to_e4m3(x: torch.Tensor) -> torch.Tensor:
     return x.clamp(-FP8_MAX, FP8_MAX).to(torch.float8_e4m3fn)
+
+
+def ue8m0(s: torch.Tensor) -> torch.Tensor:
+    """UE8M0 byte of power-of-two scales (2^e -> e + 127); 0 (an all-zero part) -> 127, i.e. 1.0."""
+    s = s.float()
+    b = (s.view(torch.int32) >> 23) & 0xFF
+    return torch.where(s > 0, b, torch.full_like(b, 127)).to(torch.uint8)
+
+
+def sf_chunks(sc: torch.Tensor) -> torch.Tensor:
+    """(..., rows, kbs) scales of a 128 x rows-padded operand -> (..., ceil(rows / 128), kbs, 512) UE8M0 chunks."""
+    *lead, rows, kbs = sc.shape
+    t = -(-rows // 128)
+    b = torch.full((*lead, t * 128, kbs), 127, dtype=torch.uint8, device=sc.device)
+    b[..., :rows, :] = ue8m0(sc)
+    n = len(lead)
+    b = b.view(*lead, t, 4, 32, kbs)                                     # (..., t, r // 32, r % 32, kb)
+    b = b.permute(*range(n), n, n + 3, n + 2, n + 1)                     # (..., t, kb, r % 32, r // 32)
+    b = b.unsqueeze(-1).expand(*lead, t, kbs, 32, 4, 4)                  # (..., t, kb, r % 32, r // 32, j)
+    return b.reshape(*lead, t, kbs, 512).contiguous()
 
 
 class Fp8Weight:
@@ -72,6 +97,12 @@ class Fp8Weight:
                 r = r - part * sc[..., None]
         self.wcq = to_e4m3(rows).view(self.nb * 16, self.kbs * 128).contiguous()
         self.csc = csc.contiguous()
+        # scale-factor chunks of each block's 144-row B operand: 128 weight rows, 12 checksum parts, 116 unused. The
+        # parts split sums of codes, so their scale factors are the part scale times the block's weight scale.
+        bs = torch.zeros(self.nb, 256, self.kbs, dtype=torch.float32, device=dev)
+        bs[:, :128] = self.sw[:, None, :]
+        bs[:, 128:140] = (csc * self.sw[:, :, None]).transpose(1, 2)     # parts of sums of codes, times the block scale
+        self.sfb = sf_chunks(bs).transpose(1, 2).reshape(self.nb, self.kbs, 1024).contiguous()
         dq = deq.view(self.nb, 128, k).double()
         pl, sg = dq.sum(1), (dq * s.view(1, 128, 1).double()).sum(1)
         self.wstat = torch.stack([torch.linalg.vector_norm(dq, dim=(1, 2)), torch.linalg.vector_norm(pl, dim=1),
@@ -87,6 +118,7 @@ class Fp8Act:
     q: torch.Tensor         # (m, k) float8_e4m3fn
     sa: torch.Tensor        # (m, k / 128) fp32 powers of two
     row_sq: torch.Tensor    # (m,) ||dequantized row||^2
+    sf: torch.Tensor        # (ceil(m / 128), k / 128, 512) uint8 UE8M0 scale-factor chunks
 
     def dequantized(self) -> torch.Tensor:
         m, k = self.q.shape
@@ -101,9 +133,10 @@ def quantize_act(x: torch.Tensor, out: Optional[Fp8Act] = None, rows: Optional[t
     if out is None:
         out = Fp8Act(torch.empty(m, k, dtype=torch.float8_e4m3fn, device=x.device),
                      torch.empty(m, k // 128, dtype=torch.float32, device=x.device),
-                     torch.empty(m, dtype=torch.float32, device=x.device))
+                     torch.empty(m, dtype=torch.float32, device=x.device),
+                     torch.full((-(-m // 128), k // 128, 512), 127, dtype=torch.uint8, device=x.device))
     _native.check(_native.lib().sdc_fp8_quant_act(
-        x.data_ptr(), x.stride(0), m, k, out.q.data_ptr(), out.sa.data_ptr(), out.row_sq.data_ptr(),
+        x.data_ptr(), x.stride(0), m, k, out.q.data_ptr(), out.sa.data_ptr(), out.sf.data_ptr(), out.row_sq.data_ptr(),
         None if rows is None else rows.data_ptr(), 0 if rows is None else rows.numel(),
         None if check is None else check.data_ptr(), _stream_ptr(x.device)), "fp8 quantize")
     return out
@@ -120,8 +153,7 @@ def checked_linear_fp8(xa: Fp8Act, fw: Fp8Weight, state: torch.Tensor, slot: int
     s = fw.mask
     ir, ic, ix = (-1, -1, 0) if inject is None else (int(inject[0]), int(inject[1]), int(inject[2]))
     _native.check(_native.lib().sdc_gemm_fp8(
-        xa.q.data_ptr(), xa.sa.data_ptr(), fw.wq.data_ptr(), fw.wcq.data_ptr(), fw.sw.data_ptr(), fw.csc.data_ptr(),
-        m, fw.n, k, out.data_ptr(), out.stride(0), xa.row_sq.data_ptr(), fw.wstat.data_ptr(), state.data_ptr(),
+        xa.q.data_ptr(), xa.sf.data_ptr(), fw.wq.data_ptr(), fw.wcq.data_ptr(), fw.sfb.data_ptr(), m, fw.n, k, out.data_ptr(), out.stride(0), xa.row_sq.data_ptr(), fw.wstat.data_ptr(), state.data_ptr(),
         int(slot), s[0], s[1], s[2], s[3], float(z_alarm), float(fw.prod_coef), float(fw.out_coef),
         float(abft.ABS_FLOOR), float(math.sqrt(k)), error_word(dev).data_ptr(), ir, ic, ix, _stream_ptr(dev)),
         "fp8 checked GEMM")
@@ -136,7 +168,7 @@ class Fp8Linears:
         self.device = torch.device(device)
         self.weights: dict[str, Fp8Weight] = {}
         self.cap = (0, 0)
-        self._q = self._sa = self._rs = None
+        self._q = self._sa = self._rs = self._sf = None
 
     def add(self, name: str, weight: torch.Tensor) -> Fp8Weight:
         fw = Fp8Weight(weight)
@@ -152,11 +184,15 @@ class Fp8Linears:
         self._q = torch.empty(rows * k, dtype=torch.float8_e4m3fn, device=self.device)
         self._sa = torch.empty(rows * (k // 128), dtype=torch.float32, device=self.device)
         self._rs = torch.empty(rows, dtype=torch.float32, device=self.device)
+        # bytes of rows past m are never written: 127 (1.0) keeps the padded MMA rows finite
+        self._sf = torch.full((-(-rows // 128) * (k // 128) * 512,), 127, dtype=torch.uint8, device=self.device)
         self.cap = (rows, k)
 
     def act(self, m: int, k: int) -> Fp8Act:
         self.reserve(m, k)
-        return Fp8Act(self._q[: m * k].view(m, k), self._sa[: m * (k // 128)].view(m, k // 128), self._rs[:m])
+        t = -(-m // 128)
+        return Fp8Act(self._q[: m * k].view(m, k), self._sa[: m * (k // 128)].view(m, k // 128), self._rs[:m],
+                      self._sf[: t * (k // 128) * 512].view(t, k // 128, 512))
 
     def linear(self, name: str, x: torch.Tensor, state: torch.Tensor, slot: int, out: torch.Tensor,
                qcheck: Optional[torch.Tensor] = None, sample: Optional[torch.Tensor] = None) -> torch.Tensor:
