@@ -1,4 +1,5 @@
-"""Builds the native library `sdcguard_b200/_lib/libsdcguard_b200.so` from `csrc/*.cu` and `csrc/*.cpp`.
+"""Builds the native library `sdcguard_b200/_lib/libsdcguard_b200.so` from `csrc/*.cu` and `csrc/*.cpp`, and the
+host-only probe library `_lib/libsdcguard_host.so` from `csrc/host/*.cpp`.
 
 Every CUDA source is compiled for sm_100a only (`-gencode arch=compute_100a,code=sm_100a`) with nvcc, in
 parallel, into objects under `_lib/obj/`, then linked into one shared library that Python loads with ctypes
@@ -23,6 +24,8 @@ SRC = PKG / "csrc"
 OUT = PKG / "_lib"
 OBJ = OUT / "obj"
 LIB = OUT / "libsdcguard_b200.so"
+HOST_SRC = SRC / "host"
+HOST_LIB = OUT / "libsdcguard_host.so"     # host-only C++ (cuBLAS / cuBLASLt probe), linked to the CUDA libraries
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVFLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
@@ -88,6 +91,23 @@ def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = Fals
     return LIB
 
 
+def build_host(force: bool = False) -> Path:
+    """The host-only library: `csrc/host/*.cpp` with g++, linked to cuBLAS, cuBLASLt and the CUDA runtime."""
+    srcs = sorted(HOST_SRC.glob("*.cpp"))
+    OUT.mkdir(parents=True, exist_ok=True)
+    if not force and HOST_LIB.exists() and HOST_LIB.stat().st_mtime >= max(p.stat().st_mtime for p in srcs):
+        return HOST_LIB
+    home = cuda_home()
+    tmp = HOST_LIB.with_suffix(".so.tmp")
+    cmd = ["g++", *CXXFLAGS, "-shared", "-I", str(home / "include"), *map(str, srcs), "-o", str(tmp),
+           "-L", str(home / "lib64"), f"-Wl,-rpath,{home / 'lib64'}", "-lcublasLt", "-lcublas", "-lcudart"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"building the host library failed:\n{' '.join(cmd)}\n{r.stdout}\n{r.stderr}")
+    os.replace(tmp, HOST_LIB)
+    return HOST_LIB
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--force", action="store_true")
@@ -95,6 +115,7 @@ def main(argv=None) -> int:
     ap.add_argument("-v", "--verbose", action="store_true")
     a = ap.parse_args(argv)
     print(build(force=a.force, verbose=a.verbose, ptxas_verbose=a.ptxas_verbose))
+    print(build_host(force=a.force))
     return 0
 
 

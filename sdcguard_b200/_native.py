@@ -73,6 +73,11 @@ SIGNATURES: dict[str, tuple] = {
     "sdc_gemm_bf16_push": (I, [P, L, P, P, I, I, I, P, P, F, P, P, P, P, I, U, U, U, U, F, F, F, F, F, P, I, I, I, U,
                                I, I, L, P, P, P, P, P, P]),
     "sdc_tp_reduce_local": (I, [P, P, P, P, I, I, I, I, L, P, F, P, P, P]),
+    "sdc_screen_fma": (I, [L, U64, I, L, P, P]),
+    "sdc_screen_special": (I, [L, U64, L, P, P, P]),
+    "sdc_screen_compare": (I, [L, P, P, P, P, L, P, P]),
+    "sdc_screen_mem_fill": (I, [P, L, L, U64, I, P]),
+    "sdc_screen_mem_check": (I, [P, L, L, U64, I, L, P, P]),
     "sdc_gemm_fp8": (I, [P, P, P, P, P, I, I, I, P, L, P, P, P, I, U, U, U, U, F, F, F, F, F, P, I, I, U, P]),
     "sdc_fp8_quant_act": (I, [P, L, I, I, P, P, P, P, P, I, P, P]),
     "sdc_ep_dispatch": (I, [P, P, I, I, I, I, I, I, I, P, P, P, P, P, P, P, P, I, I, I, P]),
