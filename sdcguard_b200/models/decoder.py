@@ -213,13 +213,22 @@ class CheckedDecoder:
         return self._bufs["dscratch"]
 
     # ---------------------------------------------------------------- ops
+    def inject_next(self, name: str, row: int, col: int, xor_bits: int) -> None:
+        """Fault injection: the next eager (not graph-captured) bf16 GEMM of layer `name` (e.g. "L0.down") flips
+        `xor_bits` of its fp32 accumulator (row, col) before the check and the rounding."""
+        self._inject = (name, (row, col, xor_bits))
+
     def _linear(self, x, w, cw, name, out, row_sq, sample=None):
         if self.precision == "fp8":
             return self.fp8.linear(name, x, self.state.state, self.slot[name], out,
                                    qcheck=self.state.state[self.slot[name + ".q"]], sample=sample)
         if not self.checked:
             return torch.matmul(x, w.t(), out=out)
-        return gemm.checked_linear(x, cw, self.state.state, self.slot[name], row_sq=row_sq, out=out)
+        inj = None
+        if getattr(self, "_inject", None) and self._inject[0] == name and \
+                not torch.cuda.is_current_stream_capturing():
+            inj, self._inject = self._inject[1], None
+        return gemm.checked_linear(x, cw, self.state.state, self.slot[name], row_sq=row_sq, out=out, inject=inj)
 
     def _st(self, name) -> torch.Tensor:
         return self.state.state[self.slot[name]]

@@ -9,7 +9,9 @@ provider detection are not part of this card.
 from __future__ import annotations
 
 import argparse
+import hashlib
 import json
+import os
 import time
 
 import torch
@@ -67,11 +69,46 @@ def run(device="cuda:0", seconds: float = 20.0, size: int = 8192, seed: int = 0)
         copies += 1
     torch.cuda.synchronize()
     r = st.read()[0]
-    return {"device": torch.cuda.get_device_name(dev), "gemm_size": size,
+    # output fingerprint: the checked GEMM is deterministic, so every healthy GPU of a model gives the same bits
+    gemm.checked_linear(x, cw, st.state, slot, row_sq=rs, out=y)
+    fp = hashlib.sha256(y.view(torch.int16).cpu().numpy().tobytes()).hexdigest()[:32]
+    return {"device": torch.cuda.get_device_name(dev), "gemm_size": size, "seed": seed, "seconds": seconds,
+            "output_fingerprint": fp,
             "checked_gemm_tflops": round(flops / ms_checked / 1e9, 1), "cublas_gemm_tflops": round(flops / ms_cublas / 1e9, 1),
             "d2d_gbs": round(2 * src.numel() * 2 / ms_copy / 1e6, 1),
             "gemm_checks": r["checks"], "gemm_wrong": int(r["z"] > abft.Z_ALARM), "worst_z": round(r["z"], 3),
             "gemms": gemms, "copies_verified": copies * pages, "copies_wrong": wrong_copies}
+
+
+SCHEMA = "sdcguard-b200-check/1"
+
+
+def card(res: dict, device="cuda:0") -> dict:
+    """A shareable card: the result, hashed hardware identity, versions, a fingerprint of the deterministic GEMM
+    output keyed by the exact setup, and a digest of the card's contents (board.validate checks it)."""
+    from .screen_ops import smi
+    dev = torch.device(device)
+    tel = smi(dev.index)
+    ident = tel.get("uuid") or tel.get("serial") or ""
+    c = {"schema": SCHEMA, "result": "PASS" if res["gemm_wrong"] == 0 and res["copies_wrong"] == 0 else "FAIL",
+         "gpu": {"name": res["device"], "id_hash": hashlib.sha256(ident.encode()).hexdigest()[:16] if ident else None,
+                 "driver": tel.get("driver_version")},
+         "versions": {"torch": torch.__version__, "cuda": torch.version.cuda},
+         "minutes": round(res["seconds"] / 60, 3),
+         "speed": {"checked_tflops": res["checked_gemm_tflops"], "cublas_tflops": res["cublas_gemm_tflops"],
+                   "d2d_gbs": res["d2d_gbs"]},
+         "checked": {"gemm_checks": res["gemm_checks"], "copies_verified": res["copies_verified"],
+                     "wrong": res["gemm_wrong"] + res["copies_wrong"], "worst_z": res["worst_z"]},
+         "fingerprint": {"key": f"{res['device']}|{res['gemm_size']}|{res['seed']}|{torch.version.cuda}",
+                         "output": res["output_fingerprint"]},
+         "provider": os.environ.get("SDCGUARD_PROVIDER", "not stated")}
+    c["digest"] = card_digest(c)
+    return c
+
+
+def card_digest(c: dict) -> str:
+    body = {k: v for k, v in c.items() if k != "digest"}
+    return hashlib.sha256(json.dumps(body, sort_keys=True, separators=(",", ":")).encode()).hexdigest()[:32]
 
 
 def main(argv=None) -> int:
@@ -81,11 +118,15 @@ def main(argv=None) -> int:
     ap.add_argument("--size", type=int, default=8192)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--json", action="store_true")
+    ap.add_argument("--share", help="write the shareable card (board input) to this file")
     a = ap.parse_args(argv)
     if not torch.cuda.is_available():
         print("sdcguard check: no CUDA device")
         return 1
     res = run(a.device, a.seconds, a.size, a.seed)
+    if a.share:
+        with open(a.share, "w") as f:
+            json.dump(card(res, a.device), f, indent=1)
     if a.json:
         print(json.dumps(res, sort_keys=True))
     else:

@@ -36,3 +36,25 @@ def test_math_modes_gpu_clean():
     r = modes.screen("cuda:0", shape=(512, 1024, 512))
     assert r["verdict"] == "pass", r
     assert len(r["modes"]) >= 5, r["skipped"]
+
+
+def test_workload_screen_clean_then_simulated_failure_with_evidence(tmp_path):
+    from sdcguard_b200.tools import screen
+    r = screen.run("cuda:0", "tiny", minutes=0, rounds=1)
+    assert r["verdict"] == "PASS" and r["checks"] > 0 and r["rounds"][0]["mismatched_tokens"] == 0, r
+    r = screen.run("cuda:0", "tiny", minutes=0, rounds=1, simulate=True, out_dir=str(tmp_path))
+    assert r["verdict"] == "FAIL" and r["failed_rounds"] == [0], r
+    ev = r["rounds"][0]["evidence"]
+    assert any("down" in str(e["detail"]) for e in r["rounds"][0]["events"]), r["rounds"][0]["events"]
+    rp = screen.replay(ev)
+    assert rp["reproducible"] is False and rp["alarms"] == 0, rp      # an injected flip does not come back
+
+
+def test_check_card_is_valid_board_input():
+    from sdcguard_b200.tools import board, check
+    res = check.run("cuda:0", seconds=1.0, size=2048)
+    c = check.card(res)
+    c["minutes"] = 1.0          # the board counts cards of a minute or more; this test checks for one second
+    c["digest"] = check.card_digest(c)
+    assert board.validate(c) is None and c["result"] == "PASS", c
+    assert len(c["fingerprint"]["output"]) == 32
