@@ -1,0 +1,80 @@
+"""Server probes against fakes (no GPU): readiness verdicts from metrics, isolation and consistency against a
+deterministic fake model, throughput bookkeeping, and the stack-change decision."""
+from sdcguard_b200.tools import _client, consistency, decide, isolation, perf, ready
+
+
+def _next(ctx):
+    return (sum(ctx) * 31 + len(ctx)) % 1000
+
+
+def fake_complete(base, prompt, n):
+    ctx, out = list(prompt), []
+    for _ in range(n):
+        t = _next(ctx)
+        out.append(t)
+        ctx.append(t)
+    return out
+
+
+def _metrics(checks, tokens, alarms=0, protected=1, ops=10, ops_checked=10, polls=3, started="1", line=6.0):
+    return _client.parse_metrics(
+        f"sdcguard_protected {protected}\nsdcguard_checks_total {checks}\nsdcguard_alarms_total {alarms}\n"
+        f"sdcguard_ops_total {ops}\nsdcguard_ops_checked {ops_checked}\nsdcguard_alarm_line {line}\n"
+        f"sdcguard_polls_total {polls}\nsdcguard_generated_tokens_total {tokens}\n"
+        f'sdcguard_worker_info{{gpu="B200",uuid="u",pid="7",started="{started}"}} 1\n'
+        f'sdcguard_stack_info{{model="tiny",precision="bf16",weights_digest="abc"}} 1\n')
+
+
+def test_ready_verdicts():
+    assert ready.judge(_metrics(10, 5), _metrics(20, 9))["verdict"] == "PROTECTED"
+    assert ready.judge(_metrics(10, 5), _metrics(10, 5))["verdict"] == "IDLE"
+    assert ready.judge(_metrics(10, 5), _metrics(10, 9))["verdict"] == "NOT PROTECTED"      # tokens, no checks
+    assert ready.judge(_metrics(10, 5), _metrics(20, 9, alarms=1))["verdict"] == "FAULT FOUND"
+    assert ready.judge(_metrics(10, 5), _metrics(20, 9, protected=0))["verdict"] == "NOT PROTECTED"
+    assert ready.judge(_metrics(10, 5), _metrics(20, 9, line=1000))["verdict"] == "NOT PROTECTED"
+    assert ready.judge(_metrics(10, 5), _metrics(20, 9, started="2"))["verdict"] == "NOT PROTECTED"
+    assert ready.judge(_metrics(10, 5), _metrics(20, 9, ops_checked=8))["verdict"] == "NOT PROTECTED"
+    assert ready.judge(None, _metrics(1, 1))["verdict"] == "NOT PROTECTED"
+    dec = {"decision": "ACCEPT", "candidate_stack": {"model": "tiny", "precision": "fp8", "weights_digest": "abc"}}
+    q = ready.qualified(_metrics(1, 1), dec)
+    assert q["verdict"] == "NOT THE QUALIFIED STACK" and "precision" in q["why"][0]
+
+
+def test_isolation_consistency_perf_on_fake_model():
+    assert isolation.run("x", probes=2, primers=3, complete=fake_complete)["verdict"] == "ISOLATED"
+    assert consistency.run("x", probes=2, complete=fake_complete)["verdict"] == "CONSISTENT"
+    calls = [0]
+
+    def flaky(base, prompt, n):          # the 3rd call (the batched one) differs: a batch-dependent server
+        calls[0] += 1
+        out = fake_complete(base, prompt, n)
+        return [out[0] + 1] + out[1:] if calls[0] == 3 else out
+
+    assert isolation.run("x", probes=1, primers=0, complete=flaky)["verdict"] == "INFLUENCED"
+
+    def bad_prefill(base, prompt, n):
+        out = fake_complete(base, prompt, n)
+        return [(out[0] + 1) % 1000] if n == 1 else out
+
+    r = consistency.run("x", probes=1, complete=bad_prefill)
+    assert r["verdict"] == "INCONSISTENT" and len(r["mismatches"]) == 4
+    p = perf.run("x", clients=2, prompt=8, tokens=4, seconds=0.2, max_requests=10, complete=fake_complete)
+    assert p["requests"] == 10 and p["errors"] == 0 and p["latency_ms"]["p50"] is not None
+
+
+def _result(tps=100.0, alarms=0, iso="ISOLATED", cons="CONSISTENT", readyv="PROTECTED", checks=50):
+    text = (f"sdcguard_protected 1\nsdcguard_checks_total {checks}\nsdcguard_alarms_total {alarms}\n"
+            "sdcguard_ops_total 4\nsdcguard_ops_checked 4\n")
+    return {"ready": {"verdict": readyv}, "perf": {"total_tokens_per_s": tps, "errors": 0},
+            "isolation": {"verdict": iso, "failed": 0}, "consistency": {"verdict": cons, "checks": 4},
+            "metrics": text, "stack": {"model": "tiny"}}
+
+
+def test_decide_sections():
+    assert decide.decide(_result(), _result(95.0))["decision"] == "ACCEPT"
+    d = decide.decide(_result(), _result(50.0))
+    assert d["decision"] == "REJECT" and d["failed"] == ["performance"]
+    assert decide.decide(_result(), _result(50.0), {"waive": ["performance"]})["decision"] == "ACCEPT"
+    assert decide.decide(_result(), _result(alarms=2))["decision"] == "REJECT"
+    assert decide.decide(_result(), _result(checks=0))["decision"] == "INCONCLUSIVE"
+    assert decide.decide(_result(), _result(iso="INFLUENCED"))["failed"] == ["isolation"]
