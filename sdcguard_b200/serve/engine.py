@@ -279,6 +279,32 @@ class LLMEngine:
         if max_new_tokens > 1:
             self._decode([int(x) for x in plens], self.block_tables(pages), out_tokens, max_new_tokens)
 
+    def score(self, seqs: Sequence[Sequence[int]], topk: int = 20) -> list[tuple[torch.Tensor, torch.Tensor]]:
+        """Teacher-forced log-probabilities: for every sequence, one prefill over all its tokens with logits at every
+        position; returns per sequence (values, ids) of the top-k log-softmax entries, (len, topk) on the host.
+        Position p's distribution is the prediction of token p + 1. Checks run as in any prefill."""
+        dev = self.device
+        group = self.model.nq // self.model.nkv
+        out = []
+        for ids in seqs:
+            n = len(ids)
+            if n > self.max_prefill_tokens:
+                raise ValueError(f"sequence of {n} tokens exceeds max_prefill_tokens {self.max_prefill_tokens}")
+            pages = self.alloc.alloc(-(-n // PAGE))
+            try:
+                meta = StepMeta(
+                    mode="prefill", tokens=torch.tensor(list(ids), dtype=torch.long).to(dev),
+                    pos=torch.arange(n, dtype=torch.int32).to(dev),
+                    slots=torch.tensor([pages[p // PAGE] * PAGE + p % PAGE for p in range(n)], dtype=torch.int64).to(dev),
+                    block_table=self.block_tables([pages]), logits_rows=torch.arange(n, dtype=torch.int64).to(dev),
+                    tiles=attention.prefill_tiles([0], [n], group).to(dev))
+                logits = self.model.forward(meta, self.cache)
+                v, i = torch.log_softmax(logits.float(), -1).topk(topk, -1)
+                out.append((v.cpu(), i.cpu()))
+            finally:
+                self.alloc.release(pages)
+        return out
+
     def generate(self, prompts: torch.Tensor, prompt_lens: Sequence[int], max_new_tokens: int) -> torch.Tensor:
         """prompts: (N, max_len) int64 token ids (ideally pinned host memory); returns (N, max_new_tokens) int64
         generated ids on the host. Greedy decoding, no early stop (synthetic workloads)."""

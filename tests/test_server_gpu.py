@@ -65,3 +65,42 @@ def test_qualify_and_decide(tmp_path):
     assert d["sections"]["arithmetic"]["verdict"] == "NO FAULT OBSERVED", d
     assert d["decision"] == "ACCEPT", json.dumps(d["sections"])
     assert d["candidate_stack"]["precision"] == "fp8"
+
+
+def test_gate_model_same_stack_passes_and_fp8_is_scored():
+    from sdcguard_b200.tools import gate_model
+    ref = gate_model.reference("tiny", prompts=4, prompt_len=48, new=16)
+    assert ref["recorded_is_top1"] > 0.9, ref["recorded_is_top1"]
+    same = gate_model.check(ref)
+    assert same["verdict"] == "PASS" and same["mean_kl"] < 1e-6 and same["top1_agreement"] == 1.0, same
+    assert same["alarms"] == 0
+    f8 = gate_model.check(ref, precision="fp8", noise=same)
+    assert f8["mean_kl"] > 0 and f8["verdict"] in ("PASS", "WARN", "FAIL") and f8["alarms"] == 0, f8
+
+
+def test_case_capture_replay_and_investigate(tmp_path):
+    """A GEMM accumulator flip captured as a case: the recheck shows the output was wrong, replays on this GPU do
+    not reproduce it, the casefile calls it a transient fault and investigate says NOT REPRODUCED."""
+    import torch
+
+    from sdcguard_b200.ops import gemm
+    from sdcguard_b200.tools import casefile, investigate
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(256, 1024, generator=g).bfloat16().cuda()
+    w = (torch.randn(512, 1024, generator=g) * 0.03).bfloat16().cuda()
+    cw = gemm.CheckedWeight(w)
+    st = gemm.StateTable("cuda:0", 2)
+    slot = st.add("t", cw.nb)
+    y = gemm.checked_linear(x, cw, st.state, slot, inject=(7, 300, 1 << 29))
+    d = st.read()[0]
+    assert d["row"] == 7 and d["block"] == 2
+    case = casefile.capture(x, w, y, d["row"], d["block"])
+    p = str(tmp_path / "case.pt")
+    casefile.save(case, p)
+    case = torch.load(p, weights_only=False)
+    assert casefile.recheck(case)["output_wrong"]
+    rep = casefile.replay(case, 12)
+    assert not rep["reproduced"], rep
+    cf = casefile.casefile(case, [rep])
+    assert cf["outcome"] == "most consistent with: transient fault on the incident GPU", cf
+    assert investigate.investigate(case, 4, ["cuda:0"])["verdict"] == "NOT REPRODUCED"

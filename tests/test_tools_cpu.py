@@ -52,3 +52,74 @@ def test_known_issue_verdicts():
     assert hop["6862950"] == "applies"
     hop = {r["id"]: r["verdict"] for r in known_issues.match({"cublas": (12, 8, 0), "cc": "9.0"})}
     assert hop["6862950"] == "not active"
+
+
+def test_gate_model_kl_and_verdict_lines():
+    import math
+
+    import torch
+
+    from sdcguard_b200.tools import gate_model
+    v = torch.log(torch.tensor([0.5, 0.3, 0.2]))
+    i = torch.tensor([4, 7, 9])
+    assert abs(gate_model.compare_position(v, i, v, i)) < 1e-12
+    # candidate moved mass from token 4 to 7 and lists a new token 11
+    cv = torch.log(torch.tensor([0.4, 0.4, 0.2]))
+    kl = gate_model.compare_position(v, i, cv, torch.tensor([4, 7, 11]))
+    assert kl > 0.01
+    base = {"mean_kl": 1e-4, "top1_agreement": 1.0, "worst_prompt_kl": 1e-3, "positions": 1000}
+    assert gate_model.verdict(base)["verdict"] == "PASS"
+    assert gate_model.verdict({**base, "mean_kl": 5e-3})["verdict"] == "WARN"
+    assert gate_model.verdict({**base, "top1_agreement": 0.9})["verdict"] == "FAIL"
+    noisy = {"mean_kl": 2e-3, "top1_agreement": 0.985, "worst_prompt_kl": 0.04}
+    assert gate_model.verdict({**base, "mean_kl": 5e-3, "top1_agreement": 0.984}, noisy)["verdict"] == "PASS"
+    assert math.isclose(gate_model.verdict(base, noisy)["lines"]["pass_kl"], 6e-3)
+
+
+def _case(wrong=True):
+    import torch
+
+    from sdcguard_b200.tools import casefile
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(4, 256, generator=g).bfloat16()
+    w = (torch.randn(256, 256, generator=g) * 0.05).bfloat16()
+    y = (x.float() @ w.float().t()).bfloat16()
+    if wrong:
+        y[2, 130] = y[2, 130] * 4 + 1
+    c = casefile.capture(x, w, y, 2, 1)
+    c["stack"] = {"torch": "t", "cuda": "c", "gpu_name": "B200", "gpu_uuid": "GPU-A", "cublas": None, "cc": None}
+    return c
+
+
+def test_casefile_explanations():
+    from sdcguard_b200.tools import casefile
+    c = _case()
+    rc = casefile.recheck(c)
+    assert rc["output_wrong"] and rc["first_bad_column"] == 130
+    h = casefile.sha256(c)
+    st = dict(c["stack"])
+    here = {"case_sha256": h, "gpu_uuid": "GPU-A", "stack": st, "runs": 20, "reproduced": 0}
+    peer = {"case_sha256": h, "gpu_uuid": "GPU-B", "stack": {**st, "gpu_uuid": "GPU-B"}, "runs": 20, "reproduced": 0}
+    r = casefile.casefile(c, [here, peer])
+    assert r["outcome"] == "most consistent with: transient fault on the incident GPU", r
+    r = casefile.casefile(c, [{**here, "reproduced": 5}, peer])
+    assert r["outcome"] == "most consistent with: persistent defect of the incident GPU", r
+    r = casefile.casefile(c, [{**here, "reproduced": 5}, {**peer, "reproduced": 3}])
+    assert r["outcome"] == "most consistent with: software or library defect", r
+    r = casefile.casefile(c, [{**here, "case_sha256": "other"}])
+    assert r["outcome"] == "INCONCLUSIVE" and r["replays"]["ignored_other_case"] == 1 and r["next_steps"]
+    ok = _case(wrong=False)
+    assert casefile.casefile(ok, [])["outcome"] == "most consistent with: false alarm of the check"
+
+
+def test_investigate_classification():
+    from sdcguard_b200.tools.investigate import classify
+    ok = {"checked_kernel_wrong": 0, "library_wrong": 0, "alarms": 0}
+    ours = {"checked_kernel_wrong": 3, "library_wrong": 0, "alarms": 3}
+    both = {"checked_kernel_wrong": 3, "library_wrong": 2, "alarms": 3}
+    assert classify([ok, ok], []) == "NOT REPRODUCED"
+    assert classify([ours, ok], []) == "DEVICE"
+    assert classify([ours, ours], []) == "SOFTWARE PATH"
+    assert classify([both, both], []) == "NOT ONE GPU"
+    assert classify([ours], []) == "INCONCLUSIVE"
+    assert classify([ok], [{"error": "x"}]) == "INCONCLUSIVE"
