@@ -55,6 +55,7 @@ class Transfer:
     pages: list              # producer page ids covering the prompt
     checksums: list          # uint64 per page
     first_token: int
+    page_gens: Optional[list] = None   # lifetime generation of each producer page (when recorded)
 
 
 @dataclass
@@ -161,8 +162,10 @@ class PrefixCache:
                 self.owned.add(pages[b])
 
 
-def produce(engine: LLMEngine, requests: list[tuple[str, list]], seed: int = kvx.DEFAULT_SEED) -> list[Transfer]:
-    """Prefill on the producer; pages stay allocated until `release_producer`."""
+def produce(engine: LLMEngine, requests: list[tuple[str, list]], seed: int = kvx.DEFAULT_SEED,
+            sink=None) -> list[Transfer]:
+    """Prefill on the producer; pages stay allocated until `release_producer`. sink: optional
+    `lifetime.adapter.EventSink` that records the page lifetimes (pool "prefill")."""
     dev = engine.device
     plens = [len(t) for _, t in requests]
     maxlen = max(plens)
@@ -175,6 +178,14 @@ def produce(engine: LLMEngine, requests: list[tuple[str, list]], seed: int = kvx
     pages = [engine.alloc.alloc(-(-n // PAGE)) for n in plens]
     out = torch.zeros(len(requests), 1, dtype=torch.long, device=dev)
     engine.prefill(prompts.to(dev), plens, pages, out)
+    gens = None
+    if sink is not None:
+        gens = []
+        for (rid, _), pg in zip(requests, pages):
+            for p in pg:
+                sink.alloc("prefill", p, rid)
+                sink.local_write("prefill", p, rid)
+            gens.append([sink.gen[("prefill", p)] for p in pg])
     flat = torch.tensor([p for pg in pages for p in pg], dtype=torch.int32, device=dev)
     sums = kvx.page_checksums(engine.cache, flat, seed).cpu().tolist()
     first = out[:, 0].cpu().tolist()
@@ -182,19 +193,22 @@ def produce(engine: LLMEngine, requests: list[tuple[str, list]], seed: int = kvx
     for i, (rid, toks) in enumerate(requests):
         k = len(pages[i])
         res.append(Transfer(rid, plens[i], list(toks), pages[i], [s & 0xFFFFFFFFFFFFFFFF for s in sums[o:o + k]],
-                            int(first[i])))
+                            int(first[i]), None if gens is None else gens[i]))
         o += k
     return res
 
 
-def release_producer(engine: LLMEngine, transfers: Sequence[Transfer]) -> None:
+def release_producer(engine: LLMEngine, transfers: Sequence[Transfer], sink=None) -> None:
     for t in transfers:
         engine.alloc.release(t.pages)
+        if sink is not None:
+            for p in t.pages:
+                sink.free("prefill", p)
 
 
 def consume(engine: LLMEngine, transfers: Sequence[Transfer], src_cache: torch.Tensor, prefix: PrefixCache,
             rec: Recorder, max_new_tokens: int, *, verify_cached_prefix: bool = False, seed: int = kvx.DEFAULT_SEED,
-            corrupt: Optional[dict] = None) -> torch.Tensor:
+            corrupt: Optional[dict] = None, sink=None) -> torch.Tensor:
     """Receive every request's KV pages (reusing cached prefix pages), check them, decode. Returns generated ids
     (N, max_new_tokens) on the host. `corrupt` = {request index: page index} flips one bit in that producer page
     before the pull (fault injection: the pulled page then mismatches its checksum); only for a producer cache in
@@ -209,6 +223,11 @@ def consume(engine: LLMEngine, transfers: Sequence[Transfer], src_cache: torch.T
         owned.append(fresh)
         local_pages.append(cached + fresh)
         c = len(cached)
+        if sink is not None:
+            for p in fresh:
+                sink.alloc("decode", p, t.request_id)
+            for p in cached:
+                sink.share("decode", p, t.request_id)
         total = len(t.pages)
         src = torch.tensor(t.pages[c:], dtype=torch.int32, device=dev)
         dst = torch.tensor(fresh[:total - c], dtype=torch.int32, device=dev)
@@ -219,6 +238,10 @@ def consume(engine: LLMEngine, transfers: Sequence[Transfer], src_cache: torch.T
             flip_bit_in_page(src_cache, pg)
         _, res = kvx.pull_pages(src_cache, engine.cache, src, dst, want, seed)
         res = res.cpu().tolist()
+        if sink is not None:
+            for j, (sp, dp) in enumerate(zip(t.pages[c:], fresh[:total - c])):
+                sink.transfer("read", "decode-pull", ("prefill", sp), ("decode", dp),
+                              src_gen=t.page_gens[c + j] if t.page_gens else None)
         mism = [c + j for j, r in enumerate(res) if r != 1]
         rec.transfer(t.request_id, t.prompt_tokens, c * PAGE, t.checksums, mism)
         if verify_cached_prefix and c:
@@ -232,10 +255,18 @@ def consume(engine: LLMEngine, transfers: Sequence[Transfer], src_cache: torch.T
             prefix.insert(t.token_ids, local_pages[-1][:t.prompt_tokens // PAGE])
     out = torch.zeros(N, max_new_tokens, dtype=torch.long, device=dev)
     out[:, 0] = torch.tensor([t.first_token for t in transfers], device=dev)
+    if sink is not None:
+        for t, pg in zip(transfers, local_pages):
+            for p in pg[:len(t.pages)]:
+                sink.consume("decode", p, t.request_id)
     engine.decode_from([t.prompt_tokens for t in transfers], local_pages, out, max_new_tokens)
     host = out.cpu()
     for pg in owned:
         engine.alloc.release([p for p in pg if p not in prefix.owned])
+        if sink is not None:
+            for p in pg:
+                if p not in prefix.owned:
+                    sink.free("decode", p)
     return host
 
 
@@ -282,7 +313,7 @@ def write_recording(out_dir: str, rec: Recorder, requests: list, meta: dict) -> 
 
 def run_single_process(out_dir: Optional[str], *, checked: bool = True, verify_cached_prefix: bool = False,
                        groups: int = 8, per_group: int = 20, new_tokens: int = 32, corrupt: Optional[dict] = None,
-                       model_cfg=None, producer_device="cuda:0", consumer_device=None) -> dict:
+                       model_cfg=None, producer_device="cuda:0", consumer_device=None, sink=None) -> dict:
     """Producer and consumer engines in this process (same GPU, or two GPUs of this process)."""
     from ..models.decoder import QWEN3_0_6B
     cfg = model_cfg or QWEN3_0_6B
@@ -298,14 +329,14 @@ def run_single_process(out_dir: Optional[str], *, checked: bool = True, verify_c
                                                                      model=None)
     rec, prefix = Recorder(), PrefixCache()
     t0 = time.perf_counter()
-    transfers = produce(prod, reqs)
+    transfers = produce(prod, reqs, sink=sink)
     for t in transfers:
         rec.cache("prefill", t.request_id, t.prompt_tokens, 0, 0, 1, ev.digest(ev.json_bytes(t.token_ids)))
     out = consume(cons, transfers, prod.cache, prefix, rec, new_tokens, verify_cached_prefix=verify_cached_prefix,
-                  corrupt=corrupt)
+                  corrupt=corrupt, sink=sink)
     torch.cuda.synchronize()
     wall = time.perf_counter() - t0
-    release_producer(prod, transfers)
+    release_producer(prod, transfers, sink=sink)
     meta = {"num_requests": len(reqs), "groups": groups, "new_tokens": new_tokens, "verify_cached_prefix": verify_cached_prefix,
             "wall_s": round(wall, 3)}
     if out_dir:

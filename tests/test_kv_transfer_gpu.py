@@ -65,3 +65,17 @@ def test_pd_end_to_end_gate(tmp_path):
                                verify_cached_prefix=True, corrupt={4: 88})
     rc, out = gate(tmp_path / "bad")
     assert rc == 2 and "native_checksum_mismatch" in out
+
+
+def test_pd_page_lifetimes_obey_the_ledger_rules():
+    """The P/D path's recorded page lifetimes (producer pages, pulls, shared prefix pages, consumes, frees) replayed
+    through the lifetime ledger: no rule broken."""
+    from sdcguard_b200.lifetime import adapter
+    from sdcguard_b200.models.decoder import TINY
+    from sdcguard_b200.serve import pd
+    sink = adapter.EventSink()
+    pd.run_single_process(None, groups=2, per_group=3, new_tokens=4, model_cfg=TINY, sink=sink)
+    r = adapter.check(sink.events)
+    kinds = {e["ev"] for e in sink.events}
+    assert {"alloc", "submit", "complete", "consume", "share", "free"} <= kinds, kinds
+    assert r["violations"] == [], r["violations"][:3]
