@@ -7,6 +7,14 @@
     sdcguard selftest                                        GPU self-test of every checked kernel
     sdcguard campaign                                        fault-injection campaign on the GPU paths
     sdcguard check                                           GPU check card (GEMM, bandwidth, injected faults)
+    sdcguard screen / screen-ops / modes                     workload, operator and math-mode screens of a GPU
+    sdcguard blas / kernels / issues                         cuBLASLt algorithm sweep, kernel inventory, known issues
+    sdcguard certify / fleet / board                         signed certificates, fleet view, results board
+    sdcguard casefile / investigate                          incident casefile and replays of a flagged GEMM
+    sdcguard gate-model                                      teacher-forced output comparison of two stacks
+    sdcguard serve / ready / perf / isolation / consistency  HTTP server and outside-in probes
+    sdcguard qualify / decide                                stack-change qualification and decision
+    sdcguard lifetime / assess / bundle                      KV lifetime explorer, scoped assessment, evidence bundle
     sdcguard version
 
 The first three keep the reference's commands, exit codes and output (src/sdcguard/cli.py:343-463 dispatch).
@@ -37,6 +45,28 @@ COMMANDS = {
     "selftest": _lazy(".tools.selftest", "main"),
     "campaign": _lazy(".tools.campaign", "main"),
     "check": _lazy(".tools.check", "main"),
+    "screen": _lazy(".tools.screen", "main"),
+    "screen-ops": _lazy(".tools.screen_ops", "main"),
+    "modes": _lazy(".tools.modes", "main"),
+    "blas": _lazy(".tools.blas", "main"),
+    "kernels": _lazy(".tools.kernels", "main"),
+    "issues": _lazy(".tools.known_issues", "main"),
+    "certify": _lazy(".tools.certify", "main"),
+    "fleet": _lazy(".tools.fleet", "main"),
+    "board": _lazy(".tools.board", "main"),
+    "casefile": _lazy(".tools.casefile", "main"),
+    "investigate": _lazy(".tools.investigate", "main"),
+    "gate-model": _lazy(".tools.gate_model", "main"),
+    "serve": _lazy(".serve.http", "main"),
+    "ready": _lazy(".tools.ready", "main"),
+    "perf": _lazy(".tools.perf", "main"),
+    "isolation": _lazy(".tools.isolation", "main"),
+    "consistency": _lazy(".tools.consistency", "main"),
+    "qualify": _lazy(".tools.qualify", "main"),
+    "decide": _lazy(".tools.decide", "main"),
+    "lifetime": _lazy(".lifetime.__main__", "main"),
+    "assess": _lazy(".evidence.assessment", "main"),
+    "bundle": _lazy(".evidence.bundle", "main"),
     "version": _version,
 }
 
