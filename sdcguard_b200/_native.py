@@ -73,6 +73,7 @@ SIGNATURES: dict[str, tuple] = {
     "sdc_gemm_bf16_push": (I, [P, L, P, P, I, I, I, P, P, F, P, P, P, P, I, U, U, U, U, F, F, F, F, F, P, I, I, I, U,
                                I, I, L, P, P, P, P, P, P]),
     "sdc_tp_reduce_local": (I, [P, P, P, P, I, I, I, I, L, P, F, P, P, P]),
+    "sdc_seal_verify": (I, [P, L, I, I, P, I, P, P]),
     "sdc_screen_fma": (I, [L, U64, I, L, P, P]),
     "sdc_screen_special": (I, [L, U64, L, P, P, P]),
     "sdc_screen_compare": (I, [L, P, P, P, P, L, P, P]),

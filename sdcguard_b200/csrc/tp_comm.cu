@@ -147,11 +147,16 @@ __global__ void __launch_bounds__(256) ag_pull_kernel(Peers shards, Peers seals,
 }
 
 // Seals of a bf16 [M][N] tensor: one warp per (row, block); the producer side of a checked transfer.
+// Seals of every (row, 128-column block) of x. Verify mode (want != null): compare with the seals the sender computed
+// and report a mismatch into the state row as (row, block, peer) with an infinite score (pipeline-parallel receives).
 __global__ void __launch_bounds__(256) seal_rows_kernel(const __nv_bfloat16* __restrict__ x, long long ld, int M,
-                                                        int N, uint32_t* __restrict__ seals) {
+                                                        int N, uint32_t* __restrict__ seals,
+                                                        const uint32_t* __restrict__ want, int peer,
+                                                        unsigned long long* state) {
   const int nb = (N + 127) / 128;
   const int lane = threadIdx.x & 31;
   const long long wid = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  if (want != nullptr && blockIdx.x == 0 && threadIdx.x == 0 && state != nullptr) atomicAdd(state + 2, 1ull);
   if (wid >= static_cast<long long>(M) * nb) return;
   const long long row = wid / nb;
   const int b = static_cast<int>(wid % nb);
@@ -161,7 +166,13 @@ __global__ void __launch_bounds__(256) seal_rows_kernel(const __nv_bfloat16* __r
   uint32_t h = seal_term(v.x, static_cast<uint32_t>(lane * 2)) + seal_term(v.y, static_cast<uint32_t>(lane * 2 + 1));
 #pragma unroll
   for (int m = 16; m > 0; m >>= 1) h += __shfl_xor_sync(0xffffffffu, h, m);
-  if (lane == 0) seals[row * nb + b] = h;
+  if (lane == 0) {
+    if (want == nullptr) {
+      seals[row * nb + b] = h;
+    } else if (__ldg(want + row * nb + b) != h) {
+      report(state, __int_as_float(0x7f800000), static_cast<unsigned long long>(row * nb + b) * MAXW + peer);
+    }
+  }
 }
 
 }  // namespace tp
@@ -224,7 +235,18 @@ int sdc_seal_rows(const void* x, long long ld, int M, int N, void* seals, void* 
   if (M <= 0) return 0;
   const long long warps = static_cast<long long>(M) * ((N + 127) / 128);
   seal_rows_kernel<<<static_cast<unsigned>((warps * 32 + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(x), ld, M, N, static_cast<uint32_t*>(seals));
+      static_cast<const __nv_bfloat16*>(x), ld, M, N, static_cast<uint32_t*>(seals), nullptr, 0, nullptr);
+  return static_cast<int>(cudaGetLastError());
+}
+
+// Recompute the seals of a received x (M, N) and compare with the sender's (want, [M][nb]); mismatches go to state
+// (the collective location encoding: (row nb + block) 8 + peer).
+int sdc_seal_verify(const void* x, long long ld, int M, int N, const void* want, int peer, void* state, void* stream) {
+  if (M <= 0) return 0;
+  const long long warps = static_cast<long long>(M) * ((N + 127) / 128);
+  seal_rows_kernel<<<static_cast<unsigned>((warps * 32 + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), ld, M, N, nullptr, static_cast<const uint32_t*>(want), peer,
+      static_cast<unsigned long long*>(state));
   return static_cast<int>(cudaGetLastError());
 }
 

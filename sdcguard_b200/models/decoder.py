@@ -233,21 +233,30 @@ class CheckedDecoder:
     def _st(self, name) -> torch.Tensor:
         return self.state.state[self.slot[name]]
 
-    def forward(self, meta: StepMeta, cache: torch.Tensor) -> torch.Tensor:
+    def forward(self, meta: StepMeta, cache: torch.Tensor, layers: Optional[tuple] = None,
+                hidden: Optional[tuple] = None, last: bool = True):
         """Runs one step; returns logits (L, vocab) bf16 for meta.logits_rows. cache: (layers, blocks, 2, nkv,
-        16, 128) bf16."""
+        16, 128) bf16. Pipeline stages: layers=(lo, hi) runs only those layers (cache then holds hi - lo layers),
+        hidden=(x, resid) enters after layer lo - 1 instead of the embedding, and last=False returns the (x, resid)
+        pair after layer hi - 1 (x: the last sublayer's output, not yet added to the residual resid)."""
         cfg = self.cfg
         T = meta.tokens.shape[0]
         B = self.buffers(T)
         x, resid, y, rs = B["x"][:T], B["resid"][:T], B["y"][:T], B["rs"][:T]
         qkv, q, att, ors = B["qkv"][:T], B["q"][:T], B["attn"][:T], B["ors"][:T]
         a, gu, act = B["a"][:T], B["gu"][:T], B["act"][:T]
-        torch.index_select(self.embed, 0, meta.tokens, out=x)
+        lo, hi = layers or (0, len(self.layers))
+        if hidden is None:
+            torch.index_select(self.embed, 0, meta.tokens, out=x)
+        else:
+            x.copy_(hidden[0])
+            resid.copy_(hidden[1])
         S = meta.sample_rows
         chk = self.checked and S is not None and S.numel() > 0
         nq, nkv, D = self.nq, self.nkv, cfg.head_dim
-        for i, lw in enumerate(self.layers):
-            lc = cache[i]
+        for i in range(lo, hi):
+            lw = self.layers[i]
+            lc = cache[i - lo]
             if i == 0:
                 layers.add_rmsnorm(x, lw.ln1, cfg.rms_eps, residual=None, resid_out=resid, out=y, row_sq=rs)
             else:
@@ -285,6 +294,8 @@ class CheckedDecoder:
             if chk:
                 layers.silu_mul(gu, out=act, rows=S, check=self._st(f"L{i}.act"))
             self._linear(act, lw.down, lw.cw.get("down"), f"L{i}.down", x, rs, S)
+        if not last:
+            return x, resid
         # final norm on the rows that produce tokens, then the LM head
         L = meta.logits_rows.shape[0]
         xs = x.index_select(0, meta.logits_rows)
