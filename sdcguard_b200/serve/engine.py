@@ -54,7 +54,7 @@ class LLMEngine:
     def __init__(self, cfg: DecoderConfig, device="cuda", checked: bool = True, num_blocks: Optional[int] = None,
                  max_prefill_tokens: int = 16384, max_num_seqs: int = 256, sample_every: int = 64,
                  cuda_graph: bool = True, seed: int = 0, kv_fraction: float = 0.6, model: Optional[CheckedDecoder] = None,
-                 max_model_len: int = 4096, precision: str = "bf16"):
+                 max_model_len: int = 4096, precision: str = "bf16", cache: Optional[torch.Tensor] = None):
         self.cfg = cfg
         self.device = torch.device(device)
         self.model = model or CheckedDecoder(cfg, self.device, checked=checked, seed=seed, precision=precision)
@@ -63,11 +63,18 @@ class LLMEngine:
         self.max_num_seqs = max_num_seqs
         self.sample_every = sample_every
         self.cuda_graph = cuda_graph
-        if num_blocks is None:
-            free, _ = torch.cuda.mem_get_info(self.device)
-            num_blocks = int(free * kv_fraction) // kv_bytes_per_page(cfg, self.model.nkv)
-        self.cache = torch.zeros(cfg.layers, num_blocks, 2, self.model.nkv, PAGE, cfg.head_dim,
-                                 dtype=torch.bfloat16, device=self.device)
+        if cache is not None:          # caller-owned KV memory (e.g. a symmetric buffer peers read from)
+            want = (cfg.layers, cache.shape[1], 2, self.model.nkv, PAGE, cfg.head_dim)
+            if tuple(cache.shape) != want or cache.dtype != torch.bfloat16:
+                raise ValueError(f"cache must be bf16 {want}, got {tuple(cache.shape)} {cache.dtype}")
+            num_blocks = cache.shape[1]
+            self.cache = cache
+        else:
+            if num_blocks is None:
+                free, _ = torch.cuda.mem_get_info(self.device)
+                num_blocks = int(free * kv_fraction) // kv_bytes_per_page(cfg, self.model.nkv)
+            self.cache = torch.zeros(cfg.layers, num_blocks, 2, self.model.nkv, PAGE, cfg.head_dim,
+                                     dtype=torch.bfloat16, device=self.device)
         self.alloc = BlockAllocator(num_blocks)
         self.guard = ServeGuard(self.model)
         # every activation buffer and the GEMM workspace are sized once, before any CUDA graph is captured
