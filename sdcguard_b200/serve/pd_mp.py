@@ -111,7 +111,7 @@ def run(args) -> dict:
     from ..lifetime import adapter
     viol = len(adapter.check(sink.events)["violations"])
     tot_viol = int(_max(float(viol), dev))
-    mism = sum(1 for r in rec.records if r.get("native_result") == "failed")
+    mism = sum(1 for r in rec.records if r.get("kind") == "verification" and r.get("native_result") == "mismatch")
     tot_mism = int(_max(float(mism), dev))
     tokens = sum(len(t) + args.new_tokens for _, t in reqs)
     res = {"world": world, "prefill_ranks": P, "decode_ranks": D, "requests": len(reqs), "device_ms": round(dev_ms, 2),
