@@ -233,10 +233,10 @@ class CheckedDecoder:
     def _st(self, name) -> torch.Tensor:
         return self.state.state[self.slot[name]]
 
-    def forward(self, meta: StepMeta, cache: torch.Tensor, layers: Optional[tuple] = None,
+    def forward(self, meta: StepMeta, cache: torch.Tensor, layer_range: Optional[tuple] = None,
                 hidden: Optional[tuple] = None, last: bool = True):
         """Runs one step; returns logits (L, vocab) bf16 for meta.logits_rows. cache: (layers, blocks, 2, nkv,
-        16, 128) bf16. Pipeline stages: layers=(lo, hi) runs only those layers (cache then holds hi - lo layers),
+        16, 128) bf16. Pipeline stages: layer_range=(lo, hi) runs only those layers (cache then holds hi - lo layers),
         hidden=(x, resid) enters after layer lo - 1 instead of the embedding, and last=False returns the (x, resid)
         pair after layer hi - 1 (x: the last sublayer's output, not yet added to the residual resid)."""
         cfg = self.cfg
@@ -245,7 +245,7 @@ class CheckedDecoder:
         x, resid, y, rs = B["x"][:T], B["resid"][:T], B["y"][:T], B["rs"][:T]
         qkv, q, att, ors = B["qkv"][:T], B["q"][:T], B["attn"][:T], B["ors"][:T]
         a, gu, act = B["a"][:T], B["gu"][:T], B["act"][:T]
-        lo, hi = layers or (0, len(self.layers))
+        lo, hi = layer_range or (0, len(self.layers))
         if hidden is None:
             torch.index_select(self.embed, 0, meta.tokens, out=x)
         else:

@@ -1,6 +1,6 @@
 """Pipeline parallelism with sealed stage-to-stage transfers on NCCL point-to-point, overlapped with compute.
 
-Each stage runs a contiguous range of decoder layers (`CheckedDecoder.forward(layers=..., hidden=..., last=...)`)
+Each stage runs a contiguous range of decoder layers (`CheckedDecoder.forward(layer_range=..., hidden=..., last=...)`)
 over a sequence of microbatches. Between stages the residual-stream state (x, resid) moves with `isend` / `irecv`
 (NCCL over NVLink on GPUs, gloo on CPU), together with its seals: the exact 32-bit hash of every (row, 128-column
 block) that the sender computes from the bits it sends (`seal_rows` kernel) and the receiver recomputes from the bits
@@ -131,10 +131,10 @@ def run_stage(model, comm: SealedP2P, metas: Sequence, cache: torch.Tensor, stag
             x, r = comm.recv([(T, H), (T, H)], stage - 1)
             hidden = (x, r)
         if stage < stages - 1:
-            x, r = model.forward(meta, cache, layers=(lo, hi), hidden=hidden, last=False)
+            x, r = model.forward(meta, cache, layer_range=(lo, hi), hidden=hidden, last=False)
             pending += comm.send([x.clone(), r.clone()], stage + 1)   # the activation buffers are reused next
         else:
-            outs.append(model.forward(meta, cache, layers=(lo, hi), hidden=hidden).clone())
+            outs.append(model.forward(meta, cache, layer_range=(lo, hi), hidden=hidden).clone())
     for w in pending:
         if hasattr(w, "wait"):
             w.wait()

@@ -32,7 +32,9 @@ def _run(out, extra=()):
            "--new-tokens", "4", "--out", str(out), *extra]
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     r = subprocess.run(cmd, cwd=ROOT, capture_output=True, text=True, env=env, timeout=500)
-    assert r.returncode == 0, r.stderr[-3000:]
+    if r.returncode != 0:
+        i = r.stderr.find("Traceback")
+        raise AssertionError(r.stderr[i:i + 4000] if i >= 0 else r.stderr[-3000:])
     return json.loads([x for x in r.stdout.splitlines() if x.startswith("{")][-1])
 
 

@@ -56,8 +56,8 @@ def test_staged_forward_matches_whole_model():
     staged = []
     for mt in metas:
         c0, c1 = _cache(m, 1, dev), _cache(m, 1, dev)
-        x, r = m.forward(mt, c0, layers=(0, 1), last=False)
-        staged.append(m.forward(mt, c1, layers=(1, 2), hidden=(x.clone(), r.clone())).float().cpu())
+        x, r = m.forward(mt, c0, layer_range=(0, 1), last=False)
+        staged.append(m.forward(mt, c1, layer_range=(1, 2), hidden=(x.clone(), r.clone())).float().cpu())
     for a, b in zip(whole, staged):
         assert torch.equal(a, b)
     assert not [r for r in m.read_checks(reset=True) if r["z"] > 6]
