@@ -39,6 +39,14 @@ class EventSink:
             self._f.write(json.dumps(ev) + "\n")
             self._f.flush()
 
+    def ingest(self, events: list) -> None:
+        """Events recorded by another process (a producer's page allocations), in order, before this one's own."""
+        for e in events:
+            if e["ev"] == "alloc":
+                k = (e["region"][0], int(e["region"][1]))
+                self.gen[k] = self.gen.get(k, 0) + 1
+            self._emit(e)
+
     def handle(self, pool: str, idx: int) -> list:
         return [[pool, int(idx)], self.gen.get((pool, int(idx)), 0)]
 

@@ -56,6 +56,7 @@ class Transfer:
     checksums: list          # uint64 per page
     first_token: int
     page_gens: Optional[list] = None   # lifetime generation of each producer page (when recorded)
+    pool: str = "prefill"              # lifetime pool name of the producer's pages
 
 
 @dataclass
@@ -163,7 +164,7 @@ class PrefixCache:
 
 
 def produce(engine: LLMEngine, requests: list[tuple[str, list]], seed: int = kvx.DEFAULT_SEED,
-            sink=None) -> list[Transfer]:
+            sink=None, pool: str = "prefill") -> list[Transfer]:
     """Prefill on the producer; pages stay allocated until `release_producer`. sink: optional
     `lifetime.adapter.EventSink` that records the page lifetimes (pool "prefill")."""
     dev = engine.device
@@ -183,9 +184,9 @@ def produce(engine: LLMEngine, requests: list[tuple[str, list]], seed: int = kvx
         gens = []
         for (rid, _), pg in zip(requests, pages):
             for p in pg:
-                sink.alloc("prefill", p, rid)
-                sink.local_write("prefill", p, rid)
-            gens.append([sink.gen[("prefill", p)] for p in pg])
+                sink.alloc(pool, p, rid)
+                sink.local_write(pool, p, rid)
+            gens.append([sink.gen[(pool, p)] for p in pg])
     flat = torch.tensor([p for pg in pages for p in pg], dtype=torch.int32, device=dev)
     sums = kvx.page_checksums(engine.cache, flat, seed).cpu().tolist()
     first = out[:, 0].cpu().tolist()
@@ -193,7 +194,7 @@ def produce(engine: LLMEngine, requests: list[tuple[str, list]], seed: int = kvx
     for i, (rid, toks) in enumerate(requests):
         k = len(pages[i])
         res.append(Transfer(rid, plens[i], list(toks), pages[i], [s & 0xFFFFFFFFFFFFFFFF for s in sums[o:o + k]],
-                            int(first[i]), None if gens is None else gens[i]))
+                            int(first[i]), None if gens is None else gens[i], pool))
         o += k
     return res
 
@@ -203,7 +204,7 @@ def release_producer(engine: LLMEngine, transfers: Sequence[Transfer], sink=None
         engine.alloc.release(t.pages)
         if sink is not None:
             for p in t.pages:
-                sink.free("prefill", p)
+                sink.free(t.pool, p)
 
 
 def consume(engine: LLMEngine, transfers: Sequence[Transfer], src_cache: torch.Tensor, prefix: PrefixCache,
@@ -240,7 +241,7 @@ def consume(engine: LLMEngine, transfers: Sequence[Transfer], src_cache: torch.T
         res = res.cpu().tolist()
         if sink is not None:
             for j, (sp, dp) in enumerate(zip(t.pages[c:], fresh[:total - c])):
-                sink.transfer("read", "decode-pull", ("prefill", sp), ("decode", dp),
+                sink.transfer("read", "decode-pull", (t.pool, sp), ("decode", dp),
                               src_gen=t.page_gens[c + j] if t.page_gens else None)
         mism = [c + j for j, r in enumerate(res) if r != 1]
         rec.transfer(t.request_id, t.prompt_tokens, c * PAGE, t.checksums, mism)

@@ -72,12 +72,12 @@ def run(args) -> dict:
     t0 = time.perf_counter()
     a.record()
     if rank < P:
-        transfers = pd.produce(eng, mine, sink=sink)
+        transfers = pd.produce(eng, mine, sink=sink, pool=f"prefill{rank}")
         if args.corrupt_page is not None and transfers and rank == 0:
             pd.flip_bit_in_page(eng.cache, transfers[0].pages[args.corrupt_page % len(transfers[0].pages)])
         torch.cuda.synchronize(dev)        # every page written before the consumer reads it
         dst = P + rank % D
-        dist.send_object_list([[t.__dict__ for t in transfers]], dst=dst)
+        dist.send_object_list([[t.__dict__ for t in transfers], list(sink.events)], dst=dst)
         ack = [None]
         dist.recv_object_list(ack, src=dst)
         pd.release_producer(eng, transfers, sink=sink)
@@ -89,9 +89,10 @@ def run(args) -> dict:
         for p in range(P):
             if p % D != c:
                 continue
-            box = [None]
+            box = [None, None]
             dist.recv_object_list(box, src=p)
             transfers = [pd.Transfer(**d) for d in box[0]]
+            sink.ingest(box[1])                # the producer's page allocations precede the pulls
             src_view = _wrap(buf.addr[p], shape, torch.bfloat16, dev)
             outs.append(pd.consume(eng, transfers, src_view, prefix, rec, args.new_tokens,
                                    verify_cached_prefix=args.verify_cached_prefix, sink=sink))
