@@ -109,6 +109,7 @@ class CheckedDecoder:
         if precision == "fp8" and not checked:
             raise ValueError("the fp8 path is the checked fp8 GEMM")
         self.precision = precision
+        self._side = torch.cuda.Stream(torch.device(device)) if checked and torch.cuda.is_available() else None
         self.cfg = cfg
         self.moe = moe_layers
         self.device = torch.device(device)
@@ -200,6 +201,12 @@ class CheckedDecoder:
             gemm.reserve_workspace(dev, min(T, 1024), cfg.vocab)
         return self._bufs
 
+    def _side_stream(self) -> torch.cuda.Stream:
+        """The stream replay checks run on (created once, before any graph capture needs it)."""
+        if getattr(self, "_side", None) is None:
+            self._side = torch.cuda.Stream(self.device)
+        return self._side
+
     def decode_scratch(self, nseq: int, max_ctx: int) -> torch.Tensor:
         """Split-KV partials for decode; sized once for the largest batch and context seen (graph-safe: a decode
         graph is captured after the engine reserved it)."""
@@ -254,7 +261,27 @@ class CheckedDecoder:
         S = meta.sample_rows
         chk = self.checked and S is not None and S.numel() > 0
         nq, nkv, D = self.nq, self.nkv, cfg.head_dim
+        # Replay checks write nothing the forward reads, so they run on a side stream next to the main chain (filling
+        # SMs the small decode kernels leave idle) and rejoin before the buffers they compare are overwritten: the
+        # norm-1 / rope / attention replays before norm 2 of the same layer, the norm-2 / SwiGLU replays before the
+        # next layer's norm 1.
+        main = torch.cuda.current_stream(self.device)
+        side = self._side_stream() if chk else None
+
+        def replay(fn):
+            if side is None:
+                fn()
+                return
+            side.wait_stream(main)
+            with torch.cuda.stream(side):
+                fn()
+
+        def join():
+            if side is not None:
+                main.wait_stream(side)
+
         for i in range(lo, hi):
+            join()
             lw = self.layers[i]
             lc = cache[i - lo]
             if i == 0:
@@ -262,38 +289,44 @@ class CheckedDecoder:
             else:
                 layers.add_rmsnorm(x, lw.ln1, cfg.rms_eps, residual=resid, resid_out=resid, out=y, row_sq=rs)
             if chk:
-                layers.add_rmsnorm(resid, lw.ln1, cfg.rms_eps, out=y, rows=S, check=self._st(f"L{i}.norm1"))
+                replay(lambda: layers.add_rmsnorm(resid, lw.ln1, cfg.rms_eps, out=y, rows=S,
+                                                  check=self._st(f"L{i}.norm1")))
             self._linear(y, lw.qkv, lw.cw.get("qkv"), f"L{i}.qkv", qkv, rs, S)
             layers.qk_norm_rope_kv(qkv, nq, nkv, meta.pos, meta.slots, lw.q_norm, lw.k_norm, cfg.rms_eps, self.rope,
                                    q, lc)
             if chk:
-                layers.qk_norm_rope_kv(qkv, nq, nkv, meta.pos, meta.slots, lw.q_norm, lw.k_norm, cfg.rms_eps,
-                                       self.rope, q, lc, rows=S, check=self._st(f"L{i}.rope_kv"))
+                replay(lambda: layers.qk_norm_rope_kv(qkv, nq, nkv, meta.pos, meta.slots, lw.q_norm, lw.k_norm,
+                                                      cfg.rms_eps, self.rope, q, lc, rows=S,
+                                                      check=self._st(f"L{i}.rope_kv")))
             ors.zero_()
             if meta.mode == "prefill":
                 attention.prefill(q, lc, meta.block_table, meta.pos, meta.tiles, nq, nkv, out=att, row_sq=ors)
                 if chk:
-                    attention.prefill(q, lc, meta.block_table, meta.pos, meta.sample_tiles, nq, nkv, out=att,
-                                      row_idx=meta.sample_idx, check=self._st(f"L{i}.attn"))
+                    replay(lambda: attention.prefill(q, lc, meta.block_table, meta.pos, meta.sample_tiles, nq, nkv,
+                                                     out=att, row_idx=meta.sample_idx, check=self._st(f"L{i}.attn")))
             else:
                 scratch = self.decode_scratch(T, meta.max_ctx)
                 attention.decode(q, lc, meta.block_table, meta.seq_req, meta.ctx, nq, nkv, meta.max_ctx, out=att,
                                  row_sq=ors, scratch=scratch)
                 if chk:
-                    attention.decode(q, lc, meta.block_table, meta.seq_req, meta.ctx, nq, nkv, meta.max_ctx,
-                                     out=att, seq_idx=S, scratch=scratch, check=self._st(f"L{i}.attn"))
+                    replay(lambda: attention.decode(q, lc, meta.block_table, meta.seq_req, meta.ctx, nq, nkv,
+                                                    meta.max_ctx, out=att, seq_idx=S, scratch=scratch,
+                                                    check=self._st(f"L{i}.attn")))
             self._linear(att.view(T, nq * D), lw.o, lw.cw.get("o"), f"L{i}.o", a, ors, S)
+            join()
             layers.add_rmsnorm(a, lw.ln2, cfg.rms_eps, residual=resid, resid_out=resid, out=y, row_sq=rs)
             if chk:
-                layers.add_rmsnorm(resid, lw.ln2, cfg.rms_eps, out=y, rows=S, check=self._st(f"L{i}.norm2"))
+                replay(lambda: layers.add_rmsnorm(resid, lw.ln2, cfg.rms_eps, out=y, rows=S,
+                                                  check=self._st(f"L{i}.norm2")))
             if self.moe:
                 x = self.moe[i].forward(y, S if chk else None)
                 continue
             self._linear(y, lw.gate_up, lw.cw.get("gate_up"), f"L{i}.gate_up", gu, rs, S)
             layers.silu_mul(gu, out=act, row_sq=rs)
             if chk:
-                layers.silu_mul(gu, out=act, rows=S, check=self._st(f"L{i}.act"))
+                replay(lambda: layers.silu_mul(gu, out=act, rows=S, check=self._st(f"L{i}.act")))
             self._linear(act, lw.down, lw.cw.get("down"), f"L{i}.down", x, rs, S)
+        join()
         if not last:
             return x, resid
         # final norm on the rows that produce tokens, then the LM head
