@@ -267,18 +267,21 @@ class CheckedDecoder:
         # next layer's norm 1.
         main = torch.cuda.current_stream(self.device)
         side = self._side_stream() if chk else None
+        forked = [False]      # joined only after a fork: under graph capture the side stream must be in the capture
 
         def replay(fn):
             if side is None:
                 fn()
                 return
             side.wait_stream(main)
+            forked[0] = True
             with torch.cuda.stream(side):
                 fn()
 
         def join():
-            if side is not None:
+            if side is not None and forked[0]:
                 main.wait_stream(side)
+                forked[0] = False
 
         for i in range(lo, hi):
             join()
