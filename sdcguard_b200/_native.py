@@ -88,7 +88,8 @@ SIGNATURES: dict[str, tuple] = {
     "sdc_router_topk": (I, [P, I, I, I, I, P, P, P, I, P, P]),
     "sdc_tp_signal": (I, [P, P, I, I, P]),
     "sdc_tp_reduce_scatter": (I, [P, P, P, P, I, I, I, I, P, F, P, P, P]),
-    "sdc_tp_all_gather": (I, [P, P, P, P, I, I, I, P, P, P, P]),
+    "sdc_tp_all_gather": (I, [P, P, P, P, I, I, I, P, P, P, P, P, P]),
+    "sdc_add_rmsnorm_shard": (I, [P, P, P, F, I, I, P, P, P, P, I, I, P, P, P, P]),
     "sdc_seal_rows": (I, [P, L, I, I, P, P]),
     "sdc_symm_alloc": (I, [ctypes.c_ulonglong, ctypes.POINTER(ctypes.c_void_p)]),
     "sdc_symm_free": (I, [P]),

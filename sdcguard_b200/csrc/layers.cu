@@ -14,6 +14,7 @@
 //
 // Paged KV cache layout for one layer: [num_blocks][2 (K, V)][kv_heads][16 tokens][head_dim] bf16.
 #include "common.cuh"
+#include "peer.cuh"
 
 namespace sdc {
 
@@ -53,13 +54,24 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 
 // One CTA of 128 threads per row; each thread holds VPT chunks of 8 values.
 // With `rows` (replay of sampled rows): CTA b reads input row rows[b] and writes output row b.
+// Tensor-parallel shard output (all optional): seals of the normalised rows (one 32-bit seal per 128-column block,
+// the transfer check of the all-gather that reads them) and, once every row of the launch is written, the
+// release of this rank's generation flag on every rank (the signal the all-gather waits for).
+struct ShardOut {
+  uint32_t* seal;             // [M][nb] or null
+  int world, rank;
+  long long* flag[peer::MAXW];
+  long long* gen;
+  unsigned int* done;         // CTAs finished (zero between launches); null: no signal
+};
+
 template <int VPT>
 __global__ void __launch_bounds__(128) add_rmsnorm_kernel(const __nv_bfloat16* __restrict__ x,
                                                           const __nv_bfloat16* residual,
                                                           const __nv_bfloat16* __restrict__ w, float eps, int H,
                                                           __nv_bfloat16* __restrict__ y, __nv_bfloat16* resid_out,
                                                           float* __restrict__ row_sq, const int* rows,
-                                                          unsigned long long* check) {
+                                                          unsigned long long* check, const ShardOut so) {
   __shared__ float red[4];
   __shared__ int sbad;
   int bad = 0x7fffffff;
@@ -110,6 +122,7 @@ __global__ void __launch_bounds__(128) add_rmsnorm_kernel(const __nv_bfloat16* _
 #pragma unroll
   for (int c = 0; c < VPT; ++c) {
     const int col = (c * 128 + threadIdx.x) * 8;
+    uint32_t sh = 0u;        // seal terms of this thread's 8 columns (16 threads = one 128-column block)
     if (col < H) {
       uint4 wv = *reinterpret_cast<const uint4*>(w + col);
       const __nv_bfloat162* hw = reinterpret_cast<const __nv_bfloat162*>(&wv);
@@ -124,6 +137,10 @@ __global__ void __launch_bounds__(128) add_rmsnorm_kernel(const __nv_bfloat16* _
       }
       if (check == nullptr) {
         *reinterpret_cast<uint4*>(y + row * H + col) = o;
+        if (so.seal != nullptr) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) sh += seal_term(op[i], static_cast<uint32_t>((threadIdx.x & 15) * 4 + i));
+        }
       } else {
         const uint4 f = *reinterpret_cast<const uint4*>(y + in_row * H + col);
         const uint32_t* fp = reinterpret_cast<const uint32_t*>(&f);
@@ -134,6 +151,11 @@ __global__ void __launch_bounds__(128) add_rmsnorm_kernel(const __nv_bfloat16* _
         }
       }
     }
+    if (so.seal != nullptr && check == nullptr) {
+#pragma unroll
+      for (int m = 8; m > 0; m >>= 1) sh += __shfl_xor_sync(0xffffffffu, sh, m);
+      if ((threadIdx.x & 15) == 0 && col < H) so.seal[row * ((H + 127) / 128) + col / 128] = sh;
+    }
   }
   if (check != nullptr) {
     replay_report_block(check, bad, in_row, H, &sbad);
@@ -141,6 +163,19 @@ __global__ void __launch_bounds__(128) add_rmsnorm_kernel(const __nv_bfloat16* _
   }
   const float yt = block_sum<128>(ys, red);
   if (threadIdx.x == 0 && row_sq != nullptr) row_sq[row] = yt;
+  if (so.done != nullptr) {
+    // every row of this CTA is written (block_sum synchronised the CTA); the last CTA raises the flags
+    if (threadIdx.x == 0) {
+      __threadfence_system();
+      if (atomicAdd(so.done, 1u) == gridDim.x - 1) {
+        *so.done = 0;
+        const long long g = *so.gen + 1;
+        *so.gen = g;
+        __threadfence_system();
+        for (int r = 0; r < so.world; ++r) peer::st_release_sys(so.flag[r] + so.rank, g);
+      }
+    }
+  }
 }
 
 // One warp per (token, head); heads [0, nq) are queries, [nq, nq+nkv) keys, [nq+nkv, nq+2nkv) values.
@@ -269,6 +304,17 @@ __global__ void __launch_bounds__(128) silu_mul_kernel(const __nv_bfloat16* __re
 
 }  // namespace sdc
 
+static int launch_norm(const __nv_bfloat16* X, const __nv_bfloat16* R, const __nv_bfloat16* W, float eps, int M, int H,
+                       __nv_bfloat16* Y, __nv_bfloat16* RO, float* S, const int* rows, unsigned long long* C,
+                       const sdc::ShardOut& so, cudaStream_t st) {
+  const int vpt = (H + 1023) / 1024;
+  if (vpt <= 1) sdc::add_rmsnorm_kernel<1><<<M, 128, 0, st>>>(X, R, W, eps, H, Y, RO, S, rows, C, so);
+  else if (vpt <= 2) sdc::add_rmsnorm_kernel<2><<<M, 128, 0, st>>>(X, R, W, eps, H, Y, RO, S, rows, C, so);
+  else if (vpt <= 4) sdc::add_rmsnorm_kernel<4><<<M, 128, 0, st>>>(X, R, W, eps, H, Y, RO, S, rows, C, so);
+  else sdc::add_rmsnorm_kernel<8><<<M, 128, 0, st>>>(X, R, W, eps, H, Y, RO, S, rows, C, so);
+  return static_cast<int>(cudaGetLastError());
+}
+
 extern "C" {
 
 int sdc_add_rmsnorm_bf16(const void* x, const void* residual, const void* w, float eps, int M, int H, void* y,
@@ -276,7 +322,6 @@ int sdc_add_rmsnorm_bf16(const void* x, const void* residual, const void* w, flo
   if (M <= 0) return 0;
   if (H % 8 || H > 8192) return -1;
   auto st = static_cast<cudaStream_t>(stream);
-  const int vpt = (H + 1023) / 1024;
   auto X = static_cast<const __nv_bfloat16*>(x);
   auto R = static_cast<const __nv_bfloat16*>(residual);
   auto W = static_cast<const __nv_bfloat16*>(w);
@@ -285,11 +330,27 @@ int sdc_add_rmsnorm_bf16(const void* x, const void* residual, const void* w, flo
   auto S = static_cast<float*>(row_sq);
   auto C = static_cast<unsigned long long*>(check);
   if (C != nullptr && (rows == nullptr || RO != nullptr)) return -1;   // check mode: sampled rows, no writes
-  if (vpt <= 1) sdc::add_rmsnorm_kernel<1><<<M, 128, 0, st>>>(X, R, W, eps, H, Y, RO, S, rows, C);
-  else if (vpt <= 2) sdc::add_rmsnorm_kernel<2><<<M, 128, 0, st>>>(X, R, W, eps, H, Y, RO, S, rows, C);
-  else if (vpt <= 4) sdc::add_rmsnorm_kernel<4><<<M, 128, 0, st>>>(X, R, W, eps, H, Y, RO, S, rows, C);
-  else sdc::add_rmsnorm_kernel<8><<<M, 128, 0, st>>>(X, R, W, eps, H, Y, RO, S, rows, C);
-  return static_cast<int>(cudaGetLastError());
+  return launch_norm(X, R, W, eps, M, H, Y, RO, S, rows, C, sdc::ShardOut{}, st);
+}
+
+// The tensor-parallel shard norm: add_rmsnorm of this rank's rows into its symmetric shard buffer, with the
+// shard's seals and row_sq, then the generation flag raised on every rank (flag_ptrs: every rank's flag array).
+int sdc_add_rmsnorm_shard(const void* x, const void* residual, const void* w, float eps, int M, int H, void* y,
+                          void* resid_out, void* row_sq, void* seals, int world, int rank,
+                          const unsigned long long* flag_ptrs, void* gen, void* done, void* stream) {
+  if (M <= 0) return 0;
+  if (H % 128 || H > 8192 || world < 1 || world > sdc::peer::MAXW) return -1;
+  sdc::ShardOut so{};
+  so.seal = static_cast<uint32_t*>(seals);
+  so.world = world;
+  so.rank = rank;
+  for (int r = 0; r < world; ++r) so.flag[r] = reinterpret_cast<long long*>(flag_ptrs[r]);
+  so.gen = static_cast<long long*>(gen);
+  so.done = static_cast<unsigned int*>(done);
+  return launch_norm(static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(residual),
+                     static_cast<const __nv_bfloat16*>(w), eps, M, H, static_cast<__nv_bfloat16*>(y),
+                     static_cast<__nv_bfloat16*>(resid_out), static_cast<float*>(row_sq), nullptr, nullptr, so,
+                     static_cast<cudaStream_t>(stream));
 }
 
 int sdc_qk_norm_rope_kv(const void* qkv, long long ld, int T, int nq, int nkv, int head_dim, const int* pos,

@@ -119,10 +119,11 @@ __global__ void __launch_bounds__(256) rs_pull_kernel(Peers parts, Peers seals, 
 
 // One warp per (row, 128-column block) of the full gathered tensor [world * R][N].
 // shards: peers' row shards [R][N]; seals: peers' shard seals [R][nb]; out: full buffer.
+// rss / rs_out (optional): every rank's row_sq of its shard rows, gathered into rs_out [world R] with the rows.
 __global__ void __launch_bounds__(256) ag_pull_kernel(Peers shards, Peers seals, const long long* gen,
                                                       const long long* my_flags, int world, int R, int N,
                                                       __nv_bfloat16* __restrict__ out, unsigned long long* state,
-                                                      int* err) {
+                                                      int* err, Peers rss, float* rs_out) {
   if (!wait_all(gen, my_flags, world, err)) return;
   const int nb = (N + 127) / 128;
   const int lane = threadIdx.x & 31;
@@ -140,6 +141,7 @@ __global__ void __launch_bounds__(256) ag_pull_kernel(Peers shards, Peers seals,
 #pragma unroll
   for (int m = 16; m > 0; m >>= 1) h += __shfl_xor_sync(0xffffffffu, h, m);
   if (col < N) *reinterpret_cast<uint2*>(out + grow * N + col) = v;
+  if (lane == 1 && b == 0 && rs_out != nullptr) rs_out[grow] = __ldcg(static_cast<const float*>(rss.ptr[owner]) + lr);
   if (lane == 0) {
     const uint32_t want = __ldcg(static_cast<const uint32_t*>(seals.ptr[owner]) + lr * nb + b);
     if (want != h) report(state, __int_as_float(0x7f800000), static_cast<unsigned long long>(grow) * nb + b);
@@ -220,14 +222,17 @@ int sdc_tp_reduce_local(const unsigned long long* part_ptrs, const unsigned long
 }
 
 int sdc_tp_all_gather(const unsigned long long* shard_ptrs, const unsigned long long* seal_ptrs, const void* gen,
-                      const void* my_flags, int world, int R, int N, void* out, void* state, int* err, void* stream) {
+                      const void* my_flags, int world, int R, int N, void* out, void* state, int* err,
+                      const unsigned long long* rss_ptrs, void* rs_out, void* stream) {
   if (world < 1 || world > MAXW || N % 8) return -1;
   const long long warps = static_cast<long long>(world) * R * ((N + 127) / 128);
   const unsigned blocks = static_cast<unsigned>((warps * 32 + 255) / 256);
+  Peers rss{};
+  if (rss_ptrs != nullptr) rss = make_peers(rss_ptrs, world);
   ag_pull_kernel<<<blocks > 0 ? blocks : 1, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       make_peers(shard_ptrs, world), make_peers(seal_ptrs, world), static_cast<const long long*>(gen),
       static_cast<const long long*>(my_flags), world, R, N, static_cast<__nv_bfloat16*>(out),
-      static_cast<unsigned long long*>(state), err);
+      static_cast<unsigned long long*>(state), err, rss, rss_ptrs != nullptr ? static_cast<float*>(rs_out) : nullptr);
   return static_cast<int>(cudaGetLastError());
 }
 

@@ -163,18 +163,33 @@ class TPDecoder:
             return torch.matmul(x, w.t(), out=out)
         return gemm.checked_linear(x, cw, self.state.state, self.slot[name], row_sq=row_sq, out=out, seal=seal)
 
-    def _ag(self, shard_src: torch.Tensor, R: int, out: torch.Tensor) -> torch.Tensor:
+    def _ag(self, shard_src: torch.Tensor, R: int, out: torch.Tensor,
+            rs_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """All-gather of the shards; with own collectives the shard norm already sealed and signalled them, and
+        rs_out (when given) receives the gathered row_sq the next checked GEMM needs."""
         if self.collective == "own":
-            return self.comm.all_gather(R, out)
+            return self.comm.all_gather(R, out, rs_out=rs_out, sealed=True)
         return all_gather_nccl(shard_src, out)
 
     def _norm_into_shard(self, x, w, residual, R):
-        """RMSNorm of this rank's rows, written where the all-gather reads them."""
+        """RMSNorm of this rank's rows, written where the all-gather reads them (own collectives: one kernel that
+        also seals the shard, writes its row_sq and signals the peers)."""
         B = self._bufs
-        dst = self.comm.shard(R) if self.collective == "own" else B["ys"][:R]
+        if self.collective == "own":
+            return self.comm.norm_shard(x, w, self.cfg.rms_eps, residual, B["resid"][:R], R)
+        dst = B["ys"][:R]
         layers.add_rmsnorm(x, w, self.cfg.rms_eps, residual=residual, resid_out=B["resid"][:R], out=dst,
                            row_sq=B["rss"][:R])
         return dst
+
+    def _gather_rows(self, ys, R, yfull, rs):
+        """All-gather, and the gathered rows' row_sq for the next checked bf16 GEMM (None otherwise)."""
+        want = self.checked and self.precision == "bf16"
+        if self.collective == "own":
+            self._ag(ys, R, yfull, rs_out=rs if want else None)
+            return rs if want else None
+        self._ag(ys, R, yfull)
+        return gemm.row_sqnorm(yfull, out=rs) if want else None
 
     def _rowpar(self, x, w, cw, name, T, R, row_sq, out_shard, sample=None):
         """Row-parallel GEMM + reduce-scatter into out_shard (R, H)."""
@@ -227,8 +242,7 @@ class TPDecoder:
             ys = self._norm_into_shard(xs, lw.ln1, None if i == 0 else B["resid"][:R], R)
             if chk:
                 self._norm_replay(ys, lw.ln1, R, S_loc, f"L{i}.norm1")
-            self._ag(ys, R, yfull)
-            yrs = gemm.row_sqnorm(yfull, out=rs) if self.checked and self.precision == "bf16" else None
+            yrs = self._gather_rows(ys, R, yfull, rs)
             self._linear(yfull, lw.qkv, lw.cw.get("qkv"), f"L{i}.qkv", qkv, yrs, sample=S)
             layers.qk_norm_rope_kv(qkv, nq, nkv, meta.pos, meta.slots, lw.q_norm, lw.k_norm, cfg.rms_eps, self.rope,
                                    q, lc)
@@ -254,8 +268,7 @@ class TPDecoder:
             ys = self._norm_into_shard(xs, lw.ln2, B["resid"][:R], R)
             if chk:
                 self._norm_replay(ys, lw.ln2, R, S_loc, f"L{i}.norm2")
-            self._ag(ys, R, yfull)
-            yrs = gemm.row_sqnorm(yfull, out=rs) if self.checked and self.precision == "bf16" else None
+            yrs = self._gather_rows(ys, R, yfull, rs)
             self._linear(yfull, lw.gate_up, lw.cw.get("gate_up"), f"L{i}.gate_up", gu, yrs, sample=S)
             layers.silu_mul(gu, out=act, row_sq=rs)
             if chk:

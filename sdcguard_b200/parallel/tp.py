@@ -41,11 +41,13 @@ class TPComm:
         self.part_seal = heap.alloc([2 * max_rows, nb], torch.int32)
         self.shard_buf = heap.alloc([max_rows // self.world, hidden], torch.bfloat16)
         self.shard_seal = heap.alloc([max_rows // self.world, nb], torch.int32)
+        self.shard_rss = heap.alloc([max_rows // self.world], torch.float32)   # row_sq of the shard rows
         self.flags = heap.alloc([self.world], torch.int64)
         self.gen = torch.zeros(1, dtype=torch.int64, device=heap.device)
         self.err = torch.zeros(1, dtype=torch.int32, device=heap.device)
         self.state = torch.zeros(2, abft.STATE_COLS, dtype=torch.int64, device=heap.device)   # 0: RS, 1: AG
         self.done = torch.zeros(1, dtype=torch.int32, device=heap.device)     # push-mode GEMM: CTAs finished
+        self.norm_done = torch.zeros(1, dtype=torch.int32, device=heap.device)   # shard norm: CTAs finished
         self._inject: Optional[tuple] = None
 
     def inject_next(self, row: int, col: int, bit: int = 0) -> None:
@@ -142,15 +144,32 @@ class TPComm:
             self.err.data_ptr(), self._s()), "tp reduce (local)")
         return out
 
-    def all_gather(self, R: int, out: torch.Tensor) -> torch.Tensor:
-        """Seals this rank's shard(R), signals, waits, and gathers every rank's shard into out (world R, hidden),
-        checking each row block against its owner's seal."""
-        _native.check(_native.lib().sdc_seal_rows(self.shard_buf.local.data_ptr(), self.hidden, R, self.hidden,
-                                                  self.shard_seal.local.data_ptr(), self._s()), "seal rows")
-        self.signal()
+    def norm_shard(self, x: torch.Tensor, weight: torch.Tensor, eps: float, residual: Optional[torch.Tensor],
+                   resid_out: torch.Tensor, R: int) -> torch.Tensor:
+        """add_rmsnorm of this rank's R rows straight into its shard buffer, in one kernel that also writes the
+        shard's seals and row_sq and, when every row is written, raises this rank's flag on every rank (the
+        all-gather's signal). Follow with all_gather(R, out, sealed=True)."""
+        _native.check(_native.lib().sdc_add_rmsnorm_shard(
+            x.data_ptr(), None if residual is None else residual.data_ptr(), weight.data_ptr(), float(eps), R,
+            self.hidden, self.shard_buf.local.data_ptr(), resid_out.data_ptr(), self.shard_rss.local.data_ptr(),
+            self.shard_seal.local.data_ptr(), self.world, self.rank, self.flags.ptrs, self.gen.data_ptr(),
+            self.norm_done.data_ptr(), self._s()), "shard norm")
+        return self.shard(R)
+
+    def all_gather(self, R: int, out: torch.Tensor, rs_out: Optional[torch.Tensor] = None,
+                   sealed: bool = False) -> torch.Tensor:
+        """Gathers every rank's shard into out (world R, hidden), checking each row block against its owner's seal.
+        Unless `sealed` (the shard came from norm_shard, which sealed it and signalled), seals this rank's shard
+        and signals first. rs_out: also gather the shards' row_sq (written by norm_shard)."""
+        if not sealed:
+            _native.check(_native.lib().sdc_seal_rows(self.shard_buf.local.data_ptr(), self.hidden, R, self.hidden,
+                                                      self.shard_seal.local.data_ptr(), self._s()), "seal rows")
+            self.signal()
         _native.check(_native.lib().sdc_tp_all_gather(
             self.shard_buf.ptrs, self.shard_seal.ptrs, self.gen.data_ptr(), self.flags.local.data_ptr(), self.world,
-            R, self.hidden, out.data_ptr(), self.state[1].data_ptr(), self.err.data_ptr(), self._s()), "tp all-gather")
+            R, self.hidden, out.data_ptr(), self.state[1].data_ptr(), self.err.data_ptr(),
+            self.shard_rss.ptrs if rs_out is not None else None, None if rs_out is None else rs_out.data_ptr(),
+            self._s()), "tp all-gather")
         return out
 
     def close(self) -> None:
