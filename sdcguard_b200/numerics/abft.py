@@ -225,3 +225,56 @@ def locate(flat: int, nb: int) -> tuple[int, int, bool]:
     row, rem = divmod(flat, nb * 2)
     block, which = divmod(rem, 2)
     return row, block, bool(which)
+
+
+def product_zscores(a: torch.Tensor, b: torch.Tensor, c: torch.Tensor, mask: tuple,
+                    rnd_unit: float = 0.0, judged: Optional[torch.Tensor] = None,
+                    z_alarm: float = Z_ALARM) -> torch.Tensor:
+    """Scores of batched products c ~ a @ b made by another library (cuBLAS, CPU BLAS), in float64 torch ops:
+    a (G, m, k), b (G, k, n), c (G, m, n) the product as the library returned it (already freed of any bias,
+    alpha and beta). Returns (G, m, nb) scores, the larger of plain and signed; inf = corruption, -1 = not judged.
+
+    The noise model is the accumulator model above with b's blocks in place of W's (the plain and signed block
+    sums of b are formed here in float64, so the expected side adds only its own float64 rounding). When c was
+    rounded to a narrower type (rnd_unit = its unit roundoff, 2^-8 for bf16), each element may differ from the
+    accumulator by up to rnd_unit |c| with a sign that varies from element to element: the statistical bound grows by
+    rnd_unit ||c_b||_2 and the worst-case bound of the plain sum by 1.25 rnd_unit ||c_b||_1. judged: optional (G, m, nb) bool,
+    False where the inputs themselves hold non-finite values (a product block that is then not scored).
+    Reference: src/sdcguard/checksum.py (`matmul_zscores` on the rounded output, `matmul_zscores_acc` on the
+    accumulator)."""
+    G, m, k = a.shape
+    n = b.shape[-1]
+    nb = -(-n // BLOCK)
+    pad = nb * BLOCK - n
+    s = sign_vector(mask, device=a.device)
+    bb = torch.nn.functional.pad(b.double(), (0, pad)).view(G, k, nb, BLOCK)
+    plain = bb.sum(-1)
+    signed = (bb * s).sum(-1)                                                  # (G, k, nb)
+    wmax = torch.stack([bb.square().sum((1, 3)).sqrt(), torch.linalg.vector_norm(plain, dim=1),
+                        torch.linalg.vector_norm(signed, dim=1)], -1).amax(-1)       # (G, nb)
+    babs = bb.abs().amax((1, 3))                                               # (G, nb)
+    del bb
+    a64 = a.double()
+    exp = torch.bmm(a64, torch.cat([plain, signed], -1)).view(G, m, 2, nb)
+    cc = torch.nn.functional.pad(c.double(), (0, pad)).view(G, m, nb, BLOCK)
+    sp, ssg = cc.sum(-1), (cc * s).sum(-1)
+    l2, l1 = cc.square().sum(-1).sqrt(), cc.abs().sum(-1)
+    fin_act = torch.isfinite(cc).all(-1)
+    del cc
+    prod_coef, out_coef = coefficients(k)
+    xn = torch.linalg.vector_norm(a64, dim=2).unsqueeze(-1)                  # (G, m, 1)
+    prod = prod_coef * xn * wmax.unsqueeze(1)
+    den = l2 * (out_coef + rnd_unit) + prod + ABS_FLOOR
+    worst = l1 * (out_coef + 1.25 * rnd_unit) + prod + ABS_FLOOR
+    dp = (exp[:, :, 0] - sp).abs()
+    ds = (exp[:, :, 1] - ssg).abs()
+    z = torch.maximum(torch.minimum(dp / den, dp / worst * z_alarm), ds / den)
+    fin_exp = torch.isfinite(exp).all(2)
+    bound = math.sqrt(k) * xn * babs.unsqueeze(1)
+    ok = torch.isfinite(a64).all(-1, keepdim=True) & torch.isfinite(babs).unsqueeze(1)
+    if judged is not None:
+        ok = ok & judged
+    bad = ~fin_act & fin_exp & ok
+    z = torch.where(bad & (bound < BIG), torch.full_like(z, math.inf), z)
+    z = torch.where((bad & ~(bound < BIG)) | ~fin_exp | ~ok, torch.full_like(z, -1.0), z)
+    return torch.where(torch.isnan(z), torch.full_like(z, -1.0), z)
