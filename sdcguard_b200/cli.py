@@ -15,6 +15,10 @@
     sdcguard serve / ready / perf / isolation / consistency  HTTP server and outside-in probes
     sdcguard qualify / decide                                stack-change qualification and decision
     sdcguard lifetime / assess / bundle                      KV lifetime explorer, scoped assessment, evidence bundle
+    sdcguard config-safety / record-plan / operator-setup    static deployment contracts, recording plan, setup files
+    sdcguard evidence / report-verify / upgrade              evidence report envelope, its verification, upgrade policy
+    sdcguard inventory / overhead / model-ref                client batch join, matched-run overhead, model file binding
+    sdcguard assignment / forward-inputs / regression        recorded page assignment, forward inputs, saved case
     sdcguard version
 
 The first three keep the reference's commands, exit codes and output (src/sdcguard/cli.py:343-463 dispatch).
@@ -67,6 +71,18 @@ COMMANDS = {
     "lifetime": _lazy(".lifetime.__main__", "main"),
     "assess": _lazy(".evidence.assessment", "main"),
     "bundle": _lazy(".evidence.bundle", "main"),
+    "config-safety": _lazy(".evidence.config", "main"),
+    "record-plan": _lazy(".evidence.recording_plan", "main"),
+    "operator-setup": _lazy(".evidence.operator_setup", "main"),
+    "evidence": _lazy(".evidence.report", "main"),
+    "report-verify": _lazy(".evidence.report", "verify_main"),
+    "upgrade": _lazy(".evidence.upgrade", "main"),
+    "inventory": _lazy(".evidence.inventory", "main"),
+    "overhead": _lazy(".evidence.overhead", "main"),
+    "model-ref": _lazy(".evidence.model_reference", "main"),
+    "assignment": _lazy(".evidence.assignment", "main"),
+    "forward-inputs": _lazy(".evidence.forward", "main"),
+    "regression": _lazy(".evidence.regression", "main"),
     "version": _version,
 }
 

@@ -64,7 +64,32 @@ def assess(recording: str, events: Optional[str] = None, ready_url: Optional[str
     else:
         v = "HOLD"
     out["verdict"] = v
+    out["findings"] = _findings(out, bool(events), bool(ready_url))
     return out
+
+
+def _findings(out: dict, have_events: bool, asked_ready: bool) -> list[dict]:
+    """The assessment's parts as catalog findings (for `evidence.report`)."""
+    from . import catalog
+    cov = out["coverage"]
+    d = cov.get("decision")
+    fs = [catalog.finding("recording.coverage", {"PASS": "satisfied", "HOLD": "unknown"}.get(d, "violated")
+                          if d != "ERROR" else "unknown",
+                          f"coverage gate {d}" + (f": {', '.join(cov.get('hold_reasons', []))}"
+                                                  if cov.get("hold_reasons") else ""),
+                          "recording", {"requests": cov.get("requests"), "reasons": cov.get("reasons", [])})]
+    lt = out["lifetime"]
+    fs.append(catalog.finding("recording.lifetime", "unknown" if not have_events else
+                              ("violated" if lt["violations"] else "satisfied"),
+                              "no lifetime events recorded" if not have_events else
+                              f"{len(lt['violations'])} ledger violation(s) in {lt['events']} events",
+                              "recorded lifetime events", {"events": lt.get("events", 0)}))
+    if asked_ready:
+        rv = out["readiness"].get("verdict")
+        fs.append(catalog.finding("recording.readiness", "satisfied" if rv == "PROTECTED" else
+                                  ("violated" if rv == "FAULT FOUND" else "unknown"), f"readiness {rv}",
+                                  "read-only endpoint"))
+    return fs
 
 
 def main(argv=None) -> int:

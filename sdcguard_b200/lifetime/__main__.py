@@ -1,6 +1,8 @@
 """python -m sdcguard_b200.lifetime explore --model pd-abort:buggy [--budget 3]
    python -m sdcguard_b200.lifetime explore --all
-   python -m sdcguard_b200.lifetime check events.jsonl"""
+   python -m sdcguard_b200.lifetime check events.jsonl
+   python -m sdcguard_b200.lifetime realsearch --toy push|pull|wakeup [--fixed]   (model-free search of real code)
+   python -m sdcguard_b200.lifetime conformance [--json]                          (pd.py components, CPU mocks)"""
 from __future__ import annotations
 
 import argparse
@@ -21,7 +23,21 @@ def main(argv=None) -> int:
     e.add_argument("--budget", type=int, default=3)
     c = sub.add_parser("check")
     c.add_argument("events")
+    rs = sub.add_parser("realsearch")
+    rs.add_argument("--toy", required=True, choices=("push", "pull", "wakeup"))
+    rs.add_argument("--fixed", action="store_true")
+    rs.add_argument("--json", action="store_true")
+    cf = sub.add_parser("conformance")
+    cf.add_argument("--json", action="store_true")
     a = ap.parse_args(argv)
+    if a.cmd == "realsearch":
+        from . import realsearch, toys
+        r = realsearch.search(lambda: toys.TOYS[a.toy](fixed=a.fixed))
+        print(json.dumps(r.as_dict(), indent=1) if a.json else realsearch.text(r))
+        return 1 if r.findings else 0
+    if a.cmd == "conformance":
+        from . import conformance
+        return conformance.main(["--json"] if a.json else [])
     if a.cmd == "check":
         r = adapter.check(adapter.load(a.events))
         print(json.dumps(r, indent=1))

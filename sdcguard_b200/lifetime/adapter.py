@@ -8,6 +8,8 @@ Event lines (one JSON object each; "region" is [pool, index], "gen" the allocati
   {"ev": "submit", "op": id, "kind": "read"|"write"|"load", "by": who, "src": [r, g] | null, "dst": [r, g] | null}
   {"ev": "land", "op": id}   {"ev": "complete", "op": id, "mark": [r, g] | null}   {"ev": "stop", "op": id}
   {"ev": "consume", "region": r, "gen": g, "request": req}
+  {"ev": "forward", "phase": "prefill"|"decode", "request": req, "regions": [[pool, idx, gen], ...],
+   "positions": [first, last]}      (the block table one forward pass used for a request; not a ledger action)
 
 `serve/pd.py` writes these for the prefill/decode path (producer pages, pulled pages, shared prefix pages, the decode
 that consumes them, the frees). A model finding (models.py) is a candidate ordering; this is where a real run is held
@@ -86,6 +88,12 @@ class EventSink:
         r, g = self.handle(pool, idx)
         self._emit({"ev": "consume", "region": r, "gen": g, "request": request})
 
+    def forward(self, phase: str, request: str, pool: str, pages, first: int, last: int) -> None:
+        """The block table a forward pass of `request` used (positions first..last), with each page's generation."""
+        self._emit({"ev": "forward", "phase": phase, "request": request,
+                    "regions": [[pool, int(p), self.gen.get((pool, int(p)), 0)] for p in pages],
+                    "positions": [int(first), int(last)]})
+
     def close(self) -> None:
         if self._f:
             self._f.close()
@@ -129,6 +137,8 @@ def check(events: Iterable[dict]) -> dict:
             led.stop(e["op"])
         elif k == "consume":
             led.consume(Handle(tuple(e["region"]), e["gen"]), e["request"])
+        elif k == "forward":
+            pass                          # judged by evidence.forward against the ownership the events record
         else:
             raise ValueError(f"unknown event {k!r} at line {i}")
     return {"events": n, "violations": [{"rule": v.rule, "step": v.step, "message": v.message}

@@ -90,6 +90,18 @@ class LLMEngine:
         self.phase_timing = False          # record device time of the prefill and decode phases of generate()
         self.last_phase_ms: dict = {}
 
+    def describe(self) -> dict:
+        """The engine's configuration as the offline deployment contracts read it (`evidence/config.py`)."""
+        from .. import __version__
+        return {"engine": "sdcguard_b200", "version": __version__, "model": self.cfg.name,
+                "kv_pages": int(self.alloc.num_blocks), "page_tokens": PAGE, "max_num_seqs": self.max_num_seqs,
+                "max_model_len": self.max_model_len, "checked": bool(self.checked), "sample_every": self.sample_every,
+                "kv_page_bytes": kv_bytes_per_page(self.cfg, self.model.nkv)}
+
+    def startup_line(self) -> str:
+        """One line for the startup log: `sdcguard_b200 engine: key=value ...` (parsed by `evidence.config`)."""
+        return "sdcguard_b200 engine: " + " ".join(f"{k}={v}" for k, v in self.describe().items())
+
     # ---------------------------------------------------------------- sampling of replay rows
     def _sample(self, n: int) -> list[int]:
         salt = self.step_counter % self.sample_every

@@ -182,9 +182,11 @@ def produce(engine: LLMEngine, requests: list[tuple[str, list]], seed: int = kvx
     gens = None
     if sink is not None:
         gens = []
-        for (rid, _), pg in zip(requests, pages):
+        for (rid, _), pg, n in zip(requests, pages, plens):
             for p in pg:
                 sink.alloc(pool, p, rid)
+            sink.forward("prefill", rid, pool, pg, 0, n - 1)
+            for p in pg:
                 sink.local_write(pool, p, rid)
             gens.append([sink.gen[(pool, p)] for p in pg])
     flat = torch.tensor([p for pg in pages for p in pg], dtype=torch.int32, device=dev)
@@ -260,6 +262,7 @@ def consume(engine: LLMEngine, transfers: Sequence[Transfer], src_cache: torch.T
         for t, pg in zip(transfers, local_pages):
             for p in pg[:len(t.pages)]:
                 sink.consume("decode", p, t.request_id)
+            sink.forward("decode", t.request_id, "decode", pg, t.prompt_tokens, t.prompt_tokens + max_new_tokens - 2)
     engine.decode_from([t.prompt_tokens for t in transfers], local_pages, out, max_new_tokens)
     host = out.cpu()
     for pg in owned:
