@@ -27,6 +27,7 @@
 //     The wait cannot deadlock: a tile only waits for tiles earlier in the order, and every CTA of the
 //     persistent grid is resident.
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -115,7 +116,9 @@ struct Cfg {
   static constexpr int THREADS = 128 + NWG * 128;
   static constexpr int CSB = 20 * NWG;                 // checksum blocks per checksum tile (120 columns per WG)
   static constexpr int STAGING_BYTES = NWG * 4 * 4096;  // per epilogue warp: 32 rows x 128 B of bf16 output
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + STAGING_BYTES + 1024 /*align*/ + 512 /*control*/;
+  static constexpr int CTL_BYTES = 1024;               // SmemCtl
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + STAGING_BYTES + 1024 /*align*/ + CTL_BYTES;
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory per CTA");
 };
 
 struct SmemCtl {
@@ -130,12 +133,11 @@ struct SmemCtl {
   uint32_t tmem_base;
   int abort_flag;
   int ready_ok[2];         // 0 when the coordinator gave up waiting for the band
-  unsigned long long wkey0[8];   // per epilogue warp: worst (z, flat) key of the tile
-  unsigned long long wkey1[8];   // per epilogue warp: worst (z, noise) key
-  int wunj[8];                   // per epilogue warp: pairs left unjudged
-  unsigned long long res0[2], res1[2];
-  int resunj[2];
+  unsigned long long wkey0[2][8];   // per accumulator, per epilogue warp: worst (z, flat) key of the tile
+  unsigned long long wkey1[2][8];   // per accumulator, per epilogue warp: worst (z, noise) key
+  int wunj[2][8];                   // per accumulator, per epilogue warp: pairs left unjudged
 };
+static_assert(sizeof(SmemCtl) <= Cfg<128>::CTL_BYTES && sizeof(SmemCtl) <= Cfg<256>::CTL_BYTES, "control block");
 
 // Persistent tile order. Bands (128 output rows) are taken in groups of `group` bands; inside a group come
 // first the checksum tiles of all its bands, then its output tiles column-major (the `group` bands of one
@@ -222,6 +224,54 @@ __device__ __forceinline__ void judge_pair(const Params& p, int row, int b, floa
   } else {
     unj = 1;
   }
+}
+
+// An output tile's block sums, kept by the epilogue thread that owns the row until the tile is judged.
+struct Pending {
+  bool live;        // a tile waits to be judged
+  bool valid;       // this thread has a (row, block) pair in it
+  int acc;          // accumulator slot and its phase when the tile was taken
+  uint32_t phase;
+  int row, b;
+  float P, S, Q, A;
+};
+
+// Judge the pending output tile of this warp (if any) and hand the warp's worst keys to the coordinator: wait
+// (bounded) for the band's expected sums, judge this thread's pair, reduce over the warp, and (lane 0) arrive on
+// the tile's result barrier once the coordinator has published the slot's previous result.
+template <int NWG>
+__device__ __forceinline__ void judge_pending(const Params& p, SmemCtl* ctl, Pending& pd, int ew, int lane,
+                                              volatile int* abort_flag) {
+  if (!pd.live) return;
+  pd.live = false;
+  // the coordinator has waited (bounded) for the band's expected sums; skip judging if it gave up
+  const bool ready = mbar_wait(&ctl->ready[pd.acc], pd.phase, abort_flag) && ctl->ready_ok[pd.acc] != 0;
+  unsigned long long k0 = 0ull, k1 = 0ull;
+  int unj = 0;
+  if (pd.valid) {
+    if (!ready)
+      unj = 1;
+    else
+      judge_pair(p, pd.row, pd.b, pd.P, pd.S, pd.Q, pd.A,
+                 __ldcg(p.expd + static_cast<long long>(pd.row) * p.nb + pd.b), k0, k1, unj);
+  }
+  k0 = warp_max_u64(k0);
+  k1 = warp_max_u64(k1);
+#pragma unroll
+  for (int m = 16; m > 0; m >>= 1) unj += __shfl_xor_sync(0xffffffffu, unj, m);
+  if (lane == 0) {
+    mbar_wait(&ctl->resempty[pd.acc], pd.phase ^ 1u, abort_flag);
+    ctl->wkey0[pd.acc][ew] = k0;
+    ctl->wkey1[pd.acc][ew] = k1;
+    ctl->wunj[pd.acc][ew] = unj;
+    mbar_arrive(&ctl->resfull[pd.acc]);
+  }
+}
+
+// Element k (0..23, a compile-time constant after unrolling) of three 8-register TMEM loads.
+__device__ __forceinline__ uint32_t pick24(const uint32_t (&a)[8], const uint32_t (&b)[8], const uint32_t (&c)[8],
+                                           int k) {
+  return k < 8 ? a[k] : (k < 16 ? b[k - 8] : c[k - 16]);
 }
 
 // Split-K reduce and check: one warp per (row, 128-column block); lane l owns columns 4l .. 4l+3. Sums the
@@ -317,6 +367,22 @@ __global__ void __launch_bounds__(256) split_reduce_kernel(const Params p) {
   }
 }
 
+// Split-K tuning (read once from the environment; the defaults are the measured policy):
+//   SDCGUARD_GEMM_SPLIT_MIN_K   smallest K that splits (default 2048)
+//   SDCGUARD_GEMM_SPLIT         force this many splits where splitting is eligible (default 0: from the SM count)
+static void split_policy(int* min_k, int* force) {
+  static int mk = -1, fs = 0;
+  if (mk < 0) {
+    const char* a = std::getenv("SDCGUARD_GEMM_SPLIT_MIN_K");
+    const char* b = std::getenv("SDCGUARD_GEMM_SPLIT");
+    mk = a ? std::atoi(a) : 2048;
+    fs = b ? std::atoi(b) : 0;
+    if (mk < 64) mk = 64;
+  }
+  *min_k = mk;
+  *force = fs;
+}
+
 template <int BN, bool INJ>
 __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
     gemm_abft_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
@@ -344,7 +410,7 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
     mbar_init(&ctl->drain, 1);
     for (int a = 0; a < 2; ++a) {
       mbar_init(&ctl->ready[a], 1);
-      mbar_init(&ctl->resfull[a], 1);
+      mbar_init(&ctl->resfull[a], C::NWG * 4);   // one arrival per epilogue warp
       mbar_init(&ctl->resempty[a], 1);
     }
     ctl->abort_flag = 0;
@@ -508,8 +574,14 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
           fence_acq_rel_gpu();      // release the CTA's expected sums of this tile
           atomicAdd(p.cs_done + mt, 1);
         } else {
-          const unsigned long long a0 = ctl->res0[acc], a1 = ctl->res1[acc];
-          const int u = ctl->resunj[acc];
+          unsigned long long a0 = 0ull, a1 = 0ull;
+          int u = 0;
+#pragma unroll
+          for (int w = 0; w < 4 * C::NWG; ++w) {
+            a0 = ctl->wkey0[acc][w] > a0 ? ctl->wkey0[acc][w] : a0;
+            a1 = ctl->wkey1[acc][w] > a1 ? ctl->wkey1[acc][w] : a1;
+            u += ctl->wunj[acc][w];
+          }
           // most tiles of a clean run are below the running maximum: skip their atomics
           if (a0 > ld_relaxed_gpu_u64(st + 0)) atomicMax(st + 0, a0);
           if (a1 > ld_relaxed_gpu_u64(st + 1)) atomicMax(st + 1, a1);
@@ -541,6 +613,12 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
     const long long push_off = p.push.on ? ((__ldcg(p.push.gen) + 1) & 1) * p.push.cap : 0;
     int acc = 0;
     uint32_t acc_phase = 0;
+    // The judge of an output tile runs one tile later, after the next tile's body: by then the band's expected
+    // sums (from checksum tiles on other CTAs) have had a tile's time to arrive, so the epilogue does not wait.
+    // Each warp hands its worst keys to the coordinator through an mbarrier (one arrival per warp); there is no
+    // named barrier in the loop, so a warp that gives up leaves no other warp waiting.
+    Pending pend;
+    pend.live = false;
     for (int tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x) {
       int mt, idx;
       bool cs;
@@ -549,9 +627,8 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
       const unsigned long long t_w0 = p.dbg ? globaltimer() : 0ull;
       const bool got = mbar_wait(&ctl->tfull[acc], acc_phase, abort_flag);
       const unsigned long long t_w1 = p.dbg ? globaltimer() : 0ull;
-      // every epilogue warp leaves together if any of them gave up (no named barrier is left waiting)
-      if (named_bar_or(1, C::NWG * 128, !got)) {
-        if (!got) record_error(p.err, ERR_TIMEOUT_EPILOGUE);
+      if (!got) {
+        record_error(p.err, ERR_TIMEOUT_EPILOGUE);
         *abort_flag = 1;
         break;
       }
@@ -569,16 +646,18 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
           for (int i4 = 0; i4 < 5; ++i4) {
             const int bb = blk0 + i4 * 4;
             if (bb < p.nb) {
-              uint32_t r[24];
+              uint32_t r0[8], r1[8], r2[8];
               const uint32_t ta = tacc + static_cast<uint32_t>(g * 120 + i4 * 24);
-              tmem_ld8(ta, *reinterpret_cast<uint32_t(*)[8]>(&r[0]));
-              tmem_ld8(ta + 8, *reinterpret_cast<uint32_t(*)[8]>(&r[8]));
-              tmem_ld8(ta + 16, *reinterpret_cast<uint32_t(*)[8]>(&r[16]));
+              tmem_ld8(ta, r0);
+              tmem_ld8(ta + 8, r1);
+              tmem_ld8(ta + 16, r2);
               tmem_wait_ld();
               if (row < p.M) {
                 const int nbk = min(4, p.nb - bb);
                 float* dst = prow + p.N + static_cast<long long>(bb) * 6;
-                for (int j = 0; j < 6 * nbk; ++j) dst[j] = u32_as_f32(r[j]);
+#pragma unroll
+                for (int j = 0; j < 24; ++j)
+                  if (j < 6 * nbk) dst[j] = u32_as_f32(pick24(r0, r1, r2, j));
               }
             }
           }
@@ -611,11 +690,8 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
         for (int i4 = 0; i4 < 5; ++i4) {
           const int bb = blk0 + i4 * 4;
           if (bb < p.nb) {  // warp-uniform
-            uint32_t r[24];
+            uint32_t r0[8], r1[8], r2[8];         // three separate arrays: stay in registers
             const uint32_t ta = tacc + static_cast<uint32_t>(g * 120 + i4 * 24);
-            uint32_t (&r0)[8] = *reinterpret_cast<uint32_t(*)[8]>(&r[0]);
-            uint32_t (&r1)[8] = *reinterpret_cast<uint32_t(*)[8]>(&r[8]);
-            uint32_t (&r2)[8] = *reinterpret_cast<uint32_t(*)[8]>(&r[16]);
             tmem_ld8(ta, r0);
             tmem_ld8(ta + 8, r1);
             tmem_ld8(ta + 16, r2);
@@ -625,8 +701,11 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
               for (int i = 0; i < 4; ++i) {
                 const int b = bb + i;
                 if (b < p.nb) {
-                  const float ep = u32_as_f32(r[6 * i]) + u32_as_f32(r[6 * i + 1]) + u32_as_f32(r[6 * i + 2]);
-                  const float es = u32_as_f32(r[6 * i + 3]) + u32_as_f32(r[6 * i + 4]) + u32_as_f32(r[6 * i + 5]);
+                  const float ep = u32_as_f32(pick24(r0, r1, r2, 6 * i)) + u32_as_f32(pick24(r0, r1, r2, 6 * i + 1)) +
+                                   u32_as_f32(pick24(r0, r1, r2, 6 * i + 2));
+                  const float es = u32_as_f32(pick24(r0, r1, r2, 6 * i + 3)) +
+                                   u32_as_f32(pick24(r0, r1, r2, 6 * i + 4)) +
+                                   u32_as_f32(pick24(r0, r1, r2, 6 * i + 5));
                   p.expd[static_cast<long long>(row) * p.nb + b] = make_float2(ep, es);
                 }
               }
@@ -635,10 +714,14 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
         }
         tc_fence_before();
         mbar_arrive(&ctl->tempty[acc]);
-        named_bar_sync(1, C::NWG * 128);
-        if (et == 0) {
-          // hand the tile to the coordinator, which releases the expected sums to other CTAs
+        judge_pending<C::NWG>(p, ctl, pend, ew, lane, abort_flag);
+        // hand this warp's part of the tile to the coordinator, which releases the expected sums to other CTAs
+        __syncwarp();
+        if (lane == 0) {
           mbar_wait(&ctl->resempty[acc], acc_phase ^ 1u, abort_flag);
+          ctl->wkey0[acc][ew] = 0ull;
+          ctl->wkey1[acc][ew] = 0ull;
+          ctl->wunj[acc][ew] = 0;
           mbar_arrive(&ctl->resfull[acc]);
         }
       } else {
@@ -715,45 +798,23 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
         }
         tc_fence_before();
         mbar_arrive(&ctl->tempty[acc]);   // the MMA warp may refill this accumulator now
-
-        // the coordinator has waited (bounded) for the band's expected sums; skip judging if it gave up
-        bool ready = mbar_wait(&ctl->ready[acc], acc_phase, abort_flag) && ctl->ready_ok[acc] != 0;
-        const bool skip = named_bar_or(1, C::NWG * 128, !ready);
-        unsigned long long k0 = 0ull, k1 = 0ull;
-        int unj = 0;
-        if (have && row < p.M) {
-          if (skip) {
-            unj = 1;
-          } else {
-            const int b = col0 / CSW;
-            judge_pair(p, row, b, P, S, Q, Aab, __ldcg(p.expd + static_cast<long long>(row) * p.nb + b), k0, k1, unj);
-          }
+        const unsigned long long t_e0 = p.dbg ? globaltimer() : 0ull;
+        judge_pending<C::NWG>(p, ctl, pend, ew, lane, abort_flag);
+        if (p.dbg && et == 0) {
+          unsigned long long* d = p.dbg + blockIdx.x * 8;
+          d[3] += t_e0 - t_w1;            // output tile: TMEM -> registers -> staging -> TMA store issued
+          d[4] += globaltimer() - t_e0;   // judging the previous output tile (including its wait)
         }
-        k0 = warp_max_u64(k0);
-        k1 = warp_max_u64(k1);
-#pragma unroll
-        for (int m = 16; m > 0; m >>= 1) unj += __shfl_xor_sync(0xffffffffu, unj, m);
-        if (lane == 0) {
-          ctl->wkey0[ew] = k0;
-          ctl->wkey1[ew] = k1;
-          ctl->wunj[ew] = unj;
-        }
-        named_bar_sync(1, C::NWG * 128);
-        if (et == 0) {
-          unsigned long long a0 = 0ull, a1 = 0ull;
-          int u = 0;
-#pragma unroll
-          for (int w = 0; w < 4 * C::NWG; ++w) {
-            a0 = ctl->wkey0[w] > a0 ? ctl->wkey0[w] : a0;
-            a1 = ctl->wkey1[w] > a1 ? ctl->wkey1[w] : a1;
-            u += ctl->wunj[w];
-          }
-          mbar_wait(&ctl->resempty[acc], acc_phase ^ 1u, abort_flag);
-          ctl->res0[acc] = a0;
-          ctl->res1[acc] = a1;
-          ctl->resunj[acc] = u;
-          mbar_arrive(&ctl->resfull[acc]);   // the coordinator publishes it
-        }
+        pend.live = true;
+        pend.valid = have && row < p.M;
+        pend.acc = acc;
+        pend.phase = acc_phase;
+        pend.row = row;
+        pend.b = col0 / CSW;
+        pend.P = P;
+        pend.S = S;
+        pend.Q = Q;
+        pend.A = Aab;
       }
       if (p.dbg && et == 0) {
         unsigned long long* d = p.dbg + blockIdx.x * 8;
@@ -766,6 +827,7 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
         acc_phase ^= 1u;
       }
     }
+    judge_pending<C::NWG>(p, ctl, pend, ew, lane, abort_flag);   // the last output tile
   }
 
   if (warp >= 4 && lane == 0) {
@@ -951,9 +1013,11 @@ static int gemm_run(const void* A, long long lda, const void* W, const void* Wc,
     p.push.done = static_cast<unsigned int*>(push->done);
   }
   // splitting pays when each CTA would stream a long K (measured: K = 1024 is faster unsplit)
-  if (allow_split && push == nullptr && split_eligible(M, N) && K >= 2048 && max_ctas == 0 && dbg == nullptr) {
+  int split_min_k, split_force;
+  split_policy(&split_min_k, &split_force);
+  if (allow_split && push == nullptr && split_eligible(M, N) && K >= split_min_k && max_ctas == 0 && dbg == nullptr) {
     const int kblocks = (K + BK - 1) / BK;
-    int sp = num_sms_cached() / p.total_tiles;
+    int sp = split_force > 0 ? split_force : num_sms_cached() / p.total_tiles;
     sp = sp > kMaxSplit ? kMaxSplit : sp;
     sp = sp > kblocks / 4 ? kblocks / 4 : sp;
     if (sp >= 2) {

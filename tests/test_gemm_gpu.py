@@ -89,12 +89,13 @@ def test_state_accumulates_over_calls():
 
 
 @pytest.mark.parametrize("bn", [128, 256])
-def test_split_k_small_m_output_check_seal_and_injection(bn):
-    """Decode-sized M runs split over K (partial accumulators, then the reduce-and-judge kernel)."""
+@pytest.mark.parametrize("m,n,k", [(64, 1024, 4096), (256, 4096, 1024), (256, 1024, 3072)])
+def test_split_k_small_m_output_check_seal_and_injection(bn, m, n, k):
+    """Decode-sized M runs split over K where K is long (partial accumulators, then the reduce-and-judge
+    kernel), and unsplit otherwise; both give the fused check's answers."""
     from sdcguard_b200.ops import gemm
     torch.manual_seed(3)
     dev = torch.device("cuda")
-    m, n, k = 64, 1024, 4096
     x = torch.randn(m, k, device=dev).to(torch.bfloat16)
     w = (torch.randn(n, k, device=dev) * 0.02).to(torch.bfloat16)
     b = torch.randn(n, device=dev) * 0.1
