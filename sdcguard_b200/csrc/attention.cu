@@ -419,9 +419,12 @@ __global__ void __launch_bounds__(128 + 2 * ROWS, 1) prefill_tc_kernel(const __g
 
 // ---------------------------------------------------------------------------------------------- decode
 // Split-KV decode ("flash decoding"): the keys of each (sequence, kv head) are cut into chunks of SPLIT keys at
-// absolute multiples of SPLIT; one CTA per chunk writes the chunk's softmax statistics and unnormalised output,
-// and a combine kernel merges the chunks of a row in a fixed order. Chunk boundaries and reduction orders
-// depend only on the row, so a replay of any subset of sequences reproduces their outputs bit for bit.
+// absolute multiples of SPLIT, and the chunks into segments of SEG chunks. One CTA takes a whole segment: it
+// merges the segment's chunks in order with the running-maximum softmax and writes one record (the segment's
+// softmax statistics and unnormalised output); a combine kernel merges the segments of a row in a fixed order.
+// Chunk and segment boundaries and every reduction order depend only on the row, so a replay of any subset of
+// sequences reproduces their outputs bit for bit. (One record per segment instead of one per chunk cuts the
+// record traffic of both kernels by SEG.)
 //
 // Memory path: decode reads every K and V byte of the context once, so the kernel is bound by HBM. A CTA owns
 // one (sequence, kv head) and every gridDim.z-th chunk of it; TMA copies each chunk's pages (one 16-row x
@@ -434,6 +437,8 @@ __global__ void __launch_bounds__(128 + 2 * ROWS, 1) prefill_tc_kernel(const __g
 // shared memory, then O_w = P V with P kept in registers as the A operand. The chunk record is the sum of the
 // four warps' O in a fixed order, so it depends only on the chunk, not on which CTA computed it.
 constexpr int SPLIT = 64;                  // keys per chunk (4 pages)
+constexpr int SEG = 4;                     // chunks per segment (one partial record each)
+constexpr int SEG_KEYS = SPLIT * SEG;
 constexpr int REC = D + 4;                 // floats per partial record: o[D], m, l, pad
 constexpr int PAGE_BYTES = PAGE * D * 2;   // 4 KB: one page of K (or V) of one kv head
 
@@ -447,7 +452,7 @@ struct DecodeParams {
   const int* ctx;             // [B] keys to attend (including the new token)
   const int* seq_idx;         // optional list of sequences to run (replay); null = all
   int nq, nkv;
-  int max_splits;             // chunks per sequence the partial buffer holds
+  int max_splits;             // segments per sequence the partial buffer holds
   float scale_log2;
   float* part;                // [B][nkv][max_splits][G][REC] scratch
   float* row_sq;
@@ -463,7 +468,8 @@ struct DecodeSmem {
   uint8_t k[2][2 * HALF_BYTES];         // [buffer][half][key][128 B, swizzled]; reused for per-warp O partials
   uint8_t v[2][2 * HALF_BYTES];
   float red[4][8];                      // per-warp row maxima
-  float red2[4][8];                     // per-warp row sums
+  float red2[4][8];                     // per-warp row sums (of the segment, at its end)
+  float segm[8];                        // row maxima of the segment, at its end
   int bt[MAX_BT];
   uint64_t bar[2][2];                   // [buffer][K, V]
 };
@@ -520,7 +526,7 @@ __global__ void __launch_bounds__(128) decode_split_kernel(const __grid_constant
   const int b = p.seq_idx ? p.seq_idx[blockIdx.x] : blockIdx.x;
   const int kvh = blockIdx.y;
   const int n = p.ctx[b];
-  if (static_cast<int>(blockIdx.z) * SPLIT >= n) return;
+  if (static_cast<int>(blockIdx.z) * SEG_KEYS >= n) return;
   if (tid == 0) {
     tma_prefetch_desc(&tm);
     mbar_init(&sm.bar[0][0], 1);
@@ -543,14 +549,24 @@ __global__ void __launch_bounds__(128) decode_split_kernel(const __grid_constant
     }
   }
   __syncthreads();
-  if (warp == 0) decode_issue(sm, &tm, p, 0, blockIdx.z, n, kvh, lane);
+  if (warp == 0) decode_issue(sm, &tm, p, 0, static_cast<int>(blockIdx.z) * SEG, n, kvh, lane);
   bool ok = true;
   const int mi = lane >> 3, rr = lane & 7;        // ldmatrix: matrix index and row of this lane's address
   int it = 0;
-  for (int sp = blockIdx.z; sp * SPLIT < n; sp += gridDim.z, ++it) {
+  // running statistics of the current segment (row g of this warp's fragments): max (common to the four warps),
+  // this warp's weight sum, this warp's unnormalised output
+  float m_run = -INFINITY, l_run = 0.f;
+  float o[16][4];
+#pragma unroll
+  for (int dt = 0; dt < 16; ++dt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o[dt][e] = 0.f;
+  for (int sp = static_cast<int>(blockIdx.z) * SEG; sp * SPLIT < n; ++it) {
     const int buf = it & 1;
     const uint32_t par = (it >> 1) & 1;
-    const int nsp = sp + gridDim.z;
+    const bool seg_end = (sp + 1) % SEG == 0 || (sp + 1) * SPLIT >= n;
+    // the next chunk of this CTA: the next one of the segment, or the first of its next segment
+    const int nsp = (sp + 1) % SEG != 0 ? sp + 1 : sp + 1 + (static_cast<int>(gridDim.z) - 1) * SEG;
     if (warp == 0 && nsp * SPLIT < n) decode_issue(sm, &tm, p, buf ^ 1, nsp, n, kvh, lane);   // next chunk
     const int nk = min(SPLIT, n - sp * SPLIT);
     ok = mbar_wait(&sm.bar[buf][0], par, nullptr) && ok;
@@ -586,7 +602,10 @@ __global__ void __launch_bounds__(128) decode_split_kernel(const __grid_constant
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
     if (t == 0) sm.red[warp][g] = mx;
     __syncthreads();      // (A) red[] complete; every warp is done reading k[buf]
-    const float M = fmaxf(fmaxf(sm.red[0][g], sm.red[1][g]), fmaxf(sm.red[2][g], sm.red[3][g]));
+    const float Mc = fmaxf(fmaxf(sm.red[0][g], sm.red[1][g]), fmaxf(sm.red[2][g], sm.red[3][g]));
+    const float M = fmaxf(m_run, Mc);
+    const float alpha = m_run == -INFINITY ? 0.f : ex2(m_run - M);   // rescales the segment so far
+    m_run = M;
     uint32_t pa[2];
     float lsum = 0.f;
 #pragma unroll
@@ -599,7 +618,7 @@ __global__ void __launch_bounds__(128) decode_split_kernel(const __grid_constant
     }
     lsum += __shfl_xor_sync(0xffffffffu, lsum, 1);
     lsum += __shfl_xor_sync(0xffffffffu, lsum, 2);
-    if (t == 0) sm.red2[warp][g] = lsum;
+    l_run = fmaf(l_run, alpha, lsum);
     ok = mbar_wait(&sm.bar[buf][1], par, nullptr) && ok;
     if (nk < SPLIT) {
       // the last chunk of the sequence: V rows past its last page were not loaded (their weights are zero, but
@@ -611,12 +630,11 @@ __global__ void __launch_bounds__(128) decode_split_kernel(const __grid_constant
       }
       __syncthreads();
     }
-    // O_w = P V: 16 n-tiles of 8 dims
-    float o[16][4];
+    // O_w = alpha O_w + P V: 16 n-tiles of 8 dims
 #pragma unroll
     for (int dt = 0; dt < 16; ++dt)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) o[dt][e] = 0.f;
+      for (int e = 0; e < 4; ++e) o[dt][e] *= alpha;
     {
       const uint32_t vb = smem_u32(sm.v[buf]);
       const int key = warp * 16 + (mi & 1) * 8 + rr;
@@ -628,33 +646,46 @@ __global__ void __launch_bounds__(128) decode_split_kernel(const __grid_constant
         mma_bf16(o[2 * pr + 1], pa[0], 0u, pa[1], 0u, b2, b3);
       }
     }
-    // per-warp partials (rows < G) go where this chunk's K was (no warp reads k[buf] after barrier A)
-    float* wpart = reinterpret_cast<float*>(sm.k[buf]);     // [4][G][D]
-    if (g < G) {
+    if (seg_end) {
+      // per-warp partials (rows < G) go where this chunk's K was (no warp reads k[buf] after barrier A)
+      float* wpart = reinterpret_cast<float*>(sm.k[buf]);     // [4][G][D]
+      if (g < G) {
+#pragma unroll
+        for (int dt = 0; dt < 16; ++dt)
+          *reinterpret_cast<float2*>(wpart + (warp * G + g) * D + dt * 8 + 2 * t) = make_float2(o[dt][0], o[dt][1]);
+        if (t == 0) {
+          sm.red2[warp][g] = l_run;
+          if (warp == 0) sm.segm[g] = m_run;
+        }
+      }
+      __syncthreads();      // (C) wpart, red2[] and segm[] complete
+      float* rec = p.part + ((static_cast<long long>(b) * p.nkv + kvh) * p.max_splits + sp / SEG) * G * REC;
+      for (int i = tid; i < G * D; i += 128) {
+        const int h = i / D, d = i % D;
+        rec[h * REC + d] = (wpart[(0 * G + h) * D + d] + wpart[(1 * G + h) * D + d]) +
+                           (wpart[(2 * G + h) * D + d] + wpart[(3 * G + h) * D + d]);
+      }
+      if (tid < G) {
+        rec[tid * REC + D] = sm.segm[tid];
+        rec[tid * REC + D + 1] = (sm.red2[0][tid] + sm.red2[1][tid]) + (sm.red2[2][tid] + sm.red2[3][tid]);
+      }
+      m_run = -INFINITY;
+      l_run = 0.f;
 #pragma unroll
       for (int dt = 0; dt < 16; ++dt)
-        *reinterpret_cast<float2*>(wpart + (warp * G + g) * D + dt * 8 + 2 * t) = make_float2(o[dt][0], o[dt][1]);
-    }
-    __syncthreads();      // (C) wpart and red2[] complete
-    float* rec = p.part + ((static_cast<long long>(b) * p.nkv + kvh) * p.max_splits + sp) * G * REC;
-    for (int i = tid; i < G * D; i += 128) {
-      const int h = i / D, d = i % D;
-      rec[h * REC + d] = (wpart[(0 * G + h) * D + d] + wpart[(1 * G + h) * D + d]) +
-                         (wpart[(2 * G + h) * D + d] + wpart[(3 * G + h) * D + d]);
-    }
-    if (tid < G) {
-      rec[tid * REC + D] = fmaxf(fmaxf(sm.red[0][tid], sm.red[1][tid]), fmaxf(sm.red[2][tid], sm.red[3][tid]));
-      rec[tid * REC + D + 1] = (sm.red2[0][tid] + sm.red2[1][tid]) + (sm.red2[2][tid] + sm.red2[3][tid]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o[dt][e] = 0.f;
     }
     fence_proxy_async_smem();   // this buffer's generic writes (partials, cleared rows) before its next TMA fill
-    __syncthreads();      // (D) buffer buf and red[], red2[] free for later chunks
+    __syncthreads();      // (D) buffer buf and red[], red2[], segm[] free for later chunks
+    sp = nsp;
   }
   if (!ok && tid == 0) record_error(p.err, ERR_TIMEOUT_PEER);
 }
 
-// Merges the chunks of each (sequence, kv head) in chunk order; one CTA of 128 threads. The chunk maxima and
-// weights are computed in parallel over chunks, then thread d sums dimension d over the chunks in order.
-constexpr int MAX_SPLITS = MAX_BT * PAGE / SPLIT;
+// Merges the segments of each (sequence, kv head) in segment order; one CTA of 128 threads. The segment maxima
+// and weights are computed in parallel over segments, then thread d sums dimension d over them in order.
+constexpr int MAX_SPLITS = MAX_BT * PAGE / SEG_KEYS;
 
 template <int G>
 __global__ void __launch_bounds__(128) decode_combine_kernel(const DecodeParams p) {
@@ -664,7 +695,7 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(const DecodeParams 
   const int b = p.seq_idx ? p.seq_idx[blockIdx.x] : blockIdx.x;
   const int kvh = blockIdx.y, d = threadIdx.x, lane = d & 31, warp = d >> 5;
   const int n = p.ctx[b];
-  const int ns = (n + SPLIT - 1) / SPLIT;
+  const int ns = (n + SEG_KEYS - 1) / SEG_KEYS;
   const float* base = p.part + (static_cast<long long>(b) * p.nkv + kvh) * p.max_splits * G * REC;
   float m[G];
 #pragma unroll
@@ -777,7 +808,7 @@ int sdc_attn_prefill(const void* q, void* o, const void* cache, long long num_bl
   return static_cast<int>(cudaGetLastError());
 }
 
-int sdc_attn_decode_splits(int max_ctx) { return (max_ctx + SPLIT - 1) / SPLIT; }
+int sdc_attn_decode_splits(int max_ctx) { return (max_ctx + SEG_KEYS - 1) / SEG_KEYS; }
 
 // Scratch: `part` holds nseq_rows x nkv x max_splits x (nq / nkv) x (D + 4) floats, where nseq_rows covers
 // every sequence index used (seq_idx entries included) and max_splits = sdc_attn_decode_splits(max_ctx).

@@ -66,7 +66,7 @@ def prefill(q: torch.Tensor, cache: torch.Tensor, block_table: torch.Tensor, pos
 
 
 def decode_scratch(nseq_rows: int, nq: int, nkv: int, max_ctx: int, device) -> torch.Tensor:
-    """Partial-result scratch for `decode` (per sequence, kv head and 128-key chunk)."""
+    """Partial-result scratch for `decode` (one record per sequence, kv head and 256-key segment)."""
     splits = int(_native.lib().sdc_attn_decode_splits(int(max_ctx)))
     return torch.empty(nseq_rows * nkv * splits * (nq // nkv) * 132, dtype=torch.float32, device=device)
 
@@ -76,7 +76,8 @@ def decode(q: torch.Tensor, cache: torch.Tensor, block_table: torch.Tensor, seq_
            seq_idx: Optional[torch.Tensor] = None, nseq: Optional[int] = None,
            row_sq: Optional[torch.Tensor] = None, scale: Optional[float] = None,
            scratch: Optional[torch.Tensor] = None, check: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """q: (B, nq, 128); split-KV: one CTA per (sequence, kv head, 128-key chunk), then a fixed-order combine.
+    """q: (B, nq, 128); split-KV: a CTA per (sequence, kv head) and every z-th 256-key segment (64-key chunks merged
+    in order inside the segment), then a fixed-order combine of the segments.
     seq_idx selects sequences to run (replay). scratch: from `decode_scratch` (allocated here if absent).
     With `check` (a state row; seq_idx given), the selected rows are recomputed and compared with `out`."""
     if out is None:
