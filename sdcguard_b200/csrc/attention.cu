@@ -515,6 +515,76 @@ __device__ __forceinline__ void decode_issue(DecodeSmem<G>& sm, const CUtensorMa
   }
 }
 
+// Merges the segments of each (sequence, kv head) in segment order; one CTA of 128 threads. The segment maxima
+// and weights are computed in parallel over segments, then thread d sums dimension d over them in order.
+constexpr int MAX_SPLITS = MAX_BT * PAGE / SEG_KEYS;
+
+template <int G>
+__device__ __forceinline__ void combine_row(const DecodeParams& p, int b, int kvh) {
+  __shared__ float wsh[G][MAX_SPLITS];
+  __shared__ float Lsh[G];
+  __shared__ float msh[4][G];
+  const int d = threadIdx.x, lane = d & 31, warp = d >> 5;
+  const int n = p.ctx[b];
+  const int ns = (n + SEG_KEYS - 1) / SEG_KEYS;
+  const float* base = p.part + (static_cast<long long>(b) * p.nkv + kvh) * p.max_splits * G * REC;
+  float m[G];
+#pragma unroll
+  for (int h = 0; h < G; ++h) {
+    float v = -INFINITY;
+    for (int s = d; s < ns; s += 128) v = fmaxf(v, base[(s * G + h) * REC + D]);
+#pragma unroll
+    for (int k = 16; k > 0; k >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, k));
+    if (lane == 0) msh[warp][h] = v;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int h = 0; h < G; ++h) {
+    m[h] = fmaxf(fmaxf(msh[0][h], msh[1][h]), fmaxf(msh[2][h], msh[3][h]));
+    for (int s = d; s < ns; s += 128) wsh[h][s] = ex2(base[(s * G + h) * REC + D] - m[h]);
+  }
+  __syncthreads();
+  if (warp == 0) {
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      float l = 0.f;
+      for (int s = lane; s < ns; s += 32) l = fmaf(base[(s * G + h) * REC + D + 1], wsh[h][s], l);
+#pragma unroll
+      for (int k = 16; k > 0; k >>= 1) l += __shfl_xor_sync(0xffffffffu, l, k);
+      if (lane == 0) Lsh[h] = l;
+    }
+  }
+  __syncthreads();
+  float sqsum = 0.f;
+#pragma unroll
+  for (int h = 0; h < G; ++h) {
+    float acc = 0.f;
+    const float* r = base + h * REC + d;
+#pragma unroll 8
+    for (int s = 0; s < ns; ++s) acc = fmaf(r[s * G * REC], wsh[h][s], acc);
+    const __nv_bfloat16 ob = __float2bfloat16(acc / Lsh[h]);
+    __nv_bfloat16* dst = p.o + (static_cast<long long>(b) * p.nq + kvh * G + h) * D + d;
+    if (p.check == nullptr) {
+      *dst = ob;
+    } else {
+      const float x = __bfloat162float(ob), y = __bfloat162float(*dst);
+      if (!(x == y) && !(x != x && y != y))
+        report_replay_mismatch(p.check, static_cast<unsigned long long>(b) * p.nq * D + (kvh * G + h) * D + d);
+    }
+    const float f = __bfloat162float(ob);
+    sqsum = fmaf(f, f, sqsum);
+  }
+  if (p.check != nullptr) {
+    if (blockIdx.x == 0 && blockIdx.y == 0 && d == 0) atomicAdd(p.check + 2, 1ull);
+    return;
+  }
+  if (p.row_sq != nullptr) {
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) sqsum += __shfl_xor_sync(0xffffffffu, sqsum, m);
+    if (lane == 0) atomicAdd(p.row_sq + b, sqsum);
+  }
+}
+
 template <int G>
 __global__ void __launch_bounds__(128) decode_split_kernel(const __grid_constant__ CUtensorMap tm, const DecodeParams p) {
   extern __shared__ __align__(128) unsigned char dsm_raw[];
@@ -681,77 +751,19 @@ __global__ void __launch_bounds__(128) decode_split_kernel(const __grid_constant
     sp = nsp;
   }
   if (!ok && tid == 0) record_error(p.err, ERR_TIMEOUT_PEER);
+  if (gridDim.z == 1) {   // this CTA wrote every segment of the row: merge them here, no combine launch
+    __syncthreads();
+    combine_row<G>(p, b, kvh);
+  }
 }
 
-// Merges the segments of each (sequence, kv head) in segment order; one CTA of 128 threads. The segment maxima
-// and weights are computed in parallel over segments, then thread d sums dimension d over them in order.
-constexpr int MAX_SPLITS = MAX_BT * PAGE / SEG_KEYS;
 
+
+// The merge of one (sequence b, kv head) by the 128 threads of a CTA (the combine kernel, or the split kernel
+// itself when one CTA held every segment of the row): the same arithmetic either way, so replays stay exact.
 template <int G>
 __global__ void __launch_bounds__(128) decode_combine_kernel(const DecodeParams p) {
-  __shared__ float wsh[G][MAX_SPLITS];
-  __shared__ float Lsh[G];
-  __shared__ float msh[4][G];
-  const int b = p.seq_idx ? p.seq_idx[blockIdx.x] : blockIdx.x;
-  const int kvh = blockIdx.y, d = threadIdx.x, lane = d & 31, warp = d >> 5;
-  const int n = p.ctx[b];
-  const int ns = (n + SEG_KEYS - 1) / SEG_KEYS;
-  const float* base = p.part + (static_cast<long long>(b) * p.nkv + kvh) * p.max_splits * G * REC;
-  float m[G];
-#pragma unroll
-  for (int h = 0; h < G; ++h) {
-    float v = -INFINITY;
-    for (int s = d; s < ns; s += 128) v = fmaxf(v, base[(s * G + h) * REC + D]);
-#pragma unroll
-    for (int k = 16; k > 0; k >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, k));
-    if (lane == 0) msh[warp][h] = v;
-  }
-  __syncthreads();
-#pragma unroll
-  for (int h = 0; h < G; ++h) {
-    m[h] = fmaxf(fmaxf(msh[0][h], msh[1][h]), fmaxf(msh[2][h], msh[3][h]));
-    for (int s = d; s < ns; s += 128) wsh[h][s] = ex2(base[(s * G + h) * REC + D] - m[h]);
-  }
-  __syncthreads();
-  if (warp == 0) {
-#pragma unroll
-    for (int h = 0; h < G; ++h) {
-      float l = 0.f;
-      for (int s = lane; s < ns; s += 32) l = fmaf(base[(s * G + h) * REC + D + 1], wsh[h][s], l);
-#pragma unroll
-      for (int k = 16; k > 0; k >>= 1) l += __shfl_xor_sync(0xffffffffu, l, k);
-      if (lane == 0) Lsh[h] = l;
-    }
-  }
-  __syncthreads();
-  float sqsum = 0.f;
-#pragma unroll
-  for (int h = 0; h < G; ++h) {
-    float acc = 0.f;
-    const float* r = base + h * REC + d;
-#pragma unroll 8
-    for (int s = 0; s < ns; ++s) acc = fmaf(r[s * G * REC], wsh[h][s], acc);
-    const __nv_bfloat16 ob = __float2bfloat16(acc / Lsh[h]);
-    __nv_bfloat16* dst = p.o + (static_cast<long long>(b) * p.nq + kvh * G + h) * D + d;
-    if (p.check == nullptr) {
-      *dst = ob;
-    } else {
-      const float x = __bfloat162float(ob), y = __bfloat162float(*dst);
-      if (!(x == y) && !(x != x && y != y))
-        report_replay_mismatch(p.check, static_cast<unsigned long long>(b) * p.nq * D + (kvh * G + h) * D + d);
-    }
-    const float f = __bfloat162float(ob);
-    sqsum = fmaf(f, f, sqsum);
-  }
-  if (p.check != nullptr) {
-    if (blockIdx.x == 0 && blockIdx.y == 0 && d == 0) atomicAdd(p.check + 2, 1ull);
-    return;
-  }
-  if (p.row_sq != nullptr) {
-#pragma unroll
-    for (int m = 16; m > 0; m >>= 1) sqsum += __shfl_xor_sync(0xffffffffu, sqsum, m);
-    if (lane == 0) atomicAdd(p.row_sq + b, sqsum);
-  }
+  combine_row<G>(p, p.seq_idx ? p.seq_idx[blockIdx.x] : blockIdx.x, blockIdx.y);
 }
 
 }  // namespace attn
@@ -769,7 +781,7 @@ static int launch_decode(const DecodeParams& p, const CUtensorMap& tm, dim3 grid
     attr_set = true;
   }
   decode_split_kernel<G><<<grid, 128, smem, st>>>(tm, p);
-  decode_combine_kernel<G><<<grid2, 128, 0, st>>>(p);
+  if (grid.z > 1) decode_combine_kernel<G><<<grid2, 128, 0, st>>>(p);   // z == 1: merged by the split kernel
   return static_cast<int>(cudaGetLastError());
 }
 
