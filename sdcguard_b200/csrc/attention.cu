@@ -100,6 +100,7 @@ constexpr int SOFT = 2 * ROWS;            // softmax threads: warpgroup g takes 
 
 __global__ void __launch_bounds__(128 + 2 * ROWS, 1) prefill_tc_kernel(const __grid_constant__ CUtensorMap tm,
                                                             const PrefillParams p) {
+  pdl_trigger();   // a dependent GEMM may start its prologue and weight loads now
   using namespace pf;
   extern __shared__ uint8_t pf_raw[];
   uint8_t* sm = pf_raw + ((1024 - (smem_u32(pf_raw) & 1023)) & 1023);
@@ -587,6 +588,7 @@ __device__ __forceinline__ void combine_row(const DecodeParams& p, int b, int kv
 
 template <int G>
 __global__ void __launch_bounds__(128) decode_split_kernel(const __grid_constant__ CUtensorMap tm, const DecodeParams p) {
+  pdl_trigger();   // a dependent GEMM may start its prologue and weight loads now
   extern __shared__ __align__(128) unsigned char dsm_raw[];
   // the swizzled buffers need 1024-byte alignment
   unsigned char* base = dsm_raw + ((1024 - (smem_u32(dsm_raw) & 1023)) & 1023);
@@ -763,6 +765,7 @@ __global__ void __launch_bounds__(128) decode_split_kernel(const __grid_constant
 // itself when one CTA held every segment of the row): the same arithmetic either way, so replays stay exact.
 template <int G>
 __global__ void __launch_bounds__(128) decode_combine_kernel(const DecodeParams p) {
+  pdl_trigger();   // a dependent GEMM may start its prologue and weight loads now
   combine_row<G>(p, p.seq_idx ? p.seq_idx[blockIdx.x] : blockIdx.x, blockIdx.y);
 }
 

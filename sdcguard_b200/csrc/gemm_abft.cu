@@ -441,12 +441,29 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
       bool ok = true;
       uint32_t issued = 0;        // bit s: stage s has a load in flight that we have not seen land
       uint32_t issued_phase = 0;  // bit s: the full-barrier parity of that load
+      // Programmatic dependent launch: the weights (W or its checksum rows) do not depend on the previous kernel,
+      // so the first tile's first stages load them before waiting for it; their activation halves follow the wait.
+      bool waited = false;
+      int npre = 0, pre_mt = 0, pre_kb0 = 0;
+      auto finish_wait = [&]() {
+        pdl_wait();
+        waited = true;
+        for (int i = 0; i < npre; ++i)
+          tma_load_2d(smem + i * C::STAGE_BYTES, &tmA, &ctl->full[i], (pre_kb0 + i) * BK, pre_mt * BM);
+      };
       for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
         int mt, idx, kb0, kb1;
         bool cs;
         tile_coords_k(p, tile, mt, cs, idx, kb0, kb1, kblocks);
         const uint32_t bytes = A_BYTES + (cs ? (C::CSB * CS_ROWS) * BK * 2 : C::B_BYTES);
+        if (!waited && tile != static_cast<int>(blockIdx.x)) finish_wait();
+        if (!waited) {
+          pre_mt = mt;
+          pre_kb0 = kb0;
+        }
         for (int kb = kb0; kb < kb1; ++kb) {
+          // every stage holds a weights-only load: wait for the previous kernel before reusing one
+          if (!waited && kb - kb0 >= C::STAGES) finish_wait();
           if (!mbar_wait(&ctl->empty[stage], phase ^ 1u, abort_flag)) {
             ok = false;
             break;
@@ -454,11 +471,14 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
           uint8_t* sa = smem + stage * C::STAGE_BYTES;
           uint8_t* sb = sa + A_BYTES;
           mbar_arrive_expect_tx(&ctl->full[stage], bytes);
-          tma_load_2d(sa, &tmA, &ctl->full[stage], kb * BK, mt * BM);
           if (cs)
             tma_load_2d(sb, &tmWc, &ctl->full[stage], kb * BK, idx * C::CSB * CS_ROWS);
           else
             tma_load_2d(sb, &tmW, &ctl->full[stage], kb * BK, idx * BN);
+          if (waited)
+            tma_load_2d(sa, &tmA, &ctl->full[stage], kb * BK, mt * BM);
+          else
+            ++npre;                 // its activation half is loaded by finish_wait()
           issued |= 1u << stage;
           issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
           if (++stage == C::STAGES) {
@@ -467,6 +487,7 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
           }
         }
       }
+      if (!waited) finish_wait();   // every issued stage gets its activation half
       if (!ok) {
         record_error(p.err, ERR_TIMEOUT_PRODUCER);
         *abort_flag = 1;
@@ -538,6 +559,7 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
     }
   } else if (warp == 3) {
     // ------------------------------------------------------------ check coordinator
+    pdl_wait();   // the band counters and the state row belong to the previous kernel until it completes
     // Keeps global-memory round trips off the epilogue's path: waits for each band's expected sums
     // before the epilogue needs them, and publishes the results (state atomics, band counters) after.
     // In split-K mode the check runs in the reduce kernel: nothing to coordinate.
@@ -602,6 +624,7 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------ epilogue warpgroups
+    pdl_wait();   // outputs, seals and expected sums may still be read or written by the previous kernel
     const int ew = warp - 4;          // 0 .. 4*NWG-1
     const int q = ew & 3;             // TMEM lane quarter this warp may access
     const int g = ew >> 2;            // warpgroup: checksum block within the tile
@@ -874,6 +897,16 @@ static int num_sms_cached() {
   return n;
 }
 
+// Programmatic dependent launch of the GEMM (read once from the environment): SDCGUARD_PDL = 0 turns it off.
+static bool pdl_enabled() {
+  static int m = -1;
+  if (m < 0) {
+    const char* a = std::getenv("SDCGUARD_PDL");
+    m = a ? std::atoi(a) : 1;
+  }
+  return m != 0;
+}
+
 template <int BN, bool INJ>
 static int launch(const CUtensorMap& a, const CUtensorMap& w, const CUtensorMap& wc, const CUtensorMap& c,
                   const PeerMaps& pm, const Params& p, int grid, cudaStream_t stream) {
@@ -885,8 +918,19 @@ static int launch(const CUtensorMap& a, const CUtensorMap& w, const CUtensorMap&
     if (e != cudaSuccess) return static_cast<int>(e);
     attr_done = true;
   }
-  gemm_abft_kernel<BN, INJ><<<grid, Cf::THREADS, Cf::SMEM_BYTES, stream>>>(a, w, wc, c, pm, p);
-  return static_cast<int>(cudaGetLastError());
+  // programmatic dependent launch: the CTAs may start while the previous kernel finishes (see pdl_wait)
+  cudaLaunchConfig_t cfg;
+  std::memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+  cfg.blockDim = dim3(Cf::THREADS, 1, 1);
+  cfg.dynamicSmemBytes = Cf::SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return static_cast<int>(cudaLaunchKernelEx(&cfg, gemm_abft_kernel<BN, INJ>, a, w, wc, c, pm, p));
 }
 
 }  // namespace gemm

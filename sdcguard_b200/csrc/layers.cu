@@ -72,6 +72,7 @@ __global__ void __launch_bounds__(128) add_rmsnorm_kernel(const __nv_bfloat16* _
                                                           __nv_bfloat16* __restrict__ y, __nv_bfloat16* resid_out,
                                                           float* __restrict__ row_sq, const int* rows,
                                                           unsigned long long* check, const ShardOut so) {
+  pdl_trigger();   // a dependent GEMM may start its prologue and weight loads now
   __shared__ float red[4];
   __shared__ int sbad;
   int bad = 0x7fffffff;
@@ -257,6 +258,7 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(
 __global__ void __launch_bounds__(128) silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, int I,
                                                        __nv_bfloat16* __restrict__ out, float* __restrict__ row_sq,
                                                        const int* rows, unsigned long long* check) {
+  pdl_trigger();   // a dependent GEMM may start its prologue and weight loads now
   __shared__ float red[4];
   __shared__ int sbad;
   int bad = 0x7fffffff;

@@ -8,6 +8,7 @@ namespace sdc {
 // One warp per row, 16-byte loads.
 __global__ void row_sqnorm_kernel(const __nv_bfloat16* __restrict__ x, long long ld, int M, int K,
                                   float* __restrict__ out) {
+  pdl_trigger();   // a dependent GEMM may start its prologue and weight loads now
   const int warps = blockDim.x >> 5;
   const int row = blockIdx.x * warps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;

@@ -124,6 +124,7 @@ __global__ void __launch_bounds__(256) ag_pull_kernel(Peers shards, Peers seals,
                                                       const long long* my_flags, int world, int R, int N,
                                                       __nv_bfloat16* __restrict__ out, unsigned long long* state,
                                                       int* err, Peers rss, float* rs_out) {
+  pdl_trigger();   // a dependent GEMM may start its prologue and weight loads now
   if (!wait_all(gen, my_flags, world, err)) return;
   const int nb = (N + 127) / 128;
   const int lane = threadIdx.x & 31;
