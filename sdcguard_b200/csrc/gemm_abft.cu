@@ -278,6 +278,8 @@ __device__ __forceinline__ uint32_t pick24(const uint32_t (&a)[8], const uint32_
 // splits' fp32 partials in split order, applies bias and the injected fault, forms the block sums, writes the
 // bf16 output (and its seal), and judges the block against the checksum columns (summed the same way) with the
 // fused epilogue's judge. One state update per CTA.
+constexpr int kMaxSplitDev = 8;   // most splits a launch uses (kMaxSplit on the host)
+
 template <bool INJ>
 __global__ void __launch_bounds__(256) split_reduce_kernel(const Params p) {
   __shared__ unsigned long long sk0[8], sk1[8];
@@ -295,13 +297,19 @@ __global__ void __launch_bounds__(256) split_reduce_kernel(const Params p) {
     float v[4] = {0.f, 0.f, 0.f, 0.f};
     const float* base = p.part + static_cast<long long>(row) * pw;
     if (in) {
-      for (int ks = 0; ks < p.ksplit; ++ks) {
-        const float4 t = __ldcg(reinterpret_cast<const float4*>(base + ks * plane + c));
-        v[0] += t.x;
-        v[1] += t.y;
-        v[2] += t.z;
-        v[3] += t.w;
-      }
+      // all the splits' loads in flight at once, then the sums in split order
+      float4 t[kMaxSplitDev];
+#pragma unroll
+      for (int ks = 0; ks < kMaxSplitDev; ++ks)
+        if (ks < p.ksplit) t[ks] = __ldcg(reinterpret_cast<const float4*>(base + ks * plane + c));
+#pragma unroll
+      for (int ks = 0; ks < kMaxSplitDev; ++ks)
+        if (ks < p.ksplit) {
+          v[0] += t[ks].x;
+          v[1] += t[ks].y;
+          v[2] += t[ks].z;
+          v[3] += t[ks].w;
+        }
       if (p.bias != nullptr) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) v[j] += __ldg(p.bias + c + j);
@@ -314,8 +322,15 @@ __global__ void __launch_bounds__(256) split_reduce_kernel(const Params p) {
     }
     // checksum columns: lanes 0..5 sum part i of the expected sums over the splits
     float e = 0.f;
-    if (lane < 6)
-      for (int ks = 0; ks < p.ksplit; ++ks) e += __ldcg(base + ks * plane + p.N + b * 6 + lane);
+    if (lane < 6) {
+      float ee[kMaxSplitDev];
+#pragma unroll
+      for (int ks = 0; ks < kMaxSplitDev; ++ks)
+        if (ks < p.ksplit) ee[ks] = __ldcg(base + ks * plane + p.N + b * 6 + lane);
+#pragma unroll
+      for (int ks = 0; ks < kMaxSplitDev; ++ks)
+        if (ks < p.ksplit) e += ee[ks];
+    }
     const float e0 = __shfl_sync(0xffffffffu, e, 0), e1 = __shfl_sync(0xffffffffu, e, 1);
     const float e2 = __shfl_sync(0xffffffffu, e, 2), e3 = __shfl_sync(0xffffffffu, e, 3);
     const float e4 = __shfl_sync(0xffffffffu, e, 4), e5 = __shfl_sync(0xffffffffu, e, 5);
@@ -368,14 +383,15 @@ __global__ void __launch_bounds__(256) split_reduce_kernel(const Params p) {
 }
 
 // Split-K tuning (read once from the environment; the defaults are the measured policy):
-//   SDCGUARD_GEMM_SPLIT_MIN_K   smallest K that splits (default 2048)
+//   SDCGUARD_GEMM_SPLIT_MIN_K   smallest K that splits (default 3072: measured on the decode step of the serving
+//                               bench, K = 2048 with 18 tiles runs faster unsplit than split plus the reduce)
 //   SDCGUARD_GEMM_SPLIT         force this many splits where splitting is eligible (default 0: from the SM count)
 static void split_policy(int* min_k, int* force) {
   static int mk = -1, fs = 0;
   if (mk < 0) {
     const char* a = std::getenv("SDCGUARD_GEMM_SPLIT_MIN_K");
     const char* b = std::getenv("SDCGUARD_GEMM_SPLIT");
-    mk = a ? std::atoi(a) : 2048;
+    mk = a ? std::atoi(a) : 3072;
     fs = b ? std::atoi(b) : 0;
     if (mk < 64) mk = 64;
   }
@@ -945,7 +961,7 @@ extern "C" {
 // launch leaves them zero).
 // Split-K applies to outputs of at most two bands (decode-sized M) that would leave most SMs idle; the partial
 // accumulators of up to kMaxSplit splits follow the expected sums in the workspace.
-constexpr int kMaxSplit = 8;
+constexpr int kMaxSplit = kMaxSplitDev;
 constexpr int kSplitMaxN = 32768;
 
 static long long ws_bytes_base(int M, int N) {
