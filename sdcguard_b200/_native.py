@@ -68,6 +68,7 @@ SIGNATURES: dict[str, tuple] = {
     "sdc_compare_rows_bf16": (I, [P, L, P, P, L, I, I, P, P]),
     "sdc_attn_prefill": (I, [P, P, P, L, P, I, P, P, I, P, I, I, I, F, P, P, P]),
     "sdc_attn_decode": (I, [P, P, P, L, P, I, P, P, P, I, I, I, I, I, F, P, P, P, P]),
+    "sdc_gemm_pair_clusters": (I, []),
     "sdc_attn_decode_splits": (I, [I]),
     "sdc_fingerprint_many": (I, [P, I, L, U64, P, P]),
     "sdc_gemm_bf16_push": (I, [P, L, P, P, I, I, I, P, P, F, P, P, P, P, I, U, U, U, U, F, F, F, F, F, P, I, I, I, U,

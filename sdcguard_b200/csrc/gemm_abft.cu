@@ -73,7 +73,8 @@ struct Params {
   int n_main;      // output tiles per band = ceil(N / BN)
   int n_cs;        // checksum tiles per band
   int n_per_m;     // n_main + n_cs
-  int m_tiles;
+  int m_tiles;     // 128-row bands (the check's counters are per band)
+  int m_units;     // bands of the tile order: m_tiles, or pairs of bands in CTA-pair mode
   int total_tiles;
   int group;       // bands per tile group (L2 rasterisation)
   int csb;         // checksum blocks per checksum tile
@@ -106,16 +107,23 @@ struct Params {
   float* part;               // ksplit > 1: [ksplit][M][N + 6 nb] fp32 partial accumulators
 };
 
-template <int BN>
+// PAIR: a CTA pair (cluster of two) computes a 256 x BN tile with cta_group::2 MMAs issued by the first CTA;
+// each CTA loads its 128 rows of A and half of the tile's W rows, and holds its 128 rows of the accumulator.
+template <int BN, bool PAIR = false>
 struct Cfg {
+  static_assert(!PAIR || BN == 256, "CTA pairs compute 256 x 256 tiles");
   static constexpr int NWG = BN / 128;                 // epilogue warpgroups (one per checksum block)
-  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int B_ROWS = PAIR ? BN / 2 : BN;    // W rows this CTA loads per tile
+  static constexpr int B_BYTES = B_ROWS * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (BN == 256) ? 4 : 6;
+  static constexpr int STAGES = PAIR ? 5 : ((BN == 256) ? 4 : 6);
+  // staging tiles per epilogue warp: two in pair mode, so a tile's second half never waits for the TMA store of
+  // its first half to read shared memory (the TMA unit also serves the producer's loads)
+  static constexpr int STG_BUFS = PAIR ? 2 : 1;
   static constexpr int TMEM_COLS = 2 * BN;            // two accumulators
   static constexpr int THREADS = 128 + NWG * 128;
   static constexpr int CSB = 20 * NWG;                 // checksum blocks per checksum tile (120 columns per WG)
-  static constexpr int STAGING_BYTES = NWG * 4 * 4096;  // per epilogue warp: 32 rows x 128 B of bf16 output
+  static constexpr int STAGING_BYTES = NWG * 4 * 4096 * STG_BUFS;  // per warp and buffer: 32 rows x 128 B bf16
   static constexpr int CTL_BYTES = 1024;               // SmemCtl
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + STAGING_BYTES + 1024 /*align*/ + CTL_BYTES;
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory per CTA");
@@ -137,7 +145,8 @@ struct SmemCtl {
   unsigned long long wkey1[2][8];   // per accumulator, per epilogue warp: worst (z, noise) key
   int wunj[2][8];                   // per accumulator, per epilogue warp: pairs left unjudged
 };
-static_assert(sizeof(SmemCtl) <= Cfg<128>::CTL_BYTES && sizeof(SmemCtl) <= Cfg<256>::CTL_BYTES, "control block");
+static_assert(sizeof(SmemCtl) <= Cfg<128>::CTL_BYTES && sizeof(SmemCtl) <= Cfg<256>::CTL_BYTES &&
+                  sizeof(SmemCtl) <= Cfg<256, true>::CTL_BYTES, "control block");
 
 // Persistent tile order. Bands (128 output rows) are taken in groups of `group` bands; inside a group come
 // first the checksum tiles of all its bands, then its output tiles column-major (the `group` bands of one
@@ -149,7 +158,7 @@ __device__ __forceinline__ void tile_coords(const Params& p, int tile, int& mt, 
   const int g = tile / per_group;
   const int l = tile - g * per_group;
   const int b0 = g * p.group;
-  const int gm = min(p.group, p.m_tiles - b0);
+  const int gm = min(p.group, p.m_units - b0);
   const int ncs = gm * p.n_cs;
   cs = l < ncs;
   const int l2 = cs ? l : l - ncs;
@@ -399,12 +408,12 @@ static void split_policy(int* min_k, int* force) {
   *force = fs;
 }
 
-template <int BN, bool INJ>
-__global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
+template <int BN, bool INJ, bool PAIR>
+__global__ void __launch_bounds__(Cfg<BN, PAIR>::THREADS, 1)
     gemm_abft_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                      const __grid_constant__ CUtensorMap tmWc, const __grid_constant__ CUtensorMap tmC,
                      const __grid_constant__ PeerMaps pm, const Params p) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, PAIR>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* staging = smem + C::STAGES * C::STAGE_BYTES;
@@ -413,6 +422,11 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   if (p.dbg && threadIdx.x == 0) p.dbg[blockIdx.x * 8 + 5] = globaltimer();
+  // pair mode: both CTAs of a cluster walk the same tiles; this CTA holds band 2 mt + prank of pair-band mt
+  const uint32_t prank = PAIR ? cluster_ctarank() : 0u;
+  const int t_first = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int t_step = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
+  auto band_of = [&](int mt) { return PAIR ? 2 * mt + static_cast<int>(prank) : mt; };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -421,7 +435,8 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&ctl->tfull[a], 1);
-      mbar_init(&ctl->tempty[a], C::NWG * 128);
+      // one arrival per epilogue warp (pair mode: of both CTAs) once it has read the accumulator
+      mbar_init(&ctl->tempty[a], (PAIR ? 2 : 1) * C::NWG * 4);
     }
     mbar_init(&ctl->drain, 1);
     for (int a = 0; a < 2; ++a) {
@@ -433,8 +448,13 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
     fence_mbar_init();
   }
   if (warp == 2) {
-    tmem_alloc(&ctl->tmem_base, C::TMEM_COLS);
-    tmem_relinquish();
+    if (PAIR) {
+      tmem_alloc_pair(&ctl->tmem_base, C::TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(&ctl->tmem_base, C::TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
@@ -444,6 +464,7 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
   }
   tc_fence_before();
   __syncthreads();
+  if (PAIR) cluster_sync_all();   // the peer's barriers exist before any remote arrival or pair load
   tc_fence_after();
   const uint32_t tmem_base = ctl->tmem_base;
   volatile int* abort_flag = &ctl->abort_flag;
@@ -461,18 +482,30 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
       // so the first tile's first stages load them before waiting for it; their activation halves follow the wait.
       bool waited = false;
       int npre = 0, pre_mt = 0, pre_kb0 = 0;
+      // pair mode: every load completes bytes on the first CTA's full barrier; the MMA releases each stage on
+      // both CTAs' empty barriers
+      const uint32_t full0 = PAIR ? mapa_shared(smem_u32(&ctl->full[0]), 0u) : 0u;
+      auto load_a = [&](int stg, int kb, int mt_) {
+        if (PAIR)
+          tma_load_2d_pair(smem + stg * C::STAGE_BYTES, &tmA, full0 + static_cast<uint32_t>(stg) * 8u, kb * BK,
+                           band_of(mt_) * BM);
+        else
+          tma_load_2d(smem + stg * C::STAGE_BYTES, &tmA, &ctl->full[stg], kb * BK, mt_ * BM);
+      };
       auto finish_wait = [&]() {
         pdl_wait();
         waited = true;
-        for (int i = 0; i < npre; ++i)
-          tma_load_2d(smem + i * C::STAGE_BYTES, &tmA, &ctl->full[i], (pre_kb0 + i) * BK, pre_mt * BM);
+        for (int i = 0; i < npre; ++i) load_a(i, pre_kb0 + i, pre_mt);
       };
-      for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
+      for (int tile = t_first; tile < p.total_tiles && ok; tile += t_step) {
         int mt, idx, kb0, kb1;
         bool cs;
         tile_coords_k(p, tile, mt, cs, idx, kb0, kb1, kblocks);
-        const uint32_t bytes = A_BYTES + (cs ? (C::CSB * CS_ROWS) * BK * 2 : C::B_BYTES);
-        if (!waited && tile != static_cast<int>(blockIdx.x)) finish_wait();
+        // bytes one CTA loads per stage (the pair's first CTA expects both CTAs' bytes)
+        const uint32_t bytes = A_BYTES + (cs ? (C::CSB * CS_ROWS / (PAIR ? 2 : 1)) * BK * 2 : C::B_BYTES);
+        // pair mode: the checksum tile's N columns are split evenly between the CTAs' B halves
+        const int cs_ncols = cs ? ((min(C::CSB, p.nb - idx * C::CSB) * CS_ROWS + 15) / 16) * 16 : 0;
+        if (!waited && tile != t_first) finish_wait();
         if (!waited) {
           pre_mt = mt;
           pre_kb0 = kb0;
@@ -480,19 +513,29 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
         for (int kb = kb0; kb < kb1; ++kb) {
           // every stage holds a weights-only load: wait for the previous kernel before reusing one
           if (!waited && kb - kb0 >= C::STAGES) finish_wait();
-          if (!mbar_wait(&ctl->empty[stage], phase ^ 1u, abort_flag)) {
+          if (!(PAIR && prank == 1 ? mbar_wait_cluster(&ctl->empty[stage], phase ^ 1u, abort_flag)
+                                   : mbar_wait(&ctl->empty[stage], phase ^ 1u, abort_flag))) {
             ok = false;
             break;
           }
           uint8_t* sa = smem + stage * C::STAGE_BYTES;
           uint8_t* sb = sa + A_BYTES;
-          mbar_arrive_expect_tx(&ctl->full[stage], bytes);
-          if (cs)
-            tma_load_2d(sb, &tmWc, &ctl->full[stage], kb * BK, idx * C::CSB * CS_ROWS);
-          else
-            tma_load_2d(sb, &tmW, &ctl->full[stage], kb * BK, idx * BN);
+          if (PAIR) {
+            if (prank == 0) mbar_arrive_expect_tx(&ctl->full[stage], 2u * bytes);
+            const uint32_t fb = full0 + static_cast<uint32_t>(stage) * 8u;
+            if (cs)
+              tma_load_2d_pair(sb, &tmWc, fb, kb * BK, idx * C::CSB * CS_ROWS + static_cast<int>(prank) * (cs_ncols / 2));
+            else
+              tma_load_2d_pair(sb, &tmW, fb, kb * BK, idx * BN + static_cast<int>(prank) * (BN / 2));
+          } else {
+            mbar_arrive_expect_tx(&ctl->full[stage], bytes);
+            if (cs)
+              tma_load_2d(sb, &tmWc, &ctl->full[stage], kb * BK, idx * C::CSB * CS_ROWS);
+            else
+              tma_load_2d(sb, &tmW, &ctl->full[stage], kb * BK, idx * BN);
+          }
           if (waited)
-            tma_load_2d(sa, &tmA, &ctl->full[stage], kb * BK, mt * BM);
+            load_a(stage, kb, mt);
           else
             ++npre;                 // its activation half is loaded by finish_wait()
           issued |= 1u << stage;
@@ -513,15 +556,18 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
       }
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // ------------------------------------------------------------ MMA issuer (pair mode: the first CTA only)
+    if (lane == 0 && prank == 0) {
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      const uint32_t idesc_main = idesc_bf16_f32(BM, BN);
-      for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
+      const uint32_t idesc_main = idesc_bf16_f32(PAIR ? 2 * BM : BM, BN);
+      // pair mode: the second CTA's empty and accumulator barriers, signalled by the same commits
+      const uint32_t peer_empty = PAIR ? mapa_shared(smem_u32(&ctl->empty[0]), 1u) : 0u;
+      const uint32_t peer_tfull = PAIR ? mapa_shared(smem_u32(&ctl->tfull[0]), 1u) : 0u;
+      for (int tile = t_first; tile < p.total_tiles && ok; tile += t_step) {
         int mt, idx, kb0, kb1;
         bool cs;
         tile_coords_k(p, tile, mt, cs, idx, kb0, kb1, kblocks);
@@ -529,9 +575,10 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
         if (cs) {
           const int nblk = min(C::CSB, p.nb - idx * C::CSB);
           const int ncols = ((nblk * CS_ROWS + 15) / 16) * 16;
-          idesc = idesc_bf16_f32(BM, ncols);
+          idesc = idesc_bf16_f32(PAIR ? 2 * BM : BM, ncols);
         }
-        if (!mbar_wait(&ctl->tempty[acc], acc_phase ^ 1u, abort_flag)) {
+        if (!(PAIR ? mbar_wait_cluster(&ctl->tempty[acc], acc_phase ^ 1u, abort_flag)
+                   : mbar_wait(&ctl->tempty[acc], acc_phase ^ 1u, abort_flag))) {
           ok = false;
           break;
         }
@@ -550,16 +597,29 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
 #pragma unroll
           for (int ks = 0; ks < BK / 16; ++ks) {
             // advance 16 bf16 = 32 bytes along K inside the swizzle atom: +2 in the >>4 address field
-            umma_f16(d_tmem, adesc + 2ull * ks, bdesc + 2ull * ks, idesc, (kb != kb0 || ks != 0) ? 1u : 0u);
+            if (PAIR)
+              umma_f16_pair(d_tmem, adesc + 2ull * ks, bdesc + 2ull * ks, idesc, (kb != kb0 || ks != 0) ? 1u : 0u);
+            else
+              umma_f16(d_tmem, adesc + 2ull * ks, bdesc + 2ull * ks, idesc, (kb != kb0 || ks != 0) ? 1u : 0u);
           }
-          umma_commit(&ctl->empty[stage]);
+          if (PAIR) {
+            umma_commit_pair(&ctl->empty[stage]);
+            umma_commit_pair_at(peer_empty + static_cast<uint32_t>(stage) * 8u);
+          } else {
+            umma_commit(&ctl->empty[stage]);
+          }
           if (++stage == C::STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        umma_commit(&ctl->tfull[acc]);
+        if (PAIR) {
+          umma_commit_pair(&ctl->tfull[acc]);
+          umma_commit_pair_at(peer_tfull + static_cast<uint32_t>(acc) * 8u);
+        } else {
+          umma_commit(&ctl->tfull[acc]);
+        }
         if (++acc == 2) {
           acc = 0;
           acc_phase ^= 1u;
@@ -569,7 +629,10 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
         record_error(p.err, ERR_TIMEOUT_MMA);
         *abort_flag = 1;
         // wait (bounded) for the MMAs already issued before TMEM can be released
-        umma_commit(&ctl->drain);
+        if (PAIR)
+          umma_commit_pair(&ctl->drain);
+        else
+          umma_commit(&ctl->drain);
         mbar_wait(&ctl->drain, 0, nullptr);
       }
     }
@@ -583,16 +646,18 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       unsigned long long* st = p.state + static_cast<long long>(p.slot) * 4;
-      for (int tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x) {
+      for (int tile = t_first; tile < p.total_tiles; tile += t_step) {
         int mt, idx;
         bool cs;
         tile_coords(p, tile, mt, cs, idx);
+        const int band = band_of(mt);
+        const bool in_band = band < p.m_tiles;     // pair mode: the second half of the last pair may be empty
         int ok = 1;
-        if (!cs) {
+        if (!cs && in_band) {
           ok = 0;
           const unsigned long long t0 = globaltimer();
           for (uint32_t i = 0;; ++i) {
-            if (ld_acquire_gpu(p.cs_done + mt) >= p.n_cs) {
+            if (ld_acquire_gpu(p.cs_done + band) >= p.n_cs) {
               ok = 1;
               break;
             }
@@ -608,9 +673,11 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
           *abort_flag = 1;
           break;
         }
-        if (cs) {
+        if (!in_band) {
+          // nothing of this tile is in the output
+        } else if (cs) {
           fence_acq_rel_gpu();      // release the CTA's expected sums of this tile
-          atomicAdd(p.cs_done + mt, 1);
+          atomicAdd(p.cs_done + band, 1);
         } else {
           unsigned long long a0 = 0ull, a1 = 0ull;
           int u = 0;
@@ -624,11 +691,11 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
           if (a0 > ld_relaxed_gpu_u64(st + 0)) atomicMax(st + 0, a0);
           if (a1 > ld_relaxed_gpu_u64(st + 1)) atomicMax(st + 1, a1);
           if (u) atomicAdd(st + 3, static_cast<unsigned long long>(u));
-          if (mt == 0 && idx == 0) atomicAdd(st + 2, 1ull);   // one count per launch
+          if (band == 0 && idx == 0) atomicAdd(st + 2, 1ull);   // one count per launch
           // the last output tile of the band returns the band's counters to zero for the next launch
-          if (atomicAdd(p.main_done + mt, 1) == p.n_main - 1) {
-            p.cs_done[mt] = 0;
-            p.main_done[mt] = 0;
+          if (atomicAdd(p.main_done + band, 1) == p.n_main - 1) {
+            p.cs_done[band] = 0;
+            p.main_done[band] = 0;
           }
         }
         mbar_arrive(&ctl->resempty[acc]);
@@ -658,13 +725,16 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
     // named barrier in the loop, so a warp that gives up leaves no other warp waiting.
     Pending pend;
     pend.live = false;
-    for (int tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x) {
+    for (int tile = t_first; tile < p.total_tiles; tile += t_step) {
       int mt, idx;
       bool cs;
       tile_coords(p, tile / p.ksplit, mt, cs, idx);
-      const int row = mt * BM + row_in_tile;
+      const int band = band_of(mt);
+      const int row = band * BM + row_in_tile;
       const unsigned long long t_w0 = p.dbg ? globaltimer() : 0ull;
-      const bool got = mbar_wait(&ctl->tfull[acc], acc_phase, abort_flag);
+      // pair mode: the second CTA learns that its accumulator is complete from the first CTA (forwarded below)
+      const bool got = PAIR && prank == 1 ? mbar_wait_cluster(&ctl->tfull[acc], acc_phase, abort_flag)
+                                          : mbar_wait(&ctl->tfull[acc], acc_phase, abort_flag);
       const unsigned long long t_w1 = p.dbg ? globaltimer() : 0ull;
       if (!got) {
         record_error(p.err, ERR_TIMEOUT_EPILOGUE);
@@ -673,6 +743,18 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
       }
       tc_fence_after();
       const uint32_t tacc = tmem_base + static_cast<uint32_t>(acc * BN) + lane_off;
+      // this warp is done reading the accumulator (each thread fenced its TMEM loads before the warp sync; pair
+      // mode: the MMA and its barrier are in the first CTA). One arrival per warp: arrivals on one barrier
+      // serialise, remote ones most of all.
+      auto release_acc = [&]() {
+        __syncwarp();
+        if (lane == 0) {
+          if (PAIR && prank == 1)
+            mbar_arrive_remote(mapa_shared(smem_u32(&ctl->tempty[acc]), 0u));
+          else
+            mbar_arrive(&ctl->tempty[acc]);
+        }
+      };
 
       if (p.ksplit > 1) {
         // ---- split-K: store this split's fp32 accumulator rows; the reduce kernel sums and checks them
@@ -721,7 +803,7 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
           }
         }
         tc_fence_before();
-        mbar_arrive(&ctl->tempty[acc]);
+        release_acc();
       } else if (cs) {
         // ---- checksum tile: E = A @ Wc^T, three bf16 parts per sum added in fp32
         const int blk0 = idx * C::CSB + g * 20;   // first block of this warpgroup
@@ -752,7 +834,7 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
           }
         }
         tc_fence_before();
-        mbar_arrive(&ctl->tempty[acc]);
+        release_acc();
         judge_pending<C::NWG>(p, ctl, pend, ew, lane, abort_flag);
         // hand this warp's part of the tile to the coordinator, which releases the expected sums to other CTAs
         __syncwarp();
@@ -770,9 +852,10 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
         float P = 0.f, S = 0.f, Q = 0.f, Aab = 0.f;
         uint32_t seal = 0u;
         if (have) {
-          uint8_t* stg = staging + ew * 4096;     // this warp's 32 x 128 B staging tile
 #pragma unroll 1
           for (int h = 0; h < CSW / 64; ++h) {
+            // this warp's 32 x 128 B staging tile for this half (alternating when there are two)
+            uint8_t* stg = staging + (ew * C::STG_BUFS + (C::STG_BUFS > 1 ? h : 0)) * 4096;
             uint32_t r[64];
             uint32_t (&ra)[32] = *reinterpret_cast<uint32_t(*)[32]>(&r[0]);
             uint32_t (&rb)[32] = *reinterpret_cast<uint32_t(*)[32]>(&r[32]);
@@ -805,8 +888,9 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
 #pragma unroll
               for (int j = 0; j < 32; ++j) seal += seal_term(packed[j], static_cast<uint32_t>(h * 32 + j));
             }
-            // the previous store from this staging tile must have read it before we overwrite it
-            if (lane == 0) bulk_wait_read0();
+            // the store that last used this staging tile must have read it before we overwrite it (with two tiles
+            // per warp, the store of the other half may still be reading)
+            if (lane == 0) bulk_wait_read<C::STG_BUFS - 1>();
             __syncwarp();
             uint8_t* myrow = stg + lane * 128;
 #pragma unroll
@@ -822,7 +906,7 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
                 tma_store_2d(&pm.m[owner], stg, cbase,
                              static_cast<int>(push_off) + p.push.rank * p.push.R + (mt * BM - owner * p.push.R) + q * 32);
               } else {
-                tma_store_2d(&tmC, stg, cbase, mt * BM + q * 32);
+                tma_store_2d(&tmC, stg, cbase, band * BM + q * 32);
               }
               bulk_commit();
             }
@@ -836,7 +920,7 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
           }
         }
         tc_fence_before();
-        mbar_arrive(&ctl->tempty[acc]);   // the MMA warp may refill this accumulator now
+        release_acc();   // the MMA warp may refill this accumulator now
         const unsigned long long t_e0 = p.dbg ? globaltimer() : 0ull;
         judge_pending<C::NWG>(p, ctl, pend, ew, lane, abort_flag);
         if (p.dbg && et == 0) {
@@ -875,9 +959,13 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
   }
   tc_fence_before();
   __syncthreads();
+  if (PAIR) cluster_sync_all();   // no CTA leaves (or frees TMEM) while its peer may still use it or its barriers
   if (warp == 2) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, C::TMEM_COLS);
+    if (PAIR)
+      tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+    else
+      tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
   if (p.push.on && threadIdx.x == 0) {
     // every store of this CTA (tensor stores and seals) is complete; the last CTA publishes the generation
@@ -923,14 +1011,14 @@ static bool pdl_enabled() {
   return m != 0;
 }
 
-template <int BN, bool INJ>
+template <int BN, bool INJ, bool PAIR>
 static int launch(const CUtensorMap& a, const CUtensorMap& w, const CUtensorMap& wc, const CUtensorMap& c,
                   const PeerMaps& pm, const Params& p, int grid, cudaStream_t stream) {
-  using Cf = Cfg<BN>;
+  using Cf = Cfg<BN, PAIR>;
   static bool attr_done = false;
   if (!attr_done) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_abft_kernel<BN, INJ>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         Cf::SMEM_BYTES);
+    cudaError_t e = cudaFuncSetAttribute(gemm_abft_kernel<BN, INJ, PAIR>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM_BYTES);
     if (e != cudaSuccess) return static_cast<int>(e);
     attr_done = true;
   }
@@ -941,12 +1029,62 @@ static int launch(const CUtensorMap& a, const CUtensorMap& w, const CUtensorMap&
   cfg.blockDim = dim3(Cf::THREADS, 1, 1);
   cfg.dynamicSmemBytes = Cf::SMEM_BYTES;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (PAIR) {   // CTA pairs: clusters of two along x (the grid is even)
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = 2;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  if (pdl_enabled()) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pdl_enabled() ? 1 : 0;
-  return static_cast<int>(cudaLaunchKernelEx(&cfg, gemm_abft_kernel<BN, INJ>, a, w, wc, c, pm, p));
+  cfg.numAttrs = na;
+  return static_cast<int>(cudaLaunchKernelEx(&cfg, gemm_abft_kernel<BN, INJ, PAIR>, a, w, wc, c, pm, p));
+}
+
+// How many CTA-pair clusters of the pair kernel can be resident at once: a launch uses at most that many
+// (a tile's epilogue waits for its band's checksum tiles, which may run in any other cluster).
+static int pair_max_clusters() {
+  static int n = -1;
+  if (n < 0) {
+    using Cf = Cfg<256, true>;
+    n = 0;
+    if (cudaFuncSetAttribute(gemm_abft_kernel<256, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Cf::SMEM_BYTES) == cudaSuccess) {
+      cudaLaunchConfig_t cfg;
+      std::memset(&cfg, 0, sizeof(cfg));
+      cfg.gridDim = dim3(2, 1, 1);
+      cfg.blockDim = dim3(Cf::THREADS, 1, 1);
+      cfg.dynamicSmemBytes = Cf::SMEM_BYTES;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int c = 0;
+      if (cudaOccupancyMaxActiveClusters(&c, gemm_abft_kernel<256, false, true>, &cfg) == cudaSuccess) n = c;
+    }
+    cudaGetLastError();
+  }
+  return n;
+}
+
+// CTA-pair mode for 256-wide tiles (read once from the environment): SDCGUARD_GEMM_PAIR = 0 turns it off.
+static bool pair_enabled() {
+  static int m = -1;
+  if (m < 0) {
+    const char* a = std::getenv("SDCGUARD_GEMM_PAIR");
+    m = a ? std::atoi(a) : 1;
+  }
+  return m != 0;
 }
 
 }  // namespace gemm
@@ -975,6 +1113,9 @@ static long long part_bytes(int M, int N) {
 }
 
 static bool split_eligible(int M, int N) { return (M + BM - 1) / BM <= 2 && N <= kSplitMaxN; }
+
+// CTA-pair clusters of the 256-wide pair kernel that can be resident at once (0: pair mode unavailable).
+int sdc_gemm_pair_clusters() { return pair_max_clusters(); }
 
 long long sdc_gemm_ws_bytes(int M, int N) {
   return ws_bytes_base(M, N) + (split_eligible(M, N) ? part_bytes(M, N) + 256 : 0);
@@ -1014,12 +1155,17 @@ static int gemm_run(const void* A, long long lda, const void* W, const void* Wc,
   p.n_cs = (nb + p.csb - 1) / p.csb;
   p.n_per_m = p.n_main + p.n_cs;
   p.m_tiles = (M + BM - 1) / BM;
-  p.total_tiles = p.m_tiles * p.n_per_m;
+  // CTA pairs (256 x 256 tiles, cta_group::2): for outputs with at least two bands and enough tiles to fill the
+  // GPU with pairs; not with push or split-K (decode-sized outputs)
+  const bool pair = bn == 256 && push == nullptr && p.m_tiles >= 2 && max_ctas == 0 && pair_enabled() &&
+                    pair_max_clusters() > 0;
+  p.m_units = pair ? (p.m_tiles + 1) / 2 : p.m_tiles;
+  p.total_tiles = p.m_units * p.n_per_m;
   {
     // bands per group: the group's A rows stay within about 24 MB of L2
-    const long long band_bytes = static_cast<long long>(BM) * K * 2;
+    const long long band_bytes = static_cast<long long>(pair ? 2 * BM : BM) * K * 2;
     int g = static_cast<int>((24ll << 20) / (band_bytes > 0 ? band_bytes : 1));
-    p.group = g < 1 ? 1 : (g > 16 ? 16 : (g > p.m_tiles ? p.m_tiles : g));
+    p.group = g < 1 ? 1 : (g > 16 ? 16 : (g > p.m_units ? p.m_units : g));
   }
   p.C = static_cast<__nv_bfloat16*>(Cout);
   p.ldc = ldc;
@@ -1075,7 +1221,7 @@ static int gemm_run(const void* A, long long lda, const void* W, const void* Wc,
   // splitting pays when each CTA would stream a long K (measured: K = 1024 is faster unsplit)
   int split_min_k, split_force;
   split_policy(&split_min_k, &split_force);
-  if (allow_split && push == nullptr && split_eligible(M, N) && K >= split_min_k && max_ctas == 0 && dbg == nullptr) {
+  if (!pair && allow_split && push == nullptr && split_eligible(M, N) && K >= split_min_k && max_ctas == 0 && dbg == nullptr) {
     const int kblocks = (K + BK - 1) / BK;
     int sp = split_force > 0 ? split_force : num_sms_cached() / p.total_tiles;
     sp = sp > kMaxSplit ? kMaxSplit : sp;
@@ -1089,8 +1235,8 @@ static int gemm_run(const void* A, long long lda, const void* W, const void* Wc,
   }
   CUtensorMap ma, mw, mc, mo;
   if (!make_map(&ma, A, M, K, lda, BM)) return -2;
-  if (!make_map(&mw, W, N, K, K, bn)) return -3;
-  if (!make_map(&mc, Wc, static_cast<long long>(nb) * CS_ROWS, K, K, p.csb * CS_ROWS)) return -4;
+  if (!make_map(&mw, W, N, K, K, pair ? bn / 2 : bn)) return -3;
+  if (!make_map(&mc, Wc, static_cast<long long>(nb) * CS_ROWS, K, K, p.csb * CS_ROWS / (pair ? 2 : 1))) return -4;
   if (!make_map(&mo, Cout, M, N, ldc, 32, false)) return -5;
   int grid = p.total_tiles;
   const int cap = max_ctas > 0 ? max_ctas : num_sms_cached();
@@ -1098,10 +1244,18 @@ static int gemm_run(const void* A, long long lda, const void* W, const void* Wc,
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool inj = inj_row >= 0;
   int rc;
-  if (bn == 256)
-    rc = inj ? launch<256, true>(ma, mw, mc, mo, pm, p, grid, st) : launch<256, false>(ma, mw, mc, mo, pm, p, grid, st);
-  else
-    rc = inj ? launch<128, true>(ma, mw, mc, mo, pm, p, grid, st) : launch<128, false>(ma, mw, mc, mo, pm, p, grid, st);
+  if (pair) {
+    const int clusters = p.total_tiles < pair_max_clusters() ? p.total_tiles : pair_max_clusters();
+    grid = 2 * clusters;
+    rc = inj ? launch<256, true, true>(ma, mw, mc, mo, pm, p, grid, st)
+             : launch<256, false, true>(ma, mw, mc, mo, pm, p, grid, st);
+  } else if (bn == 256) {
+    rc = inj ? launch<256, true, false>(ma, mw, mc, mo, pm, p, grid, st)
+             : launch<256, false, false>(ma, mw, mc, mo, pm, p, grid, st);
+  } else {
+    rc = inj ? launch<128, true, false>(ma, mw, mc, mo, pm, p, grid, st)
+             : launch<128, false, false>(ma, mw, mc, mo, pm, p, grid, st);
+  }
   if (rc != 0 || p.ksplit == 1) return rc;
   const long long warps = static_cast<long long>(M) * nb;
   const unsigned blocks = static_cast<unsigned>((warps * 32 + 255) / 256);
