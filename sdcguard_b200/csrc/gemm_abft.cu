@@ -191,17 +191,14 @@ __device__ __forceinline__ unsigned long long ld_relaxed_gpu_u64(const unsigned 
 // fp32 accumulator block (bias included), ex the expected plain / signed sums from the checksum rows. Noise
 // model of the fp32 accumulation (c1, c2, c3 folded into prod_coef and out_coef). Sets the state keys
 // (z bits << 32 | flat, z bits << 32 | noise bits) or marks the pair unjudged.
-__device__ __forceinline__ void judge_pair(const Params& p, int row, int b, float P, float S, float Q, float Aab,
-                                           float2 ex, unsigned long long& k0, unsigned long long& k1, int& unj) {
+// As judge_pair, with the pair's block statistics (ws), bias block sums (bs, zero without bias) and row sum of
+// squares (rsq) already loaded.
+__device__ __forceinline__ void judge_pair_loaded(const Params& p, int row, int b, float P, float S, float Q,
+                                                  float Aab, float2 ex, float4 ws, float2 bs, float rsq,
+                                                  unsigned long long& k0, unsigned long long& k1, int& unj) {
   const long long o = static_cast<long long>(row) * p.nb + b;
-  const float4 ws = __ldg(p.wstat + b);
-  float ep = ex.x, es = ex.y;
-  if (p.bsum != nullptr) {
-    const float2 bs = __ldg(p.bsum + b);
-    ep += bs.x;
-    es += bs.y;
-  }
-  const float xn = sqrtf(__ldg(p.row_sq + row));
+  const float ep = ex.x + bs.x, es = ex.y + bs.y;
+  const float xn = sqrtf(rsq);
   const float prod = p.prod_coef * xn * fmaxf(ws.x, fmaxf(ws.y, ws.z));
   const float den = sqrtf(Q) * p.out_coef + prod + p.abs_floor;
   const float dp = fabsf(ep - P), ds = fabsf(es - S);
@@ -235,15 +232,41 @@ __device__ __forceinline__ void judge_pair(const Params& p, int row, int b, floa
   }
 }
 
+__device__ __forceinline__ void judge_pair(const Params& p, int row, int b, float P, float S, float Q, float Aab,
+                                           float2 ex, unsigned long long& k0, unsigned long long& k1, int& unj) {
+  const float2 bs = p.bsum != nullptr ? __ldg(p.bsum + b) : make_float2(0.f, 0.f);
+  judge_pair_loaded(p, row, b, P, S, Q, Aab, ex, __ldg(p.wstat + b), bs, __ldg(p.row_sq + row), k0, k1, unj);
+}
+
 // An output tile's block sums, kept by the epilogue thread that owns the row until the tile is judged.
 struct Pending {
   bool live;        // a tile waits to be judged
   bool valid;       // this thread has a (row, block) pair in it
+  bool pre;         // judge_prefetch ran: ready and the loaded values below are set
+  bool ready;       // the band's expected sums were published (the coordinator did not give up)
   int acc;          // accumulator slot and its phase when the tile was taken
   uint32_t phase;
   int row, b;
   float P, S, Q, A;
+  float2 ex, bs;    // expected sums, bias block sums
+  float4 ws;        // block statistics of W
+  float rsq;        // row sum of squares
 };
+
+// Wait (bounded) for the pending tile's expected sums and issue the judge's loads, early in the next tile's
+// epilogue so that their latency overlaps its body.
+__device__ __forceinline__ void judge_prefetch(const Params& p, SmemCtl* ctl, Pending& pd, volatile int* abort_flag) {
+  if (!pd.live || pd.pre) return;
+  pd.pre = true;
+  // the coordinator has waited (bounded) for the band's expected sums; skip judging if it gave up
+  pd.ready = mbar_wait(&ctl->ready[pd.acc], pd.phase, abort_flag) && ctl->ready_ok[pd.acc] != 0;
+  if (pd.valid && pd.ready) {
+    pd.ex = __ldcg(p.expd + static_cast<long long>(pd.row) * p.nb + pd.b);
+    pd.ws = __ldg(p.wstat + pd.b);
+    pd.bs = p.bsum != nullptr ? __ldg(p.bsum + pd.b) : make_float2(0.f, 0.f);
+    pd.rsq = __ldg(p.row_sq + pd.row);
+  }
+}
 
 // Judge the pending output tile of this warp (if any) and hand the warp's worst keys to the coordinator: wait
 // (bounded) for the band's expected sums, judge this thread's pair, reduce over the warp, and (lane 0) arrive on
@@ -252,17 +275,15 @@ template <int NWG>
 __device__ __forceinline__ void judge_pending(const Params& p, SmemCtl* ctl, Pending& pd, int ew, int lane,
                                               volatile int* abort_flag) {
   if (!pd.live) return;
+  judge_prefetch(p, ctl, pd, abort_flag);
   pd.live = false;
-  // the coordinator has waited (bounded) for the band's expected sums; skip judging if it gave up
-  const bool ready = mbar_wait(&ctl->ready[pd.acc], pd.phase, abort_flag) && ctl->ready_ok[pd.acc] != 0;
   unsigned long long k0 = 0ull, k1 = 0ull;
   int unj = 0;
   if (pd.valid) {
-    if (!ready)
+    if (!pd.ready)
       unj = 1;
     else
-      judge_pair(p, pd.row, pd.b, pd.P, pd.S, pd.Q, pd.A,
-                 __ldcg(p.expd + static_cast<long long>(pd.row) * p.nb + pd.b), k0, k1, unj);
+      judge_pair_loaded(p, pd.row, pd.b, pd.P, pd.S, pd.Q, pd.A, pd.ex, pd.ws, pd.bs, pd.rsq, k0, k1, unj);
   }
   k0 = warp_max_u64(k0);
   k1 = warp_max_u64(k1);
@@ -646,6 +667,8 @@ __global__ void __launch_bounds__(Cfg<BN, PAIR>::THREADS, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       unsigned long long* st = p.state + static_cast<long long>(p.slot) * 4;
+      unsigned long long m0 = 0ull, m1 = 0ull;   // this CTA's worst keys so far
+      long long unj_all = 0;
       for (int tile = t_first; tile < p.total_tiles; tile += t_step) {
         int mt, idx;
         bool cs;
@@ -687,10 +710,10 @@ __global__ void __launch_bounds__(Cfg<BN, PAIR>::THREADS, 1)
             a1 = ctl->wkey1[acc][w] > a1 ? ctl->wkey1[acc][w] : a1;
             u += ctl->wunj[acc][w];
           }
-          // most tiles of a clean run are below the running maximum: skip their atomics
-          if (a0 > ld_relaxed_gpu_u64(st + 0)) atomicMax(st + 0, a0);
-          if (a1 > ld_relaxed_gpu_u64(st + 1)) atomicMax(st + 1, a1);
-          if (u) atomicAdd(st + 3, static_cast<unsigned long long>(u));
+          // the CTA's worst keys and unjudged count are kept here and published once, after its last tile
+          m0 = a0 > m0 ? a0 : m0;
+          m1 = a1 > m1 ? a1 : m1;
+          unj_all += u;
           if (band == 0 && idx == 0) atomicAdd(st + 2, 1ull);   // one count per launch
           // the last output tile of the band returns the band's counters to zero for the next launch
           if (atomicAdd(p.main_done + band, 1) == p.n_main - 1) {
@@ -704,6 +727,9 @@ __global__ void __launch_bounds__(Cfg<BN, PAIR>::THREADS, 1)
           acc_phase ^= 1u;
         }
       }
+      if (m0) atomicMax(st + 0, m0);
+      if (m1) atomicMax(st + 1, m1);
+      if (unj_all) atomicAdd(st + 3, static_cast<unsigned long long>(unj_all));
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------ epilogue warpgroups
@@ -743,6 +769,7 @@ __global__ void __launch_bounds__(Cfg<BN, PAIR>::THREADS, 1)
       }
       tc_fence_after();
       const uint32_t tacc = tmem_base + static_cast<uint32_t>(acc * BN) + lane_off;
+      judge_prefetch(p, ctl, pend, abort_flag);   // the previous tile's judge inputs load during this tile's body
       // this warp is done reading the accumulator (each thread fenced its TMEM loads before the warp sync; pair
       // mode: the MMA and its barrier are in the first CTA). One arrival per warp: arrivals on one barrier
       // serialise, remote ones most of all.
@@ -929,6 +956,7 @@ __global__ void __launch_bounds__(Cfg<BN, PAIR>::THREADS, 1)
           d[4] += globaltimer() - t_e0;   // judging the previous output tile (including its wait)
         }
         pend.live = true;
+        pend.pre = false;
         pend.valid = have && row < p.M;
         pend.acc = acc;
         pend.phase = acc_phase;

@@ -2,6 +2,7 @@
 profiling and for the numbers in the profile summaries.
 
     python -m sdcguard_b200.tools.kernel_bench gemm --m 4096 --n 28672 --k 4096 [--iters 10]
+    python -m sdcguard_b200.tools.kernel_bench gemm-timeline --m 256 --n 4096 --k 1024   # per-CTA phases
     python -m sdcguard_b200.tools.kernel_bench decode --batch 256 --nq 16 --nkv 8 --ctx 1600
     python -m sdcguard_b200.tools.kernel_bench prefill --seqs 8 --len 2048 --nq 16 --nkv 8
 
@@ -56,6 +57,50 @@ def bench_gemm(m, n, k, iters, bn=None):
     return {"kernel": "checked_gemm", "m": m, "n": n, "k": k, "bn": bn or gemm.pick_bn(m, n), "us": round(ms * 1e3, 1),
             "tflops": round(fl / ms / 1e9, 1), "cublas_us": round(mc * 1e3, 1),
             "cublas_tflops": round(fl / mc / 1e9, 1), "worst_clean_z": round(r["z"], 4), "checks": r["checks"]}
+
+
+def gemm_timeline(m, n, k, iters, bn=None):
+    """Where a checked GEMM's time goes inside the kernel, from its per-CTA global-timer records (the kernel's
+    debug timers: CTA start and end, time waiting for each accumulator, epilogue time, output-tile body, judge).
+    Averages over CTAs of the median launch (L2 flushed before each); times in microseconds from the earliest
+    CTA start. The timers cost a few loads and stores per tile; the launch is otherwise the production kernel, except
+    that split-K is off while they run (shapes that would split over K show the unsplit kernel)."""
+    from ..ops import gemm
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(0)
+    x = torch.randn(m, k, device=dev, generator=g).bfloat16()
+    w = (torch.randn(n, k, device=dev, generator=g) * 0.02).bfloat16()
+    cw = gemm.CheckedWeight(w)
+    st = gemm.StateTable(dev, 2)
+    s = st.add("gemm", cw.nb)
+    rs = gemm.row_sqnorm(x)
+    out = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+    nsm = torch.cuda.get_device_properties(dev).multi_processor_count
+    dbg = torch.zeros(nsm * 8, dtype=torch.int64, device=dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.int8, device=dev)
+    for _ in range(3):
+        gemm.checked_linear(x, cw, st.state, s, row_sq=rs, out=out, bn=bn)
+    runs = []
+    for _ in range(max(1, iters)):
+        flush.zero_()
+        dbg.zero_()
+        torch.cuda.synchronize()
+        gemm.checked_linear(x, cw, st.state, s, row_sq=rs, out=out, bn=bn, dbg=dbg)
+        torch.cuda.synchronize()
+        d = dbg.view(nsm, 8).cpu()
+        d = d[d[:, 6] > 0]
+        t0 = int(d[:, 5].min())
+        runs.append({"ctas": int(d.shape[0]), "end_max_us": (int(d[:, 6].max()) - t0) / 1e3,
+                     "end_mean_us": float((d[:, 6] - t0).double().mean()) / 1e3,
+                     "tiles_per_cta": float(d[:, 2].double().mean()),
+                     "wait_accumulator_us": float(d[:, 0].double().mean()) / 1e3,
+                     "epilogue_us": float(d[:, 1].double().mean()) / 1e3,
+                     "output_body_us": float(d[:, 3].double().mean()) / 1e3,
+                     "judge_us": float(d[:, 4].double().mean()) / 1e3})
+    runs.sort(key=lambda r: r["end_max_us"])
+    r = runs[len(runs) // 2]
+    return {"kernel": "checked_gemm_timeline", "m": m, "n": n, "k": k,
+            **{kk: round(v, 2) if isinstance(v, float) else v for kk, v in r.items()}}
 
 
 def bench_fp8(m, n, k, iters):
@@ -134,6 +179,11 @@ def main(argv=None) -> int:
     a.add_argument("--n", type=int, default=28672)
     a.add_argument("--k", type=int, default=4096)
     a.add_argument("--bn", type=int, default=None)
+    t = sub.add_parser("gemm-timeline")
+    t.add_argument("--m", type=int, default=256)
+    t.add_argument("--n", type=int, default=4096)
+    t.add_argument("--k", type=int, default=1024)
+    t.add_argument("--bn", type=int, default=None)
     b = sub.add_parser("decode")
     b.add_argument("--batch", type=int, default=256)
     b.add_argument("--nq", type=int, default=16)
@@ -148,11 +198,13 @@ def main(argv=None) -> int:
     c.add_argument("--len", type=int, default=2048)
     c.add_argument("--nq", type=int, default=16)
     c.add_argument("--nkv", type=int, default=8)
-    for p in (a, b, c, f):
+    for p in (a, b, c, f, t):
         p.add_argument("--iters", type=int, default=10)
     args = ap.parse_args(argv)
     if args.what == "gemm":
         r = bench_gemm(args.m, args.n, args.k, args.iters, args.bn)
+    elif args.what == "gemm-timeline":
+        r = gemm_timeline(args.m, args.n, args.k, args.iters, args.bn)
     elif args.what == "fp8":
         r = bench_fp8(args.m, args.n, args.k, args.iters)
     elif args.what == "decode":
