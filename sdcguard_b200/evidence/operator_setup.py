@@ -19,7 +19,6 @@ import argparse
 import hashlib
 import json
 import os
-import sys
 
 from . import config, inventory, overhead
 

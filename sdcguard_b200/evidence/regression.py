@@ -22,7 +22,6 @@ import argparse
 import hashlib
 import json
 import os
-import sys
 
 CASE_FILE = os.path.join(os.path.dirname(os.path.abspath(__file__)), "data", "pd_abort_case.json")
 

@@ -18,7 +18,7 @@ from __future__ import annotations
 
 import copy
 from dataclasses import dataclass, field
-from typing import Callable, Optional
+from typing import Callable
 
 from .ledger import RULES
 

@@ -21,13 +21,11 @@ vLLM integration points of src/sdcguard/vllm_plugin.py:2315-2501; here the model
 """
 from __future__ import annotations
 
-import math
 from dataclasses import dataclass, field
 from typing import Optional
 
 import torch
 
-from ..numerics import abft
 from ..ops import attention, gemm, layers
 
 

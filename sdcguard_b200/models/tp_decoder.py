@@ -27,7 +27,6 @@ from typing import Optional
 import torch
 import torch.distributed as dist
 
-from ..numerics import abft
 from ..ops import attention, gemm, layers
 from ..parallel.tp import TPComm, all_gather_nccl, reduce_scatter_nccl
 from .decoder import DecoderConfig, LayerWeights, StepMeta

@@ -20,7 +20,6 @@ import torch.distributed as dist
 
 from .. import _native
 from ..numerics import abft
-from .symm import SymmetricHeap
 
 TOL = 4.0     # multiplier on the rounding bound of the linearity check
 

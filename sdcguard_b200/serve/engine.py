@@ -15,7 +15,6 @@ patch :2430-2501 with mark_step/poll); here the engine is this package's own, wi
 """
 from __future__ import annotations
 
-import math
 import time
 from dataclasses import dataclass
 from typing import Optional, Sequence

@@ -12,7 +12,6 @@ from __future__ import annotations
 import math
 from typing import Callable, Optional
 
-import torch
 
 from ..numerics import abft
 from ..utils.events import EventLog, SDCEvent, device_identity

@@ -23,7 +23,6 @@ import argparse
 import ctypes
 import json
 import math
-from typing import Optional
 
 import torch
 

@@ -34,7 +34,6 @@ import hashlib
 import io
 import json
 import math
-from typing import Optional
 
 import torch
 

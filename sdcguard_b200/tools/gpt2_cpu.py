@@ -22,7 +22,7 @@ import torch
 
 from ..models.gpt2 import GPT2, GPT2Config
 from ..numerics import abft
-from ..numerics.cpu_abft import U32, protect_cpu
+from ..numerics.cpu_abft import protect_cpu
 from ..utils.inject import flip_bit_
 
 

@@ -13,7 +13,6 @@ from __future__ import annotations
 
 import argparse
 import json
-import math
 
 import torch
 

@@ -35,7 +35,6 @@ per step).
 from __future__ import annotations
 
 import contextlib
-import math
 from typing import Optional
 
 import torch

@@ -18,7 +18,7 @@ Reference: `FaultModel` :54, `fault_model` :72, `corrupt_` :161, `FaultInjector`
 from __future__ import annotations
 
 import random
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 from typing import Optional
 
 import torch
