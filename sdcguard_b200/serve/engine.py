@@ -101,11 +101,6 @@ class LLMEngine:
         """One line for the startup log: `sdcguard_b200 engine: key=value ...` (parsed by `evidence.config`)."""
         return "sdcguard_b200 engine: " + " ".join(f"{k}={v}" for k, v in self.describe().items())
 
-    # ---------------------------------------------------------------- sampling of replay rows
-    def _sample(self, n: int) -> list[int]:
-        salt = self.step_counter % self.sample_every
-        return [r for r in range(n) if (r + salt) % self.sample_every == 0]
-
     # ---------------------------------------------------------------- prefill
     def _prefill_batch(self, reqs: list[int], prompts_dev: torch.Tensor, plens: list[int], bt_dev: torch.Tensor,
                        bt_host: list[list[int]], out_tokens: torch.Tensor) -> None:
@@ -135,13 +130,18 @@ class LLMEngine:
             block_table=bt_b, logits_rows=torch.tensor(last, dtype=torch.int64).to(dev, non_blocking=True),
             tiles=tiles.to(dev, non_blocking=True))
         if self.checked:
-            samp = self._sample(T)
-            per_req: list[list[int]] = [[] for _ in reqs]
-            ri = 0
-            for tkn in samp:
-                while tkn >= starts[ri] + lens[ri]:
-                    ri += 1
-                per_req[ri].append(tkn)
+            # replay sample: per request a run of ceil(n / sample_every) consecutive tokens at an offset that
+            # rotates with the step, so successive prefills of a prompt length cover all of it. One run per
+            # request makes one replay tile, which attends only to the keys up to the run's end (rows spread over
+            # the whole prompt would make the replay read the request's full context).
+            samp, per_req = [], []
+            for i in range(len(reqs)):
+                n = lens[i]
+                k = -(-n // self.sample_every)
+                o = min(((self.step_counter + i) % self.sample_every) * k, n - k)
+                run = list(range(starts[i] + o, starts[i] + o + k))
+                samp.extend(run)
+                per_req.append(run)
             rt, ridx = attention.replay_tiles(per_req, group)
             meta.sample_rows = torch.tensor(samp, dtype=torch.int32).to(dev, non_blocking=True)
             meta.sample_tiles = rt.to(dev, non_blocking=True)
