@@ -68,7 +68,8 @@ def build(sections: dict) -> dict:
             allf[k] = f
             keys.append(k)
         secs[name] = {"sha256": _sha(doc), "verdict": doc.get("verdict") if isinstance(doc, dict) else None,
-                      "scope": doc.get("scope") if isinstance(doc, dict) else None, "findings": keys, "document": doc}
+                      "scope": doc.get("scope") if isinstance(doc, dict) else None, "findings": sorted(keys),
+                      "document": doc}     # sorted: a document's key order does not survive every JSON writer
     counts = {v: sum(1 for f in allf.values() if f["verdict"] == v) for v in catalog.VERDICTS}
     return {"schema": SCHEMA, "catalog_sha256": catalog.catalog_hash(), "sections": secs, "findings": allf,
             "counts": counts, "envelope_sha256": _sha({"sections": {k: v["sha256"] for k, v in secs.items()},
