@@ -55,3 +55,34 @@ def test_record_plan_setup_model_ref_regression_lifetime(tmp_path):
     assert cli.main(["regression", "export", str(tmp_path / "case")]) == 0
     assert cli.main(["regression", "verify", str(tmp_path / "case")]) == 0
     assert cli.main(["lifetime", "conformance"]) == 0
+
+
+def test_inventory_overhead_assignment_forward_cli(tmp_path):
+    from sdcguard_b200.coverage import evidence as ev
+    from sdcguard_b200.evidence import inventory
+    from sdcguard_b200.lifetime import conformance
+    rec = tmp_path / "rec"
+    rec.mkdir()
+    prompts = {"e1": [1, 2, 3], "e2": [5, 6]}
+    (rec / "REQUEST_PLAN.json").write_text(json.dumps({"requests": [
+        {"request_id": r, "prompt_tokens": len(t), "prompt_sha256": ev.digest(ev.json_bytes(t))}
+        for r, t in prompts.items()]}))
+    (rec / "OBSERVER.json").write_text(json.dumps({"records": [{"request_id": r} for r in prompts]}))
+    inv = tmp_path / "inv.json"
+    inv.write_text(json.dumps(inventory.from_prompts({"c1": [1, 2, 3], "c2": [5, 6]})))
+    assert cli.main(["inventory", str(inv), str(rec)]) == 0
+    line = {"metric": "m", "n_gpus": 1, "dtype": "bf16", "config": {"a": 1}, "unit": "tok/s"}
+    (tmp_path / "on.jsonl").write_text(json.dumps(dict(line, value=98.0)) + "\n")
+    (tmp_path / "off.jsonl").write_text(json.dumps(dict(line, value=100.0)) + "\n")
+    assert cli.main(["overhead", "compare", "--on", str(tmp_path / "on.jsonl"), "--off", str(tmp_path / "off.jsonl"),
+                     "--bound", "3"]) == 0
+    assert cli.main(["overhead", "compare", "--on", str(tmp_path / "on.jsonl"), "--off", str(tmp_path / "off.jsonl"),
+                     "--bound", "1"]) == 3
+    with conformance.cpu_transfers():
+        events = conformance._scenario("prefix_reuse")
+    ev_path = tmp_path / "lifetime.jsonl"
+    ev_path.write_text("".join(json.dumps(e) + "\n" for e in events))
+    assert cli.main(["assignment", "inspect", str(ev_path)]) == 0
+    assert cli.main(["forward-inputs", "inspect", str(ev_path)]) == 0
+    assert cli.main(["forward-inputs", "packet", str(ev_path), "--out", str(tmp_path / "fp.json")]) == 0
+    assert cli.main(["forward-inputs", "verify", str(tmp_path / "fp.json")]) == 0
