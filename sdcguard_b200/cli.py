@@ -7,6 +7,7 @@
     sdcguard selftest                                        GPU self-test of every checked kernel
     sdcguard campaign                                        fault-injection campaign on the GPU paths
     sdcguard check                                           GPU check card (GEMM, bandwidth, injected faults)
+    sdcguard nhc [--cached]                                  node health check on every GPU (exit 0 / 1 / 2)
     sdcguard screen / screen-ops / modes                     workload, operator and math-mode screens of a GPU
     sdcguard blas / kernels / issues                         cuBLASLt algorithm sweep, kernel inventory, known issues
     sdcguard certify / fleet / board                         signed certificates, fleet view, results board
@@ -49,6 +50,7 @@ COMMANDS = {
     "selftest": _lazy(".tools.selftest", "main"),
     "campaign": _lazy(".tools.campaign", "main"),
     "check": _lazy(".tools.check", "main"),
+    "nhc": _lazy(".tools.nhc", "main"),
     "screen": _lazy(".tools.screen", "main"),
     "screen-ops": _lazy(".tools.screen_ops", "main"),
     "modes": _lazy(".tools.modes", "main"),
