@@ -152,10 +152,72 @@ class SDCGuard:
                     self.modules.append(mod)
         return model
 
+    def should_check(self, step: int) -> bool:
+        """True on every `check_every`-th step, and on every step of a window opened by after_restart() or observe()."""
+        if step % self.check_every == 0:
+            return True
+        windows = [w for w in (getattr(self, "_dense", None), getattr(self, "_spike", None)) if w is not None]
+        return any(a <= step < b for a, b in windows)
+
+    def after_restart(self, step: int, steps: int = 50) -> "SDCGuard":
+        """Call when training resumes from a checkpoint (after a crash, say): every step from `step` to
+        `step + steps` is checked, so a GPU that is still bad is named before it costs another run."""
+        self._dense = (step, step + steps)
+        return self
+
+    def observe(self, step: int, loss=None, grad_norm=None, steps: int = 50, threshold: float = 8.0) -> bool:
+        """Watch the loss and gradient norm (numbers, after each step). When one is not finite, or lies more than
+        `threshold` robust deviations (1.4826 x median absolute deviation) above the median of its last 200 values
+        (once 20 are known), every step from the next one for `steps` steps is checked. A loss or gradient spike is
+        often the first sign of corruption; this turns it into a checked window. Returns True when it opened or
+        extended one; the reasons go to `self.anomalies`."""
+        import collections
+        import math
+        import statistics
+        hist = getattr(self, "_watch", None)
+        if hist is None:
+            hist = self._watch = {}
+            self.anomalies = []
+        why = []
+        for name, v in (("loss", loss), ("grad_norm", grad_norm)):
+            if v is None:
+                continue
+            try:
+                v = float(v)
+            except (TypeError, ValueError):
+                continue
+            h = hist.setdefault(name, collections.deque(maxlen=200))
+            if not math.isfinite(v):
+                why.append(f"{name} is {v}")
+                continue
+            if len(h) >= 20:
+                med = statistics.median(h)
+                spread = max(statistics.median(abs(x - med) for x in h) * 1.4826, 1e-3 * abs(med), 1e-12)
+                if (v - med) / spread > threshold:
+                    why.append(f"{name} {v:.4g}, recent median {med:.4g}")
+            h.append(v)
+        if not why:
+            return False
+        start = step + 1
+        prev = getattr(self, "_spike", None)
+        end = max(prev[1] if prev is not None and prev[1] > start else 0, start + steps)
+        self._spike = (start, end)
+        self.anomalies.append({"step": step, "why": why, "checked_through": end - 1})
+        return True
+
     @contextlib.contextmanager
-    def at_step(self, step: int):
+    def on_step(self, step: int):
+        """Wrap one training step: checked when should_check(step), otherwise untouched. Yields whether it is."""
+        if self.should_check(step):
+            with self.at_step(step, force=True):
+                yield True
+        else:
+            yield False
+
+    @contextlib.contextmanager
+    def at_step(self, step: int, force: bool = False):
         self.step = step
-        self.active = step % self.check_every == 0
+        self.active = force or step % self.check_every == 0
         try:
             yield self
         finally:
