@@ -20,8 +20,15 @@ class SDCGuardCallback(TrainerCallback):
         self._ctx = None
 
     def on_step_begin(self, args, state, control, **kw):
-        self._ctx = self.guard.at_step(state.global_step)
+        step = state.global_step
+        self._ctx = self.guard.at_step(step, force=self.guard.should_check(step))   # schedule and windows
         self._ctx.__enter__()
+
+    def on_log(self, args, state, control, logs=None, **kw):
+        """Loss and gradient-norm spikes in the trainer's logs open a checked window (SDCGuard.observe)."""
+        if logs:
+            self.guard.observe(state.global_step, loss=logs.get("loss"), grad_norm=logs.get("grad_norm"))
+        return control
 
     def on_step_end(self, args, state, control, **kw):
         if self._ctx is not None:
