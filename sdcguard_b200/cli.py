@@ -11,7 +11,7 @@
     sdcguard screen / screen-ops / modes                     workload, operator and math-mode screens of a GPU
     sdcguard blas / kernels / issues                         cuBLASLt algorithm sweep, kernel inventory, known issues
     sdcguard certify / fleet / board                         signed certificates, fleet view, results board
-    sdcguard casefile / investigate                          incident casefile and replays of a flagged GEMM
+    sdcguard casefile / replay / investigate                 incident casefile, replays of a flagged GEMM here
     sdcguard gate-model                                      teacher-forced output comparison of two stacks
     sdcguard serve / ready / perf / isolation / consistency  HTTP server and outside-in probes
     sdcguard qualify / decide                                stack-change qualification and decision
@@ -61,6 +61,7 @@ COMMANDS = {
     "fleet": _lazy(".tools.fleet", "main"),
     "board": _lazy(".tools.board", "main"),
     "casefile": _lazy(".tools.casefile", "main"),
+    "replay": _lazy(".tools.casefile", "replay_main"),
     "investigate": _lazy(".tools.investigate", "main"),
     "gate-model": _lazy(".tools.gate_model", "main"),
     "serve": _lazy(".serve.http", "main"),

@@ -187,5 +187,31 @@ def main(argv=None) -> int:
     return 0
 
 
+def replay_main(argv=None) -> int:
+    """`sdcguard replay CASE.pt [--times N] [--device D] [--save OUT.json]`: recompute a captured block here, print
+    the replay record (the casefile's input), exit 1 when a recomputation came out wrong or alarmed again, 0 when
+    none did, 2 when it could not run. (Reference: `sdcguard replay`, src/sdcguard/cli.py:214, screen.py:657.)"""
+    ap = argparse.ArgumentParser(prog="sdcguard replay")
+    ap.add_argument("case")
+    ap.add_argument("--times", type=int, default=200)
+    ap.add_argument("--device", default="cuda:0")
+    ap.add_argument("--save")
+    a = ap.parse_args(argv)
+    if a.times < 1:
+        print("sdcguard replay: --times must be at least 1")
+        return 2
+    try:
+        case = torch.load(a.case, weights_only=False)
+        r = replay(case, a.times, a.device)
+    except (OSError, RuntimeError, KeyError, ValueError) as e:
+        print(f"sdcguard replay: could not run ({type(e).__name__}: {e})")
+        return 2
+    print(json.dumps(r, indent=1, default=str))
+    if a.save:
+        with open(a.save, "w") as f:
+            json.dump(r, f, indent=1, default=str)
+    return 1 if r["reproduced"] else 0
+
+
 if __name__ == "__main__":
     raise SystemExit(main())

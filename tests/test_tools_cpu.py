@@ -123,3 +123,9 @@ def test_investigate_classification():
     assert classify([both, both], []) == "NOT ONE GPU"
     assert classify([ours], []) == "INCONCLUSIVE"
     assert classify([ok], [{"error": "x"}]) == "INCONCLUSIVE"
+
+
+def test_replay_command_refuses_what_it_cannot_run(tmp_path):
+    from sdcguard_b200 import cli
+    assert cli.main(["replay", str(tmp_path / "missing.pt")]) == 2
+    assert cli.main(["replay", str(tmp_path / "missing.pt"), "--times", "0"]) == 2
