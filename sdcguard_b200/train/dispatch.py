@@ -43,6 +43,7 @@ from torch.utils._python_dispatch import TorchDispatchMode
 from ..numerics import abft
 from ..ops import gemm
 from ..utils.events import EventLog, SDCEvent, device_identity
+from .guard import SDCGuard
 
 aten = torch.ops.aten
 
@@ -94,9 +95,23 @@ class DispatchGuard(TorchDispatchMode):
         self._saved_flags = None
 
     # ---------------------------------------------------------------- schedule
+    # the same schedule as SDCGuard: every N-th step, plus the windows of after_restart() and observe()
+    should_check = SDCGuard.should_check
+    after_restart = SDCGuard.after_restart
+    observe = SDCGuard.observe
+
     @contextlib.contextmanager
-    def at_step(self, step: int):
-        if step % self.check_every:
+    def on_step(self, step: int):
+        """Wrap one training step: checked when should_check(step), otherwise untouched. Yields whether it is."""
+        if self.should_check(step):
+            with self.at_step(step, force=True):
+                yield True
+        else:
+            yield False
+
+    @contextlib.contextmanager
+    def at_step(self, step: int, force: bool = False):
+        if step % self.check_every and not force:
             yield self
             return
         self._cw_cache.clear()

@@ -121,3 +121,14 @@ def test_reduced_precision_flags_restored():
     with g.at_step(0):
         assert not m.allow_bf16_reduced_precision_reduction and not m.allow_fp16_reduced_precision_reduction
     assert (m.allow_bf16_reduced_precision_reduction, m.allow_fp16_reduced_precision_reduction) == before
+
+
+def test_schedule_windows_drive_on_step():
+    g = DispatchGuard(device="cpu", check_every=100)
+    a, b = torch.randn(8, 16), torch.randn(16, 8)
+    g.after_restart(5, steps=2)
+    for step in range(4, 9):
+        with g.on_step(step) as checked:
+            a @ b
+        assert checked == (step in (5, 6))
+    assert g.coverage()["checked"] == 2
