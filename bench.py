@@ -13,9 +13,12 @@ overhead; an end-to-end number through the public API (`LLMEngine.generate`, wal
 tokens out each step); a short fault-injection campaign (single-bit flips in GEMM accumulators, KV pages and
 replayed rows) with the false alarms of the timed clean run; SM clocks sampled during the timed region.
 
---impl reference runs the unmodified reference package (baseline/_ref) through its public API on the same load:
-`sdcguard.serve.ServeGuard().attach(model)` on a stock Hugging Face transformers Qwen3 model of the same shape
-(random init, bf16), generating with `model.generate` in batches.
+--impl reference runs the unmodified reference package (installed in baseline/_ref) on its stock serving path, the
+way its own vLLM experiments run it: vLLM's offline `LLM` engine on the same Qwen3-0.6B shape (random weights,
+16-token KV blocks, prefix caching off so every step redoes every prompt), once with the reference's vLLM plugin
+on (SDCGUARD=1: every linear layer checked by its Triton check, attention recompute on, stock settings) and once
+with it off, each in a process of its own per GPU. The line reports the checked throughput as `value` and the
+unchecked one beside it.
 """
 from __future__ import annotations
 
@@ -29,7 +32,7 @@ import time
 
 import torch
 
-BASELINE_VALUE = None          # BASELINE.md has no published number for this config
+BASELINE_VALUE = None          # no published number exists for this config
 METRIC = "checked tokens/s (prompt + generated) on Qwen3-0.6B-shaped serving, 256 req x 1024-2048 in / 128 out"
 
 
@@ -43,14 +46,23 @@ def parse():
     ap.add_argument("--new-tokens", type=int, default=128)
     ap.add_argument("--no-unchecked", action="store_true", help="skip the unchecked comparison run")
     ap.add_argument("--no-campaign", action="store_true", help="skip the fault-injection campaign")
+    ap.add_argument("--ref-child", choices=["checked", "unchecked"], help=argparse.SUPPRESS)
+    ap.add_argument("--ref-rank", default="0", help=argparse.SUPPRESS)
     return ap.parse_args()
 
 
 # ------------------------------------------------------------------------------------------ distributed
-def dist_setup():
+def dist_setup(use_gpu: bool = True):
+    """Rank, world size and local rank from torchrun's environment; NCCL over this rank's GPU, or (for the
+    reference arm, whose GPU belongs to the serving process it starts) gloo on the host."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if not use_gpu:
+        if world > 1:
+            import datetime
+            torch.distributed.init_process_group("gloo", timeout=datetime.timedelta(seconds=1500))
+        return rank, world, local
     torch.cuda.set_device(local)
     if world > 1:
         import datetime
@@ -207,61 +219,186 @@ def run_ours(args, rank, world, local):
 
 
 # ------------------------------------------------------------------------------------------ reference arm
-def run_reference(args, rank, world, local):
-    ref = os.path.join(os.path.dirname(os.path.abspath(__file__)), "baseline", "_ref")
-    if not os.path.isdir(os.path.join(ref, "sdcguard")):
-        return {"unavailable": "reference not installed in baseline/_ref"}
-    sys.path.insert(0, ref)
-    from sdcguard.serve import ServeGuard      # the reference's public serving API
-    from transformers import Qwen3Config, Qwen3ForCausalLM
-    cfg = Qwen3Config(vocab_size=151936, hidden_size=1024, intermediate_size=3072, num_hidden_layers=28,
-                      num_attention_heads=16, num_key_value_heads=8, head_dim=128, max_position_embeddings=40960,
-                      rope_theta=1_000_000.0, rms_norm_eps=1e-6, tie_word_embeddings=True)
-    torch.manual_seed(0)
-    with torch.device("cuda"):
-        model = Qwen3ForCausalLM(cfg).to(torch.bfloat16).eval()
-    guard = ServeGuard().attach(model)
-    prompts, lens = make_load(args.requests, seed=1234 + rank, vocab=cfg.vocab_size)
-    prompts = prompts.pin_memory()
+QWEN3_0_6B_HF = {
+    "architectures": ["Qwen3ForCausalLM"], "model_type": "qwen3", "hidden_size": 1024, "intermediate_size": 3072,
+    "num_hidden_layers": 28, "num_attention_heads": 16, "num_key_value_heads": 8, "head_dim": 128,
+    "vocab_size": 151936, "max_position_embeddings": 40960, "rope_theta": 1000000.0, "rms_norm_eps": 1e-06,
+    "tie_word_embeddings": True, "torch_dtype": "bfloat16", "hidden_act": "silu", "attention_bias": False,
+    "attention_dropout": 0.0, "bos_token_id": 151643, "eos_token_id": 151645, "use_cache": True,
+    "use_sliding_window": False, "max_window_layers": 28, "initializer_range": 0.02,
+}
+
+
+def _ref_dir() -> str:
+    return os.path.join(os.path.dirname(os.path.abspath(__file__)), "baseline", "_ref")
+
+
+def _child_env(local: int, checked: bool) -> dict:
+    """Environment of one reference serving process: this rank's GPU only, no torchrun variables (the engine
+    builds its own one-process world), the reference package first on the path so vLLM finds its plugin entry
+    point, and the plugin on (SDCGUARD=1, its stock defaults) or off."""
+    env = {k: v for k, v in os.environ.items()
+           if k not in ("RANK", "LOCAL_RANK", "WORLD_SIZE", "LOCAL_WORLD_SIZE", "GROUP_RANK", "ROLE_RANK",
+                        "ROLE_WORLD_SIZE", "MASTER_ADDR", "MASTER_PORT", "TORCHELASTIC_RUN_ID",
+                        "TORCHELASTIC_RESTART_COUNT", "TORCHELASTIC_MAX_RESTARTS", "GROUP_WORLD_SIZE")}
+    env["CUDA_VISIBLE_DEVICES"] = str(local)
+    env["PYTHONPATH"] = _ref_dir() + os.pathsep + env.get("PYTHONPATH", "")
+    env["VLLM_ENABLE_V1_MULTIPROCESSING"] = "0"       # engine core in this process: CUDA events see its work
+    env["HF_HUB_OFFLINE"] = "1"
+    env["TRANSFORMERS_OFFLINE"] = "1"
+    env["VLLM_CACHE_ROOT"] = f"/tmp/sdcguard_ref_vllm_cache_{local}"
+    env["SDCGUARD"] = "1" if checked else "0"
+    return env
+
+
+def ref_child(args) -> None:
+    """One reference serving process (`bench.py --ref-child checked|unchecked`): vLLM's offline `LLM` on the
+    Qwen3-0.6B shape (config only, random weights through vLLM's dummy loader, no tokenizer), prefix caching off
+    so repeated steps redo every prompt, 16-token KV blocks. With SDCGUARD=1 vLLM loads the reference's plugin
+    (its `vllm.general_plugins` entry point) and every linear layer and attention layer is checked as the
+    reference ships it. Protocol on stdout/stdin: after the warm-up it prints READY and waits for a line GO, runs
+    the timed steps, then prints its timings as one line `REFRESULT {json}`."""
+    import torch
+    from vllm import LLM, SamplingParams
+    from vllm.inputs import TokensPrompt
+    import vllm
+    mdir = f"/tmp/sdcguard_ref_model_{os.getpid()}"
+    os.makedirs(mdir, exist_ok=True)
+    with open(os.path.join(mdir, "config.json"), "w") as f:
+        json.dump(QWEN3_0_6B_HF, f)
+    rank = int(args.ref_rank)
+    prompts, lens = make_load(args.requests, seed=1234 + rank, vocab=QWEN3_0_6B_HF["vocab_size"])
+    reqs = [TokensPrompt(prompt_token_ids=prompts[i, :lens[i]].tolist()) for i in range(args.requests)]
+    sp = SamplingParams(max_tokens=args.new_tokens, min_tokens=args.new_tokens, ignore_eos=True, temperature=0.0)
+    llm = LLM(model=mdir, load_format="dummy", skip_tokenizer_init=True, dtype="bfloat16", block_size=16,
+              max_model_len=2048 + args.new_tokens, enable_prefix_caching=False, seed=0,
+              gpu_memory_utilization=float(os.environ.get("SDCGUARD_REF_GPU_MEM", "0.85")))
     tokens_per_step = sum(lens) + args.requests * args.new_tokens
-    batch = int(os.environ.get("SDCGUARD_REF_BATCH", "64"))
+    h2d = sum(lens) * 8
 
     def step():
-        outs = []
-        for b0 in range(0, args.requests, batch):
-            idx = list(range(b0, min(args.requests, b0 + batch)))
-            L = max(lens[i] for i in idx)
-            ids = torch.zeros(len(idx), L, dtype=torch.long)
-            mask = torch.zeros(len(idx), L, dtype=torch.long)
-            for j, i in enumerate(idx):           # left padding, as batched generation needs
-                ids[j, L - lens[i]:] = prompts[i, :lens[i]]
-                mask[j, L - lens[i]:] = 1
-            ids = ids.pin_memory().to("cuda", non_blocking=True)
-            mask = mask.pin_memory().to("cuda", non_blocking=True)
-            with torch.no_grad():
-                out = model.generate(input_ids=ids, attention_mask=mask, max_new_tokens=args.new_tokens,
-                                     min_new_tokens=args.new_tokens, do_sample=False, pad_token_id=0)
-            outs.append(out[:, L:].cpu())
+        outs = llm.generate(reqs, sp, use_tqdm=False)
+        n = sum(len(o.outputs[0].token_ids) for o in outs)
+        assert n == args.requests * args.new_tokens, f"generated {n} tokens"
         return outs
 
     for _ in range(args.warmup):
         step()
-    guard.poll()
-    with ClockSampler(local) as clk:
-        dev_ms, wall_ms = time_steps(step, args.steps, world)
-    events = guard.poll()
-    return {"dev_ms": dev_ms, "wall_ms": wall_ms, "tokens_per_step": tokens_per_step, "clocks": clk.summary(),
-            "false_alarms": int(sum_over_ranks(len(events), world))}
+    plugin = None
+    if os.environ.get("SDCGUARD") == "1":
+        from sdcguard import vllm_plugin as plugin     # the reference's public read-back call
+        plugin.poll(wait=True)
+    print("READY", flush=True)
+    sys.stdin.readline()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    a.record()
+    for _ in range(args.steps):
+        step()
+    b.record()
+    torch.cuda.synchronize()
+    t1 = time.perf_counter()
+    alarms, checked_layers = 0, None
+    if plugin is not None:
+        alarms = len(plugin.poll(wait=True) or [])
+        g = plugin.guard()
+        checked_layers = len(getattr(g, "layers", []) or []) if g is not None else 0
+    print("REFRESULT " + json.dumps({"dev_ms": a.elapsed_time(b) / args.steps, "wall_ms": (t1 - t0) * 1000 / args.steps,
+                      "tokens_per_step": tokens_per_step, "h2d_bytes": h2d, "alarms": alarms,
+                      "checked_layers": checked_layers, "vllm": vllm.__version__}), flush=True)
+
+
+def _ref_phase(args, rank, world, local, checked: bool) -> dict:
+    """Start this rank's reference serving process, wait for its READY, barrier over the ranks, release the timed
+    steps together (GO), and collect its timings; clocks are sampled while it runs."""
+    cmd = [sys.executable, os.path.abspath(__file__), "--ref-child", "checked" if checked else "unchecked",
+           "--ref-rank", str(rank), "--steps", str(args.steps), "--warmup", str(args.warmup),
+           "--requests", str(args.requests), "--new-tokens", str(args.new_tokens)]
+    log = open(f"/tmp/sdcguard_ref_{'c' if checked else 'u'}_{rank}.log", "w")
+    p = subprocess.Popen(cmd, env=_child_env(local, checked), stdin=subprocess.PIPE, stdout=subprocess.PIPE,
+                         stderr=log, text=True)
+    ok = False
+    for line in p.stdout:
+        if line.strip() == "READY":
+            ok = True
+            break
+    flag = torch.tensor([1 if ok else 0], dtype=torch.int64)
+    if world > 1:
+        torch.distributed.all_reduce(flag, op=torch.distributed.ReduceOp.MIN)
+    res = None
+    if int(flag.item()) == 1:
+        with ClockSampler(local) as clk:
+            p.stdin.write("GO\n")
+            p.stdin.flush()
+            for line in p.stdout:
+                line = line.strip()
+                if line.startswith("REFRESULT "):
+                    res = json.loads(line[len("REFRESULT "):])
+                    break
+        if res is not None:
+            res["clocks"] = clk.summary()
+    try:
+        p.stdin.close()
+    except OSError:
+        pass
+    try:
+        p.wait(timeout=120)
+    except subprocess.TimeoutExpired:
+        p.kill()
+    log.close()
+    got = torch.tensor([1 if res is not None else 0], dtype=torch.int64)
+    if world > 1:
+        torch.distributed.all_reduce(got, op=torch.distributed.ReduceOp.MIN)
+    if int(got.item()) == 0:
+        tail = open(log.name).read()[-600:].replace("\n", " | ")
+        return {"failed": f"reference serving process ({'checked' if checked else 'unchecked'}) on rank {rank} "
+                          f"gave no timings (rc {p.returncode}): {tail}"}
+    for k in ("dev_ms", "wall_ms"):
+        res[k] = max_over_ranks_cpu(res[k], world)
+    res["alarms"] = int(sum_over_ranks_cpu(res["alarms"], world))
+    return res
+
+
+def max_over_ranks_cpu(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks_cpu(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64)
+    torch.distributed.all_reduce(t)
+    return float(t.item())
+
+
+def run_reference(args, rank, world, local):
+    if not os.path.isdir(os.path.join(_ref_dir(), "sdcguard")):
+        return {"unavailable": "reference not installed in baseline/_ref"}
+    checked = _ref_phase(args, rank, world, local, checked=True)
+    if "failed" in checked:
+        return {"unavailable": checked["failed"]}
+    out = dict(checked)
+    if not args.no_unchecked:
+        un = _ref_phase(args, rank, world, local, checked=False)
+        if "failed" not in un:
+            out["unchecked_dev_ms"] = un["dev_ms"]
+    out["false_alarms"] = checked["alarms"]
+    return out
 
 
 def main():
     args = parse()
-    rank, world, local = dist_setup()
+    if args.ref_child:
+        ref_child(args)
+        return
+    rank, world, local = dist_setup(use_gpu=args.impl == "ours")
     n = world
-    try:
-        res = run_ours(args, rank, world, local) if args.impl == "ours" else run_reference(args, rank, world, local)
-    finally:
-        pass
+    res = run_ours(args, rank, world, local) if args.impl == "ours" else run_reference(args, rank, world, local)
     if rank == 0:
         base = {"n_gpus": n, "steps": args.steps, "warmup": args.warmup, "dtype": "bf16",
                 "data": "synthetic (random token ids, random-init weights N(0,0.02))",
@@ -280,21 +417,23 @@ def main():
                     "vs_baseline": None if BASELINE_VALUE is None else round(tps / BASELINE_VALUE, 4),
                     "clocks": res["clocks"],
                     "e2e": {"value": round(n * res["tokens_per_step"] / (res["wall_ms"] / 1000.0), 1),
-                            "unit": "tokens/s (wall clock through generate(), pinned prompts in, tokens out)",
-                            "h2d_bytes_per_step": args.requests * 2048 * 8,
+                            "unit": "tokens/s (wall clock through generate(), prompts in, tokens out)",
+                            "h2d_bytes_per_step": res.get("h2d_bytes", args.requests * 2048 * 8),
                             "d2h_bytes_per_step": args.requests * args.new_tokens * 8},
                     "false_alarms_clean_run": res["false_alarms"]}
+            if "unchecked_dev_ms" in res:
+                u = n * res["tokens_per_step"] / (res["unchecked_dev_ms"] / 1000.0)
+                line["unchecked_value"] = round(u, 1)
+                line["overhead_pct"] = round(100.0 * (u / tps - 1.0), 2)
             if args.impl == "reference":
                 line["impl"] = "reference"
-                line["checks"] = "reference ServeGuard on every nn.Linear (Triton check); no attention/KV checks"
+                line["path"] = (f"vllm {res.get('vllm')} LLM.generate + reference vllm_plugin (SDCGUARD=1, stock "
+                                f"settings: linear-layer Triton check, attention recompute)")
+                line["checked_layers"] = res.get("checked_layers")
             else:
                 line["impl"] = "ours"
                 line["gpu_launches"] = res["launches"]
                 line["coverage"] = res["coverage"]
-                if "unchecked_dev_ms" in res:
-                    u = n * res["tokens_per_step"] / (res["unchecked_dev_ms"] / 1000.0)
-                    line["unchecked_value"] = round(u, 1)
-                    line["overhead_pct"] = round(100.0 * (u / tps - 1.0), 2)
                 if "campaign" in res:
                     line["detection"] = res["campaign"]
         print(json.dumps(line), flush=True)

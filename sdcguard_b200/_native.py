@@ -59,6 +59,7 @@ F = c_float
 # name -> (restype, argtypes)
 SIGNATURES: dict[str, tuple] = {
     "sdc_gemm_ws_bytes": (L, [I, I]),
+    "sdc_gemm_counter_bytes": (L, []),
     "sdc_gemm_bf16": (I, [P, L, P, P, I, I, I, P, L, P, P, F, P, P, P, P, I, U, U, U, U, F, F, F, F, F, P, I, I, I, I,
                           U, P, P, P]),
     "sdc_row_sqnorm_bf16": (I, [P, L, I, I, P, P]),
@@ -142,6 +143,23 @@ def lib():
                 setattr(wrapped, name, _Counted(fn))
         _lib = wrapped
         return _lib
+
+
+WAIT_LIMIT_UNITS = ("attention", "ep_comm", "gemm_abft", "gemm_fp8", "tp_comm")
+DEFAULT_WAIT_NS = 2_000_000_000
+
+
+def set_wait_limit(ns: int = DEFAULT_WAIT_NS) -> None:
+    """Deadline of every bounded device-side wait of this library's kernels (mbarrier phases, peer flags, band
+    counters), in nanoseconds, on the CURRENT CUDA device. 2 s by default; a wait that runs out records an error
+    code in the launch's error word and the kernel returns. Call outside stream capture (it is a synchronous copy
+    to each compiled unit's own copy of the limit)."""
+    h = lib()
+    for unit in WAIT_LIMIT_UNITS:
+        fn = getattr(h._h, f"sdc_set_wait_ns_{unit}")
+        fn.restype = c_int
+        fn.argtypes = [ctypes.c_ulonglong]
+        check(fn(int(ns)), f"sdc_set_wait_ns_{unit}")
 
 
 def available() -> bool:

@@ -871,3 +871,6 @@ int sdc_attn_decode(const void* q, void* o, const void* cache, long long num_blo
 }
 
 }  // extern "C"
+
+// run-time wait limit of this unit (see common.cuh)
+SDC_WAIT_LIMIT_SETTER(attention)

@@ -22,8 +22,22 @@ enum : int {
   ERR_BAD_ARG = 5,
 };
 
-// Default deadline for a single wait: 2 s of %globaltimer. Normal waits last microseconds.
-constexpr unsigned long long kWaitNs = 2000000000ull;
+// Deadline of a single wait in ns of %globaltimer: 2 s unless the host lowers it. Normal waits last microseconds;
+// a test that makes a wait run out sets a short limit so the kernel returns its error status quickly. The library
+// is built without relocatable device code, so every translation unit holds its own copy of the limit and exports
+// a setter for it (SDC_WAIT_LIMIT_SETTER); the Python side calls every unit's setter. A setter writes the copy of
+// the current device and must not run while a stream of that device is being captured into a graph.
+static __device__ unsigned long long g_wait_ns = 2000000000ull;
+__device__ __forceinline__ unsigned long long wait_limit_ns() {
+  return *static_cast<volatile unsigned long long*>(&g_wait_ns);
+}
+static inline int set_wait_limit_of_unit(unsigned long long ns) {
+  return static_cast<int>(cudaMemcpyToSymbol(g_wait_ns, &ns, sizeof(ns)));
+}
+#define SDC_WAIT_LIMIT_SETTER(unit)                                        \
+  extern "C" int sdc_set_wait_ns_##unit(unsigned long long ns) {           \
+    return ::sdc::set_wait_limit_of_unit(ns);                              \
+  }
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -65,7 +79,7 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 // Waits for the phase with the given parity to complete. Gives up when `abort` (shared flag) is set
-// by another role or after kWaitNs; returns false then.
+// by another role or after wait_limit_ns(); returns false then.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
   if (mbar_test(bar, parity)) return true;
   const unsigned long long t0 = globaltimer();
@@ -73,7 +87,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     if (mbar_test(bar, parity)) return true;
     if ((i & 255u) == 0u) {
       if (abort && *abort) return false;
-      if (globaltimer() - t0 > kWaitNs) return false;
+      if (globaltimer() - t0 > wait_limit_ns()) return false;
     }
   }
 }
@@ -121,7 +135,7 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
     if (mbar_test_acq_cluster(bar, parity)) return true;
     if ((i & 255u) == 0u) {
       if (abort && *abort) return false;
-      if (globaltimer() - t0 > kWaitNs) return false;
+      if (globaltimer() - t0 > wait_limit_ns()) return false;
     }
   }
 }

@@ -403,3 +403,6 @@ int sdc_router_topk(const void* logits, int ld, int T, int E, int K, int* ids, f
 }
 
 }  // extern "C"
+
+// run-time wait limit of this unit (see common.cuh)
+SDC_WAIT_LIMIT_SETTER(ep_comm)

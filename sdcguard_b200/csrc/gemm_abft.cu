@@ -684,7 +684,7 @@ __global__ void __launch_bounds__(Cfg<BN, PAIR>::THREADS, 1)
               ok = 1;
               break;
             }
-            if ((i & 63u) == 63u && (globaltimer() - t0 > kWaitNs || *abort_flag)) break;
+            if ((i & 63u) == 63u && (globaltimer() - t0 > wait_limit_ns() || *abort_flag)) break;
           }
           if (!ok) record_error(p.err, ERR_TIMEOUT_PEER);
         }
@@ -1145,6 +1145,10 @@ static bool split_eligible(int M, int N) { return (M + BM - 1) / BM <= 2 && N <=
 // CTA-pair clusters of the 256-wide pair kernel that can be resident at once (0: pair mode unavailable).
 int sdc_gemm_pair_clusters() { return pair_max_clusters(); }
 
+// Bytes at the start of a workspace that hold the band counters. They return to zero at the end of every
+// launch that completes; after a launch whose wait ran out (error word set) the caller zeroes them again.
+long long sdc_gemm_counter_bytes() { return COUNTER_BYTES; }
+
 long long sdc_gemm_ws_bytes(int M, int N) {
   return ws_bytes_base(M, N) + (split_eligible(M, N) ? part_bytes(M, N) + 256 : 0);
 }
@@ -1381,3 +1385,6 @@ extern "C" int sdc_gemm_bf16_noalloc(const void* A, long long lda, const void* W
                   s2, s3, zthr, prod_coef, out_coef, abs_floor, bound_coef, err, bn, max_ctas, -1, -1, 0u, nullptr,
                   nullptr, stream, false);
 }
+
+// run-time wait limit of this unit (see common.cuh)
+SDC_WAIT_LIMIT_SETTER(gemm_abft)

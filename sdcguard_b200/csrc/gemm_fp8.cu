@@ -610,3 +610,6 @@ int sdc_fp8_quant_act(const void* x, long long ldx, int M, int K, void* xq, floa
 }
 
 }  // extern "C"
+
+// run-time wait limit of this unit (see common.cuh)
+SDC_WAIT_LIMIT_SETTER(gemm_fp8)

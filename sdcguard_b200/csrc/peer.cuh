@@ -3,7 +3,7 @@
 // pointer, and one collective step is a generation flag that every rank publishes to every peer.
 //
 //   signal : gen += 1 on this rank; store gen into flags[my_rank] of every peer (release, system scope).
-//   wait   : spin (bounded by kWaitNs of %globaltimer) until every flags[r] of this rank >= gen (acquire).
+//   wait   : spin (bounded by wait_limit_ns() of %globaltimer) until every flags[r] of this rank >= gen (acquire).
 //
 // Every rank calls signal/wait the same number of times in the same order, so the generations agree; the
 // counter lives on the device, which keeps the sequence valid inside CUDA graphs.
@@ -53,7 +53,7 @@ __device__ inline bool wait_all(const long long* gen, const long long* my_flags,
     const unsigned long long t0 = globaltimer();
     for (int r = 0; r < world && ok; ++r) {
       while (ld_acquire_sys(my_flags + r) < g) {
-        if (globaltimer() - t0 > kWaitNs) {
+        if (globaltimer() - t0 > wait_limit_ns()) {
           ok = 0;
           record_error(err, ERR_TIMEOUT_PEER);
           break;

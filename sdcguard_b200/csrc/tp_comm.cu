@@ -257,3 +257,6 @@ int sdc_seal_verify(const void* x, long long ld, int M, int N, const void* want,
 }
 
 }  // extern "C"
+
+// run-time wait limit of this unit (see common.cuh)
+SDC_WAIT_LIMIT_SETTER(tp_comm)

@@ -32,7 +32,12 @@ def _stream_ptr(device: torch.device) -> int:
 
 def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
     """Per-device workspace of at least nbytes, zero-filled when (re)allocated. Reallocation must not happen
-    while a CUDA graph is being captured: engines call `reserve_workspace` with their largest shape first."""
+    while a CUDA graph is being captured: engines call `reserve_workspace` with their largest shape first.
+
+    One workspace serves every checked GEMM of the device, so checked GEMMs of one device must not run
+    concurrently on different streams (the engines and guards of this package issue them on one stream; the
+    replay checks that run on side streams launch no GEMM). Its band counters return to zero at the end of every
+    launch that completes; `take_errors` zeroes them after a launch whose wait ran out."""
     idx = device.index if device.index is not None else torch.cuda.current_device()
     with _ws_lock:
         ws = _WS.get(idx)
@@ -43,6 +48,30 @@ def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
             ws = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
             _WS[idx] = ws
         return ws
+
+
+ERROR_NAMES = {0: "none", 1: "producer wait timed out", 2: "MMA wait timed out", 3: "epilogue wait timed out",
+               4: "peer or band wait timed out", 5: "bad argument"}
+
+
+def take_errors(device: torch.device) -> int:
+    """Read and clear the device's kernel error word (first error code recorded by any launch since the last
+    call; 0 = none). One device-to-host copy on the current stream, so call it where a sync is acceptable (poll
+    time). When a wait ran out, a checked GEMM may have stopped in the middle of a band and left its counters
+    raised: they are zeroed on the current stream, so the next launch starts from clean counters instead of
+    judging against the expected sums of an unfinished launch."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    e = _ERR.get(idx)
+    if e is None:
+        return 0
+    code = int(e.item())
+    if code:
+        e.zero_()
+        ws = _WS.get(idx)
+        if ws is not None:
+            n = int(_native.lib().sdc_gemm_counter_bytes())
+            ws[:n].zero_()
+    return code
 
 
 def reserve_workspace(device: torch.device, m: int, n: int) -> None:

@@ -37,6 +37,8 @@ import math
 
 import torch
 
+from ..utils.events import load_evidence, plain
+
 SUPPORTED, CONTRADICTED, NOT_TESTED = "supported", "contradicted", "not tested"
 WEAK = 10           # fewer replays than this on one side are weak evidence of absence
 
@@ -61,7 +63,7 @@ def capture(x: torch.Tensor, w: torch.Tensor, y: torch.Tensor, row: int, block: 
     return {"format": "sdcguard-b200-case/1", "kind": "gemm", "row": row, "block": block, "note": note,
             "x_row": x[row].detach().to("cpu", torch.bfloat16).clone(),
             "w_block": w[c0:c1].detach().to("cpu", torch.bfloat16).clone(),
-            "y_block": y[row, c0:c1].detach().to("cpu", torch.bfloat16).clone(), "stack": stack()}
+            "y_block": y[row, c0:c1].detach().to("cpu", torch.bfloat16).clone(), "stack": plain(stack())}
 
 
 def sha256(case: dict) -> str:
@@ -172,7 +174,7 @@ def main(argv=None) -> int:
     ap.add_argument("--save-replay")
     ap.add_argument("--device", default="cuda:0")
     a = ap.parse_args(argv)
-    case = torch.load(a.case, weights_only=False)
+    case = load_evidence(a.case)
     reps = []
     for p in a.replays:
         with open(p) as f:
@@ -201,7 +203,7 @@ def replay_main(argv=None) -> int:
         print("sdcguard replay: --times must be at least 1")
         return 2
     try:
-        case = torch.load(a.case, weights_only=False)
+        case = load_evidence(a.case)
         r = replay(case, a.times, a.device)
     except (OSError, RuntimeError, KeyError, ValueError) as e:
         print(f"sdcguard replay: could not run ({type(e).__name__}: {e})")

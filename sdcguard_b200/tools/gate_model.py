@@ -36,6 +36,8 @@ from typing import Optional
 
 import torch
 
+from ..utils.events import load_evidence
+
 TOPK = 20
 
 
@@ -153,7 +155,7 @@ def main(argv=None) -> int:
         torch.save(ref, a.out)
         print(json.dumps({"out": a.out, "recorded_is_top1": ref["recorded_is_top1"]}))
         return 0
-    ref = torch.load(a.ref, weights_only=False)
+    ref = load_evidence(a.ref)
     noise = None
     if a.noise:
         with open(a.noise) as f:

@@ -22,6 +22,8 @@ import json
 
 import torch
 
+from ..utils.events import load_evidence
+
 from .casefile import replay
 
 
@@ -60,7 +62,7 @@ def main(argv=None) -> int:
     ap.add_argument("case")
     ap.add_argument("--runs", type=int, default=20)
     a = ap.parse_args(argv)
-    r = investigate(torch.load(a.case, weights_only=False), a.runs)
+    r = investigate(load_evidence(a.case), a.runs)
     print(json.dumps(r, indent=1))
     return 0 if r["verdict"] == "NOT REPRODUCED" else 1
 

@@ -12,8 +12,8 @@ limit, such as Slurm's HealthCheckProgram); it reports the cached FAIL at any ag
 --max-age-hours as UNKNOWN. `--simulate-faults` prints what a FAIL line looks like, runs nothing and never touches
 the cached status. The GPUs' checks run at the same time.
 
-Reference: src/sdcguard/cli.py:65-106 (`_deadline`, `_stop_group`, `_run_check`), :228-330 (`_nhc_status`,
-`_nhc_previous`, `_nhc_cached`, `cmd_nhc`: one line, exit codes, sticky FAIL, cached mode).
+Reference: src/sdcguard/cli.py:65-106 (deadline and process-group kill around a check), :228-330 (`cmd_nhc`: one
+line, exit codes, sticky FAIL, the cached mode and its status.json record, whose three fields are kept).
 """
 from __future__ import annotations
 
@@ -24,7 +24,10 @@ import os
 import signal
 import subprocess
 import sys
+import tempfile
+import threading
 import time
+from dataclasses import dataclass
 from typing import Callable, Optional
 
 
@@ -69,54 +72,99 @@ def _finish(p: subprocess.Popen, t_end: float) -> dict:
 
 
 def run_all(cmds: list[list[str]], limit: float) -> list[dict]:
-    """Every GPU's check at once, each in its own process group, all under one deadline."""
+    """Every GPU's check at once, each in its own process group, all under one deadline. Each check's output is
+    drained by a thread of its own, so a check that writes a lot of log never blocks on a full pipe while another
+    one is being waited for (a healthy check must not look hung)."""
     t_end = time.monotonic() + limit
     procs = [subprocess.Popen(c, stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True, start_new_session=True)
              for c in cmds]
+    results: list[Optional[dict]] = [None] * len(procs)
+
+    def collect(i: int) -> None:
+        results[i] = _finish(procs[i], t_end)
+
+    workers = [threading.Thread(target=collect, args=(i,), daemon=True) for i in range(len(procs))]
     try:
-        return [_finish(p, t_end) for p in procs]
+        for w in workers:
+            w.start()
+        for w in workers:
+            while w.is_alive():
+                w.join(timeout=0.5)
     except BaseException:               # an interrupt: stop every group, then let it propagate
         for p in procs:
             _stop_group(p)
         raise
+    return [r if r is not None else {"code": None, "result": None, "timed_out": True} for r in results]
 
 
-def previous(out: str) -> Optional[dict]:
-    try:
-        with open(os.path.join(out, "status.json")) as f:
-            st = json.load(f)
-        return st if isinstance(st, dict) else None
-    except (OSError, ValueError):
-        return None
+@dataclass
+class NodeStatus:
+    """The node's last health line, kept in OUT/status.json as {"time", "code", "line"} (the file the scheduler's
+    cached health hook reads). A FAIL (code 1) outlives any number of checks that could not finish; only a clean
+    check replaces it."""
+
+    line: str
+    code: int
+    time: float
+
+    NAME = "status.json"
+
+    @classmethod
+    def load(cls, out: str) -> Optional["NodeStatus"]:
+        try:
+            with open(os.path.join(out, cls.NAME)) as f:
+                raw = json.load(f)
+        except (OSError, ValueError):
+            return None
+        if not isinstance(raw, dict):
+            return None
+        return cls(line=str(raw.get("line", "")), code=raw.get("code"), time=raw.get("time"))
+
+    def store(self, out: str) -> None:
+        """Replace the file atomically (a reader never sees half a record); a read-only OUT is not an error."""
+        try:
+            os.makedirs(out, exist_ok=True)
+            fd, tmp = tempfile.mkstemp(dir=out, prefix=".status.")
+            with os.fdopen(fd, "w") as f:
+                json.dump({"time": self.time, "code": self.code, "line": self.line}, f)
+            os.replace(tmp, os.path.join(out, self.NAME))
+        except OSError:
+            pass
+
+    def age_hours(self, now: float) -> Optional[float]:
+        try:
+            h = (now - float(self.time)) / 3600.0
+        except (TypeError, ValueError):
+            return None
+        return h if math.isfinite(h) and h >= 0 else None
+
+    def carry_fail(self, line: str, code: int) -> tuple[str, int]:
+        """What to report when a new check ended with (line, code): an inconclusive result keeps a recorded FAIL."""
+        if code == 2 and self.code == 1:
+            return f"{self.line or 'FAIL'} (a later check: {line})", 1
+        return line, code
+
+    def cached_report(self, max_age_hours: float, now: float, out: str) -> tuple[str, int]:
+        age = self.age_hours(now)
+        if age is None:
+            return f"UNKNOWN: unreadable sdcguard check result in {out}", 2
+        if self.code == 1:
+            return self.line or "FAIL", 1
+        if age > max_age_hours:
+            return f"UNKNOWN: last sdcguard check was {age:.0f} hours ago (limit {max_age_hours:g})", 2
+        return self.line or "OK", self.code if self.code in (0, 2) else 2
 
 
 def write_status(out: str, line: str, code: int) -> None:
-    try:
-        os.makedirs(out, exist_ok=True)
-        tmp = os.path.join(out, "status.json.tmp")
-        with open(tmp, "w") as f:
-            json.dump({"time": time.time(), "code": code, "line": line}, f)
-        os.replace(tmp, os.path.join(out, "status.json"))
-    except OSError:
-        pass
+    NodeStatus(line=line, code=code, time=time.time()).store(out)
 
 
 def cached(out: str, max_age_hours: float) -> tuple[str, int]:
-    st = previous(out)
+    """The cached mode: report the stored status, never run anything."""
+    st = NodeStatus.load(out)
     if st is None:
         return f"UNKNOWN: no readable sdcguard check result in {out} yet", 2
-    try:
-        age_h = (time.time() - float(st.get("time", 0))) / 3600
-        if not math.isfinite(age_h) or age_h < 0:
-            raise ValueError("timestamp")
-    except (TypeError, ValueError):
-        return f"UNKNOWN: unreadable sdcguard check result in {out}", 2
-    if st.get("code") == 1:                 # a failure stays a failure until a clean check
-        return str(st.get("line", "FAIL")), 1
-    if age_h > max_age_hours:
-        return f"UNKNOWN: last sdcguard check was {age_h:.0f} hours ago (limit {max_age_hours:g})", 2
-    code = st.get("code") if st.get("code") in (0, 2) else 2
-    return str(st.get("line", "OK")), code
+    return st.cached_report(max_age_hours, time.time(), out)
 
 
 def judge(devices: list[str], runs: list[dict], limit: float) -> tuple[str, int]:
@@ -144,10 +192,9 @@ def run_nhc(devices: list[str], seconds: float, out: str,
     limit = deadline(seconds) if limit is None else limit
     runs = run_all([command(d, seconds) for d in devices], limit)
     line, code = judge(devices, runs, limit)
-    if code == 2:
-        prev = previous(out)
-        if prev is not None and prev.get("code") == 1:      # a FAIL is cleared only by a clean check
-            line, code = f"{prev.get('line', 'FAIL')} (a later check: {line})", 1
+    prev = NodeStatus.load(out)
+    if prev is not None:
+        line, code = prev.carry_fail(line, code)
     write_status(out, line, code)
     return line, code
 

@@ -26,6 +26,8 @@ from typing import Optional
 
 import torch
 
+from ..utils.events import load_evidence, plain
+
 from ..models.decoder import TINY, DecoderConfig
 from .screen_ops import smi
 
@@ -80,7 +82,7 @@ def run(device="cuda:0", size: str = "small", minutes: float = 2.0, seed: int = 
                 os.makedirs(out_dir, exist_ok=True)
                 path = os.path.join(out_dir, f"evidence_r{r}.pt")
                 torch.save({"size": size, "seed": seed, "round": r, "prompts": prompts, "lens": lens, "new": new,
-                            "tokens_a": a, "tokens_b": b, "events": row["events"], "gpu": rep["gpu"],
+                            "tokens_a": a.cpu(), "tokens_b": b.cpu(), "events": plain(row["events"]), "gpu": plain(rep["gpu"]),
                             "simulated": simulate and r == 0}, path)
                 row["evidence"] = path
         rep["rounds"].append(row)
@@ -105,7 +107,7 @@ def replay(path: str, device="cuda:0") -> dict:
     """Rerun a saved round twice on this device: reproducible (a check alarms or the tokens differ from the saved
     ones again) or not."""
     from ..serve.engine import LLMEngine
-    ev = torch.load(path, weights_only=False)
+    ev = load_evidence(path)
     cfg = SIZES[ev["size"]]
     batch, plen, new = ev["prompts"].shape[0], ev["prompts"].shape[1], ev["new"]
     eng = LLMEngine(cfg, device=device, checked=True, num_blocks=batch * (-(-(plen + new) // 16)) + 8,

@@ -14,8 +14,22 @@ from typing import Optional
 log = logging.getLogger("sdcguard")
 
 
+def load_evidence(path: str) -> dict:
+    """Read an evidence or case file (`.pt`) that may come from another node: tensors land on the CPU (a file saved
+    on cuda:N loads on a host with fewer GPUs) and only plain data is unpickled (tensors, dicts, lists, strings,
+    numbers), so a crafted file cannot run code. Callers move the tensors to their device themselves."""
+    import torch
+    return torch.load(path, map_location="cpu", weights_only=True)
+
+
+def plain(obj):
+    """`obj` as plain JSON-able data (dicts, lists, strings, numbers), for evidence files read by `load_evidence`."""
+    return json.loads(json.dumps(obj, default=str))
+
+
 def device_identity(device=None) -> dict:
-    """Host, rank, and (for a CUDA device) name, UUID, PCI bus id and physical index of the GPU."""
+    """Host, rank, and (for a CUDA device) name, UUID, PCI bus id and physical index of the GPU. The fields follow
+    the reference's identity record (src/sdcguard/events.py:14-41), which names the GPU to pull by UUID and bus."""
     import torch
     info: dict = {"host": socket.gethostname(), "rank": None, "device": None, "gpu_uuid": None}
     try:

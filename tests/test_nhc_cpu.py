@@ -50,3 +50,14 @@ def test_cached_mode(tmp_path):
     st["time"] -= 48 * 3600
     json.dump(st, open(os.path.join(out, "status.json"), "w"))
     assert nhc.cached(out, 24) == ("FAIL: bad", 1)                    # a FAIL is reported at any age
+
+
+def test_chatty_checks_do_not_block_each_other(tmp_path):
+    """Two checks that each write far more than a pipe buffer of log: both finish, neither is reported hung."""
+    res = {"gemm_checks": 3, "gemm_wrong": 0, "copies_wrong": 0, "worst_z": 0.01}
+    body = (f"import json, sys; sys.stderr.write('x' * (1 << 20)); sys.stderr.flush(); "
+            f"print('y' * (1 << 19)); print(json.dumps({res!r}))")
+    t0 = time.time()
+    line, code = nhc.run_nhc(["cuda:0", "cuda:1"], 1, str(tmp_path / "nhc"),
+                             command=lambda d, s: [sys.executable, "-c", body], limit=20.0)
+    assert code == 0 and line.startswith("OK: 2 GPUs") and time.time() - t0 < 15
