@@ -76,7 +76,7 @@ def evaluate(files: dict) -> dict:
             for k, want in d.items():
                 if k in v and not ev.same(v[k], want):
                     reasons.append("derived_observation_disagrees:" + k)
-            if not obs._planned_scope_matches(plans[0], v.get("proof", {})):
+            if not obs.plan_matches_proof(plans[0], v.get("proof", {})):
                 reasons.append("planned_chunk_scope_disagrees_with_verification")
             proof = v.get("proof", {})
             if proof.get("num_tokens") != n:

@@ -78,7 +78,7 @@ def transfer_scope(plans, records, *, prompt_tokens, local_tokens, remote_tokens
             or type(proof.get("plan_sequence")) is not int or proof["plan_sequence"] != pid
             or not plan.get("request_id") or plan.get("request_id") != rec.get("request_id")):
         R.append("receive_plan_to_verification_join_unverified")
-    if not observer._planned_scope_matches(plan, proof):
+    if not observer.plan_matches_proof(plan, proof):
         R.append("planned_chunk_scope_disagrees_with_verification")
     if (type(load.get("num_tokens")) is not int or load["num_tokens"] != prompt_tokens
             or type(load.get("num_local_computed_tokens")) is not int or load["num_local_computed_tokens"] != local_tokens):
