@@ -13,6 +13,8 @@
 // CTAs/SMs at a different time and compared bit for bit (sdcguard_b200/ops/attention.py). The reference checks
 // attention by a sampled fp32 recompute against an error bound (src/sdcguard/serve_attn.py:5-48, kernels
 // `_attn_part` :335 and `_attn_judge` :414); an exact replay needs no bound and sees every flipped bit.
+#include <cstdlib>
+
 #include "common.cuh"
 #include "tma_host.h"
 
@@ -418,6 +420,360 @@ __global__ void __launch_bounds__(128 + 2 * ROWS, 1) prefill_tc_kernel(const __g
   }
 }
 
+// ---------------------------------------------------------------------------------------------- prefill, ping-pong
+// Two query tiles per CTA that share their key / value tiles (consecutive tiles of one request, so they attend to
+// the same keys), so the tensor pipe always has one tile's MMAs to run while the other tile's softmax runs:
+//   warp 0      TMA: K and V pages of each 128-key tile into one of two stages (shared by both query tiles);
+//   warp 1      MMA, in the order PV0(j-1), S0(j), PV1(j-1), S1(j) for key tile j: S_x = Q_x K_j^T into TMEM,
+//               O_x += P_x V_{j-1} with P_x read from TMEM (the A operand of a tcgen05 MMA may live in tensor
+//               memory), so P never goes through shared memory;
+//   warps 4-7   softmax of query tile 0, warps 8-11 of query tile 1: one thread per row owns the row's whole key
+//               tile (no exchange between threads): masked maximum, conditional rescale of O (only when the
+//               reference maximum moves by more than 2^8), P = exp2(S - max) rounded to bf16 and written back
+//               over the first 64 columns of S_x, the row sum of those bf16 weights; at the end O / l.
+// TMEM: S_0, S_1, O_0, O_1 (128 columns each). S_x(j + 1) overwrites P_x(j) only after PV_x(j) in the MMA order
+// (tcgen05 MMAs of one thread run in issue order), and the commit that signals S_x(j) also covers PV_x(j - 1), so
+// the softmax may rescale O_x as soon as it sees S_x(j). Every decision is per row and key tiles start at absolute
+// multiples of 128, so rows are reproduced bit for bit whatever tile (or pair) they are computed in.
+namespace pp {
+constexpr int KT = 128;
+constexpr int HALF_B = 128 * 128;
+constexpr int TILE_B = 2 * HALF_B;
+constexpr int OFF_Q = 0, OFF_K = 2 * TILE_B, OFF_V = 4 * TILE_B, OFF_CTL = 6 * TILE_B;
+constexpr float RESCALE_LOG2 = 8.f;
+constexpr int PG_BYTES = PAGE * D * 2;
+struct Ctl {
+  uint64_t k_full[2], v_full[2], kv_empty[2];
+  uint64_t s_full[2], p_full[2], o_done[2];   // per query tile
+  uint64_t q_ready, drain;
+  uint32_t tmem_base;
+  int abort_flag;
+  int maxpos[2];
+  int tok[2][ROWS];
+  int pos[2][ROWS];
+};
+constexpr int SMEM = OFF_CTL + static_cast<int>(sizeof(Ctl)) + 1024;
+constexpr int THREADS = 128 + 2 * ROWS;   // warpgroup 0: warp 0 TMA, warp 1 TMEM + MMA; warpgroups 1, 2: softmax
+constexpr int P_COL = 64;                 // P_x lives in columns [64, 128) of S_x (bf16 pairs)
+}  // namespace pp
+
+__global__ void __launch_bounds__(pp::THREADS, 1) prefill_pp_kernel(const __grid_constant__ CUtensorMap tm,
+                                                                    const PrefillParams p) {
+  pdl_trigger();
+  using namespace pp;
+  extern __shared__ uint8_t pp_raw[];
+  uint8_t* sm = pp_raw + ((1024 - (smem_u32(pp_raw) & 1023)) & 1023);
+  Ctl* ctl = reinterpret_cast<Ctl*>(sm + OFF_CTL);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int G = p.nq / p.nkv;
+  const int tpc = ROWS / G;
+  const int kvh = blockIdx.y;
+  const int4 t0 = p.tiles[2 * blockIdx.x], t1 = p.tiles[2 * blockIdx.x + 1];
+  const int req = t0.x;
+  if (tid == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&ctl->k_full[i], 1);
+      mbar_init(&ctl->v_full[i], 1);
+      mbar_init(&ctl->kv_empty[i], 1);
+      mbar_init(&ctl->s_full[i], 1);
+      mbar_init(&ctl->p_full[i], ROWS);
+      mbar_init(&ctl->o_done[i], 1);
+      ctl->maxpos[i] = -1;
+    }
+    mbar_init(&ctl->q_ready, 2 * ROWS);
+    mbar_init(&ctl->drain, 1);
+    ctl->abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&ctl->tmem_base, 512);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) tma_prefetch_desc(&tm);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  // softmax thread: query tile x = warp / 4 - 1, row = TMEM lane it may access = (warp % 4) * 32 + lane
+  if (warp >= 4) {
+    const int x = (warp >> 2) - 1, r = (warp & 3) * 32 + lane;
+    const int4 tl = x ? t1 : t0;
+    const int ti = r / G;
+    int tok = -1;
+    if (tl.x == req && ti < tl.z && ti < tpc) tok = tl.w >= 0 ? p.row_idx[tl.w + ti] : tl.y + ti;
+    ctl->tok[x][r] = tok;
+    const int ps = tok >= 0 ? p.pos[tok] : -1;
+    ctl->pos[x][r] = ps;
+    if (ps >= 0) atomicMax(&ctl->maxpos[x], ps);
+  }
+  __syncthreads();
+  const int nt0 = ctl->maxpos[0] >= 0 ? ctl->maxpos[0] / KT + 1 : 0;
+  const int nt1 = ctl->maxpos[1] >= 0 ? ctl->maxpos[1] / KT + 1 : 0;
+  const int ntiles = max(nt0, nt1);
+  const int maxpos = max(ctl->maxpos[0], ctl->maxpos[1]);
+  const uint32_t tmem = ctl->tmem_base;
+  volatile int* abort_flag = &ctl->abort_flag;
+  const int* bt = p.block_table + static_cast<long long>(req) * p.max_pages;
+
+  if (warp == 0 && ntiles > 0) {
+    // ------------------------------------------------------------ TMA producer (all 32 lanes issue)
+    bool ok = true;
+    int last = -1;
+    for (int j = 0; j < ntiles && ok; ++j) {
+      const int st = j & 1;
+      bool got = true;
+      if (lane == 0) got = mbar_wait(&ctl->kv_empty[st], ((j >> 1) & 1u) ^ 1u, abort_flag);
+      if (!__shfl_sync(0xffffffffu, got ? 1 : 0, 0)) {
+        ok = false;
+        break;
+      }
+      const int npg = min(KT / PAGE, maxpos / PAGE - j * (KT / PAGE) + 1);
+      uint8_t* kbuf = sm + OFF_K + st * TILE_B;
+      uint8_t* vbuf = sm + OFF_V + st * TILE_B;
+      if (npg < KT / PAGE) {
+        // the weights of keys past the last page are zero, but stale shared memory could hold NaN patterns
+        for (int i = lane; i < (KT - npg * PAGE) * 16; i += 32) {
+          const int rr = npg * PAGE + (i >> 4), c = i & 15;
+          *reinterpret_cast<uint4*>(vbuf + (c >> 3) * HALF_B + rr * 128 + (c & 7) * 16) = make_uint4(0, 0, 0, 0);
+        }
+        fence_proxy_async_smem();
+      }
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&ctl->k_full[st], npg * PG_BYTES);
+        mbar_arrive_expect_tx(&ctl->v_full[st], npg * PG_BYTES);
+      }
+      __syncwarp();
+      if (lane < 4 * npg) {
+        const int pg = lane >> 2, kv = (lane >> 1) & 1, half = lane & 1;
+        const long long blk = bt[j * (KT / PAGE) + pg];
+        const int row = static_cast<int>(((blk * 2 + kv) * p.nkv + kvh) * PAGE);
+        uint8_t* dst = (kv ? vbuf : kbuf) + half * HALF_B + pg * PAGE * 128;
+        tma_load_2d(dst, &tm, kv ? &ctl->v_full[st] : &ctl->k_full[st], half * 64, row);
+      }
+      last = j;
+    }
+    if (!ok && lane == 0) {
+      *abort_flag = 1;
+      for (int j = last > 0 ? last - 1 : 0; j <= last; ++j) {
+        mbar_wait(&ctl->k_full[j & 1], (j >> 1) & 1u, nullptr);
+        mbar_wait(&ctl->v_full[j & 1], (j >> 1) & 1u, nullptr);
+      }
+    }
+  } else if (warp == 1 && ntiles > 0) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      bool ok = mbar_wait(&ctl->q_ready, 0, abort_flag);
+      const uint32_t idesc_s = idesc_bf16_f32(128, KT);
+      const uint32_t idesc_o = idesc_bf16_f32(128, D) | (1u << 16);     // B (V) MN-major
+      const int nt[2] = {nt0, nt1};
+      for (int j = 0; j <= ntiles && ok; ++j) {
+        if (j < ntiles) {
+          ok = mbar_wait(&ctl->k_full[j & 1], (j >> 1) & 1u, abort_flag);
+          if (!ok) break;
+        }
+        if (j >= 1) {
+          ok = mbar_wait(&ctl->v_full[(j - 1) & 1], ((j - 1) >> 1) & 1u, abort_flag);
+          if (!ok) break;
+        }
+        tc_fence_after();
+        for (int x = 0; x < 2 && ok; ++x) {
+          const uint32_t s_col = tmem + x * KT, o_col = tmem + 2 * KT + x * D;
+          if (j >= 1 && j - 1 < nt[x]) {
+            // O_x += P_x(j-1) V(j-1): P_x in columns [64, 128) of S_x (bf16 pairs), 8 columns per K = 16 step
+            ok = mbar_wait(&ctl->p_full[x], (j - 1) & 1u, abort_flag);
+            if (!ok) break;
+            tc_fence_after();
+            const uint32_t va = smem_u32(sm + OFF_V + ((j - 1) & 1) * TILE_B);
+#pragma unroll
+            for (int ks = 0; ks < KT / 16; ++ks) {
+              const uint64_t bd = umma_desc_sw128_mn(va + ks * 2048, HALF_B, 1024);
+              umma_f16_tmem_a(o_col, s_col + P_COL + ks * 8, bd, idesc_o, (j - 1 > 0 || ks > 0) ? 1u : 0u);
+            }
+            if (j - 1 == nt[x] - 1) umma_commit(&ctl->o_done[x]);
+          }
+          if (j < nt[x]) {
+            const uint32_t qa = smem_u32(sm + OFF_Q + x * TILE_B);
+            const uint32_t ka = smem_u32(sm + OFF_K + (j & 1) * TILE_B);
+#pragma unroll
+            for (int ks = 0; ks < D / 16; ++ks) {
+              const uint32_t off = (ks >> 2) * HALF_B + (ks & 3) * 32;
+              umma_f16(s_col, umma_desc_sw128(qa + off), umma_desc_sw128(ka + off), idesc_s, ks ? 1u : 0u);
+            }
+            umma_commit(&ctl->s_full[x]);
+          }
+        }
+        if (ok && j >= 1) umma_commit(&ctl->kv_empty[(j - 1) & 1]);
+      }
+      if (!ok) {
+        record_error(nullptr, ERR_TIMEOUT_MMA);
+        *abort_flag = 1;
+        umma_commit(&ctl->drain);
+        mbar_wait(&ctl->drain, 0, nullptr);
+      }
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ softmax / output: thread = one row of tile x
+    const int x = (warp >> 2) - 1;
+    const int r = (warp & 3) * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const int tok = ctl->tok[x][r];
+    const int pos = ctl->pos[x][r];
+    const int head = kvh * G + (r % G);
+    const int my_tiles = x ? nt1 : nt0;
+    {
+      // Q row -> shared memory (128-byte swizzle, dims halves in separate 16 KB halves of the tile)
+      uint8_t* qd = sm + OFF_Q + x * TILE_B;
+      const uint4* src = reinterpret_cast<const uint4*>(p.q + (static_cast<long long>(tok < 0 ? 0 : tok) * p.nq + head) * D);
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        const uint4 v = tok >= 0 ? src[c] : make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(qd + (c >> 3) * HALF_B + r * 128 + (((c & 7) ^ (r & 7)) << 4)) = v;
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&ctl->q_ready);
+    }
+    const uint32_t s_col = tmem + x * KT + lane_off, o_col = tmem + 2 * KT + x * D + lane_off;
+    float m_use = -INFINITY, l = 0.f;
+    bool stop = my_tiles == 0;
+    for (int j = 0; j < my_tiles; ++j) {
+      if (!mbar_wait(&ctl->s_full[x], j & 1u, abort_flag)) {
+        *abort_flag = 1;
+        stop = true;
+      }
+      if (__any_sync(0xffffffffu, stop)) {
+        stop = true;
+        break;
+      }
+      tc_fence_after();
+      const int kbase = j * KT;
+      // S row of this key tile in two 64-column halves: the maximum over both (the second half stays in registers),
+      // then the weights of the second half, then the first half again. P (bf16 pairs) goes to columns [64, 128):
+      // the weights of keys [64, 128) over columns [96, 128) and those of keys [0, 64) over [64, 96), each written
+      // only after the S values under it were read.
+      const int lim = pos - kbase;      // keys [0, lim] of this tile are visible to the row
+      uint32_t v[2][32];
+      float mx = -INFINITY;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        tmem_ld32(s_col + h * 64, v[0]);
+        tmem_ld32(s_col + h * 64 + 32, v[1]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (h * 64 + c * 32 + i <= lim) mx = fmaxf(mx, u32_as_f32(v[c][i]));
+        }
+      }
+      mx *= p.scale_log2;                // scale > 0: the maximum commutes with it
+      float alpha = 1.f;
+      if (mx > -INFINITY && (m_use == -INFINITY || mx > m_use + RESCALE_LOG2)) {
+        alpha = m_use == -INFINITY ? 1.f : ex2(m_use - mx);
+        l *= alpha;
+        m_use = mx;
+      }
+      if (__any_sync(0xffffffffu, alpha != 1.f)) {
+        // PV_x(j-1) is complete (the commit of S_x(j) covers it): rescale this row of O_x
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tmem_ld32(o_col + c * 32, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(u32_as_f32(o[i]) * alpha);
+          tmem_st32(o_col + c * 32, o);
+        }
+      }
+      const bool live = m_use > -INFINITY;
+      float ls = 0.f;
+#pragma unroll
+      for (int h = 1; h >= 0; --h) {
+        if (h == 0) {
+          tmem_ld32(s_col, v[0]);
+          tmem_ld32(s_col + 32, v[1]);
+          tmem_wait_ld();
+        }
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            const int key = h * 64 + c * 32 + i;
+            const float p0 = (key <= lim && live) ? ex2(u32_as_f32(v[c][i]) * p.scale_log2 - m_use) : 0.f;
+            const float p1 = (key + 1 <= lim && live) ? ex2(u32_as_f32(v[c][i + 1]) * p.scale_log2 - m_use) : 0.f;
+            const uint32_t w = pack_bf16x2(p0, p1);
+            pk[i >> 1] = w;
+            const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w));
+            ls += f.x + f.y;
+          }
+          tmem_st16(s_col + P_COL + h * 32 + c * 16, pk);
+        }
+      }
+      l += ls;
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&ctl->p_full[x]);
+    }
+    if (!stop && my_tiles > 0) {
+      if (!mbar_wait(&ctl->o_done[x], 0, abort_flag)) {
+        *abort_flag = 1;
+        stop = true;
+      }
+      if (__any_sync(0xffffffffu, stop)) stop = true;
+    }
+    if (!stop && my_tiles > 0) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      __nv_bfloat16* orow = p.o + (static_cast<long long>(tok < 0 ? 0 : tok) * p.nq + head) * D;
+      float sq = 0.f;
+      int bad = -1;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld32(o_col + c * 32, v);
+        tmem_wait_ld();
+        uint32_t w[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          w[i] = pack_bf16x2(u32_as_f32(v[2 * i]) * inv, u32_as_f32(v[2 * i + 1]) * inv);
+          const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+          sq = fmaf(f.x, f.x, fmaf(f.y, f.y, sq));
+        }
+        if (tok >= 0) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const uint4 nv = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+            if (p.check == nullptr) {
+              dst[i] = nv;
+            } else if (bad < 0) {
+              const uint4 ov = dst[i];
+              const uint32_t a[4] = {nv.x, nv.y, nv.z, nv.w}, b[4] = {ov.x, ov.y, ov.z, ov.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int dd = bf16x2_diff(a[e], b[e]);
+                if (bad < 0 && dd >= 0) bad = c * 32 + i * 8 + e * 2 + dd;
+              }
+            }
+          }
+        }
+      }
+      if (tok >= 0) {
+        if (p.check != nullptr && bad >= 0)
+          report_replay_mismatch(p.check, static_cast<unsigned long long>(tok) * p.nq * D + head * D + bad);
+        if (p.check == nullptr && p.row_sq != nullptr) atomicAdd(p.row_sq + tok, sq);
+      }
+    }
+    if (p.check != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && r == 0 && x == 0) atomicAdd(p.check + 2, 1ull);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 // ---------------------------------------------------------------------------------------------- decode
 // Split-KV decode ("flash decoding"): the keys of each (sequence, kv head) are cut into chunks of SPLIT keys at
 // absolute multiples of SPLIT, and the chunks into segments of SEG chunks. One CTA takes a whole segment: it
@@ -816,10 +1172,23 @@ int sdc_attn_prefill(const void* q, void* o, const void* cache, long long num_bl
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, pf::SMEM);
     if (e != cudaSuccess) return static_cast<int>(e);
+    e = cudaFuncSetAttribute(prefill_pp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, pp::SMEM);
+    if (e != cudaSuccess) return static_cast<int>(e);
     attr = true;
   }
-  dim3 grid(ntiles, nkv);
-  prefill_tc_kernel<<<grid, 128 + pf::SOFT, pf::SMEM, static_cast<cudaStream_t>(stream)>>>(tm, p);
+  static const bool pingpong = [] {
+    const char* v = std::getenv("SDCGUARD_PREFILL_PINGPONG");
+    return v == nullptr || v[0] != '0';
+  }();
+  if (pingpong) {
+    // tiles come in pairs of one request (entries 2i and 2i + 1; an odd count is padded by the caller)
+    if (ntiles % 2) return -3;
+    dim3 grid(ntiles / 2, nkv);
+    prefill_pp_kernel<<<grid, pp::THREADS, pp::SMEM, static_cast<cudaStream_t>(stream)>>>(tm, p);
+  } else {
+    dim3 grid(ntiles, nkv);
+    prefill_tc_kernel<<<grid, 128 + pf::SOFT, pf::SMEM, static_cast<cudaStream_t>(stream)>>>(tm, p);
+  }
   return static_cast<int>(cudaGetLastError());
 }
 

@@ -812,20 +812,29 @@ __global__ void __launch_bounds__(Cfg<BN, PAIR>::THREADS, 1)
         } else {
           const int col0 = idx * BN + g * CSW;
           if (col0 < p.N) {
+            // Each thread holds one row of the accumulator; stores straight from registers would touch 32 rows per
+            // warp instruction. A 32 x 32 block at a time goes through this warp's staging tile instead (16-byte
+            // columns XOR-swizzled by row: conflict-free both ways) and leaves as 32 full 128-byte row segments.
+            float* tile32 = reinterpret_cast<float*>(staging + ew * C::STG_BUFS * 4096);
+            const int row0 = band * BM + q * 32;
+            float* part0 = p.part + (static_cast<long long>(ks) * p.M + row0) * pw;
 #pragma unroll 1
-            for (int h = 0; h < CSW / 64; ++h) {
-              uint32_t r[64];
-              tmem_ld32(tacc + static_cast<uint32_t>(g * CSW + h * 64), *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
-              tmem_ld32(tacc + static_cast<uint32_t>(g * CSW + h * 64 + 32), *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+            for (int h = 0; h < CSW / 32; ++h) {
+              uint32_t r[32];
+              tmem_ld32(tacc + static_cast<uint32_t>(g * CSW + h * 32), r);
               tmem_wait_ld();
-              const int cbase = col0 + h * 64;
-              if (row < p.M) {
 #pragma unroll
-                for (int j = 0; j < 64; j += 4)
-                  if (cbase + j < p.N)    // N % 8 == 0: a group of 4 is all in or all out
-                    *reinterpret_cast<float4*>(prow + cbase + j) = make_float4(
-                        u32_as_f32(r[j]), u32_as_f32(r[j + 1]), u32_as_f32(r[j + 2]), u32_as_f32(r[j + 3]));
+              for (int j = 0; j < 8; ++j)
+                *reinterpret_cast<float4*>(tile32 + lane * 32 + ((j ^ (lane & 7)) << 2)) = make_float4(
+                    u32_as_f32(r[4 * j]), u32_as_f32(r[4 * j + 1]), u32_as_f32(r[4 * j + 2]), u32_as_f32(r[4 * j + 3]));
+              __syncwarp();
+              const int c = col0 + h * 32 + lane;
+#pragma unroll 4
+              for (int rr = 0; rr < 32; ++rr) {
+                const float val = tile32[rr * 32 + ((((lane >> 2) ^ rr) & 7) << 2) + (lane & 3)];
+                if (row0 + rr < p.M && c < p.N) part0[static_cast<long long>(rr) * pw + c] = val;
               }
+              __syncwarp();
             }
           }
         }

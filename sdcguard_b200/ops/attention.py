@@ -22,28 +22,46 @@ def _s(t: torch.Tensor) -> int:
     return torch.cuda.current_stream(t.device).cuda_stream
 
 
+def _pairs(per_request: list[list[tuple]]) -> list[tuple]:
+    """Tiles two by two within each request (the prefill kernel runs the two tiles of a pair in one CTA on shared
+    key / value tiles); a request with an odd number of tiles gets an empty partner (0 tokens)."""
+    pairs = []
+    for tiles in per_request:
+        for i in range(0, len(tiles), 2):
+            a = tiles[i]
+            b = tiles[i + 1] if i + 1 < len(tiles) else (a[0], a[1] + a[2], 0, -1)
+            pairs.append((a, b))
+    return pairs
+
+
 def prefill_tiles(q_starts: Sequence[int], q_lens: Sequence[int], group: int) -> torch.Tensor:
-    """(n, 4) int32 tiles (request, first token, tokens, -1) covering every request's new tokens, ordered
-    longest-running first (later tiles of a causal prompt attend to more keys)."""
+    """(2 n, 4) int32 tiles (request, first token, tokens, -1) covering every request's new tokens, as n pairs of
+    consecutive tiles of one request (entries 2i and 2i + 1), pairs ordered by the keys they attend to, most first
+    (later tiles of a causal prompt attend to more keys), so the longest CTAs start first."""
     tpc = ROWS // group
-    tiles = []
-    for r, (s, n) in enumerate(zip(q_starts, q_lens)):
-        for off in range(0, n, tpc):
-            tiles.append((r, s + off, min(tpc, n - off), -1))
-    tiles.sort(key=lambda t: -(t[1]))
-    return torch.tensor(tiles, dtype=torch.int32).view(-1, 4)
+    per = [[(r, s + off, min(tpc, n - off), -1) for off in range(0, n, tpc)] for r, (s, n) in
+           enumerate(zip(q_starts, q_lens))]
+    pairs = _pairs(per)
+    # keys a pair attends to: its last token's position within its request
+    pairs.sort(key=lambda pr: -(pr[0][1] - q_starts[pr[0][0]] + pr[0][2] + pr[1][2]))
+    flat = [t for pr in pairs for t in pr]
+    return torch.tensor(flat, dtype=torch.int32).view(-1, 4)
 
 
 def replay_tiles(sampled: Sequence[Sequence[int]], group: int) -> tuple[torch.Tensor, torch.Tensor]:
-    """Tiles for a replay of sampled tokens: sampled[r] lists request r's sampled token indices."""
+    """Tiles for a replay of sampled tokens (sampled[r] lists request r's sampled token indices), in pairs of one
+    request as `prefill_tiles` makes them; returns (tiles, row_idx)."""
     tpc = ROWS // group
-    tiles, idx = [], []
+    per, idx = [], []
     for r, toks in enumerate(sampled):
+        mine = []
         for off in range(0, len(toks), tpc):
             chunk = list(toks[off:off + tpc])
-            tiles.append((r, 0, len(chunk), len(idx)))
+            mine.append((r, 0, len(chunk), len(idx)))
             idx.extend(chunk)
-    t = torch.tensor(tiles, dtype=torch.int32).view(-1, 4)
+        per.append(mine)
+    flat = [t for pr in _pairs(per) for t in pr]
+    t = torch.tensor(flat, dtype=torch.int32).view(-1, 4)
     return t, torch.tensor(idx, dtype=torch.int32)
 
 
