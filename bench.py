@@ -46,6 +46,11 @@ def parse():
     ap.add_argument("--new-tokens", type=int, default=128)
     ap.add_argument("--no-unchecked", action="store_true", help="skip the unchecked comparison run")
     ap.add_argument("--no-campaign", action="store_true", help="skip the fault-injection campaign")
+    ap.add_argument("--no-tp", action="store_true", help="skip the tensor-parallel block (config 4 at TP = N)")
+    ap.add_argument("--tp-steps", type=int, default=1)
+    ap.add_argument("--tp-batch", type=int, default=64)
+    ap.add_argument("--tp-prompt", type=int, default=2048)
+    ap.add_argument("--tp-new-tokens", type=int, default=256)
     ap.add_argument("--ref-child", choices=["checked", "unchecked"], help=argparse.SUPPRESS)
     ap.add_argument("--ref-rank", default="0", help=argparse.SUPPRESS)
     return ap.parse_args()
@@ -215,7 +220,38 @@ def run_ours(args, rank, world, local):
     if not args.no_campaign:
         from sdcguard_b200.tools import campaign
         res["campaign"] = campaign.quick(seed=rank)
+    if not args.no_tp and world > 1:
+        res["tp"] = run_tp(args, world)
+    elif not args.no_tp:
+        res["tp"] = {"skipped": "TP = 1 is the single-GPU engine of the headline; the block runs from N = 2"}
     return res
+
+
+def run_tp(args, world: int) -> dict:
+    """Config 4 on this job's GPUs: the Llama-3-8B-shaped decoder at TP = N (batch 64, prompt 2048, 256 generated),
+    checked (this library's GEMMs, the reduce-scatter pushed from the row-parallel GEMM's epilogue with seals, the
+    sealed all-gather fused with the shard norm, all over NVLink peer memory) against unchecked (cuBLAS + NCCL),
+    device time max over ranks, plus one profiled short generate() per arm for the collectives' device time."""
+    import argparse as ap
+    from sdcguard_b200.serve import tp_serve
+    targs = ap.Namespace(model="llama3-8b", batch=args.tp_batch, prompt=args.tp_prompt,
+                         new_tokens=args.tp_new_tokens, steps=args.tp_steps, warmup=1, max_prefill_tokens=16384,
+                         arms="checked,unchecked", inject=True, precision="bf16", seed=0, pg_timeout=300,
+                         profile_kernels=True)
+    r = tp_serve.run(targs)
+    c, u = r.get("checked", {}), r.get("unchecked", {})
+    return {"config": r.get("config"), "tp": world,
+            "checked": round(c.get("tokens_per_s", 0.0), 1),
+            "unchecked": round(u.get("tokens_per_s", 0.0), 1), "overhead_pct": r.get("overhead_pct"),
+            "unit": "tokens/s (prompt + generated, whole job; device time max over ranks)",
+            "ms_per_step": {"checked": round(c.get("dev_ms", 0.0), 2), "unchecked": round(u.get("dev_ms", 0.0), 2)},
+            "phase_ms": {"checked": c.get("phase_ms"), "unchecked": u.get("phase_ms")},
+            "checks": c.get("checks"), "unjudged": c.get("unjudged"), "worst_clean_z": c.get("worst_clean_z"),
+            "false_alarms": c.get("false_alarms"),
+            "injected_transfer_flip_detected_on_ranks": c.get("injected_transfer_flip_detected_on_ranks"),
+            "ranks_agree": r.get("ranks_agree"), "same_tokens_checked_vs_unchecked": r.get("same_tokens_checked_vs_unchecked"),
+            "kernels_checked": c.get("kernels"), "kernels_unchecked": u.get("kernels"),
+            "kernel_timing": "torch.profiler CUDA activity, one short generate (prefill + 4 decode steps) per arm"}
 
 
 # ------------------------------------------------------------------------------------------ reference arm
@@ -436,6 +472,8 @@ def main():
                 line["coverage"] = res["coverage"]
                 if "campaign" in res:
                     line["detection"] = res["campaign"]
+                if "tp" in res:
+                    line["tp"] = res["tp"]
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()

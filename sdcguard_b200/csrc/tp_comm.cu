@@ -42,12 +42,31 @@ __device__ __forceinline__ void report(unsigned long long* state, float z, unsig
   atomicMax(state + 1, static_cast<unsigned long long>(__float_as_uint(z)) << 32);
 }
 
-// One warp per (row, 128-column block) of this rank's rows; lane l owns columns 4l..4l+3 of the block.
-// parts: peers' partial outputs [M][N] bf16; seals: peers' seals [M][nb] u32; out: this rank's [R][N].
-// local = true (after a push-mode GEMM): peer r's partial rows are slot r of this rank's own receive buffer
-// (rows [off + r R, off + (r + 1) R) with off = (gen & 1) cap: consecutive pushes alternate between two regions),
-// so every read is local; the sums and checks are the same.
-__global__ void __launch_bounds__(256) rs_pull_kernel(Peers parts, Peers seals, const long long* gen,
+// Work layout of the pull kernels: a grid of at most 148 x 8 CTAs (each waits for the peers' flags once) whose
+// warps stride over (row, 128-column block) items; lane l owns columns 4l..4l+3 of an item's block. NVLink loads
+// have microseconds of latency, so a warp issues all loads of a step before using any of them: every peer's
+// partial of an item (reduce-scatter), or four items (all-gather).
+constexpr int PULL_CTAS = 148 * 8;
+constexpr int AG_UNROLL = 4;
+
+__device__ __forceinline__ uint32_t warp_sum_u32(uint32_t h) {
+#pragma unroll
+  for (int m = 16; m > 0; m >>= 1) h += __shfl_xor_sync(0xffffffffu, h, m);
+  return h;
+}
+__device__ __forceinline__ float warp_sum_f32(float v) {
+#pragma unroll
+  for (int m = 16; m > 0; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
+  return v;
+}
+
+// Reduce-scatter owner side. parts: peers' partial outputs [M][N] bf16; seals: peers' seals [M][nb] u32; out: this
+// rank's rows [R][N]. local = true (after a push-mode GEMM): peer r's partial rows are slot r of this rank's own
+// receive buffer (rows [off + r R, off + (r + 1) R) with off = (gen & 1) cap: consecutive pushes alternate between
+// two regions), so every read is local; the sums and checks are the same. Sums run in rank order in fp32, every
+// peer's bits are checked against its seal, and the block sum of the stored bf16 output is checked against the sum
+// of the inputs' block sums (linearity of the checksum) within the rounding bound.
+__global__ void __launch_bounds__(256) rs_pull_kernel(const __grid_constant__ Peers parts, const __grid_constant__ Peers seals, const long long* gen,
                                                       const long long* my_flags, int world, int rank, int R, int N,
                                                       __nv_bfloat16* __restrict__ out, float tol,
                                                       unsigned long long* state, int* err, bool local,
@@ -56,96 +75,124 @@ __global__ void __launch_bounds__(256) rs_pull_kernel(Peers parts, Peers seals, 
   const long long off = local ? (__ldcg(gen) & 1) * cap : 0;
   const int nb = (N + 127) / 128;
   const int lane = threadIdx.x & 31;
-  const long long wid = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   if (blockIdx.x == 0 && threadIdx.x == 0 && state != nullptr) atomicAdd(state + 2, 1ull);
-  if (wid >= static_cast<long long>(R) * nb) return;
-  const int lr = static_cast<int>(wid / nb), b = static_cast<int>(wid % nb);
-  const long long row = static_cast<long long>(rank) * R + lr;
-  const int col = b * 128 + lane * 4;
-  const bool in = col < N;   // N % 8 == 0: a lane's 4 columns are all in or all out
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  float sum_in = 0.f, abs_in = 0.f;
-  int bad_peer = -1;
-  for (int r = 0; r < world; ++r) {
-    uint2 v = make_uint2(0u, 0u);
-    const long long prow = local ? off + static_cast<long long>(r) * R + lr : row;
-    const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(local ? parts.ptr[rank] : parts.ptr[r]);
-    if (in) v = __ldcg(reinterpret_cast<const uint2*>(src + prow * N + col));
-    uint32_t h = seal_term(v.x, static_cast<uint32_t>(lane * 2)) + seal_term(v.y, static_cast<uint32_t>(lane * 2 + 1));
+  const long long items = static_cast<long long>(R) * nb;
+  const long long nwarps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+  for (long long wid = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; wid < items;
+       wid += nwarps) {
+    const int lr = static_cast<int>(wid / nb), b = static_cast<int>(wid % nb);
+    const long long row = static_cast<long long>(rank) * R + lr;
+    const int col = b * 128 + lane * 4;
+    const bool in = col < N;   // N % 8 == 0: a lane's 4 columns are all in or all out
+    uint2 v[MAXW];
+    uint32_t want[MAXW];
 #pragma unroll
-    for (int m = 16; m > 0; m >>= 1) h += __shfl_xor_sync(0xffffffffu, h, m);
-    const float2 a = bf2(v.x), c = bf2(v.y);
-    acc[0] += a.x;
-    acc[1] += a.y;
-    acc[2] += c.x;
-    acc[3] += c.y;
-    sum_in += (a.x + a.y) + (c.x + c.y);
-    abs_in += (fabsf(a.x) + fabsf(a.y)) + (fabsf(c.x) + fabsf(c.y));
-    if (lane == 0) {
-      const uint32_t want = __ldcg(static_cast<const uint32_t*>(local ? seals.ptr[rank] : seals.ptr[r]) + prow * nb + b);
-      if (want != h && bad_peer < 0) bad_peer = r;
+    for (int r = 0; r < MAXW; ++r) {
+      v[r] = make_uint2(0u, 0u);
+      want[r] = 0u;
+      if (r < world) {
+        const long long prow = local ? off + static_cast<long long>(r) * R + lr : row;
+        const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(local ? parts.ptr[rank] : parts.ptr[r]);
+        if (in) v[r] = __ldcg(reinterpret_cast<const uint2*>(src + prow * N + col));
+        if (lane == 0)
+          want[r] = __ldcg(static_cast<const uint32_t*>(local ? seals.ptr[rank] : seals.ptr[r]) + prow * nb + b);
+      }
     }
-  }
-  uint2 o;
-  {
-    __nv_bfloat162 p0 = __floats2bfloat162_rn(acc[0], acc[1]);
-    __nv_bfloat162 p1 = __floats2bfloat162_rn(acc[2], acc[3]);
-    o.x = *reinterpret_cast<uint32_t*>(&p0);
-    o.y = *reinterpret_cast<uint32_t*>(&p1);
-  }
-  if (in) *reinterpret_cast<uint2*>(out + static_cast<long long>(lr) * N + col) = o;
-  const float2 q0 = bf2(o.x), q1 = bf2(o.y);
-  float sum_out = (q0.x + q0.y) + (q1.x + q1.y);
-  float abs_out = (fabsf(q0.x) + fabsf(q0.y)) + (fabsf(q1.x) + fabsf(q1.y));
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    float sum_in = 0.f, abs_in = 0.f;
+    int bad_peer = -1;
 #pragma unroll
-  for (int m = 16; m > 0; m >>= 1) {
-    sum_in += __shfl_xor_sync(0xffffffffu, sum_in, m);
-    abs_in += __shfl_xor_sync(0xffffffffu, abs_in, m);
-    sum_out += __shfl_xor_sync(0xffffffffu, sum_out, m);
-    abs_out += __shfl_xor_sync(0xffffffffu, abs_out, m);
-  }
-  if (lane == 0) {
-    const unsigned long long flat = static_cast<unsigned long long>(lr) * nb + b;
-    if (bad_peer >= 0) {
-      report(state, __int_as_float(0x7f800000), flat * MAXW + bad_peer);
-    } else {
-      // bf16 rounding of every output (2^-9 relative) and the fp32 adds (world terms per output)
-      const float bound = tol * (abs_out * 0.001953125f + abs_in * world * 5.96e-8f) + 1e-30f;
-      const float z = fabsf(sum_out - sum_in) / bound;
-      if (!(z <= 1.0f)) report(state, z > 3.0e38f || z != z ? __int_as_float(0x7f800000) : z * 6.0f, flat * MAXW);
+    for (int r = 0; r < MAXW; ++r) {
+      if (r >= world) break;
+      const uint32_t h = warp_sum_u32(seal_term(v[r].x, static_cast<uint32_t>(lane * 2)) +
+                                      seal_term(v[r].y, static_cast<uint32_t>(lane * 2 + 1)));
+      const float2 a = bf2(v[r].x), c = bf2(v[r].y);
+      acc[0] += a.x;
+      acc[1] += a.y;
+      acc[2] += c.x;
+      acc[3] += c.y;
+      sum_in += (a.x + a.y) + (c.x + c.y);
+      abs_in += (fabsf(a.x) + fabsf(a.y)) + (fabsf(c.x) + fabsf(c.y));
+      if (lane == 0 && want[r] != h && bad_peer < 0) bad_peer = r;
+    }
+    uint2 o;
+    {
+      __nv_bfloat162 p0 = __floats2bfloat162_rn(acc[0], acc[1]);
+      __nv_bfloat162 p1 = __floats2bfloat162_rn(acc[2], acc[3]);
+      o.x = *reinterpret_cast<uint32_t*>(&p0);
+      o.y = *reinterpret_cast<uint32_t*>(&p1);
+    }
+    if (in) *reinterpret_cast<uint2*>(out + static_cast<long long>(lr) * N + col) = o;
+    const float2 q0 = bf2(o.x), q1 = bf2(o.y);
+    const float sum_out = warp_sum_f32((q0.x + q0.y) + (q1.x + q1.y));
+    const float abs_out = warp_sum_f32((fabsf(q0.x) + fabsf(q0.y)) + (fabsf(q1.x) + fabsf(q1.y)));
+    sum_in = warp_sum_f32(sum_in);
+    abs_in = warp_sum_f32(abs_in);
+    if (lane == 0) {
+      const unsigned long long flat = static_cast<unsigned long long>(lr) * nb + b;
+      if (bad_peer >= 0) {
+        report(state, __int_as_float(0x7f800000), flat * MAXW + bad_peer);
+      } else {
+        // bf16 rounding of every output (2^-9 relative) and the fp32 adds (world terms per output)
+        const float bound = tol * (abs_out * 0.001953125f + abs_in * world * 5.96e-8f) + 1e-30f;
+        const float z = fabsf(sum_out - sum_in) / bound;
+        if (!(z <= 1.0f)) report(state, z > 3.0e38f || z != z ? __int_as_float(0x7f800000) : z * 6.0f, flat * MAXW);
+      }
     }
   }
 }
 
-// One warp per (row, 128-column block) of the full gathered tensor [world * R][N].
-// shards: peers' row shards [R][N]; seals: peers' shard seals [R][nb]; out: full buffer.
-// rss / rs_out (optional): every rank's row_sq of its shard rows, gathered into rs_out [world R] with the rows.
-__global__ void __launch_bounds__(256) ag_pull_kernel(Peers shards, Peers seals, const long long* gen,
+// All-gather: the full gathered tensor [world * R][N] from every rank's row shard [R][N] and its seals [R][nb], each
+// (row, block) checked against its owner's seal. rss / rs_out (optional): every rank's row_sq of its shard rows,
+// gathered into rs_out [world R] with the rows.
+__global__ void __launch_bounds__(256) ag_pull_kernel(const __grid_constant__ Peers shards, const __grid_constant__ Peers seals, const long long* gen,
                                                       const long long* my_flags, int world, int R, int N,
                                                       __nv_bfloat16* __restrict__ out, unsigned long long* state,
-                                                      int* err, Peers rss, float* rs_out) {
+                                                      int* err, const __grid_constant__ Peers rss, float* rs_out) {
   pdl_trigger();   // a dependent GEMM may start its prologue and weight loads now
   if (!wait_all(gen, my_flags, world, err)) return;
   const int nb = (N + 127) / 128;
   const int lane = threadIdx.x & 31;
-  const long long wid = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   if (blockIdx.x == 0 && threadIdx.x == 0 && state != nullptr) atomicAdd(state + 2, 1ull);
-  if (wid >= static_cast<long long>(world) * R * nb) return;
-  const long long grow = wid / nb;
-  const int b = static_cast<int>(wid % nb);
-  const int owner = static_cast<int>(grow / R);
-  const long long lr = grow - static_cast<long long>(owner) * R;
-  const int col = b * 128 + lane * 4;
-  uint2 v = make_uint2(0u, 0u);
-  if (col < N) v = __ldcg(reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(shards.ptr[owner]) + lr * N + col));
-  uint32_t h = seal_term(v.x, static_cast<uint32_t>(lane * 2)) + seal_term(v.y, static_cast<uint32_t>(lane * 2 + 1));
+  const long long items = static_cast<long long>(world) * R * nb;
+  const long long nwarps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+  for (long long w0 = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; w0 < items;
+       w0 += nwarps * AG_UNROLL) {
+    uint2 v[AG_UNROLL];
+    uint32_t want[AG_UNROLL];
+    float rsv[AG_UNROLL];
 #pragma unroll
-  for (int m = 16; m > 0; m >>= 1) h += __shfl_xor_sync(0xffffffffu, h, m);
-  if (col < N) *reinterpret_cast<uint2*>(out + grow * N + col) = v;
-  if (lane == 1 && b == 0 && rs_out != nullptr) rs_out[grow] = __ldcg(static_cast<const float*>(rss.ptr[owner]) + lr);
-  if (lane == 0) {
-    const uint32_t want = __ldcg(static_cast<const uint32_t*>(seals.ptr[owner]) + lr * nb + b);
-    if (want != h) report(state, __int_as_float(0x7f800000), static_cast<unsigned long long>(grow) * nb + b);
+    for (int u = 0; u < AG_UNROLL; ++u) {
+      const long long wid = w0 + u * nwarps;
+      v[u] = make_uint2(0u, 0u);
+      want[u] = 0u;
+      rsv[u] = 0.f;
+      if (wid < items) {
+        const long long grow = wid / nb;
+        const int b = static_cast<int>(wid % nb);
+        const int owner = static_cast<int>(grow / R);
+        const long long lr = grow - static_cast<long long>(owner) * R;
+        const int col = b * 128 + lane * 4;
+        if (col < N)
+          v[u] = __ldcg(reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(shards.ptr[owner]) + lr * N + col));
+        if (lane == 0) want[u] = __ldcg(static_cast<const uint32_t*>(seals.ptr[owner]) + lr * nb + b);
+        if (lane == 1 && b == 0 && rs_out != nullptr) rsv[u] = __ldcg(static_cast<const float*>(rss.ptr[owner]) + lr);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < AG_UNROLL; ++u) {
+      const long long wid = w0 + u * nwarps;
+      if (wid >= items) break;
+      const long long grow = wid / nb;
+      const int b = static_cast<int>(wid % nb);
+      const int col = b * 128 + lane * 4;
+      const uint32_t h = warp_sum_u32(seal_term(v[u].x, static_cast<uint32_t>(lane * 2)) +
+                                      seal_term(v[u].y, static_cast<uint32_t>(lane * 2 + 1)));
+      if (col < N) *reinterpret_cast<uint2*>(out + grow * N + col) = v[u];
+      if (lane == 1 && b == 0 && rs_out != nullptr) rs_out[grow] = rsv[u];
+      if (lane == 0 && want[u] != h)
+        report(state, __int_as_float(0x7f800000), static_cast<unsigned long long>(grow) * nb + b);
+    }
   }
 }
 
@@ -183,6 +230,12 @@ __global__ void __launch_bounds__(256) seal_rows_kernel(const __nv_bfloat16* __r
 
 using namespace sdc::tp;
 
+// CTAs of a pull kernel over `items` warp items: enough for one item per warp, at most PULL_CTAS.
+static unsigned pull_blocks(long long items) {
+  const long long b = (items * 32 + 255) / 256;
+  return static_cast<unsigned>(b < 1 ? 1 : (b > PULL_CTAS ? PULL_CTAS : b));
+}
+
 extern "C" {
 
 using sdc::peer::make_peers;
@@ -198,9 +251,8 @@ int sdc_tp_reduce_scatter(const unsigned long long* part_ptrs, const unsigned lo
                           const void* my_flags, int world, int rank, int R, int N, void* out, float tol, void* state,
                           int* err, void* stream) {
   if (world < 1 || world > MAXW || N % 8) return -1;
-  const long long warps = static_cast<long long>(R) * ((N + 127) / 128);
-  const unsigned blocks = static_cast<unsigned>((warps * 32 + 255) / 256);
-  rs_pull_kernel<<<blocks > 0 ? blocks : 1, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+  const unsigned blocks = pull_blocks(static_cast<long long>(R) * ((N + 127) / 128));
+  rs_pull_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       make_peers(part_ptrs, world), make_peers(seal_ptrs, world), static_cast<const long long*>(gen),
       static_cast<const long long*>(my_flags), world, rank, R, N, static_cast<__nv_bfloat16*>(out), tol,
       static_cast<unsigned long long*>(state), err, false, 0);
@@ -213,9 +265,8 @@ int sdc_tp_reduce_local(const unsigned long long* part_ptrs, const unsigned long
                         const void* my_flags, int world, int rank, int R, int N, long long cap, void* out, float tol,
                         void* state, int* err, void* stream) {
   if (world < 1 || world > MAXW || N % 8) return -1;
-  const long long warps = static_cast<long long>(R) * ((N + 127) / 128);
-  const unsigned blocks = static_cast<unsigned>((warps * 32 + 255) / 256);
-  rs_pull_kernel<<<blocks > 0 ? blocks : 1, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+  const unsigned blocks = pull_blocks(static_cast<long long>(R) * ((N + 127) / 128));
+  rs_pull_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       make_peers(part_ptrs, world), make_peers(seal_ptrs, world), static_cast<const long long*>(gen),
       static_cast<const long long*>(my_flags), world, rank, R, N, static_cast<__nv_bfloat16*>(out), tol,
       static_cast<unsigned long long*>(state), err, true, cap);
@@ -226,11 +277,10 @@ int sdc_tp_all_gather(const unsigned long long* shard_ptrs, const unsigned long 
                       const void* my_flags, int world, int R, int N, void* out, void* state, int* err,
                       const unsigned long long* rss_ptrs, void* rs_out, void* stream) {
   if (world < 1 || world > MAXW || N % 8) return -1;
-  const long long warps = static_cast<long long>(world) * R * ((N + 127) / 128);
-  const unsigned blocks = static_cast<unsigned>((warps * 32 + 255) / 256);
+  const unsigned blocks = pull_blocks(static_cast<long long>(world) * R * ((N + 127) / 128));
   Peers rss{};
   if (rss_ptrs != nullptr) rss = make_peers(rss_ptrs, world);
-  ag_pull_kernel<<<blocks > 0 ? blocks : 1, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+  ag_pull_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       make_peers(shard_ptrs, world), make_peers(seal_ptrs, world), static_cast<const long long*>(gen),
       static_cast<const long long*>(my_flags), world, R, N, static_cast<__nv_bfloat16*>(out),
       static_cast<unsigned long long*>(state), err, rss, rss_ptrs != nullptr ? static_cast<float*>(rs_out) : nullptr);

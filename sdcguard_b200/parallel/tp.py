@@ -194,11 +194,20 @@ def seal_rows(x: torch.Tensor, seals: torch.Tensor) -> torch.Tensor:
 
 
 # ------------------------------------------------------------------------------------------ NCCL baseline
+def _single(group) -> bool:
+    """One rank (or no process group at all): every collective is a local copy."""
+    return not dist.is_initialized() or dist.get_world_size(group) == 1
+
+
 def reduce_scatter_nccl(partial: torch.Tensor, out: torch.Tensor, group=None) -> torch.Tensor:
+    if _single(group):
+        return out.copy_(partial[: out.shape[0]]) if out.data_ptr() != partial.data_ptr() else out
     dist.reduce_scatter_tensor(out, partial, group=group)
     return out
 
 
 def all_gather_nccl(shard: torch.Tensor, out: torch.Tensor, group=None) -> torch.Tensor:
+    if _single(group):
+        return out.copy_(shard[: out.shape[0]]) if out.data_ptr() != shard.data_ptr() else out
     dist.all_gather_into_tensor(out, shard, group=group)
     return out

@@ -57,13 +57,49 @@ def _timed(fn, steps: int, world: int) -> tuple[float, float]:
     return _max(a.elapsed_time(b) / steps, world), _max((t1 - t0) * 1000 / steps, world)
 
 
+# kernels of the collectives (and the GEMMs fused with them) whose device time the profiled pass reports
+COLLECTIVE_KERNELS = ("rs_pull_kernel", "ag_pull_kernel", "reduce_local", "add_rmsnorm_shard", "seal_rows_kernel",
+                      "signal_kernel", "gemm_abft_kernel", "nccl", "nvjet", "cutlass")
+
+
+def kernel_times(eng, prompts, lens, world: int, dev) -> dict:
+    """Mean device time per launch (us, max over ranks) of the collective and GEMM kernels in one profiled short
+    generate() (prefill of the whole batch, 4 decode steps), from the CUDA activity records of torch.profiler.
+    Shares for reading where a step's time goes; the step's throughput is timed separately without the
+    profiler."""
+    from torch.profiler import ProfilerActivity, profile
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        eng.generate(prompts, lens, 5)
+        torch.cuda.synchronize()
+    rows = {}
+    for e in prof.key_averages():
+        t = getattr(e, "device_time_total", 0.0) or 0.0
+        if t > 0 and any(k in e.key for k in COLLECTIVE_KERNELS):
+            name = e.key.split("(")[0].replace("void ", "")[:80]
+            rows[name] = {"launches": e.count, "us_per_launch": t / e.count, "total_us": t}
+    names = sorted(rows)
+    if world > 1:           # every rank reports the same names in the same order (max over ranks)
+        objs = [None] * world
+        dist.all_gather_object(objs, names)
+        names = sorted(set().union(*objs))
+        vals = torch.tensor([[rows.get(n, {}).get("us_per_launch", 0.0), rows.get(n, {}).get("total_us", 0.0)]
+                             for n in names], dtype=torch.float64, device=dev).view(-1, 2)
+        if vals.numel():
+            dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+        return {n: {"launches": rows.get(n, {}).get("launches"), "us_per_launch": round(float(v[0]), 2),
+                    "total_us": round(float(v[1]), 1)} for n, v in zip(names, vals.cpu())}
+    return {n: {"launches": rows[n]["launches"], "us_per_launch": round(rows[n]["us_per_launch"], 2),
+                "total_us": round(rows[n]["total_us"], 1)} for n in names}
+
+
 def run(args) -> dict:
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    if world > 1:
+    if world > 1 and not dist.is_initialized():     # (bench.py calls run() inside its own process group)
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=args.pg_timeout))
     cfg = CONFIGS.get(args.model) or {"llama3-8b": LLAMA3_8B, "tiny": TINY}[args.model]
     g = torch.Generator().manual_seed(args.seed)
@@ -99,12 +135,16 @@ def run(args) -> dict:
         step()
         eng.phase_timing = False
         phases = {k: round(_max(v, world), 2) for k, v in eng.last_phase_ms.items()}
+        if getattr(args, "profile_kernels", False):
+            r_k = kernel_times(eng, prompts, lens, world, dev)
         ev = eng.guard.poll()
         cov = eng.guard.coverage_report()
         outs[arm] = box["out"]
         r = {"dev_ms": dev_ms, "wall_ms": wall_ms, "tokens_per_s": tokens_per_step / (dev_ms / 1e3),
              "e2e_tokens_per_s": tokens_per_step / (wall_ms / 1e3), "gpu_launches": launches,
              "phase_ms": phases}
+        if getattr(args, "profile_kernels", False):
+            r["kernels"] = r_k
         if checked:
             r.update(checks=cov["checks"], unjudged=cov["unjudged"], worst_clean_z=cov["worst_clean_z"],
                      false_alarms=int(_max(len(ev), world)))
@@ -155,6 +195,8 @@ def main(argv=None) -> int:
                     help="checked arm's projections: bf16, or block-scaled fp8 (the unchecked arm stays bf16)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--pg-timeout", type=int, default=300)
+    ap.add_argument("--profile-kernels", action="store_true",
+                    help="also report per-kernel device time of the collectives from one profiled short generate()")
     a = ap.parse_args(argv)
     res = run(a)
     if int(os.environ.get("RANK", "0")) == 0:
