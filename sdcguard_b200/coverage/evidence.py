@@ -5,8 +5,8 @@ no-follow regular-file reads, bounded zip archives, and a lexical node allowance
 Hashes establish local consistency of a recording, not its authenticity.
 
 The bounds and the canonical encoding are an interface shared with the reference's recordings and verdict files
-(src/sdcguard/evidence_io.py:15-49, evidence_json_budget.py:14-118, required_gate.py:26-57), so they are the same
-numbers; the code is this package's own.
+(src/sdcguard/evidence_io.py:15-49, evidence_json_budget.py:14-118, required_gate.py:26-57): recordings valid
+there are valid here, so the limits are the same numbers.
 """
 from __future__ import annotations
 
@@ -15,6 +15,7 @@ import io as _io
 import json
 import math
 import os
+import re
 import stat
 import zipfile
 import zlib
@@ -89,37 +90,48 @@ def digest(data: bytes) -> str:
     return hashlib.sha256(data).hexdigest()
 
 
-def _pairs(pairs):
-    out = {}
-    for k, v in pairs:
-        if k in out:
-            raise ValueError(f"duplicate JSON key: {k}")
-        out[k] = v
-    return out
+def _object_without_duplicates(pairs):
+    """JSON object hook: the keys of one object must be distinct (the first repeated key is named)."""
+    obj = dict(pairs)
+    if len(obj) != len(pairs):
+        seen = set()
+        dup = next(k for k, _ in pairs if k in seen or seen.add(k))
+        raise ValueError(f"duplicate JSON key: {dup}")
+    return obj
 
 
-def _bad_constant(name):
+def _refuse_constant(name):
     raise ValueError(f"non-finite JSON value: {name}")
 
 
+_STRICT = json.JSONDecoder(object_pairs_hook=_object_without_duplicates, parse_constant=_refuse_constant)
+
+
 def parse_json(raw: bytes, *, max_nodes: int = MAX_JSON_NODES):
+    """Strict JSON of at most MAX_FILE_BYTES: UTF-8, no duplicate keys, no NaN/Infinity, bounded depth and node
+    count (the whole document must be one value)."""
     if not isinstance(raw, bytes) or len(raw) > MAX_FILE_BYTES:
         raise EvidenceError("JSON input exceeds the bounded regular-file contract")
     try:
-        value = json.loads(raw.decode("utf-8"), object_pairs_hook=_pairs, parse_constant=_bad_constant)
+        value = _STRICT.decode(raw.decode("utf-8"))
         _check_tree(value, max_nodes)
-        return value
     except (ValueError, UnicodeError, TypeError, RecursionError) as e:
         raise EvidenceError("malformed strict JSON: " + str(e)) from e
+    return value
 
 
 # ------------------------------------------------------------------------------------------ files
+_UNSAFE_PART = re.compile(r"^(|\.|\.\.)$|:")
+
+
 def relative(name) -> list[str]:
-    """Split a safe relative member name (no absolute paths, dot segments, drive letters, NUL or backslash)."""
-    if (not isinstance(name, str) or not name or "\\" in name or "\x00" in name or name.startswith("/")
-            or any(part in ("", ".", "..") or ":" in part for part in name.split("/"))):
+    """The parts of a safe relative member name: a non-empty string of '/'-separated parts, none empty, '.',
+    '..' or holding ':' (a drive letter), and no backslash, NUL or leading '/'."""
+    ok = isinstance(name, str) and name and not name.startswith("/") and "\\" not in name and "\x00" not in name
+    parts = name.split("/") if ok else []
+    if not ok or any(_UNSAFE_PART.search(part) for part in parts):
         raise EvidenceError("unsafe relative evidence path")
-    return name.split("/")
+    return parts
 
 
 def _open_dir(path: Path) -> int:
