@@ -283,6 +283,7 @@ def _child_env(local: int, checked: bool) -> dict:
     env["HF_HUB_OFFLINE"] = "1"
     env["TRANSFORMERS_OFFLINE"] = "1"
     env["VLLM_CACHE_ROOT"] = f"/tmp/sdcguard_ref_vllm_cache_{local}"
+    env["VLLM_HOST_IP"] = "127.0.0.1"          # the engine's own one-process group over loopback
     env["SDCGUARD"] = "1" if checked else "0"
     return env
 

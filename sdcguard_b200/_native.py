@@ -60,6 +60,9 @@ F = c_float
 SIGNATURES: dict[str, tuple] = {
     "sdc_gemm_ws_bytes": (L, [I, I]),
     "sdc_gemm_counter_bytes": (L, []),
+    "sdc_gemm_set_capture": (I, [P]),
+    "sdc_gemm_capture_bytes": (L, []),
+    "sdc_gemm_capture_max_k": (I, []),
     "sdc_gemm_bf16": (I, [P, L, P, P, I, I, I, P, L, P, P, F, P, P, P, P, I, U, U, U, U, F, F, F, F, F, P, I, I, I, I,
                           U, P, P, P]),
     "sdc_row_sqnorm_bf16": (I, [P, L, I, I, P, P]),
@@ -102,6 +105,7 @@ SIGNATURES: dict[str, tuple] = {
     "sdc_enable_peer_access": (I, [I]),
     "sdc_kv_page_checksums": (I, [P, L, L, I, P, I, ctypes.c_ulonglong, P, P]),
     "sdc_kv_pull_pages": (I, [P, L, P, L, L, I, P, P, I, ctypes.c_ulonglong, P, P, P, P, P]),
+    "sdc_spot_check": (I, [P, L, P, P, L, P, I, I, P, I, P, I, F, F, P, P]),
 }
 
 
@@ -139,7 +143,7 @@ def lib():
             fn.restype = res
             fn.argtypes = args
             if not (name.endswith("_bytes") or name.endswith("_splits") or "_symm_" in name or "_ipc_" in name
-                    or name.endswith("_peer_access")):
+                    or name.endswith("_peer_access") or "_capture" in name):
                 setattr(wrapped, name, _Counted(fn))
         _lib = wrapped
         return _lib

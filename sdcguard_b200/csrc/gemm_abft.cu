@@ -26,6 +26,7 @@
 //     bits), checks executed, checksums left unjudged (layout of src/sdcguard/serve.py:55-65).
 //     The wait cannot deadlock: a tile only waits for tiles earlier in the order, and every CTA of the
 //     persistent grid is resident.
+#include <cstddef>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -69,6 +70,8 @@ struct PeerMaps {
 
 struct Params {
   int M, N, K;
+  const __nv_bfloat16* a;    // A (for the alarm capture: the row of an alarming block is copied from here)
+  long long lda;
   int nb;          // checksum blocks = ceil(N / 128)
   int n_main;      // output tiles per band = ceil(N / BN)
   int n_cs;        // checksum tiles per band
@@ -187,6 +190,53 @@ __device__ __forceinline__ unsigned long long ld_relaxed_gpu_u64(const unsigned 
   return v;
 }
 
+// ------------------------------------------------------------------------------------------------ alarm capture
+// The first alarm of a device (any checked GEMM launch, until the host clears the record) leaves its evidence in a
+// device buffer: where (state slot, row, block), its scores and the sums it was judged on, and the input row of A.
+// The host rechecks it in float64 against the layer's weights (sdcguard_b200.ops.gemm.read_capture). Only an
+// alarm runs this code; a launch with no alarm is unchanged. The buffer is set per device by
+// sdc_gemm_set_capture (null: no capture).
+constexpr int CAPTURE_MAX_K = 16384;
+struct CaptureBuf {
+  int flag;                  // 0 free, 2 being written, 1 complete
+  int slot, row, block, k, which;
+  unsigned long long state_row;   // address of the launch's state row (which table and slot alarmed)
+  float z, den, P, S, ep, es, Q, Aab, rsq, pad[3];
+  __nv_bfloat16 x[CAPTURE_MAX_K];
+};
+static_assert(offsetof(CaptureBuf, x) == 80, "capture header layout (read by ops/gemm.py)");
+static __device__ CaptureBuf* g_capture = nullptr;
+
+// (scalars by value: taking the address of the kernel's parameter block would copy it to local memory)
+__device__ __noinline__ void capture_alarm(const __nv_bfloat16* a, long long lda, int M, int K,
+                                           const unsigned long long* state_row, int slot, int row, int b, int which,
+                                           float z, float den, float P, float S, float ep, float es, float Q, float Aab,
+                                           float rsq) {
+  CaptureBuf* c = g_capture;
+  if (c == nullptr || a == nullptr || K > CAPTURE_MAX_K || row >= M) return;
+  if (atomicCAS(&c->flag, 0, 2) != 0) return;
+  c->state_row = reinterpret_cast<unsigned long long>(state_row);
+  c->slot = slot;
+  c->row = row;
+  c->block = b;
+  c->k = K;
+  c->which = which;
+  c->z = z;
+  c->den = den;
+  c->P = P;
+  c->S = S;
+  c->ep = ep;
+  c->es = es;
+  c->Q = Q;
+  c->Aab = Aab;
+  c->rsq = rsq;
+  const uint4* src = reinterpret_cast<const uint4*>(a + static_cast<long long>(row) * lda);
+  uint4* dst = reinterpret_cast<uint4*>(c->x);
+  for (int i = 0; i < K / 8; ++i) dst[i] = __ldcg(src + i);
+  __threadfence();
+  atomicExch(&c->flag, 1);
+}
+
 // Judges one (row, 128-column block) pair: P, S, Q, Aab are the plain, signed, squared and absolute sums of the
 // fp32 accumulator block (bias included), ex the expected plain / signed sums from the checksum rows. Noise
 // model of the fp32 accumulation (c1, c2, c3 folded into prod_coef and out_coef). Sets the state keys
@@ -227,6 +277,9 @@ __device__ __forceinline__ void judge_pair_loaded(const Params& p, int row, int 
     const unsigned long long zb = static_cast<unsigned long long>(__float_as_uint(z)) << 32;
     k0 = zb | ((static_cast<unsigned long long>(o) * 2ull + which) & 0xffffffffull);
     k1 = zb | __float_as_uint(den);
+    if (!(z <= p.zthr))
+      capture_alarm(p.a, p.lda, p.M, p.K, p.state + static_cast<long long>(p.slot) * 4, p.slot, row, b, which, z, den,
+                    P, S, ep, es, Q, Aab, rsq);
   } else {
     unj = 1;
   }
@@ -1154,6 +1207,14 @@ static bool split_eligible(int M, int N) { return (M + BM - 1) / BM <= 2 && N <=
 // CTA-pair clusters of the 256-wide pair kernel that can be resident at once (0: pair mode unavailable).
 int sdc_gemm_pair_clusters() { return pair_max_clusters(); }
 
+// Sets the alarm-capture record of the current device (a device buffer of sdc_gemm_capture_bytes(), zeroed by the
+// caller), or disables capture with null. Call outside stream capture, before the launches it should cover.
+int sdc_gemm_set_capture(void* buf) {
+  return static_cast<int>(cudaMemcpyToSymbol(g_capture, &buf, sizeof(buf)));
+}
+long long sdc_gemm_capture_bytes() { return static_cast<long long>(sizeof(CaptureBuf)); }
+int sdc_gemm_capture_max_k() { return CAPTURE_MAX_K; }
+
 // Bytes at the start of a workspace that hold the band counters. They return to zero at the end of every
 // launch that completes; after a launch whose wait ran out (error word set) the caller zeroes them again.
 long long sdc_gemm_counter_bytes() { return COUNTER_BYTES; }
@@ -1190,6 +1251,8 @@ static int gemm_run(const void* A, long long lda, const void* W, const void* Wc,
   p.M = M;
   p.N = N;
   p.K = K;
+  p.a = static_cast<const __nv_bfloat16*>(A);
+  p.lda = lda;
   p.nb = nb;
   p.csb = (bn == 256) ? Cfg<256>::CSB : Cfg<128>::CSB;
   p.n_main = (N + bn - 1) / bn;

@@ -26,7 +26,7 @@ from typing import Optional
 
 import torch
 
-from ..ops import attention, gemm, layers
+from ..ops import attention, spot, gemm, layers
 
 
 @dataclass(frozen=True)
@@ -98,7 +98,7 @@ class CheckedDecoder:
 
     def __init__(self, cfg: DecoderConfig, device="cuda", checked: bool = True, seed: int = 0,
                  weights: Optional[dict] = None, tp_rank: int = 0, tp_size: int = 1, moe_layers: Optional[list] = None,
-                 precision: str = "bf16"):
+                 precision: str = "bf16", settings=None):
         """moe_layers: one `models.moe.MoELayer` per layer in place of the dense MLP (expert-parallel models).
         precision "fp8": the four projections of every layer run on the block-scaled fp8 checked GEMM (activations
         quantized per call with 1 x 128 scales, replay-checked on the sampled rows); the LM head stays bf16."""
@@ -107,6 +107,8 @@ class CheckedDecoder:
         if precision == "fp8" and not checked:
             raise ValueError("the fp8 path is the checked fp8 GEMM")
         self.precision = precision
+        from ..serve.settings import CheckSettings
+        self.settings = settings if settings is not None else CheckSettings.from_env()
         self._side = torch.cuda.Stream(torch.device(device)) if checked and torch.cuda.is_available() else None
         self.cfg = cfg
         self.moe = moe_layers
@@ -140,11 +142,16 @@ class CheckedDecoder:
         if precision == "fp8":
             from ..ops.fp8 import Fp8Linears
             self.fp8 = Fp8Linears(dev)
+        self.spot_schedules: dict = {}
+        self._spot_turn = 0
+        self.slot_weights: dict = {}       # state slot -> CheckedWeight (the float64 recheck of a captured alarm)
         if checked:
             for i, lw in enumerate(self.layers):
-                for name in ("qkv", "o", "gate_up", "down"):
+                for p_i, name in enumerate(("qkv", "o", "gate_up", "down")):
                     if getattr(lw, name) is None:
                         continue
+                    if precision == "bf16" and not self.settings.gemm_checked(i, p_i):
+                        continue       # outside this replica's share: runs unchecked on the library GEMM
                     if precision == "fp8":
                         fw = self.fp8.add(f"L{i}.{name}", getattr(lw, name))
                         self.slot[f"L{i}.{name}"] = self.state.add(f"layers.{i}.{name} (ABFT fp8 GEMM)", fw.nb)
@@ -153,10 +160,16 @@ class CheckedDecoder:
                     cw = gemm.CheckedWeight(getattr(lw, name))
                     lw.cw[name] = cw
                     self.slot[f"L{i}.{name}"] = self.state.add(f"layers.{i}.{name} (ABFT GEMM)", cw.nb)
+                    self.slot_weights[self.slot[f"L{i}.{name}"]] = cw
+                    if self.settings.spot:
+                        self.slot[f"L{i}.{name}.spot"] = self.state.add(f"layers.{i}.{name} (spot check)",
+                                                                         getattr(lw, name).shape[0], "rowblock")
+                        self.spot_schedules[f"L{i}.{name}"] = spot.SpotSchedule(getattr(lw, name).shape[0])
                 for name in ("norm1", "rope_kv", "attn", "norm2", "act"):
                     self.slot[f"L{i}.{name}"] = self.state.add(f"layers.{i}.{name} (replay)", 1)
             self.lm_cw = gemm.CheckedWeight(self.lm_head)
             self.slot["lm_head"] = self.state.add("lm_head (ABFT GEMM)", self.lm_cw.nb)
+            self.slot_weights[self.slot["lm_head"]] = self.lm_cw
             self.slot["final_norm"] = self.state.add("final_norm (replay)", 1)
         if moe_layers:
             for i, m in enumerate(moe_layers):
@@ -227,7 +240,7 @@ class CheckedDecoder:
         if self.precision == "fp8":
             return self.fp8.linear(name, x, self.state.state, self.slot[name], out,
                                    qcheck=self.state.state[self.slot[name + ".q"]], sample=sample)
-        if not self.checked:
+        if not self.checked or (self.precision == "bf16" and name not in self.slot):
             return torch.matmul(x, w.t(), out=out)
         inj = None
         if getattr(self, "_inject", None) and self._inject[0] == name and \
@@ -237,6 +250,19 @@ class CheckedDecoder:
 
     def _st(self, name) -> torch.Tensor:
         return self.state.state[self.slot[name]]
+
+    def _next_spot_target(self, lo: int, hi: int):
+        """The projection the spot check recomputes in this step: the registered ones take turns."""
+        names = [n for n in self.spot_schedules if lo <= int(n[1:].split(".")[0]) < hi]
+        if not names:
+            return None
+        self._spot_turn += 1
+        return names[self._spot_turn % len(names)]
+
+    def _spot(self, name: str, x: torch.Tensor, w: torch.Tensor, y: torch.Tensor, T: int) -> None:
+        sched = self.spot_schedules[name]
+        rows, cols = sched.sample(T, self._spot_turn // max(1, len(self.spot_schedules)), self.device)
+        spot.spot_check(x, w, y, rows, cols, self._st(name + ".spot"))
 
     def forward(self, meta: StepMeta, cache: torch.Tensor, layer_range: Optional[tuple] = None,
                 hidden: Optional[tuple] = None, last: bool = True):
@@ -258,13 +284,16 @@ class CheckedDecoder:
             resid.copy_(hidden[1])
         S = meta.sample_rows
         chk = self.checked and S is not None and S.numel() > 0
+        st = self.settings
+        spot_on = self.checked and st.spot and meta.mode == "prefill" and self.precision == "bf16" and T > 0
+        spot_target = self._next_spot_target(lo, hi) if spot_on else None
         nq, nkv, D = self.nq, self.nkv, cfg.head_dim
         # Replay checks write nothing the forward reads, so they run on a side stream next to the main chain (filling
         # SMs the small decode kernels leave idle) and rejoin before the buffers they compare are overwritten: the
         # norm-1 / rope / attention replays before norm 2 of the same layer, the norm-2 / SwiGLU replays before the
         # next layer's norm 1.
         main = torch.cuda.current_stream(self.device)
-        side = self._side_stream() if chk else None
+        side = self._side_stream() if (chk or spot_target is not None) else None
         forked = [False]      # joined only after a fork: under graph capture the side stream must be in the capture
 
         def replay(fn):
@@ -289,44 +318,52 @@ class CheckedDecoder:
                 layers.add_rmsnorm(x, lw.ln1, cfg.rms_eps, residual=None, resid_out=resid, out=y, row_sq=rs)
             else:
                 layers.add_rmsnorm(x, lw.ln1, cfg.rms_eps, residual=resid, resid_out=resid, out=y, row_sq=rs)
-            if chk:
+            if chk and st.norms:
                 replay(lambda: layers.add_rmsnorm(resid, lw.ln1, cfg.rms_eps, out=y, rows=S,
                                                   check=self._st(f"L{i}.norm1")))
             self._linear(y, lw.qkv, lw.cw.get("qkv"), f"L{i}.qkv", qkv, rs, S)
+            if spot_target == f"L{i}.qkv":
+                replay(lambda: self._spot(f"L{i}.qkv", y, lw.qkv, qkv, T))
             layers.qk_norm_rope_kv(qkv, nq, nkv, meta.pos, meta.slots, lw.q_norm, lw.k_norm, cfg.rms_eps, self.rope,
                                    q, lc)
-            if chk:
+            if chk and st.rope:
                 replay(lambda: layers.qk_norm_rope_kv(qkv, nq, nkv, meta.pos, meta.slots, lw.q_norm, lw.k_norm,
                                                       cfg.rms_eps, self.rope, q, lc, rows=S,
                                                       check=self._st(f"L{i}.rope_kv")))
             ors.zero_()
             if meta.mode == "prefill":
                 attention.prefill(q, lc, meta.block_table, meta.pos, meta.tiles, nq, nkv, out=att, row_sq=ors)
-                if chk:
+                if chk and st.attn:
                     replay(lambda: attention.prefill(q, lc, meta.block_table, meta.pos, meta.sample_tiles, nq, nkv,
                                                      out=att, row_idx=meta.sample_idx, check=self._st(f"L{i}.attn")))
             else:
                 scratch = self.decode_scratch(T, meta.max_ctx)
                 attention.decode(q, lc, meta.block_table, meta.seq_req, meta.ctx, nq, nkv, meta.max_ctx, out=att,
                                  row_sq=ors, scratch=scratch)
-                if chk:
+                if chk and st.attn:
                     replay(lambda: attention.decode(q, lc, meta.block_table, meta.seq_req, meta.ctx, nq, nkv,
                                                     meta.max_ctx, out=att, seq_idx=S, scratch=scratch,
                                                     check=self._st(f"L{i}.attn")))
             self._linear(att.view(T, nq * D), lw.o, lw.cw.get("o"), f"L{i}.o", a, ors, S)
+            if spot_target == f"L{i}.o":
+                replay(lambda: self._spot(f"L{i}.o", att.view(T, nq * D), lw.o, a, T))
             join()
             layers.add_rmsnorm(a, lw.ln2, cfg.rms_eps, residual=resid, resid_out=resid, out=y, row_sq=rs)
-            if chk:
+            if chk and st.norms:
                 replay(lambda: layers.add_rmsnorm(resid, lw.ln2, cfg.rms_eps, out=y, rows=S,
                                                   check=self._st(f"L{i}.norm2")))
             if self.moe:
                 x = self.moe[i].forward(y, S if chk else None)
                 continue
             self._linear(y, lw.gate_up, lw.cw.get("gate_up"), f"L{i}.gate_up", gu, rs, S)
+            if spot_target == f"L{i}.gate_up":
+                replay(lambda: self._spot(f"L{i}.gate_up", y, lw.gate_up, gu, T))
             layers.silu_mul(gu, out=act, row_sq=rs)
-            if chk:
+            if chk and st.act:
                 replay(lambda: layers.silu_mul(gu, out=act, rows=S, check=self._st(f"L{i}.act")))
             self._linear(act, lw.down, lw.cw.get("down"), f"L{i}.down", x, rs, S)
+            if spot_target == f"L{i}.down":
+                replay(lambda: self._spot(f"L{i}.down", act, lw.down, x, T))
         join()
         if not last:
             return x, resid

@@ -74,6 +74,89 @@ def take_errors(device: torch.device) -> int:
     return code
 
 
+_CAP: dict = {}          # device index -> capture record (uint8)
+_CAP_HEADER = 80         # bytes before the captured row: 6 int32, the state row's address, 12 float32
+
+
+def enable_capture(device: torch.device) -> torch.Tensor:
+    """Give the checked GEMMs of `device` an alarm-capture record (once per device; call before any CUDA graph is
+    captured). The first alarm of any checked GEMM afterwards leaves its evidence there until `read_capture`."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    buf = _CAP.get(idx)
+    if buf is None:
+        lib = _native.lib()
+        buf = torch.zeros(int(lib.sdc_gemm_capture_bytes()), dtype=torch.uint8, device=torch.device("cuda", idx))
+        with torch.cuda.device(idx):
+            _native.check(lib.sdc_gemm_set_capture(buf.data_ptr()), "gemm capture")
+        _CAP[idx] = buf
+    return buf
+
+
+def read_capture(device: torch.device, clear: bool = True) -> Optional[dict]:
+    """The captured alarm of `device` (one device-to-host copy), or None: the state slot, row and block that
+    alarmed, its score, noise, the accumulator's plain / signed / squared / absolute block sums, the expected
+    sums, and the input row (bf16, on the CPU). clear: free the record for the next alarm."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    buf = _CAP.get(idx)
+    if buf is None:
+        return None
+    head = buf[:_CAP_HEADER].cpu()
+    ints = head.view(torch.int32)[:6].tolist()
+    if ints[0] != 1:
+        return None
+    state_row = int(head[24:32].view(torch.int64)[0]) & 0xFFFFFFFFFFFFFFFF
+    f = head.view(torch.float32)[8:20].tolist()
+    k = ints[4]
+    x = buf[_CAP_HEADER:_CAP_HEADER + 2 * k].cpu().view(torch.bfloat16).clone()
+    if clear:
+        buf[:_CAP_HEADER].zero_()
+    return {"state_row": state_row, "slot": ints[1], "row": ints[2], "block": ints[3], "k": k,
+            "signed": bool(ints[5]), "z": f[0],
+            "noise": f[1], "actual_plain": f[2], "actual_signed": f[3], "expected_plain": f[4],
+            "expected_signed": f[5], "sum_sq": f[6], "sum_abs": f[7], "row_sq": f[8], "x_row": x}
+
+
+def recheck_capture(cap: dict, cw: "CheckedWeight") -> dict:
+    """Float64 recheck of a captured alarm against the layer's weights (as they are now) and the checksum rows
+    built when the layer was registered. Verdicts:
+      weights_changed  the current weights' block sums no longer match the registered checksum rows
+      output_wrong     the accumulator's block sums are off the exact product, the expected sums are right
+      expected_wrong   the expected sums (checksum tiles) are off the exact product, the accumulator is right
+      both_wrong       both are off
+      not_reproduced   both agree with the exact product within the noise the alarm was judged with"""
+    b = cap["block"]
+    c0, c1 = b * abft.BLOCK, min((b + 1) * abft.BLOCK, cw.n)
+    x = cap["x_row"].double().to(cw.weight.device)
+    w = cw.weight[c0:c1].double()
+    signs = abft.sign_vector(cw.mask, device=w.device)[: c1 - c0]
+    vals = w @ x
+    if cw.bias is not None:
+        vals = vals + cw.bias[c0:c1].double()
+    exact = (float(vals.sum()), float((vals * signs).sum()))
+    # what the registered checksum rows say the block sums are (three bf16 parts per sum)
+    parts = cw.cs.wc[b * abft.CS_ROWS:(b + 1) * abft.CS_ROWS].double() @ x
+    reg = (float(parts[:3].sum()), float(parts[3:].sum()))
+    if cw.cs.bsum is not None:
+        reg = (reg[0] + float(cw.cs.bsum[b, 0]), reg[1] + float(cw.cs.bsum[b, 1]))
+    noise = max(cap["noise"], abft.ABS_FLOOR)
+    line = abft.Z_ALARM * noise
+    act = (cap["actual_plain"], cap["actual_signed"])
+    exp = (cap["expected_plain"], cap["expected_signed"])
+    off = lambda a, e: any(abs(u - v) > line for u, v in zip(a, e))     # noqa: E731
+    if off(reg, exact):
+        verdict = "weights_changed"
+    elif off(act, exact) and off(exp, exact):
+        verdict = "both_wrong"
+    elif off(act, exact):
+        verdict = "output_wrong"
+    elif off(exp, exact):
+        verdict = "expected_wrong"
+    else:
+        verdict = "not_reproduced"
+    return {"verdict": verdict, "exact": exact, "registered_checksums": reg, "actual": act, "expected": exp,
+            "line": line}
+
+
 def reserve_workspace(device: torch.device, m: int, n: int) -> None:
     workspace(device, int(_native.lib().sdc_gemm_ws_bytes(m, n)))
 
@@ -111,9 +194,36 @@ class StateTable:
         return len(self.names) - 1
 
     def read(self, reset: bool = False) -> list[dict]:
+        """Every row now (one device-to-host copy, which waits for the stream), decoded; reset zeroes the table."""
         rows = self.state[: len(self.names)].cpu().tolist()
         if reset:
             self.state.zero_()
+        return self.decode(rows)
+
+    def slot_of(self, state_row_address: int) -> Optional[int]:
+        """The slot whose row is at this device address, or None when the row belongs to another table."""
+        base = self.state.data_ptr()
+        off = state_row_address - base
+        row_bytes = abft.STATE_COLS * 8
+        if off < 0 or off % row_bytes or off // row_bytes >= len(self.names):
+            return None
+        return off // row_bytes
+
+    def read_async(self, reset: bool = True) -> "PendingRead":
+        """Start a read that never waits: on the current stream, the rows are copied to a device snapshot (and the
+        table zeroed when reset), the snapshot to pinned host memory, and an event is recorded. The returned read
+        is decoded once its event has completed (`PendingRead.result`)."""
+        n = len(self.names)
+        snap = self.state[:n].clone()
+        if reset:
+            self.state.zero_()
+        host = torch.empty(snap.shape, dtype=snap.dtype, pin_memory=True)
+        host.copy_(snap, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(self.device))
+        return PendingRead(self, host, ev, snap)
+
+    def decode(self, rows) -> list[dict]:
         out = []
         for i, r in enumerate(rows):
             d = abft.decode_state_row(r)
@@ -128,6 +238,24 @@ class StateTable:
                 d["row"], d["block"], d["signed"] = abft.locate(d["flat"], self.nbs[i])
             out.append(d)
         return out
+
+
+class PendingRead:
+    """A state-table read in flight (see StateTable.read_async)."""
+
+    def __init__(self, table: "StateTable", host: torch.Tensor, event, snap: torch.Tensor):
+        self.table, self.host, self.event, self._snap = table, host, event, snap
+
+    def ready(self) -> bool:
+        return self.event.query()
+
+    def result(self, wait: bool = False):
+        """The decoded rows, or None while the copy is still in flight (wait=True blocks until it lands)."""
+        if not wait and not self.event.query():
+            return None
+        self.event.synchronize()
+        self._snap = None
+        return self.table.decode(self.host.tolist())
 
 
 class CheckedWeight:

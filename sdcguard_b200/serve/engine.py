@@ -56,6 +56,13 @@ class LLMEngine:
                  max_model_len: int = 4096, precision: str = "bf16", cache: Optional[torch.Tensor] = None):
         self.cfg = cfg
         self.device = torch.device(device)
+        # a checked engine trusts this library's kernels on this device only after they reproduced their
+        # references on clean and corrupted cases (once per device and process)
+        self.verification = None
+        if checked and self.device.type == "cuda":
+            from ..ops import gemm, verify
+            self.verification = verify.verified(self.device)
+            gemm.enable_capture(self.device)      # the first alarm's evidence is kept on the device
         self.model = model or CheckedDecoder(cfg, self.device, checked=checked, seed=seed, precision=precision)
         self.checked = self.model.checked
         self.max_prefill_tokens = max_prefill_tokens
@@ -75,7 +82,8 @@ class LLMEngine:
             self.cache = torch.zeros(cfg.layers, num_blocks, 2, self.model.nkv, PAGE, cfg.head_dim,
                                      dtype=torch.bfloat16, device=self.device)
         self.alloc = BlockAllocator(num_blocks)
-        self.guard = ServeGuard(self.model)
+        settings = getattr(self.model, "settings", None)
+        self.guard = ServeGuard(self.model, z_alarm=settings.z_alarm if settings is not None else 6.0)
         # every activation buffer and the GEMM workspace are sized once, before any CUDA graph is captured
         self.model.buffers(max(max_prefill_tokens, max_num_seqs))
         self.max_model_len = -(-max_model_len // 256) * 256

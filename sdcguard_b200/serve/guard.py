@@ -12,6 +12,8 @@ from __future__ import annotations
 import math
 from typing import Callable, Optional
 
+import torch
+
 
 from ..numerics import abft
 from ..utils.events import EventLog, SDCEvent, device_identity
@@ -29,6 +31,7 @@ class ServeGuard:
         self._identity = None
         self.weight_scan = None
         self.scan_budget_mb = 0.0
+        self.captures: list[dict] = []       # captured alarms with their float64 rechecks
 
     def mark_step(self, step: int) -> None:
         self.step = step
@@ -38,9 +41,80 @@ class ServeGuard:
         self.weight_scan = scan
         self.scan_budget_mb = budget_mb
 
-    def poll(self, reset: bool = True) -> list[SDCEvent]:
-        """Read every state row (one device->host copy), record events for alarms, reset the rows."""
-        rows = self.model.state.read(reset=reset)
+    def poll(self, reset: bool = True, wait: bool = True) -> list[SDCEvent]:
+        """Read the state rows, record events for alarms, reset the rows.
+
+        wait=True: read everything up to now (one device-to-host copy that waits for the stream), together with any
+        read still in flight. wait=False never waits for the GPU: it turns the results of the previous poll's read
+        into events if that read has landed, and starts the next read (a device snapshot and a pinned-memory copy
+        ordered after the work queued so far). Results therefore arrive one poll late, as in the reference's
+        poll (src/sdcguard/serve.py:1090-1129)."""
+        events: list[SDCEvent] = []
+        pending = getattr(self, "_pending", None)
+        if pending is not None and (wait or pending.ready()):
+            events += self._fold(pending.result(wait=True))
+            self._pending = pending = None
+        if wait:
+            events += self._fold(self.model.state.read(reset=reset))
+            events += self._runtime_errors()
+            self._attach_capture(events)
+        elif pending is None:
+            self._pending = self.model.state.read_async(reset=reset)
+        if self.weight_scan is not None:
+            for ev in self.weight_scan.poll(self.scan_budget_mb, step=self.step):
+                self.log.add(ev)
+                events.append(ev)
+                if self.on_alert:
+                    self.on_alert(ev)
+        return events
+
+    def _attach_capture(self, events: list[SDCEvent]) -> None:
+        """The device's captured alarm (the first GEMM alarm since the last read: its input row, its block sums,
+        the sums it was judged against) goes into the detail of the checksum event of the same layer, with the
+        float64 recheck against the layer's weights (weights changed / output wrong / expected side wrong /
+        not reproduced)."""
+        from ..ops import gemm
+        dev = getattr(self.model, "device", None)
+        if dev is None or torch.device(dev).type != "cuda":
+            return
+        cap = gemm.read_capture(torch.device(dev))
+        if cap is None:
+            return
+        slot = self.model.state.slot_of(cap["state_row"])
+        if slot is None:       # an alarm of another table's GEMM (another model or tool on this device)
+            return
+        cw = getattr(self.model, "slot_weights", {}).get(slot)
+        rec = gemm.recheck_capture(cap, cw) if cw is not None and cw.k == cap["k"] else None
+        name = self.model.state.names[slot]
+        kept = {k: v for k, v in cap.items() if k != "x_row"}
+        for ev in events:
+            if ev.detector == "checksum" and ev.detail.get("layer") == name:
+                ev.detail["captured"] = kept
+                ev.detail["recheck"] = rec
+                self.captures.append({"layer": name, "captured": kept, "recheck": rec, "x_row": cap["x_row"]})
+                return
+        self.captures.append({"layer": name, "captured": kept, "recheck": rec, "x_row": cap["x_row"]})
+
+    def _runtime_errors(self) -> list[SDCEvent]:
+        """A kernel whose bounded wait ran out (its error word is set): reported as an event of its own, and the
+        GEMM band counters it may have left raised are cleared (ops.gemm.take_errors)."""
+        from ..ops import gemm
+        dev = getattr(self.model, "device", None)
+        if dev is None or torch.device(dev).type != "cuda":
+            return []
+        code = gemm.take_errors(torch.device(dev))
+        if not code:
+            return []
+        if self._identity is None:
+            self._identity = device_identity(dev)
+        ev = SDCEvent(detector="runtime", step=self.step,
+                      detail={"error_code": code, "what": gemm.ERROR_NAMES.get(code, "unknown")}, identity=self._identity)
+        self.log.add(ev)
+        if self.on_alert:
+            self.on_alert(ev)
+        return [ev]
+
+    def _fold(self, rows) -> list[SDCEvent]:
         events = []
         for r in rows:
             t = self.totals.setdefault(r["name"], {"checks": 0, "unjudged": 0, "worst_z": 0.0, "alarms": 0})
@@ -53,17 +127,12 @@ class ServeGuard:
                 t["alarms"] += 1
                 if self._identity is None:
                     self._identity = device_identity(self.model.device)
-                det = "checksum" if "GEMM" in r["name"] else "collective" if "collective" in r["name"] else "replay"
+                det = ("checksum" if "GEMM" in r["name"] else "collective" if "collective" in r["name"]
+                       else "spot" if "spot" in r["name"] else "replay")
                 detail = {"layer": r["name"], "z": z, "noise": r["noise"], "flat": r["flat"]}
                 if "row" in r:
                     detail.update({k: r[k] for k in ("row", "block", "signed", "peer") if k in r})
                 ev = SDCEvent(detector=det, step=self.step, detail=detail, identity=self._identity)
-                self.log.add(ev)
-                events.append(ev)
-                if self.on_alert:
-                    self.on_alert(ev)
-        if self.weight_scan is not None:
-            for ev in self.weight_scan.poll(self.scan_budget_mb, step=self.step):
                 self.log.add(ev)
                 events.append(ev)
                 if self.on_alert:

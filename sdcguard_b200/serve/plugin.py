@@ -10,15 +10,17 @@ Here the engine is this package's own, so the hooks are explicit:
     hooks.report()                             # coverage, alarms, attributed requests
 
   * weights_loaded: runs once at registration (builds the weight scan, collects the stack identity);
-  * after_step(kind, rows_to_requests): counts steps, polls the guard every `poll_every` steps (one device->host
-    read), attributes each alarm's row to the request it belongs to;
+  * after_step(kind, rows_to_requests): counts steps and polls the guard every `poll_every` steps without waiting
+    for the GPU (the results of a poll's read are turned into alerts at the next poll), or waiting when
+    `poll_seconds` have passed since the last read; attributes each alarm's row to the request it belongs to;
   * require: refuse to serve a model whose GEMMs are not checked (the SDCGUARD_REQUIRE rule).
-Environment: SDCGUARD_POLL_EVERY (default 16), SDCGUARD_REQUIRE (1: require), SDCGUARD_SCAN_MB (weight scan budget
-per poll, default 0 = off).
+Environment: SDCGUARD_POLL_EVERY (default 16), SDCGUARD_POLL_SECONDS (default 2), SDCGUARD_REQUIRE (1: require),
+SDCGUARD_SCAN_MB (weight scan budget per poll, default 0 = off).
 """
 from __future__ import annotations
 
 import os
+import time
 from typing import Callable, Optional
 
 from ..utils import stack as stack_mod
@@ -30,10 +32,14 @@ class UncheckedServingRefused(RuntimeError):
 
 
 class PluginHooks:
-    def __init__(self, engine, poll_every: int = 16, on_alert: Optional[Callable[[SDCEvent], None]] = None):
+    def __init__(self, engine, poll_every: int = 16, on_alert: Optional[Callable[[SDCEvent], None]] = None,
+                 poll_seconds: float = 2.0):
         self.engine = engine
         self.guard = engine.guard
         self.poll_every = max(1, poll_every)
+        self.poll_seconds = poll_seconds
+        self._last_poll = time.monotonic()
+        self._inflight_rows: list[tuple[str, list[int]]] = []   # rows of the steps the pending read covers
         self.on_alert = on_alert
         self.steps = 0
         self.polls = 0
@@ -61,23 +67,29 @@ class PluginHooks:
         self._rows.append((kind, list(rows_to_requests)))
         for h in self.step_hooks:
             h(kind, self.steps)
-        if self.steps % self.poll_every == 0:
-            self.poll()
+        late = time.monotonic() - self._last_poll >= self.poll_seconds
+        if self.steps % self.poll_every == 0 or late:
+            self.poll(wait=late)
 
-    def poll(self) -> list[SDCEvent]:
+    def poll(self, wait: bool = True) -> list[SDCEvent]:
+        """wait=False: alerts from the previous poll's read if it has landed, and a new read started (never waits
+        for the GPU); wait=True: everything up to now."""
         self.polls += 1
-        events = self.guard.poll()
+        self._last_poll = time.monotonic()
+        events = self.guard.poll(wait=wait)
+        windows = self._inflight_rows + self._rows
         for ev in events:
             req = None
             row = ev.detail.get("row")
             if row is not None:
-                for _, mapping in reversed(self._rows):
+                for _, mapping in reversed(windows):
                     if 0 <= row < len(mapping):
                         req = mapping[row]
                         break
             self.alerts.append({"detector": ev.detector, "step": ev.step, "detail": ev.detail, "request": req})
             if self.on_alert:
                 self.on_alert(ev)
+        self._inflight_rows = [] if wait else list(self._rows)
         self._rows.clear()
         return events
 
@@ -89,11 +101,12 @@ class PluginHooks:
 def register(engine, poll_every: Optional[int] = None, require: Optional[bool] = None,
              on_alert: Optional[Callable[[SDCEvent], None]] = None, scan_mb: Optional[float] = None) -> PluginHooks:
     poll_every = int(os.environ.get("SDCGUARD_POLL_EVERY", "16")) if poll_every is None else poll_every
+    poll_seconds = float(os.environ.get("SDCGUARD_POLL_SECONDS", "2"))
     require = os.environ.get("SDCGUARD_REQUIRE", "0") == "1" if require is None else require
     scan_mb = float(os.environ.get("SDCGUARD_SCAN_MB", "0")) if scan_mb is None else scan_mb
     if require and not getattr(engine.model, "checked", False):
         raise UncheckedServingRefused("SDCGUARD_REQUIRE is set and the model's GEMMs are not checked")
-    hooks = PluginHooks(engine, poll_every, on_alert)
+    hooks = PluginHooks(engine, poll_every, on_alert, poll_seconds)
     hooks.weights_loaded(scan_mb)
     engine.hooks = hooks
     return hooks

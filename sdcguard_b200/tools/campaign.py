@@ -8,6 +8,12 @@ Targets:
     `below_noise`: the arithmetic identity cannot see them, and neither can any other tolerance check.
   * replay_rows: one bit of a stored output row that the replay sample covers (norm, activation, attention).
     The exact comparison sees every such flip.
+  * spot_sampled_outputs: one bit of one stored GEMM output that the spot check samples, judged against that
+    output's own bound (catches changes below its block's ABFT noise).
+
+GEMM flips are also split by whether they change the stored bf16 output: a flip in a low fp32 mantissa bit that
+the rounding to bf16 erases changes nothing any reader sees (`output_unchanged`), while `output_changing` counts
+the flips a consumer of the layer would receive.
 
 The reference's equivalent is its FaultInjector plus harm study (src/sdcguard/inject.py:198,
 experiments/harm_study.py); its rounded-output check caught 47.9% of single-bit flips in bf16 outputs on the
@@ -52,13 +58,17 @@ def quick(seed: int = 0, trials: int = 96, device="cuda") -> dict:
     ref = (x.float() @ w.float().t())
     by_class: dict = {}
     below_noise = {"flips": 0, "caught": 0}
-    slots = []
+    clean_out = out.clone()
+    slots, stored = [], []
     for t in range(trials):
         row, col, bit = rng.randrange(m), rng.randrange(n), rng.randrange(32)
         s = st.add(f"inj{t}", cw.nb)
         gemm.checked_linear(x, cw, st.state, s, row_sq=rs, out=out, inject=(row, col, 1 << bit))
+        stored.append(out[row, col].clone())        # the flipped element as the layer stored it
         slots.append((s, row, col, bit))
     torch.cuda.synchronize()
+    changed = [bool((v.view(torch.int16) != clean_out[r, c].view(torch.int16)).item())
+               for v, (_, r, c, _) in zip(stored, slots)]
     rows = st.read()
     clean = rows[clean_slot]
     # noise scale of each block, to classify flips that are below it
@@ -67,7 +77,10 @@ def quick(seed: int = 0, trials: int = 96, device="cuda") -> dict:
     wmax = cw.cs.wstat[:, :3].amax(1).cpu()
     blocks = ref.view(m, cw.nb, 128)
     cn = blocks.pow(2).sum(-1).sqrt().cpu()
-    for (s, row, col, bit) in slots:
+    visible = {"flips": 0, "caught": 0}              # flips that change the stored bf16 output
+    visible_hi = {"flips": 0, "caught": 0}           # ... among bits >= 16 (the bf16 part of the accumulator)
+    invisible = {"flips": 0, "caught": 0}            # flips the rounding to bf16 erases (no stored value changes)
+    for (s, row, col, bit), ch in zip(slots, changed):
         r = rows[s]
         caught = r["z"] > abft.Z_ALARM and r.get("row") == row and r.get("block") == col // 128
         v = float(ref[row, col])
@@ -86,10 +99,42 @@ def quick(seed: int = 0, trials: int = 96, device="cuda") -> dict:
         else:
             below_noise["flips"] += 1
             below_noise["caught"] += int(caught)
+        for bucket, member in ((visible, ch), (visible_hi, ch and bit >= 16), (invisible, not ch)):
+            if member:
+                bucket["flips"] += 1
+                bucket["caught"] += int(caught)
     tot = sum(c["flips"] for c in by_class.values())
     cau = sum(c["caught"] for c in by_class.values())
     above = sum(c["above_noise"] for c in by_class.values())
     cabove = sum(c["caught_above_noise"] for c in by_class.values())
+
+    # spot targets: one bit of one stored output that the spot check samples (bf16 bits: 0-6 mantissa, 7-14
+    # exponent, 15 sign), judged against that output's own bound; and the clean samples for false alarms
+    from ..ops import spot as spot_ops
+    sched = spot_ops.SpotSchedule(n)
+    sst = torch.zeros(2 * trials + 1, abft.STATE_COLS, dtype=torch.int64, device=dev)
+    spot_rows_all = []
+    for t in range(trials):
+        rows_t, cols_t = sched.sample(m, t, dev)
+        rr, cc = sched.rows(m, t), sched.columns(t)
+        row, col, bit = rr[rng.randrange(len(rr))], cc[rng.randrange(len(cc))], rng.randrange(16)
+        yy = clean_out.clone()
+        yy.view(torch.int16)[row, col] ^= (1 << bit) if bit < 15 else -(1 << 15)
+        spot_ops.spot_check(x, w, yy, rows_t, cols_t, sst[t])
+        spot_ops.spot_check(x, w, clean_out, rows_t, cols_t, sst[trials + t])
+        spot_rows_all.append((row, col, bit))
+    torch.cuda.synchronize()
+    sp = sst.cpu().tolist()
+    spot_by = {}
+    for t, (row, col, bit) in enumerate(spot_rows_all):
+        d = abft.decode_state_row(sp[t])
+        hit = d["z"] > abft.Z_ALARM and d["flat"] == row * n + col
+        cls = "sign" if bit == 15 else ("exponent" if bit >= 7 else "mantissa")
+        c = spot_by.setdefault(cls, {"flips": 0, "caught": 0})
+        c["flips"] += 1
+        c["caught"] += int(hit)
+    spot_false = sum(1 for t in range(trials) if abft.decode_state_row(sp[trials + t])["z"] > abft.Z_ALARM)
+    spot_caught = sum(c["caught"] for c in spot_by.values())
 
     # replay targets: flip one bit of a sampled row of a norm output and of an activation output
     hid = torch.randn(256, 1024, device=dev).bfloat16()
@@ -116,10 +161,16 @@ def quick(seed: int = 0, trials: int = 96, device="cuda") -> dict:
                              "above_noise": above, "caught_above_noise": cabove,
                              "rate_above_noise": round(cabove / max(1, above), 4),
                              "below_noise": below_noise, "by_bit_class": by_class,
+                             "output_changing": dict(visible, rate=round(visible["caught"] / max(1, visible["flips"]), 4)),
+                             "output_changing_bits_16_31": dict(
+                                 visible_hi, rate=round(visible_hi["caught"] / max(1, visible_hi["flips"]), 4)),
+                             "output_unchanged": invisible,
                              "clean_checks": 16, "clean_worst_z": round(clean["z"], 4),
                              "false_alarms": int(clean["z"] > abft.Z_ALARM)},
         "replay_rows": {"flips": rep_n, "caught": rep_caught, "rate": round(rep_caught / max(1, rep_n), 4),
                         "false_alarms": int(clean_rep[0, 0].item() != 0)},
+        "spot_sampled_outputs": {"flips": trials, "caught": spot_caught, "rate": round(spot_caught / max(1, trials), 4),
+                                 "by_bit_class": spot_by, "clean_checks": trials, "false_alarms": spot_false},
     }
 
 
@@ -148,3 +199,7 @@ def main(argv=None) -> int:
     ok = g["caught_above_noise"] == g["above_noise"] and not g["false_alarms"] and r["caught"] == r["flips"] \
         and not r["false_alarms"]
     return 0 if ok else 1
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

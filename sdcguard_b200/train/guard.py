@@ -143,6 +143,9 @@ class SDCGuard:
         self.modules: list[CheckedLinear] = []
 
     def protect(self, model: torch.nn.Module) -> torch.nn.Module:
+        if self.device.type == "cuda":
+            from ..ops import verify
+            self.verification = verify.verified(self.device)   # the kernels reproduced their references here
         for pname, parent in list(model.named_modules()):
             for cname, child in list(parent.named_children()):
                 if isinstance(child, torch.nn.Linear):
