@@ -13,29 +13,60 @@ from __future__ import annotations
 
 import argparse
 import json
+import os
+import time
 
 import torch
 
 L2_FLUSH_BYTES = 256 << 20     # larger than the 126 MB L2
 
 
-def _timed(fn, iters: int, flush: bool = True) -> float:
+_CLOCKS: list = []        # clock summaries of the timed regions of this process (kept with the result)
+
+
+def _timed(fn, iters: int, flush: bool = True, soak_s: float = 0.6) -> float:
+    """Median CUDA-event time (ms) of `iters` launches after 3 warm-ups, L2 flushed before each; the SM clock is
+    sampled (nvidia-smi, 100 ms) over the timed launches and a soak of the same launch of `soak_s` seconds, so
+    every timing carries the clocks it ran at."""
+    from ..utils.gpuinfo import Sampler
     buf = torch.empty(L2_FLUSH_BYTES, dtype=torch.int8, device="cuda") if flush else None
     for _ in range(3):
         fn()
     torch.cuda.synchronize()
     ts = []
-    for _ in range(iters):
-        if buf is not None:
-            buf.zero_()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        fn()
-        b.record()
-        b.synchronize()
-        ts.append(a.elapsed_time(b))
+    with Sampler(torch.cuda.current_device(), period_ms=100) as clk:
+        for _ in range(iters):
+            if buf is not None:
+                buf.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            b.synchronize()
+            ts.append(a.elapsed_time(b))
+        t0 = time.time()
+        while time.time() - t0 < soak_s:
+            for _ in range(8):
+                fn()
+            torch.cuda.synchronize()
+    _CLOCKS.append(clk.summary())
     ts.sort()
     return ts[len(ts) // 2]
+
+
+def measured_peaks() -> dict:
+    """The pool's measured roofline denominators (MEASURED_PEAKS.json at the repository root, written by the
+    driver), or the earlier fallback measurement when it is absent."""
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))),
+                        "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                "source": "measured"}
+    except (OSError, ValueError, KeyError):
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
 
 
 def bench_gemm(m, n, k, iters, bn=None):
@@ -210,6 +241,16 @@ def main(argv=None) -> int:
         r = bench_decode(args.batch, args.nq, args.nkv, args.ctx, args.iters)
     else:
         r = bench_prefill(args.seqs, args.len, args.nq, args.nkv, args.iters)
+    peaks = measured_peaks()
+    if _CLOCKS:
+        r["clocks"] = _CLOCKS[0]
+        if len(_CLOCKS) > 1:
+            r["clocks_library"] = _CLOCKS[1]
+    if "tflops" in r:
+        r[f"fraction_of_{peaks['source']}_bf16"] = round(r["tflops"] / peaks["bf16_tflops"], 3)
+    if "gbs" in r:
+        r[f"fraction_of_{peaks['source']}_hbm"] = round(r["gbs"] / peaks["hbm_gbs"], 3)
+    r["peaks"] = peaks
     print(json.dumps(r), flush=True)
     return 0
 
