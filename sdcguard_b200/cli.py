@@ -1,6 +1,7 @@
 """`sdcguard` command line.
 
     sdcguard gate DIR --require checksum [--arm A] [--json]   per-request KV-checksum coverage gate (exit 0 PASS, 2 HOLD)
+    sdcguard gate capture|add|run|compare|workaround|...      upgrade gate of library GEMMs (exit 0 / 1 / 2)
     sdcguard transfer-check DIR [--json]                     transfer-only coverage (exit 0 PASS, 2 HOLD)
     sdcguard transfer-compare BASE CAND [--json]             coverage preservation between two builds (always 2)
     sdcguard pd-record OUT [--gpus ...]                      record a checked prefill/decode run of this engine
@@ -20,6 +21,7 @@
     sdcguard evidence / report-verify / upgrade              evidence report envelope, its verification, upgrade policy
     sdcguard inventory / overhead / model-ref                client batch join, matched-run overhead, model file binding
     sdcguard assignment / forward-inputs / regression        recorded page assignment, forward inputs, saved case
+    sdcguard train-bench / kernel-bench / calibrate          training cost, kernel timings, noise-model calibration
     sdcguard version
 
 The first three keep the reference's commands, exit codes and output (src/sdcguard/cli.py:343-463 dispatch).
@@ -35,6 +37,18 @@ def _version(argv) -> int:
     return 0
 
 
+LEGACY_GATE = ("capture", "add", "run", "compare", "investigate", "workaround", "pin", "model-ref", "model-check")
+
+
+def _gate(argv) -> int:
+    """`sdcguard gate SUBCOMMAND ...` without --require is the upgrade gate of library GEMMs
+    (tools/upgrade_gate.py); anything else is the KV-checksum coverage gate."""
+    import importlib
+    if argv and argv[0] in LEGACY_GATE and not any(a == "--require" or a.startswith("--require=") for a in argv):
+        return importlib.import_module(".tools.upgrade_gate", __package__).main(argv)
+    return importlib.import_module(".coverage.gate", __package__).main(argv)
+
+
 def _lazy(module: str, fn: str):
     def run(argv):
         import importlib
@@ -43,7 +57,7 @@ def _lazy(module: str, fn: str):
 
 
 COMMANDS = {
-    "gate": _lazy(".coverage.gate", "main"),
+    "gate": lambda argv: _gate(argv),
     "transfer-check": _lazy(".coverage.transfer", "main"),
     "transfer-compare": _lazy(".coverage.transfer", "main_compare"),
     "pd-record": _lazy(".serve.pd", "main"),
@@ -86,6 +100,9 @@ COMMANDS = {
     "assignment": _lazy(".evidence.assignment", "main"),
     "forward-inputs": _lazy(".evidence.forward", "main"),
     "regression": _lazy(".evidence.regression", "main"),
+    "train-bench": _lazy(".tools.train_bench", "main"),
+    "kernel-bench": _lazy(".tools.kernel_bench", "main"),
+    "calibrate": _lazy(".tools.calibrate", "main"),
     "version": _version,
 }
 
