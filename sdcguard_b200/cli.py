@@ -22,6 +22,7 @@
     sdcguard inventory / overhead / model-ref                client batch join, matched-run overhead, model file binding
     sdcguard assignment / forward-inputs / regression        recorded page assignment, forward inputs, saved case
     sdcguard train-bench / kernel-bench / calibrate          training cost, kernel timings, noise-model calibration
+    sdcguard nvsentinel RESULT|ALERTS.jsonl [--dry-run]      health events for NVIDIA NVSentinel
     sdcguard version
 
 The first three keep the reference's commands, exit codes and output (src/sdcguard/cli.py:343-463 dispatch).
@@ -101,6 +102,7 @@ COMMANDS = {
     "forward-inputs": _lazy(".evidence.forward", "main"),
     "regression": _lazy(".evidence.regression", "main"),
     "train-bench": _lazy(".tools.train_bench", "main"),
+    "nvsentinel": _lazy(".utils.nvsentinel", "main"),
     "kernel-bench": _lazy(".tools.kernel_bench", "main"),
     "calibrate": _lazy(".tools.calibrate", "main"),
     "version": _version,

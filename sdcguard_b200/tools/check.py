@@ -72,8 +72,12 @@ def run(device="cuda:0", seconds: float = 20.0, size: int = 8192, seed: int = 0)
     # output fingerprint: the checked GEMM is deterministic, so every healthy GPU of a model gives the same bits
     gemm.checked_linear(x, cw, st.state, slot, row_sq=rs, out=y)
     fp = hashlib.sha256(y.view(torch.int16).cpu().numpy().tobytes()).hexdigest()[:32]
+    from ..utils.events import device_identity
+    ident = device_identity(dev)
+    wrong = int(r["z"] > abft.Z_ALARM) + wrong_copies
     return {"device": torch.cuda.get_device_name(dev), "gemm_size": size, "seed": seed, "seconds": seconds,
-            "output_fingerprint": fp,
+            "result": "PASS" if wrong == 0 else "FAIL", "gpu_uuid": ident.get("gpu_uuid"),
+            "pci_bus_id": ident.get("pci_bus_id"), "output_fingerprint": fp,
             "checked_gemm_tflops": round(flops / ms_checked / 1e9, 1), "cublas_gemm_tflops": round(flops / ms_cublas / 1e9, 1),
             "d2d_gbs": round(2 * src.numel() * 2 / ms_copy / 1e6, 1),
             "gemm_checks": r["checks"], "gemm_wrong": int(r["z"] > abft.Z_ALARM), "worst_z": round(r["z"], 3),
