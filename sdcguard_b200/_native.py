@@ -106,6 +106,15 @@ SIGNATURES: dict[str, tuple] = {
     "sdc_kv_page_checksums": (I, [P, L, L, I, P, I, ctypes.c_ulonglong, P, P]),
     "sdc_kv_pull_pages": (I, [P, L, P, L, L, I, P, P, I, ctypes.c_ulonglong, P, P, P, P, P]),
     "sdc_spot_check": (I, [P, L, P, P, L, P, I, I, P, I, P, I, F, F, P, P]),
+    "sdc_gemm_bf16_grouped": (I, [P, L, P, P, I, I, I, I, P, L, P, P, P, P, P, P, I, U, U, U, U, F, F, F, F, F, P, I,
+                                  I, I, U, P]),
+    "sdc_silu_mul_bf16_bands": (I, [P, I, I, P, P, P, P]),
+    "sdc_moe_plan": (I, [P, I, I, I, I, P, P, P, P, P, P, P]),
+    "sdc_moe_gather": (I, [P, L, I, I, I, I, P, P, P, P, P, P]),
+    "sdc_moe_combine": (I, [P, I, I, I, P, P, P, L, I, P]),
+    "sdc_prep_rowblock": (I, [P, L, I, I, U, U, U, U, P, P, P, P, P]),
+    "sdc_prep_colblock": (I, [P, L, I, I, U, U, U, U, P, P, P, P]),
+    "sdc_ep_receive_grouped": (I, [P, P, P, P, P, I, I, I, I, I, P, P, P, P, P, P, P, P, P]),
 }
 
 

@@ -117,31 +117,74 @@ __device__ __forceinline__ void report(unsigned long long* state, float z, unsig
 
 // Receiver: wait for every source, then one warp per (src, e, slot) of the capacity: verify and compact.
 // Compact order: expert e major, then source, then slot. offs (out, [epr + 1]) and map (out) are written too.
+// Grouped layout (gr.gband set): every expert's rows start on a 128-row band and are padded with zero rows to
+// whole bands (pad rows have map -1), the band -> expert table and the band count are written, and each row's
+// sum of squares goes to gr.row_sq: the input of the grouped checked GEMM (sdc_gemm_bf16_grouped), with no
+// host-side counts.
+struct Grouped {
+  int* gband;
+  int* gcount;
+  float* row_sq;
+};
+
 __global__ void __launch_bounds__(256) receive_kernel(const __nv_bfloat16* __restrict__ rows,
                                                       const uint32_t* __restrict__ seals, const int* __restrict__ cnt,
                                                       const long long* gen, const long long* my_flags, Geo g,
                                                       __nv_bfloat16* __restrict__ out, int* __restrict__ map,
-                                                      int* __restrict__ offs, unsigned long long* state, int* err) {
+                                                      int* __restrict__ offs, unsigned long long* state, int* err,
+                                                      Grouped gr) {
   if (!peer::wait_all(gen, my_flags, g.world, err)) return;
   __shared__ int soff[MAXW * 16 + 1];
+  __shared__ int sexp[17];     // first row of each expert (and the end)
+  __shared__ int sn[16];       // rows of each expert
+  const bool grouped = gr.gband != nullptr;
   // exclusive offsets of (e, src) in compact order, from the published counts
   if (threadIdx.x == 0) {
     int acc = 0;
     for (int e = 0; e < g.epr; ++e) {
       if (blockIdx.x == 0) offs[e] = acc;
+      sexp[e] = acc;
+      const int a0 = acc;
       for (int src = 0; src < g.world; ++src) {
         soff[e * g.world + src] = acc;
         acc += __ldcg(cnt + src * g.epr + e);
       }
+      sn[e] = acc - a0;
+      if (grouped) acc = (acc + 127) / 128 * 128;
     }
-    if (blockIdx.x == 0) offs[g.epr] = acc;
+    sexp[g.epr] = acc;
+    if (blockIdx.x == 0) {
+      offs[g.epr] = acc;
+      if (grouped) {
+        for (int b = 0, e = 0; b < acc / 128; ++b) {
+          while (e + 1 < g.epr && sexp[e + 1] <= b * 128) ++e;
+          gr.gband[b] = e;
+        }
+        *gr.gcount = acc / 128;
+      }
+    }
   }
   __syncthreads();
   if (blockIdx.x == 0 && threadIdx.x == 0 && state != nullptr) atomicAdd(state + 2, 1ull);
   const long long w = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31, hl = lane & 15, half = lane >> 4;
   const long long per_src = static_cast<long long>(g.epr) * g.cap;
-  if (w >= g.world * per_src) return;
+  if (w >= g.world * per_src) {
+    // grouped layout: warps past the received rows zero the pad rows of each expert
+    const long long pw = w - g.world * per_src;
+    if (!grouped || pw >= static_cast<long long>(g.epr) * 128) return;
+    const int e = static_cast<int>(pw / 128), k = static_cast<int>(pw % 128);
+    const int n = sn[e];
+    if (k >= (n + 127) / 128 * 128 - n) return;
+    const long long r = sexp[e] + n + k;
+    uint4* op = reinterpret_cast<uint4*>(out + r * g.H);
+    for (int q = lane; q < g.H / 8; q += 32) op[q] = make_uint4(0, 0, 0, 0);
+    if (lane == 0) {
+      map[r] = -1;
+      gr.row_sq[r] = 0.f;
+    }
+    return;
+  }
   const int src = static_cast<int>(w / per_src);
   const int e = static_cast<int>((w % per_src) / g.cap);
   const int s = static_cast<int>(w % g.cap);
@@ -150,6 +193,7 @@ __global__ void __launch_bounds__(256) receive_kernel(const __nv_bfloat16* __res
   const int c = soff[e * g.world + src] + s;
   const uint4* rp = reinterpret_cast<const uint4*>(rows + row * g.H);
   uint4* op = reinterpret_cast<uint4*>(out + static_cast<long long>(c) * g.H);
+  float ss = 0.f;
   for (int b0 = 0; b0 < g.nb; b0 += 2) {
     const int b = b0 + half;
     const int q = b * 16 + hl;
@@ -158,8 +202,21 @@ __global__ void __launch_bounds__(256) receive_kernel(const __nv_bfloat16* __res
     if (in) v = __ldcg(rp + q);
     const uint32_t h = half_warp_seal(v, hl);
     if (in) op[q] = v;
+    if (grouped) {
+      const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wv[j]));
+        ss = fmaf(f.x, f.x, fmaf(f.y, f.y, ss));
+      }
+    }
     if (hl == 0 && b < g.nb && h != __ldcg(seals + row * g.nb + b))
       report(state, __int_as_float(0x7f800000), static_cast<unsigned long long>(row) * g.nb + b);
+  }
+  if (grouped) {
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
+    if (lane == 0) gr.row_sq[c] = ss;
   }
   if (lane == 0) map[c] = (src << 24) | (e << 20) | s;
 }
@@ -172,6 +229,7 @@ __global__ void __launch_bounds__(256) combine_push_kernel(const __nv_bfloat16* 
   const int lane = threadIdx.x & 31, hl = lane & 15, half = lane >> 4;
   if (w >= offs[g.epr]) return;
   const int m = map[w];
+  if (m < 0) return;   // a pad row of the grouped layout
   const int src = m >> 24, e = (m >> 20) & 15, s = m & 0xFFFFF;
   const long long row = region(g, g.rank, e) + s;           // in the source's buffer, this rank's region
   const uint4* sp = reinterpret_cast<const uint4*>(y + w * g.H);
@@ -358,7 +416,24 @@ int sdc_ep_receive(const void* rows, const void* seals, const int* cnt, const vo
                    static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(rows), static_cast<const uint32_t*>(seals), cnt,
       static_cast<const long long*>(gen), static_cast<const long long*>(my_flags), g,
-      static_cast<__nv_bfloat16*>(out), map, offs, static_cast<unsigned long long*>(state), err);
+      static_cast<__nv_bfloat16*>(out), map, offs, static_cast<unsigned long long*>(state), err,
+      Grouped{nullptr, nullptr, nullptr});
+  return static_cast<int>(cudaGetLastError());
+}
+
+// As sdc_ep_receive, into the grouped layout of the grouped checked GEMM: out / map / row_sq hold
+// world * epr * cap + epr * 128 rows; gband [that / 128] and gcount [1] are written on the device.
+int sdc_ep_receive_grouped(const void* rows, const void* seals, const int* cnt, const void* gen, const void* my_flags,
+                           int world, int rank, int epr, int cap, int H, void* out, int* map, int* offs, int* gband,
+                           int* gcount, float* row_sq, void* state, int* err, void* stream) {
+  if (bad_geo(world, epr, H, 1) || gband == nullptr || gcount == nullptr || row_sq == nullptr) return -1;
+  const Geo g = geo(world, rank, epr, cap, H, 0, 1);
+  receive_kernel<<<blocks_for_warps(static_cast<long long>(world) * epr * cap + epr * 128ll), 256, 0,
+                   static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(rows), static_cast<const uint32_t*>(seals), cnt,
+      static_cast<const long long*>(gen), static_cast<const long long*>(my_flags), g,
+      static_cast<__nv_bfloat16*>(out), map, offs, static_cast<unsigned long long*>(state), err,
+      Grouped{gband, gcount, row_sq});
   return static_cast<int>(cudaGetLastError());
 }
 

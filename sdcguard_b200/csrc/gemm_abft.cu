@@ -108,6 +108,13 @@ struct Params {
   int ksplit;                // K splits (1: the fused epilogue; > 1: partial accumulators + reduce kernel)
   int kb_per;                // k-blocks per split
   float* part;               // ksplit > 1: [ksplit][M][N + 6 nb] fp32 partial accumulators
+  // Grouped mode (null gband: off). The rows of A are grouped by expert, each expert's rows starting on a band
+  // boundary; band b belongs to expert gband[b], and only the first *gcount bands hold rows (both written on the
+  // device by the kernel before this one, read after the programmatic-launch wait). W and Wc are the experts'
+  // matrices stacked (expert e's rows start at e * g_wrows and e * g_wcrows), wstat is [experts][nb].
+  const int* gband;
+  const int* gcount;
+  int g_wrows, g_wcrows;
 };
 
 // PAIR: a CTA pair (cluster of two) computes a 256 x BN tile with cta_group::2 MMAs issued by the first CTA;
@@ -156,12 +163,13 @@ static_assert(sizeof(SmemCtl) <= Cfg<128>::CTL_BYTES && sizeof(SmemCtl) <= Cfg<2
 // W slab are consecutive). The tiles in flight at any time then share a few W slabs and the group's A rows,
 // which stay in L2, instead of streaming all of W once per band. Every output tile still comes after the
 // checksum tiles of its band, which is what the band wait relies on.
-__device__ __forceinline__ void tile_coords(const Params& p, int tile, int& mt, bool& cs, int& idx) {
+// m_units: the bands (or pairs) of this launch (p.m_units, or the device count in grouped mode).
+__device__ __forceinline__ void tile_coords(const Params& p, int m_units, int tile, int& mt, bool& cs, int& idx) {
   const int per_group = p.group * p.n_per_m;
   const int g = tile / per_group;
   const int l = tile - g * per_group;
   const int b0 = g * p.group;
-  const int gm = min(p.group, p.m_units - b0);
+  const int gm = min(p.group, m_units - b0);
   const int ncs = gm * p.n_cs;
   cs = l < ncs;
   const int l2 = cs ? l : l - ncs;
@@ -171,10 +179,10 @@ __device__ __forceinline__ void tile_coords(const Params& p, int tile, int& mt, 
 
 // Split-K: tile t of the persistent order is (base tile t / ksplit, split t % ksplit); consecutive splits of a
 // tile go to different CTAs.
-__device__ __forceinline__ void tile_coords_k(const Params& p, int tile, int& mt, bool& cs, int& idx, int& kb0,
-                                              int& kb1, int kblocks) {
+__device__ __forceinline__ void tile_coords_k(const Params& p, int m_units, int tile, int& mt, bool& cs, int& idx,
+                                              int& kb0, int& kb1, int kblocks) {
   const int ks = tile % p.ksplit;
-  tile_coords(p, tile / p.ksplit, mt, cs, idx);
+  tile_coords(p, m_units, tile / p.ksplit, mt, cs, idx);
   kb0 = ks * p.kb_per;
   kb1 = min(kblocks, kb0 + p.kb_per);
 }
@@ -315,7 +323,7 @@ __device__ __forceinline__ void judge_prefetch(const Params& p, SmemCtl* ctl, Pe
   pd.ready = mbar_wait(&ctl->ready[pd.acc], pd.phase, abort_flag) && ctl->ready_ok[pd.acc] != 0;
   if (pd.valid && pd.ready) {
     pd.ex = __ldcg(p.expd + static_cast<long long>(pd.row) * p.nb + pd.b);
-    pd.ws = __ldg(p.wstat + pd.b);
+    pd.ws = __ldg(p.wstat + pd.b + (p.gband != nullptr ? __ldcg(p.gband + pd.row / BM) * p.nb : 0));
     pd.bs = p.bsum != nullptr ? __ldg(p.bsum + pd.b) : make_float2(0.f, 0.f);
     pd.rsq = __ldg(p.row_sq + pd.row);
   }
@@ -543,6 +551,11 @@ __global__ void __launch_bounds__(Cfg<BN, PAIR>::THREADS, 1)
   const uint32_t tmem_base = ctl->tmem_base;
   volatile int* abort_flag = &ctl->abort_flag;
   const int kblocks = (p.K + BK - 1) / BK;
+  // grouped mode: the band count and the band -> expert table come from the previous kernel
+  if (p.gcount != nullptr) pdl_wait();
+  const int m_units = p.gcount != nullptr ? min(__ldcg(p.gcount), p.m_units) : p.m_units;
+  const int total_tiles = p.gcount != nullptr ? m_units * p.n_per_m : p.total_tiles;
+  const int m_tiles = p.gcount != nullptr ? m_units : p.m_tiles;
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -554,7 +567,7 @@ __global__ void __launch_bounds__(Cfg<BN, PAIR>::THREADS, 1)
       uint32_t issued_phase = 0;  // bit s: the full-barrier parity of that load
       // Programmatic dependent launch: the weights (W or its checksum rows) do not depend on the previous kernel,
       // so the first tile's first stages load them before waiting for it; their activation halves follow the wait.
-      bool waited = false;
+      bool waited = p.gcount != nullptr;   // grouped mode waited above (the weights' rows depend on the table)
       int npre = 0, pre_mt = 0, pre_kb0 = 0;
       // pair mode: every load completes bytes on the first CTA's full barrier; the MMA releases each stage on
       // both CTAs' empty barriers
@@ -571,10 +584,16 @@ __global__ void __launch_bounds__(Cfg<BN, PAIR>::THREADS, 1)
         waited = true;
         for (int i = 0; i < npre; ++i) load_a(i, pre_kb0 + i, pre_mt);
       };
-      for (int tile = t_first; tile < p.total_tiles && ok; tile += t_step) {
+      for (int tile = t_first; tile < total_tiles && ok; tile += t_step) {
         int mt, idx, kb0, kb1;
         bool cs;
-        tile_coords_k(p, tile, mt, cs, idx, kb0, kb1, kblocks);
+        tile_coords_k(p, m_units, tile, mt, cs, idx, kb0, kb1, kblocks);
+        int wrow0 = 0, wcrow0 = 0;   // grouped mode: the band's expert's rows in the stacked W and Wc
+        if (p.gband != nullptr) {
+          const int e = __ldcg(p.gband + mt);
+          wrow0 = e * p.g_wrows;
+          wcrow0 = e * p.g_wcrows;
+        }
         // bytes one CTA loads per stage (the pair's first CTA expects both CTAs' bytes)
         const uint32_t bytes = A_BYTES + (cs ? (C::CSB * CS_ROWS / (PAIR ? 2 : 1)) * BK * 2 : C::B_BYTES);
         // pair mode: the checksum tile's N columns are split evenly between the CTAs' B halves
@@ -598,15 +617,16 @@ __global__ void __launch_bounds__(Cfg<BN, PAIR>::THREADS, 1)
             if (prank == 0) mbar_arrive_expect_tx(&ctl->full[stage], 2u * bytes);
             const uint32_t fb = full0 + static_cast<uint32_t>(stage) * 8u;
             if (cs)
-              tma_load_2d_pair(sb, &tmWc, fb, kb * BK, idx * C::CSB * CS_ROWS + static_cast<int>(prank) * (cs_ncols / 2));
+              tma_load_2d_pair(sb, &tmWc, fb, kb * BK,
+                               wcrow0 + idx * C::CSB * CS_ROWS + static_cast<int>(prank) * (cs_ncols / 2));
             else
-              tma_load_2d_pair(sb, &tmW, fb, kb * BK, idx * BN + static_cast<int>(prank) * (BN / 2));
+              tma_load_2d_pair(sb, &tmW, fb, kb * BK, wrow0 + idx * BN + static_cast<int>(prank) * (BN / 2));
           } else {
             mbar_arrive_expect_tx(&ctl->full[stage], bytes);
             if (cs)
-              tma_load_2d(sb, &tmWc, &ctl->full[stage], kb * BK, idx * C::CSB * CS_ROWS);
+              tma_load_2d(sb, &tmWc, &ctl->full[stage], kb * BK, wcrow0 + idx * C::CSB * CS_ROWS);
             else
-              tma_load_2d(sb, &tmW, &ctl->full[stage], kb * BK, idx * BN);
+              tma_load_2d(sb, &tmW, &ctl->full[stage], kb * BK, wrow0 + idx * BN);
           }
           if (waited)
             load_a(stage, kb, mt);
@@ -641,10 +661,10 @@ __global__ void __launch_bounds__(Cfg<BN, PAIR>::THREADS, 1)
       // pair mode: the second CTA's empty and accumulator barriers, signalled by the same commits
       const uint32_t peer_empty = PAIR ? mapa_shared(smem_u32(&ctl->empty[0]), 1u) : 0u;
       const uint32_t peer_tfull = PAIR ? mapa_shared(smem_u32(&ctl->tfull[0]), 1u) : 0u;
-      for (int tile = t_first; tile < p.total_tiles && ok; tile += t_step) {
+      for (int tile = t_first; tile < total_tiles && ok; tile += t_step) {
         int mt, idx, kb0, kb1;
         bool cs;
-        tile_coords_k(p, tile, mt, cs, idx, kb0, kb1, kblocks);
+        tile_coords_k(p, m_units, tile, mt, cs, idx, kb0, kb1, kblocks);
         uint32_t idesc = idesc_main;
         if (cs) {
           const int nblk = min(C::CSB, p.nb - idx * C::CSB);
@@ -722,12 +742,12 @@ __global__ void __launch_bounds__(Cfg<BN, PAIR>::THREADS, 1)
       unsigned long long* st = p.state + static_cast<long long>(p.slot) * 4;
       unsigned long long m0 = 0ull, m1 = 0ull;   // this CTA's worst keys so far
       long long unj_all = 0;
-      for (int tile = t_first; tile < p.total_tiles; tile += t_step) {
+      for (int tile = t_first; tile < total_tiles; tile += t_step) {
         int mt, idx;
         bool cs;
-        tile_coords(p, tile, mt, cs, idx);
+        tile_coords(p, m_units, tile, mt, cs, idx);
         const int band = band_of(mt);
-        const bool in_band = band < p.m_tiles;     // pair mode: the second half of the last pair may be empty
+        const bool in_band = band < m_tiles;     // pair mode: the second half of the last pair may be empty
         int ok = 1;
         if (!cs && in_band) {
           ok = 0;
@@ -804,10 +824,10 @@ __global__ void __launch_bounds__(Cfg<BN, PAIR>::THREADS, 1)
     // named barrier in the loop, so a warp that gives up leaves no other warp waiting.
     Pending pend;
     pend.live = false;
-    for (int tile = t_first; tile < p.total_tiles; tile += t_step) {
+    for (int tile = t_first; tile < total_tiles; tile += t_step) {
       int mt, idx;
       bool cs;
-      tile_coords(p, tile / p.ksplit, mt, cs, idx);
+      tile_coords(p, m_units, tile / p.ksplit, mt, cs, idx);
       const int band = band_of(mt);
       const int row = band * BM + row_in_tile;
       const unsigned long long t_w0 = p.dbg ? globaltimer() : 0ull;
@@ -1236,12 +1256,20 @@ struct PushArgs {
   void* done;                            // this rank's CTA completion counter (zero)
 };
 
+// Grouped mode (see Params::gband): `experts` matrices of N rows stacked in W, their checksum rows in Wc.
+struct GroupArgs {
+  int experts;
+  const int* gband;    // [max bands] expert of each band
+  const int* gcount;   // [1] bands in use
+};
+
 static int gemm_run(const void* A, long long lda, const void* W, const void* Wc, int M, int N, int K, void* Cout,
                     long long ldc, const float* bias, const float* bsum, float bias_max, const float* row_sq,
                     const float* wstat, void* ws, unsigned long long* state, int slot, unsigned s0, unsigned s1,
                     unsigned s2, unsigned s3, float zthr, float prod_coef, float out_coef, float abs_floor,
                     float bound_coef, int* err, int bn, int max_ctas, int inj_row, int inj_col, unsigned inj_xor,
-                    void* dbg, void* seal, void* stream, bool allow_split, const PushArgs* push = nullptr) {
+                    void* dbg, void* seal, void* stream, bool allow_split, const PushArgs* push = nullptr,
+                    const GroupArgs* grp = nullptr) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   if ((K % 8) || (N % 8) || (lda % 8) || (ldc % 8) || (bn != 128 && bn != 256)) return -1;
   if ((M + BM - 1) / BM > MAX_BANDS) return -1;
@@ -1261,8 +1289,11 @@ static int gemm_run(const void* A, long long lda, const void* W, const void* Wc,
   p.m_tiles = (M + BM - 1) / BM;
   // CTA pairs (256 x 256 tiles, cta_group::2): for outputs with at least two bands and enough tiles to fill the
   // GPU with pairs; not with push or split-K (decode-sized outputs)
-  const bool pair = bn == 256 && push == nullptr && p.m_tiles >= 2 && max_ctas == 0 && pair_enabled() &&
-                    pair_max_clusters() > 0;
+  if (grp != nullptr && (push != nullptr || grp->experts < 1 || N % CSW || bias != nullptr || grp->gband == nullptr ||
+                         grp->gcount == nullptr))
+    return -1;
+  const bool pair = bn == 256 && push == nullptr && grp == nullptr && p.m_tiles >= 2 && max_ctas == 0 &&
+                    pair_enabled() && pair_max_clusters() > 0;
   p.m_units = pair ? (p.m_tiles + 1) / 2 : p.m_tiles;
   p.total_tiles = p.m_units * p.n_per_m;
   {
@@ -1302,6 +1333,14 @@ static int gemm_run(const void* A, long long lda, const void* W, const void* Wc,
   p.ksplit = 1;
   p.kb_per = (K + BK - 1) / BK;
   p.part = nullptr;
+  const int experts = grp != nullptr ? grp->experts : 1;
+  if (grp != nullptr) {
+    p.gband = grp->gband;
+    p.gcount = grp->gcount;
+    p.g_wrows = N;
+    p.g_wcrows = nb * CS_ROWS;
+    if (static_cast<long long>(experts) * N >= (1ll << 31)) return -1;
+  }
   PeerMaps pm;
   std::memset(&pm, 0, sizeof(pm));
   if (push != nullptr) {
@@ -1325,7 +1364,7 @@ static int gemm_run(const void* A, long long lda, const void* W, const void* Wc,
   // splitting pays when each CTA would stream a long K (measured: K = 1024 is faster unsplit)
   int split_min_k, split_force;
   split_policy(&split_min_k, &split_force);
-  if (!pair && allow_split && push == nullptr && split_eligible(M, N) && K >= split_min_k && max_ctas == 0 && dbg == nullptr) {
+  if (!pair && allow_split && push == nullptr && grp == nullptr && split_eligible(M, N) && K >= split_min_k && max_ctas == 0 && dbg == nullptr) {
     const int kblocks = (K + BK - 1) / BK;
     int sp = split_force > 0 ? split_force : num_sms_cached() / p.total_tiles;
     sp = sp > kMaxSplit ? kMaxSplit : sp;
@@ -1339,8 +1378,9 @@ static int gemm_run(const void* A, long long lda, const void* W, const void* Wc,
   }
   CUtensorMap ma, mw, mc, mo;
   if (!make_map(&ma, A, M, K, lda, BM)) return -2;
-  if (!make_map(&mw, W, N, K, K, pair ? bn / 2 : bn)) return -3;
-  if (!make_map(&mc, Wc, static_cast<long long>(nb) * CS_ROWS, K, K, p.csb * CS_ROWS / (pair ? 2 : 1))) return -4;
+  if (!make_map(&mw, W, static_cast<long long>(experts) * N, K, K, pair ? bn / 2 : bn)) return -3;
+  if (!make_map(&mc, Wc, static_cast<long long>(experts) * nb * CS_ROWS, K, K, p.csb * CS_ROWS / (pair ? 2 : 1)))
+    return -4;
   if (!make_map(&mo, Cout, M, N, ldc, 32, false)) return -5;
   int grid = p.total_tiles;
   const int cap = max_ctas > 0 ? max_ctas : num_sms_cached();
@@ -1397,6 +1437,25 @@ int sdc_gemm_bf16_push(const void* A, long long lda, const void* W, const void* 
   return gemm_run(A, lda, W, Wc, M, N, K, reinterpret_cast<void*>(recv_ptrs[rank]), N, bias, bsum, bias_max, row_sq,
                   wstat, ws, state, slot, s0, s1, s2, s3, zthr, prod_coef, out_coef, abs_floor, bound_coef, err, bn, 0,
                   inj_row, inj_col, inj_xor, nullptr, nullptr, stream, false, &pa);
+}
+
+// Grouped checked GEMM (mixture-of-experts layers): C[M,N] = A[M,K] @ W_e^T for the rows of each expert e in one
+// launch, with the same check. A's rows are grouped by expert, each group starting on a 128-row band and padded
+// with zero rows to whole bands; gband[b] is the expert of band b and *gcount the number of bands in use, both
+// written on the device (sdc_moe_group), so the launch needs no host-side counts and can be graph-captured.
+// W = [experts * N, K] (expert e's rows at e * N), Wc = [experts * 6 nb, K], wstat = [experts][nb]. M is the
+// capacity of A and C in rows; N % 128 == 0, no bias, no split-K, single CTAs (a band pair could straddle
+// two experts).
+int sdc_gemm_bf16_grouped(const void* A, long long lda, const void* W, const void* Wc, int experts, int M, int N,
+                          int K, void* Cout, long long ldc, const float* row_sq, const float* wstat, const int* gband,
+                          const int* gcount, void* ws, unsigned long long* state, int slot, unsigned s0, unsigned s1,
+                          unsigned s2, unsigned s3, float zthr, float prod_coef, float out_coef, float abs_floor,
+                          float bound_coef, int* err, int bn, int inj_row, int inj_col, unsigned inj_xor,
+                          void* stream) {
+  GroupArgs ga{experts, gband, gcount};
+  return gemm_run(A, lda, W, Wc, M, N, K, Cout, ldc, nullptr, nullptr, 0.f, row_sq, wstat, ws, state, slot, s0, s1,
+                  s2, s3, zthr, prod_coef, out_coef, abs_floor, bound_coef, err, bn, 0, inj_row, inj_col, inj_xor,
+                  nullptr, nullptr, stream, false, nullptr, &ga);
 }
 
 }  // extern "C"

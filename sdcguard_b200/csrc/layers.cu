@@ -257,8 +257,11 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(
 // out[row, :] = silu(gu[row, :I]) * gu[row, I:]; one CTA of 128 threads per row, I % 8 == 0.
 __global__ void __launch_bounds__(128) silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, int I,
                                                        __nv_bfloat16* __restrict__ out, float* __restrict__ row_sq,
-                                                       const int* rows, unsigned long long* check) {
+                                                       const int* rows, unsigned long long* check,
+                                                       const int* gcount) {
   pdl_trigger();   // a dependent GEMM may start its prologue and weight loads now
+  // grouped rows (mixture of experts): only the first *gcount 128-row bands are in use (CTA-uniform exit)
+  if (gcount != nullptr && static_cast<long long>(blockIdx.x) >= 128ll * __ldcg(gcount)) return;
   __shared__ float red[4];
   __shared__ int sbad;
   int bad = 0x7fffffff;
@@ -376,7 +379,18 @@ int sdc_silu_mul_bf16(const void* gu, int M, int I, void* out, void* row_sq, con
   if (I % 8 || (check != nullptr && rows == nullptr)) return -1;
   sdc::silu_mul_kernel<<<M, 128, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(gu), I, static_cast<__nv_bfloat16*>(out), static_cast<float*>(row_sq), rows,
-      static_cast<unsigned long long*>(check));
+      static_cast<unsigned long long*>(check), nullptr);
+  return static_cast<int>(cudaGetLastError());
+}
+
+// silu_mul over grouped expert rows: M is the buffers' capacity, rows past 128 * (*gcount) are skipped (the
+// band count written on the device by sdc_moe_plan or the expert-parallel receive).
+int sdc_silu_mul_bf16_bands(const void* gu, int M, int I, void* out, void* row_sq, const int* gcount, void* stream) {
+  if (M <= 0) return 0;
+  if (I % 8 || gcount == nullptr) return -1;
+  sdc::silu_mul_kernel<<<M, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(gu), I, static_cast<__nv_bfloat16*>(out), static_cast<float*>(row_sq), nullptr,
+      nullptr, gcount);
   return static_cast<int>(cudaGetLastError());
 }
 

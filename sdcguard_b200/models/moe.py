@@ -1,18 +1,25 @@
 """Mixture-of-experts layer (Mixtral-style: softmax router, top-k, renormalised weights, SwiGLU experts) on this
-library's kernels, expert-parallel over the ranks:
+library's kernels, expert-parallel over the ranks or with every expert on this GPU:
 
     logits = checked GEMM  x @ Wr^T                 ABFT (router rows padded to a multiple of 8)
     ids, w = router_topk(logits)                     exact replay of a rotating sample of tokens
-    rows   = dispatch(x, ids)                        sealed transfer over NVLink, verified on arrival
-    per local expert e:  h = silu(x_e Wg^T) * (x_e Wu^T);  y_e = h Wd^T      ABFT on both GEMMs
-    y      = combine(y_e, w)                         sealed transfer back, verified, weighted sum in fp32
+    rows   = dispatch(x, ids)                        "own": sealed transfer over NVLink, verified on arrival;
+                                                     "local": on-device grouping (ops.moe.Grouping)
+    h      = grouped checked GEMM  rows @ W13_e^T    ABFT, all local experts in one launch (rows of each expert
+    a      = silu(h_gate) * h_up                     start on a 128-row band; band -> expert table on the device)
+    y_e    = grouped checked GEMM  a @ W2_e^T        ABFT, one launch
+    y      = combine(y_e, w)                         sealed transfer back ("own"), weighted sum in fp32, k order
+
+Nothing in a checked layer reads back to the host: the band table and band count the grouped GEMMs need are written
+by the dispatch (or grouping) kernel, so a step of MoE layers can be captured in a CUDA graph. The "nccl" arm is the
+unchecked baseline: torch.distributed all-to-all and PyTorch's grouped GEMM.
 
 Expert weights are generated per global expert from a seed, so every rank can build the same reference and any
 EP size builds the same model. Config: Mixtral-8x7B shape = hidden 4096, 8 experts, top-2, expert FFN 14336.
 
 Reference: the reference samples rows of vLLM's fused MoE for recompute (src/sdcguard/serve_moe.py:123-165,
-`MoEChecks` :748) and the router for replay (src/sdcguard/serve_route.py, `RouteChecks` :588); it does not check
-the expert-parallel all-to-all.
+`MoEChecks` :748), checks PyTorch's `_grouped_mm` per group (src/sdcguard/guard.py:102-143) and replays the router
+(src/sdcguard/serve_route.py, `RouteChecks` :588); it does not check the expert-parallel all-to-all.
 """
 from __future__ import annotations
 
@@ -22,6 +29,7 @@ import torch
 import torch.distributed as dist
 
 from ..ops import gemm, layers
+from ..ops import moe as moe_ops
 from ..parallel.ep import EPComm, router_topk
 
 
@@ -41,14 +49,19 @@ class MoELayer:
     def __init__(self, hidden: int, inter: int, experts: int, top_k: int, comm: Optional[EPComm], device,
                  checked: bool = True, seed: int = 0, state: Optional[gemm.StateTable] = None, name: str = "moe",
                  collective: str = "own"):
-        """collective "own": the sealed peer-memory all-to-all (needs comm); "nccl": the unchecked baseline
-        exchange over torch.distributed (comm may be None)."""
+        """collective "own": the sealed peer-memory all-to-all (needs comm); "local": every expert on this GPU,
+        rows grouped on the device (no all-to-all, comm unused); "nccl": the unchecked baseline exchange over
+        torch.distributed (comm may be None)."""
+        if collective not in ("own", "local", "nccl"):
+            raise ValueError(f"collective {collective!r}: own, local or nccl")
         self.H, self.I, self.E, self.k = hidden, inter, experts, top_k
         self.comm = comm
         self.collective = collective
         self.device = torch.device(device)
         self.checked = checked
-        if comm is not None:
+        if collective == "local":
+            self.rank, self.world = 0, 1
+        elif comm is not None:
             self.rank, self.world = comm.rank, comm.world
         else:
             self.rank = dist.get_rank() if dist.is_initialized() else 0
@@ -67,9 +80,12 @@ class MoELayer:
         self.name = name
         if checked:
             self.cw_r = gemm.CheckedWeight(self.router)
-            self.cw13 = [gemm.CheckedWeight(w) for w in self.w13]
-            self.cw2 = [gemm.CheckedWeight(w) for w in self.w2]
-        self.attach(state or gemm.StateTable(self.device, 8 + 2 * self.epr), name)
+            self.s13 = gemm.CheckedWeightStack(self.w13)
+            self.s2 = gemm.CheckedWeightStack(self.w2)
+        self._grouping: Optional[moe_ops.Grouping] = None
+        self._bufs: dict = {}
+        self.baseline_path = None
+        self.attach(state or gemm.StateTable(self.device, 8), name)
 
     def attach(self, table: gemm.StateTable, name: str) -> None:
         """Register this layer's check slots in `table` (a model's shared state table)."""
@@ -80,22 +96,25 @@ class MoELayer:
             return
         self.slots["router"] = table.add(f"{name}.router (ABFT GEMM)", self.cw_r.nb)
         self.slots["route"] = table.add(f"{name}.route (replay)", 1)
-        for j, e in enumerate(self.local):
-            self.slots[f"up{j}"] = table.add(f"{name}.expert{e}.gate_up (ABFT GEMM)", self.cw13[j].nb)
-            self.slots[f"down{j}"] = table.add(f"{name}.expert{e}.down (ABFT GEMM)", self.cw2[j].nb)
+        self.slots["up"] = table.add(f"{name}.experts.gate_up (ABFT GEMM)", self.s13.nb)
+        self.slots["down"] = table.add(f"{name}.experts.down (ABFT GEMM)", self.s2.nb)
 
     def inject_next(self, slot: str, row: int, col: int, bit: int) -> None:
-        """Fault injection: flip `bit` of fp32 accumulator (row, col) of the next GEMM in `slot` ("router",
-        "up<j>" or "down<j>" for local expert j) before its check."""
+        """Fault injection: flip `bit` of fp32 accumulator (row, col) of the next GEMM in `slot` before its check:
+        "router" (row = token), "up" or "down" (row = row of the grouped expert input: the experts' rows on 128-row
+        bands in local expert order)."""
         self._inject = (slot, (row, col, 1 << bit))
+
+    def _take(self, slot):
+        if getattr(self, "_inject", None) and self._inject[0] == slot:
+            inj, self._inject = self._inject[1], None
+            return inj
+        return None
 
     def _lin(self, x, w, cw, slot, out=None):
         if not self.checked:
             return torch.matmul(x, w.t(), out=out) if out is not None else torch.matmul(x, w.t())
-        inj = None
-        if getattr(self, "_inject", None) and self._inject[0] == slot:
-            inj, self._inject = self._inject[1], None
-        return gemm.checked_linear(x, cw, self.state.state, self.slots[slot], out=out, inject=inj)
+        return gemm.checked_linear(x, cw, self.state.state, self.slots[slot], out=out, inject=self._take(slot))
 
     def forward(self, x: torch.Tensor, sample: Optional[torch.Tensor] = None) -> torch.Tensor:
         logits = self._lin(x, self.router, getattr(self, "cw_r", None), "router")
@@ -105,22 +124,73 @@ class MoELayer:
         self.last_ids, self.last_wts = ids, wts
         if self.collective == "nccl":
             return self._forward_nccl(x, ids, wts)
-        xe, offs = self.comm.dispatch(x, ids)
-        ye = torch.empty_like(xe)
-        self._experts(xe, offs, ye)
-        return self.comm.combine(ye, wts)
+        if not self.checked:
+            raise ValueError("the unchecked arm uses collective 'nccl'")
+        if self.collective == "local":
+            grp = self._grouping_for(x.shape[0])
+            xg, rsq = grp.group(x, ids)
+            yg = self._experts_grouped(xg, rsq, grp.gband, grp.gcount)
+            return grp.combine(yg, wts)
+        xg, rsq, gband, gcount = self.comm.dispatch_grouped(x, ids)
+        yg = self._experts_grouped(xg, rsq, gband, gcount)
+        return self.comm.combine(yg, wts)
 
-    def _experts(self, xe, offs, ye):
+    def _grouping_for(self, T: int) -> moe_ops.Grouping:
+        g = self._grouping
+        if g is None or g.T < T:
+            g = self._grouping = moe_ops.Grouping(max(T, 1), self.k, self.epr, self.H, self.device, e_lo=self.local[0])
+        return g
+
+    def _buffers(self, cap: int):
+        b = self._bufs
+        if b.get("cap", 0) < cap:
+            dev, bf = self.device, torch.bfloat16
+            b.update(cap=cap, h=torch.empty(cap, 2 * self.I, dtype=bf, device=dev),
+                     act=torch.empty(cap, self.I, dtype=bf, device=dev),
+                     act_sq=torch.empty(cap, dtype=torch.float32, device=dev),
+                     y=torch.empty(cap, self.H, dtype=bf, device=dev))
+        return b
+
+    def _experts_grouped(self, xg, rsq, gband, gcount):
+        """Both expert GEMMs of every local expert as two grouped checked launches (and SwiGLU between)."""
+        cap = xg.shape[0]
+        b = self._buffers(cap)
+        st = self.state.state
+        h = gemm.checked_linear_grouped(xg, self.s13, gband, gcount, st, self.slots["up"], row_sq=rsq,
+                                        out=b["h"][:cap], inject=self._take("up"))
+        act, asq = layers.silu_mul_bands(h, gcount, out=b["act"][:cap], row_sq=b["act_sq"][:cap])
+        return gemm.checked_linear_grouped(act, self.s2, gband, gcount, st, self.slots["down"], row_sq=asq,
+                                           out=b["y"][:cap], inject=self._take("down"))
+
+    def _experts_unchecked(self, xe, offs_host):
+        """Baseline expert MLPs: PyTorch's grouped GEMM when it runs here, else one cuBLAS GEMM per expert."""
+        if self.baseline_path in (None, "grouped_mm") and hasattr(torch, "_grouped_mm") and xe.shape[0] > 0:
+            try:
+                if "w13_t" not in self._bufs:
+                    self._bufs["w13_t"] = torch.stack(self.w13).transpose(1, 2)     # (E, H, 2I), column-major
+                    self._bufs["w2_t"] = torch.stack(self.w2).transpose(1, 2)       # (E, I, H)
+                ends = torch.tensor(offs_host[1:], dtype=torch.int32, device=xe.device)
+                h = torch._grouped_mm(xe, self._bufs["w13_t"], offs=ends)
+                act, _ = layers.silu_mul(h)
+                y = torch._grouped_mm(act, self._bufs["w2_t"], offs=ends)
+                self.baseline_path = "grouped_mm"
+                return y
+            except (RuntimeError, TypeError, NotImplementedError):
+                self.baseline_path = "per_expert"
+        self.baseline_path = "per_expert"
+        ye = torch.empty_like(xe)
         for j in range(self.epr):
-            a, b = offs[j], offs[j + 1]
-            if b == a:
-                continue
-            h = self._lin(xe[a:b], self.w13[j], getattr(self, "cw13", [None] * self.epr)[j], f"up{j}")
-            act, _ = layers.silu_mul(h)
-            self._lin(act, self.w2[j], getattr(self, "cw2", [None] * self.epr)[j], f"down{j}", out=ye[a:b])
+            a, b = offs_host[j], offs_host[j + 1]
+            if b > a:
+                h = torch.matmul(xe[a:b], self.w13[j].t())
+                act, _ = layers.silu_mul(h)
+                torch.matmul(act, self.w2[j].t(), out=ye[a:b])
+        return ye
 
     def _forward_nccl(self, x, ids, wts):
-        """Baseline exchange: all_to_all_single of rows sorted by expert, cuBLAS experts, all_to_all back."""
+        """Baseline exchange: all_to_all_single of rows sorted by expert, unchecked experts, all_to_all back. The
+        split sizes are read to the host once per layer (all_to_all_single takes host lists); every permutation
+        is built on the device."""
         T, K = ids.shape
         flat = ids.view(-1).long()
         order = torch.argsort(flat, stable=True)
@@ -131,36 +201,34 @@ class MoELayer:
             dist.all_to_all_single(recv_cnt, cnt_e)                               # (src, local expert) counts
         else:
             recv_cnt.copy_(cnt_e)
-        sc = cnt_e.view(self.world, self.epr).sum(1).tolist()
-        rc_m = recv_cnt.view(self.world, self.epr).tolist()
-        rc = [sum(r) for r in rc_m]
+        both = torch.stack([cnt_e, recv_cnt]).cpu()
+        sc = both[0].view(self.world, self.epr).sum(1).tolist()
+        rc_m = both[1].view(self.world, self.epr)
+        rc = rc_m.sum(1).tolist()
         recv = torch.empty(sum(rc), self.H, dtype=x.dtype, device=x.device)
         if self.world > 1:
             dist.all_to_all_single(recv, send, rc, sc)
         else:
             recv.copy_(send)
-        # received rows: by source, then local expert; regroup by expert for the GEMMs
-        starts, pos = [], 0
-        for src in range(self.world):
-            for e in range(self.epr):
-                starts.append((e, src, pos, rc_m[src][e]))
-                pos += rc_m[src][e]
-        perm = [i for e in range(self.epr) for (ee, src, p0, n) in starts if ee == e for i in range(p0, p0 + n)]
-        perm_t = torch.tensor(perm, dtype=torch.long, device=x.device)
-        xe = recv.index_select(0, perm_t)
+        # received rows come by source, then local expert: regroup by expert with a stable sort of expert ids
+        dev = x.device
+        eid = torch.repeat_interleave(torch.arange(self.epr, device=dev).repeat(self.world),
+                                      rc_m.reshape(-1).to(dev))
+        perm = torch.argsort(eid, stable=True)
+        xe = recv.index_select(0, perm)
+        per_e = rc_m.sum(0).tolist()
         offs = [0]
-        for e in range(self.epr):
-            offs.append(offs[-1] + sum(rc_m[src][e] for src in range(self.world)))
-        ye = torch.empty_like(xe)
-        self._experts(xe, offs, ye)
+        for n in per_e:
+            offs.append(offs[-1] + n)
+        ye = self._experts_unchecked(xe, offs)
         back = torch.empty_like(recv)
-        back.index_copy_(0, perm_t, ye)
+        back.index_copy_(0, perm, ye)
         ret = torch.empty_like(send)
         if self.world > 1:
             dist.all_to_all_single(ret, back, sc, rc)
         else:
             ret.copy_(back)
-        y = torch.zeros(T, self.H, dtype=torch.float32, device=x.device)
+        y = torch.zeros(T, self.H, dtype=torch.float32, device=dev)
         y.index_add_(0, order // K, ret.float() * wts.view(-1)[order].unsqueeze(1))
         return y.to(torch.bfloat16)
 

@@ -279,6 +279,87 @@ class CheckedWeight:
         """Recompute the checksums after the weight was changed on purpose (e.g. a reload)."""
         self.cs = abft.weight_checksums(self.weight, self.bias, self.mask)
 
+    @classmethod
+    def _assemble(cls, b: torch.Tensor, cs: abft.WeightChecksums, bias, c1, c2, c3) -> "CheckedWeight":
+        self = cls.__new__(cls)
+        self.weight = b
+        self.bias = None if bias is None else bias.detach().float().contiguous()
+        self.cs, self.mask = cs, cs.mask
+        n, k = b.shape
+        self.prod_coef, self.out_coef = abft.coefficients(k, c1, c2, c3)
+        self.n, self.k, self.nb = n, k, cs.nb
+        return self
+
+    @classmethod
+    def on_device(cls, weight: torch.Tensor, bias: Optional[torch.Tensor] = None, c1: float = abft.C1,
+                  c2: float = abft.C2, c3: float = abft.C3) -> "CheckedWeight":
+        """As CheckedWeight(weight, bias), with the checksum rows and block statistics built by one device pass
+        (`sdc_prep_colblock`) instead of fp64 PyTorch reductions: the forward weight after each optimizer step."""
+        w = weight.detach().contiguous()
+        if not w.is_cuda:
+            return cls(w, bias, c1=c1, c2=c2, c3=c3)
+        n, k = w.shape
+        if n % 8 or k % 8:
+            raise ValueError(f"checked GEMM needs n and k multiples of 8 (got n={n}, k={k})")
+        cs = _prep(w, transpose=False)
+        if bias is not None:
+            cs.bsum, cs.bias_max = _bias_sums(bias, n, cs.mask), float(bias.detach().abs().max()) if n else 0.0
+        return cls._assemble(w, cs, bias, c1, c2, c3)
+
+    @classmethod
+    def of_transpose(cls, m: torch.Tensor, c1: float = abft.C1, c2: float = abft.C2,
+                     c3: float = abft.C3) -> "CheckedWeight":
+        """CheckedWeight of B = m^T for m (r, c) bf16, built in one device pass over m (`sdc_prep_rowblock`): the
+        transpose and its checksum rows together. The training guard's W^T (for dX) and X^T (for dW)."""
+        m = m.detach()
+        if m.stride(-1) != 1:
+            m = m.contiguous()
+        if not m.is_cuda:
+            return cls(m.t().contiguous(), c1=c1, c2=c2, c3=c3)
+        r, c = m.shape
+        if r % 8 or c % 8:
+            raise ValueError(f"checked GEMM needs n and k multiples of 8 (got {c} x {r})")
+        cs, t = _prep(m, transpose=True)
+        return cls._assemble(t, cs, None, c1, c2, c3)
+
+
+def _bias_sums(bias: torch.Tensor, n: int, mask) -> torch.Tensor:
+    nb = -(-n // abft.BLOCK)
+    b64 = torch.zeros(nb * abft.BLOCK, dtype=torch.float64, device=bias.device)
+    b64[:n] = bias.detach().double()
+    bb = b64.view(nb, abft.BLOCK)
+    s = abft.sign_vector(mask, device=bias.device)
+    return torch.stack([bb.sum(1), (bb * s.view(1, abft.BLOCK)).sum(1)], dim=1).float().contiguous()
+
+
+_PREP_ACC: dict = {}
+
+
+def _prep(m: torch.Tensor, transpose: bool):
+    """Device checksum data: of B = m (transpose False) or of B = m^T (True, also returning m^T)."""
+    dev = m.device
+    r, c = m.shape
+    mask = abft.sign_mask()
+    nb = -(-(c if transpose else r) // abft.BLOCK)
+    acc = _PREP_ACC.get(dev)
+    if acc is None or acc.numel() < nb * 4:
+        acc = _PREP_ACC[dev] = torch.empty(max(nb * 4, 1024), dtype=torch.float32, device=dev)
+    wstat = torch.empty(nb, 4, dtype=torch.float32, device=dev)
+    lib = _native.lib()
+    if transpose:
+        t = torch.empty(c, r, dtype=torch.bfloat16, device=dev)
+        wc = torch.empty(nb * abft.CS_ROWS, r, dtype=torch.bfloat16, device=dev)
+        _native.check(lib.sdc_prep_rowblock(m.data_ptr(), m.stride(0), r, c, mask[0], mask[1], mask[2], mask[3],
+                                            t.data_ptr(), wc.data_ptr(), wstat.data_ptr(), acc.data_ptr(),
+                                            _stream_ptr(dev)), "checksum prep (rows)")
+        cs = abft.WeightChecksums(n=c, k=r, nb=nb, wc=wc, wstat=wstat, bsum=None, bias_max=0.0, mask=mask)
+        return cs, t
+    wc = torch.empty(nb * abft.CS_ROWS, c, dtype=torch.bfloat16, device=dev)
+    _native.check(lib.sdc_prep_colblock(m.data_ptr(), m.stride(0), r, c, mask[0], mask[1], mask[2], mask[3],
+                                        wc.data_ptr(), wstat.data_ptr(), acc.data_ptr(), _stream_ptr(dev)),
+                  "checksum prep (columns)")
+    return abft.WeightChecksums(n=r, k=c, nb=nb, wc=wc, wstat=wstat, bsum=None, bias_max=0.0, mask=mask)
+
 
 def row_sqnorm(x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     m, k = x.shape
@@ -332,6 +413,68 @@ def checked_linear(x: torch.Tensor, cw: CheckedWeight, state: torch.Tensor, slot
         err.data_ptr(), int(bn), int(max_ctas), inj_row, inj_col, inj_xor,
         None if dbg is None else dbg.data_ptr(), None if seal is None else seal.data_ptr(), _stream_ptr(dev))
     _native.check(rc, "checked GEMM launch")
+    return out
+
+
+class CheckedWeightStack:
+    """The weights of several experts (each (n, k) bf16, no bias) stacked for `checked_linear_grouped`: W as
+    (experts * n, k), the checksum rows as (experts * 6 nb, k), block statistics (experts, nb, 4)."""
+
+    def __init__(self, weights: list, c1: float = abft.C1, c2: float = abft.C2, c3: float = abft.C3):
+        if not weights:
+            raise ValueError("CheckedWeightStack needs at least one weight")
+        n, k = weights[0].shape
+        if any(w.shape != (n, k) or w.dtype != torch.bfloat16 for w in weights):
+            raise ValueError("expert weights must share one (n, k) shape and be bf16")
+        if n % abft.BLOCK or k % 8:
+            raise ValueError(f"grouped checked GEMM needs n a multiple of 128 and k of 8 (got n={n}, k={k})")
+        css = [abft.weight_checksums(w) for w in weights]
+        self.mask = css[0].mask
+        self.weight = torch.cat([w.contiguous() for w in weights]).contiguous()
+        self.wc = torch.cat([c.wc for c in css]).contiguous()
+        self.wstat = torch.cat([c.wstat for c in css]).contiguous()
+        self.experts, self.n, self.k, self.nb = len(weights), n, k, css[0].nb
+        self.prod_coef, self.out_coef = abft.coefficients(k, c1, c2, c3)
+
+    def expert(self, e: int) -> torch.Tensor:
+        return self.weight[e * self.n:(e + 1) * self.n]
+
+
+def checked_linear_grouped(x: torch.Tensor, stack: CheckedWeightStack, gband: torch.Tensor, gcount: torch.Tensor,
+                           state: torch.Tensor, slot: int, row_sq: Optional[torch.Tensor] = None,
+                           out: Optional[torch.Tensor] = None, z_alarm: float = abft.Z_ALARM,
+                           bn: Optional[int] = None, inject: Optional[tuple] = None) -> torch.Tensor:
+    """y[r] = x[r] @ W_e^T for the rows r of every expert e, in one launch with the ABFT check folded into
+    `state[slot]`. x (cap, k) holds the experts' rows grouped on 128-row bands (ops.moe.group or the
+    expert-parallel receive); gband (cap / 128) int32 is the expert of each band and gcount (1,) int32 the bands in
+    use, both on the device: nothing is read back, so the call can be graph-captured. Rows past the bands in use
+    are neither read nor written."""
+    if x.dtype != torch.bfloat16 or x.dim() != 2 or x.stride(1) != 1:
+        raise ValueError("checked_linear_grouped needs a 2-D bf16 x with unit column stride")
+    m, k = x.shape
+    if k != stack.k:
+        raise ValueError(f"x has {k} columns, the weights {stack.k}")
+    dev = x.device
+    if out is None:
+        out = torch.empty(m, stack.n, dtype=torch.bfloat16, device=dev)
+    if m == 0:
+        return out
+    if row_sq is None:
+        row_sq = row_sqnorm(x)
+    lib = _native.lib()
+    ws = workspace(dev, int(lib.sdc_gemm_ws_bytes(m, stack.n)))
+    err = error_word(dev)
+    if bn is None:
+        bn = 256 if stack.n % 256 == 0 and pick_bn(m, stack.n) == 256 else 128
+    s = stack.mask
+    inj_row, inj_col, inj_xor = (-1, -1, 0) if inject is None else (int(inject[0]), int(inject[1]), int(inject[2]))
+    rc = lib.sdc_gemm_bf16_grouped(
+        x.data_ptr(), x.stride(0), stack.weight.data_ptr(), stack.wc.data_ptr(), stack.experts, m, stack.n, k,
+        out.data_ptr(), out.stride(0), row_sq.data_ptr(), stack.wstat.data_ptr(), gband.data_ptr(),
+        gcount.data_ptr(), ws.data_ptr(), state.data_ptr(), int(slot), s[0], s[1], s[2], s[3], float(z_alarm),
+        float(stack.prod_coef), float(stack.out_coef), float(abft.ABS_FLOOR), float(math.sqrt(k)), err.data_ptr(),
+        int(bn), inj_row, inj_col, inj_xor, _stream_ptr(dev))
+    _native.check(rc, "grouped checked GEMM launch")
     return out
 
 

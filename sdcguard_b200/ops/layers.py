@@ -66,6 +66,19 @@ def silu_mul(gu: torch.Tensor, out: Optional[torch.Tensor] = None, row_sq: Optio
     return out, row_sq
 
 
+def silu_mul_bands(gu: torch.Tensor, gcount: torch.Tensor, out: Optional[torch.Tensor] = None,
+                   row_sq: Optional[torch.Tensor] = None):
+    """silu_mul over grouped expert rows: only the first 128 * gcount rows (gcount on the device) are computed."""
+    m, i = gu.shape[0], gu.shape[-1] // 2
+    if out is None:
+        out = torch.empty(m, i, dtype=torch.bfloat16, device=gu.device)
+    if row_sq is None:
+        row_sq = torch.empty(m, dtype=torch.float32, device=gu.device)
+    _native.check(_native.lib().sdc_silu_mul_bf16_bands(gu.data_ptr(), m, i, out.data_ptr(), row_sq.data_ptr(),
+                                                        gcount.data_ptr(), _s(gu)), "silu_mul (bands)")
+    return out, row_sq
+
+
 def compare_rows(a: torch.Tensor, idx: Optional[torch.Tensor], b: torch.Tensor, state_row: torch.Tensor) -> None:
     """Exact comparison of replayed rows b[i] with a[idx[i]] (2-D bf16); mismatches go to `state_row`."""
     s = b.shape[0]

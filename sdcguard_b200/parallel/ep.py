@@ -2,9 +2,11 @@
 
     comm = EPComm(heap, max_tokens, hidden, experts, top_k)
     ids, wts = router_topk(logits, top_k)                  # softmax, top-k, renormalise (Mixtral)
-    x_e, offs = comm.dispatch(x, ids)                      # rows for this rank's experts, grouped by expert
-    y_e = experts(x_e, offs)                               # checked GEMMs per local expert
-    y = comm.combine(y_e, wts)                             # rows back to their tokens, weighted sum over k
+    x_g, row_sq, gband, gcount = comm.dispatch_grouped(x, ids)   # this rank's expert rows on 128-row bands
+    y_g = grouped checked GEMMs (gband, gcount)           # models.moe: both expert GEMMs, one launch each
+    y = comm.combine(y_g, wts)                             # rows back to their tokens, weighted sum over k
+
+`dispatch` (compact rows and host-side offsets, one device-to-host read) is kept for tools that want the counts.
 
 Every row carries its seals (exact 32-bit hash per 128 columns) through both transfers; the receiving side
 re-hashes the bits that arrived. Results fold into `state` rows 0 (dispatch) and 1 (combine).
@@ -66,8 +68,12 @@ class EPComm:
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
         self.counts = torch.zeros(self.world * self.epr, dtype=torch.int32, device=dev)
         self.plan = torch.empty(max_tokens * top_k, 2, dtype=torch.int32, device=dev)
-        self.recv = torch.empty(rows, hidden, dtype=torch.bfloat16, device=dev)
-        self.map = torch.empty(rows, dtype=torch.int32, device=dev)
+        grows = rows + self.epr * 128          # the grouped layout pads each expert to whole 128-row bands
+        self.recv = torch.empty(grows, hidden, dtype=torch.bfloat16, device=dev)
+        self.map = torch.empty(grows, dtype=torch.int32, device=dev)
+        self.row_sq = torch.zeros(grows, dtype=torch.float32, device=dev)
+        self.gband = torch.zeros(grows // 128 + 1, dtype=torch.int32, device=dev)
+        self.gcount = torch.zeros(1, dtype=torch.int32, device=dev)
         self.offs = torch.zeros(self.epr + 1, dtype=torch.int32, device=dev)
         self.state = torch.zeros(2, abft.STATE_COLS, dtype=torch.int64, device=dev)   # 0 dispatch, 1 combine
         self._inj_d = (-1, 0, 0)
@@ -82,9 +88,7 @@ class EPComm:
         """Flip a bit of compact expert-output row `row` as it is pushed back."""
         self._inj_c = (row, col, bit)
 
-    def dispatch(self, x: torch.Tensor, ids: torch.Tensor) -> tuple[torch.Tensor, list[int]]:
-        """x (T, H) bf16, ids (T, k) int32 -> rows for this rank's experts (compact, grouped by local expert) and
-        the per-expert row offsets (host list; one device->host read)."""
+    def _send(self, x: torch.Tensor, ids: torch.Tensor) -> None:
         T = x.shape[0]
         if T > self.cap:
             raise ValueError(f"{T} tokens exceed the capacity {self.cap}")
@@ -98,6 +102,28 @@ class EPComm:
             x.data_ptr(), ids.data_ptr(), T, self.k, self.H, self.world, self.rank, self.epr, self.cap,
             self.counts.data_ptr(), self.plan.data_ptr(), self.d_rows.ptrs, self.d_seal.ptrs, self.d_meta.ptrs,
             self.d_cnt.ptrs, self.flags.ptrs, self.gen.data_ptr(), inj[0], inj[1], inj[2], _s(dev)), "ep dispatch")
+
+    def dispatch_grouped(self, x: torch.Tensor, ids: torch.Tensor):
+        """x (T, H) bf16, ids (T, k) int32 -> (rows, row_sq, gband, gcount): this rank's expert rows grouped by
+        local expert, each expert's rows starting on a 128-row band and padded with zero rows, their sums of
+        squares, the band -> local expert table and the number of bands in use (device tensors; nothing is read
+        back). The input of `ops.gemm.checked_linear_grouped`."""
+        self._send(x, ids)
+        dev = x.device
+        _native.check(_native.lib().sdc_ep_receive_grouped(
+            self.d_rows.local.data_ptr(), self.d_seal.local.data_ptr(), self.d_cnt.local.data_ptr(),
+            self.gen.data_ptr(), self.flags.local.data_ptr(), self.world, self.rank, self.epr, self.cap, self.H,
+            self.recv.data_ptr(), self.map.data_ptr(), self.offs.data_ptr(), self.gband.data_ptr(),
+            self.gcount.data_ptr(), self.row_sq.data_ptr(), self.state[0].data_ptr(), self.err.data_ptr(), _s(dev)),
+            "ep receive (grouped)")
+        return self.recv, self.row_sq, self.gband, self.gcount
+
+    def dispatch(self, x: torch.Tensor, ids: torch.Tensor) -> tuple[torch.Tensor, list[int]]:
+        """x (T, H) bf16, ids (T, k) int32 -> rows for this rank's experts (compact, grouped by local expert) and
+        the per-expert row offsets (host list; one device->host read)."""
+        self._send(x, ids)
+        dev = x.device
+        lib = _native.lib()
         _native.check(lib.sdc_ep_receive(
             self.d_rows.local.data_ptr(), self.d_seal.local.data_ptr(), self.d_cnt.local.data_ptr(),
             self.gen.data_ptr(), self.flags.local.data_ptr(), self.world, self.rank, self.epr, self.cap, self.H,

@@ -140,8 +140,14 @@ class ServeGuard:
         return events
 
     def coverage_report(self) -> dict:
-        checked = sum(1 for t in self.totals.values() if t["checks"] > 0)
-        return {"ops": len(self.totals), "ops_checked": checked,
+        """ops / ops_checked: the checks that run on every step they cover (ABFT GEMMs, replays, transfers) and how
+        many of them have run. The spot check takes one projection per prefill step in turn, so its slots are
+        counted apart (sampled_ops, sampled_ops_run): a short window leaves some of them unvisited by design."""
+        every = {n: t for n, t in self.totals.items() if "spot check" not in n}
+        sampled = {n: t for n, t in self.totals.items() if "spot check" in n}
+        checked = sum(1 for t in every.values() if t["checks"] > 0)
+        return {"ops": len(every), "ops_checked": checked, "sampled_ops": len(sampled),
+                "sampled_ops_run": sum(1 for t in sampled.values() if t["checks"] > 0),
                 "checks": sum(t["checks"] for t in self.totals.values()),
                 "unjudged": sum(t["unjudged"] for t in self.totals.values()),
                 "alarms": sum(t["alarms"] for t in self.totals.values()),

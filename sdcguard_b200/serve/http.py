@@ -140,6 +140,7 @@ class Server:
             "# TYPE sdcguard_checks_total counter", f"sdcguard_checks_total {cov['checks']}",
             f"sdcguard_alarms_total {cov['alarms']}", f"sdcguard_unjudged_total {cov['unjudged']}",
             f"sdcguard_ops_total {cov['ops']}", f"sdcguard_ops_checked {cov['ops_checked']}",
+            f"sdcguard_sampled_ops_total {cov['sampled_ops']}", f"sdcguard_sampled_ops_run {cov['sampled_ops_run']}",
             f"sdcguard_alarm_line {g.z_alarm}", f"sdcguard_worst_clean_z {cov['worst_clean_z']}",
             f"sdcguard_polls_total {c['polls']}", f"sdcguard_requests_total {c['requests']}",
             f"sdcguard_prompt_tokens_total {c['prompt_tokens']}",

@@ -96,7 +96,7 @@ def campaign(eng, model, moe, comm, rank, world, trials, seed, dev):
             culprit = t % world
             if kind == "expert_gemm":
                 if rank == culprit:
-                    layer.inject_next("up0", rng.randrange(4), rng.randrange(2 * model.cfg.intermediate),
+                    layer.inject_next("up", rng.randrange(4), rng.randrange(2 * model.cfg.intermediate),
                                       rng.choice([24, 27, 29, 30]))
             elif kind == "dispatch":
                 if rank == culprit:
