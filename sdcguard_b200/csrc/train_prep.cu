@@ -1,0 +1,234 @@
+// Checksum rows of the training GEMMs' B operands, built on the device (sm_100a).
+//
+// The checked GEMM computes C = A @ B^T with B an (N, K) row-major bf16 matrix and needs, per block of 128 rows of
+// B, the plain and signed sums of those rows (each split into three bf16 parts) and four block statistics. In
+// training, B changes every step: W after each optimizer step (forward), W^T for dX = dY W, and X^T for
+// dW = dY^T X. Two kernels build these in one pass over the source, in the layout sdcguard_b200.numerics.abft
+// defines (wc: 6 rows per block, plain hi/mid/lo then signed hi/mid/lo; wstat: ||B_b||_F, ||plain||_2, ||signed||_2,
+// max |B_b|):
+//
+//   rowblock_kernel : source M (R, C) and B = M^T (C, R): the sums run along each row of M inside a 128-column
+//                     block (one warp per (row, block), fp64), so W^T's and X^T's checksum rows come from W and X
+//                     as they are; the same pass writes B = M^T through a shared-memory tile when asked.
+//   colblock_kernel : source M = B (N, K): the sums run down 128-row blocks (the forward weight after an update).
+//
+// Sums are in fp64 and split with round-to-nearest-even conversions from double (hi + mid + lo carries about 24
+// significant bits). The statistics are accumulated in fp32 with atomics (order-dependent in the last bits; they
+// only scale the noise model), then finalized by a one-CTA kernel. This replaces per-step fp64 PyTorch reductions
+// and transposes (several launches and an fp64 copy of each operand) with two or three launches per operand.
+//
+// Reference: the reference's training check builds its expected side per step in its Triton kernels
+// (src/sdcguard/guard.py:497 `_checked_backward`, checksum.py:160 `_split3`).
+#include "common.cuh"
+
+namespace sdc {
+namespace prep {
+
+constexpr int BLK = 128;
+
+__device__ __forceinline__ void split3_store(double v, __nv_bfloat16* dst, long long stride) {
+  const __nv_bfloat16 hi = __double2bfloat16(v);
+  const double r = v - static_cast<double>(__bfloat162float(hi));
+  const __nv_bfloat16 mid = __double2bfloat16(r);
+  const __nv_bfloat16 lo = __double2bfloat16(r - static_cast<double>(__bfloat162float(mid)));
+  dst[0] = hi;
+  dst[stride] = mid;
+  dst[2 * stride] = lo;
+}
+
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+  for (int m = 16; m > 0; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
+  return v;
+}
+__device__ __forceinline__ float warp_sum_f(float v) {
+#pragma unroll
+  for (int m = 16; m > 0; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
+  return v;
+}
+__device__ __forceinline__ float warp_max_f(float v) {
+#pragma unroll
+  for (int m = 16; m > 0; m >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, m));
+  return v;
+}
+
+struct Signs {
+  uint32_t w[4];
+};
+
+// Adds a CTA's block statistics (squares, plain^2, signed^2; max |x|) into acc[b] (zeroed by the launcher).
+__device__ __forceinline__ void add_stats(float* acc, float sq, float pl, float sg, float mx, float* red) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  sq = warp_sum_f(sq);
+  pl = warp_sum_f(pl);
+  sg = warp_sum_f(sg);
+  mx = warp_max_f(mx);
+  if (lane == 0) {
+    red[warp * 4 + 0] = sq;
+    red[warp * 4 + 1] = pl;
+    red[warp * 4 + 2] = sg;
+    red[warp * 4 + 3] = mx;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float a = 0.f, b = 0.f, c = 0.f, d = 0.f;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) {
+      a += red[w * 4];
+      b += red[w * 4 + 1];
+      c += red[w * 4 + 2];
+      d = fmaxf(d, red[w * 4 + 3]);
+    }
+    atomicAdd(acc + 0, a);
+    atomicAdd(acc + 1, b);
+    atomicAdd(acc + 2, c);
+    atomicMax(reinterpret_cast<unsigned int*>(acc + 3), __float_as_uint(d));   // non-negative floats order as ints
+  }
+}
+
+// Grid (ceil(R / 64), nb), 256 threads. Tile: 64 rows of M x the 128 columns of block b.
+__global__ void __launch_bounds__(256) rowblock_kernel(const __nv_bfloat16* __restrict__ M, long long ldm, int R,
+                                                       int C, Signs sg, __nv_bfloat16* __restrict__ T,
+                                                       __nv_bfloat16* __restrict__ wc, float* __restrict__ acc) {
+  __shared__ __align__(16) __nv_bfloat16 tile[64][BLK + 8];
+  __shared__ float red[32];
+  const int r0 = blockIdx.x * 64, b = blockIdx.y, c0 = b * BLK;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // load 64 x 128 (16-byte chunks, zero outside the matrix)
+  for (int i = threadIdx.x; i < 64 * 16; i += 256) {
+    const int rr = i >> 4, ch = i & 15;
+    const int r = r0 + rr, c = c0 + ch * 8;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (r < R && c < C) v = *reinterpret_cast<const uint4*>(M + static_cast<long long>(r) * ldm + c);
+    *reinterpret_cast<uint4*>(&tile[rr][ch * 8]) = v;
+  }
+  __syncthreads();
+  // sums along the row inside the block: warp w takes rows w, w + 8, ...; lane l holds columns 4l .. 4l + 3
+  const uint32_t sbits = (sg.w[lane >> 3] >> ((lane & 7) * 4)) & 0xfu;
+  float sq = 0.f, pl2 = 0.f, sg2 = 0.f, mx = 0.f;
+  for (int rr = warp; rr < 64; rr += 8) {
+    const int r = r0 + rr;
+    double p = 0.0, s = 0.0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float x = __bfloat162float(tile[rr][lane * 4 + j]);
+      p += x;
+      s += ((sbits >> j) & 1u) ? -static_cast<double>(x) : static_cast<double>(x);
+      sq = fmaf(x, x, sq);
+      mx = fmaxf(mx, fabsf(x));
+    }
+    p = warp_sum_d(p);
+    s = warp_sum_d(s);
+    if (r < R) {
+      if (lane == 0) split3_store(p, wc + static_cast<long long>(b * 6) * R + r, R);
+      if (lane == 1) split3_store(s, wc + static_cast<long long>(b * 6 + 3) * R + r, R);
+      if (lane == 0) {
+        pl2 += static_cast<float>(p * p);
+        sg2 += static_cast<float>(s * s);
+      }
+    }
+  }
+  if (T != nullptr) {
+    // T[c][r0 .. r0 + 63] for the block's 128 columns: 8 rows of the tile per 16-byte chunk
+    for (int i = threadIdx.x; i < BLK * 8; i += 256) {
+      const int cc = i >> 3, ch = i & 7;
+      const int c = c0 + cc, r = r0 + ch * 8;
+      if (c >= C || r >= R) continue;
+      __align__(16) __nv_bfloat16 v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = tile[ch * 8 + j][cc];
+      __nv_bfloat16* dst = T + static_cast<long long>(c) * R + r;
+      if (r + 8 <= R && (R % 8) == 0) {
+        *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(v);
+      } else {
+        for (int j = 0; j < 8 && r + j < R; ++j) dst[j] = v[j];
+      }
+    }
+  }
+  add_stats(acc + b * 4, sq, pl2, sg2, mx, red);
+}
+
+// Grid (ceil(C / 64), nb), 256 threads. Tile: the 128 rows of block b x 64 columns; thread (q, c) sums rows
+// 32q .. 32q + 31 of column c, the four quarters are added in order.
+__global__ void __launch_bounds__(256) colblock_kernel(const __nv_bfloat16* __restrict__ M, long long ldm, int R,
+                                                       int C, Signs sg, __nv_bfloat16* __restrict__ wc,
+                                                       float* __restrict__ acc) {
+  __shared__ double part[2][4][64];
+  __shared__ float red[32];
+  const int cl = threadIdx.x & 63, q = threadIdx.x >> 6;
+  const int c = blockIdx.x * 64 + cl, b = blockIdx.y;
+  double p = 0.0, s = 0.0;
+  float sq = 0.f, mx = 0.f;
+  if (c < C) {
+    for (int j = 0; j < 32; ++j) {
+      const int rr = q * 32 + j, r = b * BLK + rr;
+      if (r >= R) break;
+      const float x = __bfloat162float(M[static_cast<long long>(r) * ldm + c]);
+      p += x;
+      s += ((sg.w[rr >> 5] >> (rr & 31)) & 1u) ? -static_cast<double>(x) : static_cast<double>(x);
+      sq = fmaf(x, x, sq);
+      mx = fmaxf(mx, fabsf(x));
+    }
+  }
+  part[0][q][cl] = p;
+  part[1][q][cl] = s;
+  __syncthreads();
+  float pl2 = 0.f, sg2 = 0.f;
+  if (q == 0 && c < C) {
+    const double P = ((part[0][0][cl] + part[0][1][cl]) + part[0][2][cl]) + part[0][3][cl];
+    const double S = ((part[1][0][cl] + part[1][1][cl]) + part[1][2][cl]) + part[1][3][cl];
+    split3_store(P, wc + static_cast<long long>(b * 6) * C + c, C);
+    split3_store(S, wc + static_cast<long long>(b * 6 + 3) * C + c, C);
+    pl2 = static_cast<float>(P * P);
+    sg2 = static_cast<float>(S * S);
+  }
+  add_stats(acc + b * 4, sq, pl2, sg2, mx, red);
+}
+
+__global__ void finalize_kernel(const float* __restrict__ acc, int nb, float* __restrict__ wstat) {
+  for (int b = threadIdx.x; b < nb; b += blockDim.x) {
+    wstat[b * 4 + 0] = sqrtf(acc[b * 4 + 0]);
+    wstat[b * 4 + 1] = sqrtf(acc[b * 4 + 1]);
+    wstat[b * 4 + 2] = sqrtf(acc[b * 4 + 2]);
+    wstat[b * 4 + 3] = acc[b * 4 + 3];
+  }
+}
+
+}  // namespace prep
+}  // namespace sdc
+
+extern "C" {
+
+// Checksum data of B = M^T for M (R, C) bf16 row-major (ld elements): wc (6 nb, R) bf16 with nb = ceil(C / 128),
+// wstat (nb, 4) fp32, and B itself into T (C, R) when T is not null. acc: device scratch of nb * 4 floats.
+int sdc_prep_rowblock(const void* M, long long ldm, int R, int C, unsigned s0, unsigned s1, unsigned s2, unsigned s3,
+                      void* T, void* wc, float* wstat, float* acc, void* stream) {
+  if (R <= 0 || C <= 0) return 0;
+  if (C % 8 || ldm % 8) return -1;
+  auto st = static_cast<cudaStream_t>(stream);
+  const int nb = (C + 127) / 128;
+  cudaError_t e = cudaMemsetAsync(acc, 0, sizeof(float) * 4 * nb, st);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  sdc::prep::Signs sg{{s0, s1, s2, s3}};
+  sdc::prep::rowblock_kernel<<<dim3((R + 63) / 64, nb), 256, 0, st>>>(
+      static_cast<const __nv_bfloat16*>(M), ldm, R, C, sg, static_cast<__nv_bfloat16*>(T),
+      static_cast<__nv_bfloat16*>(wc), acc);
+  sdc::prep::finalize_kernel<<<1, 256, 0, st>>>(acc, nb, wstat);
+  return static_cast<int>(cudaGetLastError());
+}
+
+// Checksum data of B = M for M (R, C) bf16 row-major: wc (6 nb, C) with nb = ceil(R / 128), wstat (nb, 4).
+int sdc_prep_colblock(const void* M, long long ldm, int R, int C, unsigned s0, unsigned s1, unsigned s2, unsigned s3,
+                      void* wc, float* wstat, float* acc, void* stream) {
+  if (R <= 0 || C <= 0) return 0;
+  auto st = static_cast<cudaStream_t>(stream);
+  const int nb = (R + 127) / 128;
+  cudaError_t e = cudaMemsetAsync(acc, 0, sizeof(float) * 4 * nb, st);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  sdc::prep::Signs sg{{s0, s1, s2, s3}};
+  sdc::prep::colblock_kernel<<<dim3((C + 63) / 64, nb), 256, 0, st>>>(
+      static_cast<const __nv_bfloat16*>(M), ldm, R, C, sg, static_cast<__nv_bfloat16*>(wc), acc);
+  sdc::prep::finalize_kernel<<<1, 256, 0, st>>>(acc, nb, wstat);
+  return static_cast<int>(cudaGetLastError());
+}
+
+}  // extern "C"

@@ -12,7 +12,9 @@ Results fold into a device state table; the host reads it once per checked step.
     guard.events                                # SDCEvents (detector "checksum", detail: layer, phase, row, block)
 
 The backward operands are laid out for the kernel's C = A B^T form: dX = dY (W^T)^T with W^T materialised, and
-dW = (dY^T) (X^T)^T with dY^T and X^T materialised; the checksum rows of W^T and of X^T are built for the step.
+dW = (dY^T) (X^T)^T with dY^T and X^T materialised. W^T and X^T come with their checksum rows from one device pass
+over W and X (`CheckedWeight.of_transpose`, `csrc/train_prep.cu`), and the forward weight's checksum rows after an
+optimizer step from one pass over W (`CheckedWeight.on_device`): no fp64 PyTorch reductions on the training path.
 Shapes the kernel does not take (dimensions not multiples of 8) run unchecked and are counted in `coverage()`.
 
 Reference: `SDCGuard` (src/sdcguard/guard.py:788): `protect` :1096 swaps nn.Linear for a checked-linear autograd
@@ -35,7 +37,9 @@ PHASES = ("fwd", "dx", "dw")
 
 
 class _Cache:
-    """Checksum data of one weight, rebuilt when the weight's version changes (after an optimizer step)."""
+    """Checksum data of one weight, rebuilt when the weight's version changes (after an optimizer step). A weight
+    kept in fp32 (mixed precision under autocast) is checked as its bf16 copy, which is what autocast would feed the
+    GEMM; the copy is made once per version."""
 
     def __init__(self):
         self.key = None
@@ -45,14 +49,16 @@ class _Cache:
     def get(self, w: torch.Tensor, b: Optional[torch.Tensor]):
         key = (w.data_ptr(), w._version, None if b is None else b._version)
         if key != self.key:
-            self.cw = gemm.CheckedWeight(w.detach(), b)
+            wb = w.detach() if w.dtype == torch.bfloat16 else w.detach().to(torch.bfloat16)
+            bb = None if b is None else b.detach()
+            self.cw = gemm.CheckedWeight.on_device(wb, bb)
             self.cwT = None
             self.key = key
         return self.cw
 
-    def get_t(self, w: torch.Tensor):
+    def get_t(self):
         if self.cwT is None:
-            self.cwT = gemm.CheckedWeight(w.detach().t().contiguous())
+            self.cwT = gemm.CheckedWeight.of_transpose(self.cw.weight)
         return self.cwT
 
 
@@ -65,9 +71,11 @@ class _CheckedLinearFn(torch.autograd.Function):
         cw = mod.cache.get(w, b)
         y = gemm.checked_linear(x2, cw, g.table.state, mod.slots["fwd"], z_alarm=g.z_alarm,
                                 inject=g._take_inject(mod.name, "fwd"))
-        ctx.save_for_backward(x2, w)
+        ctx.save_for_backward(x2, cw.weight)
+        ctx.wdtype = w.dtype
         ctx.mod = mod
         ctx.has_bias = b is not None
+        ctx.bdtype = None if b is None else b.dtype
         ctx.xshape = x.shape
         return y.view(*x.shape[:-1], w.shape[0])
 
@@ -80,18 +88,19 @@ class _CheckedLinearFn(torch.autograd.Function):
         m = dy2.shape[0]
         dx = dw = db = None
         if ctx.needs_input_grad[0]:
-            dx = gemm.checked_linear(dy2, mod.cache.get_t(w), g.table.state, mod.slots["dx"], z_alarm=g.z_alarm,
+            dx = gemm.checked_linear(dy2, mod.cache.get_t(), g.table.state, mod.slots["dx"], z_alarm=g.z_alarm,
                                      inject=g._take_inject(mod.name, "dx")).view(ctx.xshape)
         if ctx.needs_input_grad[1]:
             if m % 8 == 0:
-                xt = gemm.CheckedWeight(x2.t().contiguous())        # (k, m): rows = output columns of dW
+                xt = gemm.CheckedWeight.of_transpose(x2)            # X^T (k, m): rows = output columns of dW
                 dw = gemm.checked_linear(dy2.t().contiguous(), xt, g.table.state, mod.slots["dw"],
                                          z_alarm=g.z_alarm, inject=g._take_inject(mod.name, "dw"))
             else:
                 dw = dy2.t() @ x2
                 g.unchecked += 1
+            dw = dw.to(ctx.wdtype)
         if ctx.has_bias and ctx.needs_input_grad[2]:
-            db = dy2.float().sum(0).to(dy2.dtype)
+            db = dy2.float().sum(0).to(ctx.bdtype)
         return dx, dw, db, None
 
 
@@ -112,14 +121,19 @@ class CheckedLinear(torch.nn.Module):
 
     def forward(self, x):
         g = self.guard
-        ok = (g.active and x.is_cuda and x.dtype == torch.bfloat16 and self.weight.dtype == torch.bfloat16
-              and self.in_features % 8 == 0 and self.out_features % 8 == 0)
+        # bf16 operands, or fp32 ones under a bf16 autocast region (checked as the bf16 copies autocast would use)
+        amp = x.is_cuda and torch.is_autocast_enabled("cuda") and torch.get_autocast_dtype("cuda") == torch.bfloat16
+        ok = (g.active and x.is_cuda and self.in_features % 8 == 0 and self.out_features % 8 == 0 and
+              ((x.dtype == torch.bfloat16 and self.weight.dtype == torch.bfloat16) or
+               (amp and x.dtype in (torch.float32, torch.bfloat16) and self.weight.dtype == torch.float32)))
         if not ok:
             if g.active:
                 g.unchecked += 1
             return F.linear(x, self.weight, self.bias)
         g.checked_calls += 1
-        return _CheckedLinearFn.apply(x, self.weight, self.bias, self)
+        xb = x if x.dtype == torch.bfloat16 else x.to(torch.bfloat16)
+        with torch.autocast("cuda", enabled=False):
+            return _CheckedLinearFn.apply(xb, self.weight, self.bias, self)
 
 
 class SDCGuard:
