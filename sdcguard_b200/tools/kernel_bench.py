@@ -201,6 +201,47 @@ def bench_prefill(seqs, length, nq, nkv, iters):
             "us": round(ms * 1e3, 1), "tflops": round(fl / ms / 1e9, 1)}
 
 
+def bench_moe(tokens, experts, top_k, hidden, inter, iters):
+    """Grouped checked gate_up GEMM of a MoE layer (every expert in one launch, rows grouped on the device) against
+    PyTorch's grouped GEMM (`torch._grouped_mm`, unchecked) on the same grouped rows, plus the grouping kernels."""
+    from ..ops import gemm, moe
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(0)
+    x = torch.randn(tokens, hidden, device=dev, generator=g).bfloat16()
+    ids = torch.stack([torch.randperm(experts, device=dev, generator=g)[:top_k] for _ in range(tokens)]).int()
+    ws = [(torch.randn(2 * inter, hidden, device=dev, generator=g) * 0.02).bfloat16() for _ in range(experts)]
+    stack = gemm.CheckedWeightStack(ws)
+    grp = moe.Grouping(tokens, top_k, experts, hidden, dev)
+    xg, rsq = grp.group(x, ids)
+    st = gemm.StateTable(dev, 2)
+    s = st.add("moe (ABFT GEMM)", stack.nb)
+    out = torch.empty(grp.cap, 2 * inter, dtype=torch.bfloat16, device=dev)
+    ms = _timed(lambda: gemm.checked_linear_grouped(xg, stack, grp.gband, grp.gcount, st.state, s, row_sq=rsq,
+                                                    out=out), iters)
+    mg = _timed(lambda: grp.group(x, ids), iters)
+    rows = grp.expert_rows()
+    pairs = tokens * top_k
+    fl = 2.0 * pairs * hidden * 2 * inter
+    r = {"kernel": "grouped_checked_gemm", "tokens": tokens, "experts": experts, "top_k": top_k, "hidden": hidden,
+         "inter": inter, "padded_rows": int(grp.gcount.item()) * 128, "us": round(ms * 1e3, 1),
+         "tflops": round(fl / ms / 1e9, 1), "grouping_us": round(mg * 1e3, 1),
+         "weight_gbs": round(stack.weight.numel() * 2 / ms / 1e6, 1)}
+    if hasattr(torch, "_grouped_mm"):
+        # the same grouped rows, compact (no band padding), through PyTorch's grouped GEMM
+        xc = torch.cat([xg[a:a + n] for a, n in rows])
+        ends = torch.tensor([sum(n for _, n in rows[:e + 1]) for e in range(experts)], dtype=torch.int32,
+                            device=dev)
+        wt = torch.stack(ws).transpose(1, 2)
+        try:
+            mt = _timed(lambda: torch._grouped_mm(xc, wt, offs=ends), iters)
+            r.update(torch_grouped_mm_us=round(mt * 1e3, 1), torch_grouped_mm_tflops=round(fl / mt / 1e9, 1))
+        except (RuntimeError, TypeError, NotImplementedError) as e:
+            r["torch_grouped_mm"] = f"unavailable: {type(e).__name__}: {str(e)[:120]}"
+    row = st.read()[0]
+    r.update(worst_clean_z=round(row["z"], 4), unjudged=row["unjudged"])
+    return r
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(prog="python -m sdcguard_b200.tools.kernel_bench")
     sub = ap.add_subparsers(dest="what", required=True)
@@ -228,7 +269,13 @@ def main(argv=None) -> int:
     c.add_argument("--len", type=int, default=2048)
     c.add_argument("--nq", type=int, default=16)
     c.add_argument("--nkv", type=int, default=8)
-    for p in (a, b, c, f, t):
+    mo = sub.add_parser("moe")
+    mo.add_argument("--tokens", type=int, default=256)
+    mo.add_argument("--experts", type=int, default=8)
+    mo.add_argument("--top-k", type=int, default=2)
+    mo.add_argument("--hidden", type=int, default=4096)
+    mo.add_argument("--inter", type=int, default=14336)
+    for p in (a, b, c, f, t, mo):
         p.add_argument("--iters", type=int, default=10)
     args = ap.parse_args(argv)
     if args.what == "gemm":
@@ -239,6 +286,8 @@ def main(argv=None) -> int:
         r = bench_fp8(args.m, args.n, args.k, args.iters)
     elif args.what == "decode":
         r = bench_decode(args.batch, args.nq, args.nkv, args.ctx, args.iters)
+    elif args.what == "moe":
+        r = bench_moe(args.tokens, args.experts, args.top_k, args.hidden, args.inter, args.iters)
     else:
         r = bench_prefill(args.seqs, args.len, args.nq, args.nkv, args.iters)
     peaks = measured_peaks()

@@ -3,7 +3,7 @@ dW = dY^T X) through the checked sm_100a GEMM, so all three carry the ABFT check
 Results fold into a device state table; the host reads it once per checked step.
 
     guard = SDCGuard(check_every=10)
-    guard.protect(model)                        # swaps nn.Linear modules (bf16, CUDA) for CheckedLinear
+    guard.protect(model)                        # every nn.Linear's forward goes through the guard (class swap)
     for step, batch in enumerate(loader):
         with guard.at_step(step):               # checked on steps where step % check_every == 0
             loss = model(batch).loss
@@ -104,11 +104,13 @@ class _CheckedLinearFn(torch.autograd.Function):
         return dx, dw, db, None
 
 
-class CheckedLinear(torch.nn.Module):
+class CheckedLinear:
+    """The guard's state of one protected linear layer: its name, check slots and checksum cache. The layer object
+    itself stays in the model (train.swap gives it a subclass whose forward calls `forward` here), so copies,
+    pickles and references to the layer behave as they did."""
+
     def __init__(self, lin: torch.nn.Linear, guard: "SDCGuard", name: str):
-        super().__init__()
-        self.weight = lin.weight
-        self.bias = lin.bias
+        self.layer = lin
         self.in_features, self.out_features = lin.in_features, lin.out_features
         self.guard = guard
         self.name = name
@@ -119,21 +121,26 @@ class CheckedLinear(torch.nn.Module):
         for ph in PHASES:
             self.slots[ph] = guard.table.add(f"{name}.{ph} (ABFT GEMM)", nbs[ph])
 
-    def forward(self, x):
+    @property
+    def weight(self):
+        return self.layer.weight
+
+    def forward(self, layer: torch.nn.Linear, x):
         g = self.guard
+        w, b = layer.weight, layer.bias
         # bf16 operands, or fp32 ones under a bf16 autocast region (checked as the bf16 copies autocast would use)
         amp = x.is_cuda and torch.is_autocast_enabled("cuda") and torch.get_autocast_dtype("cuda") == torch.bfloat16
         ok = (g.active and x.is_cuda and self.in_features % 8 == 0 and self.out_features % 8 == 0 and
-              ((x.dtype == torch.bfloat16 and self.weight.dtype == torch.bfloat16) or
-               (amp and x.dtype in (torch.float32, torch.bfloat16) and self.weight.dtype == torch.float32)))
+              ((x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16) or
+               (amp and x.dtype in (torch.float32, torch.bfloat16) and w.dtype == torch.float32)))
         if not ok:
             if g.active:
                 g.unchecked += 1
-            return F.linear(x, self.weight, self.bias)
+            return F.linear(x, w, b)
         g.checked_calls += 1
         xb = x if x.dtype == torch.bfloat16 else x.to(torch.bfloat16)
         with torch.autocast("cuda", enabled=False):
-            return _CheckedLinearFn.apply(xb, self.weight, self.bias, self)
+            return _CheckedLinearFn.apply(xb, w, b, self)
 
 
 class SDCGuard:
@@ -160,13 +167,22 @@ class SDCGuard:
         if self.device.type == "cuda":
             from ..ops import verify
             self.verification = verify.verified(self.device)   # the kernels reproduced their references here
-        for pname, parent in list(model.named_modules()):
-            for cname, child in list(parent.named_children()):
-                if isinstance(child, torch.nn.Linear):
-                    full = f"{pname}.{cname}" if pname else cname
-                    mod = CheckedLinear(child, self, full)
-                    setattr(parent, cname, mod)
-                    self.modules.append(mod)
+        from . import swap
+        for name, mod in list(model.named_modules()):
+            if isinstance(mod, torch.nn.Linear) and not swap.is_checked(mod):
+                st = CheckedLinear(mod, self, name)
+                swap.take_over(mod, st)
+                self.modules.append(st)
+        return model
+
+    def release(self, model: torch.nn.Module) -> torch.nn.Module:
+        """Undo protect(): every layer this guard took over gets its original class back."""
+        from . import swap
+        mine = {id(st) for st in self.modules}
+        for _, mod in model.named_modules():
+            st = swap.state_of(mod)
+            if st is not None and id(st) in mine:
+                swap.give_back(mod)
         return model
 
     def should_check(self, step: int) -> bool:
