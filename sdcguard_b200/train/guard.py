@@ -62,46 +62,61 @@ class _Cache:
         return self.cwT
 
 
+def _fwd_gemm(mod: "CheckedLinear", x, w, b):
+    """The checked forward GEMM of a protected layer: x (..., k) bf16 -> (..., n) bf16, with the bf16 weight used
+    (a copy of an fp32 weight, made once per version)."""
+    g = mod.guard
+    k = x.shape[-1]
+    x2 = x.reshape(-1, k).contiguous()
+    cw = mod.cache.get(w, b)
+    y = gemm.checked_linear(x2, cw, g.table.state, mod.slots["fwd"], z_alarm=g.z_alarm,
+                            inject=g._take_inject(mod.name, "fwd"))
+    return y.view(*x.shape[:-1], w.shape[0]), x2, cw.weight
+
+
+def _bwd_gemms(mod: "CheckedLinear", dy, x2, wb, xshape, need_x: bool, need_w: bool, need_b: bool):
+    """dX = dY W and dW = dY^T X on the checked GEMM (dW unchecked when the token count is not a multiple of 8),
+    db = the column sums of dY in fp32. wb: the bf16 weight of the forward."""
+    g = mod.guard
+    n = wb.shape[0]
+    dy2 = dy.reshape(-1, n).to(torch.bfloat16).contiguous()
+    m = dy2.shape[0]
+    dx = dw = db = None
+    if need_x:
+        dx = gemm.checked_linear(dy2, mod.cache.get_t(), g.table.state, mod.slots["dx"], z_alarm=g.z_alarm,
+                                 inject=g._take_inject(mod.name, "dx")).view(xshape)
+    if need_w:
+        if m % 8 == 0:
+            xt = gemm.CheckedWeight.of_transpose(x2)            # X^T (k, m): rows = output columns of dW
+            dw = gemm.checked_linear(dy2.t().contiguous(), xt, g.table.state, mod.slots["dw"],
+                                     z_alarm=g.z_alarm, inject=g._take_inject(mod.name, "dw"))
+        else:
+            dw = dy2.t() @ x2
+            g.unchecked += 1
+    if need_b:
+        db = dy2.float().sum(0)
+    return dx, dw, db
+
+
 class _CheckedLinearFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, w, b, mod):
-        g = mod.guard
-        k = x.shape[-1]
-        x2 = x.reshape(-1, k).contiguous()
-        cw = mod.cache.get(w, b)
-        y = gemm.checked_linear(x2, cw, g.table.state, mod.slots["fwd"], z_alarm=g.z_alarm,
-                                inject=g._take_inject(mod.name, "fwd"))
-        ctx.save_for_backward(x2, cw.weight)
+        y, x2, wb = _fwd_gemm(mod, x, w, b)
+        ctx.save_for_backward(x2, wb)
         ctx.wdtype = w.dtype
         ctx.mod = mod
         ctx.has_bias = b is not None
         ctx.bdtype = None if b is None else b.dtype
         ctx.xshape = x.shape
-        return y.view(*x.shape[:-1], w.shape[0])
+        return y
 
     @staticmethod
     def backward(ctx, dy):
-        x2, w = ctx.saved_tensors
-        mod, g = ctx.mod, ctx.mod.guard
-        n = w.shape[0]
-        dy2 = dy.reshape(-1, n).contiguous()
-        m = dy2.shape[0]
-        dx = dw = db = None
-        if ctx.needs_input_grad[0]:
-            dx = gemm.checked_linear(dy2, mod.cache.get_t(), g.table.state, mod.slots["dx"], z_alarm=g.z_alarm,
-                                     inject=g._take_inject(mod.name, "dx")).view(ctx.xshape)
-        if ctx.needs_input_grad[1]:
-            if m % 8 == 0:
-                xt = gemm.CheckedWeight.of_transpose(x2)            # X^T (k, m): rows = output columns of dW
-                dw = gemm.checked_linear(dy2.t().contiguous(), xt, g.table.state, mod.slots["dw"],
-                                         z_alarm=g.z_alarm, inject=g._take_inject(mod.name, "dw"))
-            else:
-                dw = dy2.t() @ x2
-                g.unchecked += 1
-            dw = dw.to(ctx.wdtype)
-        if ctx.has_bias and ctx.needs_input_grad[2]:
-            db = dy2.float().sum(0).to(ctx.bdtype)
-        return dx, dw, db, None
+        x2, wb = ctx.saved_tensors
+        need_b = ctx.has_bias and ctx.needs_input_grad[2]
+        dx, dw, db = _bwd_gemms(ctx.mod, dy, x2, wb, ctx.xshape, ctx.needs_input_grad[0], ctx.needs_input_grad[1],
+                                need_b)
+        return (dx, None if dw is None else dw.to(ctx.wdtype), None if db is None else db.to(ctx.bdtype), None)
 
 
 class CheckedLinear:
@@ -125,6 +140,37 @@ class CheckedLinear:
     def weight(self):
         return self.layer.weight
 
+    # ---- the operators of train.compiled call these (under torch.compile, and on DTensor local shards)
+    @property
+    def state_id(self) -> int:
+        sid = getattr(self, "_sid", None)
+        if sid is None:
+            from . import compiled
+            sid = self._sid = compiled.register(self)
+        return sid
+
+    def runnable(self, x, w) -> bool:
+        ok = (self.guard.active and x.is_cuda and x.shape[-1] % 8 == 0 and w.shape[0] % 8 == 0 and
+              x.dtype in (torch.bfloat16, torch.float32) and w.dtype in (torch.bfloat16, torch.float32))
+        if self.guard.active and not ok:
+            self.guard.unchecked += 1
+        return ok
+
+    def checked_forward(self, x, w, b):
+        self.guard.checked_calls += 1
+        y, _, _ = _fwd_gemm(self, x.to(torch.bfloat16), w, b)
+        return y.to(x.dtype)
+
+    def checked_backward(self, gy, x, w, need_x, need_w, need_b):
+        c = self.cache
+        if c.cw is None or c.key[:2] != (w.data_ptr(), w._version):
+            c.get(w, None)                       # the forward's cache entry is normally still current
+        xb = x.to(torch.bfloat16)
+        dx, dw, db = _bwd_gemms(self, gy, xb.reshape(-1, x.shape[-1]).contiguous(), self.cache.cw.weight, x.shape,
+                                need_x, need_w, need_b)
+        return (None if dx is None else dx.to(x.dtype), None if dw is None else dw.to(w.dtype),
+                None if db is None else db.to(w.dtype))
+
     def forward(self, layer: torch.nn.Linear, x):
         g = self.guard
         w, b = layer.weight, layer.bias
@@ -137,6 +183,9 @@ class CheckedLinear:
             if g.active:
                 g.unchecked += 1
             return F.linear(x, w, b)
+        if torch.compiler.is_compiling():
+            from . import compiled
+            return compiled.checked_linear(x, w, b, self.state_id)
         g.checked_calls += 1
         xb = x if x.dtype == torch.bfloat16 else x.to(torch.bfloat16)
         with torch.autocast("cuda", enabled=False):
