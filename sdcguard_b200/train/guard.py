@@ -69,6 +69,7 @@ def _fwd_gemm(mod: "CheckedLinear", x, w, b):
     k = x.shape[-1]
     x2 = x.reshape(-1, k).contiguous()
     cw = mod.cache.get(w, b)
+    g._keep(mod.slots["fwd"], cw)
     y = gemm.checked_linear(x2, cw, g.table.state, mod.slots["fwd"], z_alarm=g.z_alarm,
                             inject=g._take_inject(mod.name, "fwd"))
     return y.view(*x.shape[:-1], w.shape[0]), x2, cw.weight
@@ -83,11 +84,13 @@ def _bwd_gemms(mod: "CheckedLinear", dy, x2, wb, xshape, need_x: bool, need_w: b
     m = dy2.shape[0]
     dx = dw = db = None
     if need_x:
+        g._keep(mod.slots["dx"], mod.cache.get_t())
         dx = gemm.checked_linear(dy2, mod.cache.get_t(), g.table.state, mod.slots["dx"], z_alarm=g.z_alarm,
                                  inject=g._take_inject(mod.name, "dx")).view(xshape)
     if need_w:
         if m % 8 == 0:
             xt = gemm.CheckedWeight.of_transpose(x2)            # X^T (k, m): rows = output columns of dW
+            g._keep(mod.slots["dw"], xt)
             dw = gemm.checked_linear(dy2.t().contiguous(), xt, g.table.state, mod.slots["dw"],
                                      z_alarm=g.z_alarm, inject=g._take_inject(mod.name, "dw"))
         else:
@@ -194,8 +197,27 @@ class CheckedLinear:
 
 class SDCGuard:
     def __init__(self, check_every: int = 1, z_alarm: float = abft.Z_ALARM, device=None,
-                 log: Optional[EventLog] = None, on_alert=None):
+                 log: Optional[EventLog] = None, on_alert=None, replicas: bool = False, replica_group=None,
+                 recompute: bool = False, exact_reductions: bool = True, keep_evidence: bool = True,
+                 evidence_dir: Optional[str] = None, confirm_runs: int = 20):
+        """replicas: after each checked step every rank shares (a multiple of check_every, an after_restart()
+        window), compare the protected model's weight fingerprints across the data-parallel ranks (a collective).
+        recompute: blocks run through guard.checkpoint() are fingerprinted in the forward and in the backward
+        recompute on checked steps. exact_reductions: on checked steps, PyTorch's bf16 GEMMs (the unchecked ones,
+        attention's among them) keep their split-K partial sums in fp32. keep_evidence: the operands of each
+        checked GEMM of a step are kept until the step's check is read, so an alarm comes with its input row,
+        a float64 recheck and `confirm_runs` replays of the flagged block on this GPU; evidence_dir: each such
+        alarm is also saved there (torch.save, loadable with weights_only=True)."""
         self.check_every = max(1, int(check_every))
+        self.replicas, self.replica_group = replicas, replica_group
+        self.exact_reductions = exact_reductions
+        self.keep_evidence, self.evidence_dir, self.confirm_runs = keep_evidence, evidence_dir, confirm_runs
+        self._kept: dict = {}
+        self._model_ref = None
+        self.recompute = None
+        if recompute:
+            from .recompute import RecomputeCheck
+            self.recompute = RecomputeCheck()
         self.z_alarm = z_alarm
         self.device = torch.device(device or "cuda")
         self.table = gemm.StateTable(self.device, 512)
@@ -217,6 +239,10 @@ class SDCGuard:
             from ..ops import verify
             self.verification = verify.verified(self.device)   # the kernels reproduced their references here
         from . import swap
+        import weakref
+        self._model_ref = weakref.ref(model)
+        if self.device.type == "cuda" and self.keep_evidence:
+            gemm.enable_capture(self.device)
         for name, mod in list(model.named_modules()):
             if isinstance(mod, torch.nn.Linear) and not swap.is_checked(mod):
                 st = CheckedLinear(mod, self, name)
@@ -300,12 +326,54 @@ class SDCGuard:
     def at_step(self, step: int, force: bool = False):
         self.step = step
         self.active = force or step % self.check_every == 0
+        flag = torch.backends.cuda.matmul.allow_bf16_reduced_precision_reduction
+        if self.active and self.exact_reductions:
+            torch.backends.cuda.matmul.allow_bf16_reduced_precision_reduction = False
         try:
             yield self
         finally:
+            torch.backends.cuda.matmul.allow_bf16_reduced_precision_reduction = flag
             if self.active:
                 self.flush(step)
+                if self.replicas and (step % self.check_every == 0 or self._in_window(step, "_dense")):
+                    self._replica_check(step)
             self.active = False
+            self._kept.clear()
+
+    def _in_window(self, step: int, name: str) -> bool:
+        w = getattr(self, name, None)
+        return w is not None and w[0] <= step < w[1]
+
+    def _replica_check(self, step: int) -> None:
+        """Weight fingerprints voted across the data-parallel ranks (only on steps every rank checks: a rank that
+        entered the collective alone would wait for the others)."""
+        import torch.distributed as dist
+        model = self._model_ref() if self._model_ref is not None else None
+        if model is None or not (dist.is_available() and dist.is_initialized()):
+            return
+        if dist.get_world_size(self.replica_group) < 2:
+            return
+        from .replica import check_replicas
+        for ev in check_replicas(list(model.parameters()), group=self.replica_group, step=step):
+            self._emit(ev)
+
+    def checkpoint(self, fn, *args, name: Optional[str] = None, **kw):
+        """Activation checkpointing of a block (torch.utils.checkpoint, non-reentrant); on checked steps with
+        recompute=True the block's forward and its backward recompute are fingerprinted and compared."""
+        import torch.utils.checkpoint as ckpt
+        if self.active and self.recompute is not None:
+            return self.recompute.checkpoint(fn, *args, name=name, **kw)
+        return ckpt.checkpoint(fn, *args, use_reentrant=False, **kw)
+
+    def _keep(self, slot: int, cw) -> None:
+        if self.keep_evidence and self.active:
+            self._kept[slot] = cw
+
+    def _emit(self, ev: SDCEvent) -> None:
+        self.log.add(ev)
+        self.events.append(ev)
+        if self.on_alert:
+            self.on_alert(ev)
 
     def inject_next(self, layer: str, phase: str, row: int, col: int, bit: int) -> None:
         """Fault injection: flip `bit` of fp32 accumulator (row, col) of the next `phase` GEMM of `layer`."""
@@ -316,6 +384,9 @@ class SDCGuard:
 
     def flush(self, step: Optional[int] = None) -> list[SDCEvent]:
         rows = self.table.read(reset=True)
+        if self.recompute is not None:
+            for ev in self.recompute.read(step):
+                self._emit(ev)
         self.steps_checked += 1
         new = []
         ident = None
@@ -334,7 +405,62 @@ class SDCGuard:
             else:
                 self.worst_clean = max(self.worst_clean, r["z"])
         self.events += new
+        if new and self.device.type == "cuda" and self.keep_evidence:
+            self._evidence(new, step)
         return new
+
+    def _evidence(self, new: list, step) -> None:
+        """The device's captured alarm (input row and block sums, recorded by the GEMM that alarmed): a float64
+        recheck against that GEMM's B operand kept for the step, `confirm_runs` replays of the block on this GPU,
+        and an evidence file when evidence_dir is set."""
+        cap = gemm.read_capture(self.device)
+        if cap is None:
+            return
+        slot = self.table.slot_of(cap["state_row"])
+        if slot is None:
+            return
+        name = self.table.names[slot]
+        layer, ph = name.split(" ")[0].rsplit(".", 1)
+        cw = self._kept.get(slot)
+        rec = gemm.recheck_capture(cap, cw) if cw is not None and cw.k == cap["k"] else None
+        confirm = self._confirm(cap, cw) if cw is not None and cw.k == cap["k"] else None
+        kept = {k: v for k, v in cap.items() if k != "x_row"}
+        for ev in new:
+            if ev.detail.get("layer") == layer and ev.detail.get("phase") == ph:
+                ev.detail.update(captured=kept, recheck=rec, confirm=confirm)
+                break
+        if self.evidence_dir and cw is not None:
+            import os
+            os.makedirs(self.evidence_dir, exist_ok=True)
+            b = cap["block"]
+            path = os.path.join(self.evidence_dir, f"step{step}_{layer}_{ph}_r{cap['row']}_b{b}.pt")
+            torch.save({"format": "sdcguard-b200-train-evidence/1", "layer": layer, "phase": ph, "step": step,
+                        "x_row": cap["x_row"], "w_block": cw.weight[b * abft.BLOCK:(b + 1) * abft.BLOCK].cpu(),
+                        "captured": kept, "recheck": rec, "confirm": confirm}, path)
+            for ev in new:
+                if ev.detail.get("layer") == layer and ev.detail.get("phase") == ph:
+                    ev.detail["evidence"] = path
+
+    def _confirm(self, cap: dict, cw) -> dict:
+        """Replays of the flagged (row, block) on this GPU with the checked GEMM: how many of `confirm_runs` alarm
+        or leave the float64 envelope (a fault that follows the device and its kernel reproduces; a transient
+        one does not)."""
+        b = cap["block"]
+        c0, c1 = b * abft.BLOCK, min((b + 1) * abft.BLOCK, cw.n)
+        x = cap["x_row"].to(self.device).view(1, -1).contiguous()
+        wb = cw.weight[c0:c1].contiguous()
+        cwb = gemm.CheckedWeight(wb)
+        tab = gemm.StateTable(self.device, 1)
+        s = tab.add("confirm", cwb.nb)
+        ref = (wb.double() @ x.double().view(-1))
+        env = 2.0 ** -8 * ref.abs() + 1.01 * x.shape[1] * 2.0 ** -24 * (wb.double().abs() @ x.double().abs().view(-1))
+        wrong = alarms = 0
+        for _ in range(max(0, self.confirm_runs)):
+            y = gemm.checked_linear(x, cwb, tab.state, s)[0].double()
+            wrong += int(((y - ref).abs() > env + 1e-30).any())
+            alarms += int(tab.read(reset=True)[0]["z"] > self.z_alarm)
+        return {"runs": self.confirm_runs, "wrong_outputs": wrong, "alarms": alarms,
+                "reproduced": wrong + alarms > 0}
 
     def coverage(self) -> dict:
         return {"layers": len(self.modules), "checked_calls": self.checked_calls, "unchecked_calls": self.unchecked,

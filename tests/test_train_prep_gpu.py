@@ -80,3 +80,29 @@ def test_autocast_training_step_checked():
             loss = model(x).float().pow(2).mean()
         loss.backward()
     assert len(guard.events) == 1 and guard.events[0].detail["phase"] == "dw"
+
+
+def test_alarm_evidence_recheck_and_confirm(tmp_path):
+    from sdcguard_b200.train.guard import SDCGuard
+    from sdcguard_b200.utils.events import load_evidence
+    dev = torch.device("cuda")
+    torch.manual_seed(1)
+    model = torch.nn.Sequential(torch.nn.Linear(256, 384), torch.nn.GELU(), torch.nn.Linear(384, 256)).to(
+        dev, torch.bfloat16)
+    guard = SDCGuard(check_every=1, device=dev, recompute=True, evidence_dir=str(tmp_path), confirm_runs=5)
+    guard.protect(model)
+    x = torch.randn(64, 256, device=dev, dtype=torch.bfloat16)
+    with guard.on_step(0):
+        y = guard.checkpoint(model, x)
+        y.float().pow(2).mean().backward()
+    assert guard.events == [] and guard.recompute.checks == 1
+    guard.inject_next("2", "fwd", 7, 200, 29)         # one flipped exponent bit, this step only
+    with guard.on_step(1):
+        model(x).float().sum().backward()
+    assert len(guard.events) == 1
+    d = guard.events[0].detail
+    assert d["captured"]["row"] == 7 and d["captured"]["block"] == 200 // 128
+    assert d["recheck"]["verdict"] == "output_wrong"
+    assert d["confirm"]["runs"] == 5 and d["confirm"]["reproduced"] is False    # a transient flip: not on replay
+    ev = load_evidence(d["evidence"])
+    assert ev["layer"] == "2" and ev["x_row"].shape == (384,) and ev["w_block"].shape == (128, 384)
