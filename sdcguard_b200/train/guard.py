@@ -37,20 +37,23 @@ PHASES = ("fwd", "dx", "dw")
 
 
 class _Cache:
-    """Checksum data of one weight, rebuilt when the weight's version changes (after an optimizer step). A weight
+    """Checksum data of one weight, built once per checked step (and again if the weight changes within the step):
+    the optimizer changes weights between steps, and fused optimizers (AdamW(fused=True)) do so without bumping the
+    tensors' version counters, so a version check alone would keep stale checksums and a stale bf16 copy. A weight
     kept in fp32 (mixed precision under autocast) is checked as its bf16 copy, which is what autocast would feed the
-    GEMM; the copy is made once per version."""
+    GEMM; the bias is copied with it, so the GEMM adds the bias the checksums were built from."""
 
-    def __init__(self):
+    def __init__(self, guard: "SDCGuard"):
+        self.guard = guard
         self.key = None
         self.cw: Optional[gemm.CheckedWeight] = None
         self.cwT: Optional[gemm.CheckedWeight] = None
 
     def get(self, w: torch.Tensor, b: Optional[torch.Tensor]):
-        key = (w.data_ptr(), w._version, None if b is None else b._version)
+        key = (self.guard.epoch, w.data_ptr(), w._version, None if b is None else (b.data_ptr(), b._version))
         if key != self.key:
-            wb = w.detach() if w.dtype == torch.bfloat16 else w.detach().to(torch.bfloat16)
-            bb = None if b is None else b.detach()
+            wb = w.detach().to(torch.bfloat16, copy=True)
+            bb = None if b is None else b.detach().float().clone()
             self.cw = gemm.CheckedWeight.on_device(wb, bb)
             self.cwT = None
             self.key = key
@@ -132,7 +135,7 @@ class CheckedLinear:
         self.in_features, self.out_features = lin.in_features, lin.out_features
         self.guard = guard
         self.name = name
-        self.cache = _Cache()
+        self.cache = _Cache(guard)
         self.slots = {}
         n, k = lin.out_features, lin.in_features
         nbs = {"fwd": -(-n // abft.BLOCK), "dx": -(-k // abft.BLOCK), "dw": -(-k // abft.BLOCK)}
@@ -166,7 +169,7 @@ class CheckedLinear:
 
     def checked_backward(self, gy, x, w, need_x, need_w, need_b):
         c = self.cache
-        if c.cw is None or c.key[:2] != (w.data_ptr(), w._version):
+        if c.cw is None or c.key[:3] != (self.guard.epoch, w.data_ptr(), w._version):
             c.get(w, None)                       # the forward's cache entry is normally still current
         xb = x.to(torch.bfloat16)
         dx, dw, db = _bwd_gemms(self, gy, xb.reshape(-1, x.shape[-1]).contiguous(), self.cache.cw.weight, x.shape,
@@ -209,6 +212,7 @@ class SDCGuard:
         a float64 recheck and `confirm_runs` replays of the flagged block on this GPU; evidence_dir: each such
         alarm is also saved there (torch.save, loadable with weights_only=True)."""
         self.check_every = max(1, int(check_every))
+        self.epoch = 0                      # checked steps begun: the checksum caches are per checked step
         self.replicas, self.replica_group = replicas, replica_group
         self.exact_reductions = exact_reductions
         self.keep_evidence, self.evidence_dir, self.confirm_runs = keep_evidence, evidence_dir, confirm_runs
@@ -326,6 +330,8 @@ class SDCGuard:
     def at_step(self, step: int, force: bool = False):
         self.step = step
         self.active = force or step % self.check_every == 0
+        if self.active:
+            self.epoch += 1
         flag = torch.backends.cuda.matmul.allow_bf16_reduced_precision_reduction
         if self.active and self.exact_reductions:
             torch.backends.cuda.matmul.allow_bf16_reduced_precision_reduction = False

@@ -106,3 +106,31 @@ def test_alarm_evidence_recheck_and_confirm(tmp_path):
     assert d["confirm"]["runs"] == 5 and d["confirm"]["reproduced"] is False    # a transient flip: not on replay
     ev = load_evidence(d["evidence"])
     assert ev["layer"] == "2" and ev["x_row"].shape == (384,) and ev["w_block"].shape == (128, 384)
+
+
+def test_fused_optimizer_keeps_checks_current():
+    """AdamW(fused=True) updates weights without bumping their version counters: the checked steps must still use
+    the updated weights (same training as without the guard) and raise no alarm."""
+    from sdcguard_b200.train.guard import SDCGuard
+    dev = torch.device("cuda")
+
+    def make():
+        torch.manual_seed(3)
+        m = torch.nn.Sequential(torch.nn.Linear(256, 512), torch.nn.GELU(), torch.nn.Linear(512, 256)).to(dev)
+        return m, torch.optim.AdamW(m.parameters(), lr=1e-2, fused=True)
+    (m1, o1), (m2, o2) = make(), make()
+    guard = SDCGuard(check_every=1, device=dev)
+    guard.protect(m1)
+    x = torch.randn(128, 256, device=dev)
+    for step in range(4):
+        for m, o, g in ((m1, o1, guard), (m2, o2, None)):
+            ctx = g.on_step(step) if g is not None else torch.autocast("cuda", enabled=False)
+            with ctx:
+                with torch.autocast("cuda", dtype=torch.bfloat16):
+                    loss = m(x).float().pow(2).mean()
+                loss.backward()
+            o.step()
+            o.zero_grad()
+    assert guard.coverage()["alarms"] == 0
+    for p1, p2 in zip(m1.parameters(), m2.parameters()):
+        assert float((p1 - p2).abs().max()) < 5e-3 * float(p2.abs().max()) + 1e-3
