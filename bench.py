@@ -221,7 +221,10 @@ def run_ours(args, rank, world, local):
         from sdcguard_b200.tools import campaign
         res["campaign"] = campaign.quick(seed=rank)
     if not args.no_tp and world > 1:
-        res["tp"] = run_tp(args, world)
+        try:
+            res["tp"] = run_tp(args, world)
+        except Exception as e:  # noqa: BLE001  (the headline line is printed with the TP block's error instead)
+            res["tp"] = {"error": f"{type(e).__name__}: {str(e)[:300]}"}
     elif not args.no_tp:
         res["tp"] = {"skipped": "TP = 1 is the single-GPU engine of the headline; the block runs from N = 2"}
     return res

@@ -74,7 +74,9 @@ def _run(every: int, args, dev, batches) -> dict:
         out.update(checked_steps=len(checked_times),
                    ms_per_checked_step=sum(checked_times) / max(1, len(checked_times)),
                    checks=cov["checks"], alarms=cov["alarms"], worst_clean_z=round(cov["worst_clean_z"], 4),
-                   checked_calls=cov["checked_calls"], unchecked_calls=cov["unchecked_calls"])
+                   checked_calls=cov["checked_calls"], unchecked_calls=cov["unchecked_calls"],
+                   alarm_examples=[{k: e.detail.get(k) for k in ("layer", "phase", "z", "row", "block")}
+                                   for e in guard.events[:5]])
     del model, opt
     torch.cuda.empty_cache()
     return out
