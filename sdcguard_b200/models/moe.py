@@ -82,6 +82,9 @@ class MoELayer:
             self.cw_r = gemm.CheckedWeight(self.router)
             self.s13 = gemm.CheckedWeightStack(self.w13)
             self.s2 = gemm.CheckedWeightStack(self.w2)
+            # the per-expert weights become views of the stacks (one copy of the expert weights in memory)
+            self.w13 = [self.s13.expert(j) for j in range(self.epr)]
+            self.w2 = [self.s2.expert(j) for j in range(self.epr)]
         self._grouping: Optional[moe_ops.Grouping] = None
         self._bufs: dict = {}
         self.baseline_path = None
