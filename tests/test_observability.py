@@ -52,8 +52,20 @@ def test_metrics_and_stack_identity():
     t = m.text().decode()
     assert 'sdcguard_alarms_total{detector="replay"} 1.0' in t and "sdcguard_worst_clean_z 0.5" in t
     s2 = dict(s1, model="b")
-    assert stack.compare(s1, s2) == {"model": {"a": "a", "b": "b"}}
+    assert stack.field_differences(s1, s2) == {"model": {"a": "a", "b": "b"}}
     assert stack.fingerprint(s1) != stack.fingerprint(s2)
+    base = {"model": "m", "model_config": "c", "weights_digest": "w", "precision": "bf16", "library_build": "l",
+            "gpu": "B200", "device": "cuda:0"}
+    assert stack.compare(base, dict(base, device="cuda:3"))["same"] is True          # per-worker field
+    r = stack.compare(base, dict(base, precision="fp8"))
+    assert r["same"] is False and "precision" in r["why"]
+    no_digest = {k: v for k, v in base.items() if k != "weights_digest"}
+    assert stack.compare(base, no_digest)["same"] is None
+    assert stack.compare(no_digest, no_digest)["same"] is None
+    assert stack.compare(None, base)["same"] is None
+    assert stack.shared(base) == stack.shared(dict(base, device="cuda:1", pid="9"))
+    page = 'x 1\nsdcguard_stack_info{model="m",gpu="B200"} 1.0\n'
+    assert stack.from_metrics(page) == {"model": "m", "gpu": "B200"}
 
 
 def test_clock_sample_summary():
