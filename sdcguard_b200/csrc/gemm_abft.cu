@@ -68,6 +68,12 @@ struct PeerMaps {
   CUtensorMap m[8];           // every rank's receive buffer [world R][N] (push mode)
 };
 
+// Row stride (floats) of the split-K partial accumulators: N outputs and 6 nb checksum columns, rounded up to a
+// multiple of 4 so every row starts on a 16-byte boundary (the reduce kernel reads them as float4).
+__host__ __device__ __forceinline__ long long part_stride(int N, int nb) {
+  return (static_cast<long long>(N) + 6ll * nb + 3) / 4 * 4;
+}
+
 struct Params {
   int M, N, K;
   const __nv_bfloat16* a;    // A (for the alarm capture: the row of an alarming block is copied from here)
@@ -107,7 +113,7 @@ struct Params {
   Push push;
   int ksplit;                // K splits (1: the fused epilogue; > 1: partial accumulators + reduce kernel)
   int kb_per;                // k-blocks per split
-  float* part;               // ksplit > 1: [ksplit][M][N + 6 nb] fp32 partial accumulators
+  float* part;               // ksplit > 1: [ksplit][M][part_stride(N, nb)] fp32 partial accumulators
   // Grouped mode (null gband: off). The rows of A are grouped by expert, each expert's rows starting on a band
   // boundary; band b belongs to expert gband[b], and only the first *gcount bands hold rows (both written on the
   // device by the kernel before this one, read after the programmatic-launch wait). W and Wc are the experts'
@@ -377,7 +383,7 @@ __global__ void __launch_bounds__(256) split_reduce_kernel(const Params p) {
   __shared__ int su[8];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long wid = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-  const long long pw = static_cast<long long>(p.N) + 6ll * p.nb;
+  const long long pw = part_stride(p.N, p.nb);
   const long long plane = static_cast<long long>(p.M) * pw;
   unsigned long long k0 = 0ull, k1 = 0ull;
   int unj = 0;
@@ -859,7 +865,7 @@ __global__ void __launch_bounds__(Cfg<BN, PAIR>::THREADS, 1)
       if (p.ksplit > 1) {
         // ---- split-K: store this split's fp32 accumulator rows; the reduce kernel sums and checks them
         const int ks = tile % p.ksplit;
-        const long long pw = static_cast<long long>(p.N) + 6ll * p.nb;
+        const long long pw = part_stride(p.N, p.nb);
         float* prow = p.part + (static_cast<long long>(ks) * p.M + row) * pw;
         if (cs) {
           const int blk0 = idx * C::CSB + g * 20;
@@ -1219,7 +1225,7 @@ static long long ws_bytes_base(int M, int N) {
 
 static long long part_bytes(int M, int N) {
   const long long nb = (N + CSW - 1) / CSW;
-  return static_cast<long long>(kMaxSplit) * M * (N + 6 * nb) * 4;
+  return static_cast<long long>(kMaxSplit) * M * part_stride(N, static_cast<int>(nb)) * 4;
 }
 
 static bool split_eligible(int M, int N) { return (M + BM - 1) / BM <= 2 && N <= kSplitMaxN; }

@@ -141,20 +141,14 @@ class CheckedLinear:
         nbs = {"fwd": -(-n // abft.BLOCK), "dx": -(-k // abft.BLOCK), "dw": -(-k // abft.BLOCK)}
         for ph in PHASES:
             self.slots[ph] = guard.table.add(f"{name}.{ph} (ABFT GEMM)", nbs[ph])
+        from . import compiled
+        self.state_id = compiled.register(self)      # (at protect time: the traced forward only reads it)
 
     @property
     def weight(self):
         return self.layer.weight
 
     # ---- the operators of train.compiled call these (under torch.compile, and on DTensor local shards)
-    @property
-    def state_id(self) -> int:
-        sid = getattr(self, "_sid", None)
-        if sid is None:
-            from . import compiled
-            sid = self._sid = compiled.register(self)
-        return sid
-
     def runnable(self, x, w) -> bool:
         ok = (self.guard.active and x.is_cuda and x.shape[-1] % 8 == 0 and w.shape[0] % 8 == 0 and
               x.dtype in (torch.bfloat16, torch.float32) and w.dtype in (torch.bfloat16, torch.float32))

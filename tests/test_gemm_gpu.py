@@ -111,3 +111,26 @@ def test_split_k_small_m_output_check_seal_and_injection(bn, m, n, k):
     rows = st.read()
     assert rows[0]["checks"] == 1 and rows[0]["unjudged"] == 0 and rows[0]["z"] < 2.0, rows[0]
     assert rows[1]["z"] > abft.Z_ALARM and rows[1]["row"] == 10 and rows[1]["block"] == 5, rows[1]
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 128, 4096), (64, 640, 4096), (200, 1152, 3072), (7, 384, 16384)])
+def test_split_k_odd_block_counts(m, n, k):
+    """Split-K with an odd number of 128-column blocks: the partial accumulators' rows are padded to 16 bytes (the
+    reduce kernel reads them as float4), so every shape the GEMM takes splits cleanly."""
+    from sdcguard_b200.ops import gemm
+    torch.manual_seed(5)
+    dev = torch.device("cuda")
+    x = torch.randn(m, k, device=dev).to(torch.bfloat16)
+    w = (torch.randn(n, k, device=dev) * 0.02).to(torch.bfloat16)
+    cw = gemm.CheckedWeight(w)
+    st = gemm.StateTable(dev, 2)
+    s0, s1 = st.add("clean", cw.nb), st.add("inj", cw.nb)
+    y = gemm.checked_linear(x, cw, st.state, s0)
+    ref = x.double() @ w.double().t()
+    assert float((y.double() - ref).abs().max()) <= 2 ** -7 * float(ref.abs().max()) + 1e-3
+    r, c = m - 1, n - 3
+    gemm.checked_linear(x, cw, st.state, s1, inject=(r, c, 1 << 29))
+    rows = st.read()
+    assert rows[0]["z"] < 2.0 and rows[0]["unjudged"] == 0, rows[0]
+    assert rows[1]["z"] > abft.Z_ALARM and rows[1]["row"] == r and rows[1]["block"] == c // 128, rows[1]
+    assert gemm.error_word(dev).item() == 0

@@ -109,28 +109,27 @@ def test_alarm_evidence_recheck_and_confirm(tmp_path):
 
 
 def test_fused_optimizer_keeps_checks_current():
-    """AdamW(fused=True) updates weights without bumping their version counters: the checked steps must still use
-    the updated weights (same training as without the guard) and raise no alarm."""
+    """AdamW(fused=True) updates weights without bumping their version counters: every checked step must use the
+    updated weights (its checked forward equals plain PyTorch on the current weights) and raise no alarm."""
     from sdcguard_b200.train.guard import SDCGuard
     dev = torch.device("cuda")
-
-    def make():
-        torch.manual_seed(3)
-        m = torch.nn.Sequential(torch.nn.Linear(256, 512), torch.nn.GELU(), torch.nn.Linear(512, 256)).to(dev)
-        return m, torch.optim.AdamW(m.parameters(), lr=1e-2, fused=True)
-    (m1, o1), (m2, o2) = make(), make()
+    torch.manual_seed(3)
+    m = torch.nn.Sequential(torch.nn.Linear(256, 512), torch.nn.GELU(), torch.nn.Linear(512, 256)).to(dev)
+    opt = torch.optim.AdamW(m.parameters(), lr=1e-2, fused=True)
     guard = SDCGuard(check_every=1, device=dev)
-    guard.protect(m1)
+    guard.protect(m)
     x = torch.randn(128, 256, device=dev)
     for step in range(4):
-        for m, o, g in ((m1, o1, guard), (m2, o2, None)):
-            ctx = g.on_step(step) if g is not None else torch.autocast("cuda", enabled=False)
-            with ctx:
-                with torch.autocast("cuda", dtype=torch.bfloat16):
-                    loss = m(x).float().pow(2).mean()
-                loss.backward()
-            o.step()
-            o.zero_grad()
+        with guard.on_step(step):
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                y = m(x)
+                loss = y.float().pow(2).mean()
+            loss.backward()
+        # the checked forward of this step against PyTorch on the weights it had (bf16 autocast arithmetic)
+        with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+            h = torch.nn.functional.gelu(torch.nn.functional.linear(x, m[0].weight, m[0].bias))
+            ref = torch.nn.functional.linear(h, m[2].weight, m[2].bias)
+        assert float((y.float() - ref.float()).abs().max()) < 0.02 * float(ref.float().abs().max()), step
+        opt.step()
+        opt.zero_grad()
     assert guard.coverage()["alarms"] == 0
-    for p1, p2 in zip(m1.parameters(), m2.parameters()):
-        assert float((p1 - p2).abs().max()) < 5e-3 * float(p2.abs().max()) + 1e-3
