@@ -4,6 +4,7 @@
     sdcguard gate capture|add|run|compare|workaround|...      upgrade gate of library GEMMs (exit 0 / 1 / 2)
     sdcguard transfer-check DIR [--json]                     transfer-only coverage (exit 0 PASS, 2 HOLD)
     sdcguard transfer-compare BASE CAND [--json]             coverage preservation between two builds (always 2)
+    sdcguard checksum-observer / checksum-client / native-checks  inspect | capture | verify offline evidence packets
     sdcguard pd-record OUT [--gpus ...]                      record a checked prefill/decode run of this engine
     sdcguard selftest                                        GPU self-test of every checked kernel
     sdcguard campaign                                        fault-injection campaign on the GPU paths
@@ -61,6 +62,9 @@ COMMANDS = {
     "gate": lambda argv: _gate(argv),
     "transfer-check": _lazy(".coverage.transfer", "main"),
     "transfer-compare": _lazy(".coverage.transfer", "main_compare"),
+    "checksum-observer": _lazy(".coverage.packets", "observer_main"),
+    "checksum-client": _lazy(".coverage.packets", "client_main"),
+    "native-checks": _lazy(".coverage.packets", "native_main"),
     "pd-record": _lazy(".serve.pd", "main"),
     "selftest": _lazy(".tools.selftest", "main"),
     "campaign": _lazy(".tools.campaign", "main"),
