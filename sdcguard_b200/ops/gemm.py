@@ -303,7 +303,9 @@ class CheckedWeight:
             raise ValueError(f"checked GEMM needs n and k multiples of 8 (got n={n}, k={k})")
         cs = _prep(w, transpose=False)
         if bias is not None:
-            cs.bsum, cs.bias_max = _bias_sums(bias, n, cs.mask), float(bias.detach().abs().max()) if n else 0.0
+            # the bias's largest magnitude is not read back here (a host read per layer would stall a training
+            # step): 0 means a non-finite output counts as corruption unless the weights and inputs can produce it
+            cs.bsum, cs.bias_max = _bias_sums(bias, n, cs.mask), 0.0
         return cls._assemble(w, cs, bias, c1, c2, c3)
 
     @classmethod

@@ -30,38 +30,50 @@ SHAPES = [  # (M, N, K): decode and prefill sizes of Qwen3-0.6B, Llama-3-8B shar
     (64, 4096, 14336), (512, 3072, 768), (2048, 768, 3072), (4096, 4096, 1024), (4096, 6144, 4096),
     (8192, 1024, 3072), (16384, 768, 768), (1024, 28672, 4096),
 ]
-DISTRIBUTIONS = ("normal", "uniform", "heavy", "wide", "cancel")
+DISTRIBUTIONS = ("normal", "uniform", "heavy", "wide", "cancel", "softmax_grad")
+# training GEMMs with a long K (the token count): dW of the projections and of a 50304-word LM head at 32 x 512
+# tokens, and dX of that head (K = the vocabulary)
+TRAIN_SHAPES = [(2304, 768, 16384), (768, 3072, 16384), (3072, 768, 16384), (50304, 768, 16384),
+                (16384, 768, 50304), (16384, 2304, 768)]
 
 
 def _inputs(kind: str, m: int, n: int, k: int, g: torch.Generator, dev) -> tuple[torch.Tensor, torch.Tensor]:
     if kind == "normal":
-        x, w = torch.randn(m, k, generator=g), torch.randn(n, k, generator=g) * 0.02
+        x, w = torch.randn(m, k, generator=g, device=dev), torch.randn(n, k, generator=g, device=dev) * 0.02
     elif kind == "uniform":
-        x, w = torch.rand(m, k, generator=g) * 2 - 1, (torch.rand(n, k, generator=g) * 2 - 1) * 0.05
+        x = torch.rand(m, k, generator=g, device=dev) * 2 - 1
+        w = (torch.rand(n, k, generator=g, device=dev) * 2 - 1) * 0.05
     elif kind == "heavy":          # Student-t-like tails: a few very large activations per row
-        x = torch.randn(m, k, generator=g) / (torch.rand(m, k, generator=g) + 0.05)
-        w = torch.randn(n, k, generator=g) * 0.02
+        x = torch.randn(m, k, generator=g, device=dev) / (torch.rand(m, k, generator=g, device=dev) + 0.05)
+        w = torch.randn(n, k, generator=g, device=dev) * 0.02
     elif kind == "wide":           # rows and columns over many binades
-        x = torch.randn(m, k, generator=g) * torch.exp2(torch.randint(-12, 12, (m, 1), generator=g).float())
-        w = torch.randn(n, k, generator=g) * 0.02 * torch.exp2(torch.randint(-6, 6, (n, 1), generator=g).float())
+        ex = torch.randint(-12, 12, (m, 1), generator=g, device=dev).float()
+        ew = torch.randint(-6, 6, (n, 1), generator=g, device=dev).float()
+        x = torch.randn(m, k, generator=g, device=dev) * torch.exp2(ex)
+        w = torch.randn(n, k, generator=g, device=dev) * 0.02 * torch.exp2(ew)
+    elif kind == "softmax_grad":   # rows of a softmax cross-entropy gradient: tiny, one-signed, a few large negatives
+        x = torch.rand(m, k, generator=g, device=dev) * 2e-9
+        hit = torch.rand(m, k, generator=g, device=dev) < 2e-4
+        x[hit] = -6e-5
+        w = torch.randn(n, k, generator=g, device=dev)
     else:                          # rows whose dot products nearly cancel
-        x = torch.randn(m, k, generator=g)
+        x = torch.randn(m, k, generator=g, device=dev)
         x[:, k // 2:] = -x[:, : k - k // 2].flip(1)
-        w = torch.randn(n, k, generator=g) * 0.02
+        w = torch.randn(n, k, generator=g, device=dev) * 0.02
         w[:, k // 2:] = w[:, : k - k // 2].flip(1)
     return x.to(dev).bfloat16(), w.to(dev).bfloat16()
 
 
 def run(device="cuda", reps: int = 2, scale: float = 1.0, target: float = 0.5, shapes=None) -> dict:
     dev = torch.device(device)
-    g = torch.Generator().manual_seed(20261202)
+    g = torch.Generator(device=dev).manual_seed(20261202)
     rows, worst = [], 0.0
     checks = 0
     for (m, n, k) in shapes or SHAPES:
         for kind in DISTRIBUTIONS:
             for bias in (False, True):
                 x, w = _inputs(kind, m, n, k, g, dev)
-                b = (torch.randn(n, generator=g) * 0.1).to(dev).bfloat16() if bias else None
+                b = (torch.randn(n, generator=g, device=dev) * 0.1).bfloat16() if bias else None
                 cw = gemm.CheckedWeight(w, b, c1=abft.C1 * scale, c2=abft.C2 * scale, c3=abft.C3 * scale)
                 table = gemm.StateTable(dev, 1)
                 slot = table.add("calibration", cw.nb)
@@ -88,8 +100,11 @@ def main(argv=None) -> int:
     ap.add_argument("--scale", type=float, default=1.0, help="multiplier on the coefficients C1, C2, C3")
     ap.add_argument("--target", type=float, default=0.5)
     ap.add_argument("--out")
+    ap.add_argument("--set", choices=("serve", "train", "all"), default="serve",
+                    help="shape grid: serving and prefill shapes, long-K training shapes, or both")
     a = ap.parse_args(argv)
-    res = run(a.device, a.reps, a.scale, a.target)
+    shapes = {"serve": SHAPES, "train": TRAIN_SHAPES, "all": SHAPES + TRAIN_SHAPES}[a.set]
+    res = run(a.device, a.reps, a.scale, a.target, shapes=shapes)
     text = json.dumps(res, indent=1)
     if a.out:
         with open(a.out, "w") as f:

@@ -41,7 +41,7 @@ def test_colblock_matches_reference(n, k):
     a, r = _parts_value(cw.cs.wc), _parts_value(ref.wc)
     assert float(((a - r).abs() / (r.abs().amax() + 1e-30)).max()) < 2 ** -20
     assert torch.allclose(cw.cs.wstat, ref.wstat, rtol=1e-4, atol=1e-6)
-    assert torch.allclose(cw.cs.bsum, ref.bsum) and abs(cw.cs.bias_max - ref.bias_max) < 1e-6
+    assert torch.allclose(cw.cs.bsum, ref.bsum) and cw.cs.bias_max == 0.0     # not read back (no host sync)
     # the checked GEMM with these checksums: clean
     x = torch.randn(256, k, device=dev, generator=g).bfloat16()
     st = gemm.StateTable(dev, 1)
