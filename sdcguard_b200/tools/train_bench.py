@@ -82,6 +82,52 @@ def _run(every: int, args, dev, batches) -> dict:
     return out
 
 
+def profile_steps(args, dev, batches, every: int = 1) -> dict:
+    """Kernel time of one plain and one checked step (torch.profiler CUDA activity; one launch list each): where a
+    checked step's extra time goes."""
+    from torch.profiler import ProfilerActivity, profile
+    from ..train.guard import SDCGuard
+    out = {}
+    for name, checked in (("plain", False), ("checked", True)):
+        model = _model(args.seed, args.vocab, dev)
+        opt = torch.optim.AdamW(model.parameters(), lr=6e-4, fused=True)
+        guard = SDCGuard(check_every=1, device=dev) if checked else None
+        if guard is not None:
+            guard.protect(model)
+
+        def step(i):
+            ctx = guard.on_step(i) if guard is not None else _null()
+            with ctx:
+                with torch.autocast("cuda", dtype=torch.bfloat16):
+                    logits = model(batches[0][:, :-1])
+                    loss = F.cross_entropy(logits.float().view(-1, logits.shape[-1]), batches[0][:, 1:].reshape(-1))
+                loss.backward()
+            opt.step()
+            opt.zero_grad(set_to_none=True)
+        for i in range(3):
+            step(i)
+        torch.cuda.synchronize()
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            t0 = time.perf_counter()
+            step(3)
+            torch.cuda.synchronize()
+            wall = (time.perf_counter() - t0) * 1e3
+        agg: dict = {}
+        for e in prof.events():
+            if e.device_type.name == "CUDA":
+                k = e.name[:90]
+                a = agg.setdefault(k, [0.0, 0])
+                a[0] += e.device_time_total / 1e3 if hasattr(e, "device_time_total") else e.cuda_time_total / 1e3
+                a[1] += 1
+        top = sorted(agg.items(), key=lambda kv: -kv[1][0])[:15]
+        out[name] = {"wall_ms": round(wall, 2), "kernel_ms": round(sum(v[0] for v in agg.values()), 2),
+                     "launches": sum(v[1] for v in agg.values()),
+                     "top": [[round(v[0], 3), v[1], k] for k, v in top]}
+        del model, opt, guard
+        torch.cuda.empty_cache()
+    return out
+
+
 class _null:
     def __enter__(self):
         return False
@@ -99,6 +145,7 @@ def main(argv=None) -> int:
     ap.add_argument("--seq", type=int, default=512)
     ap.add_argument("--vocab", type=int, default=50304)
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--profile", action="store_true", help="also profile one plain and one checked step")
     args = ap.parse_args(argv)
     dev = torch.device("cuda")
     torch.backends.cuda.matmul.allow_bf16_reduced_precision_reduction = True
@@ -115,7 +162,8 @@ def main(argv=None) -> int:
     from ..utils.gpuinfo import Sampler
     with Sampler(torch.cuda.current_device(), period_ms=200) as clk:
         _run(0, argparse.Namespace(**{**vars(args), "steps": 10, "warmup": 2}), dev, batches)
-    print(json.dumps({"tool": "train_bench", "model": "GPT-2 small (124M, vocab padded to %d)" % args.vocab,
+    prof = profile_steps(args, dev, batches) if args.profile else None
+    print(json.dumps({"tool": "train_bench", "profile": prof, "model": "GPT-2 small (124M, vocab padded to %d)" % args.vocab,
                       "batch": args.batch, "seq": args.seq, "dtype": "bf16 autocast, fp32 master weights",
                       "data": "synthetic token ids", "gpu": torch.cuda.get_device_name(dev),
                       "plain_ms_per_step": round(base["ms_per_step"], 2), "arms": arms,
