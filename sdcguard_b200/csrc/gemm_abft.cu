@@ -1228,7 +1228,17 @@ static long long part_bytes(int M, int N) {
   return static_cast<long long>(kMaxSplit) * M * part_stride(N, static_cast<int>(nb)) * 4;
 }
 
-static bool split_eligible(int M, int N) { return (M + BM - 1) / BM <= 2 && N <= kSplitMaxN; }
+// Split-K applies to decode-sized outputs (at most two bands), and to outputs whose partial accumulators fit in
+// 256 MB when K is long (kLongK and up: the training GEMMs dW = dY^T X, whose K is the token count, have few output
+// tiles and would leave most SMs idle). The workspace of an eligible shape holds the partials.
+constexpr int kLongK = 8192;
+constexpr long long kSplitMaxPartBytes = 256ll << 20;
+static bool split_decode(int M, int N) { return (M + BM - 1) / BM <= 2 && N <= kSplitMaxN; }
+static bool split_eligible(int M, int N) {
+  const long long nb = (N + CSW - 1) / CSW;
+  return split_decode(M, N) ||
+         static_cast<long long>(kMaxSplit) * M * part_stride(N, static_cast<int>(nb)) * 4 <= kSplitMaxPartBytes;
+}
 
 // CTA-pair clusters of the 256-wide pair kernel that can be resident at once (0: pair mode unavailable).
 int sdc_gemm_pair_clusters() { return pair_max_clusters(); }
@@ -1370,7 +1380,9 @@ static int gemm_run(const void* A, long long lda, const void* W, const void* Wc,
   // splitting pays when each CTA would stream a long K (measured: K = 1024 is faster unsplit)
   int split_min_k, split_force;
   split_policy(&split_min_k, &split_force);
-  if (!pair && allow_split && push == nullptr && grp == nullptr && split_eligible(M, N) && K >= split_min_k && max_ctas == 0 && dbg == nullptr) {
+  const int split_k_min = split_decode(M, N) ? split_min_k : kLongK;
+  if (!pair && allow_split && push == nullptr && grp == nullptr && split_eligible(M, N) && K >= split_k_min &&
+      max_ctas == 0 && dbg == nullptr) {
     const int kblocks = (K + BK - 1) / BK;
     int sp = split_force > 0 ? split_force : num_sms_cached() / p.total_tiles;
     sp = sp > kMaxSplit ? kMaxSplit : sp;

@@ -184,6 +184,60 @@ __global__ void __launch_bounds__(256) colblock_kernel(const __nv_bfloat16* __re
   add_stats(acc + b * 4, sq, pl2, sg2, mx, red);
 }
 
+// Transpose of a bf16 matrix, T = M^T (M: R x C with row stride ldm; T: C x R, row stride R). Grid (ceil(C / 64),
+// ceil(R / 64)), 256 threads: a 64 x 64 tile goes through shared memory as 32-bit words (two bf16 of a row) with a
+// row stride of 33 words, so the column reads of the second half touch 32 different banks; both the 16-byte global
+// loads and the 16-byte global stores are coalesced (8 threads cover 128 contiguous bytes of a row).
+__global__ void __launch_bounds__(256) transpose_kernel(const __nv_bfloat16* __restrict__ M, long long ldm, int R,
+                                                        int C, __nv_bfloat16* __restrict__ T, int vec) {
+  __shared__ uint32_t tile[64][33];
+  const int c0 = blockIdx.x * 64, r0 = blockIdx.y * 64;
+  // vec: both base pointers 16-byte aligned, ldm and R multiples of 8 (checked by the launcher)
+  const bool full = vec && r0 + 64 <= R && c0 + 64 <= C;
+  for (int i = threadIdx.x; i < 64 * 8; i += 256) {
+    const int row = i >> 3, q = i & 7;            // 8 chunks of 8 bf16 per tile row
+    const int r = r0 + row, c = c0 + q * 8;
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
+    if (full) {
+      const uint4 v = *reinterpret_cast<const uint4*>(M + static_cast<long long>(r) * ldm + c);
+      w[0] = v.x;
+      w[1] = v.y;
+      w[2] = v.z;
+      w[3] = v.w;
+    } else if (r < R) {
+      const unsigned short* src = reinterpret_cast<const unsigned short*>(M + static_cast<long long>(r) * ldm);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const unsigned short h = (c + j < C) ? src[c + j] : 0;
+        w[j >> 1] |= static_cast<uint32_t>(h) << ((j & 1) * 16);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) tile[row][q * 4 + j] = w[j];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < 64 * 8; i += 256) {
+    const int cc = i >> 3, rq = i & 7;            // T row c0 + cc, its columns r0 + 8 rq .. + 7
+    const int c = c0 + cc, r = r0 + rq * 8;
+    if (c >= C || r >= R) continue;
+    const int word = cc >> 1, hi = (cc & 1) * 16;
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t a = (tile[rq * 8 + 2 * j][word] >> hi) & 0xffffu;
+      const uint32_t b = (tile[rq * 8 + 2 * j + 1][word] >> hi) & 0xffffu;
+      o[j] = a | (b << 16);
+    }
+    __nv_bfloat16* dst = T + static_cast<long long>(c) * R + r;
+    if (full) {
+      *reinterpret_cast<uint4*>(dst) = make_uint4(o[0], o[1], o[2], o[3]);
+    } else {
+      unsigned short* d16 = reinterpret_cast<unsigned short*>(dst);
+      for (int j = 0; j < 8 && r + j < R; ++j) d16[j] = static_cast<unsigned short>((o[j >> 1] >> ((j & 1) * 16)) & 0xffffu);
+    }
+  }
+}
+
 __global__ void finalize_kernel(const float* __restrict__ acc, int nb, float* __restrict__ wstat) {
   for (int b = threadIdx.x; b < nb; b += blockDim.x) {
     wstat[b * 4 + 0] = sqrtf(acc[b * 4 + 0]);
@@ -213,6 +267,16 @@ int sdc_prep_rowblock(const void* M, long long ldm, int R, int C, unsigned s0, u
       static_cast<const __nv_bfloat16*>(M), ldm, R, C, sg, static_cast<__nv_bfloat16*>(T),
       static_cast<__nv_bfloat16*>(wc), acc);
   sdc::prep::finalize_kernel<<<1, 256, 0, st>>>(acc, nb, wstat);
+  return static_cast<int>(cudaGetLastError());
+}
+
+// T (C x R) = M^T for M (R x C) bf16 with row stride ldm.
+int sdc_transpose_bf16(const void* M, long long ldm, int R, int C, void* T, void* stream) {
+  if (R <= 0 || C <= 0) return 0;
+  const int vec = (reinterpret_cast<uintptr_t>(M) % 16 == 0 && reinterpret_cast<uintptr_t>(T) % 16 == 0 &&
+                   ldm % 8 == 0 && R % 8 == 0) ? 1 : 0;
+  sdc::prep::transpose_kernel<<<dim3((C + 63) / 64, (R + 63) / 64), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(M), ldm, R, C, static_cast<__nv_bfloat16*>(T), vec);
   return static_cast<int>(cudaGetLastError());
 }
 

@@ -334,6 +334,19 @@ def _bias_sums(bias: torch.Tensor, n: int, mask) -> torch.Tensor:
     return torch.stack([bb.sum(1), (bb * s.view(1, abft.BLOCK)).sum(1)], dim=1).float().contiguous()
 
 
+def transpose(m: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """m^T as a new contiguous bf16 tensor, by a tiled shared-memory transpose kernel (PyTorch's strided copy of
+    `.t().contiguous()` is several times slower at these sizes)."""
+    if m.dtype != torch.bfloat16 or m.dim() != 2 or m.stride(1) != 1 or not m.is_cuda:
+        return m.t().contiguous()
+    r, c = m.shape
+    if out is None:
+        out = torch.empty(c, r, dtype=torch.bfloat16, device=m.device)
+    _native.check(_native.lib().sdc_transpose_bf16(m.data_ptr(), m.stride(0), r, c, out.data_ptr(),
+                                                   _stream_ptr(m.device)), "transpose")
+    return out
+
+
 _PREP_ACC: dict = {}
 
 
@@ -349,10 +362,10 @@ def _prep(m: torch.Tensor, transpose: bool):
     wstat = torch.empty(nb, 4, dtype=torch.float32, device=dev)
     lib = _native.lib()
     if transpose:
-        t = torch.empty(c, r, dtype=torch.bfloat16, device=dev)
+        t = transpose(m)
         wc = torch.empty(nb * abft.CS_ROWS, r, dtype=torch.bfloat16, device=dev)
         _native.check(lib.sdc_prep_rowblock(m.data_ptr(), m.stride(0), r, c, mask[0], mask[1], mask[2], mask[3],
-                                            t.data_ptr(), wc.data_ptr(), wstat.data_ptr(), acc.data_ptr(),
+                                            None, wc.data_ptr(), wstat.data_ptr(), acc.data_ptr(),
                                             _stream_ptr(dev)), "checksum prep (rows)")
         cs = abft.WeightChecksums(n=c, k=r, nb=nb, wc=wc, wstat=wstat, bsum=None, bias_max=0.0, mask=mask)
         return cs, t

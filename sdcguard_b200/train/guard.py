@@ -94,7 +94,7 @@ def _bwd_gemms(mod: "CheckedLinear", dy, x2, wb, xshape, need_x: bool, need_w: b
         if m % 8 == 0:
             xt = gemm.CheckedWeight.of_transpose(x2)            # X^T (k, m): rows = output columns of dW
             g._keep(mod.slots["dw"], xt)
-            dw = gemm.checked_linear(dy2.t().contiguous(), xt, g.table.state, mod.slots["dw"],
+            dw = gemm.checked_linear(gemm.transpose(dy2), xt, g.table.state, mod.slots["dw"],
                                      z_alarm=g.z_alarm, inject=g._take_inject(mod.name, "dw"))
         else:
             dw = dy2.t() @ x2

@@ -134,3 +134,23 @@ def test_split_k_odd_block_counts(m, n, k):
     assert rows[0]["z"] < 2.0 and rows[0]["unjudged"] == 0, rows[0]
     assert rows[1]["z"] > abft.Z_ALARM and rows[1]["row"] == r and rows[1]["block"] == c // 128, rows[1]
     assert gemm.error_word(dev).item() == 0
+
+
+@pytest.mark.parametrize("m,n,k", [(768, 768, 16384), (384, 3072, 8192)])
+def test_split_k_long_k_few_tiles(m, n, k):
+    """Long-K GEMMs with few output tiles (training dW shapes) split over K too: same output and check as unsplit."""
+    from sdcguard_b200.ops import gemm
+    torch.manual_seed(6)
+    dev = torch.device("cuda")
+    x = (torch.randn(m, k, device=dev) * 0.1).to(torch.bfloat16)
+    w = torch.randn(n, k, device=dev).to(torch.bfloat16)
+    cw = gemm.CheckedWeight(w)
+    st = gemm.StateTable(dev, 2)
+    s0, s1 = st.add("clean", cw.nb), st.add("inj", cw.nb)
+    y = gemm.checked_linear(x, cw, st.state, s0)
+    ref = x.double() @ w.double().t()
+    assert float((y.double() - ref).abs().max()) <= 2 ** -7 * float(ref.abs().max()) + 1e-3
+    gemm.checked_linear(x, cw, st.state, s1, inject=(m // 2, n // 3, 1 << 29))
+    rows = st.read()
+    assert rows[0]["z"] < 2.0 and rows[0]["unjudged"] == 0, rows[0]
+    assert rows[1]["z"] > abft.Z_ALARM and rows[1]["row"] == m // 2 and rows[1]["block"] == (n // 3) // 128

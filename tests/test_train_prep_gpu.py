@@ -133,3 +133,12 @@ def test_fused_optimizer_keeps_checks_current():
         opt.step()
         opt.zero_grad()
     assert guard.coverage()["alarms"] == 0
+
+
+@pytest.mark.parametrize("r,c", [(256, 384), (200, 136), (16384, 768), (70, 50)])
+def test_transpose_kernel(r, c):
+    from sdcguard_b200.ops import gemm
+    m = torch.randn(r, c, device="cuda").bfloat16()
+    assert torch.equal(gemm.transpose(m), m.t().contiguous())
+    big = torch.randn(r, c + 8, device="cuda").bfloat16()[:, 3:3 + c]     # a strided, unaligned view
+    assert torch.equal(gemm.transpose(big.contiguous()), big.t().contiguous())
