@@ -5,6 +5,7 @@
     sdcguard transfer-check DIR [--json]                     transfer-only coverage (exit 0 PASS, 2 HOLD)
     sdcguard transfer-compare BASE CAND [--json]             coverage preservation between two builds (always 2)
     sdcguard checksum-observer / checksum-client / native-checks  inspect | capture | verify offline evidence packets
+    sdcguard operator run --out DIR --require checksum      supervised coverage capture of this engine, then the gate
     sdcguard pd-record OUT [--gpus ...]                      record a checked prefill/decode run of this engine
     sdcguard selftest                                        GPU self-test of every checked kernel
     sdcguard campaign                                        fault-injection campaign on the GPU paths
@@ -66,6 +67,7 @@ COMMANDS = {
     "checksum-client": _lazy(".coverage.packets", "client_main"),
     "native-checks": _lazy(".coverage.packets", "native_main"),
     "pd-record": _lazy(".serve.pd", "main"),
+    "operator": _lazy(".serve.operator", "main"),
     "selftest": _lazy(".tools.selftest", "main"),
     "campaign": _lazy(".tools.campaign", "main"),
     "check": _lazy(".tools.check", "main"),
