@@ -9,7 +9,8 @@ Sections (each judged on its own evidence, never by comparing the candidate's nu
   arithmetic    FAULT (the candidate's checks alarmed, or an alert in --alerts) / NO FAULT OBSERVED (its checks ran:
                 checks went up under load and every checked op ran) / INCONCLUSIVE (no evidence that checks ran)
   protection    PROTECTED / NOT PROTECTED: `ready` on the candidate
-  isolation     ISOLATED / INFLUENCED: a request's greedy output does not depend on its batch
+  isolation     NO LEAK SEEN / LEAK / INCONCLUSIVE: a request's greedy output does not depend on the request
+                before it or on its batch
   consistency   CONSISTENT / INCONSISTENT: decoded tokens equal the prefilled prediction of the same context
   performance   OK / REGRESSED: candidate throughput at least policy min_throughput_ratio (default 0.9) of baseline
   kernels       (with --kernels) the library kernels the change added, and whether any matches a listed issue
@@ -50,7 +51,9 @@ def decide(base: dict, cand: dict, policy: Optional[dict] = None, alerts: Option
     sec = {"arithmetic": _arith(cand, alerts or [])}
     r = cand["ready"]["verdict"]
     sec["protection"] = {"verdict": "PROTECTED" if r == "PROTECTED" else "NOT PROTECTED", "ready": r}
-    sec["isolation"] = {"verdict": cand["isolation"]["verdict"], "failed": cand["isolation"]["failed"]}
+    iso = cand["isolation"]
+    sec["isolation"] = {"verdict": iso["verdict"],
+                        "failed": sum(1 for r in iso.get("probes", []) if r.get("verdict") != "NO LEAK SEEN")}
     sec["consistency"] = {"verdict": cand["consistency"]["verdict"], "checks": cand["consistency"]["checks"]}
     b, c = base["perf"]["total_tokens_per_s"], cand["perf"]["total_tokens_per_s"]
     ratio = c / b if b else 0.0
@@ -61,7 +64,7 @@ def decide(base: dict, cand: dict, policy: Optional[dict] = None, alerts: Option
         d = diff(*kernels)
         flagged = [k for k in d["only_after"] if kernels[1]["kernels"][k]["flags"]]
         sec["kernels"] = {"verdict": "FLAGGED" if flagged else "OK", "added": d["only_after"], "flagged": flagged}
-    passing = {"arithmetic": "NO FAULT OBSERVED", "protection": "PROTECTED", "isolation": "ISOLATED",
+    passing = {"arithmetic": "NO FAULT OBSERVED", "protection": "PROTECTED", "isolation": "NO LEAK SEEN",
                "consistency": "CONSISTENT", "performance": "OK", "kernels": "OK"}
     failed = [k for k, v in sec.items() if v["verdict"] != passing[k] and k not in pol["waive"]]
     if sec["arithmetic"]["verdict"] == "FAULT":

@@ -1,13 +1,27 @@
-"""Cross-request influence probe: does what other requests are doing change a request's greedy output?
+"""Does one request's answer depend on other requests? Two probes against a running server of this package
+(`sdcguard serve`, or any server with the same token-id completions API):
 
-    python -m sdcguard_b200.tools.isolation http://127.0.0.1:8000 --probes 4 --primers 8
+    python -m sdcguard_b200.tools.isolation http://127.0.0.1:8000 --probes 4 --primers 3 --repeats 2
 
-Each probe prompt is sent alone (twice: the server must repeat itself), then again while `primers` other requests
-with different prompts and lengths run concurrently. With greedy decoding every token must match the solo answer.
-A difference means the result depends on the batch it shared (batch-dependent kernels, a shared-state bug, or a
-fault in one of the co-scheduled paths). Exit code 0 when every probe matched, 1 otherwise.
+A server can compute every GEMM right and still answer one request with another's data: a stale buffer, a KV page
+reused too early, a cached prefix read from the wrong pages. Checks of the arithmetic cannot see these.
 
-Reference: src/sdcguard/isolation.py (`primer_probe` :95).
+1. Primer dependence. A probe prompt is sent alone, greedy, right after a primer request that also ran alone; each
+   (primer, probe) pair is repeated. On an isolated server the probe's tokens do not depend on which primer came
+   before. The control is the probe after the same primer, repeated: it must agree exactly, otherwise the server is
+   not deterministic at batch size 1 and the probe can judge nothing.
+2. Concurrency. The probe is sent while other requests of different prompts and lengths run in the same batches; a
+   batch-dependent answer is reported.
+
+Verdicts: LEAK (a probe's answer changed with the primer in the same way every time that primer came before it,
+while every control repeat agreed; or a concurrent answer differed from the solo one on a server whose solo repeats
+agree), NO LEAK SEEN (neither, with every control agreeing), INCONCLUSIVE (a control disagreed, a request failed, or
+answers changed in ways that do not repeat with their primer: one differing token cannot be told from a server that
+is not deterministic). NO LEAK SEEN covers these prompts, this load and this server only. Exit 0 / 1 (LEAK) / 2.
+
+Reference: src/sdcguard/isolation.py:1-40 (the probes and verdict rules; the canary probe that looks for another
+request's random code in an answer needs a trained model that copies its context, which this package's random-init
+serving shapes are not).
 """
 from __future__ import annotations
 
@@ -15,48 +29,112 @@ import argparse
 import json
 import random
 import threading
-from typing import Callable
+from typing import Callable, Optional
 
 from . import _client
 
+SCHEMA = "sdcguard.isolation/1"
 
-def run(base: str, probes: int = 4, primers: int = 8, prompt: int = 64, tokens: int = 16, seed: int = 0,
-        vocab: int = 1000, complete: Callable = _client.complete) -> dict:
+
+def _first_diff(a, b) -> Optional[int]:
+    if a is None or b is None:
+        return 0
+    for i, (x, y) in enumerate(zip(a, b)):
+        if x != y:
+            return i
+    return None if len(a) == len(b) else min(len(a), len(b))
+
+
+def primer_probe(base: str, probe: list, primers: list, repeats: int, tokens: int, complete: Callable) -> dict:
+    """The probe's answers after each primer, `repeats` times each (primer and probe sent one after the other)."""
+    answers: dict = {}
+    for rep in range(repeats):
+        for pi, pr in enumerate(primers):
+            complete(base, pr, tokens)
+            answers.setdefault(pi, []).append(complete(base, probe, tokens))
+    controls_agree = all(all(a == ans[0] for a in ans) for ans in answers.values())
+    # the answer after each primer (its repeats agree), and whether it differs from the first primer's
+    per = {pi: ans[0] for pi, ans in answers.items() if all(a == ans[0] for a in ans)}
+    base_ans = per.get(0)
+    changed_repeatably = [pi for pi, a in per.items() if pi != 0 and base_ans is not None and a != base_ans]
+    unstable = [pi for pi, ans in answers.items() if pi not in per]
+    if not controls_agree:
+        verdict = "INCONCLUSIVE"
+    elif changed_repeatably:
+        verdict = "LEAK"
+    else:
+        verdict = "NO LEAK SEEN"
+    return {"verdict": verdict, "controls_agree": controls_agree, "unstable_primers": unstable,
+            "primers_changing_the_answer": changed_repeatably,
+            "first_difference": {pi: _first_diff(base_ans, per[pi]) for pi in changed_repeatably}}
+
+
+def concurrency_probe(base: str, probe: list, others: list, tokens: int, complete: Callable) -> dict:
+    solo = complete(base, probe, tokens)
+    again = complete(base, probe, tokens)
+    got: dict = {}
+
+    def fire(key, ids):
+        try:
+            got[key] = complete(base, ids, tokens)
+        except Exception as e:  # noqa: BLE001  (a failed request makes the probe inconclusive)
+            got[key] = e
+    th = [threading.Thread(target=fire, args=(i, x)) for i, x in enumerate(others)]
+    th.append(threading.Thread(target=fire, args=("probe", probe)))
+    for t in th:
+        t.start()
+    for t in th:
+        t.join()
+    mixed = got.get("probe")
+    failed = any(isinstance(v, Exception) for v in got.values())
+    if failed or solo != again:
+        verdict = "INCONCLUSIVE"
+    else:
+        verdict = "LEAK" if mixed != solo else "NO LEAK SEEN"
+    return {"verdict": verdict, "solo_repeats_agree": solo == again, "failed_requests": failed,
+            "first_difference": None if isinstance(mixed, Exception) else _first_diff(solo, mixed)}
+
+
+def run(base: str, probes: int = 4, primers: int = 3, repeats: int = 2, prompt: int = 24, tokens: int = 16,
+        others: int = 8, seed: int = 0, vocab: int = 1000, complete: Callable = _client.complete) -> dict:
     rng = random.Random(seed)
     rows = []
     for p in range(probes):
-        ids = [rng.randrange(vocab) for _ in range(prompt)]
-        solo = complete(base, ids, tokens)
-        again = complete(base, ids, tokens)
-        prim = [[rng.randrange(vocab) for _ in range(rng.randrange(8, 4 * prompt))] for _ in range(primers)]
-        got: dict = {}
-
-        def fire(i, x):
-            got[i] = complete(base, x, tokens)
-
-        th = [threading.Thread(target=fire, args=(i, x)) for i, x in enumerate(prim)]
-        th.append(threading.Thread(target=fire, args=("probe", ids)))
-        for t in th:
-            t.start()
-        for t in th:
-            t.join()
-        mixed = got.get("probe")
-        rows.append({"probe": p, "repeat_matches": solo == again, "with_primers_matches": mixed == solo,
-                     "first_difference": next((i for i, (a, b) in enumerate(zip(solo, mixed or [])) if a != b), None)})
-    bad = [r for r in rows if not (r["repeat_matches"] and r["with_primers_matches"])]
-    return {"url": base, "probes": rows, "verdict": "ISOLATED" if not bad else "INFLUENCED", "failed": len(bad)}
+        probe = [rng.randrange(vocab) for _ in range(prompt)]
+        prim = [[rng.randrange(vocab) for _ in range(rng.randrange(8, 6 * prompt))] for _ in range(primers)]
+        conc = [[rng.randrange(vocab) for _ in range(rng.randrange(8, 6 * prompt))] for _ in range(others)]
+        try:
+            a = primer_probe(base, probe, prim, repeats, tokens, complete)
+            b = concurrency_probe(base, probe, conc, tokens, complete)
+        except Exception as e:  # noqa: BLE001
+            rows.append({"probe": p, "verdict": "INCONCLUSIVE", "error": str(e)[:300]})
+            continue
+        v = ("LEAK" if "LEAK" in (a["verdict"], b["verdict"]) else
+             "INCONCLUSIVE" if "INCONCLUSIVE" in (a["verdict"], b["verdict"]) else "NO LEAK SEEN")
+        rows.append({"probe": p, "verdict": v, "primer": a, "concurrency": b})
+    verdicts = [r["verdict"] for r in rows]
+    verdict = ("LEAK" if "LEAK" in verdicts else "INCONCLUSIVE" if "INCONCLUSIVE" in verdicts or not rows
+               else "NO LEAK SEEN")
+    return {"schema": SCHEMA, "url": base, "verdict": verdict, "probes": rows,
+            "scope": "these prompts, this load and this server only"}
 
 
 def main(argv=None) -> int:
-    ap = argparse.ArgumentParser(prog="python -m sdcguard_b200.tools.isolation")
+    ap = argparse.ArgumentParser(prog="sdcguard isolation")
     ap.add_argument("url")
     ap.add_argument("--probes", type=int, default=4)
-    ap.add_argument("--primers", type=int, default=8)
+    ap.add_argument("--primers", type=int, default=3)
+    ap.add_argument("--repeats", type=int, default=2)
+    ap.add_argument("--tokens", type=int, default=16)
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--out")
     a = ap.parse_args(argv)
-    r = run(a.url, a.probes, a.primers, seed=a.seed)
-    print(json.dumps(r))
-    return 0 if r["verdict"] == "ISOLATED" else 1
+    r = run(a.url, a.probes, a.primers, a.repeats, tokens=a.tokens, seed=a.seed)
+    if a.out:
+        with open(a.out, "w") as f:
+            json.dump(r, f, indent=1)
+    print(json.dumps({k: v for k, v in r.items() if k != "probes"}))
+    return {"NO LEAK SEEN": 0, "LEAK": 1}.get(r["verdict"], 2)
 
 
 if __name__ == "__main__":

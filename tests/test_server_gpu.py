@@ -36,7 +36,7 @@ def test_server_probes(tmp_path):
     try:
         r = ready.check(url, probe=True)
         assert r["verdict"] == "PROTECTED", r
-        assert isolation.run(url, probes=2, primers=6)["verdict"] == "ISOLATED"
+        assert isolation.run(url, probes=2, primers=3)["verdict"] == "NO LEAK SEEN"
         c = consistency.run(url, probes=2)
         assert c["verdict"] == "CONSISTENT", c
         p = perf.run(url, clients=4, prompt=64, tokens=8, seconds=3)

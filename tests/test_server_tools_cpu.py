@@ -1,5 +1,7 @@
 """Server probes against fakes (no GPU): readiness verdicts from metrics, isolation and consistency against a
 deterministic fake model, throughput bookkeeping, and the stack-change decision."""
+import threading
+
 from sdcguard_b200.tools import _client, consistency, decide, isolation, perf, ready
 
 
@@ -41,7 +43,7 @@ def test_ready_verdicts():
 
 
 def test_isolation_consistency_perf_on_fake_model():
-    assert isolation.run("x", probes=2, primers=3, complete=fake_complete)["verdict"] == "ISOLATED"
+    assert isolation.run("x", probes=2, primers=3, complete=fake_complete)["verdict"] == "NO LEAK SEEN"
     assert consistency.run("x", probes=2, complete=fake_complete)["verdict"] == "CONSISTENT"
     calls = [0]
 
@@ -50,7 +52,22 @@ def test_isolation_consistency_perf_on_fake_model():
         out = fake_complete(base, prompt, n)
         return [out[0] + 1] + out[1:] if calls[0] == 3 else out
 
-    assert isolation.run("x", probes=1, primers=0, complete=flaky)["verdict"] == "INFLUENCED"
+    calls[0] = -100                          # (the concurrency probe's batched call comes after the primer probe)
+
+    def batch_dependent(base, prompt, n):    # the probe's answer changes when other requests share its batch
+        out = fake_complete(base, prompt, n)
+        batched = threading.current_thread() is not threading.main_thread()     # sent beside other requests
+        return [out[0] + 1] + out[1:] if batched and len(prompt) == 24 else out
+    assert isolation.run("x", probes=1, primers=2, complete=batch_dependent)["verdict"] == "LEAK"
+
+    state = {"last": None}
+
+    def remembers(base, prompt, n):          # the answer depends on the previous request: a stale buffer
+        out = fake_complete(base, prompt, n)
+        prev, state["last"] = state["last"], prompt
+        return [(out[0] + len(prev or [])) % 1000] + out[1:] if len(prompt) == 24 else out
+    assert isolation.run("x", probes=1, primers=3, complete=remembers)["verdict"] == "LEAK"
+    del flaky
 
     def bad_prefill(base, prompt, n):
         out = fake_complete(base, prompt, n)
@@ -62,11 +79,11 @@ def test_isolation_consistency_perf_on_fake_model():
     assert p["requests"] == 10 and p["errors"] == 0 and p["latency_ms"]["p50"] is not None
 
 
-def _result(tps=100.0, alarms=0, iso="ISOLATED", cons="CONSISTENT", readyv="PROTECTED", checks=50):
+def _result(tps=100.0, alarms=0, iso="NO LEAK SEEN", cons="CONSISTENT", readyv="PROTECTED", checks=50):
     text = (f"sdcguard_protected 1\nsdcguard_checks_total {checks}\nsdcguard_alarms_total {alarms}\n"
             "sdcguard_ops_total 4\nsdcguard_ops_checked 4\n")
     return {"ready": {"verdict": readyv}, "perf": {"total_tokens_per_s": tps, "errors": 0},
-            "isolation": {"verdict": iso, "failed": 0}, "consistency": {"verdict": cons, "checks": 4},
+            "isolation": {"verdict": iso, "probes": []}, "consistency": {"verdict": cons, "checks": 4},
             "metrics": text, "stack": {"model": "tiny"}}
 
 
@@ -77,4 +94,4 @@ def test_decide_sections():
     assert decide.decide(_result(), _result(50.0), {"waive": ["performance"]})["decision"] == "ACCEPT"
     assert decide.decide(_result(), _result(alarms=2))["decision"] == "REJECT"
     assert decide.decide(_result(), _result(checks=0))["decision"] == "INCONCLUSIVE"
-    assert decide.decide(_result(), _result(iso="INFLUENCED"))["failed"] == ["isolation"]
+    assert decide.decide(_result(), _result(iso="LEAK"))["failed"] == ["isolation"]
