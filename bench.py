@@ -27,6 +27,7 @@ import json
 import os
 import statistics
 import subprocess
+import threading
 import sys
 import time
 
@@ -280,7 +281,11 @@ def _child_env(local: int, checked: bool) -> dict:
            if k not in ("RANK", "LOCAL_RANK", "WORLD_SIZE", "LOCAL_WORLD_SIZE", "GROUP_RANK", "ROLE_RANK",
                         "ROLE_WORLD_SIZE", "MASTER_ADDR", "MASTER_PORT", "TORCHELASTIC_RUN_ID",
                         "TORCHELASTIC_RESTART_COUNT", "TORCHELASTIC_MAX_RESTARTS", "GROUP_WORLD_SIZE")}
-    env["CUDA_VISIBLE_DEVICES"] = str(local)
+    # this rank's GPU: the local-th entry of the job's visible devices (all ranks share the first one with
+    # SDCGUARD_REF_SAME_GPU=1, which tests the multi-rank plumbing on one GPU)
+    visible = [d for d in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if d.strip()]
+    pick = 0 if os.environ.get("SDCGUARD_REF_SAME_GPU") == "1" else local
+    env["CUDA_VISIBLE_DEVICES"] = visible[pick] if pick < len(visible) else str(pick)
     env["PYTHONPATH"] = _ref_dir() + os.pathsep + env.get("PYTHONPATH", "")
     env["VLLM_ENABLE_V1_MULTIPROCESSING"] = "0"       # engine core in this process: CUDA events see its work
     env["HF_HUB_OFFLINE"] = "1"
@@ -355,13 +360,25 @@ def _ref_phase(args, rank, world, local, checked: bool) -> dict:
     cmd = [sys.executable, os.path.abspath(__file__), "--ref-child", "checked" if checked else "unchecked",
            "--ref-rank", str(rank), "--steps", str(args.steps), "--warmup", str(args.warmup),
            "--requests", str(args.requests), "--new-tokens", str(args.new_tokens)]
-    log = open(f"/tmp/sdcguard_ref_{'c' if checked else 'u'}_{rank}.log", "w")
+    log_dir = os.environ.get("SDCGUARD_REF_LOG_DIR", "/tmp")
+    os.makedirs(log_dir, exist_ok=True)
+    log = open(os.path.join(log_dir, f"sdcguard_ref_{'c' if checked else 'u'}_{rank}.log"), "w")
     p = subprocess.Popen(cmd, env=_child_env(local, checked), stdin=subprocess.PIPE, stdout=subprocess.PIPE,
                          stderr=log, text=True)
+    # the engine must report READY within SDCGUARD_REF_START_S seconds (default 600): a watchdog ends a child that
+    # hangs in its startup, so every rank reaches the agreement below in bounded time and the line names the cause
+    start_limit = float(os.environ.get("SDCGUARD_REF_START_S", "600"))
+    ready_seen = threading.Event()
+
+    def watchdog():
+        if not ready_seen.wait(start_limit) and p.poll() is None:
+            p.kill()
+    threading.Thread(target=watchdog, daemon=True).start()
     ok = False
     for line in p.stdout:
         if line.strip() == "READY":
             ok = True
+            ready_seen.set()
             break
     flag = torch.tensor([1 if ok else 0], dtype=torch.int64)
     if world > 1:
