@@ -12,6 +12,8 @@ Endpoints
                          sdcguard_polls_total (check results read back), sdcguard_requests_total,
                          sdcguard_prompt_tokens_total, sdcguard_generated_tokens_total, sdcguard_worker_info{gpu, uuid,
                          pid, started} and sdcguard_stack_info{model, precision, checked, torch, cuda, weights_digest}.
+  POST /v1/score         {"prompt": [token ids], "top_k": k}: teacher-forced top-k log-probabilities of every position
+                         (one prefill): {"top_logprobs": [[...]], "top_ids": [[...]]}, position p predicting token p + 1.
   GET  /health, GET /v1/models, GET /sdcguard/status (coverage report and events as JSON).
 
 Requests are batched: a worker thread takes the first waiting request and every other one that arrives within the
@@ -38,8 +40,9 @@ from ..numerics import abft
 
 
 class Request:
-    def __init__(self, ids: list[int], max_tokens: int):
+    def __init__(self, ids: list[int], max_tokens: int, score_topk: int = 0):
         self.ids, self.max_tokens = ids, max_tokens
+        self.score_topk = score_topk          # > 0: a teacher-forced scoring request instead of a generation
         self.done = threading.Event()
         self.out: Optional[list[int]] = None
         self.error: Optional[str] = None
@@ -84,12 +87,39 @@ class Server:
             raise RuntimeError(r.error)
         return r.out
 
+    def score(self, ids: list[int], topk: int, timeout: float = 600.0) -> dict:
+        """Teacher-forced top-k log-probabilities of every position of `ids` (one prefill, checks included)."""
+        r = Request(ids, 0, score_topk=max(1, min(int(topk), 20)))
+        self.q.put(r)
+        if not r.done.wait(timeout):
+            raise TimeoutError("request timed out")
+        if r.error:
+            raise RuntimeError(r.error)
+        return r.out
+
+    def _run_score(self, r: Request) -> None:
+        try:
+            (v, i), = self.eng.score([r.ids], r.score_topk)
+            ev = self.eng.guard.poll()
+            with self.lock:
+                self.events.extend(ev)
+                self.counters["polls"] += 1
+                self.counters["requests"] += 1
+                self.counters["prompt_tokens"] += len(r.ids)
+            r.out = {"top_logprobs": v.tolist(), "top_ids": i.tolist()}
+        except Exception as e:  # noqa: BLE001  (returned to the request)
+            r.error = f"{type(e).__name__}: {e}"
+        r.done.set()
+
     def _worker(self) -> None:
         torch.cuda.set_device(self.eng.device)
         while not self.stop.is_set():
             try:
                 first = self.q.get(timeout=0.1)
             except queue.Empty:
+                continue
+            if first.score_topk:
+                self._run_score(first)
                 continue
             batch = [first]
             t_end = time.time() + self.window
@@ -98,9 +128,13 @@ class Server:
                 if left <= 0:
                     break
                 try:
-                    batch.append(self.q.get(timeout=left))
+                    nxt = self.q.get(timeout=left)
                 except queue.Empty:
                     break
+                if nxt.score_topk:            # scoring runs on its own, after this batch
+                    self._run_score(nxt)
+                    continue
+                batch.append(nxt)
             try:
                 L = max(len(r.ids) for r in batch)
                 prompts = torch.zeros(len(batch), L, dtype=torch.long)
@@ -176,6 +210,17 @@ def make_app(server: Server):
                 "choices": [{"index": 0, "token_ids": out, "text": " ".join(map(str, out)), "finish_reason": "length"}],
                 "usage": {"prompt_tokens": len(ids), "completion_tokens": len(out),
                           "total_tokens": len(ids) + len(out)}}
+
+    @app.post("/v1/score")
+    def score(body: dict):
+        """{"prompt": token ids, "top_k": k} -> per position p the top-k log-probabilities of token p + 1."""
+        try:
+            ids = server.tokens(body.get("prompt", ""))
+            return server.score(ids, int(body.get("top_k", 5)))
+        except ValueError as e:
+            raise HTTPException(status_code=400, detail=str(e)) from e
+        except (RuntimeError, TimeoutError) as e:
+            raise HTTPException(status_code=500, detail=str(e)) from e
 
     @app.get("/metrics", response_class=PlainTextResponse)
     def metrics():

@@ -28,6 +28,11 @@ def complete(base: str, prompt, max_tokens: int, timeout: float = 600.0) -> list
     return r["choices"][0]["token_ids"]
 
 
+def score(base: str, prompt, top_k: int = 5, timeout: float = 600.0) -> dict:
+    """Teacher-forced top-k log-probabilities of every position (POST /v1/score)."""
+    return post(base.rstrip("/") + "/v1/score", {"prompt": prompt, "top_k": top_k}, timeout)
+
+
 def parse_metrics(text: str) -> dict:
     """{name: value} for unlabelled samples; {name: [(labels, value), ...]} under name + '{}' for labelled ones."""
     out: dict = {}

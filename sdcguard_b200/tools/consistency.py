@@ -1,54 +1,120 @@
-"""Decode-versus-prefill consistency probe: the token a server decoded must be the token it predicts when the same
-context arrives as a prompt.
+"""Does a server give the same answer along its different serving paths? Decode against prefill:
 
-    python -m sdcguard_b200.tools.consistency http://127.0.0.1:8000 --probes 4 --tokens 16
+    python -m sdcguard_b200.tools.consistency http://127.0.0.1:8000 --probes 4 --tokens 24
 
-For each probe prompt P the server generates t_1..t_n. Then, for a few cut points k, the prompt P + t_1..t_k is sent
-with max_tokens 1: the answer must be t_(k+1). The first path computes position |P| + k in a decode step (one row,
-reading the KV cache); the second in a prefill (a tile of rows, fresh KV); with deterministic kernels and no fault
-both give the same greedy token, except when the two top logits are within rounding of each other (reported as a
-near tie only if the tokens differ and the server repeats itself). A prefix cache, KV transfer or decode kernel that
-corrupts state shows up here as a mismatch.
+A server reaches a token by different code depending on its state: decoded one at a time against the KV cache, or
+computed in one prefill over the whole context. Each path has its own kernels (split-KV decode attention against
+paged prefill attention, decode-sized GEMMs against prefill-sized ones) and bookkeeping, and a fault or bug can live
+in one path only.
 
-Reference: src/sdcguard/consistency.py (`prefix_probe` :143).
+For each probe prompt P the server decodes t_1..t_n greedily. Two checks:
+
+1. Cut points: P + t_1..t_k sent as a new prompt with max_tokens 1 must give t_(k+1) (position |P| + k computed by
+   a prefill instead of a decode step).
+2. Log-probabilities: P + t_1..t_n scored in one teacher-forced prefill (POST /v1/score, top-k log-probabilities of
+   every position). At every position the decoded token must be the prefill's top token, or within MIN_GAP nats of
+   it. A decoded token that the prefill ranks more than MIN_GAP nats below its top token, at a position where the
+   prefill is sure of its top token (top two MIN_MARGIN nats apart), is a mismatch; a decoded token outside the
+   prefill's top-k is a mismatch unless the k-th entry is within MIN_GAP of the top. Near ties between the top two
+   prefill tokens are reported but do not count: rounding differences between the two paths can flip them.
+
+Verdicts: CONSISTENT (no mismatch), INCONSISTENT (a mismatch), INCONCLUSIVE (a request failed or the server does not
+score). CONSISTENT covers these prompts and this server only. Exit 0 / 1 / 2.
+
+Reference: src/sdcguard/consistency.py:1-45 (the decode-versus-prefill probe and its MIN_GAP / MIN_MARGIN lines; the
+prefix-cache probe applies to servers with a prefix cache, which this package's engine does not keep).
 """
 from __future__ import annotations
 
 import argparse
 import json
 import random
-from typing import Callable
+from typing import Callable, Optional
 
 from . import _client
 
+SCHEMA = "sdcguard.consistency/1"
+MIN_GAP = 0.5       # nats
+MIN_MARGIN = 1.0    # nats
 
-def run(base: str, probes: int = 4, prompt: int = 48, tokens: int = 16, cuts=(1, 4, 8, 15), seed: int = 0,
-        vocab: int = 1000, complete: Callable = _client.complete) -> dict:
+
+def logprob_check(prompt_len: int, gen: list, scored: dict) -> dict:
+    """Compare decoded tokens with the teacher-forced prefill distribution of the same context."""
+    vals, ids = scored["top_logprobs"], scored["top_ids"]
+    rows, ties, compared = [], 0, 0
+    for j, tok in enumerate(gen):
+        pos = prompt_len + j - 1                     # the position whose distribution predicts gen[j]
+        if pos < 0 or pos >= len(vals):
+            continue
+        v, i = vals[pos], ids[pos]
+        compared += 1
+        top, margin = v[0], (v[0] - v[1]) if len(v) > 1 else float("inf")
+        if tok == i[0]:
+            continue
+        if margin < MIN_GAP:
+            ties += 1
+            continue
+        if tok in i:
+            gap = top - v[i.index(tok)]
+        else:
+            gap = top - v[-1]                        # at least this far below the top
+            if gap < MIN_GAP:
+                ties += 1
+                continue
+        if gap > MIN_GAP and margin >= MIN_MARGIN:
+            rows.append({"generated_index": j, "decoded": tok, "prefill_top": i[0], "gap_nats": round(gap, 4),
+                         "prefill_margin_nats": round(margin, 4)})
+        else:
+            ties += 1
+    return {"mismatches": rows, "near_ties": ties, "compared": compared}
+
+
+def run(base: str, probes: int = 4, prompt: int = 48, tokens: int = 24, cuts=(1, 4, 8, 15), seed: int = 0,
+        vocab: int = 1000, top_k: int = 5, complete: Callable = _client.complete,
+        score: Optional[Callable] = _client.score) -> dict:
     rng = random.Random(seed)
-    rows = []
+    cut_rows, lp_rows, ties, failed, compared = [], [], 0, [], 0
     for p in range(probes):
         ids = [rng.randrange(vocab) for _ in range(prompt)]
-        gen = complete(base, ids, tokens)
-        for k in cuts:
-            if k >= len(gen):
-                continue
-            nxt = complete(base, ids + gen[:k], 1)
-            rows.append({"probe": p, "cut": k, "decoded": gen[k], "prefilled": nxt[0], "match": nxt[0] == gen[k]})
-    bad = [r for r in rows if not r["match"]]
-    return {"url": base, "checks": len(rows), "mismatches": bad, "verdict": "CONSISTENT" if not bad else
-            "INCONSISTENT"}
+        try:
+            gen = complete(base, ids, tokens)
+            for k in cuts:
+                if k >= len(gen):
+                    continue
+                nxt = complete(base, ids + gen[:k], 1)
+                cut_rows.append({"probe": p, "cut": k, "decoded": gen[k], "prefilled": nxt[0],
+                                 "match": nxt[0] == gen[k]})
+            if score is not None:
+                lp = logprob_check(len(ids), gen, score(base, ids + gen, top_k))
+                ties += lp["near_ties"]
+                compared += lp["compared"]
+                lp_rows += [dict(r, probe=p) for r in lp["mismatches"]]
+        except Exception as e:  # noqa: BLE001  (a failed request makes the verdict inconclusive)
+            failed.append({"probe": p, "error": str(e)[:300]})
+    bad = [r for r in cut_rows if not r["match"]]
+    verdict = ("INCONSISTENT" if bad or lp_rows else
+               "INCONCLUSIVE" if failed or not (cut_rows or compared) else "CONSISTENT")
+    return {"schema": SCHEMA, "url": base, "verdict": verdict, "checks": len(cut_rows),
+            "logprob_positions": compared, "mismatches": bad,
+            "logprob_mismatches": lp_rows, "near_ties": ties, "failed": failed,
+            "scope": "these prompts and this server only"}
 
 
 def main(argv=None) -> int:
-    ap = argparse.ArgumentParser(prog="python -m sdcguard_b200.tools.consistency")
+    ap = argparse.ArgumentParser(prog="sdcguard consistency")
     ap.add_argument("url")
     ap.add_argument("--probes", type=int, default=4)
-    ap.add_argument("--tokens", type=int, default=16)
+    ap.add_argument("--tokens", type=int, default=24)
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-score", action="store_true", help="cut points only (for servers without /v1/score)")
+    ap.add_argument("--out")
     a = ap.parse_args(argv)
-    r = run(a.url, a.probes, tokens=a.tokens, seed=a.seed)
-    print(json.dumps(r))
-    return 0 if r["verdict"] == "CONSISTENT" else 1
+    r = run(a.url, a.probes, tokens=a.tokens, seed=a.seed, score=None if a.no_score else _client.score)
+    if a.out:
+        with open(a.out, "w") as f:
+            json.dump(r, f, indent=1)
+    print(json.dumps({k: v for k, v in r.items() if k not in ("mismatches", "logprob_mismatches")}))
+    return {"CONSISTENT": 0, "INCONSISTENT": 1}.get(r["verdict"], 2)
 
 
 if __name__ == "__main__":

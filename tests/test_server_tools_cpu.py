@@ -18,6 +18,16 @@ def fake_complete(base, prompt, n):
     return out
 
 
+def fake_score(base, prompt, k):
+    """Teacher-forced scores of the fake model: at each position its next token first (margin 3 nats)."""
+    vals, ids = [], []
+    for p in range(len(prompt)):
+        t = _next(list(prompt[: p + 1]))
+        ids.append([t] + [(t + j) % 1000 for j in range(1, k)])
+        vals.append([-0.1] + [-3.1 - j for j in range(1, k)])
+    return {"top_logprobs": vals, "top_ids": ids}
+
+
 def _metrics(checks, tokens, alarms=0, protected=1, ops=10, ops_checked=10, polls=3, started="1", line=6.0):
     return _client.parse_metrics(
         f"sdcguard_protected {protected}\nsdcguard_checks_total {checks}\nsdcguard_alarms_total {alarms}\n"
@@ -44,7 +54,20 @@ def test_ready_verdicts():
 
 def test_isolation_consistency_perf_on_fake_model():
     assert isolation.run("x", probes=2, primers=3, complete=fake_complete)["verdict"] == "NO LEAK SEEN"
-    assert consistency.run("x", probes=2, complete=fake_complete)["verdict"] == "CONSISTENT"
+    assert consistency.run("x", probes=2, complete=fake_complete, score=fake_score)["verdict"] == "CONSISTENT"
+
+    def wrong_decode(base, prompt, n):     # decode goes wrong after 3 tokens, while prefill paths are right
+        out = fake_complete(base, prompt, n)
+        return out[:3] + [(t + 7) % 1000 for t in out[3:]] if n > 1 else out
+    r = consistency.run("x", probes=1, cuts=(), complete=wrong_decode, score=fake_score)
+    assert r["verdict"] == "INCONSISTENT" and r["logprob_mismatches"][0]["generated_index"] == 3
+
+    def tied_score(base, prompt, k):       # a near tie at every position: reported, never counted
+        d = fake_score(base, prompt, k)
+        d["top_logprobs"] = [[-0.1, -0.2] + v[2:] for v in d["top_logprobs"]]
+        return d
+    r = consistency.run("x", probes=1, cuts=(), complete=wrong_decode, score=tied_score)
+    assert r["verdict"] == "CONSISTENT" and r["near_ties"] > 0 and not r["logprob_mismatches"]
     calls = [0]
 
     def flaky(base, prompt, n):          # the 3rd call (the batched one) differs: a batch-dependent server
@@ -73,7 +96,7 @@ def test_isolation_consistency_perf_on_fake_model():
         out = fake_complete(base, prompt, n)
         return [(out[0] + 1) % 1000] if n == 1 else out
 
-    r = consistency.run("x", probes=1, complete=bad_prefill)
+    r = consistency.run("x", probes=1, complete=bad_prefill, score=None)
     assert r["verdict"] == "INCONSISTENT" and len(r["mismatches"]) == 4
     p = perf.run("x", clients=2, prompt=8, tokens=4, seconds=0.2, max_requests=10, complete=fake_complete)
     assert p["requests"] == 10 and p["errors"] == 0 and p["latency_ms"]["p50"] is not None
