@@ -118,3 +118,16 @@ def test_decide_sections():
     assert decide.decide(_result(), _result(alarms=2))["decision"] == "REJECT"
     assert decide.decide(_result(), _result(checks=0))["decision"] == "INCONCLUSIVE"
     assert decide.decide(_result(), _result(iso="LEAK"))["failed"] == ["isolation"]
+
+
+def test_perf_measure_and_compare():
+    m = perf.measure("x", rounds=3, warmup=0.05, clients=2, prompt=8, tokens=4, seconds=0.1, complete=fake_complete)
+    assert len(m["rounds"]) == 3 and m["errors"] == 0 and m["spread"] is not None
+    base = {"total_tokens_per_s": 100.0, "errors": 0, "spread": 0.01, "rounds": [1, 2],
+            "latency_ms": {"p50": 10.0}}
+    assert perf.compare(base, dict(base, total_tokens_per_s=110.0))["verdict"] == "FASTER"
+    assert perf.compare(base, dict(base, total_tokens_per_s=101.0))["verdict"] == "SAME"
+    assert perf.compare(base, dict(base, total_tokens_per_s=90.0))["verdict"] == "SLOWER"
+    noisy = dict(base, spread=0.2)
+    assert perf.compare(base, dict(noisy, total_tokens_per_s=110.0))["verdict"] == "SAME"
+    assert perf.compare(base, dict(base, errors=1))["verdict"] == "INCONCLUSIVE"
