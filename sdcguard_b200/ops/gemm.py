@@ -301,7 +301,7 @@ class CheckedWeight:
         n, k = w.shape
         if n % 8 or k % 8:
             raise ValueError(f"checked GEMM needs n and k multiples of 8 (got n={n}, k={k})")
-        cs = _prep(w, transpose=False)
+        cs = _prep(w, transposed=False)
         if bias is not None:
             # the bias's largest magnitude is not read back here (a host read per layer would stall a training
             # step): 0 means a non-finite output counts as corruption unless the weights and inputs can produce it
@@ -321,7 +321,7 @@ class CheckedWeight:
         r, c = m.shape
         if r % 8 or c % 8:
             raise ValueError(f"checked GEMM needs n and k multiples of 8 (got {c} x {r})")
-        cs, t = _prep(m, transpose=True)
+        cs, t = _prep(m, transposed=True)
         return cls._assemble(t, cs, None, c1, c2, c3)
 
 
@@ -350,18 +350,18 @@ def transpose(m: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tens
 _PREP_ACC: dict = {}
 
 
-def _prep(m: torch.Tensor, transpose: bool):
+def _prep(m: torch.Tensor, transposed: bool):
     """Device checksum data: of B = m (transpose False) or of B = m^T (True, also returning m^T)."""
     dev = m.device
     r, c = m.shape
     mask = abft.sign_mask()
-    nb = -(-(c if transpose else r) // abft.BLOCK)
+    nb = -(-(c if transposed else r) // abft.BLOCK)
     acc = _PREP_ACC.get(dev)
     if acc is None or acc.numel() < nb * 4:
         acc = _PREP_ACC[dev] = torch.empty(max(nb * 4, 1024), dtype=torch.float32, device=dev)
     wstat = torch.empty(nb, 4, dtype=torch.float32, device=dev)
     lib = _native.lib()
-    if transpose:
+    if transposed:
         t = transpose(m)
         wc = torch.empty(nb * abft.CS_ROWS, r, dtype=torch.bfloat16, device=dev)
         _native.check(lib.sdc_prep_rowblock(m.data_ptr(), m.stride(0), r, c, mask[0], mask[1], mask[2], mask[3],
