@@ -277,10 +277,13 @@ def _child_env(local: int, checked: bool) -> dict:
     """Environment of one reference serving process: this rank's GPU only, no torchrun variables (the engine
     builds its own one-process world), the reference package first on the path so vLLM finds its plugin entry
     point, and the plugin on (SDCGUARD=1, its stock defaults) or off."""
+    # torchrun's variables, every TORCHELASTIC_* among them: with TORCHELASTIC_USE_AGENT_STORE set, torch's TCP
+    # rendezvous connects as a client to a store the elastic agent would host, so the engine's own one-process
+    # group would wait for a server that never starts
     env = {k: v for k, v in os.environ.items()
            if k not in ("RANK", "LOCAL_RANK", "WORLD_SIZE", "LOCAL_WORLD_SIZE", "GROUP_RANK", "ROLE_RANK",
-                        "ROLE_WORLD_SIZE", "MASTER_ADDR", "MASTER_PORT", "TORCHELASTIC_RUN_ID",
-                        "TORCHELASTIC_RESTART_COUNT", "TORCHELASTIC_MAX_RESTARTS", "GROUP_WORLD_SIZE")}
+                        "ROLE_NAME", "ROLE_WORLD_SIZE", "MASTER_ADDR", "MASTER_PORT", "GROUP_WORLD_SIZE")
+           and not k.startswith(("TORCHELASTIC_", "TORCH_ELASTIC_"))}
     # this rank's GPU: the local-th entry of the job's visible devices (all ranks share the first one with
     # SDCGUARD_REF_SAME_GPU=1, which tests the multi-rank plumbing on one GPU)
     visible = [d for d in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if d.strip()]
