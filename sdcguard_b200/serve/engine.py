@@ -21,6 +21,7 @@ from typing import Optional, Sequence
 
 import torch
 
+from ..utils.trace import nvtx_range
 from ..models.decoder import CheckedDecoder, DecoderConfig, StepMeta
 from ..ops import attention
 from .guard import ServeGuard
@@ -346,10 +347,12 @@ class LLMEngine:
             ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)] if self.phase_timing else None
             if ev:
                 ev[0].record()
-            self.prefill(prompts_dev, plens, pages, out_tokens)
+            with nvtx_range("sdcguard.prefill"):
+                self.prefill(prompts_dev, plens, pages, out_tokens)
             if ev:
                 ev[1].record()
-            self.decode_from(plens, pages, out_tokens, max_new_tokens)
+            with nvtx_range("sdcguard.decode"):
+                self.decode_from(plens, pages, out_tokens, max_new_tokens)
             if ev:
                 ev[2].record()
             host = torch.empty(N, max_new_tokens, dtype=torch.long, pin_memory=True)

@@ -17,6 +17,7 @@ import torch
 
 from ..numerics import abft
 from ..utils.events import EventLog, SDCEvent, device_identity
+from ..utils.trace import nvtx_range
 
 
 class ServeGuard:
@@ -49,6 +50,10 @@ class ServeGuard:
         into events if that read has landed, and starts the next read (a device snapshot and a pinned-memory copy
         ordered after the work queued so far). Results therefore arrive one poll late, as in the reference's
         poll (src/sdcguard/serve.py:1090-1129)."""
+        with nvtx_range("sdcguard.poll"):
+            return self._poll(reset, wait)
+
+    def _poll(self, reset: bool, wait: bool) -> list[SDCEvent]:
         events: list[SDCEvent] = []
         pending = getattr(self, "_pending", None)
         if pending is not None and (wait or pending.ready()):

@@ -383,6 +383,11 @@ class SDCGuard:
         return self._inject.pop((layer, phase), None)
 
     def flush(self, step: Optional[int] = None) -> list[SDCEvent]:
+        from ..utils.trace import nvtx_range
+        with nvtx_range("sdcguard.flush"):
+            return self._flush(step)
+
+    def _flush(self, step: Optional[int] = None) -> list[SDCEvent]:
         rows = self.table.read(reset=True)
         if self.recompute is not None:
             for ev in self.recompute.read(step):
