@@ -116,6 +116,8 @@ SIGNATURES: dict[str, tuple] = {
     "sdc_prep_colblock": (I, [P, L, I, I, U, U, U, U, P, P, P, P]),
     "sdc_transpose_bf16": (I, [P, L, I, I, P, P]),
     "sdc_dequant_weights": (I, [P, I, I, I, I, P, P, I, P, P]),
+    "sdc_gemm_fp8_grouped": (I, [P, P, P, P, P, I, I, I, I, P, L, P, P, P, P, P, I, U, U, U, U, F, F, F, F, F, P, I,
+                                 I, U, P]),
     "sdc_ep_receive_grouped": (I, [P, P, P, P, P, I, I, I, I, I, P, P, P, P, P, P, P, P, P]),
 }
 

@@ -81,6 +81,13 @@ struct Params8 {
   int* err;
   int inj_row, inj_col;
   uint32_t inj_xor;
+  // grouped mode (null gband: off): A's rows grouped by expert on 128-row tiles, tile mt of expert gband[mt], the
+  // first *gcount row tiles in use (both written on the device before this launch); the experts' W, Wc, sfb and
+  // wstat stacked (expert e at W row e * g_wrows, Wc row e * g_wcrows, sfb byte e * g_sfb, wstat entry e * nb)
+  const int* gband;
+  const int* gcount;
+  int g_wrows, g_wcrows;
+  long long g_sfb;
 };
 
 struct Ctl {
@@ -135,12 +142,13 @@ __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gsrc, uint3
                : "memory");
 }
 
-__device__ __forceinline__ void tile_coords8(const Params8& p, int tile, int& mt, int& nt) {
+// m_tiles: the row tiles of this launch (p.m_tiles, or the device count in grouped mode)
+__device__ __forceinline__ void tile_coords8(const Params8& p, int m_tiles, int tile, int& mt, int& nt) {
   const int per_group = p.group * p.nb;
   const int g = tile / per_group;
   const int l = tile - g * per_group;
   const int b0 = g * p.group;
-  const int gm = min(p.group, p.m_tiles - b0);
+  const int gm = min(p.group, m_tiles - b0);
   mt = b0 + l % gm;
   nt = l / gm;
 }
@@ -152,10 +160,11 @@ __device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long
 }
 
 // the judge of the bf16 kernel (no bias in this GEMM)
-__device__ __forceinline__ void judge8(const Params8& p, int row, int b, float P, float S, float Q, float Aab, float ep,
-                                       float es, unsigned long long& k0, unsigned long long& k1, int& unj) {
+// (wb: the index of the block's statistics, b plus the expert's offset in grouped mode)
+__device__ __forceinline__ void judge8(const Params8& p, int row, int b, int wb, float P, float S, float Q, float Aab,
+                                       float ep, float es, unsigned long long& k0, unsigned long long& k1, int& unj) {
   const long long o = static_cast<long long>(row) * p.nb + b;
-  const float4 ws = __ldg(p.wstat + b);
+  const float4 ws = __ldg(p.wstat + wb);
   const float xn = sqrtf(__ldg(p.row_sq + row));
   const float prod = p.prod_coef * xn * fmaxf(ws.x, fmaxf(ws.y, ws.z));
   const float den = sqrtf(Q) * p.out_coef + prod + p.abs_floor;
@@ -230,6 +239,10 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = ctl->tmem_base;
   volatile int* abort_flag = &ctl->abort_flag;
+  // grouped mode: the row-tile count and the tile -> expert table come from the kernel before this launch (this
+  // kernel is launched without programmatic serialization, so that kernel has completed)
+  const int m_tiles = p.gcount != nullptr ? min(__ldcg(p.gcount), p.m_tiles) : p.m_tiles;
+  const int total_tiles = m_tiles * p.nb;
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer: operands + scale-factor chunks
@@ -238,11 +251,12 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t phase = 0;
       bool ok = true;
       uint32_t issued = 0, issued_phase = 0;
-      for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
+      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
         int mt, nt;
-        tile_coords8(p, tile, mt, nt);
+        tile_coords8(p, m_tiles, tile, mt, nt);
+        const int e = p.gband != nullptr ? __ldcg(p.gband + mt) : 0;   // grouped mode: the tile's expert
         const uint8_t* sfa = p.sfa + static_cast<long long>(mt) * p.kbs * SFA_BYTES;
-        const uint8_t* sfb = p.sfb + static_cast<long long>(nt) * p.kbs * SFB_BYTES;
+        const uint8_t* sfb = p.sfb + e * p.g_sfb + static_cast<long long>(nt) * p.kbs * SFB_BYTES;
         for (int kb = 0; kb < p.kbs; ++kb) {
           if (!mbar_wait(&ctl->empty[stage], phase ^ 1u, abort_flag)) {
             ok = false;
@@ -252,8 +266,8 @@ __global__ void __launch_bounds__(THREADS, 1)
           uint8_t* sb = sa + A_BYTES;
           mbar_arrive_expect_tx(&ctl->full[stage], STAGE_TX);
           tma_load_2d(sa, &tmA, &ctl->full[stage], kb * BK, mt * BM);
-          tma_load_2d(sb, &tmW, &ctl->full[stage], kb * BK, nt * BN);
-          tma_load_2d(sb + BN * BK, &tmWc, &ctl->full[stage], kb * BK, nt * CSR);
+          tma_load_2d(sb, &tmW, &ctl->full[stage], kb * BK, e * p.g_wrows + nt * BN);
+          tma_load_2d(sb + BN * BK, &tmWc, &ctl->full[stage], kb * BK, e * p.g_wcrows + nt * CSR);
           bulk_g2s(sa + SF_OFF, sfa + kb * SFA_BYTES, SFA_BYTES, &ctl->full[stage]);
           bulk_g2s(sa + SF_OFF + SFA_BYTES, sfb + kb * SFB_BYTES, SFB_BYTES, &ctl->full[stage]);
           issued |= 1u << stage;
@@ -279,7 +293,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       bool ok = true;
       int t = 0;
       const uint32_t sfa_t = tmem_base + SFA_COL, sfb_t = tmem_base + SFB_COL;
-      for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x, ++t) {
+      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x, ++t) {
         const int acc = t & 1;
         if (!mbar_wait(&ctl->tempty[acc], ((t >> 1) & 1u) ^ 1u, abort_flag)) {
           ok = false;
@@ -328,9 +342,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     unsigned long long* st = p.state + static_cast<long long>(p.slot) * 4;
     uint8_t* stg = staging + ew * 4096;
     int t = 0;
-    for (int tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x, ++t) {
+    for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++t) {
       int mt, nt;
-      tile_coords8(p, tile, mt, nt);
+      tile_coords8(p, m_tiles, tile, mt, nt);
+      const int wb = (p.gband != nullptr ? __ldcg(p.gband + mt) * p.nb : 0) + nt;   // the block's statistics
       const int row = mt * BM + row_in_tile;
       const bool valid = row < p.M;
       const int acc_i = t & 1;
@@ -412,7 +427,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (valid) {
           const float ep = ((cs[0] + cs[1]) + (cs[2] + cs[3])) + (cs[4] + cs[5]);
           const float es = ((cs[6] + cs[7]) + (cs[8] + cs[9])) + (cs[10] + cs[11]);
-          judge8(p, row, nt, P, S, Q, Aab, ep, es, k0, k1, unj);
+          judge8(p, row, nt, wb, P, S, Q, Aab, ep, es, k0, k1, unj);
         }
         k0 = warp_max_u64(k0);
         k1 = warp_max_u64(k1);
@@ -539,11 +554,15 @@ extern "C" {
 // A_q [M][K] E4M3 codes with scale-factor chunks sfa [ceil(M/128)][K/128][512] (sdc_fp8_quant_act); W_q [N][K],
 // Wc_q [16 N/128][K] checksum rows, sfb [N/128][K/128][1024] the scale-factor chunks of each block's 144-row B
 // operand (ops/fp8.py). N and K must be multiples of 128; sfa and sfb 16-byte aligned.
-int sdc_gemm_fp8(const void* Aq, const void* sfa, const void* Wq, const void* Wcq, const void* sfb, int M, int N, int K, void* Cout, long long ldc, const float* row_sq, const float* wstat,
-                 unsigned long long* state, int slot, unsigned s0, unsigned s1, unsigned s2, unsigned s3, float zthr,
-                 float prod_coef, float out_coef, float abs_floor, float bound_coef, int* err, int inj_row,
-                 int inj_col, unsigned inj_xor, void* stream) {
+static int fp8_run(const void* Aq, const void* sfa, const void* Wq, const void* Wcq, const void* sfb, int M, int N,
+                   int K, void* Cout, long long ldc, const float* row_sq, const float* wstat, unsigned long long* state,
+                   int slot, unsigned s0, unsigned s1, unsigned s2, unsigned s3, float zthr, float prod_coef,
+                   float out_coef, float abs_floor, float bound_coef, int* err, int inj_row, int inj_col,
+                   unsigned inj_xor, void* stream, int experts, const int* gband, const int* gcount) {
   if (M <= 0) return 0;
+  if (experts < 1 || (experts > 1 && (gband == nullptr || gcount == nullptr)) ||
+      static_cast<long long>(experts) * N >= (1ll << 31))
+    return -1;
   if (N <= 0 || K <= 0 || N % BN || K % BK || K / BK > MAX_KBS || ldc % 8) return -1;
   if ((reinterpret_cast<uintptr_t>(sfa) | reinterpret_cast<uintptr_t>(sfb)) & 15) return -7;
   Params8 p;
@@ -581,10 +600,15 @@ int sdc_gemm_fp8(const void* Aq, const void* sfa, const void* Wq, const void* Wc
   p.inj_row = inj_row;
   p.inj_col = inj_col;
   p.inj_xor = inj_xor;
+  p.gband = gband;
+  p.gcount = gcount;
+  p.g_wrows = N;
+  p.g_wcrows = p.nb * CSR;
+  p.g_sfb = static_cast<long long>(p.nb) * p.kbs * SFB_BYTES;
   CUtensorMap ma, mw, mc, mo;
   if (!make_map_u8_sw128(&ma, Aq, M, K, K, BK, BM)) return -2;
-  if (!make_map_u8_sw128(&mw, Wq, N, K, K, BK, BN)) return -3;
-  if (!make_map_u8_sw128(&mc, Wcq, static_cast<long long>(p.nb) * CSR, K, K, BK, CSR)) return -4;
+  if (!make_map_u8_sw128(&mw, Wq, static_cast<long long>(experts) * N, K, K, BK, BN)) return -3;
+  if (!make_map_u8_sw128(&mc, Wcq, static_cast<long long>(experts) * p.nb * CSR, K, K, BK, CSR)) return -4;
   if (!make_map_bf16_sw128(&mo, Cout, M, N, ldc, 64, 32, false)) return -5;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
@@ -592,6 +616,32 @@ int sdc_gemm_fp8(const void* Aq, const void* sfa, const void* Wq, const void* Wc
   const int grid = p.total_tiles < sms ? p.total_tiles : sms;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   return inj_row >= 0 ? launch8<true>(ma, mw, mc, mo, p, grid, st) : launch8<false>(ma, mw, mc, mo, p, grid, st);
+}
+
+int sdc_gemm_fp8(const void* Aq, const void* sfa, const void* Wq, const void* Wcq, const void* sfb, int M, int N, int K,
+                 void* Cout, long long ldc, const float* row_sq, const float* wstat, unsigned long long* state, int slot,
+                 unsigned s0, unsigned s1, unsigned s2, unsigned s3, float zthr, float prod_coef, float out_coef,
+                 float abs_floor, float bound_coef, int* err, int inj_row, int inj_col, unsigned inj_xor,
+                 void* stream) {
+  return fp8_run(Aq, sfa, Wq, Wcq, sfb, M, N, K, Cout, ldc, row_sq, wstat, state, slot, s0, s1, s2, s3, zthr,
+                 prod_coef, out_coef, abs_floor, bound_coef, err, inj_row, inj_col, inj_xor, stream, 1, nullptr,
+                 nullptr);
+}
+
+// Grouped fp8 checked GEMM (mixture-of-experts layers): A's rows grouped by expert on 128-row tiles (tile mt of
+// expert gband[mt], the first *gcount tiles in use: sdc_moe_plan / the expert-parallel receive), the experts'
+// quantized weights stacked: Wq [experts N][K], Wcq [experts 16 N/128][K], sfb [experts][N/128][K/128][1024],
+// wstat [experts][N/128]. M is the capacity of A and C in rows; sfa covers every row tile of A.
+int sdc_gemm_fp8_grouped(const void* Aq, const void* sfa, const void* Wq, const void* Wcq, const void* sfb, int experts,
+                         int M, int N, int K, void* Cout, long long ldc, const float* row_sq, const float* wstat,
+                         const int* gband, const int* gcount, unsigned long long* state, int slot, unsigned s0,
+                         unsigned s1, unsigned s2, unsigned s3, float zthr, float prod_coef, float out_coef,
+                         float abs_floor, float bound_coef, int* err, int inj_row, int inj_col, unsigned inj_xor,
+                         void* stream) {
+  if (gband == nullptr || gcount == nullptr) return -1;
+  return fp8_run(Aq, sfa, Wq, Wcq, sfb, M, N, K, Cout, ldc, row_sq, wstat, state, slot, s0, s1, s2, s3, zthr,
+                 prod_coef, out_coef, abs_floor, bound_coef, err, inj_row, inj_col, inj_xor, stream, experts, gband,
+                 gcount);
 }
 
 // x [M][K] bf16 (row stride ldx) -> xq [M][K] E4M3 codes, sa [M][K/128], sfa [ceil(M/128)][K/128][512] UE8M0

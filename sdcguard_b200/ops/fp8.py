@@ -160,6 +160,53 @@ def checked_linear_fp8(xa: Fp8Act, fw: Fp8Weight, state: torch.Tensor, slot: int
     return out
 
 
+class Fp8WeightStack:
+    """The fp8-quantized weights of several experts (each (n, k), one shared sign pattern) stacked for
+    `checked_linear_fp8_grouped`: codes (experts n, k), checksum rows (experts 16 n / 128, k), scale-factor chunks
+    (experts n / 128, k / 128, 1024), block statistics (experts n / 128, 4)."""
+
+    def __init__(self, weights: list, c1: float = abft.C1, c2: float = abft.C2, c3: float = abft.C3):
+        if not weights:
+            raise ValueError("Fp8WeightStack needs at least one weight")
+        mask = abft.sign_mask()
+        fws = [Fp8Weight(w, mask=mask, c1=c1, c2=c2, c3=c3) for w in weights]
+        f0 = fws[0]
+        if any((f.n, f.k) != (f0.n, f0.k) for f in fws):
+            raise ValueError("expert weights must share one (n, k) shape")
+        self.experts, self.n, self.k, self.nb, self.kbs, self.mask = len(fws), f0.n, f0.k, f0.nb, f0.kbs, mask
+        self.wq = torch.cat([f.wq for f in fws]).contiguous()
+        self.wcq = torch.cat([f.wcq for f in fws]).contiguous()
+        self.sfb = torch.cat([f.sfb for f in fws]).contiguous()
+        self.wstat = torch.cat([f.wstat for f in fws]).contiguous()
+        self.prod_coef, self.out_coef = f0.prod_coef, f0.out_coef
+        self.members = fws
+
+    def expert(self, e: int) -> Fp8Weight:
+        return self.members[e]
+
+
+def checked_linear_fp8_grouped(xa: Fp8Act, stack: Fp8WeightStack, gband: torch.Tensor, gcount: torch.Tensor,
+                               state: torch.Tensor, slot: int, out: Optional[torch.Tensor] = None,
+                               z_alarm: float = abft.Z_ALARM, inject: Optional[tuple] = None) -> torch.Tensor:
+    """The fp8 checked GEMM over every expert's rows in one launch: xa quantizes the grouped rows (expert rows on
+    128-row tiles, ops.moe.Grouping or the expert-parallel receive), gband / gcount on the device."""
+    m, k = xa.q.shape
+    if k != stack.k:
+        raise ValueError(f"activations have {k} columns, the weights {stack.k}")
+    dev = xa.q.device
+    if out is None:
+        out = torch.empty(m, stack.n, dtype=torch.bfloat16, device=dev)
+    s = stack.mask
+    ir, ic, ix = (-1, -1, 0) if inject is None else (int(inject[0]), int(inject[1]), int(inject[2]))
+    _native.check(_native.lib().sdc_gemm_fp8_grouped(
+        xa.q.data_ptr(), xa.sf.data_ptr(), stack.wq.data_ptr(), stack.wcq.data_ptr(), stack.sfb.data_ptr(),
+        stack.experts, m, stack.n, k, out.data_ptr(), out.stride(0), xa.row_sq.data_ptr(), stack.wstat.data_ptr(),
+        gband.data_ptr(), gcount.data_ptr(), state.data_ptr(), int(slot), s[0], s[1], s[2], s[3], float(z_alarm),
+        float(stack.prod_coef), float(stack.out_coef), float(abft.ABS_FLOOR), float(math.sqrt(k)),
+        error_word(dev).data_ptr(), ir, ic, ix, _stream_ptr(dev)), "grouped fp8 checked GEMM")
+    return out
+
+
 class Fp8Linears:
     """The fp8 projections of a model: quantized weights by name, one activation scratch sized for the largest
     call (views keep their data pointers, so CUDA graphs can capture the calls), and the quantizer replay check."""
