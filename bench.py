@@ -368,9 +368,9 @@ def _ref_phase(args, rank, world, local, checked: bool) -> dict:
     log = open(os.path.join(log_dir, f"sdcguard_ref_{'c' if checked else 'u'}_{rank}.log"), "w")
     p = subprocess.Popen(cmd, env=_child_env(local, checked), stdin=subprocess.PIPE, stdout=subprocess.PIPE,
                          stderr=log, text=True)
-    # the engine must report READY within SDCGUARD_REF_START_S seconds (default 420): a watchdog ends a child that
+    # the engine must report READY within SDCGUARD_REF_START_S seconds (default 600): a watchdog ends a child that
     # hangs in its startup, so every rank reaches the agreement below in bounded time and the line names the cause
-    start_limit = float(os.environ.get("SDCGUARD_REF_START_S", "420"))
+    start_limit = float(os.environ.get("SDCGUARD_REF_START_S", "600"))
     ready_seen = threading.Event()
 
     def watchdog():
