@@ -385,6 +385,33 @@ class CheckedDecoder:
     def read_checks(self, reset: bool = False) -> list[dict]:
         return self.state.read(reset=reset)
 
+    def check_coverage(self) -> dict:
+        """Which linear layers carry the ABFT check: counts of checked and unchecked projections (the LM head
+        included), the share of linear-layer weight elements that are checked, and how many of the checked ones are
+        fp8 layers (each with its quantization replay)."""
+        checked = unchecked = fp8 = 0
+        w_checked = w_total = 0
+        for i, lw in enumerate(self.layers):
+            for name in ("qkv", "o", "gate_up", "down"):
+                w = getattr(lw, name)
+                if w is None:
+                    continue
+                w_total += w.numel()
+                if f"L{i}.{name}" in self.slot:
+                    checked += 1
+                    w_checked += w.numel()
+                    fp8 += f"L{i}.{name}.q" in self.slot
+                else:
+                    unchecked += 1
+        w_total += self.lm_head.numel()
+        if "lm_head" in self.slot:
+            checked += 1
+            w_checked += self.lm_head.numel()
+        else:
+            unchecked += 1
+        return {"layers_checked": checked, "layers_unchecked": unchecked, "fp8_layers_checked": fp8,
+                "weights_checked_ratio": w_checked / w_total if w_total else 0.0}
+
     def sample(self, logits: torch.Tensor) -> torch.Tensor:
         """Greedy next token (the engine's sampler)."""
         return torch.argmax(logits, dim=-1)

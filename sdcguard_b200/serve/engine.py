@@ -15,9 +15,11 @@ patch :2430-2501 with mark_step/poll); here the engine is this package's own, wi
 """
 from __future__ import annotations
 
+import queue
+import threading
 import time
 from dataclasses import dataclass
-from typing import Optional, Sequence
+from typing import Callable, Optional, Sequence
 
 import torch
 
@@ -48,6 +50,50 @@ class BlockAllocator:
 
 def kv_bytes_per_page(cfg: DecoderConfig, nkv: int) -> int:
     return cfg.layers * 2 * nkv * PAGE * cfg.head_dim * 2
+
+
+class TokenTap:
+    """Hands each generated token column to a host callback as soon as the GPU has written it, without making the
+    launching thread wait: after a column is produced, the engine queues a copy of it into pinned memory and an
+    event on the stream; a tap thread waits for the events in order and calls on_tokens(rows, column, ids).
+
+    Only generate() calls that pass on_tokens pay for this (one small copy and an event per step)."""
+
+    def __init__(self, device: torch.device, n: int, max_new: int, on_tokens: Callable):
+        self.host = torch.empty(max_new, n, dtype=torch.long, pin_memory=True)
+        self.device = device
+        self.on_tokens = on_tokens
+        self.q: "queue.Queue" = queue.Queue()
+        self.error: Optional[BaseException] = None
+        self.thread = threading.Thread(target=self._run, daemon=True)
+        self.thread.start()
+
+    def push(self, rows: Sequence[int], col: int, src: torch.Tensor) -> None:
+        """src: the column's tokens for `rows` (a contiguous range), on the device."""
+        r0 = rows[0]
+        self.host[col, r0:r0 + len(rows)].copy_(src, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(self.device))
+        self.q.put((list(rows), col, ev))
+
+    def _run(self) -> None:
+        while True:
+            item = self.q.get()
+            if item is None:
+                return
+            rows, col, ev = item
+            try:
+                ev.synchronize()
+                r0 = rows[0]
+                self.on_tokens(rows, col, self.host[col, r0:r0 + len(rows)].tolist())
+            except BaseException as e:  # noqa: BLE001  (kept and raised by close())
+                self.error = self.error or e
+
+    def close(self) -> None:
+        self.q.put(None)
+        self.thread.join()
+        if self.error is not None:
+            raise self.error
 
 
 class LLMEngine:
@@ -97,6 +143,7 @@ class LLMEngine:
         self.hooks = None                  # serve.plugin.PluginHooks (register() sets it)
         self.phase_timing = False          # record device time of the prefill and decode phases of generate()
         self.last_phase_ms: dict = {}
+        self.tap: Optional[TokenTap] = None   # set during a generate() call that streams its tokens
 
     def describe(self) -> dict:
         """The engine's configuration as the offline deployment contracts read it (`evidence/config.py`)."""
@@ -253,6 +300,8 @@ class LLMEngine:
                 else:
                     nxt = out()
                 out_tokens[rows, s + 1] = nxt
+                if self.tap is not None:
+                    self.tap.push(idx, s + 1, nxt)
                 if self.hooks is not None:
                     self.hooks.after_step("decode", idx)
             self.step_counter += max_new - 1
@@ -332,9 +381,13 @@ class LLMEngine:
                 self.alloc.release(pages)
         return out
 
-    def generate(self, prompts: torch.Tensor, prompt_lens: Sequence[int], max_new_tokens: int) -> torch.Tensor:
+    def generate(self, prompts: torch.Tensor, prompt_lens: Sequence[int], max_new_tokens: int,
+                 on_tokens: Optional[Callable] = None) -> torch.Tensor:
         """prompts: (N, max_len) int64 token ids (ideally pinned host memory); returns (N, max_new_tokens) int64
-        generated ids on the host. Greedy decoding, no early stop (synthetic workloads)."""
+        generated ids on the host. Greedy decoding, no early stop (synthetic workloads).
+
+        on_tokens(rows, column, ids): called from a tap thread with each generated column once the GPU has written
+        it (column 0 after the prefill, then one per decode step), for streaming responses (TokenTap)."""
         dev = self.device
         N = prompts.shape[0]
         plens = [int(x) for x in prompt_lens]
@@ -347,8 +400,12 @@ class LLMEngine:
             ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)] if self.phase_timing else None
             if ev:
                 ev[0].record()
+            if on_tokens is not None and dev.type == "cuda":
+                self.tap = TokenTap(dev, N, max_new_tokens, on_tokens)
             with nvtx_range("sdcguard.prefill"):
                 self.prefill(prompts_dev, plens, pages, out_tokens)
+            if self.tap is not None:
+                self.tap.push(list(range(N)), 0, out_tokens[:, 0])
             if ev:
                 ev[1].record()
             with nvtx_range("sdcguard.decode"):
@@ -360,7 +417,13 @@ class LLMEngine:
             torch.cuda.current_stream(dev).synchronize()
             if ev:
                 self.last_phase_ms = {"prefill": ev[0].elapsed_time(ev[1]), "decode": ev[1].elapsed_time(ev[2])}
+            if self.tap is not None:
+                tap, self.tap = self.tap, None
+                tap.close()
             return host
         finally:
+            if self.tap is not None:
+                tap, self.tap = self.tap, None
+                tap.q.put(None)
             for pg in pages:
                 self.alloc.release(pg)

@@ -20,6 +20,20 @@ from ..utils.events import EventLog, SDCEvent, device_identity
 from ..utils.trace import nvtx_range
 
 
+CONFIRMING_RECHECKS = ("output_wrong", "both_wrong", "weights_changed")
+
+
+def confirmed(ev: SDCEvent) -> bool:
+    """Does an event carry its own evidence of a wrong result? A captured GEMM alarm whose float64 recheck shows a
+    wrong output or changed weights, or a weight-scan finding (a fingerprint that no longer matches the load).
+    Replays that differed are confirmed too (an exact replay has no rounding envelope to sit inside), and so is a
+    spot check past its rigorous bound."""
+    if ev.detector in ("weights", "replay", "quantization", "collective", "spot", "kv_transfer", "alltoall"):
+        return True
+    rec = (ev.detail or {}).get("recheck") or {}
+    return rec.get("verdict") in CONFIRMING_RECHECKS
+
+
 class ServeGuard:
     def __init__(self, model, z_alarm: float = abft.Z_ALARM, log: Optional[EventLog] = None,
                  on_alert: Optional[Callable[[SDCEvent], None]] = None):
@@ -133,7 +147,8 @@ class ServeGuard:
                 if self._identity is None:
                     self._identity = device_identity(self.model.device)
                 det = ("checksum" if "GEMM" in r["name"] else "collective" if "collective" in r["name"]
-                       else "spot" if "spot" in r["name"] else "replay")
+                       else "spot" if "spot" in r["name"] else "quantization" if ".quant" in r["name"]
+                       else "replay")
                 detail = {"layer": r["name"], "z": z, "noise": r["noise"], "flat": r["flat"]}
                 if "row" in r:
                     detail.update({k: r[k] for k in ("row", "block", "signed", "peer") if k in r})
@@ -151,11 +166,16 @@ class ServeGuard:
         every = {n: t for n, t in self.totals.items() if "spot check" not in n}
         sampled = {n: t for n, t in self.totals.items() if "spot check" in n}
         checked = sum(1 for t in every.values() if t["checks"] > 0)
+        quant = {n: t for n, t in self.totals.items() if ".quant" in n}
         return {"ops": len(every), "ops_checked": checked, "sampled_ops": len(sampled),
                 "sampled_ops_run": sum(1 for t in sampled.values() if t["checks"] > 0),
                 "checks": sum(t["checks"] for t in self.totals.values()),
                 "unjudged": sum(t["unjudged"] for t in self.totals.values()),
                 "alarms": sum(t["alarms"] for t in self.totals.values()),
+                "fp8_calls_judged": sum(t["checks"] for t in quant.values()),
+                "fp8_findings": sum(t["alarms"] for t in quant.values()),
+                "alerts": len(self.log.events),
+                "confirmed_alerts": sum(1 for e in self.log.events if confirmed(e)),
                 "worst_clean_z": max((t["worst_z"] for t in self.totals.values() if t["alarms"] == 0), default=0.0)}
 
     def worst_z(self) -> float:

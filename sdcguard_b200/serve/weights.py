@@ -15,6 +15,7 @@ sm_100a kernel over all tensors of the slice).
 """
 from __future__ import annotations
 
+import time
 from typing import Iterable, Optional
 
 import torch
@@ -30,8 +31,10 @@ class WeightScan:
                  log: Optional[EventLog] = None):
         self.names: list[str] = []
         self.tensors: list[torch.Tensor] = []
+        self.left_out: list[str] = []          # named entries with nothing to fingerprint (None or empty)
         for name, t in named:
             if t is None or t.numel() == 0:
+                self.left_out.append(name)
                 continue
             self.names.append(name)
             self.tensors.append(t.detach())
@@ -42,6 +45,9 @@ class WeightScan:
         self.cursor = 0
         self.scanned_bytes = 0
         self.repairs = 0
+        self.passes = 0                        # completed sweeps over every entry
+        self.clean_at: list[Optional[float]] = [None] * len(self.tensors)   # last compare that matched
+        self.changed: set = set()              # entries found changed (and not repaired back) since load
 
     def _fp(self, idx) -> list[tuple[int, int]]:
         idx = list(idx)
@@ -59,14 +65,20 @@ class WeightScan:
 
     def _check(self, idx: list[int], step: Optional[int]) -> list[SDCEvent]:
         now = self._fp(idx)
+        t = time.time()
         events = []
         for i, fp in zip(idx, now):
             self.scanned_bytes += self.tensors[i].numel() * self.tensors[i].element_size()
             if fp == self.ref[i]:
+                self.clean_at[i] = t
                 continue
             detail = {"weight": self.names[i], "expected": list(self.ref[i]), "found": list(fp)}
+            self.changed.add(i)
             if self.host is not None:
                 detail.update(self._repair(i))
+                if detail.get("repaired"):
+                    self.changed.discard(i)
+                    self.clean_at[i] = t
             ev = SDCEvent(detector="weights", step=step, detail=detail,
                           identity=device_identity(self.tensors[i].device))
             self.log.add(ev)
@@ -98,10 +110,26 @@ class WeightScan:
             idx.append(i)
             got += self.tensors[i].numel() * self.tensors[i].element_size()
             self.cursor = (self.cursor + 1) % len(self.tensors)
+            if self.cursor == 0:
+                self.passes += 1
         return self._check(idx, step)
 
     def full(self, step: Optional[int] = None) -> list[SDCEvent]:
-        return self._check(list(range(len(self.tensors))), step)
+        ev = self._check(list(range(len(self.tensors))), step)
+        self.passes += 1
+        return ev
+
+    def stats(self, now: Optional[float] = None) -> dict:
+        """What the scan has verified: entries held, sweeps completed, entries never compared since load, entries
+        found changed (not repaired), repairs written, and the age of the least recently verified entry (None
+        while an entry has never been compared)."""
+        now = time.time() if now is None else now
+        never = sum(1 for c in self.clean_at if c is None)
+        ok = [c for c in self.clean_at if c is not None]
+        return {"entries": len(self.tensors), "passes": self.passes, "never_compared": never,
+                "changed": len(self.changed), "repairs": self.repairs, "left_out": len(self.left_out),
+                "oldest_age_seconds": (now - min(ok)) if ok and not never else None,
+                "scanned_bytes": self.scanned_bytes}
 
     def digest(self) -> str:
         """One hex digest of every registered weight fingerprint (model identity)."""

@@ -78,19 +78,16 @@ def compare_position(rv: torch.Tensor, ri: torch.Tensor, cv: torch.Tensor, ci: t
     return sum((r[t] / rs) * math.log((r[t] / rs) / (c[t] / cs)) for t in u if r[t] > 0)
 
 
-def check(ref: dict, precision: str = "bf16", checked: bool = True, device: str = "cuda:0",
-          noise: Optional[dict] = None) -> dict:
+def _against(ref: dict, sc: list) -> dict:
+    """Per-position comparison of candidate scores sc[k] = (values, ids) with the reference's."""
     seqs = ref["seqs"]
-    L = max(len(s) for s in seqs)
-    eng = _engine(ref["model"], precision, checked, ref["seed"], device, L, len(seqs))
-    sc = eng.score(seqs, TOPK)
-    p0 = ref["prompt_len"] - 1                 # first position whose next token is a recorded completion token
+    plens = ref.get("prompt_lens") or [ref["prompt_len"]] * len(seqs)
     per_prompt, agree, total, dlp = [], 0, 0, []
     for k, s in enumerate(seqs):
-        rv, ri = ref["values"][k], ref["ids"][k]
-        cv, ci = sc[k]
+        rv, ri = torch.as_tensor(ref["values"][k]), torch.as_tensor(ref["ids"][k])
+        cv, ci = torch.as_tensor(sc[k][0]), torch.as_tensor(sc[k][1])
         kls = []
-        for p in range(p0, len(s) - 1):
+        for p in range(plens[k] - 1, len(s) - 1):   # positions whose next token is a recorded completion token
             kls.append(compare_position(rv[p], ri[p], cv[p], ci[p]))
             agree += int(ri[p, 0] == ci[p, 0])
             total += 1
@@ -100,12 +97,50 @@ def check(ref: dict, precision: str = "bf16", checked: bool = True, device: str 
             if rl.numel() and cl.numel():
                 dlp.append(float(cl[0] - rl[0]))
         per_prompt.append(sum(kls) / len(kls))
-    mean_kl = sum(per_prompt) / len(per_prompt)
-    top1 = agree / total
+    return {"positions": total, "mean_kl": sum(per_prompt) / len(per_prompt), "top1_agreement": agree / total,
+            "worst_prompt_kl": max(per_prompt), "mean_abs_delta_logprob": sum(map(abs, dlp)) / max(1, len(dlp))}
+
+
+def check(ref: dict, precision: str = "bf16", checked: bool = True, device: str = "cuda:0",
+          noise: Optional[dict] = None) -> dict:
+    seqs = ref["seqs"]
+    L = max(len(s) for s in seqs)
+    eng = _engine(ref["model"], precision, checked, ref["seed"], device, L, len(seqs))
+    sc = eng.score(seqs, TOPK)
     res = {"format": "sdcguard-b200-model-check/1", "stack": {"precision": precision, "checked": checked},
-           "reference_stack": ref["stack"], "positions": total, "mean_kl": mean_kl, "top1_agreement": top1,
-           "worst_prompt_kl": max(per_prompt), "mean_abs_delta_logprob": sum(map(abs, dlp)) / max(1, len(dlp)),
-           "alarms": len(eng.guard.poll())}
+           "reference_stack": ref["stack"], **_against(ref, sc), "alarms": len(eng.guard.poll())}
+    res.update(verdict(res, noise))
+    return res
+
+
+def reference_url(url: str, prompts: int = 8, prompt_len: int = 48, new: int = 16, prompt_seed: int = 1234,
+                  vocab: int = 1000, complete=None, score=None) -> dict:
+    """`reference` against a running server: greedy completions of a fixed prompt set, then the top-20
+    log-probabilities of every position of prompt + completion from its /v1/score (one teacher-forced prefill)."""
+    from . import _client
+    complete, score = complete or _client.complete, score or _client.score
+    g = torch.Generator().manual_seed(prompt_seed)
+    P = torch.randint(1, vocab, (prompts, prompt_len), generator=g).tolist()
+    seqs, vals, ids = [], [], []
+    for p in P:
+        s = p + list(complete(url, p, new))
+        r = score(url, s, TOPK)
+        seqs.append(s)
+        vals.append(r["top_logprobs"])
+        ids.append(r["top_ids"])
+    return {"format": "sdcguard-b200-model-ref/1", "url": url, "prompt_len": prompt_len,
+            "prompt_lens": [prompt_len] * prompts, "seqs": seqs, "values": vals, "ids": ids}
+
+
+def check_url(ref: dict, url: str, noise: Optional[dict] = None, score=None) -> dict:
+    """`check` against a running server: the reference's sequences scored by its /v1/score."""
+    from . import _client
+    score = score or _client.score
+    sc = []
+    for s in ref["seqs"]:
+        r = score(url, s, TOPK)
+        sc.append((r["top_logprobs"], r["top_ids"]))
+    res = {"format": "sdcguard-b200-model-check/1", "url": url, **_against(ref, sc)}
     res.update(verdict(res, noise))
     return res
 

@@ -115,7 +115,28 @@ def run(base: str, probes: int = 4, primers: int = 3, repeats: int = 2, prompt: 
     verdicts = [r["verdict"] for r in rows]
     verdict = ("LEAK" if "LEAK" in verdicts else "INCONCLUSIVE" if "INCONCLUSIVE" in verdicts or not rows
                else "NO LEAK SEEN")
-    return {"schema": SCHEMA, "url": base, "verdict": verdict, "probes": rows,
+    why = []
+    for r in rows:
+        if "error" in r:
+            why.append(f"probe {r['probe']}: a request failed ({r['error'][:120]})")
+            continue
+        a, b = r["primer"], r["concurrency"]
+        if a["primers_changing_the_answer"]:
+            why.append(f"probe {r['probe']}: primers {a['primers_changing_the_answer']} changed its answer, the same "
+                       "way on every repeat")
+        if not a["controls_agree"]:
+            why.append(f"probe {r['probe']}: repeats after the same primer disagree (the server is not "
+                       "deterministic at batch size 1)")
+        if b["verdict"] == "LEAK":
+            why.append(f"probe {r['probe']}: its answer changed when other requests shared its batches (first "
+                       f"difference at token {b['first_difference']})")
+        elif b["verdict"] == "INCONCLUSIVE":
+            why.append(f"probe {r['probe']}: the concurrency probe was inconclusive")
+    differing = sum(len(r["primer"]["primers_changing_the_answer"]) for r in rows if "primer" in r)
+    return {"schema": SCHEMA, "url": base, "verdict": verdict, "why": why, "probes": rows,
+            "primer": {"pairs": probes * (primers - 1), "pairs_differing": differing},
+            "probe_set": {"probes": probes, "primers": primers, "repeats": repeats, "prompt": prompt,
+                          "tokens": tokens, "others": others, "seed": seed},
             "scope": "these prompts, this load and this server only"}
 
 

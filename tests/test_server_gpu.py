@@ -1,6 +1,8 @@
 """The HTTP server on a B200 (tiny model, a subprocess) probed from outside: ready (with a probe request) says
-PROTECTED, greedy outputs are isolated from their batch and decode agrees with prefill, throughput is measured; an
-unchecked server reads NOT PROTECTED; qualify + decide accept an fp8 candidate against the bf16 baseline."""
+PROTECTED, greedy outputs are isolated from their batch and decode agrees with prefill, streamed throughput and
+latencies are measured; an unchecked server reads NOT PROTECTED; qualify serves a baseline and two candidates and
+decides each: the same stack with the weight scan on is accepted with verified weights, the fp8 stack's arithmetic
+and quantization checks ran clean."""
 import json
 import os
 import socket
@@ -39,8 +41,8 @@ def test_server_probes(tmp_path):
         assert isolation.run(url, probes=2, primers=3)["verdict"] == "NO LEAK SEEN"
         c = consistency.run(url, probes=2)
         assert c["verdict"] == "CONSISTENT", c
-        p = perf.run(url, clients=4, prompt=64, tokens=8, seconds=3)
-        assert p["requests"] > 0 and p["errors"] == 0, p
+        p = perf.measure(url, perf.default_load(16), concurrency=4, max_tokens=8, rounds=2, warmup=2)
+        assert p["complete"] and p["median"]["ttft_p50_ms"] > 0 and p["median"]["output_tokens_per_s"] > 0, p
     finally:
         srv.stop()
     port = _port()
@@ -53,18 +55,27 @@ def test_server_probes(tmp_path):
 
 
 def test_qualify_and_decide(tmp_path):
-    from sdcguard_b200.tools import decide, qualify
+    from sdcguard_b200.tools import qualify
     os.chdir(ROOT)
-    p1, p2 = _port(), _port()
     out = str(tmp_path / "q")
-    os.makedirs(out)
-    base = qualify.run_one("baseline", _cmd(p1), f"http://127.0.0.1:{p1}", out, seconds=2, clients=4)
-    cand = qualify.run_one("candidate", _cmd(p2, "--precision fp8"), f"http://127.0.0.1:{p2}", out, seconds=2,
-                           clients=4)
-    d = decide.decide(base, cand, {"waive": ["performance"]})
-    assert d["sections"]["arithmetic"]["verdict"] == "NO FAULT OBSERVED", d
-    assert d["decision"] == "ACCEPT", json.dumps(d["sections"])
-    assert d["candidate_stack"]["precision"] == "fp8"
+    args = "--model tiny --max-num-seqs 16 --max-model-len 512"
+    pol = tmp_path / "policy.json"
+    pol.write_text(json.dumps({"performance": {"required": False}}))
+    rc = qualify.main(["--out", out, "--baseline", args, "--candidate", f"scan={args} --weight-scan-mb 4096",
+                       "--candidate", f"fp8={args} --precision fp8", "--no-repeat-baseline", "--rounds", "2",
+                       "--concurrency", "4", "--max-tokens", "8", "--quality-prompts", "4", "--policy", str(pol)])
+    with open(os.path.join(out, "decision_scan.json")) as f:
+        d = json.load(f)
+    assert d["decision"] == "ACCEPT", d["why"]
+    assert d["arithmetic"]["verdict"] == "NO FAULT OBSERVED" and d["weights"]["verdict"] == "VERIFIED", d["weights"]
+    assert d["approximation"]["verdict"] == "WITHIN" and d["tested"]["longest_prompt"] > 0
+    with open(os.path.join(out, "decision_fp8.json")) as f:
+        f8 = json.load(f)
+    assert f8["arithmetic"]["verdict"] == "NO FAULT OBSERVED", f8["arithmetic"]
+    assert f8["quantization"]["verdict"] == "RIGHT", f8["quantization"]
+    assert f8["scope"]["stacks"]["candidate"]["precision"] == "fp8"
+    assert rc in (0, 1, 2) and os.path.exists(os.path.join(out, "report.txt"))
+    assert os.path.exists(os.path.join(out, "repro_fp8.sh"))
 
 
 def test_gate_model_same_stack_passes_and_fp8_is_scored():
