@@ -11,6 +11,7 @@ turns those lines into an inventory and compares inventories:
     python -m sdcguard_b200.tools.kernels diff before.json after.json
     python -m sdcguard_b200.tools.kernels show serve.json
     python -m sdcguard_b200.tools.kernels parse cublaslt.log --out inv.json
+    python -m sdcguard_b200.tools.kernels test serve.json --out tested.json [--repeats 3]
 
 An inventory lists each distinct kernel (types, compute type, epilogue, configuration) with its calls, the shapes it
 ran and its share of the matmul work (2 m n k batch per call). Coverage counts a workload kernel as exercised when
@@ -19,7 +20,18 @@ kernels whose configuration matches a listed wrong-result issue (algorithm 66 wi
 This library's checked paths run no cuBLAS at all; the inventory is for unchecked arms and foreign jobs. Lines that
 are not matmul Trace lines are ignored; unreadable matmul Trace lines are counted, never guessed.
 
-Reference: src/sdcguard/kernels.py:1-44 (commands, keys and coverage rules), `parse_line` :82, `main` :522.
+`test` runs every inventoried call again on this GPU, at its shape, in a fresh process with cuBLASLt's log on: the
+operands laid out as the call had them (transposes and batch), random inputs, outputs into NaN-filled buffers, each
+shape `--repeats` times, every output judged against float64 with a rounding bound (bf16 / fp16 output rounding plus
+fp32 accumulation with tensor-core truncation over k). Per call: PASSED when every run was right and cuBLASLt ran
+the same kernel here (the inventory's key among the keys logged for that shape); WRONG when an output element was
+outside the bound or never written; OTHER KERNEL when the runs were right but cuBLASLt chose another kernel here
+(other conditions: run it where the workload runs); NOT RUN for calls this cannot replay (types other than bf16 /
+fp16 in and out with fp32 compute, epilogues other than the default, outputs too large for the float64 check).
+Random inputs: a fault that needs the workload's own data or memory layout may not show.
+
+Reference: src/sdcguard/kernels.py:1-44 (commands, keys and coverage rules), `parse_line` :82, `test_calls` :346,
+`main` :522.
 """
 from __future__ import annotations
 
@@ -186,6 +198,153 @@ def record(cmd: list[str], out: str, seconds: Optional[float] = None) -> dict:
     return inv
 
 
+_SHAPE = re.compile(r"m=(\d+) n=(\d+) k=(\d+) batch=(\d+) (OP_\w)/(OP_\w)")
+REPLAY_TYPES = ("bf16", "fp16")
+MAX_ELEMENTS = 64e6
+
+
+def parse_shape(key: str) -> Optional[dict]:
+    mt = _SHAPE.match(key)
+    if not mt:
+        return None
+    m, n, k, b, ta, tb = mt.groups()
+    return {"m": int(m), "n": int(n), "k": int(k), "batch": int(b), "transa": ta, "transb": tb}
+
+
+def rerunnable(e: dict, shape: Optional[dict], max_elements: float = MAX_ELEMENTS) -> Optional[str]:
+    """Why an inventoried call cannot be replayed here (None when it can)."""
+    t = e["types"]
+    if shape is None:
+        return "unreadable shape"
+    if t[0] not in REPLAY_TYPES or len(set(t[:2] + t[3:])) != 1:
+        return f"types {t[0]} x {t[1]} -> {t[3]} (replayed: bf16 or fp16 in and out)"
+    if shape["m"] * shape["n"] * shape["batch"] > max_elements:
+        return "an output too large for the float64 reference here"
+    return None
+
+
+def _replay_key(e: dict, s: dict) -> tuple:
+    return (s["m"], s["n"], s["k"], s["batch"], s["transa"], s["transb"], e["types"][0])
+
+
+def judge_output(y, ref, a_abs, b_abs, k: int, dtype: str) -> dict:
+    """Elements outside |y - ref| <= u_out |ref| + k 2^-22 (|A| |B|) (+ tiny), and elements never written (NaN)."""
+    import torch
+    u_out = 2.0 ** -8 if dtype == "bf16" else 2.0 ** -11
+    mag = torch.matmul(a_abs, b_abs)
+    bound = u_out * ref.abs() + k * 2.0 ** -22 * mag + 1e-30
+    yd = y.double()
+    unwritten = int(torch.isnan(yd).sum())
+    bad = int(((yd - ref).abs() > bound).sum()) if not unwritten else int((~torch.isfinite(yd)).sum())
+    return {"wrong": bad, "unwritten": unwritten}
+
+
+def _worker_main(todo_path: str, out_path: str) -> None:
+    """Child process of `test`: replays each shape with the operand layouts of its cuBLAS call."""
+    import torch
+    with open(todo_path) as f:
+        todo = json.load(f)
+    dev = torch.device("cuda")
+    res = []
+    for t in todo:
+        dt = torch.bfloat16 if t["dtype"] == "bf16" else torch.float16
+        m, n, k, b = t["m"], t["n"], t["k"], t["batch"]
+        g = torch.Generator(device=dev).manual_seed(1234 + len(res))
+        wrong = unwritten = 0
+        for _ in range(t["repeats"]):
+            # column-major D (m x n) = op(A) op(B) is row-major Y (n x m) = op(B)^T op(A)^T; build each operand in
+            # the storage its transpose flag implies so that cuBLAS sees the same call
+            A = torch.randn(b, *((m, k) if t["transa"] == "OP_T" else (k, m)), generator=g, device=dev).to(dt)
+            B = torch.randn(b, *((k, n) if t["transb"] == "OP_T" else (n, k)), generator=g, device=dev).to(dt)
+            a_op = A.transpose(1, 2) if t["transa"] == "OP_T" else A          # (b, k, m) view
+            b_op = B.transpose(1, 2) if t["transb"] == "OP_T" else B          # (b, n, k) view
+            y = torch.full((b, n, m), float("nan"), dtype=dt, device=dev)
+            if b == 1:
+                torch.matmul(b_op[0], a_op[0], out=y[0])
+            else:
+                torch.bmm(b_op, a_op, out=y)
+            torch.cuda.synchronize()
+            ref = torch.matmul(b_op.double(), a_op.double())
+            j = judge_output(y, ref, b_op.double().abs(), a_op.double().abs(), k, t["dtype"])
+            wrong += j["wrong"] > 0 or j["unwritten"] > 0
+            unwritten += j["unwritten"] > 0
+        res.append({"runs": t["repeats"], "runs_wrong": wrong, "runs_unwritten": unwritten})
+    with open(out_path, "w") as f:
+        json.dump({"results": res, "gpu": torch.cuda.get_device_name(dev)}, f)
+
+
+def _run_worker(todo: list, log_dir: str, timeout: float = 1800.0) -> tuple:
+    os.makedirs(log_dir, exist_ok=True)
+    tp, op = os.path.join(log_dir, "todo.json"), os.path.join(log_dir, "results.json")
+    log = os.path.join(log_dir, "cublaslt.log")
+    with open(tp, "w") as f:
+        json.dump(todo, f)
+    env = dict(os.environ, CUBLASLT_LOG_LEVEL="5", CUBLASLT_LOG_FILE=log)
+    subprocess.run([sys.executable, "-m", "sdcguard_b200.tools.kernels", "_worker", tp, op], env=env, check=True,
+                   timeout=timeout)
+    with open(op) as f:
+        out = json.load(f)
+    lines = []
+    for name in sorted(os.listdir(log_dir)):
+        if name.startswith("cublaslt"):
+            with open(os.path.join(log_dir, name), errors="replace") as f:
+                lines.extend(f)
+    return out, lines
+
+
+def test_calls(inv: dict, repeats: int = 3, log_dir: str = "kernel_test_logs", max_shapes: int = 200,
+               runner=None, max_elements: float = MAX_ELEMENTS) -> dict:
+    """The verdict of every inventoried call replayed here (see the module docstring)."""
+    todo, index, rows, not_run = [], {}, [], []
+    order = sorted(inv["kernels"].items(), key=lambda kv: -kv[1]["work"])
+    for key, e in order:
+        for sk in e["shapes"]:
+            s = parse_shape(sk)
+            why = rerunnable(e, s, max_elements)
+            if why is None and s is not None:
+                rk = _replay_key(e, s)
+                if rk not in index:
+                    if len(todo) >= max_shapes:
+                        why = f"past --max-shapes {max_shapes}"
+                    else:
+                        index[rk] = len(todo)
+                        todo.append(dict(s, dtype=e["types"][0], repeats=repeats))
+            rows.append({"kernel": key, "shape": sk, "call": f"{key} | {sk}", "calls_in_workload": e["shapes"][sk],
+                         "why_not_run": why, "replay": index.get(_replay_key(e, s)) if s and why is None else None})
+    out, lines = (runner or _run_worker)(todo, log_dir) if todo else ({"results": [], "gpu": None}, [])
+    ran: dict = {}
+    for line in lines:
+        try:
+            c = parse_line(line)
+        except ValueError:
+            continue
+        if c is None:
+            continue
+        rk = (c["m"], c["n"], c["k"], c["batch"], c["transa"], c["transb"], c["types"][0])
+        ran.setdefault(rk, set()).add(kernel_key(c))
+    counts = dict.fromkeys(("PASSED", "WRONG", "OTHER KERNEL", "NOT RUN"), 0)
+    calls = []
+    for r in rows:
+        if r["why_not_run"] is not None:
+            counts["NOT RUN"] += 1
+            calls.append({"call": r["call"], "kernel": r["kernel"], "verdict": "NOT RUN", "why": r["why_not_run"]})
+            continue
+        res = out["results"][r["replay"]]
+        t = todo[r["replay"]]
+        here = ran.get((t["m"], t["n"], t["k"], t["batch"], t["transa"], t["transb"], t["dtype"]), set())
+        if res["runs_wrong"]:
+            v = "WRONG"
+        elif r["kernel"] in here:
+            v = "PASSED"
+        else:
+            v = "OTHER KERNEL"
+        counts[v] += 1
+        calls.append({"call": r["call"], "kernel": r["kernel"], "verdict": v, "runs": res["runs"],
+                      "runs_wrong": res["runs_wrong"], "ran_here": sorted(here)[:4]})
+    return {"format": "sdcguard-b200-kernel-test/1", "source": inv.get("source"), "gpu": out.get("gpu"),
+            "repeats": repeats, "counts": counts, "calls": calls, "shapes_replayed": len(todo)}
+
+
 def _load(p: str) -> dict:
     with open(p) as f:
         d = json.load(f)
@@ -212,7 +371,26 @@ def main(argv=None) -> int:
     df.add_argument("after")
     sh = sub.add_parser("show")
     sh.add_argument("inventory")
+    te = sub.add_parser("test")
+    te.add_argument("inventory")
+    te.add_argument("--out")
+    te.add_argument("--repeats", type=int, default=3)
+    te.add_argument("--max-shapes", type=int, default=200)
+    te.add_argument("--log-dir", default="kernel_test_logs")
+    wk = sub.add_parser("_worker")
+    wk.add_argument("todo")
+    wk.add_argument("result")
     a = ap.parse_args(argv)
+    if a.cmd == "_worker":
+        _worker_main(a.todo, a.result)
+        return 0
+    if a.cmd == "test":
+        r = test_calls(_load(a.inventory), a.repeats, a.log_dir, a.max_shapes)
+        if a.out:
+            with open(a.out, "w") as f:
+                json.dump(r, f, indent=1)
+        print(json.dumps(r["counts"]))
+        return 1 if r["counts"]["WRONG"] else 0 if r["counts"]["PASSED"] else 2
     if a.cmd == "record":
         cmd = a.command[1:] if a.command[:1] == ["--"] else a.command
         inv = record(cmd, a.out, a.seconds)

@@ -129,3 +129,47 @@ def test_replay_command_refuses_what_it_cannot_run(tmp_path):
     from sdcguard_b200 import cli
     assert cli.main(["replay", str(tmp_path / "missing.pt")]) == 2
     assert cli.main(["replay", str(tmp_path / "missing.pt"), "--times", "0"]) == 2
+
+
+def test_kernel_test_verdicts(tmp_path):
+    """`kernels test` bookkeeping with a fake replay worker: PASSED when the same kernel ran and every run was right,
+    OTHER KERNEL when another kernel ran, WRONG on a wrong run, NOT RUN for types it does not replay."""
+    inv = kernels.inventory([_line(1536, 16, 8960), _line(256, 16, 1536, algo=SPLIT), _line(128, 8, 64),
+                             _line(64, 64, 64, t="R_32F")])
+    seen = {}
+
+    def runner(todo, log_dir):
+        seen["todo"] = todo
+        res = []
+        for t in todo:
+            res.append({"runs": 3, "runs_wrong": 1 if t["m"] == 128 else 0, "runs_unwritten": 0})
+        # here the 1536-row shape runs the inventory's kernel, the 256-row one another
+        lines = [_line(1536, 16, 8960), _line(256, 16, 1536), _line(128, 8, 64)]
+        return {"results": res, "gpu": "fake"}, lines
+
+    r = kernels.test_calls(inv, repeats=3, log_dir=str(tmp_path), runner=runner)
+    v = {c["call"].split(" | ")[1].split(" batch")[0]: c["verdict"] for c in r["calls"]}
+    assert v["m=1536 n=16 k=8960"] == "PASSED"
+    assert v["m=256 n=16 k=1536"] == "OTHER KERNEL"
+    assert v["m=128 n=8 k=64"] == "WRONG"
+    assert v["m=64 n=64 k=64"] == "NOT RUN"
+    assert r["counts"] == {"PASSED": 1, "WRONG": 1, "OTHER KERNEL": 1, "NOT RUN": 1}
+    assert len(seen["todo"]) == 3 and all(t["dtype"] == "bf16" and t["transa"] == "OP_T" for t in seen["todo"])
+    # the decision reads the report: one judged call on the workload's kernel makes it a source, WRONG a fault
+    from sdcguard_b200.tools import decide
+    w = decide.kernel_test_witness(r)
+    assert w.tested == 2 and w.faults and not w.unresolved
+
+
+def test_kernel_test_output_judgement():
+    import torch
+    a = torch.randn(8, 32, dtype=torch.float64)
+    b = torch.randn(32, 4, dtype=torch.float64)
+    ref = a @ b
+    y = ref.to(torch.bfloat16)
+    assert kernels.judge_output(y, ref, a.abs(), b.abs(), 32, "bf16") == {"wrong": 0, "unwritten": 0}
+    bad = y.clone()
+    bad[1, 2] += 4.0
+    assert kernels.judge_output(bad, ref, a.abs(), b.abs(), 32, "bf16")["wrong"] == 1
+    bad[0, 0] = float("nan")
+    assert kernels.judge_output(bad, ref, a.abs(), b.abs(), 32, "bf16")["unwritten"] == 1
