@@ -113,7 +113,7 @@ SIGNATURES: dict[str, tuple] = {
     "sdc_moe_gather": (I, [P, L, I, I, I, I, P, P, P, P, P, P]),
     "sdc_moe_combine": (I, [P, I, I, I, P, P, P, L, I, P]),
     "sdc_prep_rowblock": (I, [P, L, I, I, U, U, U, U, P, P, P, P, P]),
-    "sdc_prep_colblock": (I, [P, L, I, I, U, U, U, U, P, P, P, P]),
+    "sdc_prep_colblock": (I, [P, L, I, I, U, U, U, U, P, P, P, P, P, P]),
     "sdc_transpose_bf16": (I, [P, L, I, I, P, P]),
     "sdc_dequant_weights": (I, [P, I, I, I, I, P, P, I, P, P]),
     "sdc_gemm_fp8_grouped": (I, [P, P, P, P, P, I, I, I, I, P, L, P, P, P, P, P, I, U, U, U, U, F, F, F, F, F, P, I,

@@ -13,9 +13,12 @@
 //   colblock_kernel : source M = B (N, K): the sums run down 128-row blocks (the forward weight after an update).
 //
 // Sums are in fp64 and split with round-to-nearest-even conversions from double (hi + mid + lo carries about 24
-// significant bits). The statistics are accumulated in fp32 with atomics (order-dependent in the last bits; they
-// only scale the noise model), then finalized by a one-CTA kernel. This replaces per-step fp64 PyTorch reductions
-// and transposes (several launches and an fp64 copy of each operand) with two or three launches per operand.
+// significant bits). The statistics are accumulated in fp32 with atomics into a scratch block (order-dependent in
+// the last bits; they only scale the noise model); the last CTA to finish (a ticket counter after a fence) turns
+// them into wstat and leaves the scratch and the ticket zeroed for the next call, so a prep is one launch: no
+// memset and no separate finalize kernel. colblock_kernel also takes the layer's bias and writes its plain and
+// signed block sums (fp64, one CTA column per block). This replaces per-step fp64 PyTorch reductions and transposes
+// (several launches and an fp64 copy of each operand) with one launch per operand (two for a transposed one).
 //
 // Reference: the reference's training check builds its expected side per step in its Triton kernels
 // (src/sdcguard/guard.py:497 `_checked_backward`, checksum.py:160 `_split3`).
@@ -56,9 +59,13 @@ struct Signs {
   uint32_t w[4];
 };
 
-// Adds a CTA's block statistics (squares, plain^2, signed^2; max |x|) into acc[b] (zeroed by the launcher).
-__device__ __forceinline__ void add_stats(float* acc, float sq, float pl, float sg, float mx, float* red) {
+// Adds a CTA's block statistics (squares, plain^2, signed^2; max |x|) into acc[b]. The scratch acc holds nb * 4
+// floats and then a ticket counter; both are zero between calls. The CTA that draws the last ticket writes wstat
+// (square roots of the sums, and the max) for every block, zeroing acc and the ticket as it reads them.
+__device__ __forceinline__ void add_stats(float* acc_all, int b, int nb, float sq, float pl, float sg, float mx,
+                                          float* red, float* __restrict__ wstat) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __shared__ int last;
   sq = warp_sum_f(sq);
   pl = warp_sum_f(pl);
   sg = warp_sum_f(sg);
@@ -71,24 +78,42 @@ __device__ __forceinline__ void add_stats(float* acc, float sq, float pl, float 
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    float a = 0.f, b = 0.f, c = 0.f, d = 0.f;
+    float a = 0.f, bb = 0.f, c = 0.f, d = 0.f;
     for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) {
       a += red[w * 4];
-      b += red[w * 4 + 1];
+      bb += red[w * 4 + 1];
       c += red[w * 4 + 2];
       d = fmaxf(d, red[w * 4 + 3]);
     }
+    float* acc = acc_all + b * 4;
     atomicAdd(acc + 0, a);
-    atomicAdd(acc + 1, b);
+    atomicAdd(acc + 1, bb);
     atomicAdd(acc + 2, c);
     atomicMax(reinterpret_cast<unsigned int*>(acc + 3), __float_as_uint(d));   // non-negative floats order as ints
+    __threadfence();
+    unsigned int* ticket = reinterpret_cast<unsigned int*>(acc_all + nb * 4);
+    const unsigned int total = gridDim.x * gridDim.y;
+    last = (atomicAdd(ticket, 1u) == total - 1u);
+  }
+  __syncthreads();
+  if (last) {
+    __threadfence();
+    for (int i = threadIdx.x; i < nb; i += blockDim.x) {
+      float* acc = acc_all + i * 4;
+      wstat[i * 4 + 0] = sqrtf(atomicExch(acc + 0, 0.f));
+      wstat[i * 4 + 1] = sqrtf(atomicExch(acc + 1, 0.f));
+      wstat[i * 4 + 2] = sqrtf(atomicExch(acc + 2, 0.f));
+      wstat[i * 4 + 3] = __uint_as_float(atomicExch(reinterpret_cast<unsigned int*>(acc + 3), 0u));
+    }
+    if (threadIdx.x == 0) atomicExch(reinterpret_cast<unsigned int*>(acc_all + nb * 4), 0u);
   }
 }
 
 // Grid (ceil(R / 64), nb), 256 threads. Tile: 64 rows of M x the 128 columns of block b.
 __global__ void __launch_bounds__(256) rowblock_kernel(const __nv_bfloat16* __restrict__ M, long long ldm, int R,
                                                        int C, Signs sg, __nv_bfloat16* __restrict__ T,
-                                                       __nv_bfloat16* __restrict__ wc, float* __restrict__ acc) {
+                                                       __nv_bfloat16* __restrict__ wc, float* __restrict__ acc,
+                                                       float* __restrict__ wstat) {
   __shared__ __align__(16) __nv_bfloat16 tile[64][BLK + 8];
   __shared__ float red[32];
   const int r0 = blockIdx.x * 64, b = blockIdx.y, c0 = b * BLK;
@@ -144,16 +169,19 @@ __global__ void __launch_bounds__(256) rowblock_kernel(const __nv_bfloat16* __re
       }
     }
   }
-  add_stats(acc + b * 4, sq, pl2, sg2, mx, red);
+  add_stats(acc, b, gridDim.y, sq, pl2, sg2, mx, red, wstat);
 }
 
 // Grid (ceil(C / 64), nb), 256 threads. Tile: the 128 rows of block b x 64 columns; thread (q, c) sums rows
-// 32q .. 32q + 31 of column c, the four quarters are added in order.
+// 32q .. 32q + 31 of column c, the four quarters are added in order. With a bias (R entries, fp32), the CTAs of
+// column 0 also write its block sums: bsum[b] = (sum of bias[128 b ..], signed sum), fp64 sums stored as fp32.
 __global__ void __launch_bounds__(256) colblock_kernel(const __nv_bfloat16* __restrict__ M, long long ldm, int R,
                                                        int C, Signs sg, __nv_bfloat16* __restrict__ wc,
-                                                       float* __restrict__ acc) {
+                                                       float* __restrict__ acc, float* __restrict__ wstat,
+                                                       const float* __restrict__ bias, float* __restrict__ bsum) {
   __shared__ double part[2][4][64];
   __shared__ float red[32];
+  __shared__ double bred[2][4];
   const int cl = threadIdx.x & 63, q = threadIdx.x >> 6;
   const int c = blockIdx.x * 64 + cl, b = blockIdx.y;
   double p = 0.0, s = 0.0;
@@ -171,7 +199,22 @@ __global__ void __launch_bounds__(256) colblock_kernel(const __nv_bfloat16* __re
   }
   part[0][q][cl] = p;
   part[1][q][cl] = s;
+  if (bias != nullptr && blockIdx.x == 0 && threadIdx.x < BLK) {
+    // threads 0..127: entry t of the bias block; warps 0..3 reduce in fp64
+    const int t = threadIdx.x, r = b * BLK + t;
+    const double v = r < R ? static_cast<double>(bias[r]) : 0.0;
+    double bp = warp_sum_d(v);
+    double bs = warp_sum_d(((sg.w[t >> 5] >> (t & 31)) & 1u) ? -v : v);
+    if ((t & 31) == 0) {
+      bred[0][t >> 5] = bp;
+      bred[1][t >> 5] = bs;
+    }
+  }
   __syncthreads();
+  if (bias != nullptr && blockIdx.x == 0 && threadIdx.x == 0) {
+    bsum[b * 2 + 0] = static_cast<float>(((bred[0][0] + bred[0][1]) + bred[0][2]) + bred[0][3]);
+    bsum[b * 2 + 1] = static_cast<float>(((bred[1][0] + bred[1][1]) + bred[1][2]) + bred[1][3]);
+  }
   float pl2 = 0.f, sg2 = 0.f;
   if (q == 0 && c < C) {
     const double P = ((part[0][0][cl] + part[0][1][cl]) + part[0][2][cl]) + part[0][3][cl];
@@ -181,7 +224,7 @@ __global__ void __launch_bounds__(256) colblock_kernel(const __nv_bfloat16* __re
     pl2 = static_cast<float>(P * P);
     sg2 = static_cast<float>(S * S);
   }
-  add_stats(acc + b * 4, sq, pl2, sg2, mx, red);
+  add_stats(acc, b, gridDim.y, sq, pl2, sg2, mx, red, wstat);
 }
 
 // Transpose of a bf16 matrix, T = M^T (M: R x C with row stride ldm; T: C x R, row stride R). Grid (ceil(C / 64),
@@ -238,35 +281,24 @@ __global__ void __launch_bounds__(256) transpose_kernel(const __nv_bfloat16* __r
   }
 }
 
-__global__ void finalize_kernel(const float* __restrict__ acc, int nb, float* __restrict__ wstat) {
-  for (int b = threadIdx.x; b < nb; b += blockDim.x) {
-    wstat[b * 4 + 0] = sqrtf(acc[b * 4 + 0]);
-    wstat[b * 4 + 1] = sqrtf(acc[b * 4 + 1]);
-    wstat[b * 4 + 2] = sqrtf(acc[b * 4 + 2]);
-    wstat[b * 4 + 3] = acc[b * 4 + 3];
-  }
-}
-
 }  // namespace prep
 }  // namespace sdc
 
 extern "C" {
 
 // Checksum data of B = M^T for M (R, C) bf16 row-major (ld elements): wc (6 nb, R) bf16 with nb = ceil(C / 128),
-// wstat (nb, 4) fp32, and B itself into T (C, R) when T is not null. acc: device scratch of nb * 4 floats.
+// wstat (nb, 4) fp32, and B itself into T (C, R) when T is not null. acc: device scratch of nb * 4 + 1 floats, zero
+// before the call and left zero after it (calls that share it must be ordered, e.g. on one stream).
 int sdc_prep_rowblock(const void* M, long long ldm, int R, int C, unsigned s0, unsigned s1, unsigned s2, unsigned s3,
                       void* T, void* wc, float* wstat, float* acc, void* stream) {
   if (R <= 0 || C <= 0) return 0;
   if (C % 8 || ldm % 8) return -1;
   auto st = static_cast<cudaStream_t>(stream);
   const int nb = (C + 127) / 128;
-  cudaError_t e = cudaMemsetAsync(acc, 0, sizeof(float) * 4 * nb, st);
-  if (e != cudaSuccess) return static_cast<int>(e);
   sdc::prep::Signs sg{{s0, s1, s2, s3}};
   sdc::prep::rowblock_kernel<<<dim3((R + 63) / 64, nb), 256, 0, st>>>(
       static_cast<const __nv_bfloat16*>(M), ldm, R, C, sg, static_cast<__nv_bfloat16*>(T),
-      static_cast<__nv_bfloat16*>(wc), acc);
-  sdc::prep::finalize_kernel<<<1, 256, 0, st>>>(acc, nb, wstat);
+      static_cast<__nv_bfloat16*>(wc), acc, wstat);
   return static_cast<int>(cudaGetLastError());
 }
 
@@ -280,18 +312,17 @@ int sdc_transpose_bf16(const void* M, long long ldm, int R, int C, void* T, void
   return static_cast<int>(cudaGetLastError());
 }
 
-// Checksum data of B = M for M (R, C) bf16 row-major: wc (6 nb, C) with nb = ceil(R / 128), wstat (nb, 4).
+// Checksum data of B = M for M (R, C) bf16 row-major: wc (6 nb, C) with nb = ceil(R / 128), wstat (nb, 4); with a
+// bias (R fp32 entries), its block sums into bsum (nb, 2). acc as for sdc_prep_rowblock.
 int sdc_prep_colblock(const void* M, long long ldm, int R, int C, unsigned s0, unsigned s1, unsigned s2, unsigned s3,
-                      void* wc, float* wstat, float* acc, void* stream) {
+                      void* wc, float* wstat, float* acc, const float* bias, float* bsum, void* stream) {
   if (R <= 0 || C <= 0) return 0;
+  if (bias != nullptr && bsum == nullptr) return -1;
   auto st = static_cast<cudaStream_t>(stream);
   const int nb = (R + 127) / 128;
-  cudaError_t e = cudaMemsetAsync(acc, 0, sizeof(float) * 4 * nb, st);
-  if (e != cudaSuccess) return static_cast<int>(e);
   sdc::prep::Signs sg{{s0, s1, s2, s3}};
   sdc::prep::colblock_kernel<<<dim3((C + 63) / 64, nb), 256, 0, st>>>(
-      static_cast<const __nv_bfloat16*>(M), ldm, R, C, sg, static_cast<__nv_bfloat16*>(wc), acc);
-  sdc::prep::finalize_kernel<<<1, 256, 0, st>>>(acc, nb, wstat);
+      static_cast<const __nv_bfloat16*>(M), ldm, R, C, sg, static_cast<__nv_bfloat16*>(wc), acc, wstat, bias, bsum);
   return static_cast<int>(cudaGetLastError());
 }
 

@@ -301,12 +301,12 @@ class CheckedWeight:
         n, k = w.shape
         if n % 8 or k % 8:
             raise ValueError(f"checked GEMM needs n and k multiples of 8 (got n={n}, k={k})")
-        cs = _prep(w, transposed=False)
-        if bias is not None:
-            # the bias's largest magnitude is not read back here (a host read per layer would stall a training
-            # step): 0 means a non-finite output counts as corruption unless the weights and inputs can produce it
-            cs.bsum, cs.bias_max = _bias_sums(bias, n, cs.mask), 0.0
-        return cls._assemble(w, cs, bias, c1, c2, c3)
+        # the bias's block sums come from the same launch; its largest magnitude is not read back (a host read per
+        # layer would stall a training step): 0 means a non-finite output counts as corruption unless the weights
+        # and inputs can produce it
+        b32 = None if bias is None else bias.detach().float().contiguous()
+        cs = _prep(w, transposed=False, bias=b32)
+        return cls._assemble(w, cs, b32, c1, c2, c3)
 
     @classmethod
     def of_transpose(cls, m: torch.Tensor, c1: float = abft.C1, c2: float = abft.C2,
@@ -325,15 +325,6 @@ class CheckedWeight:
         return cls._assemble(t, cs, None, c1, c2, c3)
 
 
-def _bias_sums(bias: torch.Tensor, n: int, mask) -> torch.Tensor:
-    nb = -(-n // abft.BLOCK)
-    b64 = torch.zeros(nb * abft.BLOCK, dtype=torch.float64, device=bias.device)
-    b64[:n] = bias.detach().double()
-    bb = b64.view(nb, abft.BLOCK)
-    s = abft.sign_vector(mask, device=bias.device)
-    return torch.stack([bb.sum(1), (bb * s.view(1, abft.BLOCK)).sum(1)], dim=1).float().contiguous()
-
-
 def transpose(m: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """m^T as a new contiguous bf16 tensor, by a tiled shared-memory transpose kernel (PyTorch's strided copy of
     `.t().contiguous()` is several times slower at these sizes)."""
@@ -350,15 +341,17 @@ def transpose(m: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tens
 _PREP_ACC: dict = {}
 
 
-def _prep(m: torch.Tensor, transposed: bool):
-    """Device checksum data: of B = m (transpose False) or of B = m^T (True, also returning m^T)."""
+def _prep(m: torch.Tensor, transposed: bool, bias: Optional[torch.Tensor] = None):
+    """Device checksum data: of B = m (transpose False; with its bias's block sums when given) or of B = m^T (True,
+    also returning m^T). The kernels' statistics scratch (nb * 4 floats and a ticket) is zero between calls: the
+    last CTA of each launch finalizes the statistics and clears it."""
     dev = m.device
     r, c = m.shape
     mask = abft.sign_mask()
     nb = -(-(c if transposed else r) // abft.BLOCK)
     acc = _PREP_ACC.get(dev)
-    if acc is None or acc.numel() < nb * 4:
-        acc = _PREP_ACC[dev] = torch.empty(max(nb * 4, 1024), dtype=torch.float32, device=dev)
+    if acc is None or acc.numel() < nb * 4 + 1:
+        acc = _PREP_ACC[dev] = torch.zeros(max(nb * 4 + 1, 1025), dtype=torch.float32, device=dev)
     wstat = torch.empty(nb, 4, dtype=torch.float32, device=dev)
     lib = _native.lib()
     if transposed:
@@ -370,10 +363,17 @@ def _prep(m: torch.Tensor, transposed: bool):
         cs = abft.WeightChecksums(n=c, k=r, nb=nb, wc=wc, wstat=wstat, bsum=None, bias_max=0.0, mask=mask)
         return cs, t
     wc = torch.empty(nb * abft.CS_ROWS, c, dtype=torch.bfloat16, device=dev)
+    bsum = None
+    if bias is not None:
+        if bias.dtype != torch.float32 or bias.numel() != r or not bias.is_contiguous():
+            raise ValueError("bias must be a contiguous fp32 vector of the weight's rows")
+        bsum = torch.empty(nb, 2, dtype=torch.float32, device=dev)
     _native.check(lib.sdc_prep_colblock(m.data_ptr(), m.stride(0), r, c, mask[0], mask[1], mask[2], mask[3],
-                                        wc.data_ptr(), wstat.data_ptr(), acc.data_ptr(), _stream_ptr(dev)),
+                                        wc.data_ptr(), wstat.data_ptr(), acc.data_ptr(),
+                                        None if bias is None else bias.data_ptr(),
+                                        None if bsum is None else bsum.data_ptr(), _stream_ptr(dev)),
                   "checksum prep (columns)")
-    return abft.WeightChecksums(n=r, k=c, nb=nb, wc=wc, wstat=wstat, bsum=None, bias_max=0.0, mask=mask)
+    return abft.WeightChecksums(n=r, k=c, nb=nb, wc=wc, wstat=wstat, bsum=bsum, bias_max=0.0, mask=mask)
 
 
 def row_sqnorm(x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:

@@ -41,7 +41,8 @@ class _Cache:
     the optimizer changes weights between steps, and fused optimizers (AdamW(fused=True)) do so without bumping the
     tensors' version counters, so a version check alone would keep stale checksums and a stale bf16 copy. A weight
     kept in fp32 (mixed precision under autocast) is checked as its bf16 copy, which is what autocast would feed the
-    GEMM; the bias is copied with it, so the GEMM adds the bias the checksums were built from."""
+    GEMM. A bf16 weight and an fp32 bias are used in place: nothing changes them between the forward and the backward
+    of a checked step, and the host reads the step's checks (and replays alarms) before the optimizer runs."""
 
     def __init__(self, guard: "SDCGuard"):
         self.guard = guard
@@ -52,8 +53,8 @@ class _Cache:
     def get(self, w: torch.Tensor, b: Optional[torch.Tensor]):
         key = (self.guard.epoch, w.data_ptr(), w._version, None if b is None else (b.data_ptr(), b._version))
         if key != self.key:
-            wb = w.detach().to(torch.bfloat16, copy=True)
-            bb = None if b is None else b.detach().float().clone()
+            wb = w.detach().to(torch.bfloat16)
+            bb = None if b is None else b.detach()
             self.cw = gemm.CheckedWeight.on_device(wb, bb)
             self.cwT = None
             self.key = key
@@ -100,7 +101,7 @@ def _bwd_gemms(mod: "CheckedLinear", dy, x2, wb, xshape, need_x: bool, need_w: b
             dw = dy2.t() @ x2
             g.unchecked += 1
     if need_b:
-        db = dy2.float().sum(0)
+        db = dy2.sum(0, dtype=torch.float32)
     return dx, dw, db
 
 

@@ -54,6 +54,23 @@ def test_colblock_matches_reference(n, k):
     assert float(((y.double() - ref_y).abs() / (ref_y.abs() + 1e-2)).max()) < 2 ** -7
 
 
+def test_prep_scratch_is_left_zero():
+    """Each prep launch finalizes its own statistics and clears the shared scratch: back-to-back preps of different
+    block counts give the same statistics as fresh ones."""
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(7)
+    ws = [(torch.randn(n, 256, device=dev, generator=g) * 0.05).bfloat16() for n in (1024, 128, 640)]
+    first = [gemm.CheckedWeight.on_device(w).cs.wstat.clone() for w in ws]
+    for _ in range(3):
+        for w, f in zip(ws, first):
+            assert torch.equal(gemm.CheckedWeight.on_device(w).cs.wstat, f)
+            t = gemm.CheckedWeight.of_transpose(w)
+            assert torch.allclose(t.cs.wstat, abft.weight_checksums(w.t().contiguous()).wstat, rtol=1e-4, atol=1e-6)
+    acc = gemm._PREP_ACC[dev]
+    torch.cuda.synchronize()
+    assert int((acc != 0).sum()) == 0
+
+
 def test_autocast_training_step_checked():
     from sdcguard_b200.train.guard import SDCGuard
     dev = torch.device("cuda")
