@@ -161,6 +161,22 @@ def reserve_workspace(device: torch.device, m: int, n: int) -> None:
     workspace(device, int(_native.lib().sdc_gemm_ws_bytes(m, n)))
 
 
+_RESERVED_ROWS: dict = {}
+
+
+def reserve_for_rows(device: torch.device, n: int, max_m: int) -> int:
+    """Size the workspace for every row count 1..max_m of an n-column GEMM (split-K at small row counts can need
+    more than the largest count does); returns the bytes reserved. For callers whose row count varies under CUDA
+    graph capture (a serving engine's batch sizes)."""
+    key = (n, max_m)
+    need = _RESERVED_ROWS.get(key)
+    if need is None:
+        f = _native.lib().sdc_gemm_ws_bytes
+        need = _RESERVED_ROWS[key] = max(int(f(m, n)) for m in range(1, max_m + 1))
+    workspace(device, need)
+    return need
+
+
 def error_word(device: torch.device) -> torch.Tensor:
     idx = device.index if device.index is not None else torch.cuda.current_device()
     e = _ERR.get(idx)

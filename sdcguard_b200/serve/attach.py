@@ -140,8 +140,10 @@ class AttachedGuard(ServeGuard):
 
 
 def attach(model: torch.nn.Module, share: Optional[float] = None, offset: Optional[int] = None,
-           settings: Optional[CheckSettings] = None, device=None, **guard_kw) -> AttachedGuard:
-    """Swap the selected bf16 nn.Linear layers of `model` for checked ones; returns their serving guard."""
+           settings: Optional[CheckSettings] = None, device=None, max_tokens: int = 0, **guard_kw) -> AttachedGuard:
+    """Swap the selected bf16 nn.Linear layers of `model` for checked ones; returns their serving guard.
+    max_tokens > 0: size the GEMM workspace now for every row count up to it (required before capturing the model
+    in a CUDA graph)."""
     settings = settings or CheckSettings.from_env()
     if share is not None:
         settings.share = share
@@ -173,6 +175,8 @@ def attach(model: torch.nn.Module, share: Optional[float] = None, offset: Option
         cw_probe = mod.weight.shape
         slot = am.state.add(f"{name} (ABFT GEMM)", -(-cw_probe[0] // 128))
         st = LayerState(am, name, mod, slot)
+        if max_tokens > 0:
+            gemm.reserve_for_rows(device, st.cw.n, max_tokens)
         swap.take_over(mod, st)
         am.layers.append((name, mod, st, None))
     g = AttachedGuard(am, z_alarm=settings.z_alarm, **guard_kw)

@@ -1,0 +1,228 @@
+"""vLLM plugin: vLLM's unquantized bf16 linear layers run on this package's checked tcgen05 GEMM while vLLM serves.
+
+    SDCGUARD_B200=1 vllm serve <model>            # with this package installed (entry point vllm.general_plugins)
+    # or in-process: sdcguard_b200.serve.vllm_plugin.register() before constructing vllm.LLM
+
+Off unless SDCGUARD_B200=1 (vLLM loads every installed plugin). In each vLLM process that loads models:
+
+  - after vLLM has loaded a linear layer's weights (`UnquantizedLinearMethod.process_weights_after_loading`), a
+    bf16 layer on a CUDA device with both dimensions multiples of 8, selected by SDCGUARD_SHARE / SDCGUARD_OFFSET
+    (the rule of `serve.settings`), gets its checksum rows built once and a row in the device's check state table;
+  - its matmul (`UnquantizedLinearMethod.apply`) then runs as one custom operator, `sdcguard_b200_vllm::linear`,
+    whose CUDA implementation is the checked GEMM: the layer's output is the checked kernel's own, and its check
+    runs in the kernel's epilogue. The operator has a fake implementation, so vLLM's torch.compile keeps one graph
+    and its CUDA graphs capture the kernel; the GEMM workspace is sized before capture for every batch size up to
+    the scheduler's largest (max_num_batched_tokens);
+  - every SDCGUARD_POLL_EVERY model steps (default 16) the state table is read without stalling the GPU (the read
+    reports the previous one, as `ServeGuard.poll(wait=False)`), alarms are logged as `sdcguard ALERT` lines and
+    appended to SDCGUARD_LOG as JSON events;
+  - `coverage()` gives the layers checked and left out, with the reason, and the share of linear-layer weights
+    checked. Layers left out (other dtypes, quantized methods, the LM head, outside the share) run vLLM's own GEMM.
+
+The reference's plugin (SDCGUARD=1) keeps vLLM's GEMM and adds a Triton check after it; here the check is part of
+the GEMM, so a checked layer is still one launch. Differences in rounding order from cuBLAS's GEMM are in the last
+bit of the bf16 outputs.
+
+Reference: src/sdcguard/vllm_plugin.py:1-80 (what the plugin checks and its settings), `register` :2239, the
+model-runner hook :2430-2501.
+"""
+from __future__ import annotations
+
+import logging
+import os
+import threading
+from typing import Optional
+
+import torch
+
+log = logging.getLogger("sdcguard_b200")
+
+ENV = "SDCGUARD_B200"
+_STATE: dict = {}          # device -> DeviceState
+_LAYERS: list = []         # layer id -> (name, CheckedWeight, slot, device)
+_LEFT_OUT: list = []       # (name, reason)
+_LOCK = threading.Lock()
+_REGISTERED = [False]
+_COUNTER = [0]             # linear layers seen (selection index)
+_LIB = None
+
+
+class DeviceState:
+    def __init__(self, device: torch.device):
+        from ..ops import gemm
+        from .settings import CheckSettings
+        self.device = device
+        self.settings = CheckSettings.from_env()
+        self.state = gemm.StateTable(device, 512)
+        self.slot_weights: dict = {}
+        self.steps = 0
+        self.guard = None
+        gemm.enable_capture(device)
+
+
+def _max_tokens() -> int:
+    try:
+        from vllm.config import get_current_vllm_config_or_none
+        cfg = get_current_vllm_config_or_none()
+        if cfg is not None and cfg.scheduler_config is not None:
+            return int(cfg.scheduler_config.max_num_batched_tokens)
+    except Exception:  # noqa: BLE001  (older vLLM: use the setting)
+        pass
+    return int(os.environ.get("SDCGUARD_B200_MAX_TOKENS", "16384"))
+
+
+def _state(device: torch.device) -> DeviceState:
+    st = _STATE.get(device)
+    if st is None:
+        from ..ops import verify
+        verify.verified(device)               # the kernels reproduce their references on this device first
+        st = _STATE[device] = DeviceState(device)
+    return st
+
+
+def _layer_name(layer: torch.nn.Module) -> str:
+    return getattr(layer, "prefix", None) or f"linear{_COUNTER[0]}"
+
+
+def _adopt(layer: torch.nn.Module) -> None:
+    """Checksums of a loaded linear layer and its state row, when it can be checked."""
+    from ..ops import gemm
+    from .settings import layer_selected
+    w = getattr(layer, "weight", None)
+    name = _layer_name(layer)
+    with _LOCK:
+        i = _COUNTER[0]
+        _COUNTER[0] += 1
+    why = None
+    if w is None or not isinstance(w, torch.Tensor):
+        why = "no weight tensor"
+    elif w.device.type != "cuda":
+        why = "not on a CUDA device"
+    elif w.dtype != torch.bfloat16 or w.dim() != 2:
+        why = f"weight {w.dtype} {tuple(w.shape)} (the checked GEMM multiplies 2-D bf16)"
+    elif w.shape[0] % 8 or w.shape[1] % 8:
+        why = f"shape {tuple(w.shape)}: n and k must be multiples of 8"
+    if why is None:
+        st = _state(w.device)
+        if not layer_selected(i, st.settings.share, st.settings.offset):
+            why = f"outside the share {st.settings.share:g}"
+    if why is not None:
+        _LEFT_OUT.append((name, why))
+        return
+    bias = getattr(layer, "bias", None)
+    add_bias = bias is not None and not getattr(layer, "skip_bias_add", False)
+    cw = gemm.CheckedWeight(w.detach(), bias.detach() if add_bias else None)
+    slot = st.state.add(f"{name} (ABFT GEMM)", cw.nb)
+    st.slot_weights[slot] = cw
+    # the workspace is sized now, before vLLM captures CUDA graphs, for every batch size the scheduler can form
+    gemm.reserve_for_rows(w.device, cw.n, _max_tokens())
+    gemm.error_word(w.device)
+    with _LOCK:
+        layer._sdcguard_b200_id = len(_LAYERS)
+        _LAYERS.append((name, cw, slot, w.device, add_bias))
+
+
+def _linear_impl(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor], layer: int) -> torch.Tensor:
+    from ..ops import gemm
+    name, cw, slot, dev, add_bias = _LAYERS[layer]
+    x2 = x.reshape(-1, x.shape[-1])
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    st = _STATE[dev]
+    y = gemm.checked_linear(x2, cw, st.state.state, slot, z_alarm=st.settings.z_alarm)
+    if bias is not None and not add_bias:
+        y = y + bias
+    return y.view(*x.shape[:-1], cw.n)
+
+
+def _linear_fake(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor], layer: int) -> torch.Tensor:
+    return x.new_empty(*x.shape[:-1], weight.shape[0])
+
+
+def _define_op() -> None:
+    global _LIB
+    if _LIB is not None:
+        return
+    _LIB = torch.library.Library("sdcguard_b200_vllm", "DEF")
+    _LIB.define("linear(Tensor x, Tensor weight, Tensor? bias, int layer) -> Tensor")
+    _LIB.impl("linear", _linear_impl, "CUDA")
+    _LIB._register_fake("linear", _linear_fake)
+
+
+def _poll(dev: torch.device, wait: bool = False) -> list:
+    """Read the device's check state (non-blocking unless wait) and log alarms."""
+    st = _STATE[dev]
+    if st.guard is None:
+        from ..utils.events import EventLog
+        from .guard import ServeGuard
+        st.guard = ServeGuard(st, z_alarm=st.settings.z_alarm, log=EventLog(os.environ.get("SDCGUARD_LOG")))
+    events = st.guard.poll(wait=wait)
+    for ev in events:
+        log.error("sdcguard ALERT: %s on %s: %s", ev.detail.get("layer"), dev, {k: v for k, v in ev.detail.items()
+                                                                                  if k != "layer"})
+    return events
+
+
+def _after_step() -> None:
+    every = max(1, int(os.environ.get("SDCGUARD_POLL_EVERY", "16")))
+    for dev, st in list(_STATE.items()):
+        st.steps += 1
+        if st.steps % every == 0:
+            _poll(dev)
+
+
+def coverage() -> dict:
+    """Layers checked, layers left out (with reasons), the share of linear-layer weight elements checked, and the
+    serving guard's counts per device (after a final blocking read)."""
+    checked_el = sum(cw.n * cw.k for _, cw, _, _, _ in _LAYERS)
+    out = {"layers_checked": len(_LAYERS), "layers_left_out": len(_LEFT_OUT), "left_out": _LEFT_OUT[:64],
+           "checked_weight_elements": checked_el, "devices": {}}
+    for dev, st in _STATE.items():
+        _poll(dev, wait=True)
+        out["devices"][str(dev)] = st.guard.coverage_report()
+    return out
+
+
+def _patch() -> None:
+    from vllm.model_executor.layers.linear import UnquantizedLinearMethod
+    orig_load = UnquantizedLinearMethod.process_weights_after_loading
+    orig_apply = UnquantizedLinearMethod.apply
+
+    def process_weights_after_loading(self, layer):
+        orig_load(self, layer)
+        try:
+            _adopt(layer)
+        except Exception as e:  # noqa: BLE001  (a layer that cannot be adopted runs vLLM's GEMM, counted)
+            _LEFT_OUT.append((_layer_name(layer), f"not adopted: {type(e).__name__}: {e}"[:200]))
+
+    def apply(self, layer, x, bias=None):
+        lid = getattr(layer, "_sdcguard_b200_id", None)
+        if lid is None or x.dtype != torch.bfloat16:
+            return orig_apply(self, layer, x, bias)
+        return torch.ops.sdcguard_b200_vllm.linear(x, layer.weight, bias, lid)
+
+    UnquantizedLinearMethod.process_weights_after_loading = process_weights_after_loading
+    UnquantizedLinearMethod.apply = apply
+    try:
+        from vllm.v1.worker.gpu_model_runner import GPUModelRunner
+    except ImportError:
+        log.warning("sdcguard_b200: no vLLM V1 model runner to hook; results are read only by coverage()")
+        return
+    orig_exec = GPUModelRunner.execute_model
+
+    def execute_model(self, *a, **kw):
+        out = orig_exec(self, *a, **kw)
+        _after_step()
+        return out
+
+    GPUModelRunner.execute_model = execute_model
+
+
+def register() -> None:
+    """vLLM general-plugin entry point (and the in-process hook): patch vLLM once, when SDCGUARD_B200=1."""
+    if os.environ.get(ENV, "0") != "1" or _REGISTERED[0]:
+        return
+    _define_op()
+    _patch()
+    _REGISTERED[0] = True
+    log.info("sdcguard_b200: vLLM linear layers will run on the checked GEMM")
