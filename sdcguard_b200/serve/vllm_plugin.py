@@ -90,6 +90,14 @@ def _adopt(layer: torch.nn.Module) -> None:
     from .settings import layer_selected
     w = getattr(layer, "weight", None)
     name = _layer_name(layer)
+    lid = getattr(layer, "_sdcguard_b200_id", None)
+    if lid is not None:                 # weights loaded again: new checksums, same state row
+        name0, _, slot, dev, add_bias = _LAYERS[lid]
+        bias = getattr(layer, "bias", None) if add_bias else None
+        cw = gemm.CheckedWeight(w.detach(), None if bias is None else bias.detach())
+        _STATE[dev].slot_weights[slot] = cw
+        _LAYERS[lid] = (name0, cw, slot, dev, add_bias)
+        return
     with _LOCK:
         i = _COUNTER[0]
         _COUNTER[0] += 1
