@@ -1304,7 +1304,7 @@ static int gemm_run(const void* A, long long lda, const void* W, const void* Wc,
   p.n_per_m = p.n_main + p.n_cs;
   p.m_tiles = (M + BM - 1) / BM;
   // CTA pairs (256 x 256 tiles, cta_group::2): for outputs with at least two bands and enough tiles to fill the
-  // GPU with pairs; not with push or split-K (decode-sized outputs)
+  // GPU with pairs, or a long K that split-K spreads over them; not with push, nor for decode-sized split-K
   if (grp != nullptr && (push != nullptr || grp->experts < 1 || N % CSW || bias != nullptr || grp->gband == nullptr ||
                          grp->gcount == nullptr))
     return -1;
@@ -1380,11 +1380,33 @@ static int gemm_run(const void* A, long long lda, const void* W, const void* Wc,
   // splitting pays when each CTA would stream a long K (measured: K = 1024 is faster unsplit)
   int split_min_k, split_force;
   split_policy(&split_min_k, &split_force);
-  const int split_k_min = split_decode(M, N) ? split_min_k : kLongK;
-  if (!pair && allow_split && push == nullptr && grp == nullptr && split_eligible(M, N) && K >= split_k_min &&
-      max_ctas == 0 && dbg == nullptr) {
+  const bool decode = split_decode(M, N);
+  const int split_k_min = decode ? split_min_k : kLongK;
+  // CTA pairs split too when K is long (the training dW GEMMs: a 256 x 256 pair tile streams half the operand bytes
+  // per FLOP of a 128 x 128 tile, and the split fills the GPU with pairs)
+  if ((!pair || K >= kLongK) && allow_split && push == nullptr && grp == nullptr && split_eligible(M, N) &&
+      K >= split_k_min && max_ctas == 0 && dbg == nullptr) {
     const int kblocks = (K + BK - 1) / BK;
-    int sp = split_force > 0 ? split_force : num_sms_cached() / p.total_tiles;
+    const int cap_sp = kMaxSplit < kblocks / 4 ? kMaxSplit : kblocks / 4;
+    int sp;
+    if (split_force > 0) {
+      sp = split_force;
+    } else if (decode && !pair) {
+      sp = num_sms_cached() / p.total_tiles;
+    } else {
+      // long K: the split count whose waves of (tile, split) units are best balanced over the resident CTAs (or
+      // pairs): time ~ ceil(tiles * s / slots) / s in units of one whole-K tile; ties go to fewer splits
+      const int slots = pair ? pair_max_clusters() : num_sms_cached();
+      sp = 1;
+      double best = 1.0 * ((p.total_tiles + slots - 1) / slots);
+      for (int s2 = 2; s2 <= cap_sp; ++s2) {
+        const double c = static_cast<double>((static_cast<long long>(p.total_tiles) * s2 + slots - 1) / slots) / s2;
+        if (c < best * 0.97) {
+          best = c;
+          sp = s2;
+        }
+      }
+    }
     sp = sp > kMaxSplit ? kMaxSplit : sp;
     sp = sp > kblocks / 4 ? kblocks / 4 : sp;
     if (sp >= 2) {

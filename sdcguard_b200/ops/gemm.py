@@ -401,8 +401,15 @@ def row_sqnorm(x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Ten
     return out
 
 
-def pick_bn(m: int, n: int, num_sms: int = 148) -> int:
-    """256-wide tiles when there are enough of them to fill the GPU, else 128."""
+LONG_K = 8192
+
+
+def pick_bn(m: int, n: int, num_sms: int = 148, k: int = 0) -> int:
+    """256-wide tiles when there are enough of them to fill the GPU, else 128. With a long K (the training dW GEMMs,
+    K = tokens) 256-wide CTA-pair tiles whenever there are two bands: split-K spreads them over the GPU, and a pair
+    tile streams half the operand bytes per FLOP of a 128 x 128 one."""
+    if k >= LONG_K and m > 128:
+        return 256
     tiles256 = -(-m // 128) * -(-n // 256)
     return 256 if tiles256 >= num_sms * 0.75 else 128
 
@@ -432,7 +439,7 @@ def checked_linear(x: torch.Tensor, cw: CheckedWeight, state: torch.Tensor, slot
     ws = workspace(dev, int(lib.sdc_gemm_ws_bytes(m, cw.n)))
     err = error_word(dev)
     if bn is None:
-        bn = pick_bn(m, cw.n)
+        bn = pick_bn(m, cw.n, k=k)
     s = cw.mask
     inj_row, inj_col, inj_xor = (-1, -1, 0) if inject is None else (int(inject[0]), int(inject[1]), int(inject[2]))
     rc = lib.sdc_gemm_bf16(

@@ -84,7 +84,7 @@ def bench_gemm(m, n, k, iters, bn=None):
     mc = _timed(lambda: torch.matmul(x, w.t(), out=out), iters)
     r = st.read()[0]
     fl = 2.0 * m * n * k
-    return {"kernel": "checked_gemm", "m": m, "n": n, "k": k, "bn": bn or gemm.pick_bn(m, n), "us": round(ms * 1e3, 1),
+    return {"kernel": "checked_gemm", "m": m, "n": n, "k": k, "bn": bn or gemm.pick_bn(m, n, k=k), "us": round(ms * 1e3, 1),
             "tflops": round(fl / ms / 1e9, 1), "cublas_us": round(mc * 1e3, 1),
             "cublas_tflops": round(fl / mc / 1e9, 1), "worst_clean_z": round(r["z"], 4), "checks": r["checks"]}
 

@@ -136,9 +136,11 @@ def test_split_k_odd_block_counts(m, n, k):
     assert gemm.error_word(dev).item() == 0
 
 
-@pytest.mark.parametrize("m,n,k", [(768, 768, 16384), (384, 3072, 8192)])
+@pytest.mark.parametrize("m,n,k", [(768, 768, 16384), (384, 3072, 8192), (2304, 768, 16384), (3072, 768, 16384),
+                                   (768, 3072, 16384), (1000, 768, 8192), (640, 256, 8192)])
 def test_split_k_long_k_few_tiles(m, n, k):
-    """Long-K GEMMs with few output tiles (training dW shapes) split over K too: same output and check as unsplit."""
+    """Long-K GEMMs with few output tiles (training dW shapes) run as 256 x 256 CTA-pair tiles split over K (odd band
+    counts and a ragged last band included): same output and check as unsplit."""
     from sdcguard_b200.ops import gemm
     torch.manual_seed(6)
     dev = torch.device("cuda")
@@ -150,7 +152,11 @@ def test_split_k_long_k_few_tiles(m, n, k):
     y = gemm.checked_linear(x, cw, st.state, s0)
     ref = x.double() @ w.double().t()
     assert float((y.double() - ref).abs().max()) <= 2 ** -7 * float(ref.abs().max()) + 1e-3
+    assert gemm.pick_bn(m, n, k=k) == 256
+    y128 = gemm.checked_linear(x, cw, st.state, s0, bn=128)          # 128-wide tiles, no pairs
+    assert float((y128.double() - ref).abs().max()) <= 2 ** -7 * float(ref.abs().max()) + 1e-3
     gemm.checked_linear(x, cw, st.state, s1, inject=(m // 2, n // 3, 1 << 29))
     rows = st.read()
-    assert rows[0]["z"] < 2.0 and rows[0]["unjudged"] == 0, rows[0]
+    assert rows[0]["z"] < 2.0 and rows[0]["unjudged"] == 0 and rows[0]["checks"] == 2, rows[0]
     assert rows[1]["z"] > abft.Z_ALARM and rows[1]["row"] == m // 2 and rows[1]["block"] == (n // 3) // 128
+    assert gemm.error_word(dev).item() == 0
