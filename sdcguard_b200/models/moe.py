@@ -8,6 +8,9 @@ library's kernels, expert-parallel over the ranks or with every expert on this G
     h      = grouped checked GEMM  rows @ W13_e^T    ABFT, all local experts in one launch (rows of each expert
     a      = silu(h_gate) * h_up                     start on a 128-row band; band -> expert table on the device)
     y_e    = grouped checked GEMM  a @ W2_e^T        ABFT, one launch
+    (precision "fp8": before each expert GEMM the grouped rows are quantized to E4M3 with 1 x 128 power-of-two
+    scales, a rotating sample of rows replayed exactly; the expert GEMMs are the grouped block-scaled fp8 checked
+    GEMM on 128 x 128-scaled E4M3 expert weights)
     y      = combine(y_e, w)                         sealed transfer back ("own"), weighted sum in fp32, k order
 
 Nothing in a checked layer reads back to the host: the band table and band count the grouped GEMMs need are written
@@ -48,12 +51,15 @@ def router_weight(seed: int, experts: int, hidden: int, device) -> torch.Tensor:
 class MoELayer:
     def __init__(self, hidden: int, inter: int, experts: int, top_k: int, comm: Optional[EPComm], device,
                  checked: bool = True, seed: int = 0, state: Optional[gemm.StateTable] = None, name: str = "moe",
-                 collective: str = "own"):
+                 collective: str = "own", precision: str = "bf16"):
         """collective "own": the sealed peer-memory all-to-all (needs comm); "local": every expert on this GPU,
         rows grouped on the device (no all-to-all, comm unused); "nccl": the unchecked baseline exchange over
-        torch.distributed (comm may be None)."""
+        torch.distributed (comm may be None). precision "fp8" (checked only): block-scaled fp8 expert GEMMs."""
         if collective not in ("own", "local", "nccl"):
             raise ValueError(f"collective {collective!r}: own, local or nccl")
+        if precision not in ("bf16", "fp8") or (precision == "fp8" and not checked):
+            raise ValueError("precision must be bf16, or fp8 with checked=True")
+        self.precision = precision
         self.H, self.I, self.E, self.k = hidden, inter, experts, top_k
         self.comm = comm
         self.collective = collective
@@ -80,6 +86,12 @@ class MoELayer:
         self.name = name
         if checked:
             self.cw_r = gemm.CheckedWeight(self.router)
+        if checked and precision == "fp8":
+            from ..ops import fp8 as fp8_ops
+            self.f13 = fp8_ops.Fp8WeightStack(self.w13)
+            self.f2 = fp8_ops.Fp8WeightStack(self.w2)
+            self._qturn = 0
+        elif checked:
             self.s13 = gemm.CheckedWeightStack(self.w13)
             self.s2 = gemm.CheckedWeightStack(self.w2)
             # the per-expert weights become views of the stacks (one copy of the expert weights in memory)
@@ -99,6 +111,12 @@ class MoELayer:
             return
         self.slots["router"] = table.add(f"{name}.router (ABFT GEMM)", self.cw_r.nb)
         self.slots["route"] = table.add(f"{name}.route (replay)", 1)
+        if self.precision == "fp8":
+            self.slots["up"] = table.add(f"{name}.experts.gate_up (ABFT fp8 GEMM)", self.f13.nb)
+            self.slots["down"] = table.add(f"{name}.experts.down (ABFT fp8 GEMM)", self.f2.nb)
+            self.slots["up.q"] = table.add(f"{name}.experts.gate_up.quant (replay)", 1)
+            self.slots["down.q"] = table.add(f"{name}.experts.down.quant (replay)", 1)
+            return
         self.slots["up"] = table.add(f"{name}.experts.gate_up (ABFT GEMM)", self.s13.nb)
         self.slots["down"] = table.add(f"{name}.experts.down (ABFT GEMM)", self.s2.nb)
 
@@ -132,10 +150,10 @@ class MoELayer:
         if self.collective == "local":
             grp = self._grouping_for(x.shape[0])
             xg, rsq = grp.group(x, ids)
-            yg = self._experts_grouped(xg, rsq, grp.gband, grp.gcount)
+            yg = self._experts_grouped(xg, rsq, grp.gband, grp.gcount, x.shape[0] * self.k)
             return grp.combine(yg, wts)
         xg, rsq, gband, gcount = self.comm.dispatch_grouped(x, ids)
-        yg = self._experts_grouped(xg, rsq, gband, gcount)
+        yg = self._experts_grouped(xg, rsq, gband, gcount, x.shape[0] * self.k // max(1, self.world))
         return self.comm.combine(yg, wts)
 
     def _grouping_for(self, T: int) -> moe_ops.Grouping:
@@ -152,18 +170,45 @@ class MoELayer:
                      act=torch.empty(cap, self.I, dtype=bf, device=dev),
                      act_sq=torch.empty(cap, dtype=torch.float32, device=dev),
                      y=torch.empty(cap, self.H, dtype=bf, device=dev))
+            if self.precision == "fp8":
+                from ..ops import fp8 as fp8_ops
+                b.update(qx=_fp8_act(fp8_ops, cap, self.H, dev), qa=_fp8_act(fp8_ops, cap, self.I, dev))
         return b
 
-    def _experts_grouped(self, xg, rsq, gband, gcount):
+    def _quant_sample(self, rows_valid: int) -> torch.Tensor:
+        """A rotating sample of grouped rows to replay the quantization of: rows below T k lie in bands in use."""
+        n = max(1, min(8, rows_valid))
+        self._qturn += 1
+        r = (torch.arange(n, dtype=torch.int64) * 131 + self._qturn * 8) % max(1, rows_valid)
+        return r.to(torch.int32).to(self.device, non_blocking=True)
+
+    def _experts_grouped(self, xg, rsq, gband, gcount, rows_valid: int = 0):
         """Both expert GEMMs of every local expert as two grouped checked launches (and SwiGLU between)."""
         cap = xg.shape[0]
         b = self._buffers(cap)
         st = self.state.state
+        if self.precision == "fp8":
+            return self._experts_grouped_fp8(xg, gband, gcount, rows_valid, b, st)
         h = gemm.checked_linear_grouped(xg, self.s13, gband, gcount, st, self.slots["up"], row_sq=rsq,
                                         out=b["h"][:cap], inject=self._take("up"))
         act, asq = layers.silu_mul_bands(h, gcount, out=b["act"][:cap], row_sq=b["act_sq"][:cap])
         return gemm.checked_linear_grouped(act, self.s2, gband, gcount, st, self.slots["down"], row_sq=asq,
                                            out=b["y"][:cap], inject=self._take("down"))
+
+    def _experts_grouped_fp8(self, xg, gband, gcount, rows_valid, b, st):
+        from ..ops import fp8 as fp8_ops
+        cap = xg.shape[0]
+        qx = fp8_ops.quantize_act(xg, out=_fp8_view(b["qx"], cap))
+        if rows_valid > 0:
+            fp8_ops.quantize_act(xg, out=qx, rows=self._quant_sample(rows_valid), check=st[self.slots["up.q"]])
+        h = fp8_ops.checked_linear_fp8_grouped(qx, self.f13, gband, gcount, st, self.slots["up"], out=b["h"][:cap],
+                                               inject=self._take("up"))
+        act, _ = layers.silu_mul_bands(h, gcount, out=b["act"][:cap], row_sq=b["act_sq"][:cap])
+        qa = fp8_ops.quantize_act(act, out=_fp8_view(b["qa"], cap))
+        if rows_valid > 0:
+            fp8_ops.quantize_act(act, out=qa, rows=self._quant_sample(rows_valid), check=st[self.slots["down.q"]])
+        return fp8_ops.checked_linear_fp8_grouped(qa, self.f2, gband, gcount, st, self.slots["down"],
+                                                  out=b["y"][:cap], inject=self._take("down"))
 
     def _experts_unchecked(self, xe, offs_host):
         """Baseline expert MLPs: PyTorch's grouped GEMM when it runs here, else one cuBLAS GEMM per expert."""
@@ -234,6 +279,18 @@ class MoELayer:
         y = torch.zeros(T, self.H, dtype=torch.float32, device=dev)
         y.index_add_(0, order // K, ret.float() * wts.view(-1)[order].unsqueeze(1))
         return y.to(torch.bfloat16)
+
+
+def _fp8_act(fp8_ops, cap: int, k: int, dev):
+    return fp8_ops.Fp8Act(torch.empty(cap, k, dtype=torch.float8_e4m3fn, device=dev),
+                          torch.empty(cap, k // 128, dtype=torch.float32, device=dev),
+                          torch.empty(cap, dtype=torch.float32, device=dev),
+                          torch.full((-(-cap // 128), k // 128, 512), 127, dtype=torch.uint8, device=dev))
+
+
+def _fp8_view(a, rows: int):
+    """The first `rows` rows of an activation buffer (scale-factor chunks by whole 128-row tiles)."""
+    return type(a)(a.q[:rows], a.sa[:rows], a.row_sq[:rows], a.sf[: -(-rows // 128)])
 
 
 def reference_moe(x: torch.Tensor, seed: int, hidden: int, inter: int, experts: int, top_k: int,

@@ -69,7 +69,7 @@ class EPComm:
         self.counts = torch.zeros(self.world * self.epr, dtype=torch.int32, device=dev)
         self.plan = torch.empty(max_tokens * top_k, 2, dtype=torch.int32, device=dev)
         grows = rows + self.epr * 128          # the grouped layout pads each expert to whole 128-row bands
-        self.recv = torch.empty(grows, hidden, dtype=torch.bfloat16, device=dev)
+        self.recv = torch.zeros(grows, hidden, dtype=torch.bfloat16, device=dev)   # rows past the bands in use stay finite
         self.map = torch.empty(grows, dtype=torch.int32, device=dev)
         self.row_sq = torch.zeros(grows, dtype=torch.float32, device=dev)
         self.gband = torch.zeros(grows // 128 + 1, dtype=torch.int32, device=dev)

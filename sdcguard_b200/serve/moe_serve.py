@@ -67,12 +67,16 @@ def _timed(fn, steps, world):
     return _max(a.elapsed_time(b) / steps, world), _max(wall, world)
 
 
-def build(cfg, arm, comm, rank, world, dev, seed):
+def build(cfg, arm, comm, rank, world, dev, seed, precision: str = "bf16"):
+    """precision "fp8" (checked arm): block-scaled fp8 expert GEMMs and attention projections; the unchecked
+    baseline stays bf16 (PyTorch's grouped GEMM and cuBLAS)."""
     checked = arm == "checked"
+    prec = precision if checked else "bf16"
     moe = [MoELayer(cfg.hidden, cfg.intermediate, 8, 2, comm if checked else None, dev, checked=checked,
-                    seed=seed * 1000 + i, collective="own" if checked else "nccl", name=f"layers.{i}.moe")
+                    seed=seed * 1000 + i, collective="own" if checked else "nccl", name=f"layers.{i}.moe",
+                    precision=prec)
            for i in range(cfg.layers)]
-    return CheckedDecoder(cfg, dev, checked=checked, seed=seed, moe_layers=moe), moe
+    return CheckedDecoder(cfg, dev, checked=checked, seed=seed, moe_layers=moe, precision=prec), moe
 
 
 def campaign(eng, model, moe, comm, rank, world, trials, seed, dev):
@@ -151,7 +155,7 @@ def run(args) -> dict:
     comm = EPComm(heap, T_local, cfg.hidden, 8, 2)
     res: dict = {"world": world}
     for arm in args.arms.split(","):
-        model, moe = build(cfg, arm, comm, rank, world, dev, args.seed)
+        model, moe = build(cfg, arm, comm, rank, world, dev, args.seed, getattr(args, "precision", "bf16"))
         eng = LLMEngine(cfg, dev, model=model, num_blocks=pages, max_prefill_tokens=T_local, max_num_seqs=nseq,
                         cuda_graph=False, max_model_len=lens[0] + args.new_tokens)
 
@@ -181,7 +185,9 @@ def run(args) -> dict:
         res["overhead_pct"] = round(100 * (res["checked"]["dev_ms"] / res["unchecked"]["dev_ms"] - 1), 2)
     comm.close()
     res["config"] = {"model": cfg.name, "layers": cfg.layers, "ep": world, "tokens_per_step": args.tokens,
-                     "seq": lens[0], "new_tokens": args.new_tokens, "dtype": "bf16", "steps": args.steps,
+                     "seq": lens[0], "new_tokens": args.new_tokens,
+                     "dtype": ("fp8 block-scaled (checked arm), bf16 baseline" if getattr(args, "precision", "bf16") == "fp8"
+                               else "bf16"), "steps": args.steps,
                      "warmup": args.warmup}
     return res
 
@@ -198,6 +204,8 @@ def main(argv=None) -> int:
     ap.add_argument("--trials", type=int, default=8)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--pg-timeout", type=int, default=300)
+    ap.add_argument("--precision", default="bf16", choices=["bf16", "fp8"],
+                    help="fp8: block-scaled fp8 expert GEMMs and projections in the checked arm")
     a = ap.parse_args(argv)
     res = run(a)
     if int(os.environ.get("RANK", "0")) == 0:

@@ -113,3 +113,29 @@ def test_moe_layer_local_and_graph():
     assert torch.equal(yg, y2)
     layer.state.read(reset=True)
     del graph
+
+
+def test_moe_layer_fp8_experts():
+    """Block-scaled fp8 expert GEMMs: the layer against the fp32 reference within fp8's rounding, clean checks and
+    quantization replays, and an injected accumulator flip in the gate/up GEMM found at its grouped row."""
+    from sdcguard_b200.models.moe import MoELayer, reference_moe
+    dev = torch.device("cuda")
+    T, Hm, Im, Em, Km = 96, 512, 256, 8, 2
+    layer = MoELayer(Hm, Im, Em, Km, None, dev, checked=True, seed=5, collective="local", precision="fp8")
+    g = torch.Generator(device=dev).manual_seed(9)
+    x = torch.randn(T, Hm, device=dev, generator=g).bfloat16()
+    y = layer.forward(x)
+    torch.cuda.synchronize()
+    ref, _ = reference_moe(x, 5, Hm, Im, Em, Km, layer.last_ids, layer.last_wts)
+    err = float((y.float() - ref).norm() / ref.norm())
+    assert err < 0.08, err
+    rows = {r["name"]: r for r in layer.state.read(reset=True)}
+    assert all(r["z"] < 6 and r["unjudged"] == 0 for r in rows.values()), rows
+    assert sum(r["checks"] for n, r in rows.items() if "fp8 GEMM" in n) == 2
+    assert sum(r["checks"] for n, r in rows.items() if ".quant" in n) > 0
+    layer.inject_next("up", 5, 200, 29)
+    layer.forward(x)
+    torch.cuda.synchronize()
+    rows = {r["name"]: r for r in layer.state.read(reset=True)}
+    up = [r for n, r in rows.items() if "gate_up (ABFT fp8" in n][0]
+    assert up["z"] > 6 and up["row"] == 5 and up["block"] == 200 // 128, up
