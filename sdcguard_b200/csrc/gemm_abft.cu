@@ -108,7 +108,7 @@ struct Params {
   int* err;
   int inj_row, inj_col;
   uint32_t inj_xor;
-  unsigned long long* dbg;   // optional per-CTA timers (null: off): [cta][8]
+  unsigned long long* dbg;   // optional per-CTA timers (null: off): [cta][kDbgSlots]
   uint32_t* seal;            // optional [M][nb] hash of the stored bf16 bits of each (row, block) (null: off)
   Push push;
   int ksplit;                // K splits (1: the fused epilogue; > 1: partial accumulators + reduce kernel)
@@ -376,6 +376,10 @@ __device__ __forceinline__ uint32_t pick24(const uint32_t (&a)[8], const uint32_
 // bf16 output (and its seal), and judges the block against the checksum columns (summed the same way) with the
 // fused epilogue's judge. One state update per CTA.
 constexpr int kMaxSplitDev = 8;   // most splits a launch uses (kMaxSplit on the host)
+// Debug timer record per CTA (gemm-timeline): 0 waiting for accumulators, 1 epilogue, 2 tiles, 3 output-tile body,
+// 4 judge, 5 CTA start, 6 CTA end, 7 output tiles' TMEM-load waits, 8 staging-buffer waits (the previous TMA store's
+// read), 9 judge-input prefetch, 10 bias / sums / packing, 11 staging stores and TMA store issue.
+constexpr int kDbgSlots = 16;
 
 template <bool INJ>
 __global__ void __launch_bounds__(256) split_reduce_kernel(const Params p) {
@@ -509,7 +513,7 @@ __global__ void __launch_bounds__(Cfg<BN, PAIR>::THREADS, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  if (p.dbg && threadIdx.x == 0) p.dbg[blockIdx.x * 8 + 5] = globaltimer();
+  if (p.dbg && threadIdx.x == 0) p.dbg[blockIdx.x * kDbgSlots + 5] = globaltimer();
   // pair mode: both CTAs of a cluster walk the same tiles; this CTA holds band 2 mt + prank of pair-band mt
   const uint32_t prank = PAIR ? cluster_ctarank() : 0u;
   const int t_first = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
@@ -848,7 +852,9 @@ __global__ void __launch_bounds__(Cfg<BN, PAIR>::THREADS, 1)
       }
       tc_fence_after();
       const uint32_t tacc = tmem_base + static_cast<uint32_t>(acc * BN) + lane_off;
+      const unsigned long long t_jp = p.dbg ? globaltimer() : 0ull;
       judge_prefetch(p, ctl, pend, abort_flag);   // the previous tile's judge inputs load during this tile's body
+      if (p.dbg && et == 0) p.dbg[blockIdx.x * kDbgSlots + 9] += globaltimer() - t_jp;
       // this warp is done reading the accumulator (each thread fenced its TMEM loads before the warp sync; pair
       // mode: the MMA and its barrier are in the first CTA). One arrival per warp: arrivals on one barrier
       // serialise, remote ones most of all.
@@ -974,9 +980,12 @@ __global__ void __launch_bounds__(Cfg<BN, PAIR>::THREADS, 1)
             uint32_t r[64];
             uint32_t (&ra)[32] = *reinterpret_cast<uint32_t(*)[32]>(&r[0]);
             uint32_t (&rb)[32] = *reinterpret_cast<uint32_t(*)[32]>(&r[32]);
+            const unsigned long long t_l0 = p.dbg ? globaltimer() : 0ull;
             tmem_ld32(tacc + static_cast<uint32_t>(g * CSW + h * 64), ra);
             tmem_ld32(tacc + static_cast<uint32_t>(g * CSW + h * 64 + 32), rb);
             tmem_wait_ld();
+            const unsigned long long t_l1 = p.dbg ? globaltimer() : 0ull;
+            if (p.dbg && et == 0) p.dbg[blockIdx.x * kDbgSlots + 7] += t_l1 - t_l0;
             const int cbase = col0 + h * 64;
             const uint32_t sg0 = p.sgn[2 * h], sg1 = p.sgn[2 * h + 1];
             if (p.bias != nullptr) {
@@ -1003,10 +1012,14 @@ __global__ void __launch_bounds__(Cfg<BN, PAIR>::THREADS, 1)
 #pragma unroll
               for (int j = 0; j < 32; ++j) seal += seal_term(packed[j], static_cast<uint32_t>(h * 32 + j));
             }
+            const unsigned long long t_s0 = p.dbg ? globaltimer() : 0ull;
+            if (p.dbg && et == 0) p.dbg[blockIdx.x * kDbgSlots + 10] += t_s0 - t_l1;
             // the store that last used this staging tile must have read it before we overwrite it (with two tiles
             // per warp, the store of the other half may still be reading)
             if (lane == 0) bulk_wait_read<C::STG_BUFS - 1>();
             __syncwarp();
+            const unsigned long long t_s1 = p.dbg ? globaltimer() : 0ull;
+            if (p.dbg && et == 0) p.dbg[blockIdx.x * kDbgSlots + 8] += t_s1 - t_s0;
             uint8_t* myrow = stg + lane * 128;
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
@@ -1025,6 +1038,7 @@ __global__ void __launch_bounds__(Cfg<BN, PAIR>::THREADS, 1)
               }
               bulk_commit();
             }
+            if (p.dbg && et == 0) p.dbg[blockIdx.x * kDbgSlots + 11] += globaltimer() - t_s1;
           }
           if (p.push.on && row < p.M) {
             const int owner = row / p.push.R;
@@ -1039,7 +1053,7 @@ __global__ void __launch_bounds__(Cfg<BN, PAIR>::THREADS, 1)
         const unsigned long long t_e0 = p.dbg ? globaltimer() : 0ull;
         judge_pending<C::NWG>(p, ctl, pend, ew, lane, abort_flag);
         if (p.dbg && et == 0) {
-          unsigned long long* d = p.dbg + blockIdx.x * 8;
+          unsigned long long* d = p.dbg + blockIdx.x * kDbgSlots;
           d[3] += t_e0 - t_w1;            // output tile: TMEM -> registers -> staging -> TMA store issued
           d[4] += globaltimer() - t_e0;   // judging the previous output tile (including its wait)
         }
@@ -1056,7 +1070,7 @@ __global__ void __launch_bounds__(Cfg<BN, PAIR>::THREADS, 1)
         pend.A = Aab;
       }
       if (p.dbg && et == 0) {
-        unsigned long long* d = p.dbg + blockIdx.x * 8;
+        unsigned long long* d = p.dbg + blockIdx.x * kDbgSlots;
         d[0] += t_w1 - t_w0;          // waiting for the accumulator
         d[1] += globaltimer() - t_w1; // epilogue body (including the wait for expected sums)
         d[2] += 1;                    // tiles
@@ -1096,7 +1110,7 @@ __global__ void __launch_bounds__(Cfg<BN, PAIR>::THREADS, 1)
         asm volatile("st.release.sys.global.b64 [%0], %1;" ::"l"(p.push.flag_peer[r] + p.push.rank), "l"(g) : "memory");
     }
   }
-  if (p.dbg && threadIdx.x == 0) p.dbg[blockIdx.x * 8 + 6] = globaltimer();
+  if (p.dbg && threadIdx.x == 0) p.dbg[blockIdx.x * kDbgSlots + 6] = globaltimer();
 }
 
 // ------------------------------------------------------------------------------------------- host side

@@ -89,6 +89,9 @@ def bench_gemm(m, n, k, iters, bn=None):
             "cublas_tflops": round(fl / mc / 1e9, 1), "worst_clean_z": round(r["z"], 4), "checks": r["checks"]}
 
 
+DBG_SLOTS = 16     # per-CTA debug timer record of the checked GEMM (kDbgSlots in csrc/gemm_abft.cu)
+
+
 def gemm_timeline(m, n, k, iters, bn=None):
     """Where a checked GEMM's time goes inside the kernel, from its per-CTA global-timer records (the kernel's
     debug timers: CTA start and end, time waiting for each accumulator, epilogue time, output-tile body, judge).
@@ -106,7 +109,7 @@ def gemm_timeline(m, n, k, iters, bn=None):
     rs = gemm.row_sqnorm(x)
     out = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
     nsm = torch.cuda.get_device_properties(dev).multi_processor_count
-    dbg = torch.zeros(nsm * 8, dtype=torch.int64, device=dev)
+    dbg = torch.zeros(nsm * DBG_SLOTS, dtype=torch.int64, device=dev)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.int8, device=dev)
     for _ in range(3):
         gemm.checked_linear(x, cw, st.state, s, row_sq=rs, out=out, bn=bn)
@@ -117,7 +120,7 @@ def gemm_timeline(m, n, k, iters, bn=None):
         torch.cuda.synchronize()
         gemm.checked_linear(x, cw, st.state, s, row_sq=rs, out=out, bn=bn, dbg=dbg)
         torch.cuda.synchronize()
-        d = dbg.view(nsm, 8).cpu()
+        d = dbg.view(nsm, DBG_SLOTS).cpu()
         d = d[d[:, 6] > 0]
         t0 = int(d[:, 5].min())
         runs.append({"ctas": int(d.shape[0]), "end_max_us": (int(d[:, 6].max()) - t0) / 1e3,
@@ -126,7 +129,12 @@ def gemm_timeline(m, n, k, iters, bn=None):
                      "wait_accumulator_us": float(d[:, 0].double().mean()) / 1e3,
                      "epilogue_us": float(d[:, 1].double().mean()) / 1e3,
                      "output_body_us": float(d[:, 3].double().mean()) / 1e3,
-                     "judge_us": float(d[:, 4].double().mean()) / 1e3})
+                     "judge_us": float(d[:, 4].double().mean()) / 1e3,
+                     "body_tmem_load_wait_us": float(d[:, 7].double().mean()) / 1e3,
+                     "body_staging_wait_us": float(d[:, 8].double().mean()) / 1e3,
+                     "body_judge_prefetch_us": float(d[:, 9].double().mean()) / 1e3,
+                     "body_sums_pack_us": float(d[:, 10].double().mean()) / 1e3,
+                     "body_stage_store_us": float(d[:, 11].double().mean()) / 1e3})
     runs.sort(key=lambda r: r["end_max_us"])
     r = runs[len(runs) // 2]
     return {"kernel": "checked_gemm_timeline", "m": m, "n": n, "k": k,
