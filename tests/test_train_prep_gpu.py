@@ -67,7 +67,7 @@ def test_prep_scratch_is_left_zero():
             assert torch.allclose(gemm.CheckedWeight.on_device(w).cs.wstat, f, rtol=1e-5, atol=0)
             t = gemm.CheckedWeight.of_transpose(w)
             assert torch.allclose(t.cs.wstat, abft.weight_checksums(w.t().contiguous()).wstat, rtol=1e-4, atol=1e-6)
-    acc = gemm._PREP_ACC[dev]
+    acc = gemm._PREP_ACC[ws[0].device]
     torch.cuda.synchronize()
     assert int((acc != 0).sum()) == 0
 
