@@ -160,3 +160,16 @@ def test_split_k_long_k_few_tiles(m, n, k):
     assert rows[0]["z"] < 2.0 and rows[0]["unjudged"] == 0 and rows[0]["checks"] == 2, rows[0]
     assert rows[1]["z"] > abft.Z_ALARM and rows[1]["row"] == m // 2 and rows[1]["block"] == (n // 3) // 128
     assert gemm.error_word(dev).item() == 0
+
+
+@pytest.mark.parametrize("m,k", [(5, 64), (300, 1000), (64, 4096), (768, 16384), (3, 20000), (2304, 16383)])
+def test_row_sqnorm_matches_reference(m, k):
+    """Row sums of squares (warp per row for short rows, a CTA per row for long ones, a ragged tail) against fp64."""
+    from sdcguard_b200.ops import gemm
+    dev = torch.device("cuda")
+    kk = -(-k // 8) * 8
+    base = torch.randn(m, kk, device=dev).to(torch.bfloat16)
+    x = base[:, :k]                                   # row stride a multiple of 8, odd width allowed
+    r = gemm.row_sqnorm(x)
+    ref = x.double().pow(2).sum(1)
+    assert float(((r.double() - ref).abs() / ref).max()) < 1e-4
