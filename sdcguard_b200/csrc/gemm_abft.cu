@@ -309,7 +309,7 @@ __device__ __forceinline__ void judge_pair(const Params& p, int row, int b, floa
 struct Pending {
   bool live;        // a tile waits to be judged
   bool valid;       // this thread has a (row, block) pair in it
-  bool pre;         // judge_prefetch ran: ready and the loaded values below are set
+  int stage;        // 0: nothing loaded; 1: ws, bs, rsq loaded; 2: ready known and ex loaded too
   bool ready;       // the band's expected sums were published (the coordinator did not give up)
   int acc;          // accumulator slot and its phase when the tile was taken
   uint32_t phase;
@@ -320,19 +320,35 @@ struct Pending {
   float rsq;        // row sum of squares
 };
 
-// Wait (bounded) for the pending tile's expected sums and issue the judge's loads, early in the next tile's
-// epilogue so that their latency overlaps its body.
+// Early in the next tile's epilogue: issue the judge's loads that do not depend on other CTAs (block statistics,
+// bias sums, row norm), and the expected sums too if the coordinator has already published them (a non-blocking
+// test: the band's checksum tiles run on other CTAs and may still be running; the judge waits for them then, after
+// this tile's body, instead of holding the body up).
 __device__ __forceinline__ void judge_prefetch(const Params& p, SmemCtl* ctl, Pending& pd, volatile int* abort_flag) {
-  if (!pd.live || pd.pre) return;
-  pd.pre = true;
-  // the coordinator has waited (bounded) for the band's expected sums; skip judging if it gave up
-  pd.ready = mbar_wait(&ctl->ready[pd.acc], pd.phase, abort_flag) && ctl->ready_ok[pd.acc] != 0;
-  if (pd.valid && pd.ready) {
-    pd.ex = __ldcg(p.expd + static_cast<long long>(pd.row) * p.nb + pd.b);
-    pd.ws = __ldg(p.wstat + pd.b + (p.gband != nullptr ? __ldcg(p.gband + pd.row / BM) * p.nb : 0));
-    pd.bs = p.bsum != nullptr ? __ldg(p.bsum + pd.b) : make_float2(0.f, 0.f);
-    pd.rsq = __ldg(p.row_sq + pd.row);
+  if (!pd.live || pd.stage == 2) return;
+  if (pd.stage == 0) {
+    pd.stage = 1;
+    if (pd.valid) {
+      pd.ws = __ldg(p.wstat + pd.b + (p.gband != nullptr ? __ldcg(p.gband + pd.row / BM) * p.nb : 0));
+      pd.bs = p.bsum != nullptr ? __ldg(p.bsum + pd.b) : make_float2(0.f, 0.f);
+      pd.rsq = __ldg(p.row_sq + pd.row);
+    }
   }
+  if (mbar_poll(&ctl->ready[pd.acc], pd.phase)) {
+    pd.stage = 2;
+    pd.ready = ctl->ready_ok[pd.acc] != 0;
+    if (pd.valid && pd.ready) pd.ex = __ldcg(p.expd + static_cast<long long>(pd.row) * p.nb + pd.b);
+  }
+}
+
+// Before judging: everything judge_prefetch has not loaded, waiting (bounded) for the band's expected sums; skips
+// judging when the coordinator gave up on them.
+__device__ __forceinline__ void judge_inputs(const Params& p, SmemCtl* ctl, Pending& pd, volatile int* abort_flag) {
+  judge_prefetch(p, ctl, pd, abort_flag);
+  if (pd.stage == 2) return;
+  pd.stage = 2;
+  pd.ready = mbar_wait(&ctl->ready[pd.acc], pd.phase, abort_flag) && ctl->ready_ok[pd.acc] != 0;
+  if (pd.valid && pd.ready) pd.ex = __ldcg(p.expd + static_cast<long long>(pd.row) * p.nb + pd.b);
 }
 
 // Judge the pending output tile of this warp (if any) and hand the warp's worst keys to the coordinator: wait
@@ -342,7 +358,7 @@ template <int NWG>
 __device__ __forceinline__ void judge_pending(const Params& p, SmemCtl* ctl, Pending& pd, int ew, int lane,
                                               volatile int* abort_flag) {
   if (!pd.live) return;
-  judge_prefetch(p, ctl, pd, abort_flag);
+  judge_inputs(p, ctl, pd, abort_flag);
   pd.live = false;
   unsigned long long k0 = 0ull, k1 = 0ull;
   int unj = 0;
@@ -1058,7 +1074,7 @@ __global__ void __launch_bounds__(Cfg<BN, PAIR>::THREADS, 1)
           d[4] += globaltimer() - t_e0;   // judging the previous output tile (including its wait)
         }
         pend.live = true;
-        pend.pre = false;
+        pend.stage = 0;
         pend.valid = have && row < p.M;
         pend.acc = acc;
         pend.phase = acc_phase;
