@@ -24,6 +24,7 @@
     sdcguard inventory / overhead / model-ref                client batch join, matched-run overhead, model file binding
     sdcguard assignment / forward-inputs / regression        recorded page assignment, forward inputs, saved case
     sdcguard train-bench / kernel-bench / calibrate          training cost, kernel timings, noise-model calibration
+    sdcguard vllm-bench                                      vLLM with this package's plugin against vLLM alone
     sdcguard nvsentinel RESULT|ALERTS.jsonl [--dry-run]      health events for NVIDIA NVSentinel
     sdcguard version
 
@@ -110,6 +111,7 @@ COMMANDS = {
     "train-bench": _lazy(".tools.train_bench", "main"),
     "nvsentinel": _lazy(".utils.nvsentinel", "main"),
     "kernel-bench": _lazy(".tools.kernel_bench", "main"),
+    "vllm-bench": _lazy(".tools.vllm_bench", "main"),
     "calibrate": _lazy(".tools.calibrate", "main"),
     "version": _version,
 }
