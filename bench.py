@@ -48,6 +48,7 @@ def parse():
     ap.add_argument("--no-unchecked", action="store_true", help="skip the unchecked comparison run")
     ap.add_argument("--no-campaign", action="store_true", help="skip the fault-injection campaign")
     ap.add_argument("--no-tp", action="store_true", help="skip the tensor-parallel block (config 4 at TP = N)")
+    ap.add_argument("--no-tp-fp8", action="store_true", help="skip the block-scaled fp8 arm of the TP block")
     ap.add_argument("--tp-steps", type=int, default=1)
     ap.add_argument("--tp-batch", type=int, default=64)
     ap.add_argument("--tp-prompt", type=int, default=2048)
@@ -244,7 +245,22 @@ def run_tp(args, world: int) -> dict:
                          profile_kernels=True)
     r = tp_serve.run(targs)
     c, u = r.get("checked", {}), r.get("unchecked", {})
-    return {"config": r.get("config"), "tp": world,
+    fp8 = None
+    if not args.no_tp_fp8:
+        # config 4 in block-scaled fp8: the checked arm again with the four projections on the fp8 checked GEMM
+        # (1 x 128 activation and 128 x 128 weight scales), against the same bf16 unchecked arm
+        try:
+            f = tp_serve.run(ap.Namespace(**{**vars(targs), "arms": "checked", "precision": "fp8",
+                                             "profile_kernels": False})).get("checked", {})
+            fp8 = {"checked": round(f.get("tokens_per_s", 0.0), 1),
+                   "overhead_pct_vs_bf16_unchecked": (round(100.0 * (u["tokens_per_s"] / f["tokens_per_s"] - 1.0), 2)
+                                                      if f.get("tokens_per_s") and u.get("tokens_per_s") else None),
+                   "ms_per_step": round(f.get("dev_ms", 0.0), 2), "checks": f.get("checks"),
+                   "unjudged": f.get("unjudged"), "false_alarms": f.get("false_alarms"),
+                   "injected_transfer_flip_detected_on_ranks": f.get("injected_transfer_flip_detected_on_ranks")}
+        except Exception as e:  # noqa: BLE001  (the bf16 TP numbers stand; the fp8 arm reports its error)
+            fp8 = {"error": f"{type(e).__name__}: {str(e)[:300]}"}
+    return {"config": r.get("config"), "tp": world, "fp8": fp8,
             "checked": round(c.get("tokens_per_s", 0.0), 1),
             "unchecked": round(u.get("tokens_per_s", 0.0), 1), "overhead_pct": r.get("overhead_pct"),
             "unit": "tokens/s (prompt + generated, whole job; device time max over ranks)",
