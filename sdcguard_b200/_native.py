@@ -59,6 +59,7 @@ F = c_float
 # name -> (restype, argtypes)
 SIGNATURES: dict[str, tuple] = {
     "sdc_gemm_ws_bytes": (L, [I, I]),
+    "sdc_gemm_choose_split": (I, [I, I, I, I, I]),
     "sdc_gemm_counter_bytes": (L, []),
     "sdc_gemm_set_capture": (I, [P]),
     "sdc_gemm_capture_bytes": (L, []),

@@ -1270,6 +1270,35 @@ static bool split_eligible(int M, int N) {
          static_cast<long long>(kMaxSplit) * M * part_stride(N, static_cast<int>(nb)) * 4 <= kSplitMaxPartBytes;
 }
 
+// The split-K count of a launch: `tiles` output tiles (pair tiles in pair mode), `slots` CTAs (or pairs) resident
+// at once, `kblocks` 64-wide K blocks. Decode-sized outputs on single CTAs: as many splits as fill the SMs once.
+// Long K: the count whose waves of (tile, split) units are best balanced over the slots, time ~ ceil(tiles s /
+// slots) / s in units of one whole-K tile, a split taken only when it gains 3 %. At most kMaxSplit splits and a
+// quarter of the K blocks; a forced count (SDCGUARD_GEMM_SPLIT) within the same limits. Pure host arithmetic.
+extern "C" int sdc_gemm_choose_split(int tiles, int slots, int kblocks, int decode_single, int force) {
+  if (tiles <= 0 || slots <= 0) return 1;
+  const int cap_sp = kMaxSplit < kblocks / 4 ? kMaxSplit : kblocks / 4;
+  int sp;
+  if (force > 0) {
+    sp = force;
+  } else if (decode_single) {
+    sp = slots / tiles;
+  } else {
+    sp = 1;
+    double best = 1.0 * ((tiles + slots - 1) / slots);
+    for (int s2 = 2; s2 <= cap_sp; ++s2) {
+      const double c = static_cast<double>((static_cast<long long>(tiles) * s2 + slots - 1) / slots) / s2;
+      if (c < best * 0.97) {
+        best = c;
+        sp = s2;
+      }
+    }
+  }
+  sp = sp > kMaxSplit ? kMaxSplit : sp;
+  sp = sp > kblocks / 4 ? kblocks / 4 : sp;
+  return sp < 1 ? 1 : sp;
+}
+
 // CTA-pair clusters of the 256-wide pair kernel that can be resident at once (0: pair mode unavailable).
 int sdc_gemm_pair_clusters() { return pair_max_clusters(); }
 
@@ -1417,28 +1446,8 @@ static int gemm_run(const void* A, long long lda, const void* W, const void* Wc,
   if ((!pair || K >= kLongK) && allow_split && push == nullptr && grp == nullptr && split_eligible(M, N) &&
       K >= split_k_min && max_ctas == 0 && dbg == nullptr) {
     const int kblocks = (K + BK - 1) / BK;
-    const int cap_sp = kMaxSplit < kblocks / 4 ? kMaxSplit : kblocks / 4;
-    int sp;
-    if (split_force > 0) {
-      sp = split_force;
-    } else if (decode && !pair) {
-      sp = num_sms_cached() / p.total_tiles;
-    } else {
-      // long K: the split count whose waves of (tile, split) units are best balanced over the resident CTAs (or
-      // pairs): time ~ ceil(tiles * s / slots) / s in units of one whole-K tile; ties go to fewer splits
-      const int slots = pair ? pair_max_clusters() : num_sms_cached();
-      sp = 1;
-      double best = 1.0 * ((p.total_tiles + slots - 1) / slots);
-      for (int s2 = 2; s2 <= cap_sp; ++s2) {
-        const double c = static_cast<double>((static_cast<long long>(p.total_tiles) * s2 + slots - 1) / slots) / s2;
-        if (c < best * 0.97) {
-          best = c;
-          sp = s2;
-        }
-      }
-    }
-    sp = sp > kMaxSplit ? kMaxSplit : sp;
-    sp = sp > kblocks / 4 ? kblocks / 4 : sp;
+    const int slots = pair ? pair_max_clusters() : num_sms_cached();
+    const int sp = sdc_gemm_choose_split(p.total_tiles, slots, kblocks, decode && !pair ? 1 : 0, split_force);
     if (sp >= 2) {
       p.kb_per = (kblocks + sp - 1) / sp;
       p.ksplit = (kblocks + p.kb_per - 1) / p.kb_per;     // no empty split
