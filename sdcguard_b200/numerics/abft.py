@@ -233,7 +233,7 @@ def locate(flat: int, nb: int) -> tuple[int, int, bool]:
 
 def product_zscores(a: torch.Tensor, b: torch.Tensor, c: torch.Tensor, mask: tuple,
                     rnd_unit: float = 0.0, judged: Optional[torch.Tensor] = None,
-                    z_alarm: float = Z_ALARM) -> torch.Tensor:
+                    z_alarm: float = Z_ALARM, return_den: bool = False):
     """Scores of batched products c ~ a @ b made by another library (cuBLAS, CPU BLAS), in float64 torch ops:
     a (G, m, k), b (G, k, n), c (G, m, n) the product as the library returned it (already freed of any bias,
     alpha and beta). Returns (G, m, nb) scores, the larger of plain and signed; inf = corruption, -1 = not judged.
@@ -243,7 +243,8 @@ def product_zscores(a: torch.Tensor, b: torch.Tensor, c: torch.Tensor, mask: tup
     rounded to a narrower type (rnd_unit = its unit roundoff, 2^-8 for bf16), each element may differ from the
     accumulator by up to rnd_unit |c| with a sign that varies from element to element: the statistical bound grows by
     rnd_unit ||c_b||_2 and the worst-case bound of the plain sum by 1.25 rnd_unit ||c_b||_1. judged: optional (G, m, nb) bool,
-    False where the inputs themselves hold non-finite values (a product block that is then not scored).
+    False where the inputs themselves hold non-finite values (a product block that is then not scored). With
+    return_den, also the (G, m, nb) noise scale each score divides by.
     Reference: src/sdcguard/checksum.py (`matmul_zscores` on the rounded output, `matmul_zscores_acc` on the
     accumulator)."""
     G, m, k = a.shape
@@ -281,4 +282,5 @@ def product_zscores(a: torch.Tensor, b: torch.Tensor, c: torch.Tensor, mask: tup
     bad = ~fin_act & fin_exp & ok
     z = torch.where(bad & (bound < BIG), torch.full_like(z, math.inf), z)
     z = torch.where((bad & ~(bound < BIG)) | ~fin_exp | ~ok, torch.full_like(z, -1.0), z)
-    return torch.where(torch.isnan(z), torch.full_like(z, -1.0), z)
+    z = torch.where(torch.isnan(z), torch.full_like(z, -1.0), z)
+    return (z, den) if return_den else z

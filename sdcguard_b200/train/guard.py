@@ -36,6 +36,15 @@ from ..utils.events import EventLog, SDCEvent, device_identity
 PHASES = ("fwd", "dx", "dw")
 
 
+class SDCError(RuntimeError):
+    """Raised at the read-back of a checked step when the guard was built with raise_on_alert=True and a check
+    found corruption; .events holds the step's alerts."""
+
+    def __init__(self, message: str, events: Optional[list] = None):
+        super().__init__(message)
+        self.events = events or []
+
+
 class _Cache:
     """Checksum data of one weight, built once per checked step (and again if the weight changes within the step):
     the optimizer changes weights between steps, and fused optimizers (AdamW(fused=True)) do so without bumping the
@@ -197,7 +206,7 @@ class SDCGuard:
     def __init__(self, check_every: int = 1, z_alarm: float = abft.Z_ALARM, device=None,
                  log: Optional[EventLog] = None, on_alert=None, replicas: bool = False, replica_group=None,
                  recompute: bool = False, exact_reductions: bool = True, keep_evidence: bool = True,
-                 evidence_dir: Optional[str] = None, confirm_runs: int = 20):
+                 evidence_dir: Optional[str] = None, confirm_runs: int = 20, raise_on_alert: bool = False):
         """replicas: after each checked step every rank shares (a multiple of check_every, an after_restart()
         window), compare the protected model's weight fingerprints across the data-parallel ranks (a collective).
         recompute: blocks run through guard.checkpoint() are fingerprinted in the forward and in the backward
@@ -205,8 +214,10 @@ class SDCGuard:
         attention's among them) keep their split-K partial sums in fp32. keep_evidence: the operands of each
         checked GEMM of a step are kept until the step's check is read, so an alarm comes with its input row,
         a float64 recheck and `confirm_runs` replays of the flagged block on this GPU; evidence_dir: each such
-        alarm is also saved there (torch.save, loadable with weights_only=True)."""
+        alarm is also saved there (torch.save, loadable with weights_only=True). raise_on_alert: the read-back of
+        a checked step that found corruption raises SDCError (after logging and evidence)."""
         self.check_every = max(1, int(check_every))
+        self.raise_on_alert = raise_on_alert
         self.epoch = 0                      # checked steps begun: the checksum caches are per checked step
         self.replicas, self.replica_group = replicas, replica_group
         self.exact_reductions = exact_reductions
@@ -413,6 +424,9 @@ class SDCGuard:
         self.events += new
         if new and self.device.type == "cuda" and self.keep_evidence:
             self._evidence(new, step)
+        if new and self.raise_on_alert:
+            where = ", ".join(sorted({str(e.detail.get("layer", e.detector)) for e in new})[:4])
+            raise SDCError(f"sdcguard: {len(new)} alert(s) at step {step}: {where}", new)
         return new
 
     def _evidence(self, new: list, step) -> None:
