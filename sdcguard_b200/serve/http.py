@@ -225,60 +225,22 @@ class Server:
 
     def metrics(self) -> str:
         from .. import __version__
+        from .metrics import render, settings_labels
         g = self.eng.guard
-        cov = g.coverage_report()
         dev = torch.device(self.eng.device)
         if dev.type == "cuda":
             props = torch.cuda.get_device_properties(dev)
             gpu, uuid = props.name, str(getattr(props, "uuid", ""))
         else:
             gpu, uuid = "cpu", ""
-        c = self.counters
         stack = {"model": self.model_name, "precision": getattr(self.eng.model, "precision", "bf16"),
                  "checked": str(self.eng.checked).lower(), "torch": torch.__version__, "cuda": torch.version.cuda,
                  "weights_digest": self.digest, "version": __version__}
-        lab = ",".join(f'{k}="{v}"' for k, v in stack.items())
-        st = getattr(self.eng.model, "settings", None)
-        prot = dict(st.describe()) if st is not None else {}
-        prot.pop("notes", None)
-        prot["z"] = prot.pop("z_alarm", g.z_alarm)
-        prot["weight_scan"] = str(self.scan is not None).lower()
-        plab = ",".join(f'{k}="{str(v).lower() if isinstance(v, bool) else v}"' for k, v in prot.items())
-        cc = self.eng.model.check_coverage() if self.eng.checked else {
-            "layers_checked": 0, "layers_unchecked": 0, "fp8_layers_checked": 0, "weights_checked_ratio": 0.0}
-        lines = [
-            "# TYPE sdcguard_protected gauge", f"sdcguard_protected {1 if self.eng.checked else 0}",
-            "# TYPE sdcguard_checks_total counter", f"sdcguard_checks_total {cov['checks']}",
-            f"sdcguard_alarms_total {cov['alarms']}", f"sdcguard_unjudged_total {cov['unjudged']}",
-            f"sdcguard_ops_total {cov['ops']}", f"sdcguard_ops_checked {cov['ops_checked']}",
-            f"sdcguard_sampled_ops_total {cov['sampled_ops']}", f"sdcguard_sampled_ops_run {cov['sampled_ops_run']}",
-            f"sdcguard_alarm_line {g.z_alarm}", f"sdcguard_worst_clean_z {cov['worst_clean_z']}",
-            f"sdcguard_polls_total {c['polls']}", f"sdcguard_requests_total {c['requests']}",
-            f"sdcguard_prompt_tokens_total {c['prompt_tokens']}",
-            f"sdcguard_generated_tokens_total {c['generated_tokens']}",
-            f"sdcguard_longest_prompt_tokens {c['longest_prompt']}",
-            f"sdcguard_layers_checked {cc['layers_checked']}", f"sdcguard_layers_unchecked {cc['layers_unchecked']}",
-            f"sdcguard_weights_checked_ratio {cc['weights_checked_ratio']:.6f}",
-            f"sdcguard_fp8_layers_checked {cc['fp8_layers_checked']}",
-            f"sdcguard_fp8_calls_judged_total {cov['fp8_calls_judged']}",
-            f"sdcguard_fp8_findings_total {cov['fp8_findings']}",
-            f"sdcguard_alerts_total {cov['alerts']}", f"sdcguard_confirmed_alerts_total {cov['confirmed_alerts']}",
-            f'sdcguard_worker_info{{gpu="{gpu}",uuid="{uuid}",pid="{os.getpid()}",'
-            f'started="{int(self.started)}",device="{dev}"}} 1',
-            f"sdcguard_stack_info{{{lab}}} 1",
-            f"sdcguard_protection_info{{{plab}}} 1",
-        ]
-        if self.scan is not None:
-            ws = self.scan.stats()
-            lines += [f"sdcguard_weight_scan_entries {ws['entries']}",
-                      f"sdcguard_weight_scan_passes_total {ws['passes']}",
-                      f"sdcguard_weight_scan_never_compared {ws['never_compared']}",
-                      f"sdcguard_weight_scan_changed {ws['changed']}",
-                      f"sdcguard_weight_repairs_total {ws['repairs']}",
-                      f"sdcguard_weight_scan_left_out {ws['left_out']}"]
-            if ws["oldest_age_seconds"] is not None:
-                lines.append(f"sdcguard_weight_scan_oldest_age_seconds {ws['oldest_age_seconds']:.3f}")
-        return "\n".join(lines) + "\n"
+        worker = {"gpu": gpu, "uuid": uuid, "pid": os.getpid(), "started": int(self.started), "device": dev}
+        cc = self.eng.model.check_coverage() if self.eng.checked else None
+        return render(g.coverage_report(), cc, self.counters, worker, stack,
+                      settings_labels(getattr(self.eng.model, "settings", None), g.z_alarm, self.scan is not None),
+                      g.z_alarm, self.scan.stats() if self.scan is not None else None, protected=self.eng.checked)
 
     def status(self) -> dict:
         with self.lock:

@@ -17,7 +17,12 @@ Off unless SDCGUARD_B200=1 (vLLM loads every installed plugin). In each vLLM pro
     reports the previous one, as `ServeGuard.poll(wait=False)`), alarms are logged as `sdcguard ALERT` lines and
     appended to SDCGUARD_LOG as JSON events;
   - `coverage()` gives the layers checked and left out, with the reason, and the share of linear-layer weights
-    checked. Layers left out (other dtypes, quantized methods, the LM head, outside the share) run vLLM's own GEMM.
+    checked. Layers left out (other dtypes, quantized methods, the LM head, outside the share) run vLLM's own GEMM;
+  - with SDCGUARD_METRICS_PORT, each worker publishes the protection metrics of `serve.metrics` on that port plus
+    its local rank (GET /metrics), so `sdcguard ready`, `decide` and `qualify` judge a running `vllm serve`; its token
+    counter counts the tokens the worker computed;
+  - with SDCGUARD_REQUIRE (1: every layer the share selects; a fraction such as 0.9: that share of them), the first
+    model step refuses to serve (RuntimeError) when fewer are checked, or when none is.
 
 The reference's plugin (SDCGUARD=1) keeps vLLM's GEMM and adds a Triton check after it; here the check is part of
 the GEMM, so a checked layer is still one launch. Differences in rounding order from cuBLAS's GEMM are in the last
@@ -40,7 +45,10 @@ log = logging.getLogger("sdcguard_b200")
 ENV = "SDCGUARD_B200"
 _STATE: dict = {}          # device -> DeviceState
 _LAYERS: list = []         # layer id -> (name, CheckedWeight, slot, device)
-_LEFT_OUT: list = []       # (name, reason)
+_LEFT_OUT: list = []       # (name, reason, weight elements)
+_COUNTERS = {"polls": 0, "requests": 0, "prompt_tokens": 0, "generated_tokens": 0, "longest_prompt": 0, "steps": 0}
+_EXPORTER: list = []
+_STARTED = [0.0]
 _LOCK = threading.Lock()
 _REGISTERED = [False]
 _COUNTER = [0]             # linear layers seen (selection index)
@@ -58,6 +66,7 @@ class DeviceState:
         self.steps = 0
         self.guard = None
         gemm.enable_capture(device)
+        _start_exporter(device)
 
 
 def _max_tokens() -> int:
@@ -115,7 +124,7 @@ def _adopt(layer: torch.nn.Module) -> None:
         if not layer_selected(i, st.settings.share, st.settings.offset):
             why = f"outside the share {st.settings.share:g}"
     if why is not None:
-        _LEFT_OUT.append((name, why))
+        _LEFT_OUT.append((name, why, int(w.numel()) if isinstance(w, torch.Tensor) else 0))
         return
     bias = getattr(layer, "bias", None)
     add_bias = bias is not None and not getattr(layer, "skip_bias_add", False)
@@ -171,20 +180,104 @@ def _poll(dev: torch.device, wait: bool = False) -> list:
     return events
 
 
-def _after_step() -> None:
+def require_ok(checked: int, left_out: list, value: Optional[str]) -> Optional[str]:
+    """Why SDCGUARD_REQUIRE refuses (None: it does not). Layers left out by the share count as not selected."""
+    if not value:
+        return None
+    try:
+        need = float(value)
+    except ValueError:
+        return f"SDCGUARD_REQUIRE={value!r} is not 1 or a fraction"
+    selected_out = [r for r in left_out if not r[1].startswith("outside the share")]
+    total = checked + len(selected_out)
+    if checked == 0:
+        return "no linear layer is checked"
+    share = checked / total
+    if share + 1e-12 < min(1.0, need):
+        reasons: dict = {}
+        for r in selected_out:
+            reasons[r[1].split(":")[0]] = reasons.get(r[1].split(":")[0], 0) + 1
+        return (f"{checked} of {total} selected linear layers are checked ({share:.1%}), SDCGUARD_REQUIRE={value}; "
+                f"left out: {reasons}")
+    return None
+
+
+def _after_step(scheduler_output=None) -> None:
     every = max(1, int(os.environ.get("SDCGUARD_POLL_EVERY", "16")))
+    _COUNTERS["steps"] += 1
+    if _COUNTERS["steps"] == 1:
+        why = require_ok(len(_LAYERS), _LEFT_OUT, os.environ.get("SDCGUARD_REQUIRE"))
+        if why is not None:
+            raise RuntimeError(f"sdcguard_b200: refusing to serve: {why}")
+    if scheduler_output is not None:
+        n = getattr(scheduler_output, "total_num_scheduled_tokens", 0) or 0
+        per = getattr(scheduler_output, "num_scheduled_tokens", None) or {}
+        _COUNTERS["generated_tokens"] += int(n)
+        _COUNTERS["requests"] += len(per)
+        if per:
+            _COUNTERS["longest_prompt"] = max(_COUNTERS["longest_prompt"], max(int(v) for v in per.values()))
     for dev, st in list(_STATE.items()):
         st.steps += 1
         if st.steps % every == 0:
             _poll(dev)
+            _COUNTERS["polls"] += 1
+
+
+def _check_coverage() -> dict:
+    checked = sum(cw.n * cw.k for _, cw, _, _, _ in _LAYERS)
+    left = sum(r[2] for r in _LEFT_OUT)
+    return {"layers_checked": len(_LAYERS), "layers_unchecked": len(_LEFT_OUT), "fp8_layers_checked": 0,
+            "weights_checked_ratio": checked / (checked + left) if checked + left else 0.0}
+
+
+def metrics_text(dev: torch.device) -> str:
+    """The protection metrics of this worker (the device's state as of its last poll)."""
+    from .. import __version__
+    from .metrics import render, settings_labels
+    st = _STATE.get(dev)
+    cov = st.guard.coverage_report() if st is not None and st.guard is not None else {}
+    props = torch.cuda.get_device_properties(dev) if dev.type == "cuda" else None
+    worker = {"gpu": props.name if props else "cpu", "uuid": str(getattr(props, "uuid", "")) if props else "",
+              "pid": os.getpid(), "started": int(_STARTED[0]), "device": dev}
+    model = ""
+    try:
+        from vllm.config import get_current_vllm_config_or_none
+        cfg = get_current_vllm_config_or_none()
+        model = cfg.model_config.model if cfg is not None and cfg.model_config is not None else ""
+    except Exception:  # noqa: BLE001  (no vLLM config readable: the model name stays empty)
+        pass
+    try:
+        import vllm
+        vllm_version = vllm.__version__
+    except Exception:  # noqa: BLE001
+        vllm_version = ""
+    stack = {"model": model, "precision": "bf16", "checked": "true", "torch": torch.__version__,
+             "cuda": torch.version.cuda, "weights_digest": "", "version": __version__, "engine": f"vllm {vllm_version}"}
+    settings = st.settings if st is not None else None
+    z = settings.z_alarm if settings is not None else 6.0
+    counters = dict(_COUNTERS, polls=_COUNTERS["polls"])
+    return render(cov, _check_coverage(), counters, worker, stack, settings_labels(settings, z, False), z)
+
+
+def _start_exporter(dev: torch.device) -> None:
+    port = os.environ.get("SDCGUARD_METRICS_PORT")
+    if not port or _EXPORTER:
+        return
+    import time as _time
+    from .metrics import Exporter
+    _STARTED[0] = _time.time()
+    rank = int(os.environ.get("LOCAL_RANK", dev.index if dev.index is not None else 0))
+    _EXPORTER.append(Exporter(int(port) + rank, lambda: metrics_text(dev)))
+    log.info("sdcguard_b200: protection metrics on port %d", int(port) + rank)
 
 
 def coverage() -> dict:
     """Layers checked, layers left out (with reasons), the share of linear-layer weight elements checked, and the
     serving guard's counts per device (after a final blocking read)."""
     checked_el = sum(cw.n * cw.k for _, cw, _, _, _ in _LAYERS)
-    out = {"layers_checked": len(_LAYERS), "layers_left_out": len(_LEFT_OUT), "left_out": _LEFT_OUT[:64],
-           "checked_weight_elements": checked_el, "devices": {}}
+    out = {"layers_checked": len(_LAYERS), "layers_left_out": len(_LEFT_OUT),
+           "left_out": [(n, r) for n, r, _ in _LEFT_OUT[:64]], "checked_weight_elements": checked_el,
+           "weights_checked_ratio": _check_coverage()["weights_checked_ratio"], "devices": {}}
     for dev, st in _STATE.items():
         _poll(dev, wait=True)
         out["devices"][str(dev)] = st.guard.coverage_report()
@@ -201,7 +294,9 @@ def _patch() -> None:
         try:
             _adopt(layer)
         except Exception as e:  # noqa: BLE001  (a layer that cannot be adopted runs vLLM's GEMM, counted)
-            _LEFT_OUT.append((_layer_name(layer), f"not adopted: {type(e).__name__}: {e}"[:200]))
+            w = getattr(layer, "weight", None)
+            _LEFT_OUT.append((_layer_name(layer), f"not adopted: {type(e).__name__}: {e}"[:200],
+                              int(w.numel()) if isinstance(w, torch.Tensor) else 0))
 
     def apply(self, layer, x, bias=None):
         lid = getattr(layer, "_sdcguard_b200_id", None)
@@ -220,7 +315,7 @@ def _patch() -> None:
 
     def execute_model(self, *a, **kw):
         out = orig_exec(self, *a, **kw)
-        _after_step()
+        _after_step(a[0] if a else kw.get("scheduler_output"))
         return out
 
     GPUModelRunner.execute_model = execute_model

@@ -68,7 +68,12 @@ def child(a) -> None:
            "tokens_per_step": sum(lens) + a.requests * a.new_tokens, "first_tokens": first}
     if a.child == "checked":
         from ..serve import vllm_plugin
+        from . import _client
         res["coverage"] = vllm_plugin.coverage()
+        m = _client.parse_metrics(vllm_plugin.metrics_text(torch.device("cuda", torch.cuda.current_device())))
+        res["metrics"] = {k: m.get(k) for k in ("sdcguard_checks_total", "sdcguard_alarms_total",
+                                                "sdcguard_layers_checked", "sdcguard_weights_checked_ratio",
+                                                "sdcguard_polls_total", "sdcguard_generated_tokens_total")}
     print("VLLMRESULT " + json.dumps(res, default=str), flush=True)
 
 
@@ -116,7 +121,8 @@ def main(argv=None) -> int:
            "layers_checked": cov.get("layers_checked"), "layers_left_out": cov.get("layers_left_out"),
            "checks": sum(d.get("checks", 0) for d in devs), "alarms": sum(d.get("alarms", 0) for d in devs),
            "unjudged": sum(d.get("unjudged", 0) for d in devs),
-           "same_first_tokens": arms["checked"]["first_tokens"] == arms["unchecked"]["first_tokens"]}
+           "same_first_tokens": arms["checked"]["first_tokens"] == arms["unchecked"]["first_tokens"],
+           "worker_metrics": arms["checked"].get("metrics")}
     print(json.dumps(out))
     return 0
 

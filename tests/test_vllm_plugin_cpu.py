@@ -37,10 +37,31 @@ def test_patched_and_falls_back_on_cpu(plugin):
     m = ULM()
     m.process_weights_after_loading(layer)
     assert not hasattr(layer, "_sdcguard_b200_id")
-    assert ("model.layers.0.mlp.down_proj", "not on a CUDA device") in vp._LEFT_OUT
+    assert ("model.layers.0.mlp.down_proj", "not on a CUDA device", 64 * 32) in vp._LEFT_OUT
     x = torch.randn(5, 32, dtype=torch.bfloat16)
     torch.testing.assert_close(m.apply(layer, x), torch.nn.functional.linear(x, layer.weight))
     fake = vp._linear_fake(x, layer.weight, None, 0)
     assert fake.shape == (5, 64)
     cov = vp.coverage()
     assert cov["layers_checked"] == 0 and cov["layers_left_out"] >= 1
+
+
+def test_require_and_metrics_exporter(plugin):
+    """SDCGUARD_REQUIRE's rule, and the per-worker exporter serving the protection metrics `ready` reads."""
+    vp, _, _ = plugin
+    assert vp.require_ok(3, [], None) is None
+    assert vp.require_ok(3, [("a", "outside the share 0.5", 10)], "1") is None      # not selected: fine
+    assert "3 of 4" in vp.require_ok(3, [("a", "weight torch.float32 (2, 2)", 4)], "1")
+    assert vp.require_ok(3, [("a", "weight x", 4)], "0.7") is None
+    assert vp.require_ok(0, [], "0.1") == "no linear layer is checked"
+    from sdcguard_b200.serve.metrics import Exporter
+    from sdcguard_b200.tools import _client
+    ex = Exporter(0, lambda: vp.metrics_text(torch.device("cpu")), host="127.0.0.1")
+    try:
+        m = _client.scrape(f"http://127.0.0.1:{ex.port}")
+        assert m["sdcguard_protected"] == 1 and "sdcguard_layers_checked" in m and "sdcguard_alarm_line" in m
+        info = m["sdcguard_stack_info{}"][0][0]
+        assert info["engine"].startswith("vllm") and info["checked"] == "true"
+        assert m["sdcguard_worker_info{}"][0][0]["gpu"] == "cpu"
+    finally:
+        ex.close()

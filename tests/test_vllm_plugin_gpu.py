@@ -21,3 +21,6 @@ def test_vllm_plugin_small_load(tmp_path):
     assert r["layers_checked"] == 28 * 4, r
     assert r["checks"] > 0 and r["alarms"] == 0 and r["unjudged"] == 0, r
     assert r["checked_tokens_per_s"] > 0 and r["unchecked_tokens_per_s"] > 0
+    wm = r["worker_metrics"]                  # what the worker's metrics exporter would publish
+    assert wm["sdcguard_layers_checked"] == 112 and wm["sdcguard_checks_total"] > 0
+    assert wm["sdcguard_generated_tokens_total"] > 0 and wm["sdcguard_alarms_total"] == 0
