@@ -14,8 +14,9 @@ Off unless SDCGUARD_B200=1 (vLLM loads every installed plugin). In each vLLM pro
     and its CUDA graphs capture the kernel; the GEMM workspace is sized before capture for every batch size up to
     the scheduler's largest (max_num_batched_tokens);
   - every SDCGUARD_POLL_EVERY model steps (default 16) the state table is read without stalling the GPU (the read
-    reports the previous one, as `ServeGuard.poll(wait=False)`), alarms are logged as `sdcguard ALERT` lines and
-    appended to SDCGUARD_LOG as JSON events;
+    reports the previous one, as `ServeGuard.poll(wait=False)`), and after a step that ends SDCGUARD_POLL_SECONDS
+    (default 2) or more after the last read it is read at once, waiting for the GPU; alarms are logged as
+    `sdcguard ALERT` lines and appended to SDCGUARD_LOG as JSON events;
   - `coverage()` gives the layers checked and left out, with the reason, and the share of linear-layer weights
     checked. Layers left out (other dtypes, quantized methods, the LM head, outside the share) run vLLM's own GEMM;
   - with SDCGUARD_METRICS_PORT, each worker publishes the protection metrics of `serve.metrics` on that port plus
@@ -36,6 +37,7 @@ from __future__ import annotations
 import logging
 import os
 import threading
+import time
 from typing import Optional
 
 import torch
@@ -46,7 +48,8 @@ ENV = "SDCGUARD_B200"
 _STATE: dict = {}          # device -> DeviceState
 _LAYERS: list = []         # layer id -> (name, CheckedWeight, slot, device)
 _LEFT_OUT: list = []       # (name, reason, weight elements)
-_COUNTERS = {"polls": 0, "requests": 0, "prompt_tokens": 0, "generated_tokens": 0, "longest_prompt": 0, "steps": 0}
+_COUNTERS = {"polls": 0, "requests": 0, "prompt_tokens": 0, "generated_tokens": 0, "longest_prompt": 0, "steps": 0,
+             "tokens_computed": 0}
 _EXPORTER: list = []
 _STARTED = [0.0]
 _LOCK = threading.Lock()
@@ -65,6 +68,8 @@ class DeviceState:
         self.slot_weights: dict = {}
         self.steps = 0
         self.guard = None
+        self.last_read = 0.0          # time of the last read of the state table
+        self.tokens_at_read = 0       # tokens computed when the read in flight was started
         gemm.enable_capture(device)
         _start_exporter(device)
 
@@ -212,15 +217,24 @@ def _after_step(scheduler_output=None) -> None:
     if scheduler_output is not None:
         n = getattr(scheduler_output, "total_num_scheduled_tokens", 0) or 0
         per = getattr(scheduler_output, "num_scheduled_tokens", None) or {}
-        _COUNTERS["generated_tokens"] += int(n)
+        _COUNTERS["tokens_computed"] += int(n)
         _COUNTERS["requests"] += len(per)
         if per:
             _COUNTERS["longest_prompt"] = max(_COUNTERS["longest_prompt"], max(int(v) for v in per.values()))
+    poll_seconds = float(os.environ.get("SDCGUARD_POLL_SECONDS", "2"))
+    now = time.time()
     for dev, st in list(_STATE.items()):
         st.steps += 1
-        if st.steps % every == 0:
-            _poll(dev)
+        late = now - st.last_read >= poll_seconds
+        if st.steps % every == 0 or late:
+            # a step long after the last read: read now, waiting for the GPU once, so a lightly loaded server reports
+            # within a step; otherwise the read reports the one started at the previous poll
+            _poll(dev, wait=late)
             _COUNTERS["polls"] += 1
+            # the published token counter covers what the folded read covers, so checks and tokens move together
+            _COUNTERS["generated_tokens"] = _COUNTERS["tokens_computed"] if late else st.tokens_at_read
+            st.tokens_at_read = _COUNTERS["tokens_computed"]
+            st.last_read = now
 
 
 def _check_coverage() -> dict:
@@ -280,6 +294,8 @@ def coverage() -> dict:
            "weights_checked_ratio": _check_coverage()["weights_checked_ratio"], "devices": {}}
     for dev, st in _STATE.items():
         _poll(dev, wait=True)
+        _COUNTERS["generated_tokens"] = _COUNTERS["tokens_computed"]
+        st.tokens_at_read, st.last_read = _COUNTERS["tokens_computed"], time.time()
         out["devices"][str(dev)] = st.guard.coverage_report()
     return out
 

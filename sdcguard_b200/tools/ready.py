@@ -1,6 +1,7 @@
 """Is this server's math being checked right now? Asked from outside, from its metrics.
 
     sdcguard ready http://127.0.0.1:8000 [--url http://127.0.0.1:8001 ...] [--probe] [--window 2] [--max-z 6]
+    sdcguard ready --port 9400 --workers 2 [--host 127.0.0.1] [--probe URL]     # the vLLM plugin's exporters
         [--layers N] [--min-weights 0.5] [--gpus UUID,UUID] [--qualified decision.json] [--max-age-days D]
         [--strict-conditions] [--strict-alerts] [--json]
 
@@ -228,15 +229,16 @@ def qualified(second: list, decision: dict, max_age_days: Optional[float] = None
 def check(urls, probe: bool = False, window: float = 2.0, max_z: float = 6.0, layers: Optional[int] = None,
           min_weights: Optional[float] = None, gpus: Optional[list] = None, decision: Optional[dict] = None,
           max_age_days: Optional[float] = None, strict_conditions: bool = False, strict_alerts: bool = False,
-          scrape: Callable = _client.scrape, complete: Callable = _client.complete, wait: Optional[float] = None) -> dict:
+          scrape: Callable = _client.scrape, complete: Callable = _client.complete, wait: Optional[float] = None,
+          probe_url: Optional[str] = None) -> dict:
     urls = [urls] if isinstance(urls, str) else list(urls)
     window = wait if wait is not None else window
     first = [scrape(u) for u in urls]
     t0 = time.time()
     if probe:
-        for u, m in zip(urls, first):
-            if m is None:
-                continue
+        # the server's API (one for all workers), or each worker's own URL (this package's HTTP server)
+        targets = [probe_url] if probe_url else [u for u, m in zip(urls, first) if m is not None]
+        for u in targets:
             for i in range(2):
                 try:
                     complete(u, [1 + i, 2, 3, 4], 4)
@@ -265,7 +267,13 @@ def main(argv=None) -> int:
     ap = argparse.ArgumentParser(prog="sdcguard ready", description=__doc__.split("\n\n")[0])
     ap.add_argument("url", nargs="?")
     ap.add_argument("--url", dest="urls", action="append", default=[], help="another worker (repeat)")
-    ap.add_argument("--probe", action="store_true")
+    ap.add_argument("--port", type=int, help="first worker's metrics port (SDCGUARD_METRICS_PORT of a vLLM server "
+                                            "with this package's plugin; worker i answers on port + i)")
+    ap.add_argument("--workers", type=int, default=1)
+    ap.add_argument("--host", default="127.0.0.1")
+    ap.add_argument("--probe", nargs="?", const=True, default=False, metavar="API_URL",
+                    help="send two short requests between the reads (to the worker URLs, or to API_URL when the "
+                         "metrics come from exporters)")
     ap.add_argument("--window", "--wait", type=float, default=2.0)
     ap.add_argument("--max-z", type=float, default=6.0)
     ap.add_argument("--layers", type=int)
@@ -278,15 +286,18 @@ def main(argv=None) -> int:
     ap.add_argument("--json", action="store_true")
     a = ap.parse_args(argv)
     urls = ([a.url] if a.url else []) + a.urls
+    if a.port is not None:
+        urls += [f"http://{a.host}:{a.port + i}" for i in range(max(1, a.workers))]
     if not urls:
-        ap.error("give at least one worker URL")
+        ap.error("give at least one worker URL (or --port)")
     dec = None
     if a.qualified:
         with open(a.qualified) as f:
             dec = json.load(f)
-    r = check(urls, a.probe, a.window, a.max_z, a.layers, a.min_weights,
+    probe_to = a.probe if isinstance(a.probe, str) else None
+    r = check(urls, bool(a.probe), a.window, a.max_z, a.layers, a.min_weights,
               [g.strip() for g in a.gpus.split(",")] if a.gpus else None, dec, a.max_age_days,
-              a.strict_conditions, a.strict_alerts)
+              a.strict_conditions, a.strict_alerts, probe_url=probe_to)
     if a.json:
         print(json.dumps(r, indent=1))
     else:
