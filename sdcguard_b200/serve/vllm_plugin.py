@@ -30,7 +30,7 @@ the GEMM, so a checked layer is still one launch. Differences in rounding order 
 bit of the bf16 outputs.
 
 Reference: src/sdcguard/vllm_plugin.py:1-80 (what the plugin checks and its settings), `register` :2239, the
-model-runner hook :2430-2501.
+model-runner hook :2430-2501 (here the GPU worker's step, which both of vLLM 0.22's model runners serve).
 """
 from __future__ import annotations
 
@@ -322,19 +322,20 @@ def _patch() -> None:
 
     UnquantizedLinearMethod.process_weights_after_loading = process_weights_after_loading
     UnquantizedLinearMethod.apply = apply
+    # the GPU worker's step (whichever model runner, V1 or V2, it was built with) gets the scheduler's output
     try:
-        from vllm.v1.worker.gpu_model_runner import GPUModelRunner
+        from vllm.v1.worker.gpu_worker import Worker
     except ImportError:
-        log.warning("sdcguard_b200: no vLLM V1 model runner to hook; results are read only by coverage()")
+        log.warning("sdcguard_b200: no vLLM GPU worker to hook; results are read only by coverage()")
         return
-    orig_exec = GPUModelRunner.execute_model
+    orig_exec = Worker.execute_model
 
     def execute_model(self, *a, **kw):
         out = orig_exec(self, *a, **kw)
         _after_step(a[0] if a else kw.get("scheduler_output"))
         return out
 
-    GPUModelRunner.execute_model = execute_model
+    Worker.execute_model = execute_model
 
 
 def register() -> None:

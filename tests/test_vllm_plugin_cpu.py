@@ -30,6 +30,8 @@ def plugin():
 def test_patched_and_falls_back_on_cpu(plugin):
     vp, ULM, before = plugin
     assert ULM.apply is not before[0] and ULM.process_weights_after_loading is not before[1]
+    from vllm.v1.worker.gpu_worker import Worker
+    assert Worker.execute_model.__name__ == "execute_model" and Worker.execute_model.__module__.endswith("vllm_plugin")
     assert hasattr(torch.ops.sdcguard_b200_vllm, "linear")
     layer = torch.nn.Module()
     layer.weight = torch.nn.Parameter(torch.randn(64, 32, dtype=torch.bfloat16), requires_grad=False)
