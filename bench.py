@@ -12,6 +12,11 @@ The JSON line also carries: the unchecked throughput of the same engine (cuBLAS 
 overhead; an end-to-end number through the public API (`LLMEngine.generate`, wall clock, pinned prompts in and
 tokens out each step); a short fault-injection campaign (single-bit flips in GEMM accumulators, KV pages and
 replayed rows) with the false alarms of the timed clean run; SM clocks sampled during the timed region.
+At N > 1 it also carries three multi-GPU blocks, each timed on the device and taken as the max over ranks: "tp"
+(the Llama-3-8B shape at TP = N, checked against cuBLAS + NCCL), and at even N "ep" (the Mixtral-8x7B shape at
+EP = N, block-scaled fp8 checked against bf16 unchecked) and "pd" (prefill on N/2 ranks, decode on N/2, KV pages
+pulled over NVLink with in-flight checksums, the coverage gate's verdict on each decode rank's recording). "ep" and
+"pd" run as jobs of their own, one process per GPU, so a failure there leaves the headline standing.
 
 --impl reference runs the unmodified reference package (installed in baseline/_ref) on its stock serving path, the
 way its own vLLM experiments run it: vLLM's offline `LLM` engine on the same Qwen3-0.6B shape (random weights,
@@ -23,8 +28,11 @@ unchecked one beside it.
 from __future__ import annotations
 
 import argparse
+import gc
 import json
 import os
+import signal
+import socket
 import statistics
 import subprocess
 import threading
@@ -32,6 +40,8 @@ import sys
 import time
 
 import torch
+
+_T0 = time.monotonic()
 
 BASELINE_VALUE = None          # no published number exists for this config
 METRIC = "checked tokens/s (prompt + generated) on Qwen3-0.6B-shaped serving, 256 req x 1024-2048 in / 128 out"
@@ -53,6 +63,14 @@ def parse():
     ap.add_argument("--tp-batch", type=int, default=64)
     ap.add_argument("--tp-prompt", type=int, default=2048)
     ap.add_argument("--tp-new-tokens", type=int, default=256)
+    ap.add_argument("--no-ep", action="store_true", help="skip the expert-parallel block (config 5 at EP = N)")
+    ap.add_argument("--no-pd", action="store_true", help="skip the prefill/decode block (config 3 at N/2 + N/2)")
+    ap.add_argument("--ep-layers", type=int, default=4)
+    ap.add_argument("--ep-steps", type=int, default=3)
+    ap.add_argument("--block-limit", type=float, default=420.0,
+                    help="seconds a multi-GPU block's processes may run before they are ended")
+    ap.add_argument("--deadline", type=float, default=690.0,
+                    help="seconds from start after which no multi-GPU block starts (each block's limit is cut to it)")
     ap.add_argument("--ref-child", choices=["checked", "unchecked"], help=argparse.SUPPRESS)
     ap.add_argument("--ref-rank", default="0", help=argparse.SUPPRESS)
     return ap.parse_args()
@@ -229,7 +247,135 @@ def run_ours(args, rank, world, local):
             res["tp"] = {"error": f"{type(e).__name__}: {str(e)[:300]}"}
     elif not args.no_tp:
         res["tp"] = {"skipped": "TP = 1 is the single-GPU engine of the headline; the block runs from N = 2"}
+    gc.collect()
+    torch.cuda.empty_cache()
+    if world > 1 and world % 2 == 0:
+        if not args.no_ep:
+            res["ep"] = run_ep(args, rank, world, local)
+        if not args.no_pd:
+            res["pd"] = run_pd(args, rank, world, local)
     return res
+
+
+# ------------------------------------------------------------------------------------------ multi-GPU blocks
+def _free_port() -> int:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def time_left(args) -> float:
+    """Seconds left before the run's deadline, as rank 0 sees it (every rank takes the same decisions)."""
+    cdev = "cuda" if torch.distributed.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([args.deadline - (time.monotonic() - _T0)], dtype=torch.float64, device=cdev)
+    torch.distributed.broadcast(t, 0)
+    return float(t.item())
+
+
+def run_child_block(name: str, module: str, argv: list, rank: int, world: int, local: int, limit_s: float) -> dict:
+    """Run one multi-GPU block as a job of its own: every rank starts one process of `module` on its GPU (a
+    torch.distributed world of its own over a fresh loopback port, NVLS off), waits for it at most limit_s
+    seconds, and the ranks agree on the outcome. A block that fails or hangs ends its processes and reports an
+    error; the headline measured before it stands. Returns rank 0's JSON result (an empty dict elsewhere)."""
+    cdev = "cuda" if torch.distributed.get_backend() == "nccl" else "cpu"     # (gloo in the CPU tests)
+    port = torch.tensor([_free_port() if rank == 0 else 0], dtype=torch.int64, device=cdev)
+    torch.distributed.broadcast(port, 0)
+    env = {k: v for k, v in os.environ.items()
+           if k not in ("GROUP_RANK", "ROLE_RANK", "ROLE_NAME", "ROLE_WORLD_SIZE", "GROUP_WORLD_SIZE")
+           and not k.startswith(("TORCHELASTIC_", "TORCH_ELASTIC_"))}
+    env.update(RANK=str(rank), WORLD_SIZE=str(world), LOCAL_RANK=str(local), LOCAL_WORLD_SIZE=str(world),
+               MASTER_ADDR="127.0.0.1", MASTER_PORT=str(int(port.item())), NCCL_NVLS_ENABLE="0",
+               PYTHONPATH=os.path.dirname(os.path.abspath(__file__)) + os.pathsep + env.get("PYTHONPATH", ""))
+    log_dir = os.environ.get("SDCGUARD_BLOCK_LOG_DIR", "/tmp")
+    os.makedirs(log_dir, exist_ok=True)
+    log_path = os.path.join(log_dir, f"sdcguard_block_{name}_{rank}.log")
+    t0 = time.perf_counter()
+    with open(log_path, "w") as log:
+        p = subprocess.Popen([sys.executable, "-m", module, *argv], env=env, stdout=subprocess.PIPE, stderr=log,
+                             text=True, start_new_session=True)
+        try:
+            out, _ = p.communicate(timeout=limit_s)
+        except subprocess.TimeoutExpired:
+            os.killpg(p.pid, signal.SIGKILL)
+            out, _ = p.communicate()
+    lines = [x for x in (out or "").splitlines() if x.startswith("{")]
+    result = None
+    if p.returncode == 0 and (rank != 0 or lines):
+        try:
+            result = json.loads(lines[-1]) if rank == 0 else {}
+        except ValueError:
+            result = None
+    ok = torch.tensor([1 if result is not None else 0], dtype=torch.int64, device=cdev)
+    torch.distributed.all_reduce(ok, op=torch.distributed.ReduceOp.MIN)
+    if int(ok.item()) == 1:
+        if rank == 0:
+            result["block_wall_s"] = round(time.perf_counter() - t0, 1)
+        return result
+    if result is None:
+        tail = open(log_path).read()[-600:].replace("\n", " | ")
+        return {"error": f"{module} on rank {rank} ended with rc {p.returncode} after "
+                         f"{time.perf_counter() - t0:.0f} s: {tail}"}
+    return {"error": "another rank's process of this block failed (its log names the cause)"}
+
+
+def run_ep(args, rank: int, world: int, local: int) -> dict:
+    """Config 5 on this job's GPUs: the Mixtral-8x7B-shaped model at EP = N (8 experts top-2 over N ranks,
+    data-parallel attention, 8192 tokens per step over the job), the checked arm in block-scaled fp8 (grouped fp8
+    checked expert GEMMs, sealed dispatch / combine all-to-all over NVLink peer memory, router and quantizer
+    replays) against the bf16 unchecked arm (PyTorch grouped GEMM, NCCL all_to_all_single), device time max over
+    ranks, plus seeded flips in expert GEMMs, dispatched and combined rows and KV pages."""
+    argv = ["--layers", str(args.ep_layers), "--tokens", "8192", "--precision", "fp8", "--steps", str(args.ep_steps),
+            "--warmup", "2", "--trials", "2", "--pg-timeout", "120"]
+    left = time_left(args)
+    if left < 150:
+        return {"skipped": f"{left:.0f} s left before the run's deadline"}
+    r = run_child_block("ep", "sdcguard_b200.serve.moe_serve", argv, rank, world, local, min(args.block_limit, left))
+    if rank != 0 or "error" in r:
+        return r
+    c, u = r.get("checked", {}), r.get("unchecked", {})
+    return {"config": r.get("config"), "ep": world, "unit": "tokens/s (whole job; device time max over ranks)",
+            "checked_fp8": c.get("tokens_per_s"), "unchecked_bf16": u.get("tokens_per_s"),
+            "overhead_pct": r.get("overhead_pct"),
+            "ms_per_step": {"checked_fp8": c.get("dev_ms"), "unchecked_bf16": u.get("dev_ms")},
+            "checks": c.get("checks"), "false_alarms": c.get("false_alarms"), "worst_clean_z": c.get("worst_clean_z"),
+            "injection": c.get("injection"), "block_wall_s": r.get("block_wall_s")}
+
+
+def run_pd(args, rank: int, world: int, local: int) -> dict:
+    """Config 3 on this job's GPUs: prefill on the first N/2 ranks, decode on the other N/2 (4 + 4 at N = 8), 160
+    requests in 8 shared-prefix groups on the Qwen3-0.6B shape, the decode ranks pulling KV pages from the producers'
+    GPU memory with the checksumming copy. Two runs: clean (cached prefixes re-verified; the gate's verdict on every
+    decode rank's recording) and with one bit flipped in a producer page (the pull must report it)."""
+    out = {"prefill_ranks": world // 2, "decode_ranks": world // 2}
+    rec_root = os.path.join(os.environ.get("SDCGUARD_BLOCK_LOG_DIR", "/tmp"), f"sdcguard_pd_{os.getpid()}")
+    if rank == 0:
+        os.makedirs(rec_root, exist_ok=True)
+    base = ["--prefill", str(world // 2), "--model", "Qwen3-0.6B", "--groups", "8", "--per-group", "20",
+            "--new-tokens", "32", "--verify-cached-prefix", "--pg-timeout", "120"]
+    for tag, extra in (("clean", ["--out", os.path.join(rec_root, "clean")]),
+                       ("flipped_page", ["--out", os.path.join(rec_root, "flip"), "--corrupt-page", "0"])):
+        left = time_left(args)
+        if left < 100:
+            out[tag] = {"skipped": f"{left:.0f} s left before the run's deadline"}
+            continue
+        r = run_child_block(f"pd_{tag}", "sdcguard_b200.serve.pd_mp", base + extra, rank, world, local,
+                            min(args.block_limit, left))
+        if rank != 0:
+            continue
+        if "error" in r:
+            out[tag] = r
+            continue
+        out[tag] = {k: r.get(k) for k in ("requests", "tokens_per_s", "device_ms", "lifetime_violations",
+                                          "ranks_with_mismatch", "kv_pull", "gate", "block_wall_s")}
+    if rank == 0:
+        clean, flip = out.get("clean", {}), out.get("flipped_page", {})
+        gates = clean.get("gate") or []
+        out["gate_pass_all_decode_ranks"] = bool(gates) and all(g.get("decision") == "PASS" for g in gates)
+        out["flip_detected"] = ((flip.get("ranks_with_mismatch") or 0) >= 1
+                                if flip and "error" not in flip and "skipped" not in flip else None)
+    return out
 
 
 def run_tp(args, world: int) -> dict:
@@ -512,8 +658,9 @@ def main():
                 line["coverage"] = res["coverage"]
                 if "campaign" in res:
                     line["detection"] = res["campaign"]
-                if "tp" in res:
-                    line["tp"] = res["tp"]
+                for k in ("tp", "ep", "pd"):
+                    if k in res:
+                        line[k] = res[k]
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()

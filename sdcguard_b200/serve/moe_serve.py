@@ -142,7 +142,7 @@ def run(args) -> dict:
     local = int(os.environ.get("LOCAL_RANK", "0"))
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    if world > 1:
+    if world > 1 and not dist.is_initialized():
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=args.pg_timeout))
     cfg = DecoderConfig(**{**MIXTRAL.__dict__, "layers": args.layers})
     T_local = args.tokens // world

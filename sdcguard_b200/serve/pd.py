@@ -211,13 +211,15 @@ def release_producer(engine: LLMEngine, transfers: Sequence[Transfer], sink=None
 
 def consume(engine: LLMEngine, transfers: Sequence[Transfer], src_cache: torch.Tensor, prefix: PrefixCache,
             rec: Recorder, max_new_tokens: int, *, verify_cached_prefix: bool = False, seed: int = kvx.DEFAULT_SEED,
-            corrupt: Optional[dict] = None, sink=None) -> torch.Tensor:
+            corrupt: Optional[dict] = None, sink=None, stats: Optional[dict] = None) -> torch.Tensor:
     """Receive every request's KV pages (reusing cached prefix pages), check them, decode. Returns generated ids
     (N, max_new_tokens) on the host. `corrupt` = {request index: page index} flips one bit in that producer page
     before the pull (fault injection: the pulled page then mismatches its checksum); only for a producer cache in
-    this process (a peer's memory is read by the copy kernel alone)."""
+    this process (a peer's memory is read by the copy kernel alone). `stats`, when given, accumulates the pulls'
+    device time ("pull_ms", CUDA events around each pull launch) and the bytes they moved ("pull_bytes")."""
     dev = engine.device
     N = len(transfers)
+    page_bytes = engine.cache[:, 0].numel() * engine.cache.element_size()     # one page over every layer
     local_pages, owned = [], []
     for i, t in enumerate(transfers):
         cached = prefix.lookup(t.token_ids)
@@ -239,8 +241,17 @@ def consume(engine: LLMEngine, transfers: Sequence[Transfer], src_cache: torch.T
         if corrupt and i in corrupt:
             pg = t.pages[corrupt[i]]
             flip_bit_in_page(src_cache, pg)
+        if stats is not None:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
         _, res = kvx.pull_pages(src_cache, engine.cache, src, dst, want, seed)
-        res = res.cpu().tolist()
+        if stats is not None:
+            e1.record()
+        res = res.cpu().tolist()                   # waits for the pull
+        if stats is not None:
+            stats["pull_ms"] = stats.get("pull_ms", 0.0) + e0.elapsed_time(e1)
+            stats["pull_bytes"] = stats.get("pull_bytes", 0) + src.numel() * page_bytes
+            stats["pulls"] = stats.get("pulls", 0) + 1
         if sink is not None:
             for j, (sp, dp) in enumerate(zip(t.pages[c:], fresh[:total - c])):
                 sink.transfer("read", "decode-pull", (t.pool, sp), ("decode", dp),

@@ -41,6 +41,31 @@ def _max(x: float, dev) -> float:
     return float(t.item())
 
 
+NVLINK_GBS = 770.0          # measured peer copy on this pool's B200s, GB/s per direction per GPU
+
+
+def _gate(d: str) -> dict:
+    """The coverage gate's verdict on one decode rank's recording (`sdcguard gate D --require checksum`)."""
+    from ..coverage import gate
+    try:
+        ans = gate.inspect(d, ["checksum"])
+    except (ValueError, OSError, KeyError, TypeError, AttributeError) as e:
+        return {"decision": "HOLD", "error": f"{type(e).__name__}: {str(e)[:200]}"}
+    reasons = sorted({x for r in ans.get("requests", []) for x in r.get("reasons", [])} | set(ans.get("hold_reasons", [])))
+    return {"decision": ans.get("decision"), "selected_requests": ans.get("selected_requests"),
+            "passed_requests": ans.get("passed_requests"), "reasons": reasons[:8]}
+
+
+def _pull_summary(rows: list) -> dict:
+    """Bytes and device time of the decode ranks' KV pulls; bandwidth per decode rank as a fraction of NVLink."""
+    per = [r["pull_bytes"] / (r["pull_ms"] * 1e6) for r in rows if r["pull_ms"] > 0]
+    return {"bytes": sum(r["pull_bytes"] for r in rows), "launches": sum(r["pulls"] for r in rows),
+            "device_ms_max": max((r["pull_ms"] for r in rows), default=0.0),
+            "gbs_per_decode_rank": [round(x, 1) for x in per],
+            "fraction_of_nvlink": round(min(per) / NVLINK_GBS, 3) if per else None,
+            "nvlink_gbs": NVLINK_GBS, "timing": "CUDA events around each pull launch on the decode rank"}
+
+
 def run(args) -> dict:
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -66,6 +91,7 @@ def run(args) -> dict:
     sink = EventSink()
     rec = pd.Recorder()
     out_tokens = None
+    rec_dir = None
     torch.cuda.synchronize(dev)
     dist.barrier()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -84,6 +110,7 @@ def run(args) -> dict:
     else:
         c = rank - P
         prefix = pd.PrefixCache()
+        pull = {}
         outs = []
         served = []
         for p in range(P):
@@ -95,7 +122,7 @@ def run(args) -> dict:
             sink.ingest(box[1])                # the producer's page allocations precede the pulls
             src_view = _wrap(buf.addr[p], shape, torch.bfloat16, dev)
             outs.append(pd.consume(eng, transfers, src_view, prefix, rec, args.new_tokens,
-                                   verify_cached_prefix=args.verify_cached_prefix, sink=sink))
+                                   verify_cached_prefix=args.verify_cached_prefix, sink=sink, stats=pull))
             served += [(t.request_id, t.token_ids) for t in transfers]
             dist.send_object_list(["done"], dst=p)
         out_tokens = torch.cat(outs) if outs else None
@@ -105,6 +132,7 @@ def run(args) -> dict:
                                                 "verify_cached_prefix": args.verify_cached_prefix})
             with open(os.path.join(d, "lifetime.jsonl"), "w") as f:
                 f.writelines(json.dumps(e) + "\n" for e in sink.events)
+            rec_dir = d
     b.record()
     torch.cuda.synchronize(dev)
     dev_ms = _max(a.elapsed_time(b), dev)
@@ -115,10 +143,19 @@ def run(args) -> dict:
     mism = sum(1 for r in rec.records if r.get("kind") == "verification" and r.get("native_result") == "mismatch")
     tot_mism = int(_max(float(mism), dev))
     tokens = sum(len(t) + args.new_tokens for _, t in reqs)
+    # per decode rank: the KV pulls' bytes and device time, and the gate's verdict on its recording
+    mine_row = None
+    if rank >= P:
+        mine_row = {"rank": rank, "pull_bytes": pull.get("pull_bytes", 0), "pull_ms": round(pull.get("pull_ms", 0.0), 3),
+                    "pulls": pull.get("pulls", 0), "gate": _gate(rec_dir) if rec_dir else None}
+    rows = [None] * world
+    dist.all_gather_object(rows, mine_row)
+    rows = [r for r in rows if r is not None]
     res = {"world": world, "prefill_ranks": P, "decode_ranks": D, "requests": len(reqs), "device_ms": round(dev_ms, 2),
            "wall_ms": round(wall_ms, 2), "tokens_per_s": round(tokens / (dev_ms / 1e3), 1),
            "lifetime_violations": tot_viol, "ranks_with_mismatch": tot_mism, "model": cfg.name,
-           "checked": not args.unchecked}
+           "checked": not args.unchecked, "kv_pull": _pull_summary(rows),
+           "gate": [dict(r["gate"], decode_rank=r["rank"]) for r in rows if r.get("gate")] or None}
     dist.barrier()
     del eng
     heap.close()
