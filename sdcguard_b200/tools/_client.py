@@ -23,9 +23,46 @@ def post(url: str, body: dict, timeout: float = 600.0) -> dict:
         return json.loads(r.read().decode())
 
 
-def complete(base: str, prompt, max_tokens: int, timeout: float = 600.0) -> list[int]:
-    r = post(base.rstrip("/") + "/v1/completions", {"prompt": prompt, "max_tokens": max_tokens}, timeout)
+def complete(base: str, prompt, max_tokens: int, timeout: float = 600.0, extra: Optional[dict] = None) -> list[int]:
+    """Greedy completion; `extra` adds fields to the request (vLLM's `cache_salt`, for one)."""
+    r = post(base.rstrip("/") + "/v1/completions", {"prompt": prompt, "max_tokens": max_tokens, **(extra or {})},
+             timeout)
     return r["choices"][0]["token_ids"]
+
+
+def complete_salted(base: str, prompt, max_tokens: int, salt: str, timeout: float = 600.0) -> list[int]:
+    """Greedy completion under a prefix-cache salt: requests with different salts share no cached blocks on a
+    server that honours it (vLLM's `cache_salt`); a server without a prefix cache ignores the field."""
+    return complete(base, prompt, max_tokens, timeout, extra={"cache_salt": salt})
+
+
+def stream_cancel(base: str, prompt, max_tokens: int, timeout: float = 120.0) -> bool:
+    """Start a streamed greedy completion and close the connection after its first event: the server is left to
+    end a request whose client went away. Returns whether an event arrived before the close."""
+    req = urllib.request.Request(base.rstrip("/") + "/v1/completions",
+                                 data=json.dumps({"prompt": prompt, "max_tokens": max_tokens, "stream": True,
+                                                  "temperature": 0.0}).encode(),
+                                 headers={"Content-Type": "application/json"})
+    with urllib.request.urlopen(req, timeout=timeout) as r:
+        for raw in r:
+            if raw.strip().startswith(b"data:"):
+                return True
+    return False
+
+
+def prefix_cache_hits(base: str, timeout: float = 10.0) -> Optional[float]:
+    """Tokens the server has read from its prefix cache so far (vLLM's `vllm:prefix_cache_hits` counter, summed
+    over its labels), or None when the server exports no such counter."""
+    m = scrape(base, timeout)
+    if m is None:
+        return None
+    total, seen = 0.0, False
+    for name, v in m.items():
+        bare = name[:-2] if name.endswith("{}") else name
+        if bare in ("vllm:prefix_cache_hits", "vllm:prefix_cache_hits_total"):
+            seen = True
+            total += sum(x for _, x in v) if isinstance(v, list) else v
+    return total if seen else None
 
 
 def score(base: str, prompt, top_k: int = 5, timeout: float = 600.0) -> dict:

@@ -12,6 +12,13 @@ reused too early, a cached prefix read from the wrong pages. Checks of the arith
    not deterministic at batch size 1 and the probe can judge nothing.
 2. Concurrency. The probe is sent while other requests of different prompts and lengths run in the same batches; a
    batch-dependent answer is reported.
+3. Cancellation under shared prefixes. Groups of requests share a long prompt head (a server with a prefix cache
+   shares its blocks) and differ in a short tail. Each is answered alone twice (the control), then all are sent at
+   once together with more requests of the same heads that are streamed and dropped after their first event, so
+   the server ends them mid-flight and hands their KV pages back while the others still read theirs. Every answer
+   under that load must equal its solo answer. (The reference's canary probe asks a trained model to repeat a code
+   from its context and looks for another request's code; random-init weights copy nothing, so here the solo
+   answer is the witness.)
 
 Verdicts: LEAK (a probe's answer changed with the primer in the same way every time that primer came before it,
 while every control repeat agreed; or a concurrent answer differed from the solo one on a server whose solo repeats
@@ -19,9 +26,8 @@ agree), NO LEAK SEEN (neither, with every control agreeing), INCONCLUSIVE (a con
 answers changed in ways that do not repeat with their primer: one differing token cannot be told from a server that
 is not deterministic). NO LEAK SEEN covers these prompts, this load and this server only. Exit 0 / 1 (LEAK) / 2.
 
-Reference: src/sdcguard/isolation.py:1-40 (the probes and verdict rules; the canary probe that looks for another
-request's random code in an answer needs a trained model that copies its context, which this package's random-init
-serving shapes are not).
+Reference: src/sdcguard/isolation.py:1-40 (the probes and verdict rules), :179 (the canary probe: shared document
+prefixes, concurrent requests, a share of them cancelled after their first chunk).
 """
 from __future__ import annotations
 
@@ -95,8 +101,63 @@ def concurrency_probe(base: str, probe: list, others: list, tokens: int, complet
             "first_difference": None if isinstance(mixed, Exception) else _first_diff(solo, mixed)}
 
 
+def cancel_probe(base: str, groups: int = 4, per_group: int = 4, head: int = 96, tail: int = 8, tokens: int = 16,
+                 cancels_per_group: int = 2, seed: int = 0, vocab: int = 1000, complete: Callable = _client.complete,
+                 cancel: Callable = _client.stream_cancel) -> dict:
+    """Probe 3 of the module docstring. `cancel(base, ids, n)` starts a streamed request and drops it after its
+    first event."""
+    rng = random.Random(seed * 104729 + 3)
+    heads = [[rng.randrange(vocab) for _ in range(head)] for _ in range(groups)]
+    reqs = [{"group": g, "ids": heads[g] + [rng.randrange(vocab) for _ in range(tail)]}
+            for g in range(groups) for _ in range(per_group)]
+    drops = [{"group": g, "ids": heads[g] + [rng.randrange(vocab) for _ in range(tail)]}
+             for g in range(groups) for _ in range(cancels_per_group)]
+    try:
+        solo = [complete(base, r["ids"], tokens) for r in reqs]
+        again = [complete(base, r["ids"], tokens) for r in reqs]
+    except Exception as e:  # noqa: BLE001
+        return {"verdict": "INCONCLUSIVE", "error": f"solo request failed: {str(e)[:300]}"}
+    controls = [i for i, (a, b) in enumerate(zip(solo, again)) if a != b]
+    got: dict = {}
+    errors: list = []
+
+    def answer(i):
+        try:
+            got[i] = complete(base, reqs[i]["ids"], tokens)
+        except Exception as e:  # noqa: BLE001
+            errors.append(f"request {i}: {str(e)[:200]}")
+
+    dropped: list = []
+
+    def drop(j):
+        try:
+            if cancel(base, drops[j]["ids"], 4 * tokens):
+                dropped.append(j)
+        except Exception as e:  # noqa: BLE001  (a stream that could not start was not dropped mid-flight)
+            errors.append(f"cancelled request {j}: {str(e)[:200]}")
+    th = [threading.Thread(target=drop, args=(j,)) for j in range(len(drops))]
+    th += [threading.Thread(target=answer, args=(i,)) for i in range(len(reqs))]
+    for t in th:
+        t.start()
+    for t in th:
+        t.join()
+    changed = [{"request": i, "group": reqs[i]["group"], "first_difference": _first_diff(solo[i], got[i])}
+               for i in range(len(reqs)) if i in got and got[i] != solo[i] and i not in controls]
+    answered = sum(1 for i in range(len(reqs)) if i in got)
+    if changed and not controls:
+        verdict = "LEAK"
+    elif controls or answered < len(reqs) or changed or not dropped:
+        verdict = "INCONCLUSIVE"          # (no stream dropped mid-flight: the load this probe is for never ran)
+    else:
+        verdict = "NO LEAK SEEN"
+    return {"verdict": verdict, "requests": len(reqs), "cancelled": len(drops), "dropped_mid_flight": len(dropped),
+            "answered": answered,
+            "controls_disagree": controls, "changed_under_load": changed, "errors": errors[:10]}
+
+
 def run(base: str, probes: int = 4, primers: int = 3, repeats: int = 2, prompt: int = 24, tokens: int = 16,
-        others: int = 8, seed: int = 0, vocab: int = 1000, complete: Callable = _client.complete) -> dict:
+        others: int = 8, seed: int = 0, vocab: int = 1000, complete: Callable = _client.complete,
+        cancellation: bool = True, cancel: Callable = _client.stream_cancel) -> dict:
     rng = random.Random(seed)
     rows = []
     for p in range(probes):
@@ -112,7 +173,9 @@ def run(base: str, probes: int = 4, primers: int = 3, repeats: int = 2, prompt: 
         v = ("LEAK" if "LEAK" in (a["verdict"], b["verdict"]) else
              "INCONCLUSIVE" if "INCONCLUSIVE" in (a["verdict"], b["verdict"]) else "NO LEAK SEEN")
         rows.append({"probe": p, "verdict": v, "primer": a, "concurrency": b})
-    verdicts = [r["verdict"] for r in rows]
+    cp = (cancel_probe(base, tokens=tokens, seed=seed, vocab=vocab, complete=complete, cancel=cancel)
+          if cancellation else None)
+    verdicts = [r["verdict"] for r in rows] + ([cp["verdict"]] if cp else [])
     verdict = ("LEAK" if "LEAK" in verdicts else "INCONCLUSIVE" if "INCONCLUSIVE" in verdicts or not rows
                else "NO LEAK SEEN")
     why = []
@@ -132,8 +195,15 @@ def run(base: str, probes: int = 4, primers: int = 3, repeats: int = 2, prompt: 
                        f"difference at token {b['first_difference']})")
         elif b["verdict"] == "INCONCLUSIVE":
             why.append(f"probe {r['probe']}: the concurrency probe was inconclusive")
+    if cp and cp["verdict"] == "LEAK":
+        why.append(f"cancellation: {len(cp['changed_under_load'])} answers changed while requests of the same "
+                   f"prompt heads were dropped mid-flight (their solo answers repeat exactly)")
+    elif cp and cp["verdict"] == "INCONCLUSIVE":
+        why.append("cancellation: " + (cp.get("error") or
+                                       ("solo answers do not repeat" if cp["controls_disagree"] else
+                                        "requests failed or answers changed beside solo answers that do not repeat")))
     differing = sum(len(r["primer"]["primers_changing_the_answer"]) for r in rows if "primer" in r)
-    return {"schema": SCHEMA, "url": base, "verdict": verdict, "why": why, "probes": rows,
+    return {"schema": SCHEMA, "url": base, "verdict": verdict, "why": why, "probes": rows, "cancellation": cp,
             "primer": {"pairs": probes * (primers - 1), "pairs_differing": differing},
             "probe_set": {"probes": probes, "primers": primers, "repeats": repeats, "prompt": prompt,
                           "tokens": tokens, "others": others, "seed": seed},
@@ -148,9 +218,10 @@ def main(argv=None) -> int:
     ap.add_argument("--repeats", type=int, default=2)
     ap.add_argument("--tokens", type=int, default=16)
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-cancel", action="store_true", help="skip the cancellation probe")
     ap.add_argument("--out")
     a = ap.parse_args(argv)
-    r = run(a.url, a.probes, a.primers, a.repeats, tokens=a.tokens, seed=a.seed)
+    r = run(a.url, a.probes, a.primers, a.repeats, tokens=a.tokens, seed=a.seed, cancellation=not a.no_cancel)
     if a.out:
         with open(a.out, "w") as f:
             json.dump(r, f, indent=1)

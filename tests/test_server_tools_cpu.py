@@ -119,8 +119,16 @@ def test_ready_qualified():
     assert r["verdict"] == "NOT QUALIFIED" and ready.EXIT.get(r["verdict"], 1) == 1
 
 
+def fake_cancel(base, prompt, n):
+    return True
+
+
 def test_isolation_consistency_perf_on_fake_model():
-    assert isolation.run("x", probes=2, primers=3, complete=fake_complete)["verdict"] == "NO LEAK SEEN"
+    assert isolation.run("x", probes=2, primers=3, complete=fake_complete, cancel=fake_cancel)["verdict"] == \
+        "NO LEAK SEEN"
+    # no stream could be dropped (no server at "x"): the cancellation probe judges nothing
+    r = isolation.run("x", probes=1, primers=2, complete=fake_complete)
+    assert r["verdict"] == "INCONCLUSIVE" and r["cancellation"]["dropped_mid_flight"] == 0
     assert consistency.run("x", probes=2, complete=fake_complete, score=fake_score)["verdict"] == "CONSISTENT"
 
     def wrong_decode(base, prompt, n):     # decode goes wrong after 3 tokens, while prefill paths are right
@@ -326,3 +334,64 @@ def test_qualify_helpers(tmp_path):
     d = _decision()
     text = qualify.report([("fp8", d)])
     assert "fp8" in text and "ACCEPT" in text
+
+
+def test_isolation_cancellation_probe():
+    """Answers that change while requests of the same prompt heads are dropped mid-flight are a LEAK; solo answers
+    that do not repeat make the probe inconclusive."""
+    dropped = threading.Event()
+
+    def cancel(base, prompt, n):
+        dropped.set()
+        return True
+
+    def stale_after_drop(base, prompt, n):      # a dropped request's pages handed to a live one too early
+        out = fake_complete(base, prompt, n)
+        if threading.current_thread() is not threading.main_thread() and len(prompt) == 104:
+            dropped.wait(2.0)
+            return [(out[0] + 1) % 1000] + out[1:]
+        return out
+    r = isolation.cancel_probe("x", complete=stale_after_drop, cancel=cancel)
+    assert r["verdict"] == "LEAK" and len(r["changed_under_load"]) == r["requests"] == 16, r
+    assert r["dropped_mid_flight"] == r["cancelled"] == 8
+    assert isolation.run("x", probes=1, primers=2, complete=stale_after_drop, cancel=cancel)["verdict"] == "LEAK"
+    calls = {"n": 0}
+
+    def noisy(base, prompt, n):                 # solo answers that do not repeat
+        calls["n"] += 1
+        out = fake_complete(base, prompt, n)
+        return [(out[0] + calls["n"]) % 1000] + out[1:] if len(prompt) == 104 else out
+    r = isolation.cancel_probe("x", complete=noisy, cancel=cancel)
+    assert r["verdict"] == "INCONCLUSIVE" and r["controls_disagree"], r
+    assert isolation.cancel_probe("x", complete=fake_complete, cancel=cancel)["verdict"] == "NO LEAK SEEN"
+
+
+def test_consistency_prefix_cache_probe():
+    """The cached answer must equal the cold one where two cold answers agree and the hit counter shows the cache
+    read; without a counter the probe is not applicable and takes no part in the verdict."""
+    cache, hits = set(), [0.0]
+
+    def salted(bad):
+        def complete(base, prompt, n, salt):
+            key = (salt, tuple(prompt[:256]))
+            cached = key in cache
+            cache.add(key)
+            if cached:
+                hits[0] += 256
+            out = fake_complete(base, prompt, n)
+            return [(out[0] + 1) % 1000] + out[1:] if bad and cached else out
+        return complete
+    r = consistency.prefix_probe("x", complete_salted=salted(False), hits=lambda b: hits[0])
+    assert r["verdict"] == "CONSISTENT" and all(c["cache_hit"] for c in r["cases"]), r
+    r = consistency.prefix_probe("x", complete_salted=salted(True), hits=lambda b: hits[0])
+    assert r["verdict"] == "INCONSISTENT" and r["cases"][0]["cached_first_difference"] == 0, r
+    # a counter that does not move: no cache hit shown, nothing judged
+    r = consistency.prefix_probe("x", complete_salted=salted(True), hits=lambda b: 0.0)
+    assert r["verdict"] == "INCONCLUSIVE", r
+    assert consistency.prefix_probe("x", complete_salted=salted(True), hits=lambda b: None)["verdict"] == \
+        "NOT_APPLICABLE"
+    full = consistency.run("x", probes=1, complete=fake_complete, score=fake_score, complete_salted=salted(True),
+                           hits=lambda b: hits[0])
+    assert full["verdict"] == "INCONSISTENT" and full["decode_verdict"] == "CONSISTENT"
+    j = consistency.judge_against(full, dict(full, verdict="INCONSISTENT"))
+    assert j["verdict"] == "INCONSISTENT" and j["why"][0].startswith("prefix cache")
