@@ -209,6 +209,9 @@ def from_vllm(layer: torch.nn.Module, kernel) -> QuantWeights:
     module docstring). `kernel` carries `config` (weight_type, group_size, zero_points, has_g_idx,
     partition_weight_shape) and the parameter names `w_q_name`, `w_s_name`, `w_zp_name`, `w_gidx_name`."""
     c = kernel.config
+    act = getattr(c, "act_type", None)
+    if isinstance(act, torch.dtype) and act.itemsize == 1:
+        raise Unsupported(f"activations quantized to {act} inside the kernel (weight-only layers only)")
     wt = c.weight_type
     bits = int(wt.size_bits)
     if bits not in (4, 8) or not getattr(wt, "is_integer", lambda: True)():

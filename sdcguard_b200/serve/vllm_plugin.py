@@ -23,7 +23,13 @@ Off unless SDCGUARD_B200=1 (vLLM loads every installed plugin). In each vLLM pro
     its local rank (GET /metrics), so `sdcguard ready`, `decide` and `qualify` judge a running `vllm serve`; its token
     counter counts the tokens the worker computed;
   - with SDCGUARD_REQUIRE (1: every layer the share selects; a fraction such as 0.9: that share of them), the first
-    model step refuses to serve (RuntimeError) when fewer are checked, or when none is.
+    model step refuses to serve (RuntimeError) when fewer are checked, or when none is;
+  - with SDCGUARD_QUANT=1, weight-only INT4 / INT8 layers served by vLLM's mixed-precision kernels (Marlin, Machete
+    and the others behind `MPLinearKernel`) are checked too: their effective bf16 weights are read before the kernel
+    repacks them (`ops.quant.from_vllm`), the kernel itself is probed on unit vectors after the repack and must give
+    those weights bit for bit (for Machete with zero points, whichever of its two roundings matches), and the layer
+    then runs on the checked GEMM over the effective weights (kept in bf16: checked, not memory-saving). A layer the
+    reader refuses or the probe contradicts stays on vLLM's kernel, with the reason in `coverage()`.
 
 The reference's plugin (SDCGUARD=1) keeps vLLM's GEMM and adds a Triton check after it; here the check is part of
 the GEMM, so a checked layer is still one launch. Differences in rounding order from cuBLAS's GEMM are in the last
@@ -98,11 +104,12 @@ def _layer_name(layer: torch.nn.Module) -> str:
     return getattr(layer, "prefix", None) or f"linear{_COUNTER[0]}"
 
 
-def _adopt(layer: torch.nn.Module) -> None:
-    """Checksums of a loaded linear layer and its state row, when it can be checked."""
+def _adopt(layer: torch.nn.Module, weight: Optional[torch.Tensor] = None, label: str = "ABFT GEMM") -> None:
+    """Checksums of a loaded linear layer and its state row, when it can be checked (`weight`: the matrix the
+    layer multiplies by, when it is not the layer's own `weight`)."""
     from ..ops import gemm
     from .settings import layer_selected
-    w = getattr(layer, "weight", None)
+    w = weight if weight is not None else getattr(layer, "weight", None)
     name = _layer_name(layer)
     lid = getattr(layer, "_sdcguard_b200_id", None)
     if lid is not None:                 # weights loaded again: new checksums, same state row
@@ -131,10 +138,10 @@ def _adopt(layer: torch.nn.Module) -> None:
     if why is not None:
         _LEFT_OUT.append((name, why, int(w.numel()) if isinstance(w, torch.Tensor) else 0))
         return
-    bias = getattr(layer, "bias", None)
+    bias = getattr(layer, "bias", None) if weight is None else None     # (quantized kernels get it in apply)
     add_bias = bias is not None and not getattr(layer, "skip_bias_add", False)
     cw = gemm.CheckedWeight(w.detach(), bias.detach() if add_bias else None)
-    slot = st.state.add(f"{name} (ABFT GEMM)", cw.nb)
+    slot = st.state.add(f"{name} ({label})", cw.nb)
     st.slot_weights[slot] = cw
     # the workspace is sized now, before vLLM captures CUDA graphs, for every batch size the scheduler can form
     gemm.reserve_for_rows(w.device, cw.n, _max_tokens())
@@ -338,11 +345,92 @@ def _patch() -> None:
     Worker.execute_model = execute_model
 
 
+def _quant_kernel_classes() -> list:
+    """vLLM's concrete mixed-precision linear kernel classes (every imported subclass of MPLinearKernel)."""
+    import importlib
+    import pkgutil
+    from vllm.model_executor.kernels.linear import mixed_precision as mp
+    from vllm.model_executor.kernels.linear.mixed_precision.MPLinearKernel import MPLinearKernel
+    for m in pkgutil.iter_modules(mp.__path__):
+        try:
+            importlib.import_module(f"{mp.__name__}.{m.name}")
+        except Exception:  # noqa: BLE001  (a backend module that cannot import here has no layers here)
+            pass
+    out, todo = [], list(MPLinearKernel.__subclasses__())
+    while todo:
+        c = todo.pop()
+        out.append(c)
+        todo += c.__subclasses__()
+    return out
+
+
+def _adopt_quant(layer, kernel, qw, orig_apply) -> None:
+    """After the kernel's repack: probe it against the effective weights read before, then adopt the layer."""
+    from ..ops import quant
+    w = qw.effective_weight()
+    cols = quant.probe_columns(qw.k, qw.group, limit=int(os.environ.get("SDCGUARD_QUANT_PROBE_COLUMNS", "256")))
+    tried = []
+    for cand in ([qw] + ([qw.with_zero_mode(m) for m in quant.ZERO_MODES if m != qw.zero_mode]
+                         if qw.zeros is not None else [])):
+        w = cand.effective_weight() if cand is not qw else w
+        r = quant.probe(lambda x: orig_apply(kernel, layer, x, None), w, cols)
+        tried.append(f"{cand.zero_mode}: {r['mismatches']} of {r['columns'] * w.shape[0]}")
+        if r["ok"]:
+            layer._sdcguard_b200_weff = w
+            _adopt(layer, weight=w, label=f"ABFT GEMM, INT{qw.bits} effective weights ({cand.zero_mode})")
+            return
+    _LEFT_OUT.append((_layer_name(layer), "quantized kernel differs from the restated weights (" +
+                      "; ".join(tried) + ")", qw.n * qw.k))
+
+
+def _patch_quant(classes=None) -> list:
+    """SDCGUARD_QUANT=1: the mixed-precision kernels' weight loading and apply (see the module docstring)."""
+    from ..ops import quant
+    patched = []
+    for cls in (classes if classes is not None else _quant_kernel_classes()):
+        if "process_weights_after_loading" not in cls.__dict__ or "apply_weights" not in cls.__dict__:
+            continue
+        orig_load, orig_apply = cls.__dict__["process_weights_after_loading"], cls.__dict__["apply_weights"]
+
+        def process_weights_after_loading(self, layer, _load=orig_load, _apply=orig_apply):
+            qw, why = None, None
+            try:
+                qw = quant.from_vllm(layer, self)
+            except Exception as e:  # noqa: BLE001  (the reason is recorded; vLLM's own path is untouched)
+                why = f"quantized layer not read: {type(e).__name__}: {e}"[:200]
+            _load(self, layer)
+            if qw is None:
+                shape = getattr(getattr(self, "config", None), "partition_weight_shape", (0, 0))
+                _LEFT_OUT.append((_layer_name(layer), why, int(shape[0]) * int(shape[1])))
+                return
+            try:
+                _adopt_quant(layer, self, qw, _apply)
+            except Exception as e:  # noqa: BLE001
+                _LEFT_OUT.append((_layer_name(layer), f"not adopted: {type(e).__name__}: {e}"[:200], qw.n * qw.k))
+
+        def apply_weights(self, layer, x, bias=None, _apply=orig_apply):
+            lid = getattr(layer, "_sdcguard_b200_id", None)
+            if lid is None or x.dtype != torch.bfloat16:
+                return _apply(self, layer, x, bias)
+            return torch.ops.sdcguard_b200_vllm.linear(x, layer._sdcguard_b200_weff, bias, lid)
+
+        cls.process_weights_after_loading = process_weights_after_loading
+        cls.apply_weights = apply_weights
+        patched.append(cls)
+    return patched
+
+
 def register() -> None:
     """vLLM general-plugin entry point (and the in-process hook): patch vLLM once, when SDCGUARD_B200=1."""
     if os.environ.get(ENV, "0") != "1" or _REGISTERED[0]:
         return
     _define_op()
     _patch()
+    if os.environ.get("SDCGUARD_QUANT", "0") == "1":
+        try:
+            names = [c.__name__ for c in _patch_quant()]
+            log.info("sdcguard_b200: quantized linear kernels checked: %s", ", ".join(names) or "none found")
+        except ImportError as e:
+            log.warning("sdcguard_b200: no vLLM mixed-precision kernels to hook (%s)", e)
     _REGISTERED[0] = True
     log.info("sdcguard_b200: vLLM linear layers will run on the checked GEMM")

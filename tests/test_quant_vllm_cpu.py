@@ -112,3 +112,52 @@ def test_probe_and_refusals():
     layer.g_idx = torch.randperm(k, generator=g) // group
     with pytest.raises(quant.Unsupported, match="reordering"):
         quant.from_vllm(layer, _kernel(4, 8, k, n, group, False, g_idx=True))
+
+
+def test_plugin_quant_hook_on_cpu():
+    """The plugin's hook of quantized kernels: the layer is read before the kernel's own loading, the kernel is
+    probed after it, and a layer that cannot be adopted keeps the kernel's path with its reason (on the CPU: no
+    CUDA device; a kernel whose products contradict the restated weights; a layout the reader refuses)."""
+    from sdcguard_b200.serve import vllm_plugin as vp
+    n, k, group = 16, 256, 128
+    g = torch.Generator().manual_seed(4)
+    q = torch.randint(0, 16, (n, k), generator=g)
+    s = (torch.rand(n, k // group, generator=g) * 0.02 + 1e-3).to(torch.bfloat16)
+    w_eff = ((q.double() - 8) * s.double().repeat_interleave(group, 1)).to(torch.bfloat16)
+    loads = []
+
+    class FakeKernel:
+        def __init__(self, group_size=group, skew=0.0):
+            self.config = SimpleNamespace(weight_type=_wtype(4, 8), group_size=group_size, zero_points=False,
+                                          has_g_idx=False, partition_weight_shape=(k, n))
+            self.w_q_name, self.w_s_name, self.w_zp_name, self.w_gidx_name = "wq", "ws", None, None
+            self.skew = skew
+
+        def process_weights_after_loading(self, layer):
+            loads.append(layer.prefix)
+            layer.wq = torch.nn.Parameter(torch.zeros(1, dtype=torch.int32), requires_grad=False)   # "repacked"
+
+        def apply_weights(self, layer, x, bias=None):
+            w = w_eff.double().clone()
+            w[0, 0] += self.skew
+            return (x.double() @ w.t()).to(torch.bfloat16)
+
+    assert vp._patch_quant([FakeKernel]) == [FakeKernel]
+
+    def layer(prefix):
+        m = torch.nn.Module()
+        m.prefix = prefix
+        m.wq = _param(_pack(q.t(), 4, 0), input_dim=0, output_dim=1, packed_dim=0, packed_factor=8)
+        m.ws = _param(s.t().contiguous(), input_dim=0, output_dim=1)
+        return m
+    before = len(vp._LEFT_OUT)
+    FakeKernel().process_weights_after_loading(layer("q.ok"))
+    FakeKernel(skew=1.0).process_weights_after_loading(layer("q.skewed"))
+    FakeKernel(group_size=-1).process_weights_after_loading(layer("q.channelwise"))
+    assert loads == ["q.ok", "q.skewed", "q.channelwise"]
+    why = {name: r for name, r, _ in vp._LEFT_OUT[before:]}
+    assert "not on a CUDA device" in why["q.ok"]                       # read, probed bit-exact, then refused: CPU
+    assert why["q.skewed"].startswith("quantized kernel differs") and "subtract: 1 of" in why["q.skewed"]
+    assert why["q.channelwise"].startswith("quantized layer not read: Unsupported")
+    x = torch.randn(3, k).to(torch.bfloat16)
+    assert torch.equal(FakeKernel().apply_weights(layer("q.unadopted"), x), FakeKernel().apply_weights(None, x))
