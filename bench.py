@@ -349,9 +349,10 @@ def run_pd(args, rank: int, world: int, local: int) -> dict:
     GPU memory with the checksumming copy. Two runs: clean (cached prefixes re-verified; the gate's verdict on every
     decode rank's recording) and with one bit flipped in a producer page (the pull must report it)."""
     out = {"prefill_ranks": world // 2, "decode_ranks": world // 2}
-    rec_root = os.path.join(os.environ.get("SDCGUARD_BLOCK_LOG_DIR", "/tmp"), f"sdcguard_pd_{os.getpid()}")
-    if rank == 0:
-        os.makedirs(rec_root, exist_ok=True)
+    # one directory for the job (the parent group's port names it), each decode rank writing its own decode<c>/
+    rec_root = os.path.join(os.environ.get("SDCGUARD_BLOCK_LOG_DIR", "/tmp"),
+                            f"sdcguard_pd_{os.environ.get('MASTER_PORT', '0')}_{world}")
+    os.makedirs(rec_root, exist_ok=True)
     base = ["--prefill", str(world // 2), "--model", "Qwen3-0.6B", "--groups", "8", "--per-group", "20",
             "--new-tokens", "32", "--verify-cached-prefix", "--pg-timeout", "120"]
     for tag, extra in (("clean", ["--out", os.path.join(rec_root, "clean")]),
