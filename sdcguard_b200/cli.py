@@ -14,6 +14,8 @@
     sdcguard screen / screen-ops / modes                     workload, operator and math-mode screens of a GPU
     sdcguard blas / kernels / issues                         cuBLASLt algorithm sweep, kernel inventory, known issues
     sdcguard certify / fleet / board                         signed certificates, fleet view, results board
+    sdcguard keygen / verify / report / demo                 the reference's names: certify keygen / verify,
+                                                             fleet collect, selftest
     sdcguard casefile / replay / investigate                 incident casefile, replays of a flagged GEMM here
     sdcguard gate-model                                      teacher-forced output comparison of two stacks
     sdcguard serve / ready / perf / isolation / consistency  HTTP server and outside-in probes
@@ -58,6 +60,41 @@ def _lazy(module: str, fn: str):
         import importlib
         return getattr(importlib.import_module(module, __package__), fn)(argv)
     return run
+
+
+def _keygen(argv) -> int:
+    """`sdcguard keygen [--out PREFIX]`: a signing key pair for certificates (the reference's command name)."""
+    import argparse
+    ap = argparse.ArgumentParser(prog="sdcguard keygen")
+    ap.add_argument("--out", default="sdcguard")
+    a = ap.parse_args(argv)
+    return _lazy(".tools.certify", "main")(["keygen", "--out", a.out])
+
+
+def _verify(argv) -> int:
+    """`sdcguard verify CERT [CERT ...] [--pubkey P]`: check certificates; exit 1 when any is not valid."""
+    import argparse
+    ap = argparse.ArgumentParser(prog="sdcguard verify")
+    ap.add_argument("certificates", nargs="+")
+    ap.add_argument("--pubkey")
+    a = ap.parse_args(argv)
+    run = _lazy(".tools.certify", "main")
+    key = ["--pubkey", a.pubkey] if a.pubkey else []
+    return max(int(run(["verify", c, *key]) or 0) for c in a.certificates)
+
+
+def _report(argv) -> int:
+    """`sdcguard report DIR [DIR ...] [--out D] [--pubkey P] [--window-days W]`: the fleet report of screen results
+    (the reference's command name for `fleet collect`)."""
+    import argparse
+    ap = argparse.ArgumentParser(prog="sdcguard report")
+    ap.add_argument("dirs", nargs="+")
+    ap.add_argument("--out", default="fleet_report")
+    ap.add_argument("--pubkey")
+    ap.add_argument("--window-days", type=float, default=30.0)
+    a = ap.parse_args(argv)
+    return _lazy(".tools.fleet", "main")(["collect", *a.dirs, "--out", a.out, "--days", str(a.window_days),
+                                          *(["--pubkey", a.pubkey] if a.pubkey else [])])
 
 
 COMMANDS = {
@@ -114,6 +151,11 @@ COMMANDS = {
     "vllm-bench": _lazy(".tools.vllm_bench", "main"),
     "calibrate": _lazy(".tools.calibrate", "main"),
     "version": _version,
+    # the reference's names for commands this package files elsewhere
+    "keygen": _keygen,
+    "verify": _verify,
+    "report": _report,
+    "demo": _lazy(".tools.selftest", "main"),
 }
 
 

@@ -84,3 +84,25 @@ def test_board_validates_and_aggregates(tmp_path):
     agg = board.aggregate(board.load([str(d)])[0])
     assert agg["models"]["NVIDIA B200"]["fingerprint_agreement"] == [2, 3]
     assert os.path.exists(tmp_path / "out" / "index.html")
+
+
+def test_reference_command_names(tmp_path, capsys):
+    """`sdcguard keygen`, `verify` and `report`, the reference's names for certify keygen / verify and fleet
+    collect, give the same results."""
+    from sdcguard_b200 import cli
+    assert cli.main(["keygen", "--out", str(tmp_path / "k")]) == 0
+    kp, pp = str(tmp_path / "k") + ".key", str(tmp_path / "k") + ".pub"
+    keys = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    kp, pp = keys.get("private", kp), keys.get("public", pp)
+    d = tmp_path / "root" / "node1"
+    d.mkdir(parents=True)
+    good = certify.sign(certify.make(_screen()), kp)
+    (d / "certificate.json").write_text(json.dumps(good))
+    assert cli.main(["verify", str(d / "certificate.json"), "--pubkey", pp]) == 0
+    bad = dict(good, result=dict(good["result"], verdict="FAIL"))
+    (tmp_path / "bad.json").write_text(json.dumps(bad))
+    assert cli.main(["verify", str(d / "certificate.json"), str(tmp_path / "bad.json"), "--pubkey", pp]) == 1
+    capsys.readouterr()
+    rc = cli.main(["report", str(tmp_path / "root"), "--out", str(tmp_path / "rep"), "--pubkey", pp])
+    assert rc in (0, 1) and (tmp_path / "rep" / "fleet.html").exists()
+    assert cli.COMMANDS["demo"] is not None
