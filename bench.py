@@ -298,7 +298,10 @@ def run_child_block(name: str, module: str, argv: list, rank: int, world: int, l
         try:
             out, _ = p.communicate(timeout=limit_s)
         except subprocess.TimeoutExpired:
-            os.killpg(p.pid, signal.SIGKILL)
+            try:
+                os.killpg(p.pid, signal.SIGKILL)
+            except ProcessLookupError:          # it ended between the time-out and the kill
+                pass
             out, _ = p.communicate()
     lines = [x for x in (out or "").splitlines() if x.startswith("{")]
     result = None
