@@ -12,7 +12,8 @@ The JSON line also carries: the unchecked throughput of the same engine (cuBLAS 
 overhead; an end-to-end number through the public API (`LLMEngine.generate`, wall clock, pinned prompts in and
 tokens out each step); a short fault-injection campaign (single-bit flips in GEMM accumulators, KV pages and
 replayed rows) with the false alarms of the timed clean run; SM clocks sampled during the timed region.
-At N > 1 it also carries three multi-GPU blocks, each timed on the device and taken as the max over ranks: "tp"
+At N = 1 it carries "train": the training guard's cost (GPT-2 small, every 10th step checked, against plain
+training), measured in a process of its own. At N > 1 it carries three multi-GPU blocks, each timed on the device and taken as the max over ranks: "tp"
 (the Llama-3-8B shape at TP = N, checked against cuBLAS + NCCL), and at even N "ep" (the Mixtral-8x7B shape at
 EP = N, block-scaled fp8 checked against bf16 unchecked) and "pd" (prefill on N/2 ranks, decode on N/2, KV pages
 pulled over NVLink with in-flight checksums, the coverage gate's verdict on each decode rank's recording). "ep" and
@@ -65,6 +66,7 @@ def parse():
     ap.add_argument("--tp-new-tokens", type=int, default=256)
     ap.add_argument("--no-ep", action="store_true", help="skip the expert-parallel block (config 5 at EP = N)")
     ap.add_argument("--no-pd", action="store_true", help="skip the prefill/decode block (config 3 at N/2 + N/2)")
+    ap.add_argument("--no-train", action="store_true", help="skip the training block (GPT-2 small, N = 1)")
     ap.add_argument("--ep-layers", type=int, default=4)
     ap.add_argument("--ep-steps", type=int, default=3)
     ap.add_argument("--block-limit", type=float, default=420.0,
@@ -249,6 +251,8 @@ def run_ours(args, rank, world, local):
         res["tp"] = {"skipped": "TP = 1 is the single-GPU engine of the headline; the block runs from N = 2"}
     gc.collect()
     torch.cuda.empty_cache()
+    if world == 1 and not args.no_train:
+        res["train"] = run_train(args)
     if world > 1 and world % 2 == 0:
         if not args.no_ep:
             res["ep"] = run_ep(args, rank, world, local)
@@ -321,6 +325,33 @@ def run_child_block(name: str, module: str, argv: list, rank: int, world: int, l
         return {"error": f"{module} on rank {rank} ended with rc {p.returncode} after "
                          f"{time.perf_counter() - t0:.0f} s: {tail}"}
     return {"error": "another rank's process of this block failed (its log names the cause)"}
+
+
+def run_train(args) -> dict:
+    """The training guard's cost on one GPU, in a process of its own (its cuBLAS settings stay there): GPT-2 small
+    (batch 32 x 512 tokens, AdamW, bf16 autocast) trained plainly and with every 10th step checked (each nn.Linear's
+    forward, dX and dW GEMMs on the checked GEMM), device time per step with CUDA events."""
+    left = args.deadline - (time.monotonic() - _T0)
+    if left < 120:
+        return {"skipped": f"{left:.0f} s left before the run's deadline"}
+    cmd = [sys.executable, "-m", "sdcguard_b200.tools.train_bench", "--every", "10", "--steps", "40", "--warmup", "5"]
+    env = dict(os.environ, PYTHONPATH=os.path.dirname(os.path.abspath(__file__)) + os.pathsep +
+               os.environ.get("PYTHONPATH", ""))
+    try:
+        r = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=min(args.block_limit, left))
+    except subprocess.TimeoutExpired:
+        return {"error": "the training block ran past its limit"}
+    lines = [x for x in r.stdout.splitlines() if x.startswith("{")]
+    if r.returncode != 0 or not lines:
+        return {"error": f"rc {r.returncode}: " + r.stderr[-500:].replace("\n", " | ")}
+    t = json.loads(lines[-1])
+    arm = (t.get("arms") or [{}])[0]
+    return {"model": t.get("model"), "batch": t.get("batch"), "seq": t.get("seq"), "dtype": t.get("dtype"),
+            "plain_ms_per_step": t.get("plain_ms_per_step"), "checked_every": 10,
+            "ms_per_step": arm.get("ms_per_step"), "overhead_pct": arm.get("overhead_pct"),
+            "checked_step_extra_ms": arm.get("checked_step_extra_ms"),
+            **{k: arm.get(k) for k in ("checks", "alarms", "worst_clean_z") if k in arm},
+            "clocks": t.get("clocks_plain_rerun"), "seconds": t.get("seconds")}
 
 
 def run_ep(args, rank: int, world: int, local: int) -> dict:
@@ -662,7 +693,7 @@ def main():
                 line["coverage"] = res["coverage"]
                 if "campaign" in res:
                     line["detection"] = res["campaign"]
-                for k in ("tp", "ep", "pd"):
+                for k in ("train", "tp", "ep", "pd"):
                     if k in res:
                         line[k] = res[k]
         print(json.dumps(line), flush=True)
