@@ -20,7 +20,7 @@ import torch
 import torch.distributed as dist
 
 from ..ops.fingerprint import fingerprint
-from ..utils.events import EventLog, SDCEvent, device_identity
+from ..utils.events import EventLog, SDCEvent, device_identity, gather_identities, job_rank, suspect_event
 
 _DTYPES = {d: i for i, d in enumerate([torch.float32, torch.float16, torch.bfloat16, torch.float64, torch.int64,
                                         torch.int32, torch.uint8, torch.bool, torch.int8, torch.int16])}
@@ -106,14 +106,18 @@ class Canary:
         g = torch.stack([x.cpu() for x in gathered])          # (world, n, 4)
         events = []
         names = [nm for nm, _ in self.calls] + ["?"] * (n - len(self.calls))
-        for c in range(n):
-            rows = [tuple(g[r, c].tolist()) for r in range(world)]
-            top, bad = majority(rows)
+        votes = [majority([tuple(g[r, c].tolist()) for r in range(world)]) for c in range(n)]
+        if not any(bad for _, bad in votes):
+            return events
+        # every rank saw the same votes: they exchange identities together, once, to name the suspects' GPUs
+        dev = self.calls[0][1].device if self.calls else None
+        ids = gather_identities(self.group, dev) if world > 1 else [device_identity(dev)]
+        me = dist.get_rank(self.group) if world > 1 else 0
+        for c, (top, bad) in enumerate(votes):
             if bad:
-                ev = SDCEvent(detector="canary", step=step,
-                              detail={"call": c, "module": names[c], "suspect_ranks": bad, "world": world,
-                                      "no_majority": top is None},
-                              identity=device_identity(self.calls[0][1].device if self.calls else None))
+                ev = suspect_event("canary", step, bad, ids, me,
+                                   {"call": c, "module": names[c], "no_majority": top is None},
+                                   to_job_rank=lambda r: job_rank(self.group, r))
                 self.log.add(ev)
                 events.append(ev)
         return events

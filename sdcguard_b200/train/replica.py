@@ -12,7 +12,7 @@ import torch
 import torch.distributed as dist
 
 from ..ops.fingerprint import fingerprint
-from ..utils.events import SDCEvent, device_identity
+from ..utils.events import SDCEvent, device_identity, gather_identities, job_rank, suspect_event
 from .canary import majority
 
 MASK = (1 << 64) - 1
@@ -50,6 +50,7 @@ def check_replicas(params: Iterable[torch.Tensor], group=None, step: Optional[in
     top, bad = majority([tuple(r) for r in rows])
     if not bad:
         return []
-    return [SDCEvent(detector="replica", step=step,
-                     detail={"suspect_ranks": bad, "world": world, "no_majority": top is None},
-                     identity=device_identity())]
+    ids = gather_identities(group) if world > 1 else [device_identity()]
+    me = dist.get_rank(group) if world > 1 else 0
+    return [suspect_event("replica", step, bad, ids, me, {"no_majority": top is None},
+                          to_job_rank=lambda r: job_rank(group, r))]

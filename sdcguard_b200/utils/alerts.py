@@ -38,6 +38,7 @@ class Webhook:
         self.sent = 0
         self.failed = 0
         self.dropped = 0
+        self.skipped = 0
         self._t = threading.Thread(target=self._run, daemon=True, name="sdcguard-webhook")
         self._t.start()
 
@@ -49,6 +50,9 @@ class Webhook:
         return json.loads(ev.to_json())
 
     def __call__(self, ev: SDCEvent) -> None:
+        if ev.detail.get("reporter") is False:      # a cross-rank vote's finding: one rank posts it, not every rank
+            self.skipped += 1
+            return
         try:
             self.q.put_nowait(ev)
         except queue.Full:

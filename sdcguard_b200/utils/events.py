@@ -108,3 +108,52 @@ def rollback_checkpoint(first_alert_step: int, checkpoint_steps: list[int], chec
     cutoff = first_alert_step - check_every * max(1, windows)
     ok = [s for s in checkpoint_steps if s <= cutoff]
     return max(ok) if ok else None
+
+
+# ------------------------------------------------------------------------------------------ cross-rank suspects
+IDENTITY_FIELDS = ("host", "gpu_uuid", "gpu_name", "pci_bus_id", "gpu_index")
+
+
+def gather_identities(group=None, device=None) -> list:
+    """Collective: every rank's `device_identity`, in the group's rank order (None entries when the exchange
+    fails: the ranks are still named)."""
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    ids: list = [None] * world
+    try:
+        dist.all_gather_object(ids, device_identity(device), group=group)
+    except Exception:  # noqa: BLE001  identities are best effort
+        ids = [None] * world
+    return ids
+
+
+def job_rank(group, r: int) -> int:
+    """Rank r of `group` as a rank of the whole job (r itself without a group, or when it cannot be mapped)."""
+    if group is None:
+        return r
+    import torch.distributed as dist
+    try:
+        return int(dist.get_global_rank(group, r))
+    except Exception:  # noqa: BLE001
+        return r
+
+
+def suspect_event(detector: str, step, suspects: list, ids: list, my_rank: int, detail: dict,
+                  to_job_rank=lambda r: r) -> SDCEvent:
+    """The event of a cross-rank vote (canary outputs, replica weights), built the same on every rank from the same
+    suspects (ranks of the voting group) and the gathered identities `ids`. With a clear majority (fewer suspects
+    than voters) it names the suspects' GPUs and, for a single suspect, takes that GPU's identity as the event's;
+    one rank, the lowest-ranked rank that agreed with the majority (rank 0 without a majority), is marked
+    `reporter`, so alert hooks post one message per finding instead of one per rank. Ranks in `suspect_ranks` and
+    `reported_by_rank` are the job's (`to_job_rank`); `suspect_group_ranks` keeps the group's."""
+    world = len(ids)
+    clear = len(suspects) < world
+    reporter = min((r for r in range(world) if r not in suspects), default=0) if clear else 0
+    who = [dict({"rank": to_job_rank(r)}, **{k: (ids[r] or {}).get(k) for k in IDENTITY_FIELDS}) for r in suspects]
+    full = {"suspect_ranks": [to_job_rank(r) for r in suspects], "suspect_group_ranks": list(suspects),
+            "world": world, "suspects": who, "reported_by_rank": to_job_rank(my_rank),
+            "reporter": my_rank == reporter, "clear_majority": clear}
+    full.update(detail)
+    mine = ids[my_rank] if 0 <= my_rank < world and ids[my_rank] else device_identity()
+    identity = dict(ids[suspects[0]]) if clear and len(suspects) == 1 and ids[suspects[0]] else dict(mine)
+    return SDCEvent(detector=detector, step=step, detail=full, identity=identity)

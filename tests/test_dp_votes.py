@@ -62,3 +62,22 @@ def test_canary_and_replica_votes_find_the_odd_rank():
         assert len(can) == 1 and can[0]["suspect_ranks"] == [2] and can[0]["call"] == 2
         assert clean == 0
         assert len(bad) == 1 and bad[0]["suspect_ranks"] == [1]
+        # the suspects' identities were gathered; one rank (the lowest that agreed with the majority) reports
+        assert can[0]["suspects"][0]["rank"] == 2 and can[0]["suspects"][0]["host"] and can[0]["clear_majority"]
+        assert can[0]["reported_by_rank"] == r and can[0]["reporter"] == (r == 0)
+        assert bad[0]["reporter"] == (r == 0) and bad[0]["suspect_group_ranks"] == [1]
+
+
+def test_suspect_event_names_the_suspect_gpu():
+    """Built alike on every rank: a single suspect with a clear majority gives the event its GPU's identity; the
+    lowest-ranked rank of the majority reports; without a majority rank 0 does."""
+    from sdcguard_b200.utils.events import suspect_event
+    ids = [{"host": "h", "gpu_uuid": f"GPU-{r}", "pci_bus_id": f"0000:{r:02X}:00.0"} for r in range(4)]
+    evs = [suspect_event("canary", 7, [0], ids, me, {"call": 3}, to_job_rank=lambda r: r + 4) for me in range(4)]
+    assert all(e.identity["gpu_uuid"] == "GPU-0" for e in evs)
+    assert [e.detail["reporter"] for e in evs] == [False, True, False, False]
+    assert evs[2].detail["suspect_ranks"] == [4] and evs[2].detail["suspect_group_ranks"] == [0]
+    assert evs[2].detail["reported_by_rank"] == 6 and evs[2].detail["suspects"][0]["pci_bus_id"] == "0000:00:00.0"
+    split = [suspect_event("replica", 1, [0, 1, 2, 3], ids, me, {}) for me in range(4)]
+    assert [e.detail["reporter"] for e in split] == [True, False, False, False]
+    assert not split[0].detail["clear_majority"] and split[1].identity["gpu_uuid"] == "GPU-1"
